@@ -1,0 +1,154 @@
+"""Philox4x32-10 on the GPU through the C ABI, checked against the pinned oracle.
+
+Bar: uint32 and uniform streams bit-exact; normal within an absolute bound of
+NORMAL_TOL * max(1, |z|) (CUDA's logf/sincosf and glibc's differ by a few ulp;
+both are correctly rounded sqrt and explicitly rounded affine steps).
+"""
+
+import ctypes as C
+import json
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+import oracle
+from muda_b200 import capi
+from tests.helpers import curand_generator, ulp_distance_f32
+
+pytestmark = pytest.mark.gpu
+
+GOLDEN = Path(__file__).resolve().parent / "golden"
+NORMAL_TOL = 2e-6  # absolute, scaled by max(1, |z|)
+
+
+def _gen(torch, fn, g, n, dtype, offset_elems=0, *extra):
+    buf = torch.empty(n + offset_elems + 4, dtype=dtype, device="cuda")
+    ptr = buf.data_ptr() + offset_elems * buf.element_size()
+    assert fn(g, C.c_void_p(ptr), n, *extra) == 0
+    torch.cuda.synchronize()
+    return buf[offset_elems:offset_elems + n].cpu().numpy()
+
+
+CASES = [(1234, 0, 1 << 16), (1234, 4096, 1000), (42, 0, 4097), (777, 1024, 1023),
+         (9999, 6, 19), (0xDEADBEEFCAFEF00D, (1 << 34) - 64, 100003), (5, 0, 1), (5, 0, 3)]
+
+
+@pytest.mark.parametrize("seed,offset,n", CASES)
+@pytest.mark.parametrize("misalign", [0, 1])
+def test_uint_and_uniform_bit_exact(cuda, built, seed, offset, n, misalign):
+    torch = cuda
+    L = capi.curand()
+    with curand_generator(seed, torch, offset=offset) as g:
+        got_u = _gen(torch, L.curandGenerate, g, n, torch.int32, misalign).view(np.uint32)
+    want_u, _ = oracle.generate_uint(seed, offset, n)
+    assert np.array_equal(got_u, want_u)
+    with curand_generator(seed, torch, offset=offset) as g:
+        got_f = _gen(torch, L.curandGenerateUniform, g, n, torch.float32, misalign)
+    want_f, _ = oracle.generate_uniform(seed, offset, n)
+    assert np.array_equal(got_f.view(np.uint32), want_f.view(np.uint32))
+
+
+@pytest.mark.parametrize("seed,offset,n", CASES)
+def test_normal_within_tolerance(cuda, built, seed, offset, n):
+    torch = cuda
+    L = capi.curand()
+    for mean, std in ((0.0, 1.0), (10.0, 3.0)):
+        with curand_generator(seed, torch, offset=offset) as g:
+            got = _gen(torch, L.curandGenerateNormal, g, n, torch.float32, 0,
+                       C.c_float(mean), C.c_float(std))
+        want, _ = oracle.generate_normal(seed, offset, n, mean, std)
+        err = np.abs(got.astype(np.float64) - want.astype(np.float64))
+        bound = NORMAL_TOL * std * np.maximum(1.0, np.abs(want.astype(np.float64) - mean)) + \
+            4 * np.spacing(np.float32(abs(mean) + 1))
+        assert np.all(err <= bound), f"max err {err.max()} (ulp {ulp_distance_f32(got, want).max()})"
+
+
+def test_golden_vectors_on_gpu(cuda, built):
+    torch = cuda
+    L = capi.curand()
+    for c in json.loads((GOLDEN / "philox.json").read_text())["cases"]:
+        with curand_generator(c["seed"], torch, offset=c["offset"]) as g:
+            got = _gen(torch, L.curandGenerate, g, c["n"], torch.int32).view(np.uint32)
+        assert [int(v) for v in got] == c["uint"]
+        with curand_generator(c["seed"], torch, offset=c["offset"]) as g:
+            got = _gen(torch, L.curandGenerateUniform, g, c["n"], torch.float32)
+        assert [int(v) for v in got.view(np.uint32)] == c["uniform_bits"]
+
+
+def test_config_sequence_uniform_then_normal(cuda, built):
+    """Config: seed 1234, offset 0, uniform then normal on the same generator and
+    stream; the normal call continues at offset 4*ceil(n/4)."""
+    torch = cuda
+    L = capi.curand()
+    n = (1 << 20) + 3
+    with curand_generator(1234, torch) as g:
+        u = _gen(torch, L.curandGenerateUniform, g, n, torch.float32)
+        z = _gen(torch, L.curandGenerateNormal, g, n, torch.float32, 0, C.c_float(0.0),
+                 C.c_float(1.0))
+    want_u, off = oracle.generate_uniform(1234, 0, n, threads=8)
+    want_z, _ = oracle.generate_normal(1234, off, n, 0.0, 1.0, threads=8)
+    assert off == 4 * ((n + 3) // 4)
+    assert np.array_equal(u.view(np.uint32), want_u.view(np.uint32))
+    err = np.abs(z.astype(np.float64) - want_z)
+    assert np.all(err <= NORMAL_TOL * np.maximum(1.0, np.abs(want_z)))
+    exact = np.mean(z.view(np.uint32) == want_z.view(np.uint32))
+    print(f"normal: {exact:.4%} bit-identical, max |err| {err.max():.3e}")
+
+
+def test_host_generator_matches_device_stream(cuda, built):
+    torch = cuda
+    L = capi.curand()
+    n = (1 << 26) + 4096 + 5  # crosses the 256 MiB staging chunk
+    out = np.zeros(n, dtype=np.float32)
+    with curand_generator(77, None, host=True, offset=40) as g:
+        assert L.curandGenerateUniform(g, out.ctypes.data_as(C.c_void_p), n) == 0
+    want, _ = oracle.generate_uniform(77, 40, n, threads=8)
+    assert np.array_equal(out.view(np.uint32), want.view(np.uint32))
+
+
+def test_reference_gpu_moments(cuda, built):
+    """tests/curand_test.cpp:203-314: seed 9999, 65536 draws."""
+    torch = cuda
+    L = capi.curand()
+    with curand_generator(9999, torch) as g:
+        u = _gen(torch, L.curandGenerateUniform, g, 65536, torch.float32).astype(np.float64)
+        z = _gen(torch, L.curandGenerateNormal, g, 65536, torch.float32, 0, C.c_float(0.0),
+                 C.c_float(1.0)).astype(np.float64)
+    assert np.all(u > 0) and np.all(u <= 1)
+    assert abs(u.mean() - 0.5) < 0.015
+    assert abs(z.mean()) < 0.03 and abs(z.var() - 1.0) < 0.05
+
+
+def test_full_size_stream_sampled(cuda, built):
+    """2^30 uniforms (the config size): 2^20 randomly sampled Philox blocks plus the
+    first and last blocks are bit-exact with the oracle."""
+    torch = cuda
+    L = capi.curand()
+    n = 1 << 30
+    buf = torch.empty(n, dtype=torch.float32, device="cuda")
+    with curand_generator(1234, torch) as g:
+        assert L.curandGenerateUniform(g, C.c_void_p(buf.data_ptr()), n) == 0
+    blocks = n // 4
+    rng = np.random.default_rng(0)
+    idx = np.unique(np.concatenate([rng.integers(0, blocks, 1 << 20), [0, blocks - 1]]))
+    got = buf.view(-1, 4)[torch.from_numpy(idx).cuda()].cpu().numpy().view(np.uint32)
+    words = oracle.philox_gather(idx.astype(np.uint64), 1234)
+    want = ((words.astype(np.float32) + np.float32(1.0)) *
+            np.float32(2.3283064365386963e-10)).astype(np.float32)
+    assert np.array_equal(got, want.view(np.uint32))
+    del buf
+    torch.cuda.empty_cache()
+
+
+def test_unaddressable_output_is_rejected(cuda, built):
+    torch = cuda
+    L = capi.curand()
+    host = np.zeros(64, dtype=np.float32)  # pageable host memory: not device-addressable
+    with curand_generator(1, torch) as g:
+        st = L.curandGenerateUniform(g, host.ctypes.data_as(C.c_void_p), 64)
+        assert st == capi.CURAND_STATUS_ALLOCATION_FAILED
+        small = torch.empty(16, dtype=torch.float32, device="cuda")
+        # a span longer than the whole allocation segment is rejected before launch
+        st = L.curandGenerateUniform(g, C.c_void_p(small.data_ptr()), 1 << 40)
+        assert st == capi.CURAND_STATUS_ALLOCATION_FAILED

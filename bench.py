@@ -41,7 +41,7 @@ BYTES_PER_STEP = 2 * BYTES_PER_CALL
 METRIC = ("RNG HBM GB/s: Philox4x32-10 curandGenerateUniform + curandGenerateNormal, "
           "2^30 fp32 each, seed 1234")
 UNIT = "GB/s"
-CPU_SAMPLE_WORDS = 1 << 25  # per call, per CPU step (bounded sample)
+CPU_SAMPLE_WORDS = 1 << 30  # per call: the full config size (about 1.5 s on 16 host cores)
 
 
 def _peaks() -> dict:
@@ -312,9 +312,16 @@ def main() -> None:
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--words", type=int, default=None,
+                    help="override words per call (smaller cases for profiling)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
+    if args.words:
+        global N_WORDS, BYTES_PER_CALL, BYTES_PER_STEP
+        N_WORDS = args.words
+        BYTES_PER_CALL = 4 * N_WORDS
+        BYTES_PER_STEP = 2 * BYTES_PER_CALL
     if args.impl == "reference":
         run_reference(args)
     else:

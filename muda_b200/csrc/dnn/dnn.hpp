@@ -1,0 +1,49 @@
+// dnn.hpp — launch interface of the convolution and softmax kernels.
+#pragma once
+
+#include <cuda_runtime_api.h>
+
+#include <cstdint>
+
+namespace mb200::dnn {
+
+// Element-strided 4-D view (n, c, h, w) — the reference's tensor descriptor
+// strides (libraries/dnn/src/cudnn_descriptors.hpp:19-43).
+struct View4 {
+  int n, c, h, w;
+  std::int64_t ns, cs, hs, ws;
+};
+
+enum class SoftmaxAlgo : int { kFast = 0, kAccurate = 1, kLog = 2 };
+
+// Softmax over rows of `len` contiguous floats, rows `len` apart:
+// y = alpha * softmax(x) + beta * y (beta == 0: y is not read).
+cudaError_t launch_softmax_rows(const float* x, float* y, std::int64_t rows, std::int64_t len,
+                                SoftmaxAlgo algo, float alpha, float beta,
+                                cudaStream_t stream) noexcept;
+
+// Softmax over the channel axis of an arbitrary strided tensor (one reduction per
+// (n, h, w) position), or over whole (c, h, w) instances when `instance` is true.
+cudaError_t launch_softmax_strided(const float* x, const View4& xv, float* y, const View4& yv,
+                                   bool instance, SoftmaxAlgo algo, float alpha, float beta,
+                                   cudaStream_t stream) noexcept;
+
+// Convolution geometry shared by every conv kernel; mirrors the parameter block
+// the reference packs in BuildConvParams (libraries/dnn/src/cudnn_ops.mm:26-83).
+struct ConvShape {
+  View4 x;        // input  (n, c_in, h_in, w_in)
+  View4 y;        // output (n, c_out, h_out, w_out)
+  int kh, kw;     // filter spatial size
+  int pad_h, pad_w, stride_h, stride_w, dil_h, dil_w;
+  int groups;
+  bool filter_krsc;   // true: filter laid out (k, r, s, c) — NHWC; false: (k, c, r, s)
+  bool convolution;   // true: CUDNN_CONVOLUTION (filter flipped); false: cross-correlation
+};
+
+enum class ConvDtype : int { kF32 = 0, kBF16 = 1 };
+
+// Direct convolution, any geometry: one thread per output element, fp32 accumulate.
+cudaError_t launch_conv_direct(const void* x, const void* w, void* y, const ConvShape& s,
+                               ConvDtype dt, float alpha, float beta, cudaStream_t stream) noexcept;
+
+}  // namespace mb200::dnn

@@ -33,6 +33,9 @@ ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 # library name -> sources relative to csrc/
 LIBS: dict[str, list[str]] = {
     "curand": ["rand/curand_api.cpp", "rand/philox_kernels.cu"],
+    "cudnn": ["dnn/cudnn_api.cpp", "dnn/softmax_kernels.cu", "dnn/conv_direct_kernels.cu",
+              "dnn/conv_dispatch.cu"],
+    "cusparse": ["sparse/cusparse_api.cpp", "sparse/spmv_kernels.cu"],
 }
 
 COMMON_FLAGS = ["-O3", "-std=c++17", f"-I{INCLUDE}", f"-I{CSRC}"]

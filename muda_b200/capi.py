@@ -75,10 +75,104 @@ def curand() -> C.CDLL:
     return _declare(_load("curand"), CURAND_PROTOS)
 
 
+# ------------------------------------------------------------------- cuDNN --
+CUDNN_STATUS_SUCCESS = 0
+CUDNN_STATUS_BAD_PARAM = 3
+CUDNN_STATUS_EXECUTION_FAILED = 8
+CUDNN_STATUS_NOT_SUPPORTED = 9
+CUDNN_DATA_FLOAT = 0
+CUDNN_DATA_DOUBLE = 1
+CUDNN_DATA_HALF = 2
+CUDNN_DATA_BFLOAT16 = 9
+CUDNN_TENSOR_NCHW = 0
+CUDNN_TENSOR_NHWC = 1
+CUDNN_CONVOLUTION = 0
+CUDNN_CROSS_CORRELATION = 1
+CUDNN_SOFTMAX_FAST = 0
+CUDNN_SOFTMAX_ACCURATE = 1
+CUDNN_SOFTMAX_LOG = 2
+CUDNN_SOFTMAX_MODE_INSTANCE = 0
+CUDNN_SOFTMAX_MODE_CHANNEL = 1
+
+_ip = P(i32)
+CUDNN_PROTOS = {
+    "cudnnGetVersion": ([], sz),
+    "cudnnGetErrorString": ([i32], C.c_char_p),
+    "cudnnCreate": ([P(vp)], i32),
+    "cudnnDestroy": ([vp], i32),
+    "cudnnSetStream": ([vp, vp], i32),
+    "cudnnGetStream": ([vp, P(vp)], i32),
+    "cudnnCreateTensorDescriptor": ([P(vp)], i32),
+    "cudnnSetTensor4dDescriptor": ([vp, i32, i32, i32, i32, i32, i32], i32),
+    "cudnnSetTensor4dDescriptorEx": ([vp, i32, i32, i32, i32, i32, i32, i32, i32, i32], i32),
+    "cudnnGetTensor4dDescriptor": ([vp, _ip, _ip, _ip, _ip, _ip, _ip, _ip, _ip, _ip], i32),
+    "cudnnDestroyTensorDescriptor": ([vp], i32),
+    "cudnnCreateFilterDescriptor": ([P(vp)], i32),
+    "cudnnSetFilter4dDescriptor": ([vp, i32, i32, i32, i32, i32, i32], i32),
+    "cudnnGetFilter4dDescriptor": ([vp, _ip, _ip, _ip, _ip, _ip, _ip], i32),
+    "cudnnDestroyFilterDescriptor": ([vp], i32),
+    "cudnnCreateConvolutionDescriptor": ([P(vp)], i32),
+    "cudnnSetConvolution2dDescriptor": ([vp, i32, i32, i32, i32, i32, i32, i32, i32], i32),
+    "cudnnSetConvolutionGroupCount": ([vp, i32], i32),
+    "cudnnGetConvolutionGroupCount": ([vp, _ip], i32),
+    "cudnnGetConvolution2dForwardOutputDim": ([vp, vp, vp, _ip, _ip, _ip, _ip], i32),
+    "cudnnDestroyConvolutionDescriptor": ([vp], i32),
+    "cudnnGetConvolutionForwardWorkspaceSize": ([vp, vp, vp, vp, vp, i32, P(sz)], i32),
+    "cudnnConvolutionForward": ([vp, vp, vp, vp, vp, vp, vp, i32, vp, sz, vp, vp, vp], i32),
+    "cudnnSoftmaxForward": ([vp, i32, i32, vp, vp, vp, vp, vp, vp], i32),
+}
+
+
+@lru_cache(maxsize=None)
+def cudnn() -> C.CDLL:
+    return _declare(_load("cudnn"), CUDNN_PROTOS)
+
+
+# ---------------------------------------------------------------- cuSPARSE --
+CUSPARSE_STATUS_SUCCESS = 0
+CUSPARSE_STATUS_NOT_INITIALIZED = 1
+CUSPARSE_STATUS_INVALID_VALUE = 3
+CUSPARSE_STATUS_NOT_SUPPORTED = 10
+CUSPARSE_OPERATION_NON_TRANSPOSE = 0
+CUSPARSE_OPERATION_TRANSPOSE = 1
+CUSPARSE_INDEX_32I = 2
+CUSPARSE_INDEX_64I = 3
+CUSPARSE_INDEX_BASE_ZERO = 0
+CUSPARSE_INDEX_BASE_ONE = 1
+CUDA_R_32F = 0
+CUDA_R_16F = 2
+CUDA_R_16BF = 14
+
+CUSPARSE_PROTOS = {
+    "cusparseCreate": ([P(vp)], i32),
+    "cusparseDestroy": ([vp], i32),
+    "cusparseGetVersion": ([vp, P(i32)], i32),
+    "cusparseSetStream": ([vp, vp], i32),
+    "cusparseGetStream": ([vp, P(vp)], i32),
+    "cusparseGetErrorName": ([i32], C.c_char_p),
+    "cusparseGetErrorString": ([i32], C.c_char_p),
+    "cusparseCreateCsr": ([P(vp), i64, i64, i64, vp, vp, vp, i32, i32, i32, i32], i32),
+    "cusparseDestroySpMat": ([vp], i32),
+    "cusparseCreateDnVec": ([P(vp), i64, vp, i32], i32),
+    "cusparseDestroyDnVec": ([vp], i32),
+    "cusparseSpMV_bufferSize": ([vp, i32, vp, vp, vp, vp, vp, i32, i32, P(sz)], i32),
+    "cusparseSpMV": ([vp, i32, vp, vp, vp, vp, vp, i32, i32, vp], i32),
+}
+
+
+@lru_cache(maxsize=None)
+def cusparse() -> C.CDLL:
+    return _declare(_load("cusparse"), CUSPARSE_PROTOS)
+
+
 ALL_PROTOS: dict[str, dict[str, tuple[list, object]]] = {
     "curand": CURAND_PROTOS,
+    "cudnn": CUDNN_PROTOS,
+    "cusparse": CUSPARSE_PROTOS,
 }
 
 LOADERS = {
     "curand": curand,
+    "cudnn": cudnn,
+    "cusparse": cusparse,
 }

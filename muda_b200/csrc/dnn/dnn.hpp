@@ -46,4 +46,11 @@ enum class ConvDtype : int { kF32 = 0, kBF16 = 1 };
 cudaError_t launch_conv_direct(const void* x, const void* w, void* y, const ConvShape& s,
                                ConvDtype dt, float alpha, float beta, cudaStream_t stream) noexcept;
 
+// Picks the fastest kernel that supports the geometry and launches it.
+cudaError_t launch_conv(const void* x, const void* w, void* y, const ConvShape& s, ConvDtype dt,
+                        float alpha, float beta, cudaStream_t stream) noexcept;
+
+// Name of the kernel family launch_conv would use (for tests and benchmarks).
+const char* conv_path_name(const ConvShape& s, ConvDtype dt) noexcept;
+
 }  // namespace mb200::dnn

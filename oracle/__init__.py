@@ -92,3 +92,92 @@ def philox_gather(ctrs: np.ndarray, seed: int, threads: int = 8) -> np.ndarray:
     lib().oracle_philox_gather(_ptr(ctrs, C.c_uint64), len(ctrs), seed, _ptr(out, C.c_uint32),
                                threads)
     return out
+
+
+# ------------------------------------------------------------- conv/softmax --
+def _nchw_strides(shape, fmt: str):
+    n, c, h, w = shape
+    if fmt == "NCHW":
+        return (c * h * w, h * w, w, 1)
+    return (h * w * c, 1, w * c, c)  # NHWC
+
+
+def conv2d(x: np.ndarray, w: np.ndarray, xshape, wshape, *, x_fmt="NCHW", w_fmt="NCHW",
+           pad=(0, 0), stride=(1, 1), dil=(1, 1), groups=1, mode="cross", alpha=1.0,
+           beta=0.0, y: np.ndarray | None = None, y_fmt=None, accum_f64=False,
+           threads: int = 8) -> np.ndarray:
+    """Reference direct convolution (cudnn_kernels.metal:20-62) on flat buffers.
+
+    xshape = (n, c, h, w); wshape = (k, c/groups, r, s) logical; layouts by format
+    strings; x/w/y dtype float32 or bfloat16-as-uint16 (then the result is bf16)."""
+    from oracle.protos import ConvParams
+    n, c, h, wd = xshape
+    k, cg, r, s = wshape
+    oh = 1 + (h + 2 * pad[0] - (1 + (r - 1) * dil[0])) // stride[0]
+    ow = 1 + (wd + 2 * pad[1] - (1 + (s - 1) * dil[1])) // stride[1]
+    y_fmt = y_fmt or x_fmt
+    bf16 = x.dtype == np.uint16
+    if y is None:
+        y = np.zeros(n * k * oh * ow, dtype=x.dtype)
+    xs = _nchw_strides(xshape, x_fmt)
+    ys = _nchw_strides((n, k, oh, ow), y_fmt)
+    p = ConvParams(n, c, h, wd, *xs, k, oh, ow, groups, *ys, r, s, pad[0], pad[1], stride[0],
+                   stride[1], dil[0], dil[1], 0 if w_fmt == "NCHW" else 1,
+                   0 if mode == "conv" else 1, alpha, beta)
+    x = np.ascontiguousarray(x)
+    w = np.ascontiguousarray(w)
+    lib().oracle_conv2d_fwd(x.ctypes.data, w.ctypes.data, y.ctypes.data, C.byref(p), int(bf16),
+                            int(accum_f64), threads)
+    return y
+
+
+def softmax(x: np.ndarray, shape, *, algo: int = 1, channel: bool = False, alpha=1.0, beta=0.0,
+            y: np.ndarray | None = None, x_strides=None, y_strides=None,
+            threads: int = 8) -> np.ndarray:
+    """Reference softmax forward (cudnn_ops.mm:656-719 dispatch) on flat float32 buffers."""
+    from oracle.protos import Tensor4
+    n, c, h, w = shape
+    xs = x_strides or _nchw_strides(shape, "NCHW")
+    ys = y_strides or xs
+    if y is None:
+        y = np.zeros_like(x)
+    X = Tensor4(n, c, h, w, *xs)
+    Y = Tensor4(n, c, h, w, *ys)
+    lib().oracle_softmax_fwd(_ptr(x, C.c_float), _ptr(y, C.c_float), C.byref(X), C.byref(Y),
+                             algo, int(channel), alpha, beta, threads)
+    return y
+
+
+def spmv_csr(row_offsets, col_ind, values, x, *, base=0, alpha=1.0, beta=0.0, y=None,
+             with_abs=False, threads: int = 8):
+    """Reference thread-per-row CSR SpMV (cusparse_kernels.metal:54-77).
+
+    Returns y, or with with_abs=True (y, exact row result in float64, |A||x| per row
+    in float64)."""
+    ro = np.ascontiguousarray(row_offsets, dtype=np.int32)
+    ci = np.ascontiguousarray(col_ind, dtype=np.int32)
+    va = np.ascontiguousarray(values, dtype=np.float32)
+    xx = np.ascontiguousarray(x, dtype=np.float32)
+    rows = len(ro) - 1
+    y = np.zeros(rows, np.float32) if y is None else y
+    absr = np.zeros(rows, np.float64) if with_abs else None
+    exact = np.zeros(rows, np.float64) if with_abs else None
+    lib().oracle_spmv_csr(rows, ro.ctypes.data, ci.ctypes.data, va.ctypes.data, base,
+                          xx.ctypes.data, y.ctypes.data, alpha, beta,
+                          exact.ctypes.data if with_abs else None,
+                          absr.ctypes.data if with_abs else None, threads)
+    return (y, exact, absr) if with_abs else y
+
+
+def bf16_bits(a: np.ndarray) -> np.ndarray:
+    """float32 -> bfloat16 bit patterns (round to nearest even)."""
+    u = np.ascontiguousarray(a, dtype=np.float32).view(np.uint32).astype(np.uint64)
+    r = ((u + 0x7FFF + ((u >> 16) & 1)) >> 16).astype(np.uint16)
+    nan = np.isnan(a)
+    if nan.any():
+        r[nan] = 0x7FC0
+    return r
+
+
+def bf16_to_f32(b: np.ndarray) -> np.ndarray:
+    return (b.astype(np.uint32) << 16).view(np.float32)

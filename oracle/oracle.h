@@ -40,6 +40,40 @@ uint64_t oracle_generate_normal(uint64_t seed, uint64_t offset, float* out, size
 void oracle_philox_gather(const uint64_t* ctrs, size_t m, uint64_t seed, uint32_t* out,
                           int threads);
 
+/* ---- convolution / softmax (libraries/dnn/shaders/cudnn_kernels.metal) ---- */
+/* Geometry of one convolution; field meaning as in libraries/dnn/src/cudnn_kernel_params.h:8-37
+ * (element strides; w_format 0 = KCRS, 1 = KRSC; conv_mode 0 = CONVOLUTION, 1 = CROSS_CORRELATION). */
+typedef struct {
+  int n, c_in, h_in, w_in;
+  int64_t x_ns, x_cs, x_hs, x_ws;
+  int c_out, h_out, w_out, groups;
+  int64_t y_ns, y_cs, y_hs, y_ws;
+  int kh, kw, pad_h, pad_w, stride_h, stride_w, dil_h, dil_w;
+  int w_format, conv_mode;
+  float alpha, beta;
+} OracleConvParams;
+
+typedef struct {
+  int n, c, h, w;
+  int64_t ns, cs, hs, ws;
+} OracleTensor4;
+
+float oracle_bf16_round(float v);
+/* bf16 != 0: x, w, y are bf16 (widened exactly, result rounded to nearest even).
+ * accum_f64 != 0: accumulate in double (ground truth) instead of the sequential fp32 fma. */
+void oracle_conv2d_fwd(const void* x, const void* w, void* y, const OracleConvParams* p, int bf16,
+                       int accum_f64, int threads);
+/* ---- CSR SpMV (libraries/sparse/shaders/cusparse_kernels.metal:54-77) ---- */
+/* exact_row (optional): alpha * sum a_k x_col + beta * y in double;
+ * abs_row (optional): per-row sum |a_k * x_col| in double. */
+void oracle_spmv_csr(int64_t rows, const int32_t* row_offsets, const int32_t* col_ind,
+                     const float* values, int base, const float* x, float* y, float alpha,
+                     float beta, double* exact_row, double* abs_row, int threads);
+
+/* algo 0 FAST, 1 ACCURATE, 2 LOG; mode_channel 0 INSTANCE, 1 CHANNEL. */
+void oracle_softmax_fwd(const float* x, float* y, const OracleTensor4* xd, const OracleTensor4* yd,
+                        int algo, int mode_channel, float alpha, float beta, int threads);
+
 #ifdef __cplusplus
 }
 #endif

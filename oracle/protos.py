@@ -5,6 +5,39 @@ from __future__ import annotations
 import ctypes as C
 
 
+class ConvParams(C.Structure):
+    """Mirror of OracleConvParams in oracle/oracle.h."""
+    _fields_ = [
+        ("n", C.c_int), ("c_in", C.c_int), ("h_in", C.c_int), ("w_in", C.c_int),
+        ("x_ns", C.c_int64), ("x_cs", C.c_int64), ("x_hs", C.c_int64), ("x_ws", C.c_int64),
+        ("c_out", C.c_int), ("h_out", C.c_int), ("w_out", C.c_int), ("groups", C.c_int),
+        ("y_ns", C.c_int64), ("y_cs", C.c_int64), ("y_hs", C.c_int64), ("y_ws", C.c_int64),
+        ("kh", C.c_int), ("kw", C.c_int), ("pad_h", C.c_int), ("pad_w", C.c_int),
+        ("stride_h", C.c_int), ("stride_w", C.c_int), ("dil_h", C.c_int), ("dil_w", C.c_int),
+        ("w_format", C.c_int), ("conv_mode", C.c_int),
+        ("alpha", C.c_float), ("beta", C.c_float),
+    ]
+
+
+class Tensor4(C.Structure):
+    """Mirror of OracleTensor4 in oracle/oracle.h."""
+    _fields_ = [("n", C.c_int), ("c", C.c_int), ("h", C.c_int), ("w", C.c_int),
+                ("ns", C.c_int64), ("cs", C.c_int64), ("hs", C.c_int64), ("ws", C.c_int64)]
+
+
+vp = C.c_void_p
+fp = C.POINTER(C.c_float)
+
+_PROTOS: list[tuple[str, list, object]] = [
+    ("oracle_bf16_round", [C.c_float], C.c_float),
+    ("oracle_conv2d_fwd", [vp, vp, vp, C.POINTER(ConvParams), C.c_int, C.c_int, C.c_int], None),
+    ("oracle_softmax_fwd", [fp, fp, C.POINTER(Tensor4), C.POINTER(Tensor4), C.c_int, C.c_int,
+                            C.c_float, C.c_float, C.c_int], None),
+    ("oracle_spmv_csr", [C.c_int64, vp, vp, vp, C.c_int, vp, vp, C.c_float, C.c_float, vp,
+                         vp, C.c_int], None),
+]
+
+
 def declare(L: C.CDLL) -> None:
     for name, argtypes, restype in _PROTOS:
         fn = getattr(L, name, None)
@@ -12,6 +45,3 @@ def declare(L: C.CDLL) -> None:
             continue
         fn.argtypes = argtypes
         fn.restype = restype
-
-
-_PROTOS: list[tuple[str, list, object]] = []

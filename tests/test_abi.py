@@ -15,6 +15,8 @@ INCLUDE = Path(__file__).resolve().parent.parent / "include"
 
 HEADER_LIB = {
     "curand.h": "curand",
+    "cudnn.h": "cudnn",
+    "cusparse.h": "cusparse",
 }
 
 

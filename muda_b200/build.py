@@ -36,6 +36,7 @@ LIBS: dict[str, list[str]] = {
     "cudnn": ["dnn/cudnn_api.cpp", "dnn/softmax_kernels.cu", "dnn/conv_direct_kernels.cu",
               "dnn/conv_dispatch.cu"],
     "cusparse": ["sparse/cusparse_api.cpp", "sparse/spmv_kernels.cu"],
+    "cufft": ["fft/cufft_api.cpp", "fft/stockham_kernels.cu", "fft/dft_kernels.cu"],
 }
 
 COMMON_FLAGS = ["-O3", "-std=c++17", f"-I{INCLUDE}", f"-I{CSRC}"]

@@ -165,14 +165,50 @@ def cusparse() -> C.CDLL:
     return _declare(_load("cusparse"), CUSPARSE_PROTOS)
 
 
+# ------------------------------------------------------------------- cuFFT --
+CUFFT_SUCCESS = 0
+CUFFT_INVALID_PLAN = 1
+CUFFT_INVALID_TYPE = 3
+CUFFT_INVALID_VALUE = 4
+CUFFT_EXEC_FAILED = 6
+CUFFT_INVALID_SIZE = 8
+CUFFT_NOT_SUPPORTED = 16
+CUFFT_FORWARD = -1
+CUFFT_INVERSE = 1
+CUFFT_R2C = 0x2A
+CUFFT_C2R = 0x2C
+CUFFT_C2C = 0x29
+CUFFT_Z2Z = 0x69
+
+CUFFT_PROTOS = {
+    "cufftCreate": ([P(vp)], i32),
+    "cufftPlan1d": ([P(vp), i32, i32, i32], i32),
+    "cufftPlanMany": ([P(vp), i32, P(i32), P(i32), i32, i32, P(i32), i32, i32, i32, i32], i32),
+    "cufftMakePlan1d": ([vp, i32, i32, i32, P(sz)], i32),
+    "cufftMakePlanMany": ([vp, i32, P(i32), P(i32), i32, i32, P(i32), i32, i32, i32, i32, P(sz)],
+                          i32),
+    "cufftSetStream": ([vp, vp], i32),
+    "cufftGetSize": ([vp, P(sz)], i32),
+    "cufftDestroy": ([vp], i32),
+    "cufftExecC2C": ([vp, vp, vp, i32], i32),
+}
+
+
+@lru_cache(maxsize=None)
+def cufft() -> C.CDLL:
+    return _declare(_load("cufft"), CUFFT_PROTOS)
+
+
 ALL_PROTOS: dict[str, dict[str, tuple[list, object]]] = {
     "curand": CURAND_PROTOS,
     "cudnn": CUDNN_PROTOS,
     "cusparse": CUSPARSE_PROTOS,
+    "cufft": CUFFT_PROTOS,
 }
 
 LOADERS = {
     "curand": curand,
     "cudnn": cudnn,
     "cusparse": cusparse,
+    "cufft": cufft,
 }

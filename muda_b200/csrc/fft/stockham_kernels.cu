@@ -1,0 +1,315 @@
+// stockham_kernels.cu — single-pass batched C2C FFT for power-of-two lengths (sm_100a).
+//
+// Conventions of the reference (libraries/fft/src/cufft_exec.mm): X[k] =
+// sum_n x[n] exp(sign * 2*pi*i * n*k / N), sign -1 forward / +1 inverse, no
+// scaling, in-place allowed.  The reference runs one radix-2 Stockham stage per
+// launch over global memory (cufft_kernels.metal:255-296, cufft_exec.mm:58-74:
+// 12 read+write passes of the whole batch for N = 4096, plus gather and scatter).
+//
+// Here one CTA owns whole transforms and performs every stage on chip:
+//   - mixed-radix Stockham autosort (the formulation of Govindaraju et al.,
+//     "High Performance Discrete Fourier Transforms on Graphics Processors",
+//     SC 2008): pass p with radix R and span Ns reads v[r] = d[j + r*N/R],
+//     multiplies by exp(sign*2*pi*i * r*(j mod Ns) / (Ns*R)), does an R-point DFT in
+//     registers, and writes d'[(j / Ns)*Ns*R + (j mod Ns) + r*Ns];
+//   - radix 16 (4 x 4 in registers) for all passes but possibly the first, so
+//     N = 4096 takes three passes: global -> registers -> shared -> registers ->
+//     shared -> registers -> global.  Each element is read from and written to
+//     HBM exactly once per transform;
+//   - first-pass loads and last-pass stores are coalesced across the threads of a
+//     transform for unit stride (thread j touches elements j + r*N/R);
+//   - shared memory holds real and imaginary parts in separate arrays with one
+//     pad word per 16, which makes the stride-16 scatter of the first pass
+//     conflict free;
+//   - twiddles come from a table exp(-2*pi*i*m/N) computed in double on the host
+//     and rounded once (conjugated for the inverse), not from sincos per
+//     butterfly.
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+#include "common/device.hpp"
+#include "fft/fft.hpp"
+
+namespace mb200::fft {
+namespace {
+
+__device__ __forceinline__ float2 cadd(float2 a, float2 b) { return make_float2(a.x + b.x, a.y + b.y); }
+__device__ __forceinline__ float2 csub(float2 a, float2 b) { return make_float2(a.x - b.x, a.y - b.y); }
+__device__ __forceinline__ float2 cmul(float2 a, float2 b) {
+  return make_float2(fmaf(a.x, b.x, -a.y * b.y), fmaf(a.x, b.y, a.y * b.x));
+}
+// multiply by S*i
+template <int S>
+__device__ __forceinline__ float2 mul_si(float2 a) {
+  return S < 0 ? make_float2(a.y, -a.x) : make_float2(-a.y, a.x);
+}
+
+// exp(S * 2*pi*i * m / 16) for a compile-time m.
+template <int S, int M>
+__device__ __forceinline__ float2 rot16(float2 a) {
+  constexpr int m = M & 15;
+  constexpr float kC[16] = {1.0f, 0.9238795042037964f, 0.7071067690849304f, 0.3826834261417389f,
+                            0.0f, -0.3826834261417389f, -0.7071067690849304f, -0.9238795042037964f,
+                            -1.0f, -0.9238795042037964f, -0.7071067690849304f, -0.3826834261417389f,
+                            0.0f, 0.3826834261417389f, 0.7071067690849304f, 0.9238795042037964f};
+  constexpr float kS[16] = {0.0f, 0.3826834261417389f, 0.7071067690849304f, 0.9238795042037964f,
+                            1.0f, 0.9238795042037964f, 0.7071067690849304f, 0.3826834261417389f,
+                            0.0f, -0.3826834261417389f, -0.7071067690849304f, -0.9238795042037964f,
+                            -1.0f, -0.9238795042037964f, -0.7071067690849304f, -0.3826834261417389f};
+  if constexpr (m == 0) {
+    return a;
+  } else if constexpr (m == 4) {
+    return mul_si<S>(a);
+  } else if constexpr (m == 8) {
+    return make_float2(-a.x, -a.y);
+  } else if constexpr (m == 12) {
+    return mul_si<-S>(a);
+  } else {
+    return cmul(a, make_float2(kC[m], S * kS[m]));
+  }
+}
+
+// In-register R-point DFT, natural order in and out: v[k] <- sum_n v[n] W_R^{S n k}.
+template <int R, int S>
+__device__ __forceinline__ void dft(float2* v);
+
+template <int S, int R, int A, int B, int N2 = 0, int K1 = 0>
+__device__ __forceinline__ void twiddle_step(float2 (&y)[R]) {
+  if constexpr (N2 < B) {
+    if constexpr (K1 < A) {
+      y[N2 * A + K1] = rot16<S, (16 / R) * N2 * K1>(y[N2 * A + K1]);
+      twiddle_step<S, R, A, B, N2, K1 + 1>(y);
+    } else {
+      twiddle_step<S, R, A, B, N2 + 1, 0>(y);
+    }
+  }
+}
+
+template <int R, int S>
+__device__ __forceinline__ void dft(float2* v) {
+  if constexpr (R == 2) {
+    const float2 a = v[0], b = v[1];
+    v[0] = cadd(a, b);
+    v[1] = csub(a, b);
+  } else if constexpr (R == 4) {
+    const float2 a = cadd(v[0], v[2]), b = csub(v[0], v[2]);
+    const float2 c = cadd(v[1], v[3]), d = mul_si<S>(csub(v[1], v[3]));
+    v[0] = cadd(a, c);
+    v[2] = csub(a, c);
+    v[1] = cadd(b, d);
+    v[3] = csub(b, d);
+  } else {
+    // R = A * B; n = B*n1 + n2, k = k1 + A*k2:
+    //   Y[n2][k1] = W_R^{n2 k1} * sum_{n1} x[B n1 + n2] W_A^{n1 k1}
+    //   X[k1 + A k2] = sum_{n2} Y[n2][k1] W_B^{n2 k2}
+    constexpr int A = (R == 8) ? 2 : 4;
+    constexpr int B = R / A;
+    float2 y[R];
+#pragma unroll
+    for (int n2 = 0; n2 < B; ++n2) {
+      float2 s[A];
+#pragma unroll
+      for (int n1 = 0; n1 < A; ++n1) s[n1] = v[B * n1 + n2];
+      dft<A, S>(s);
+#pragma unroll
+      for (int k1 = 0; k1 < A; ++k1) y[n2 * A + k1] = s[k1];
+    }
+    twiddle_step<S, R, A, B>(y);
+#pragma unroll
+    for (int k1 = 0; k1 < A; ++k1) {
+      float2 s[B];
+#pragma unroll
+      for (int n2 = 0; n2 < B; ++n2) s[n2] = y[n2 * A + k1];
+      dft<B, S>(s);
+#pragma unroll
+      for (int k2 = 0; k2 < B; ++k2) v[k1 + A * k2] = s[k2];
+    }
+  }
+}
+
+template <int S>
+__device__ __forceinline__ float2 table_tw(const float2* __restrict__ tw, std::int64_t m) {
+  float2 w = __ldg(tw + m);
+  if (S > 0) w.y = -w.y;
+  return w;
+}
+
+// Compile-time plan of a length-N transform.
+template <int LOG2N>
+struct Plan {
+  static constexpr int N = 1 << LOG2N;
+  static constexpr int P = N >= 16 ? 16 : N;                 // points per thread
+  static constexpr int T = N / P;                            // threads per transform
+  static constexpr int TPC = T >= 256 ? 1 : 256 / T;         // transforms per CTA
+  static constexpr int THREADS = T * TPC;
+  static constexpr int FIRST_R = (LOG2N % 4 == 0) ? (N >= 16 ? 16 : N) : (1 << (LOG2N % 4));
+  static constexpr int PASSES = (LOG2N % 4 == 0) ? LOG2N / 4 : LOG2N / 4 + 1;
+  static constexpr int REGION = N + N / 16;                  // padded floats per transform
+  static constexpr int SMEM = PASSES > 1 ? TPC * REGION * 2 * 4 : 0;
+  // Resident CTAs per SM the register budget is sized for: several CTAs per SM
+  // let one CTA's HBM loads overlap another's on-chip passes.
+  static constexpr int MIN_CTAS = THREADS >= 1024 ? 1 : (THREADS >= 512 ? 2 : 3);
+};
+
+struct Ctx {
+  const float2* in;
+  float2* out;
+  std::int64_t in_stride, out_stride;
+  bool active;
+  std::int64_t inner;  // b % inner_count (post-twiddle row)
+};
+
+__device__ __forceinline__ int pad(int i) { return i + (i >> 4); }
+
+__host__ __device__ constexpr int ilog2(int v) { return v <= 1 ? 0 : 1 + ilog2(v >> 1); }
+
+// One Stockham pass.  FIRST reads global memory, LAST writes global memory,
+// the others go through shared memory (sre/sim).
+template <int LOG2N, int R, int S, bool FIRST, bool LAST>
+__device__ __forceinline__ void pass(float2 (&v)[Plan<LOG2N>::P], int j, int Ns, int log2Ns,
+                                     const Ctx& c, float* sre, float* sim,
+                                     const float2* __restrict__ tw,
+                                     const float2* __restrict__ post_tw, std::int64_t post_n) {
+  using PL = Plan<LOG2N>;
+  constexpr int N = PL::N;
+  constexpr int T = PL::T;
+  constexpr int NB = PL::P / R;  // butterflies per thread
+#pragma unroll
+  for (int q = 0; q < NB; ++q) {
+    const int b = j + q * T;
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      const int idx = b + r * (N / R);
+      if constexpr (FIRST) {
+        v[q * R + r] = c.active ? c.in[idx * c.in_stride] : make_float2(0.0f, 0.0f);
+      } else {
+        v[q * R + r] = make_float2(sre[pad(idx)], sim[pad(idx)]);
+      }
+    }
+  }
+  if constexpr (!FIRST) __syncthreads();  // all reads done before the region is rewritten
+#pragma unroll
+  for (int q = 0; q < NB; ++q) {
+    const int b = j + q * T;
+    const int k = b & (Ns - 1);
+    if (Ns > 1) {
+      // exp(S*2*pi*i * r*k/(Ns*R)) = table[r*k*N/(Ns*R)]
+      const int shift = LOG2N - log2Ns - ilog2(R);
+#pragma unroll
+      for (int r = 1; r < R; ++r)
+        v[q * R + r] = cmul(v[q * R + r], table_tw<S>(tw, (r * k) << shift));
+    }
+    dft<R, S>(&v[q * R]);
+    const int idxD = ((b >> log2Ns) << (log2Ns + ilog2(R))) + k;
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      const int o = idxD + r * Ns;
+      if constexpr (LAST) {
+        if (c.active) {
+          float2 val = v[q * R + r];
+          if (post_tw != nullptr)
+            val = cmul(val, table_tw<S>(post_tw, (c.inner * o) % post_n));
+          c.out[o * c.out_stride] = val;
+        }
+      } else {
+        sre[pad(o)] = v[q * R + r].x;
+        sim[pad(o)] = v[q * R + r].y;
+      }
+    }
+  }
+  if constexpr (!LAST) __syncthreads();
+}
+
+template <int LOG2N, int S, int PASS = 0>
+__device__ __forceinline__ void run_passes(float2 (&v)[Plan<LOG2N>::P], int j, const Ctx& c,
+                                           float* sre, float* sim, const float2* tw,
+                                           const float2* post_tw, std::int64_t post_n) {
+  using PL = Plan<LOG2N>;
+  if constexpr (PASS < PL::PASSES) {
+    constexpr int R = (PASS == 0) ? PL::FIRST_R : 16;
+    constexpr int LOG2NS = (PASS == 0) ? 0 : (ilog2(PL::FIRST_R) + 4 * (PASS - 1));
+    pass<LOG2N, R, S, PASS == 0, PASS == PL::PASSES - 1>(v, j, 1 << LOG2NS, LOG2NS, c, sre, sim,
+                                                         tw, post_tw, post_n);
+    run_passes<LOG2N, S, PASS + 1>(v, j, c, sre, sim, tw, post_tw, post_n);
+  }
+}
+
+template <int LOG2N, int S>
+__global__ void __launch_bounds__(Plan<LOG2N>::THREADS, Plan<LOG2N>::MIN_CTAS)
+    stockham_kernel(const Batch1D bt) {
+  using PL = Plan<LOG2N>;
+  extern __shared__ float smem[];
+  const int tloc = threadIdx.x / PL::T;
+  const int j = threadIdx.x % PL::T;
+  float* sre = smem + tloc * PL::REGION * 2;
+  float* sim = sre + PL::REGION;
+  for (std::int64_t t0 = static_cast<std::int64_t>(blockIdx.x) * PL::TPC; t0 < bt.batch;
+       t0 += static_cast<std::int64_t>(gridDim.x) * PL::TPC) {
+    const std::int64_t tr = t0 + tloc;
+    Ctx c;
+    c.active = tr < bt.batch;
+    const std::int64_t outer = c.active ? tr / bt.inner_count : 0;
+    c.inner = c.active ? tr % bt.inner_count : 0;
+    c.in = bt.in + outer * bt.in_outer + c.inner * bt.in_inner;
+    c.out = bt.out + outer * bt.out_outer + c.inner * bt.out_inner;
+    c.in_stride = bt.in_stride;
+    c.out_stride = bt.out_stride;
+    float2 v[PL::P];
+    run_passes<LOG2N, S>(v, j, c, sre, sim, bt.tw, bt.post_tw, bt.post_n);
+  }
+}
+
+template <int LOG2N, int S>
+cudaError_t launch_len(const Batch1D& b, cudaStream_t stream) {
+  using PL = Plan<LOG2N>;
+  auto kern = stockham_kernel<LOG2N, S>;
+  if (PL::SMEM > 48 * 1024) {
+    const cudaError_t e =
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, PL::SMEM);
+    if (e != cudaSuccess) return e;
+  }
+  const std::int64_t ctas = (b.batch + PL::TPC - 1) / PL::TPC;
+  const int sms = sm_count(current_device());
+  const std::int64_t cap = static_cast<std::int64_t>(sms > 0 ? sms : 148) * 64;
+  const unsigned grid = static_cast<unsigned>(ctas < cap ? ctas : cap);
+  kern<<<grid, PL::THREADS, PL::SMEM, stream>>>(b);
+  return cudaGetLastError();
+}
+
+template <int S>
+cudaError_t dispatch(int log2n, const Batch1D& b, cudaStream_t st) {
+  switch (log2n) {
+    case 1: return launch_len<1, S>(b, st);
+    case 2: return launch_len<2, S>(b, st);
+    case 3: return launch_len<3, S>(b, st);
+    case 4: return launch_len<4, S>(b, st);
+    case 5: return launch_len<5, S>(b, st);
+    case 6: return launch_len<6, S>(b, st);
+    case 7: return launch_len<7, S>(b, st);
+    case 8: return launch_len<8, S>(b, st);
+    case 9: return launch_len<9, S>(b, st);
+    case 10: return launch_len<10, S>(b, st);
+    case 11: return launch_len<11, S>(b, st);
+    case 12: return launch_len<12, S>(b, st);
+    case 13: return launch_len<13, S>(b, st);
+    case 14: return launch_len<14, S>(b, st);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+}  // namespace
+
+bool single_pass_supported(std::int64_t n) noexcept {
+  return n >= 2 && n <= kMaxSinglePass && (n & (n - 1)) == 0;
+}
+
+cudaError_t launch_stockham(std::int64_t n, int sign, const Batch1D& b,
+                            cudaStream_t stream) noexcept {
+  if (!single_pass_supported(n)) return cudaErrorInvalidValue;
+  if (b.batch <= 0) return cudaSuccess;
+  const int log2n = __builtin_ctzll(static_cast<unsigned long long>(n));
+  return sign < 0 ? dispatch<-1>(log2n, b, stream) : dispatch<1>(log2n, b, stream);
+}
+
+}  // namespace mb200::fft

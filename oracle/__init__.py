@@ -169,6 +169,31 @@ def spmv_csr(row_offsets, col_ind, values, x, *, base=0, alpha=1.0, beta=0.0, y=
     return (y, exact, absr) if with_abs else y
 
 
+def fft_c2c(x: np.ndarray, dims, batch: int, sign: int, *, istride=1, idist=None, ostride=1,
+            odist=None, out_len=None, exact=False, threads: int = 8) -> np.ndarray:
+    """Reference batched C2C FFT (cufft_exec.mm:101-211) on a flat complex64 array.
+
+    exact=True returns the double-precision result (complex128), otherwise the
+    restated single-precision arithmetic (complex64)."""
+    dims = list(dims)
+    total = int(np.prod(dims))
+    idist = total * istride if idist is None else idist
+    odist = total * ostride if odist is None else odist
+    if out_len is None:
+        out_len = (batch - 1) * odist + (total - 1) * ostride + 1
+    xin = np.ascontiguousarray(x, dtype=np.complex64)
+    d = np.asarray(dims, dtype=np.int32)
+    if exact:
+        out = np.zeros(out_len, np.complex128)
+        lib().oracle_fft_c2c(xin.ctypes.data, None, len(dims), d.ctypes.data, batch, istride,
+                             idist, ostride, odist, sign, 1, out.ctypes.data, threads)
+    else:
+        out = np.zeros(out_len, np.complex64)
+        lib().oracle_fft_c2c(xin.ctypes.data, out.ctypes.data, len(dims), d.ctypes.data, batch,
+                             istride, idist, ostride, odist, sign, 0, None, threads)
+    return out
+
+
 def bf16_bits(a: np.ndarray) -> np.ndarray:
     """float32 -> bfloat16 bit patterns (round to nearest even)."""
     u = np.ascontiguousarray(a, dtype=np.float32).view(np.uint32).astype(np.uint64)

@@ -63,6 +63,13 @@ float oracle_bf16_round(float v);
  * accum_f64 != 0: accumulate in double (ground truth) instead of the sequential fp32 fma. */
 void oracle_conv2d_fwd(const void* x, const void* w, void* y, const OracleConvParams* p, int bf16,
                        int accum_f64, int threads);
+/* ---- C2C FFT (libraries/fft/src/cufft_exec.mm:101-211) ---- */
+/* in/out: interleaved complex64 with element strides; use_double != 0 writes the
+ * double-precision result to out_f64 (same layout) instead of out. */
+void oracle_fft_c2c(const float* in, float* out, int rank, const int* dims, int64_t batch,
+                    int64_t istride, int64_t idist, int64_t ostride, int64_t odist, int sign,
+                    int use_double, double* out_f64, int threads);
+
 /* ---- CSR SpMV (libraries/sparse/shaders/cusparse_kernels.metal:54-77) ---- */
 /* exact_row (optional): alpha * sum a_k x_col + beta * y in double;
  * abs_row (optional): per-row sum |a_k * x_col| in double. */

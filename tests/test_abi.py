@@ -17,6 +17,7 @@ HEADER_LIB = {
     "curand.h": "curand",
     "cudnn.h": "cudnn",
     "cusparse.h": "cusparse",
+    "cufft.h": "cufft",
 }
 
 

@@ -27,10 +27,14 @@ def normwise(got, want):
     return np.linalg.norm(got - want) / max(np.linalg.norm(want), 1e-30)
 
 
-def check_f32(got, want, tol=1e-5):
+def check_f32(got, want, tol=1e-5, scale=None):
+    """Normwise relative error <= tol, and per element |err| <= 2*tol*scale + 1e-6 where
+    scale is |want| (softmax) or, for a convolution, the same convolution of |x| and |w|
+    (the magnitude its rounding error is proportional to)."""
     assert normwise(got, want) <= tol, f"normwise {normwise(got, want):.3e}"
     err = np.abs(got.astype(np.float64) - want)
-    assert np.all(err <= 2 * tol * np.abs(want) + 1e-6), f"max elementwise {err.max():.3e}"
+    scale = np.abs(want) if scale is None else scale
+    assert np.all(err <= 2 * tol * scale + 1e-6), f"max elementwise {err.max():.3e}"
 
 
 def dev(torch, a):
@@ -99,7 +103,11 @@ def test_conv_f32_matches_oracle(cuda, built, case, alpha, beta):
                          stride=stride, dil=dil, groups=groups,
                          mode="conv" if mode == 0 else "cross", alpha=alpha, beta=beta,
                          y=y0.copy(), accum_f64=True)
-    check_f32(got, want)
+    mag = oracle.conv2d(np.abs(x), np.abs(w), xshape, wshape, x_fmt=fmt[xf], w_fmt=fmt[wf],
+                        pad=pad, stride=stride, dil=dil, groups=groups,
+                        mode="conv" if mode == 0 else "cross", alpha=abs(alpha), beta=abs(beta),
+                        y=np.abs(y0), accum_f64=True)
+    check_f32(got, want, scale=mag)
 
 
 @pytest.mark.parametrize("case", CONV_CASES[:2] + CONV_CASES[5:6])

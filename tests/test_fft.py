@@ -1,0 +1,283 @@
+"""cufftPlanMany / cufftExecC2C.
+
+CPU: the oracle against the reference's known answers, and the C-ABI plan logic.
+GPU (marked): the CUDA path through the C ABI against the double-precision
+oracle; bar: relative L2 error <= 1e-5 per transform.
+"""
+
+import ctypes as C
+
+import numpy as np
+import pytest
+
+import oracle
+from muda_b200 import capi
+from tests.helpers import stream_ptr
+
+TOL = 1e-5
+
+
+def ref_signal(n):
+    """tests/cufft_test.cpp:41-46."""
+    i = np.arange(n, dtype=np.float32)
+    phase = np.float32(2.0 * np.pi) * i / np.float32(n)
+    return (np.cos(3 * phase) + 0.5 * np.sin(phase) + 1j * 0.25 * np.cos(2 * phase)).astype(
+        np.complex64)
+
+
+@pytest.mark.parametrize("n", [256, 60])
+def test_oracle_round_trip_pin(n):
+    """tests/cufft_test.cpp:34-74: forward then inverse, divided by N, recovers the input
+    (tolerance 1e-3)."""
+    x = ref_signal(n)
+    y = oracle.fft_c2c(oracle.fft_c2c(x, [n], 1, -1), [n], 1, 1) / n
+    assert np.max(np.abs(y.real - x.real)) < 1e-3 and np.max(np.abs(y.imag - x.imag)) < 1e-3
+
+
+def test_oracle_plan_many_impulse_pin():
+    """tests/cufft_test.cpp:195-238: N = 64, batch 4, impulse of amplitude b+1 -> flat spectrum."""
+    x = np.zeros(64 * 4, np.complex64)
+    for b in range(4):
+        x[b * 64] = b + 1
+    y = oracle.fft_c2c(x, [64], 4, -1)
+    for b in range(4):
+        np.testing.assert_allclose(y[b * 64:(b + 1) * 64].real, b + 1, atol=1e-4)
+
+
+def test_oracle_2d_impulse_pin():
+    """tests/cufft_test.cpp:127-153: 16 x 32 impulse -> all-ones spectrum."""
+    x = np.zeros(16 * 32, np.complex64)
+    x[0] = 1
+    y = oracle.fft_c2c(x, [16, 32], 1, -1)
+    np.testing.assert_allclose(y.real, 1.0, atol=1e-4)
+    np.testing.assert_allclose(y.imag, 0.0, atol=1e-4)
+
+
+def test_oracle_matches_numpy():
+    rng = np.random.default_rng(0)
+    for dims, b in (([4096], 2), ([60], 3), ([8, 12], 2)):
+        n = int(np.prod(dims))
+        x = (rng.standard_normal(n * b) + 1j * rng.standard_normal(n * b)).astype(np.complex64)
+        want = np.fft.fftn(x.reshape([b] + dims).astype(np.complex128),
+                           axes=tuple(range(1, len(dims) + 1))).reshape(-1)
+        got = oracle.fft_c2c(x, dims, b, -1, exact=True)
+        assert np.linalg.norm(got - want) <= 1e-12 * np.linalg.norm(want)
+
+
+def _plan_many(L, dims, batch, inembed=None, istride=1, idist=0, onembed=None, ostride=1,
+               odist=0, typ=capi.CUFFT_C2C):
+    p = C.c_void_p()
+    n = (C.c_int * len(dims))(*dims)
+    ie = (C.c_int * len(dims))(*inembed) if inembed else None
+    oe = (C.c_int * len(dims))(*onembed) if onembed else None
+    st = L.cufftPlanMany(C.byref(p), len(dims), n, ie, istride, idist, oe, ostride, odist, typ,
+                         batch)
+    return st, p
+
+
+def test_plan_argument_errors(built):
+    """Checks made before any device resource is touched (cufft_plan.mm:36-60)."""
+    L = capi.cufft()
+    assert _plan_many(L, [64], 0)[0] == capi.CUFFT_INVALID_VALUE
+    assert _plan_many(L, [0], 1)[0] == capi.CUFFT_INVALID_SIZE
+    assert _plan_many(L, [4, 4, 4, 4], 1)[0] == capi.CUFFT_INVALID_VALUE
+    assert _plan_many(L, [64], 1, typ=capi.CUFFT_Z2Z)[0] == capi.CUFFT_NOT_SUPPORTED
+    assert _plan_many(L, [64], 1, typ=0x33)[0] == capi.CUFFT_INVALID_TYPE
+    assert L.cufftPlan1d(None, 64, capi.CUFFT_C2C, 1) == capi.CUFFT_INVALID_VALUE
+    q = C.c_void_p()
+    assert L.cufftCreate(C.byref(q)) == 0
+    ws = C.c_size_t(0)
+    assert L.cufftGetSize(q, C.byref(ws)) == capi.CUFFT_INVALID_PLAN  # not configured
+    assert L.cufftExecC2C(q, C.c_void_p(256), C.c_void_p(256), -1) == capi.CUFFT_INVALID_PLAN
+    assert L.cufftDestroy(q) == 0
+    assert L.cufftDestroy(q) == capi.CUFFT_INVALID_PLAN
+    assert L.cufftSetStream(q, None) == capi.CUFFT_INVALID_PLAN
+
+
+@pytest.mark.gpu
+def test_plan_logic(cuda, built):
+    L = capi.cufft()
+    st, p = _plan_many(L, [64], 4)
+    assert st == 0
+    ws = C.c_size_t(0)
+    assert L.cufftGetSize(p, C.byref(ws)) == 0 and ws.value > 0
+    assert L.cufftSetStream(p, None) == 0
+    assert L.cufftExecC2C(p, None, None, -1) == capi.CUFFT_INVALID_VALUE
+    assert L.cufftExecC2C(p, C.c_void_p(256), C.c_void_p(256), 0) == capi.CUFFT_INVALID_VALUE
+    # unaddressable buffers are rejected before launch
+    assert L.cufftExecC2C(p, C.c_void_p(256), C.c_void_p(256), -1) == capi.CUFFT_INVALID_VALUE
+    assert L.cufftDestroy(p) == 0
+    assert L.cufftDestroy(p) == capi.CUFFT_INVALID_PLAN
+    assert L.cufftExecC2C(p, C.c_void_p(256), C.c_void_p(256), -1) == capi.CUFFT_INVALID_PLAN
+    assert _plan_many(L, [64], 0)[0] == capi.CUFFT_INVALID_VALUE
+    assert _plan_many(L, [0], 1)[0] == capi.CUFFT_INVALID_SIZE
+    assert _plan_many(L, [4, 4, 4, 4], 1)[0] == capi.CUFFT_INVALID_VALUE
+    assert _plan_many(L, [64], 1, typ=capi.CUFFT_Z2Z)[0] == capi.CUFFT_NOT_SUPPORTED
+    assert _plan_many(L, [64], 1, typ=0x33)[0] == capi.CUFFT_INVALID_TYPE
+    # an unconfigured plan has no size
+    q = C.c_void_p()
+    assert L.cufftCreate(C.byref(q)) == 0
+    assert L.cufftGetSize(q, C.byref(ws)) == capi.CUFFT_INVALID_PLAN
+    assert L.cufftMakePlan1d(q, 4096, capi.CUFFT_C2C, 8, C.byref(ws)) == 0 and ws.value > 0
+    assert L.cufftDestroy(q) == 0
+
+
+# --------------------------------------------------------------------- GPU --
+def gpu_fft(torch, x, dims, batch, sign, *, inembed=None, istride=1, idist=0, onembed=None,
+            ostride=1, odist=0, out_len=None, inplace=False):
+    L = capi.cufft()
+    st, p = _plan_many(L, dims, batch, inembed, istride, idist, onembed, ostride, odist)
+    assert st == 0, st
+    try:
+        assert L.cufftSetStream(p, C.c_void_p(stream_ptr(torch))) == 0
+        xi = torch.from_numpy(np.ascontiguousarray(x).view(np.float32)).cuda()
+        if inplace:
+            xo = xi
+        else:
+            xo = torch.zeros(2 * (out_len or len(x)), dtype=torch.float32, device="cuda")
+        assert L.cufftExecC2C(p, C.c_void_p(xi.data_ptr()), C.c_void_p(xo.data_ptr()), sign) == 0
+        torch.cuda.synchronize()
+        return xo.cpu().numpy().view(np.complex64)
+    finally:
+        assert L.cufftDestroy(p) == 0
+
+
+def rel_l2_per_transform(got, want, n, batch, dist=None, stride=1):
+    dist = n * stride if dist is None else dist
+    worst = 0.0
+    for b in range(batch):
+        idx = b * dist + np.arange(n) * stride
+        g, w = got[idx].astype(np.complex128), want[idx]
+        worst = max(worst, np.linalg.norm(g - w) / max(np.linalg.norm(w), 1e-300))
+    return worst
+
+
+def rand_c64(rng, n):
+    return (rng.standard_normal(n) + 1j * rng.standard_normal(n)).astype(np.complex64)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("n", [2, 4, 8, 16, 32, 64, 128, 256, 512, 1024, 2048, 4096, 8192, 16384])
+@pytest.mark.parametrize("sign", [-1, 1])
+def test_gpu_pow2_lengths(cuda, built, n, sign):
+    rng = np.random.default_rng(n)
+    batch = max(1, min(64, (1 << 16) // n)) + 1
+    x = rand_c64(rng, n * batch)
+    got = gpu_fft(cuda, x, [n], batch, sign)
+    want = oracle.fft_c2c(x, [n], batch, sign, exact=True)
+    assert rel_l2_per_transform(got, want, n, batch) <= TOL
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("n", [3, 5, 7, 12, 60, 100, 1000, 3000])
+def test_gpu_non_pow2_lengths(cuda, built, n):
+    rng = np.random.default_rng(n)
+    batch = 3
+    x = rand_c64(rng, n * batch)
+    for sign in (-1, 1):
+        got = gpu_fft(cuda, x, [n], batch, sign)
+        want = oracle.fft_c2c(x, [n], batch, sign, exact=True)
+        assert rel_l2_per_transform(got, want, n, batch) <= TOL
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("n", [32768, 1 << 20])
+def test_gpu_large_pow2_split(cuda, built, n):
+    rng = np.random.default_rng(5)
+    batch = 2
+    x = rand_c64(rng, n * batch)
+    got = gpu_fft(cuda, x, [n], batch, -1)
+    want = np.fft.fft(x.reshape(batch, n).astype(np.complex128), axis=1).reshape(-1)
+    assert rel_l2_per_transform(got, want, n, batch) <= TOL
+
+
+@pytest.mark.gpu
+def test_gpu_reference_round_trip_in_place(cuda, built):
+    """tests/cufft_test.cpp:34-74 on the GPU, in place (idata == odata)."""
+    for n in (256, 60):
+        x = ref_signal(n)
+        L = capi.cufft()
+        p = C.c_void_p()
+        assert L.cufftPlan1d(C.byref(p), n, capi.CUFFT_C2C, 1) == 0
+        t = cuda.from_numpy(x.view(np.float32).copy()).cuda()
+        ptr = C.c_void_p(t.data_ptr())
+        assert L.cufftSetStream(p, C.c_void_p(stream_ptr(cuda))) == 0
+        assert L.cufftExecC2C(p, ptr, ptr, capi.CUFFT_FORWARD) == 0
+        assert L.cufftExecC2C(p, ptr, ptr, capi.CUFFT_INVERSE) == 0
+        cuda.cuda.synchronize()
+        y = t.cpu().numpy().view(np.complex64) / n
+        assert L.cufftDestroy(p) == 0
+        assert np.max(np.abs(y - x)) < 1e-3
+
+
+@pytest.mark.gpu
+def test_gpu_plan_many_impulse(cuda, built):
+    x = np.zeros(64 * 4, np.complex64)
+    for b in range(4):
+        x[b * 64] = b + 1
+    y = gpu_fft(cuda, x, [64], 4, -1, inplace=True)
+    for b in range(4):
+        np.testing.assert_allclose(y[b * 64:(b + 1) * 64].real, b + 1, atol=1e-4)
+
+
+@pytest.mark.gpu
+def test_gpu_strided_layouts(cuda, built):
+    rng = np.random.default_rng(9)
+    n, batch = 1024, 5
+    istride, idist, ostride, odist = 3, 3 * 1024 + 7, 2, 2 * 1024 + 1
+    x = rand_c64(rng, (batch - 1) * idist + (n - 1) * istride + 1)
+    out_len = (batch - 1) * odist + (n - 1) * ostride + 1
+    got = gpu_fft(cuda, x, [n], batch, -1, inembed=[n], istride=istride, idist=idist,
+                  onembed=[n], ostride=ostride, odist=odist, out_len=out_len)
+    want = oracle.fft_c2c(x, [n], batch, -1, istride=istride, idist=idist, ostride=ostride,
+                          odist=odist, out_len=out_len, exact=True)
+    assert rel_l2_per_transform(got, want, n, batch, odist, ostride) <= TOL
+    # NULL inembed: the strides are ignored (cufft_plan.mm:68-83)
+    x2 = rand_c64(rng, n * batch)
+    got = gpu_fft(cuda, x2, [n], batch, -1, istride=5, idist=3, ostride=7, odist=2)
+    want = oracle.fft_c2c(x2, [n], batch, -1, exact=True)
+    assert rel_l2_per_transform(got, want, n, batch) <= TOL
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("dims", [[16, 32], [4, 6, 8], [64, 64], [3, 1, 128], [1, 256]])
+def test_gpu_multi_dim(cuda, built, dims):
+    rng = np.random.default_rng(len(dims))
+    n, batch = int(np.prod(dims)), 3
+    x = rand_c64(rng, n * batch)
+    for sign in (-1, 1):
+        got = gpu_fft(cuda, x, dims, batch, sign)
+        want = oracle.fft_c2c(x, dims, batch, sign, exact=True)
+        assert rel_l2_per_transform(got, want, n, batch) <= TOL
+
+
+@pytest.mark.gpu
+def test_gpu_config_size(cuda, built):
+    """N = 4096, batch 65536, normal(0,1) re/im (seed 3), forward then inverse
+    in place.  64 sampled transforms are checked against the oracle after each
+    direction; the whole batch satisfies the round trip ifft(fft(x)) / N = x."""
+    torch = cuda
+    from muda_b200 import synth
+    n, batch = 4096, 65536
+    x = synth.normal(torch, 2 * n * batch, seed=3)
+    x0 = x.clone()
+    L = capi.cufft()
+    p = C.c_void_p()
+    nn = (C.c_int * 1)(n)
+    assert L.cufftPlanMany(C.byref(p), 1, nn, None, 1, n, None, 1, n, capi.CUFFT_C2C, batch) == 0
+    assert L.cufftSetStream(p, C.c_void_p(stream_ptr(torch))) == 0
+    ptr = C.c_void_p(x.data_ptr())
+    rng = np.random.default_rng(0)
+    pick = np.sort(rng.choice(batch, 64, replace=False))
+    src = x0.view(batch, 2 * n)[torch.from_numpy(pick).cuda()].cpu().numpy().view(np.complex64)
+    assert L.cufftExecC2C(p, ptr, ptr, capi.CUFFT_FORWARD) == 0
+    torch.cuda.synchronize()
+    fwd = x.view(batch, 2 * n)[torch.from_numpy(pick).cuda()].cpu().numpy().view(np.complex64)
+    want = oracle.fft_c2c(src.reshape(-1), [n], 64, -1, exact=True)
+    assert rel_l2_per_transform(fwd.reshape(-1), want, n, 64) <= TOL
+    assert L.cufftExecC2C(p, ptr, ptr, capi.CUFFT_INVERSE) == 0
+    torch.cuda.synchronize()
+    assert L.cufftDestroy(p) == 0
+    err = (x.view(batch, 2 * n) / n - x0.view(batch, 2 * n)).double().norm(dim=1)
+    ref = x0.view(batch, 2 * n).double().norm(dim=1)
+    assert float((err / ref).max()) <= TOL

@@ -37,6 +37,7 @@ LIBS: dict[str, list[str]] = {
               "dnn/conv_dispatch.cu"],
     "cusparse": ["sparse/cusparse_api.cpp", "sparse/spmv_kernels.cu"],
     "cufft": ["fft/cufft_api.cpp", "fft/stockham_kernels.cu", "fft/dft_kernels.cu"],
+    "cublas": ["blas/cublas_api.cpp", "blas/gemm_simt_kernels.cu", "blas/gemm_tc_kernels.cu"],
 }
 
 COMMON_FLAGS = ["-O3", "-std=c++17", f"-I{INCLUDE}", f"-I{CSRC}"]

@@ -199,11 +199,56 @@ def cufft() -> C.CDLL:
     return _declare(_load("cufft"), CUFFT_PROTOS)
 
 
+# ------------------------------------------------------------------ cuBLAS --
+CUBLAS_STATUS_SUCCESS = 0
+CUBLAS_STATUS_NOT_INITIALIZED = 1
+CUBLAS_STATUS_INVALID_VALUE = 7
+CUBLAS_STATUS_EXECUTION_FAILED = 13
+CUBLAS_STATUS_NOT_SUPPORTED = 15
+CUBLAS_OP_N = 0
+CUBLAS_OP_T = 1
+CUBLAS_OP_C = 2
+CUBLAS_POINTER_MODE_HOST = 0
+CUBLAS_POINTER_MODE_DEVICE = 1
+CUBLAS_COMPUTE_16F = 64
+CUBLAS_COMPUTE_32F = 68
+CUBLAS_GEMM_DEFAULT = -1
+
+ll = C.c_longlong
+CUBLAS_PROTOS = {
+    "cublasCreate_v2": ([P(vp)], i32),
+    "cublasDestroy_v2": ([vp], i32),
+    "cublasGetVersion_v2": ([vp, P(i32)], i32),
+    "cublasSetStream_v2": ([vp, vp], i32),
+    "cublasGetStream_v2": ([vp, P(vp)], i32),
+    "cublasSetPointerMode_v2": ([vp, i32], i32),
+    "cublasGetPointerMode_v2": ([vp, P(i32)], i32),
+    "cublasSetMathMode": ([vp, i32], i32),
+    "cublasGetMathMode": ([vp, P(i32)], i32),
+    "cublasGetStatusName": ([i32], C.c_char_p),
+    "cublasGetStatusString": ([i32], C.c_char_p),
+    "cublasSgemm_v2": ([vp, i32, i32, i32, i32, i32, vp, vp, i32, vp, i32, vp, vp, i32], i32),
+    "cublasHgemm": ([vp, i32, i32, i32, i32, i32, vp, vp, i32, vp, i32, vp, vp, i32], i32),
+    "cublasGemmEx": ([vp, i32, i32, i32, i32, i32, vp, vp, i32, i32, vp, i32, i32, vp, vp, i32,
+                      i32, i32, i32], i32),
+    "cublasSgemmStridedBatched": ([vp, i32, i32, i32, i32, i32, vp, vp, i32, ll, vp, i32, ll,
+                                   vp, vp, i32, ll, i32], i32),
+    "cublasGemmStridedBatchedEx": ([vp, i32, i32, i32, i32, i32, vp, vp, i32, i32, ll, vp, i32,
+                                    i32, ll, vp, vp, i32, i32, ll, i32, i32, i32], i32),
+}
+
+
+@lru_cache(maxsize=None)
+def cublas() -> C.CDLL:
+    return _declare(_load("cublas"), CUBLAS_PROTOS)
+
+
 ALL_PROTOS: dict[str, dict[str, tuple[list, object]]] = {
     "curand": CURAND_PROTOS,
     "cudnn": CUDNN_PROTOS,
     "cusparse": CUSPARSE_PROTOS,
     "cufft": CUFFT_PROTOS,
+    "cublas": CUBLAS_PROTOS,
 }
 
 LOADERS = {
@@ -211,4 +256,5 @@ LOADERS = {
     "cudnn": cudnn,
     "cusparse": cusparse,
     "cufft": cufft,
+    "cublas": cublas,
 }

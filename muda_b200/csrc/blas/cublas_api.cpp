@@ -1,0 +1,350 @@
+// cublas_api.cpp — cuBLAS C ABI: handle state and the level-3 GEMM entry points.
+//
+// Mirrors libraries/blas/src/cublas_context.mm and cublas_level3.mm of the
+// reference: the same entry points, argument checks (op, sizes, leading
+// dimensions, null scalars) and status codes, column-major semantics, and the
+// same GemmEx dispatch (fp32 / fp16 operands, the scalar type chosen by the
+// compute type, cublas_level3.mm:544-608).  bf16 operands (CUDA_R_16BF) are an
+// extension the reference lacks.  In device pointer mode the scalars are read
+// by the kernel on the stream instead of synchronising the host
+// (cublas_context.mm:72-75 synchronises).
+#pragma GCC visibility push(default)
+#include "cublas_v2.h"
+#pragma GCC visibility pop
+
+#include <cuda_runtime_api.h>
+
+#include <cstdint>
+#include <cstring>
+#include <memory>
+#include <mutex>
+
+#include "blas/gemm.hpp"
+#include "common/device.hpp"
+#include "common/registry.hpp"
+
+namespace {
+
+using mb200::blas::Elem;
+using mb200::blas::GemmArgs;
+
+constexpr int kCublasVersion = 12000;
+
+struct BlasContext {
+  std::mutex mu;
+  cudaStream_t stream = nullptr;
+  cublasPointerMode_t pointer_mode = CUBLAS_POINTER_MODE_HOST;
+  cublasMath_t math_mode = CUBLAS_DEFAULT_MATH;
+};
+
+using HandleTable = mb200::Registry<BlasContext, mb200::ObjKind::kBlasHandle>;
+HandleTable& handles() {
+  static HandleTable t;
+  return t;
+}
+
+bool valid_op(cublasOperation_t op) {
+  return op == CUBLAS_OP_N || op == CUBLAS_OP_T || op == CUBLAS_OP_C;
+}
+
+float half_bits_to_float(std::uint16_t h) {
+  const std::uint32_t sign = static_cast<std::uint32_t>(h & 0x8000u) << 16;
+  std::uint32_t exp = (h >> 10) & 0x1Fu;
+  std::uint32_t man = h & 0x3FFu;
+  std::uint32_t bits;
+  if (exp == 0) {
+    if (man == 0) {
+      bits = sign;
+    } else {  // subnormal: normalise
+      exp = 127 - 15 + 1;
+      while ((man & 0x400u) == 0) {
+        man <<= 1;
+        --exp;
+      }
+      man &= 0x3FFu;
+      bits = sign | (exp << 23) | (man << 13);
+    }
+  } else if (exp == 31) {
+    bits = sign | 0x7F800000u | (man << 13);
+  } else {
+    bits = sign | ((exp + 127 - 15) << 23) | (man << 13);
+  }
+  float f;
+  std::memcpy(&f, &bits, 4);
+  return f;
+}
+
+// Elements from the first to the last addressed element of a rows x cols
+// column-major matrix (cublas_level3.mm:233-240).
+std::size_t span(int rows, int cols, std::int64_t ld) {
+  if (rows <= 0 || cols <= 0) return 0;
+  return static_cast<std::size_t>(ld) * static_cast<std::size_t>(cols - 1) +
+         static_cast<std::size_t>(rows);
+}
+
+std::size_t batch_span(int rows, int cols, std::int64_t ld, std::int64_t stride, int batch) {
+  const std::size_t one = span(rows, cols, ld);
+  if (one == 0 || batch <= 0) return 0;
+  const std::int64_t s = stride < 0 ? -stride : stride;
+  return one + static_cast<std::size_t>(s) * static_cast<std::size_t>(batch - 1);
+}
+
+struct Scalars {
+  bool device = false;
+  float alpha = 0.0f, beta = 0.0f;
+  const void* alpha_ptr = nullptr;
+  const void* beta_ptr = nullptr;
+};
+
+// Validation shared by every GEMM entry point (cublas_level3.mm:515-531).
+cublasStatus_t check_args(cublasOperation_t ta, cublasOperation_t tb, int m, int n, int k,
+                          int lda, int ldb, int ldc, int batch, const void* alpha,
+                          const void* beta) {
+  if (!valid_op(ta) || !valid_op(tb) || m < 0 || n < 0 || k < 0 || batch < 0 ||
+      alpha == nullptr || beta == nullptr)
+    return CUBLAS_STATUS_INVALID_VALUE;
+  const int min_lda = (ta == CUBLAS_OP_N) ? (m > 1 ? m : 1) : (k > 1 ? k : 1);
+  const int min_ldb = (tb == CUBLAS_OP_N) ? (k > 1 ? k : 1) : (n > 1 ? n : 1);
+  const int min_ldc = m > 1 ? m : 1;
+  if (lda < min_lda || ldb < min_ldb || ldc < min_ldc) return CUBLAS_STATUS_INVALID_VALUE;
+  return CUBLAS_STATUS_SUCCESS;
+}
+
+cublasStatus_t run_gemm(BlasContext& ctx, Elem type, cublasOperation_t ta, cublasOperation_t tb,
+                        int m, int n, int k, const void* alpha, bool half_scalars, const void* A,
+                        int lda, long long sa, const void* B, int ldb, long long sb,
+                        const void* beta, void* C, int ldc, long long sc, int batch) {
+  cudaStream_t stream;
+  cublasPointerMode_t mode;
+  {
+    std::lock_guard<std::mutex> g(ctx.mu);
+    stream = ctx.stream;
+    mode = ctx.pointer_mode;
+  }
+  if (m == 0 || n == 0 || batch == 0) return CUBLAS_STATUS_SUCCESS;
+  GemmArgs g{};
+  g.type = type;
+  g.trans_a = (ta != CUBLAS_OP_N);
+  g.trans_b = (tb != CUBLAS_OP_N);
+  g.m = m;
+  g.n = n;
+  g.k = k;
+  g.a = A;
+  g.lda = lda;
+  g.stride_a = sa;
+  g.b = B;
+  g.ldb = ldb;
+  g.stride_b = sb;
+  g.c = C;
+  g.ldc = ldc;
+  g.stride_c = sc;
+  g.batch = batch;
+  if (mode == CUBLAS_POINTER_MODE_DEVICE) {
+    // 16-bit device scalars would need a conversion kernel; the kernels read fp32.
+    if (half_scalars) return CUBLAS_STATUS_NOT_SUPPORTED;
+    if (!mb200::device_span_ok(alpha, 4) || !mb200::device_span_ok(beta, 4))
+      return CUBLAS_STATUS_INVALID_VALUE;
+    g.alpha_dev = static_cast<const float*>(alpha);
+    g.beta_dev = static_cast<const float*>(beta);
+  } else if (half_scalars) {
+    std::uint16_t ha, hb;
+    std::memcpy(&ha, alpha, 2);
+    std::memcpy(&hb, beta, 2);
+    g.alpha = half_bits_to_float(ha);
+    g.beta = half_bits_to_float(hb);
+  } else {
+    g.alpha = *static_cast<const float*>(alpha);
+    g.beta = *static_cast<const float*>(beta);
+  }
+  const int es = (type == Elem::kF32) ? 4 : 2;
+  const int a_rows = g.trans_a ? k : m, a_cols = g.trans_a ? m : k;
+  const int b_rows = g.trans_b ? n : k, b_cols = g.trans_b ? k : n;
+  if (k > 0 && (!mb200::device_span_ok(A, batch_span(a_rows, a_cols, lda, sa, batch) * es) ||
+                !mb200::device_span_ok(B, batch_span(b_rows, b_cols, ldb, sb, batch) * es)))
+    return CUBLAS_STATUS_INVALID_VALUE;
+  if (!mb200::device_span_ok(C, batch_span(m, n, ldc, sc, batch) * es))
+    return CUBLAS_STATUS_INVALID_VALUE;
+  if (!mb200::aligned_to(A, es) || !mb200::aligned_to(B, es) || !mb200::aligned_to(C, es))
+    return CUBLAS_STATUS_INVALID_VALUE;
+  cudaError_t e = cudaErrorNotSupported;
+  if (type != Elem::kF32) e = mb200::blas::launch_gemm_tc(g, stream);
+  if (e == cudaErrorNotSupported) {
+    (void)cudaGetLastError();
+    e = mb200::blas::launch_gemm_simt(g, stream);
+  }
+  return e == cudaSuccess ? CUBLAS_STATUS_SUCCESS : CUBLAS_STATUS_EXECUTION_FAILED;
+}
+
+}  // namespace
+
+extern "C" {
+
+cublasStatus_t cublasCreate_v2(cublasHandle_t* handle) {
+  if (handle == nullptr) return CUBLAS_STATUS_INVALID_VALUE;
+  auto h = handles().add<cublasHandle_t>(std::make_shared<BlasContext>());
+  if (h == nullptr) return CUBLAS_STATUS_ALLOC_FAILED;
+  *handle = h;
+  return CUBLAS_STATUS_SUCCESS;
+}
+
+cublasStatus_t cublasDestroy_v2(cublasHandle_t handle) {
+  return handles().take(handle) ? CUBLAS_STATUS_SUCCESS : CUBLAS_STATUS_NOT_INITIALIZED;
+}
+
+cublasStatus_t cublasGetVersion_v2(cublasHandle_t handle, int* version) {
+  if (version == nullptr) return CUBLAS_STATUS_INVALID_VALUE;
+  if (handle != nullptr && !handles().get(handle)) return CUBLAS_STATUS_NOT_INITIALIZED;
+  *version = kCublasVersion;
+  return CUBLAS_STATUS_SUCCESS;
+}
+
+cublasStatus_t cublasSetStream_v2(cublasHandle_t handle, cudaStream_t streamId) {
+  auto h = handles().get(handle);
+  if (!h) return CUBLAS_STATUS_NOT_INITIALIZED;
+  std::lock_guard<std::mutex> g(h->mu);
+  h->stream = streamId;
+  return CUBLAS_STATUS_SUCCESS;
+}
+
+cublasStatus_t cublasGetStream_v2(cublasHandle_t handle, cudaStream_t* streamId) {
+  if (streamId == nullptr) return CUBLAS_STATUS_INVALID_VALUE;
+  auto h = handles().get(handle);
+  if (!h) return CUBLAS_STATUS_NOT_INITIALIZED;
+  std::lock_guard<std::mutex> g(h->mu);
+  *streamId = h->stream;
+  return CUBLAS_STATUS_SUCCESS;
+}
+
+cublasStatus_t cublasSetPointerMode_v2(cublasHandle_t handle, cublasPointerMode_t mode) {
+  auto h = handles().get(handle);
+  if (!h) return CUBLAS_STATUS_NOT_INITIALIZED;
+  if (mode != CUBLAS_POINTER_MODE_HOST && mode != CUBLAS_POINTER_MODE_DEVICE)
+    return CUBLAS_STATUS_INVALID_VALUE;
+  std::lock_guard<std::mutex> g(h->mu);
+  h->pointer_mode = mode;
+  return CUBLAS_STATUS_SUCCESS;
+}
+
+cublasStatus_t cublasGetPointerMode_v2(cublasHandle_t handle, cublasPointerMode_t* mode) {
+  if (mode == nullptr) return CUBLAS_STATUS_INVALID_VALUE;
+  auto h = handles().get(handle);
+  if (!h) return CUBLAS_STATUS_NOT_INITIALIZED;
+  std::lock_guard<std::mutex> g(h->mu);
+  *mode = h->pointer_mode;
+  return CUBLAS_STATUS_SUCCESS;
+}
+
+cublasStatus_t cublasSetMathMode(cublasHandle_t handle, cublasMath_t mode) {
+  auto h = handles().get(handle);
+  if (!h) return CUBLAS_STATUS_NOT_INITIALIZED;
+  if (mode < CUBLAS_DEFAULT_MATH || mode > CUBLAS_TF32_TENSOR_OP_MATH)
+    return CUBLAS_STATUS_INVALID_VALUE;
+  std::lock_guard<std::mutex> g(h->mu);
+  h->math_mode = mode;
+  return CUBLAS_STATUS_SUCCESS;
+}
+
+cublasStatus_t cublasGetMathMode(cublasHandle_t handle, cublasMath_t* mode) {
+  if (mode == nullptr) return CUBLAS_STATUS_INVALID_VALUE;
+  auto h = handles().get(handle);
+  if (!h) return CUBLAS_STATUS_NOT_INITIALIZED;
+  std::lock_guard<std::mutex> g(h->mu);
+  *mode = h->math_mode;
+  return CUBLAS_STATUS_SUCCESS;
+}
+
+const char* cublasGetStatusName(cublasStatus_t status) {
+  switch (status) {
+    case CUBLAS_STATUS_SUCCESS: return "CUBLAS_STATUS_SUCCESS";
+    case CUBLAS_STATUS_NOT_INITIALIZED: return "CUBLAS_STATUS_NOT_INITIALIZED";
+    case CUBLAS_STATUS_ALLOC_FAILED: return "CUBLAS_STATUS_ALLOC_FAILED";
+    case CUBLAS_STATUS_INVALID_VALUE: return "CUBLAS_STATUS_INVALID_VALUE";
+    case CUBLAS_STATUS_ARCH_MISMATCH: return "CUBLAS_STATUS_ARCH_MISMATCH";
+    case CUBLAS_STATUS_MAPPING_ERROR: return "CUBLAS_STATUS_MAPPING_ERROR";
+    case CUBLAS_STATUS_EXECUTION_FAILED: return "CUBLAS_STATUS_EXECUTION_FAILED";
+    case CUBLAS_STATUS_INTERNAL_ERROR: return "CUBLAS_STATUS_INTERNAL_ERROR";
+    case CUBLAS_STATUS_NOT_SUPPORTED: return "CUBLAS_STATUS_NOT_SUPPORTED";
+  }
+  return "CUBLAS_STATUS_UNKNOWN";
+}
+
+const char* cublasGetStatusString(cublasStatus_t status) { return cublasGetStatusName(status); }
+
+cublasStatus_t cublasSgemmStridedBatched(cublasHandle_t handle, cublasOperation_t transa,
+                                         cublasOperation_t transb, int m, int n, int k,
+                                         const float* alpha, const float* A, int lda,
+                                         long long int strideA, const float* B, int ldb,
+                                         long long int strideB, const float* beta, float* C,
+                                         int ldc, long long int strideC, int batchCount) {
+  auto h = handles().get(handle);
+  if (!h) return CUBLAS_STATUS_NOT_INITIALIZED;
+  const cublasStatus_t st =
+      check_args(transa, transb, m, n, k, lda, ldb, ldc, batchCount, alpha, beta);
+  if (st != CUBLAS_STATUS_SUCCESS) return st;
+  return run_gemm(*h, Elem::kF32, transa, transb, m, n, k, alpha, false, A, lda, strideA, B, ldb,
+                  strideB, beta, C, ldc, strideC, batchCount);
+}
+
+cublasStatus_t cublasSgemm_v2(cublasHandle_t handle, cublasOperation_t transa,
+                              cublasOperation_t transb, int m, int n, int k, const float* alpha,
+                              const float* A, int lda, const float* B, int ldb, const float* beta,
+                              float* C, int ldc) {
+  return cublasSgemmStridedBatched(handle, transa, transb, m, n, k, alpha, A, lda, 0, B, ldb, 0,
+                                   beta, C, ldc, 0, 1);
+}
+
+cublasStatus_t cublasHgemm(cublasHandle_t handle, cublasOperation_t transa,
+                           cublasOperation_t transb, int m, int n, int k, const __half* alpha,
+                           const __half* A, int lda, const __half* B, int ldb, const __half* beta,
+                           __half* C, int ldc) {
+  auto h = handles().get(handle);
+  if (!h) return CUBLAS_STATUS_NOT_INITIALIZED;
+  const cublasStatus_t st = check_args(transa, transb, m, n, k, lda, ldb, ldc, 1, alpha, beta);
+  if (st != CUBLAS_STATUS_SUCCESS) return st;
+  return run_gemm(*h, Elem::kF16, transa, transb, m, n, k, alpha, true, A, lda, 0, B, ldb, 0, beta,
+                  C, ldc, 0, 1);
+}
+
+cublasStatus_t cublasGemmStridedBatchedEx(cublasHandle_t handle, cublasOperation_t transa,
+                                          cublasOperation_t transb, int m, int n, int k,
+                                          const void* alpha, const void* A, cudaDataType Atype,
+                                          int lda, long long int strideA, const void* B,
+                                          cudaDataType Btype, int ldb, long long int strideB,
+                                          const void* beta, void* C, cudaDataType Ctype, int ldc,
+                                          long long int strideC, int batchCount, int computeType,
+                                          cublasGemmAlgo_t algo) {
+  (void)algo;
+  auto h = handles().get(handle);
+  if (!h) return CUBLAS_STATUS_NOT_INITIALIZED;
+  const cublasStatus_t st =
+      check_args(transa, transb, m, n, k, lda, ldb, ldc, batchCount, alpha, beta);
+  if (st != CUBLAS_STATUS_SUCCESS) return st;
+  if (Atype == CUDA_R_32F && Btype == CUDA_R_32F && Ctype == CUDA_R_32F)
+    return run_gemm(*h, Elem::kF32, transa, transb, m, n, k, alpha, false, A, lda, strideA, B,
+                    ldb, strideB, beta, C, ldc, strideC, batchCount);
+  Elem e;
+  if (Atype == CUDA_R_16F && Btype == CUDA_R_16F && Ctype == CUDA_R_16F) {
+    e = Elem::kF16;
+  } else if (Atype == CUDA_R_16BF && Btype == CUDA_R_16BF && Ctype == CUDA_R_16BF) {
+    e = Elem::kBF16;
+  } else {
+    return CUBLAS_STATUS_NOT_SUPPORTED;
+  }
+  // Scalar type follows the compute type (cublas_level3.mm:583-602).
+  const bool half_scalars =
+      (computeType == CUBLAS_COMPUTE_16F || computeType == CUBLAS_COMPUTE_16F_PEDANTIC ||
+       computeType == static_cast<int>(CUDA_R_16F));
+  return run_gemm(*h, e, transa, transb, m, n, k, alpha, half_scalars, A, lda, strideA, B, ldb,
+                  strideB, beta, C, ldc, strideC, batchCount);
+}
+
+cublasStatus_t cublasGemmEx(cublasHandle_t handle, cublasOperation_t transa,
+                            cublasOperation_t transb, int m, int n, int k, const void* alpha,
+                            const void* A, cudaDataType Atype, int lda, const void* B,
+                            cudaDataType Btype, int ldb, const void* beta, void* C,
+                            cudaDataType Ctype, int ldc, int computeType, cublasGemmAlgo_t algo) {
+  return cublasGemmStridedBatchedEx(handle, transa, transb, m, n, k, alpha, A, Atype, lda, 0, B,
+                                    Btype, ldb, 0, beta, C, Ctype, ldc, 0, 1, computeType, algo);
+}
+
+}  // extern "C"

@@ -1,0 +1,43 @@
+// gemm.hpp — launch interface of the GEMM kernels (column-major, cuBLAS semantics).
+#pragma once
+
+#include <cuda_runtime_api.h>
+
+#include <cstdint>
+
+namespace mb200::blas {
+
+enum class Elem : int { kF32 = 0, kF16 = 1, kBF16 = 2 };
+
+// C = alpha * op(A) * op(B) + beta * C for `batch` matrices, column-major.
+// alpha/beta are taken from *alpha_dev / *beta_dev when those are non-null
+// (device pointer mode), else from alpha / beta.  beta == 0 means C is not read.
+struct GemmArgs {
+  Elem type;             // A, B and C element type
+  bool trans_a, trans_b; // op = transpose (CUBLAS_OP_T and CUBLAS_OP_C are the same for reals)
+  int m, n, k;
+  const void* a;
+  std::int64_t lda, stride_a;
+  const void* b;
+  std::int64_t ldb, stride_b;
+  void* c;
+  std::int64_t ldc, stride_c;
+  int batch;
+  float alpha, beta;
+  const float* alpha_dev;
+  const float* beta_dev;
+};
+
+// Register-blocked FFMA kernel: any type, transposes, leading dimensions and
+// strides (fp32 accumulate).  The fp32 path of cublasSgemm.
+cudaError_t launch_gemm_simt(const GemmArgs& g, cudaStream_t stream) noexcept;
+
+// tcgen05 tensor-core kernel for 16-bit A/B (bf16 or fp16) with fp32 accumulation
+// in tensor memory.  Returns cudaErrorNotSupported when the shape or layout is not
+// covered (the caller then uses launch_gemm_simt).
+cudaError_t launch_gemm_tc(const GemmArgs& g, cudaStream_t stream) noexcept;
+
+// Name of the kernel family that would serve `g` (for tests and benchmarks).
+const char* gemm_path_name(const GemmArgs& g) noexcept;
+
+}  // namespace mb200::blas

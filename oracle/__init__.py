@@ -194,6 +194,38 @@ def fft_c2c(x: np.ndarray, dims, batch: int, sign: int, *, istride=1, idist=None
     return out
 
 
+GEMM_TYPES = {"f32": 0, "f16": 1, "bf16": 2}
+
+
+def gemm(type_: str, transa: bool, transb: bool, m: int, n: int, k: int, alpha: float,
+         A: np.ndarray, lda: int, B: np.ndarray, ldb: int, beta: float, C: np.ndarray, ldc: int,
+         *, stride_a=0, stride_b=0, stride_c=0, batch=1, accum_f64=False, entries=None,
+         threads: int = 8) -> np.ndarray:
+    """Reference column-major GEMM (cublas_kernels.metal:969-1045); updates and returns C.
+
+    16-bit operands are passed as uint16 bit patterns.  entries=(rows, batch*n + cols)
+    evaluates only those entries of C."""
+    A = np.ascontiguousarray(A)
+    B = np.ascontiguousarray(B)
+    assert C.flags["C_CONTIGUOUS"]
+    rows = cols = None
+    ne = 0
+    if entries is not None:
+        rows = np.ascontiguousarray(entries[0], dtype=np.int32)
+        cols = np.ascontiguousarray(entries[1], dtype=np.int32)
+        ne = len(rows)
+    lib().oracle_gemm(GEMM_TYPES[type_], int(transa), int(transb), m, n, k, alpha, A.ctypes.data,
+                      lda, stride_a, B.ctypes.data, ldb, stride_b, beta, C.ctypes.data, ldc,
+                      stride_c, batch, int(accum_f64),
+                      rows.ctypes.data if rows is not None else None,
+                      cols.ctypes.data if cols is not None else None, ne, threads)
+    return C
+
+
+def half_bits(a: np.ndarray) -> np.ndarray:
+    return np.ascontiguousarray(a, dtype=np.float32).astype(np.float16).view(np.uint16)
+
+
 def bf16_bits(a: np.ndarray) -> np.ndarray:
     """float32 -> bfloat16 bit patterns (round to nearest even)."""
     u = np.ascontiguousarray(a, dtype=np.float32).view(np.uint32).astype(np.uint64)

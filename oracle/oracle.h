@@ -63,6 +63,17 @@ float oracle_bf16_round(float v);
  * accum_f64 != 0: accumulate in double (ground truth) instead of the sequential fp32 fma. */
 void oracle_conv2d_fwd(const void* x, const void* w, void* y, const OracleConvParams* p, int bf16,
                        int accum_f64, int threads);
+/* ---- GEMM (libraries/blas/shaders/cublas_kernels.metal:969-1045) ---- */
+/* type 0 fp32, 1 fp16, 2 bf16 (A, B, C all of that type); column-major.
+ * rows/cols (optional, n_entries long): evaluate only entries (rows[t], cols[t] % n)
+ * of batch cols[t] / n. */
+float oracle_half_round(float v);
+void oracle_gemm(int type, int transa, int transb, int m, int n, int k, float alpha,
+                 const void* A, int64_t lda, int64_t stride_a, const void* B, int64_t ldb,
+                 int64_t stride_b, float beta, void* C, int64_t ldc, int64_t stride_c, int batch,
+                 int accum_f64, const int32_t* rows, const int32_t* cols, int64_t n_entries,
+                 int threads);
+
 /* ---- C2C FFT (libraries/fft/src/cufft_exec.mm:101-211) ---- */
 /* in/out: interleaved complex64 with element strides; use_double != 0 writes the
  * double-precision result to out_f64 (same layout) instead of out. */

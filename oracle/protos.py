@@ -33,6 +33,10 @@ _PROTOS: list[tuple[str, list, object]] = [
     ("oracle_conv2d_fwd", [vp, vp, vp, C.POINTER(ConvParams), C.c_int, C.c_int, C.c_int], None),
     ("oracle_softmax_fwd", [fp, fp, C.POINTER(Tensor4), C.POINTER(Tensor4), C.c_int, C.c_int,
                             C.c_float, C.c_float, C.c_int], None),
+    ("oracle_half_round", [C.c_float], C.c_float),
+    ("oracle_gemm", [C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_float, vp,
+                     C.c_int64, C.c_int64, vp, C.c_int64, C.c_int64, C.c_float, vp, C.c_int64,
+                     C.c_int64, C.c_int, C.c_int, vp, vp, C.c_int64, C.c_int], None),
     ("oracle_fft_c2c", [vp, vp, C.c_int, vp, C.c_int64, C.c_int64, C.c_int64, C.c_int64,
                         C.c_int64, C.c_int, C.c_int, vp, C.c_int], None),
     ("oracle_spmv_csr", [C.c_int64, vp, vp, vp, C.c_int, vp, vp, C.c_float, C.c_float, vp,

@@ -18,6 +18,7 @@ HEADER_LIB = {
     "cudnn.h": "cudnn",
     "cusparse.h": "cusparse",
     "cufft.h": "cufft",
+    "cublas_v2.h": "cublas",
 }
 
 

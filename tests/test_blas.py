@@ -1,0 +1,250 @@
+"""cublasSgemm / cublasSgemmStridedBatched / cublasGemmEx / cublasGemmStridedBatchedEx /
+cublasHgemm.
+
+CPU: the oracle against the reference's known answers, and the handle logic.
+GPU (marked): the CUDA paths through the C ABI against the oracle.  Bar: fp32
+within 1e-5 normwise relative error of the double-accumulated product; 16-bit
+outputs within 1e-2 normwise relative error.
+"""
+
+import ctypes as C
+
+import numpy as np
+import pytest
+
+import oracle
+from muda_b200 import capi
+from tests.helpers import stream_ptr
+
+OPS = {False: capi.CUBLAS_OP_N, True: capi.CUBLAS_OP_T}
+
+
+def ref_case_inputs(m, n, k, ta, tb):
+    """tests/cublas_test.cpp:299-315."""
+    lda = k if ta else m
+    ldb = n if tb else k
+    A = ((np.arange(lda * (m if ta else k)) % 13) + 1).astype(np.float32) * np.float32(0.1)
+    B = ((np.arange(ldb * (k if tb else n)) % 11) + 1).astype(np.float32) * np.float32(0.1)
+    C = np.full(m * n, 2.0, np.float32)
+    return A, lda, B, ldb, C
+
+
+def op_matrix(X, ld, rows, cols, trans):
+    """op(X) as a dense (rows x cols) float64 array from a column-major buffer."""
+    if trans:
+        return X.reshape(-1, ld)[:rows, :cols].astype(np.float64)
+    return X.reshape(-1, ld).T[:rows, :cols].astype(np.float64)
+
+
+@pytest.mark.parametrize("m,n,k,ta,tb", [(32, 24, 40, False, False), (32, 24, 40, True, False),
+                                         (32, 24, 40, False, True), (32, 24, 40, True, True),
+                                         (128, 96, 64, False, False), (96, 128, 64, True, False)])
+def test_oracle_reference_sgemm_pin(m, n, k, ta, tb):
+    """tests/cublas_test.cpp:299-380 (alpha 1.25, beta 0.5, C = 2, abs tol 1e-2)."""
+    A, lda, B, ldb, C = ref_case_inputs(m, n, k, ta, tb)
+    oracle.gemm("f32", ta, tb, m, n, k, 1.25, A, lda, B, ldb, 0.5, C, m)
+    want = 1.25 * op_matrix(A, lda, m, k, ta) @ op_matrix(B, ldb, k, n, tb) + 1.0
+    assert np.max(np.abs(C.reshape(n, m).T - want)) < 1e-2
+
+
+def test_oracle_reference_hgemm_and_batched_pins():
+    """tests/cublas_test.cpp:383-441: 16^3 HGEMM of 0.5 * 0.25 -> 2.0; batch-3 8^3 SGEMM
+    of 1 * 0.5 -> 4.0."""
+    H = np.zeros(256, np.uint16)
+    oracle.gemm("f16", False, False, 16, 16, 16, 1.0, oracle.half_bits(np.full(256, 0.5)), 16,
+                oracle.half_bits(np.full(256, 0.25)), 16, 0.0, H, 16)
+    assert np.all(np.abs(H.view(np.float16).astype(np.float32) - 2.0) < 1e-2)
+    Cb = np.zeros(3 * 64, np.float32)
+    oracle.gemm("f32", False, False, 8, 8, 8, 1.0, np.ones(192, np.float32), 8,
+                np.full(192, 0.5, np.float32), 8, 0.0, Cb, 8, stride_a=64, stride_b=64,
+                stride_c=64, batch=3)
+    assert np.all(np.abs(Cb - 4.0) < 1e-4)
+
+
+def test_handle_logic(built):
+    L = capi.cublas()
+    h = C.c_void_p()
+    assert L.cublasCreate_v2(None) == capi.CUBLAS_STATUS_INVALID_VALUE
+    assert L.cublasCreate_v2(C.byref(h)) == 0
+    v = C.c_int()
+    assert L.cublasGetVersion_v2(h, C.byref(v)) == 0 and v.value == 12000
+    assert L.cublasSetPointerMode_v2(h, 1) == 0
+    assert L.cublasGetPointerMode_v2(h, C.byref(v)) == 0 and v.value == 1
+    assert L.cublasSetPointerMode_v2(h, 2) == capi.CUBLAS_STATUS_INVALID_VALUE
+    assert L.cublasSetMathMode(h, 3) == 0
+    assert L.cublasGetMathMode(h, C.byref(v)) == 0 and v.value == 3
+    assert L.cublasSetMathMode(h, 4) == capi.CUBLAS_STATUS_INVALID_VALUE
+    assert L.cublasSetPointerMode_v2(h, 0) == 0
+    assert L.cublasGetStatusName(15) == b"CUBLAS_STATUS_NOT_SUPPORTED"
+    one = C.byref(C.c_float(1.0))
+    p = C.c_void_p(256)
+    # argument checks (cublas_level3.mm:515-531)
+    assert L.cublasSgemm_v2(h, 3, 0, 4, 4, 4, one, p, 4, p, 4, one, p, 4) == \
+        capi.CUBLAS_STATUS_INVALID_VALUE
+    assert L.cublasSgemm_v2(h, 0, 0, -1, 4, 4, one, p, 4, p, 4, one, p, 4) == \
+        capi.CUBLAS_STATUS_INVALID_VALUE
+    assert L.cublasSgemm_v2(h, 0, 0, 4, 4, 4, one, p, 3, p, 4, one, p, 4) == \
+        capi.CUBLAS_STATUS_INVALID_VALUE
+    assert L.cublasSgemm_v2(h, 0, 0, 4, 4, 4, None, p, 4, p, 4, one, p, 4) == \
+        capi.CUBLAS_STATUS_INVALID_VALUE
+    # zero-size problems succeed without touching memory
+    assert L.cublasSgemm_v2(h, 0, 0, 0, 4, 4, one, p, 1, p, 4, one, p, 1) == 0
+    # unaddressable operands are rejected before launch
+    assert L.cublasSgemm_v2(h, 0, 0, 4, 4, 4, one, p, 4, p, 4, one, p, 4) == \
+        capi.CUBLAS_STATUS_INVALID_VALUE
+    # unsupported type combinations (cublas_level3.mm:607)
+    assert L.cublasGemmEx(h, 0, 0, 4, 4, 4, one, p, 0, 4, p, 2, 4, one, p, 0, 4, 68, -1) == \
+        capi.CUBLAS_STATUS_NOT_SUPPORTED
+    assert L.cublasDestroy_v2(h) == 0
+    assert L.cublasDestroy_v2(h) == capi.CUBLAS_STATUS_NOT_INITIALIZED
+    assert L.cublasSgemm_v2(h, 0, 0, 4, 4, 4, one, p, 4, p, 4, one, p, 4) == \
+        capi.CUBLAS_STATUS_NOT_INITIALIZED
+
+
+# --------------------------------------------------------------------- GPU --
+class Blas:
+    def __init__(self, torch):
+        self.L = capi.cublas()
+        self.h = C.c_void_p()
+        assert self.L.cublasCreate_v2(C.byref(self.h)) == 0
+        assert self.L.cublasSetStream_v2(self.h, C.c_void_p(stream_ptr(torch))) == 0
+
+    def close(self):
+        assert self.L.cublasDestroy_v2(self.h) == 0
+
+
+def normwise(got, want):
+    return np.linalg.norm(got.astype(np.float64) - want) / max(np.linalg.norm(want), 1e-300)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("m,n,k,ta,tb", [(32, 24, 40, False, False), (32, 24, 40, True, False),
+                                         (32, 24, 40, False, True), (32, 24, 40, True, True),
+                                         (128, 96, 64, False, False), (96, 128, 64, True, False)])
+def test_gpu_reference_sgemm_pin(cuda, built, m, n, k, ta, tb):
+    torch = cuda
+    A, lda, B, ldb, C0 = ref_case_inputs(m, n, k, ta, tb)
+    b = Blas(torch)
+    dA, dB, dC = (torch.from_numpy(x).cuda() for x in (A, B, C0))
+    al, be = C.c_float(1.25), C.c_float(0.5)
+    st = b.L.cublasSgemm_v2(b.h, OPS[ta], OPS[tb], m, n, k, C.byref(al), C.c_void_p(dA.data_ptr()),
+                            lda, C.c_void_p(dB.data_ptr()), ldb, C.byref(be),
+                            C.c_void_p(dC.data_ptr()), m)
+    b.close()
+    assert st == 0
+    want = 1.25 * op_matrix(A, lda, m, k, ta) @ op_matrix(B, ldb, k, n, tb) + 1.0
+    got = dC.cpu().numpy().reshape(n, m).T
+    assert np.max(np.abs(got - want)) < 1e-2
+
+
+def rand_case(rng, m, n, k, ta, tb, batch, pad=3):
+    lda = (k if ta else m) + pad
+    ldb = (n if tb else k) + pad
+    ldc = m + pad
+    sa = lda * (m if ta else k) + 5
+    sb = ldb * (k if tb else n) + 7
+    sc = ldc * n + 11
+    A = rng.uniform(-1, 1, sa * batch).astype(np.float32)
+    B = rng.uniform(-1, 1, sb * batch).astype(np.float32)
+    Cm = rng.uniform(-1, 1, sc * batch).astype(np.float32)
+    return A, lda, sa, B, ldb, sb, Cm, ldc, sc
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("m,n,k", [(1, 1, 1), (7, 5, 3), (33, 65, 17), (128, 128, 8),
+                                   (130, 257, 129), (300, 64, 1000), (1024, 1024, 1024)])
+@pytest.mark.parametrize("ta,tb", [(False, False), (True, False), (False, True), (True, True)])
+def test_gpu_sgemm_matches_oracle(cuda, built, m, n, k, ta, tb):
+    torch = cuda
+    rng = np.random.default_rng(m * 31 + n * 7 + k)
+    batch = 2 if m * n * k < (1 << 24) else 1
+    A, lda, sa, B, ldb, sb, C0, ldc, sc = rand_case(rng, m, n, k, ta, tb, batch)
+    alpha, beta = 0.75, (0.0 if k % 2 else -1.5)
+    dA, dB, dC = (torch.from_numpy(x).cuda() for x in (A, B, C0))
+    b = Blas(torch)
+    st = b.L.cublasSgemmStridedBatched(b.h, OPS[ta], OPS[tb], m, n, k,
+                                       C.byref(C.c_float(alpha)), C.c_void_p(dA.data_ptr()), lda,
+                                       sa, C.c_void_p(dB.data_ptr()), ldb, sb,
+                                       C.byref(C.c_float(beta)), C.c_void_p(dC.data_ptr()), ldc,
+                                       sc, batch)
+    b.close()
+    assert st == 0
+    got = dC.cpu().numpy()
+    want = oracle.gemm("f32", ta, tb, m, n, k, alpha, A, lda, B, ldb, beta, C0.copy(), ldc,
+                       stride_a=sa, stride_b=sb, stride_c=sc, batch=batch, accum_f64=True)
+    for z in range(batch):
+        idx = (z * sc + np.arange(n)[:, None] * ldc + np.arange(m)[None, :]).reshape(-1)
+        assert normwise(got[idx], want[idx].astype(np.float64)) <= 1e-5
+    # entries outside the m x n windows are untouched
+    mask = np.ones(len(got), bool)
+    for z in range(batch):
+        mask[(z * sc + np.arange(n)[:, None] * ldc + np.arange(m)[None, :]).reshape(-1)] = False
+    assert np.array_equal(got[mask], C0[mask])
+
+
+@pytest.mark.gpu
+def test_gpu_sgemm_device_pointer_mode(cuda, built):
+    torch = cuda
+    rng = np.random.default_rng(1)
+    m = n = k = 64
+    A, lda, sa, B, ldb, sb, C0, ldc, sc = rand_case(rng, m, n, k, False, False, 1, pad=0)
+    dA, dB, dC = (torch.from_numpy(x).cuda() for x in (A, B, C0))
+    scal = torch.tensor([2.0, 0.5], dtype=torch.float32, device="cuda")
+    b = Blas(torch)
+    assert b.L.cublasSetPointerMode_v2(b.h, capi.CUBLAS_POINTER_MODE_DEVICE) == 0
+    st = b.L.cublasSgemm_v2(b.h, 0, 0, m, n, k, C.c_void_p(scal.data_ptr()),
+                            C.c_void_p(dA.data_ptr()), lda, C.c_void_p(dB.data_ptr()), ldb,
+                            C.c_void_p(scal.data_ptr() + 4), C.c_void_p(dC.data_ptr()), ldc)
+    b.close()
+    assert st == 0
+    want = oracle.gemm("f32", False, False, m, n, k, 2.0, A, lda, B, ldb, 0.5, C0.copy(), ldc,
+                       accum_f64=True)
+    assert normwise(dC.cpu().numpy(), want.astype(np.float64)) <= 1e-5
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("typ", ["f16", "bf16"])
+@pytest.mark.parametrize("m,n,k,ta,tb,batch", [(16, 16, 16, False, False, 1),
+                                               (100, 70, 50, True, False, 2),
+                                               (64, 128, 96, False, True, 1),
+                                               (256, 256, 256, False, False, 3),
+                                               (512, 384, 1024, True, True, 1)])
+def test_gpu_gemm_ex_16bit(cuda, built, typ, m, n, k, ta, tb, batch):
+    torch = cuda
+    rng = np.random.default_rng(k)
+    A, lda, sa, B, ldb, sb, C0, ldc, sc = rand_case(rng, m, n, k, ta, tb, batch, pad=0)
+    conv = oracle.half_bits if typ == "f16" else oracle.bf16_bits
+    A16, B16, C16 = conv(A), conv(B), conv(C0)
+    dA, dB, dC = (torch.from_numpy(x.view(np.int16).copy()).cuda() for x in (A16, B16, C16))
+    dtype = capi.CUDA_R_16F if typ == "f16" else capi.CUDA_R_16BF
+    b = Blas(torch)
+    st = b.L.cublasGemmStridedBatchedEx(
+        b.h, OPS[ta], OPS[tb], m, n, k, C.byref(C.c_float(1.0)), C.c_void_p(dA.data_ptr()), dtype,
+        lda, sa, C.c_void_p(dB.data_ptr()), dtype, ldb, sb, C.byref(C.c_float(0.5)),
+        C.c_void_p(dC.data_ptr()), dtype, ldc, sc, batch, capi.CUBLAS_COMPUTE_32F, -1)
+    b.close()
+    assert st == 0
+    got = dC.cpu().numpy().view(np.uint16)
+    want = oracle.gemm(typ, ta, tb, m, n, k, 1.0, A16, lda, B16, ldb, 0.5, C16.copy(), ldc,
+                       stride_a=sa, stride_b=sb, stride_c=sc, batch=batch)
+    dec = (lambda v: v.view(np.float16).astype(np.float64)) if typ == "f16" else \
+        (lambda v: oracle.bf16_to_f32(v).astype(np.float64))
+    assert normwise(dec(got), dec(want)) <= 1e-2
+
+
+@pytest.mark.gpu
+def test_gpu_hgemm_reference_pin(cuda, built):
+    """tests/cublas_test.cpp:383-410: 16^3, A = 0.5, B = 0.25 -> 2.0 (fp16 scalars)."""
+    torch = cuda
+    a = torch.from_numpy(oracle.half_bits(np.full(256, 0.5)).view(np.int16).copy()).cuda()
+    bb = torch.from_numpy(oracle.half_bits(np.full(256, 0.25)).view(np.int16).copy()).cuda()
+    c = torch.zeros(256, dtype=torch.int16, device="cuda")
+    one = C.c_uint16(0x3C00)
+    zero = C.c_uint16(0)
+    b = Blas(torch)
+    st = b.L.cublasHgemm(b.h, 0, 0, 16, 16, 16, C.byref(one), C.c_void_p(a.data_ptr()), 16,
+                         C.c_void_p(bb.data_ptr()), 16, C.byref(zero), C.c_void_p(c.data_ptr()), 16)
+    b.close()
+    assert st == 0
+    got = c.cpu().numpy().view(np.float16).astype(np.float32)
+    assert np.all(np.abs(got - 2.0) < 1e-2)

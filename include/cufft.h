@@ -78,6 +78,27 @@ cufftResult cufftDestroy(cufftHandle plan);
 /* Execution — reference cufft_exec.mm:101-211 */
 cufftResult cufftExecC2C(cufftHandle plan, cufftComplex* idata, cufftComplex* odata, int direction);
 
+/* Allocation-free execution.  No counterpart in the reference: an addition of
+ * this library for callers that cannot allocate device memory when they need a
+ * transform (inside an allocator or memory-pool callback, in real-time paths
+ * that forbid allocation after start-up, or under a hard memory cap), since a
+ * plan allocates its tables and workspace.
+ *
+ * Transforms `batch` contiguous sequences of n complex values (n a power of two,
+ * 2 <= n <= 1048576; larger or non-power-of-two n returns CUFFT_INVALID_SIZE),
+ * same conventions as cufftExecC2C (sign from `direction`, no scaling, in place
+ * allowed), on `stream`.  Twiddle tables and the workspace live in one fixed
+ * device array of about 16.3 MiB that the library reserves on every GPU it is
+ * loaded on and keeps until the process exits; the call calls no cudaMalloc,
+ * cudaFree or other allocator.  The first call on a device looks up that
+ * array's device address (cudaGetSymbolAddress); make that first call before
+ * any stream capture.  Every call rewrites the tables and workspace it reads, so
+ * no state carries over from one call to the next, but all calls share the one
+ * array: calls that can overlap on the GPU (different streams, or different
+ * host threads) race and must be serialised by the caller. */
+cufftResult cufftExecC2CNoAlloc(cufftComplex* idata, cufftComplex* odata, long long n,
+                                long long batch, int direction, cudaStream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -36,7 +36,8 @@ LIBS: dict[str, list[str]] = {
     "cudnn": ["dnn/cudnn_api.cpp", "dnn/softmax_kernels.cu", "dnn/conv_direct_kernels.cu",
               "dnn/conv_dispatch.cu"],
     "cusparse": ["sparse/cusparse_api.cpp", "sparse/spmv_kernels.cu"],
-    "cufft": ["fft/cufft_api.cpp", "fft/stockham_kernels.cu", "fft/dft_kernels.cu"],
+    "cufft": ["fft/cufft_api.cpp", "fft/stockham_kernels.cu", "fft/dft_kernels.cu",
+              "fft/fft_static.cu"],
     "cublas": ["blas/cublas_api.cpp", "blas/gemm_simt_kernels.cu", "blas/gemm_tc_kernels.cu"],
 }
 

@@ -233,6 +233,52 @@ def test_gpu_gemm_ex_16bit(cuda, built, typ, m, n, k, ta, tb, batch):
 
 
 @pytest.mark.gpu
+@pytest.mark.parametrize("typ", ["bf16", "f16"])
+@pytest.mark.parametrize("m,n,k,batch,beta", [(128, 256, 64, 1, 0.0), (256, 512, 1024, 2, 0.0),
+                                              (300, 520, 200, 1, 0.5), (1000, 1000, 1000, 1, 0.0),
+                                              (129, 257, 65, 3, -1.0), (2048, 2048, 2048, 1, 0.0)])
+def test_gpu_gemm_ex_tensor_core_layout(cuda, built, typ, m, n, k, batch, beta):
+    """transa = T, transb = N (both operands K-major): the tcgen05 kernel's layout, with
+    partial tiles in M, N and K, batches, and beta != 0."""
+    torch = cuda
+    rng = np.random.default_rng(m + n + k)
+    lda = k + (8 if m % 2 else 0)
+    ldb = k + 8
+    ldc = m + 1
+    sa, sb, sc = lda * m + 64, ldb * n, ldc * n + 3
+    A = rng.uniform(-1, 1, sa * batch).astype(np.float32)
+    B = rng.uniform(-1, 1, sb * batch).astype(np.float32)
+    C0 = rng.uniform(-1, 1, sc * batch).astype(np.float32)
+    conv = oracle.half_bits if typ == "f16" else oracle.bf16_bits
+    A16, B16, C16 = conv(A), conv(B), conv(C0)
+    dA, dB, dC = (torch.from_numpy(x.view(np.int16).copy()).cuda() for x in (A16, B16, C16))
+    dtype = capi.CUDA_R_16F if typ == "f16" else capi.CUDA_R_16BF
+    b = Blas(torch)
+    st = b.L.cublasGemmStridedBatchedEx(
+        b.h, capi.CUBLAS_OP_T, capi.CUBLAS_OP_N, m, n, k, C.byref(C.c_float(1.0)),
+        C.c_void_p(dA.data_ptr()), dtype, lda, sa, C.c_void_p(dB.data_ptr()), dtype, ldb, sb,
+        C.byref(C.c_float(beta)), C.c_void_p(dC.data_ptr()), dtype, ldc, sc, batch,
+        capi.CUBLAS_COMPUTE_32F, -1)
+    b.close()
+    assert st == 0
+    got = dC.cpu().numpy().view(np.uint16)
+    # sampled check against the oracle (full check for the small shapes)
+    dec = (lambda v: v.view(np.float16).astype(np.float64)) if typ == "f16" else \
+        (lambda v: oracle.bf16_to_f32(v).astype(np.float64))
+    want = C16.copy()
+    oracle.gemm(typ, True, False, m, n, k, 1.0, A16, lda, B16, ldb, beta, want, ldc,
+                stride_a=sa, stride_b=sb, stride_c=sc, batch=batch, threads=16)
+    for z in range(batch):
+        idx = (z * sc + np.arange(n)[:, None] * ldc + np.arange(m)[None, :]).reshape(-1)
+        assert normwise(dec(got[idx]), dec(want[idx])) <= 1e-2
+    # untouched padding between columns and batches
+    mask = np.ones(len(got), bool)
+    for z in range(batch):
+        mask[(z * sc + np.arange(n)[:, None] * ldc + np.arange(m)[None, :]).reshape(-1)] = False
+    assert np.array_equal(got[mask], C16[mask])
+
+
+@pytest.mark.gpu
 def test_gpu_hgemm_reference_pin(cuda, built):
     """tests/cublas_test.cpp:383-410: 16^3, A = 0.5, B = 0.25 -> 2.0 (fp16 scalars)."""
     torch = cuda

@@ -34,7 +34,7 @@ ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 LIBS: dict[str, list[str]] = {
     "curand": ["rand/curand_api.cpp", "rand/philox_kernels.cu"],
     "cudnn": ["dnn/cudnn_api.cpp", "dnn/softmax_kernels.cu", "dnn/conv_direct_kernels.cu",
-              "dnn/conv_dispatch.cu"],
+              "dnn/conv_tc_kernels.cu", "dnn/conv_dispatch.cu"],
     "cusparse": ["sparse/cusparse_api.cpp", "sparse/spmv_kernels.cu"],
     "cufft": ["fft/cufft_api.cpp", "fft/stockham_kernels.cu", "fft/dft_kernels.cu",
               "fft/fft_static.cu"],

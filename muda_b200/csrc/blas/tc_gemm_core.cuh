@@ -1,0 +1,264 @@
+// tc_gemm_core.cuh — persistent warp-specialized tcgen05 main loop shared by the
+// bf16/fp16 GEMM and the NHWC implicit-GEMM convolution.
+//
+// One CTA per SM walks output tiles of 128 x BN (fp32 accumulators in tensor
+// memory) with a K loop of 64-element blocks:
+//   warp 0     one thread issues the TMA loads of each k-block (A: 128 rows x 128 B,
+//              B: BN rows x 128 B, 128-byte swizzle) into a STAGES-deep ring;
+//   warp 1     allocates 2*BN tensor-memory columns; one thread issues
+//              tcgen05.mma M128 N=BN K16 (four per k-block) and commits each stage
+//              back to the producer and each finished tile to the epilogue;
+//   warps 2-5  epilogue: tcgen05.ld of their 32-lane quarter, 32 columns at a time,
+//              handed to the problem's store(); the second accumulator lets the
+//              next tile's MMAs overlap this tile's epilogue.
+//
+// The problem type P supplies the geometry (a __grid_constant__ kernel parameter,
+// so its CUtensorMap members live in parameter space as TMA requires):
+//   long long tiles_total;  int num_kb;
+//   void prefetch() const;                                  // tensor-map prefetch
+//   void coords(long long t, int (&c)[3]) const;            // tile index -> coordinates
+//   void load(const int (&c)[3], int kb, void* sa, void* sb, uint64_t* bar) const;
+//   void scalars(float& alpha, float& beta) const;
+//   void store(const int (&c)[3], int row, int col0, const float (&v)[32], float alpha,
+//              float beta) const;                           // row in [0,128), 32 columns
+//
+// Every mbarrier wait is bounded (tc_ptx.cuh).  A wait that runs out marks the CTA
+// aborted, counts the event in the problem's timeout counter, drains the copies and
+// MMAs the CTA issued (bounded), frees its tensor memory and returns.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+#include "blas/tc_ptx.cuh"
+
+namespace mb200::tc {
+
+constexpr int kBM = 128;
+constexpr int kBK = 64;  // 64 x 2 bytes = one 128-byte swizzle row
+constexpr int kUmmaK = 16;
+constexpr int kAcc = 2;
+constexpr int kThreads = 192;
+
+template <int BN, int STAGES>
+struct CoreShape {
+  static constexpr int A_STAGE = kBM * kBK * 2;
+  static constexpr int B_STAGE = BN * kBK * 2;
+  static constexpr int BAR_BYTES = 256;
+  static constexpr int SMEM = STAGES * (A_STAGE + B_STAGE) + BAR_BYTES + 1024;
+  static constexpr std::uint32_t TMEM_COLS = 2 * BN < 32 ? 32 : 2 * BN;
+};
+
+template <class P, int BN, int STAGES, int FMT>
+__global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(const __grid_constant__ P p,
+                                                              unsigned int* timeouts) {
+  using S = CoreShape<BN, STAGES>;
+  extern __shared__ std::uint8_t smem_raw[];
+  std::uint8_t* base = reinterpret_cast<std::uint8_t*>(
+      (reinterpret_cast<std::uintptr_t>(smem_raw) + 1023) & ~std::uintptr_t{1023});
+  std::uint8_t* sa = base;
+  std::uint8_t* sb = base + STAGES * S::A_STAGE;
+  std::uint64_t* full = reinterpret_cast<std::uint64_t*>(sb + STAGES * S::B_STAGE);
+  std::uint64_t* empty = full + STAGES;
+  std::uint64_t* acc_full = empty + STAGES;
+  std::uint64_t* acc_empty = acc_full + kAcc;
+  std::uint64_t* mma_done = acc_empty + kAcc;
+  std::uint32_t* tmem_slot = reinterpret_cast<std::uint32_t*>(mma_done + 1);
+  volatile int* aborted = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < kAcc; ++a) {
+      mbar_init(&acc_full[a], 1);
+      mbar_init(&acc_empty[a], 4);  // one arrival per epilogue warp
+    }
+    mbar_init(mma_done, 1);
+    *aborted = 0;
+    mbar_fence_init();
+    p.prefetch();
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, S::TMEM_COLS);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const std::uint32_t tmem_base = *tmem_slot;
+  const int num_kb = p.num_kb;
+  auto fail = [&]() {
+    *aborted = 1;
+    atomicAdd(timeouts, 1u);
+  };
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------- TMA producer
+      int stage = 0;
+      std::uint32_t phase = 0;
+      std::uint32_t issued_phase[STAGES];
+      bool issued[STAGES];
+      for (int s = 0; s < STAGES; ++s) issued[s] = false;
+      for (long long t = blockIdx.x; t < p.tiles_total && !*aborted; t += gridDim.x) {
+        int c[3];
+        p.coords(t, c);
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1u)) {
+            fail();
+            break;
+          }
+          mbar_arrive_expect_tx(&full[stage], S::A_STAGE + S::B_STAGE);
+          p.load(c, kb, sa + stage * S::A_STAGE, sb + stage * S::B_STAGE, &full[stage]);
+          issued[stage] = true;
+          issued_phase[stage] = phase;
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      // Drain: every issued copy has landed before the CTA may retire.
+      for (int s = 0; s < STAGES; ++s)
+        if (issued[s] && !mbar_wait(&full[s], issued_phase[s])) fail();
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ---------------- MMA issuer
+      constexpr std::uint32_t idesc = f16_idesc(FMT, kBM, BN);
+      int stage = 0;
+      std::uint32_t phase = 0;
+      int acc = 0;
+      std::uint32_t acc_phase = 0;
+      for (long long t = blockIdx.x; t < p.tiles_total && !*aborted; t += gridDim.x) {
+        if (!mbar_wait(&acc_empty[acc], acc_phase ^ 1u)) {
+          fail();
+          break;
+        }
+        tc_fence_after();
+        const std::uint32_t d_tmem = tmem_base + static_cast<std::uint32_t>(acc * BN);
+        bool ok = true;
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(&full[stage], phase)) {
+            fail();
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const std::uint32_t a0 = smem_addr(sa + stage * S::A_STAGE);
+          const std::uint32_t b0 = smem_addr(sb + stage * S::B_STAGE);
+#pragma unroll
+          for (int k = 0; k < kBK / kUmmaK; ++k) {
+            mma_f16(d_tmem, kmajor_sw128_desc(a0 + k * kUmmaK * 2),
+                    kmajor_sw128_desc(b0 + k * kUmmaK * 2), idesc, (kb | k) != 0 ? 1u : 0u);
+          }
+          mma_commit(&empty[stage]);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        mma_commit(&acc_full[acc]);
+        if (++acc == kAcc) {
+          acc = 0;
+          acc_phase ^= 1u;
+        }
+      }
+      // Drain: all issued MMAs have completed before tensor memory is freed.
+      mma_commit(mma_done);
+      if (!mbar_wait(mma_done, 0)) fail();
+    }
+  } else {
+    // ---------------- epilogue (warps 2..5, one 32-lane quarter each)
+    const int quarter = warp & 3;
+    float alpha, beta;
+    p.scalars(alpha, beta);
+    int acc = 0;
+    std::uint32_t acc_phase = 0;
+    for (long long t = blockIdx.x; t < p.tiles_total && !*aborted; t += gridDim.x) {
+      int c[3];
+      p.coords(t, c);
+      if (!mbar_wait(&acc_full[acc], acc_phase)) {
+        fail();
+        break;
+      }
+      tc_fence_after();
+      const int row = quarter * 32 + lane;
+      const std::uint32_t t_row = tmem_base + (static_cast<std::uint32_t>(quarter * 32) << 16) +
+                                  static_cast<std::uint32_t>(acc * BN);
+#pragma unroll 1
+      for (int c0 = 0; c0 < BN; c0 += 32) {
+        float v[32];
+        tmem_load_32cols(t_row + static_cast<std::uint32_t>(c0), v);
+        p.store(c, row, c0, v, alpha, beta);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[acc]);
+      if (++acc == kAcc) {
+        acc = 0;
+        acc_phase ^= 1u;
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, S::TMEM_COLS);
+  }
+}
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+inline EncodeTiledFn encode_tiled_fn() {
+  static EncodeTiledFn fn = [] {
+    void* q = nullptr;
+    cudaDriverEntryPointQueryResult r{};
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &q, cudaEnableDefault, &r) !=
+            cudaSuccess ||
+        r != cudaDriverEntryPointSuccess)
+      return static_cast<EncodeTiledFn>(nullptr);
+    return reinterpret_cast<EncodeTiledFn>(q);
+  }();
+  return fn;
+}
+
+// Tiled map over a 16-bit tensor of `rank` dims (innermost first, strides in
+// bytes for dims 1..rank-1), box `box`, 128-byte swizzle, zero fill out of bounds.
+inline bool encode_tiled(CUtensorMap* map, int fmt, const void* base, int rank,
+                         const cuuint64_t* dims, const cuuint64_t* strides_bytes,
+                         const cuuint32_t* box) {
+  EncodeTiledFn fn = encode_tiled_fn();
+  if (fn == nullptr) return false;
+  const cuuint32_t estr[5] = {1u, 1u, 1u, 1u, 1u};
+  return fn(map, fmt == 1 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+            static_cast<cuuint32_t>(rank), const_cast<void*>(base), dims, strides_bytes, box,
+            estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) ==
+         CUDA_SUCCESS;
+}
+
+template <class P, int BN, int STAGES, int FMT>
+cudaError_t launch_tc_gemm(const P& p, int sms, unsigned int* timeouts, cudaStream_t stream) {
+  using S = CoreShape<BN, STAGES>;
+  auto kern = tc_gemm_kernel<P, BN, STAGES, FMT>;
+  const cudaError_t e =
+      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::SMEM);
+  if (e != cudaSuccess) return e;
+  const long long grid = p.tiles_total < sms ? p.tiles_total : sms;
+  if (grid <= 0) return cudaSuccess;
+  kern<<<static_cast<unsigned>(grid), kThreads, S::SMEM, stream>>>(p, timeouts);
+  return cudaGetLastError();
+}
+
+}  // namespace mb200::tc

@@ -77,6 +77,19 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, s
       : "memory");
 }
 
+// 4-D tiled TMA load (e.g. an NHWC activation rectangle); coordinates outside the
+// tensor read as zero.  The innermost coordinate must be 16-byte aligned.
+__device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, std::int32_t x,
+                                            std::int32_t y, std::int32_t z, std::int32_t w,
+                                            std::uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3, %4, %5}], [%6];" ::"r"(smem_addr(dst)),
+      "l"(reinterpret_cast<std::uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(w),
+      "r"(smem_addr(bar))
+      : "memory");
+}
+
 __device__ __forceinline__ void prefetch_tensormap(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<std::uint64_t>(map)) : "memory");
 }

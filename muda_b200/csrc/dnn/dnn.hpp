@@ -46,6 +46,13 @@ enum class ConvDtype : int { kF32 = 0, kBF16 = 1 };
 cudaError_t launch_conv_direct(const void* x, const void* w, void* y, const ConvShape& s,
                                ConvDtype dt, float alpha, float beta, cudaStream_t stream) noexcept;
 
+// tcgen05 implicit-GEMM kernel: 16-bit NHWC input/output, KRSC filter, groups 1,
+// stride 1, C a multiple of 64.  cudaErrorNotSupported for other geometries.
+bool conv_tc_supported(const ConvShape& s, ConvDtype dt, const void* x, const void* w,
+                       const void* y) noexcept;
+cudaError_t launch_conv_tc(const void* x, const void* w, void* y, const ConvShape& s,
+                           ConvDtype dt, float alpha, float beta, cudaStream_t stream) noexcept;
+
 // Picks the fastest kernel that supports the geometry and launches it.
 cudaError_t launch_conv(const void* x, const void* w, void* y, const ConvShape& s, ConvDtype dt,
                         float alpha, float beta, cudaStream_t stream) noexcept;

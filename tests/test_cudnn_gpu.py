@@ -127,6 +127,62 @@ def test_conv_bf16_matches_oracle(cuda, built, case):
     assert normwise(g, wv) <= 1e-2
 
 
+TC_CASES = [
+    # xshape (n, c, h, w), wshape (k, c, r, s), pad, dil, mode, alpha, beta
+    ((2, 64, 14, 14), (64, 64, 3, 3), (1, 1), (1, 1), 1, 1.0, 0.0),
+    ((3, 128, 9, 13), (96, 128, 3, 3), (1, 1), (1, 1), 1, 1.0, 0.0),
+    ((2, 64, 20, 30), (256, 64, 1, 1), (0, 0), (1, 1), 1, 0.5, 0.0),
+    ((1, 192, 17, 17), (300, 192, 3, 3), (0, 2), (2, 1), 1, 1.0, 0.75),
+    ((2, 64, 8, 70), (128, 64, 5, 3), (2, 1), (1, 1), 0, 1.0, 0.0),
+    ((4, 256, 28, 28), (256, 256, 3, 3), (1, 1), (1, 1), 1, 1.0, 0.0),
+]
+
+
+@pytest.mark.parametrize("case", TC_CASES)
+def test_conv_bf16_tensor_core_layout(cuda, built, case):
+    """NHWC input/output, KRSC filter, C a multiple of 64: the tcgen05 implicit GEMM."""
+    xshape, wshape, pad, dil, mode, alpha, beta = case
+    rng = np.random.default_rng(sum(xshape) + sum(wshape))
+    x = oracle.bf16_bits((rng.standard_normal(np.prod(xshape)) * 0.5).astype(np.float32))
+    w = oracle.bf16_bits((rng.standard_normal(np.prod(wshape)) * 0.5).astype(np.float32))
+    n, c, h, wd = xshape
+    k, _, r, s = wshape
+    oh = 1 + (h + 2 * pad[0] - (1 + (r - 1) * dil[0]))
+    ow = 1 + (wd + 2 * pad[1] - (1 + (s - 1) * dil[1]))
+    y0 = oracle.bf16_bits(rng.standard_normal(n * k * oh * ow).astype(np.float32))
+    got, _ = run_conv(cuda, x.view(np.int16), w.view(np.int16), xshape, wshape, x_fmt=NHWC,
+                      w_fmt=NHWC, pad=pad, dil=dil, mode=mode, alpha=alpha, beta=beta,
+                      y0=y0.view(np.int16), dtype=BF16)
+    want = oracle.conv2d(x, w, xshape, wshape, x_fmt="NHWC", w_fmt="NHWC", pad=pad, dil=dil,
+                         mode="conv" if mode == 0 else "cross", alpha=alpha, beta=beta,
+                         y=y0.copy())
+    g = oracle.bf16_to_f32(got.view(np.uint16)).astype(np.float64)
+    wv = oracle.bf16_to_f32(want).astype(np.float64)
+    assert normwise(g, wv) <= 1e-2
+
+
+def test_conv_bf16_config_shape_sampled(cuda, built):
+    """configs[4] conv: NHWC 64x56x56x256 -> 256, 3x3, pad 1 (bf16 extension path); images
+    0 and 63 are checked against the oracle."""
+    torch = cuda
+    from muda_b200 import synth
+    n, c, h, wd, k = 64, 256, 56, 56, 256
+    x = synth.normal(torch, n * h * wd * c, seed=11, std=0.02).to(torch.bfloat16)
+    w = synth.normal(torch, k * 9 * c, seed=11, std=0.02,
+                     offset=(n * h * wd * c + 3) // 4 * 4).to(torch.bfloat16)
+    xb = x.view(torch.int16).cpu().numpy()
+    wb = w.view(torch.int16).cpu().numpy()
+    got, _ = run_conv(torch, xb, wb, (n, c, h, wd), (k, c, 3, 3), x_fmt=NHWC, w_fmt=NHWC,
+                      pad=(1, 1), dtype=BF16)
+    per = h * wd * c
+    for img in (0, 63):
+        xi = xb[img * per:(img + 1) * per].view(np.uint16)
+        want = oracle.conv2d(xi, wb.view(np.uint16), (1, c, h, wd), (k, c, 3, 3), x_fmt="NHWC",
+                             w_fmt="NHWC", pad=(1, 1), threads=16)
+        g = oracle.bf16_to_f32(got[img * h * wd * k:(img + 1) * h * wd * k].view(np.uint16))
+        assert normwise(g.astype(np.float64), oracle.bf16_to_f32(want).astype(np.float64)) <= 1e-2
+
+
 # ---------------------------------------------------------------- softmax --
 def run_softmax(torch, x, shape, algo, mode, alpha=1.0, beta=0.0, y0=None, fmt=NCHW,
                 strides=None):

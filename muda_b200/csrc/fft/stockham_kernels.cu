@@ -26,8 +26,11 @@
 //     butterfly.
 #include <cuda_runtime.h>
 
+#include <array>
 #include <cstdint>
+#include <mutex>
 
+#include "blas/tc_ptx.cuh"
 #include "common/device.hpp"
 #include "fft/fft.hpp"
 
@@ -298,6 +301,206 @@ cudaError_t dispatch(int log2n, const Batch1D& b, cudaStream_t st) {
   }
 }
 
+// ---------------------------------------------------------------------------
+// Bulk-copy pipelined variant for contiguous batches (unit stride, dense batch
+// distance, 16-byte aligned): each persistent CTA owns a ring of two 32 KB
+// staging buffers filled by cp.async.bulk (one copy per group of TPC
+// transforms, completing on an mbarrier).  While the passes of group g run, the
+// copy of group g + gridDim.x is already in flight, and each finished group leaves
+// through one bulk store from the same staging buffer, so loads, compute and
+// stores of different groups overlap without any register staging.
+
+__device__ unsigned int g_fft_bulk_timeouts;
+
+// Pass of the staged kernel: FIRST reads the staging buffer `st`, LAST writes it;
+// every other read and write goes through the padded work arrays.
+template <int LOG2N, int R, int S, bool FIRST, bool LAST>
+__device__ __forceinline__ void spass(float2 (&v)[Plan<LOG2N>::P], int j, int Ns, int log2Ns,
+                                      float2* st, float* sre, float* sim,
+                                      const float2* __restrict__ tw) {
+  using PL = Plan<LOG2N>;
+  constexpr int N = PL::N;
+  constexpr int T = PL::T;
+  constexpr int NB = PL::P / R;
+#pragma unroll
+  for (int q = 0; q < NB; ++q) {
+    const int b = j + q * T;
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      const int idx = b + r * (N / R);
+      v[q * R + r] = FIRST ? st[idx] : make_float2(sre[pad(idx)], sim[pad(idx)]);
+    }
+  }
+  if constexpr (!FIRST || LAST) __syncthreads();  // reads done before the source is rewritten
+#pragma unroll
+  for (int q = 0; q < NB; ++q) {
+    const int b = j + q * T;
+    const int k = b & (Ns - 1);
+    if (Ns > 1) {
+      const int shift = LOG2N - log2Ns - ilog2(R);
+#pragma unroll
+      for (int r = 1; r < R; ++r)
+        v[q * R + r] = cmul(v[q * R + r], table_tw<S>(tw, (r * k) << shift));
+    }
+    dft<R, S>(&v[q * R]);
+    const int idxD = ((b >> log2Ns) << (log2Ns + ilog2(R))) + k;
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      const int o = idxD + r * Ns;
+      if constexpr (LAST) {
+        st[o] = v[q * R + r];
+      } else {
+        sre[pad(o)] = v[q * R + r].x;
+        sim[pad(o)] = v[q * R + r].y;
+      }
+    }
+  }
+  if constexpr (!LAST) __syncthreads();
+}
+
+template <int LOG2N, int S, int PASS = 0>
+__device__ __forceinline__ void run_spasses(float2 (&v)[Plan<LOG2N>::P], int j, float2* st,
+                                            float* sre, float* sim, const float2* tw) {
+  using PL = Plan<LOG2N>;
+  if constexpr (PASS < PL::PASSES) {
+    constexpr int R = (PASS == 0) ? PL::FIRST_R : 16;
+    constexpr int LOG2NS = (PASS == 0) ? 0 : (ilog2(PL::FIRST_R) + 4 * (PASS - 1));
+    spass<LOG2N, R, S, PASS == 0, PASS == PL::PASSES - 1>(v, j, 1 << LOG2NS, LOG2NS, st, sre, sim,
+                                                          tw);
+    run_spasses<LOG2N, S, PASS + 1>(v, j, st, sre, sim, tw);
+  }
+}
+
+template <int LOG2N>
+struct BulkPlan {
+  using PL = Plan<LOG2N>;
+  static constexpr int GROUP = PL::TPC * PL::N;                  // complex values per group
+  static constexpr int GROUP_BYTES = GROUP * 8;
+  static constexpr int WORK_BYTES = PL::TPC * PL::REGION * 2 * 4;
+  static constexpr int SMEM = 2 * GROUP_BYTES + WORK_BYTES + 64;
+};
+
+template <int LOG2N, int S>
+__global__ void __launch_bounds__(Plan<LOG2N>::THREADS, 2)
+    stockham_bulk_kernel(const float2* in, float2* out, long long groups,
+                         const float2* __restrict__ tw, unsigned int* timeouts) {
+  using PL = Plan<LOG2N>;
+  using BP = BulkPlan<LOG2N>;
+  extern __shared__ __align__(16) std::uint8_t bsmem[];
+  float2* stage0 = reinterpret_cast<float2*>(bsmem);
+  float2* stage1 = reinterpret_cast<float2*>(bsmem + BP::GROUP_BYTES);
+  float* work = reinterpret_cast<float*>(bsmem + 2 * BP::GROUP_BYTES);
+  std::uint64_t* full = reinterpret_cast<std::uint64_t*>(bsmem + 2 * BP::GROUP_BYTES +
+                                                         BP::WORK_BYTES);
+  volatile int* ok_flag = reinterpret_cast<volatile int*>(full + 2);
+  const int tloc = threadIdx.x / PL::T;
+  const int j = threadIdx.x % PL::T;
+  float* sre = work + tloc * PL::REGION * 2;
+  float* sim = sre + PL::REGION;
+  const long long stride = gridDim.x;
+  std::uint32_t phase[2] = {0u, 0u};
+  bool pending[2] = {false, false};
+
+  if (threadIdx.x == 0) {
+    tc::mbar_init(&full[0], 1);
+    tc::mbar_init(&full[1], 1);
+    tc::mbar_fence_init();
+    for (int s = 0; s < 2; ++s) {
+      const long long g = blockIdx.x + s * stride;
+      if (g < groups) {
+        tc::mbar_arrive_expect_tx(&full[s], BP::GROUP_BYTES);
+        tc::bulk_load(s ? stage1 : stage0, in + g * BP::GROUP, BP::GROUP_BYTES, &full[s]);
+        pending[s] = true;
+      }
+    }
+  }
+  __syncthreads();
+
+  int s = 0;
+  for (long long g = blockIdx.x; g < groups; g += stride, s ^= 1) {
+    float2* st = (s ? stage1 : stage0);
+    if (threadIdx.x == 0) {
+      *ok_flag = tc::mbar_wait(&full[s], phase[s]) ? 1 : 0;
+      pending[s] = false;
+    }
+    __syncthreads();
+    if (!*ok_flag) {
+      if (threadIdx.x == 0) atomicAdd(timeouts, 1u);
+      break;
+    }
+    phase[s] ^= 1u;
+    float2 v[PL::P];
+    run_spasses<LOG2N, S>(v, j, st + tloc * PL::N, sre, sim, tw);
+    tc::fence_proxy_async_smem();
+    __syncthreads();  // the whole group is in the staging buffer
+    if (threadIdx.x == 0) {
+      tc::bulk_store(out + g * BP::GROUP, st, BP::GROUP_BYTES);
+      tc::bulk_wait_read_all();  // staging buffer may be refilled
+      const long long gn = g + 2 * stride;
+      if (gn < groups) {
+        tc::mbar_arrive_expect_tx(&full[s], BP::GROUP_BYTES);
+        tc::bulk_load(st, in + gn * BP::GROUP, BP::GROUP_BYTES, &full[s]);
+        pending[s] = true;
+      }
+    }
+  }
+  if (threadIdx.x == 0) {
+    // drain: copies still in flight (only after a timeout) and all stores
+    for (int q = 0; q < 2; ++q)
+      if (pending[q] && !tc::mbar_wait(&full[q], phase[q])) atomicAdd(timeouts, 1u);
+    tc::bulk_wait_all();
+  }
+}
+
+template <int LOG2N, int S>
+cudaError_t launch_bulk_len(const float2* in, float2* out, long long groups, const float2* tw,
+                            unsigned int* timeouts, cudaStream_t stream) {
+  using BP = BulkPlan<LOG2N>;
+  auto kern = stockham_bulk_kernel<LOG2N, S>;
+  const cudaError_t e =
+      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, BP::SMEM);
+  if (e != cudaSuccess) return e;
+  const int sms = sm_count(current_device());
+  const long long cap = static_cast<long long>(sms > 0 ? sms : 148) * 2;
+  const unsigned grid = static_cast<unsigned>(groups < cap ? groups : cap);
+  kern<<<grid, Plan<LOG2N>::THREADS, BP::SMEM, stream>>>(in, out, groups, tw, timeouts);
+  return cudaGetLastError();
+}
+
+template <int S>
+cudaError_t dispatch_bulk(int log2n, const float2* in, float2* out, long long groups,
+                          const float2* tw, unsigned int* to, cudaStream_t st) {
+  switch (log2n) {
+    case 4: return launch_bulk_len<4, S>(in, out, groups, tw, to, st);
+    case 5: return launch_bulk_len<5, S>(in, out, groups, tw, to, st);
+    case 6: return launch_bulk_len<6, S>(in, out, groups, tw, to, st);
+    case 7: return launch_bulk_len<7, S>(in, out, groups, tw, to, st);
+    case 8: return launch_bulk_len<8, S>(in, out, groups, tw, to, st);
+    case 9: return launch_bulk_len<9, S>(in, out, groups, tw, to, st);
+    case 10: return launch_bulk_len<10, S>(in, out, groups, tw, to, st);
+    case 11: return launch_bulk_len<11, S>(in, out, groups, tw, to, st);
+    case 12: return launch_bulk_len<12, S>(in, out, groups, tw, to, st);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+unsigned int* bulk_timeout_counter() {
+  static std::mutex mu;
+  static std::array<unsigned int*, 64> addr{};
+  const int dev = current_device();
+  if (dev < 0 || dev >= 64) return nullptr;
+  std::lock_guard<std::mutex> g(mu);
+  if (addr[dev] == nullptr) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_fft_bulk_timeouts) != cudaSuccess) {
+      (void)cudaGetLastError();
+      return nullptr;
+    }
+    addr[dev] = static_cast<unsigned int*>(p);
+  }
+  return addr[dev];
+}
+
 }  // namespace
 
 bool single_pass_supported(std::int64_t n) noexcept {
@@ -309,6 +512,29 @@ cudaError_t launch_stockham(std::int64_t n, int sign, const Batch1D& b,
   if (!single_pass_supported(n)) return cudaErrorInvalidValue;
   if (b.batch <= 0) return cudaSuccess;
   const int log2n = __builtin_ctzll(static_cast<unsigned long long>(n));
+  // Contiguous batches of 16..4096 points take the bulk-copy pipelined kernel for
+  // all whole groups; any remainder (and every other layout) the register kernel.
+  const bool contiguous = b.in_stride == 1 && b.out_stride == 1 && b.in_outer == n &&
+                          b.out_outer == n && b.inner_count == 1 && b.post_tw == nullptr &&
+                          aligned_to(b.in, 16) && aligned_to(b.out, 16);
+  if (contiguous && n >= 16 && n <= 4096) {
+    const long long per_group = 4096 / n;  // TPC transforms of n points = 4096 values
+    const long long groups = b.batch / per_group;
+    unsigned int* to = bulk_timeout_counter();
+    if (groups > 0 && to != nullptr) {
+      const cudaError_t e = sign < 0
+                                ? dispatch_bulk<-1>(log2n, b.in, b.out, groups, b.tw, to, stream)
+                                : dispatch_bulk<1>(log2n, b.in, b.out, groups, b.tw, to, stream);
+      if (e != cudaSuccess) return e;
+      const long long done = groups * per_group;
+      if (done == b.batch) return cudaSuccess;
+      Batch1D rest = b;
+      rest.in = b.in + done * n;
+      rest.out = b.out + done * n;
+      rest.batch = b.batch - done;
+      return sign < 0 ? dispatch<-1>(log2n, rest, stream) : dispatch<1>(log2n, rest, stream);
+    }
+  }
   return sign < 0 ? dispatch<-1>(log2n, b, stream) : dispatch<1>(log2n, b, stream);
 }
 

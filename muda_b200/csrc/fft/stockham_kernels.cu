@@ -19,11 +19,13 @@
 //   - first-pass loads and last-pass stores are coalesced across the threads of a
 //     transform for unit stride (thread j touches elements j + r*N/R);
 //   - shared memory holds real and imaginary parts in separate arrays with one
-//     pad word per 16, which makes the stride-16 scatter of the first pass
+//     pad word per 32, which makes the stride-16 scatter of the first pass
 //     conflict free;
 //   - twiddles come from a table exp(-2*pi*i*m/N) computed in double on the host
 //     and rounded once (conjugated for the inverse), not from sincos per
-//     butterfly.
+//     butterfly; a radix-16 butterfly reads two table entries (w, w^4) and forms
+//     the other powers by products (apply_twiddles), which keeps table traffic
+//     through L1 small.
 #include <cuda_runtime.h>
 
 #include <array>
@@ -138,6 +140,44 @@ __device__ __forceinline__ float2 table_tw(const float2* __restrict__ tw, std::i
   return w;
 }
 
+// v[r] *= w^r for r = 1..R-1, where w = table[m] (the butterfly's base twiddle,
+// conjugated for S > 0).  Only w and w^4 are read from the table; the other powers
+// are products of at most three exact-rounded table values (w^2 = w*w,
+// w^3 = w^2*w, w^8 = (w^4)^2, w^12 = w^8*w^4, w^r = w^(r mod 4) * w^(r - r mod 4)),
+// which keeps the relative error of every twiddle within a few fp32 ulps while
+// cutting the table reads per radix-16 butterfly from 15 to 2.
+template <int R, int S>
+__device__ __forceinline__ void apply_twiddles(float2* v, const float2* __restrict__ tw, int m) {
+  if constexpr (R == 2) {
+    v[1] = cmul(v[1], table_tw<S>(tw, m));
+  } else {
+    float2 lo[4], hi[4];
+    lo[1] = table_tw<S>(tw, m);
+    lo[2] = cmul(lo[1], lo[1]);
+    lo[3] = cmul(lo[2], lo[1]);
+    if constexpr (R >= 8) {
+      hi[1] = table_tw<S>(tw, 4 * m);
+      if constexpr (R == 16) {
+        hi[2] = cmul(hi[1], hi[1]);
+        hi[3] = cmul(hi[2], hi[1]);
+      }
+    }
+#pragma unroll
+    for (int r = 1; r < R; ++r) {
+      const int a = r & 3, b = r >> 2;
+      float2 w;
+      if (b == 0) {
+        w = lo[a];
+      } else if (a == 0) {
+        w = hi[b];
+      } else {
+        w = cmul(lo[a], hi[b]);
+      }
+      v[r] = cmul(v[r], w);
+    }
+  }
+}
+
 // Compile-time plan of a length-N transform.
 template <int LOG2N>
 struct Plan {
@@ -148,7 +188,7 @@ struct Plan {
   static constexpr int THREADS = T * TPC;
   static constexpr int FIRST_R = (LOG2N % 4 == 0) ? (N >= 16 ? 16 : N) : (1 << (LOG2N % 4));
   static constexpr int PASSES = (LOG2N % 4 == 0) ? LOG2N / 4 : LOG2N / 4 + 1;
-  static constexpr int REGION = N + N / 16;                  // padded floats per transform
+  static constexpr int REGION = N + N / 32 + 1;              // padded floats per transform
   static constexpr int SMEM = PASSES > 1 ? TPC * REGION * 2 * 4 : 0;
   // Resident CTAs per SM the register budget is sized for: several CTAs per SM
   // let one CTA's HBM loads overlap another's on-chip passes.
@@ -163,7 +203,9 @@ struct Ctx {
   std::int64_t inner;  // b % inner_count (post-twiddle row)
 };
 
-__device__ __forceinline__ int pad(int i) { return i + (i >> 4); }
+// One pad word per 32: the stride-16 scatter of the first pass and the
+// stride-N/16 gathers of the later passes are conflict free.
+__device__ __forceinline__ int pad(int i) { return i + (i >> 5); }
 
 __host__ __device__ constexpr int ilog2(int v) { return v <= 1 ? 0 : 1 + ilog2(v >> 1); }
 
@@ -198,10 +240,7 @@ __device__ __forceinline__ void pass(float2 (&v)[Plan<LOG2N>::P], int j, int Ns,
     const int k = b & (Ns - 1);
     if (Ns > 1) {
       // exp(S*2*pi*i * r*k/(Ns*R)) = table[r*k*N/(Ns*R)]
-      const int shift = LOG2N - log2Ns - ilog2(R);
-#pragma unroll
-      for (int r = 1; r < R; ++r)
-        v[q * R + r] = cmul(v[q * R + r], table_tw<S>(tw, (r * k) << shift));
+      apply_twiddles<R, S>(&v[q * R], tw, k << (LOG2N - log2Ns - ilog2(R)));
     }
     dft<R, S>(&v[q * R]);
     const int idxD = ((b >> log2Ns) << (log2Ns + ilog2(R))) + k;
@@ -337,10 +376,7 @@ __device__ __forceinline__ void spass(float2 (&v)[Plan<LOG2N>::P], int j, int Ns
     const int b = j + q * T;
     const int k = b & (Ns - 1);
     if (Ns > 1) {
-      const int shift = LOG2N - log2Ns - ilog2(R);
-#pragma unroll
-      for (int r = 1; r < R; ++r)
-        v[q * R + r] = cmul(v[q * R + r], table_tw<S>(tw, (r * k) << shift));
+      apply_twiddles<R, S>(&v[q * R], tw, k << (LOG2N - log2Ns - ilog2(R)));
     }
     dft<R, S>(&v[q * R]);
     const int idxD = ((b >> log2Ns) << (log2Ns + ilog2(R))) + k;

@@ -370,7 +370,9 @@ __device__ __forceinline__ void spass(float2 (&v)[Plan<LOG2N>::P], int j, int Ns
       v[q * R + r] = FIRST ? st[idx] : make_float2(sre[pad(idx)], sim[pad(idx)]);
     }
   }
-  if constexpr (!FIRST || LAST) __syncthreads();  // reads done before the source is rewritten
+  // The work arrays alias the staging buffer, so every pass finishes its reads
+  // before any thread rewrites the buffer.
+  __syncthreads();
 #pragma unroll
   for (int q = 0; q < NB; ++q) {
     const int b = j + q * T;
@@ -407,32 +409,34 @@ __device__ __forceinline__ void run_spasses(float2 (&v)[Plan<LOG2N>::P], int j, 
   }
 }
 
+// Each of the two staging buffers holds a group's input (bulk-copied, plain
+// interleaved complex values), then — after the first pass has read it into
+// registers — that group's padded split work arrays, and finally its output for
+// the bulk store: two ~34 KB buffers per CTA, three CTAs per SM.
 template <int LOG2N>
 struct BulkPlan {
   using PL = Plan<LOG2N>;
   static constexpr int GROUP = PL::TPC * PL::N;                  // complex values per group
   static constexpr int GROUP_BYTES = GROUP * 8;
   static constexpr int WORK_BYTES = PL::TPC * PL::REGION * 2 * 4;
-  static constexpr int SMEM = 2 * GROUP_BYTES + WORK_BYTES + 64;
+  static constexpr int STAGE_BYTES =
+      ((GROUP_BYTES > WORK_BYTES ? GROUP_BYTES : WORK_BYTES) + 127) / 128 * 128;
+  static constexpr int SMEM = 2 * STAGE_BYTES + 64;
 };
 
 template <int LOG2N, int S>
-__global__ void __launch_bounds__(Plan<LOG2N>::THREADS, 2)
+__global__ void __launch_bounds__(Plan<LOG2N>::THREADS, 3)
     stockham_bulk_kernel(const float2* in, float2* out, long long groups,
                          const float2* __restrict__ tw, unsigned int* timeouts) {
   using PL = Plan<LOG2N>;
   using BP = BulkPlan<LOG2N>;
   extern __shared__ __align__(16) std::uint8_t bsmem[];
   float2* stage0 = reinterpret_cast<float2*>(bsmem);
-  float2* stage1 = reinterpret_cast<float2*>(bsmem + BP::GROUP_BYTES);
-  float* work = reinterpret_cast<float*>(bsmem + 2 * BP::GROUP_BYTES);
-  std::uint64_t* full = reinterpret_cast<std::uint64_t*>(bsmem + 2 * BP::GROUP_BYTES +
-                                                         BP::WORK_BYTES);
+  float2* stage1 = reinterpret_cast<float2*>(bsmem + BP::STAGE_BYTES);
+  std::uint64_t* full = reinterpret_cast<std::uint64_t*>(bsmem + 2 * BP::STAGE_BYTES);
   volatile int* ok_flag = reinterpret_cast<volatile int*>(full + 2);
   const int tloc = threadIdx.x / PL::T;
   const int j = threadIdx.x % PL::T;
-  float* sre = work + tloc * PL::REGION * 2;
-  float* sim = sre + PL::REGION;
   const long long stride = gridDim.x;
   std::uint32_t phase[2] = {0u, 0u};
   bool pending[2] = {false, false};
@@ -466,6 +470,8 @@ __global__ void __launch_bounds__(Plan<LOG2N>::THREADS, 2)
     }
     phase[s] ^= 1u;
     float2 v[PL::P];
+    float* sre = reinterpret_cast<float*>(st) + tloc * PL::REGION * 2;
+    float* sim = sre + PL::REGION;
     run_spasses<LOG2N, S>(v, j, st + tloc * PL::N, sre, sim, tw);
     tc::fence_proxy_async_smem();
     __syncthreads();  // the whole group is in the staging buffer
@@ -497,7 +503,7 @@ cudaError_t launch_bulk_len(const float2* in, float2* out, long long groups, con
       cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, BP::SMEM);
   if (e != cudaSuccess) return e;
   const int sms = sm_count(current_device());
-  const long long cap = static_cast<long long>(sms > 0 ? sms : 148) * 2;
+  const long long cap = static_cast<long long>(sms > 0 ? sms : 148) * 3;
   const unsigned grid = static_cast<unsigned>(groups < cap ? groups : cap);
   kern<<<grid, Plan<LOG2N>::THREADS, BP::SMEM, stream>>>(in, out, groups, tw, timeouts);
   return cudaGetLastError();

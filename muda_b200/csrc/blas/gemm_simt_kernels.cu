@@ -57,8 +57,10 @@ __global__ void __launch_bounds__(kThreads) gemm_simt(const GemmArgs g) {
   constexpr int B_PER = BN * BK / kThreads;
   constexpr int TX = BM / TM;  // threads along m
   static_assert(TX * (BN / TN) == kThreads, "tile does not match the thread count");
-  __shared__ __align__(16) float As[2][BK][BM];
-  __shared__ __align__(16) float Bs[2][BK][BN];
+  // Rows padded by 4 words: the transposing stores (8 consecutive k per 8 lanes)
+  // land in distinct banks, and rows stay 16-byte aligned for the vector reads.
+  __shared__ __align__(16) float As[2][BK][BM + 4];
+  __shared__ __align__(16) float Bs[2][BK][BN + 4];
 
   const float alpha = g.alpha_dev ? *g.alpha_dev : g.alpha;
   const float beta = g.beta_dev ? *g.beta_dev : g.beta;
@@ -133,7 +135,9 @@ __global__ void __launch_bounds__(kThreads) gemm_simt(const GemmArgs g) {
         float av[TM], bv[TN];
 #pragma unroll
         for (int i = 0; i < TM; i += 4) {
-          const float4 t = *reinterpret_cast<const float4*>(&As[buf][p][tm * TM + i]);
+          // the thread's rows come in groups of 4 spaced 4*TX apart, so the 16 lanes
+          // along m read 16 consecutive float4 (conflict free)
+          const float4 t = *reinterpret_cast<const float4*>(&As[buf][p][i * TX + tm * 4]);
           av[i] = t.x;
           av[i + 1] = t.y;
           av[i + 2] = t.z;
@@ -165,7 +169,7 @@ __global__ void __launch_bounds__(kThreads) gemm_simt(const GemmArgs g) {
       if (gj >= g.n) continue;
 #pragma unroll
       for (int i = 0; i < TM; ++i) {
-        const int gi = m0 + tm * TM + i;
+        const int gi = m0 + (i / 4) * 4 * TX + tm * 4 + (i % 4);
         if (gi >= g.m) continue;
         T* cp = Cm + gi + static_cast<std::int64_t>(gj) * g.ldc;
         const float prev = (beta == 0.0f) ? 0.0f : beta * to_f(*cp);

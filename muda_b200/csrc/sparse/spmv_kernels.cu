@@ -82,8 +82,16 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32) spmv_csr_tiles(const CsrVie
       const bool deferred = (long_rows >> rl) & 1u;
       float sum = 0.0f;
       if (!deferred) {
-#pragma unroll 2
-        for (int k = s + gl; k < e; k += S) sum = accumulate(a, x, k, sum);
+        // two independent entries per lane per step: both gathers of x are in
+        // flight together
+        float sum1 = 0.0f;
+        int k = s + gl;
+        for (; k + S < e; k += 2 * S) {
+          sum = accumulate(a, x, k, sum);
+          sum1 = accumulate(a, x, k + S, sum1);
+        }
+        if (k < e) sum = accumulate(a, x, k, sum);
+        sum += sum1;
       }
 #pragma unroll
       for (int o = S / 2; o > 0; o >>= 1) sum += __shfl_xor_sync(kFull, sum, o);

@@ -34,11 +34,12 @@ ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 LIBS: dict[str, list[str]] = {
     "curand": ["rand/curand_api.cpp", "rand/philox_kernels.cu"],
     "cudnn": ["dnn/cudnn_api.cpp", "dnn/softmax_kernels.cu", "dnn/conv_direct_kernels.cu",
-              "dnn/conv_tc_kernels.cu", "dnn/conv_dispatch.cu"],
+              "dnn/conv_tc_kernels.cu", "dnn/conv_dispatch.cu", "blas/tf32_split.cu"],
     "cusparse": ["sparse/cusparse_api.cpp", "sparse/spmv_kernels.cu"],
     "cufft": ["fft/cufft_api.cpp", "fft/stockham_kernels.cu", "fft/dft_kernels.cu",
               "fft/fft_static.cu"],
-    "cublas": ["blas/cublas_api.cpp", "blas/gemm_simt_kernels.cu", "blas/gemm_tc_kernels.cu"],
+    "cublas": ["blas/cublas_api.cpp", "blas/gemm_simt_kernels.cu", "blas/gemm_tc_kernels.cu",
+               "blas/tf32_split.cu"],
 }
 
 COMMON_FLAGS = ["-O3", "-std=c++17", f"-I{INCLUDE}", f"-I{CSRC}"]
@@ -79,7 +80,7 @@ def build(names: list[str] | None = None, jobs: int | None = None, verbose: bool
     LIBDIR.mkdir(exist_ok=True)
     newest_header = max((h.stat().st_mtime for h in _headers()), default=0.0)
 
-    jobs_list: list[tuple[Path, Path]] = []
+    jobs_list: dict[Path, Path] = {}  # object -> source (a source shared by two libraries builds once)
     objs: dict[str, list[Path]] = {}
     for name in names:
         objs[name] = []
@@ -90,10 +91,10 @@ def build(names: list[str] | None = None, jobs: int | None = None, verbose: bool
             stale = (not obj.exists() or obj.stat().st_mtime < src.stat().st_mtime
                      or obj.stat().st_mtime < newest_header)
             if stale:
-                jobs_list.append((src, obj))
+                jobs_list[obj] = src
 
     with cf.ThreadPoolExecutor(max_workers=jobs or os.cpu_count() or 4) as pool:
-        futs = [pool.submit(_run, _compile_cmd(s, o)) for s, o in jobs_list]
+        futs = [pool.submit(_run, _compile_cmd(s, o)) for o, s in jobs_list.items()]
         for f in futs:
             f.result()
     if verbose and jobs_list:

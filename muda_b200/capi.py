@@ -211,6 +211,10 @@ CUBLAS_OP_T = 1
 CUBLAS_OP_C = 2
 CUBLAS_POINTER_MODE_HOST = 0
 CUBLAS_POINTER_MODE_DEVICE = 1
+CUBLAS_DEFAULT_MATH = 0
+CUBLAS_TENSOR_OP_MATH = 1
+CUBLAS_PEDANTIC_MATH = 2
+CUBLAS_TF32_TENSOR_OP_MATH = 3
 CUBLAS_COMPUTE_16F = 64
 CUBLAS_COMPUTE_32F = 68
 CUBLAS_GEMM_DEFAULT = -1

@@ -8,6 +8,13 @@
 // extension the reference lacks.  In device pointer mode the scalars are read
 // by the kernel on the stream instead of synchronising the host
 // (cublas_context.mm:72-75 synchronises).
+//
+// fp32 GEMMs run on the tensor cores in split-tf32 form (fp32-class accuracy,
+// within 1.5 * 2^-20 relative per product) unless the math mode is
+// CUBLAS_PEDANTIC_MATH, which keeps the FFMA kernel; the split operands live in
+// a device workspace the handle owns and reuses (grown on demand, ordered after
+// the previous call that used it by an event, so a cublasSetStream between calls
+// stays safe).
 #pragma GCC visibility push(default)
 #include "cublas_v2.h"
 #pragma GCC visibility pop
@@ -21,6 +28,7 @@
 
 #include "blas/gemm.hpp"
 #include "common/device.hpp"
+#include "common/lru.hpp"
 #include "common/registry.hpp"
 
 namespace {
@@ -35,7 +43,42 @@ struct BlasContext {
   cudaStream_t stream = nullptr;
   cublasPointerMode_t pointer_mode = CUBLAS_POINTER_MODE_HOST;
   cublasMath_t math_mode = CUBLAS_DEFAULT_MATH;
+  // split-tf32 workspace: held under ws_mu for the whole call that uses it
+  std::mutex ws_mu;
+  std::shared_ptr<mb200::DeviceBuffer> ws;
+  cudaEvent_t ws_done = nullptr;  // recorded after the last call that used ws
+
+  ~BlasContext() {
+    if (ws_done != nullptr) (void)cudaEventDestroy(ws_done);
+  }
 };
+
+// fp32 GEMM on the tensor cores with the handle's workspace; cudaErrorNotSupported
+// when the shape does not qualify or the workspace cannot be had.
+cudaError_t run_tf32x3(BlasContext& ctx, const GemmArgs& g, cudaStream_t stream) {
+  const std::size_t need = mb200::blas::gemm_tf32x3_workspace(g);
+  if (need == 0) return cudaErrorNotSupported;
+  std::lock_guard<std::mutex> lk(ctx.ws_mu);
+  const int dev = mb200::current_device();
+  if (!ctx.ws || ctx.ws->bytes < need || ctx.ws->device != dev) {
+    ctx.ws.reset();
+    ctx.ws = mb200::DeviceBuffer::make(need);
+    if (!ctx.ws) return cudaErrorNotSupported;
+  }
+  cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(stream, &cap) != cudaSuccess) cap = cudaStreamCaptureStatusNone;
+  const bool ordered = cap == cudaStreamCaptureStatusNone;
+  if (ordered && ctx.ws_done != nullptr && cudaStreamWaitEvent(stream, ctx.ws_done, 0) != cudaSuccess)
+    return cudaErrorUnknown;
+  const cudaError_t e = mb200::blas::launch_gemm_tf32x3(g, ctx.ws->ptr, ctx.ws->bytes, stream);
+  if (e != cudaSuccess || !ordered) return e;
+  if (ctx.ws_done == nullptr &&
+      cudaEventCreateWithFlags(&ctx.ws_done, cudaEventDisableTiming) != cudaSuccess) {
+    ctx.ws_done = nullptr;
+    return cudaErrorUnknown;
+  }
+  return cudaEventRecord(ctx.ws_done, stream);
+}
 
 using HandleTable = mb200::Registry<BlasContext, mb200::ObjKind::kBlasHandle>;
 HandleTable& handles() {
@@ -116,10 +159,12 @@ cublasStatus_t run_gemm(BlasContext& ctx, Elem type, cublasOperation_t ta, cubla
                         const void* beta, void* C, int ldc, long long sc, int batch) {
   cudaStream_t stream;
   cublasPointerMode_t mode;
+  cublasMath_t math;
   {
     std::lock_guard<std::mutex> g(ctx.mu);
     stream = ctx.stream;
     mode = ctx.pointer_mode;
+    math = ctx.math_mode;
   }
   if (m == 0 || n == 0 || batch == 0) return CUBLAS_STATUS_SUCCESS;
   GemmArgs g{};
@@ -167,7 +212,10 @@ cublasStatus_t run_gemm(BlasContext& ctx, Elem type, cublasOperation_t ta, cubla
   if (!mb200::aligned_to(A, es) || !mb200::aligned_to(B, es) || !mb200::aligned_to(C, es))
     return CUBLAS_STATUS_INVALID_VALUE;
   cudaError_t e = cudaErrorNotSupported;
-  if (type != Elem::kF32) e = mb200::blas::launch_gemm_tc(g, stream);
+  if (type != Elem::kF32)
+    e = mb200::blas::launch_gemm_tc(g, stream);
+  else if (math != CUBLAS_PEDANTIC_MATH)
+    e = run_tf32x3(ctx, g, stream);
   if (e == cudaErrorNotSupported) {
     (void)cudaGetLastError();
     e = mb200::blas::launch_gemm_simt(g, stream);

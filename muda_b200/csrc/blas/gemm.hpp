@@ -3,6 +3,7 @@
 
 #include <cuda_runtime_api.h>
 
+#include <cstddef>
 #include <cstdint>
 
 namespace mb200::blas {
@@ -36,6 +37,16 @@ cudaError_t launch_gemm_simt(const GemmArgs& g, cudaStream_t stream) noexcept;
 // in tensor memory.  Returns cudaErrorNotSupported when the shape or layout is not
 // covered (the caller then uses launch_gemm_simt).
 cudaError_t launch_gemm_tc(const GemmArgs& g, cudaStream_t stream) noexcept;
+
+// fp32 GEMM on the tensor cores in split-tf32 form (hi/lo tf32 planes, three
+// MMAs per K step, within 1.5 * 2^-20 relative per product).  Needs a device
+// workspace of gemm_tf32x3_workspace(g) bytes (16-byte aligned) that no other
+// stream touches while the call runs; returns 0 bytes / cudaErrorNotSupported
+// when the problem is too small or the workspace would exceed 2 GiB per batch
+// entry (the caller then uses launch_gemm_simt).
+std::size_t gemm_tf32x3_workspace(const GemmArgs& g) noexcept;
+cudaError_t launch_gemm_tf32x3(const GemmArgs& g, void* workspace, std::size_t ws_bytes,
+                               cudaStream_t stream) noexcept;
 
 // Name of the kernel family that would serve `g` (for tests and benchmarks).
 const char* gemm_path_name(const GemmArgs& g) noexcept;

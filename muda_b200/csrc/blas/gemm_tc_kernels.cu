@@ -9,6 +9,16 @@
 // groups of 16 tile-rows so the CTAs in flight share A and B panels in L2.  A and
 // B must be K-major (cublas transa = T, transb = N) with 16-byte aligned leading
 // dimensions; other layouts use the FFMA kernel.
+//
+// fp32 GEMM (the reference's cublasSgemm arithmetic, cublas_kernels.metal:969-1006:
+// fp32 products accumulated in fp32, then C = alpha*acc + beta*C) runs on the same
+// loop in split-tf32 form: one pass writes each operand, in any transpose and
+// layout, as K-major hi/lo tf32 planes into the handle's workspace, and the
+// tensor cores accumulate lo*hi + hi*lo + hi*hi (within 1.5 * 2^-20 relative
+// per product, the accuracy class of an fp32 FMA loop).  Problems with fewer output tiles
+// than half the SMs split K across CTAs; each split writes raw sums to the
+// workspace and one pass adds them in split order (deterministic) and applies
+// alpha and beta.
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
@@ -20,6 +30,7 @@
 
 #include "blas/gemm.hpp"
 #include "blas/tc_gemm_core.cuh"
+#include "blas/tf32_split.hpp"
 #include "common/device.hpp"
 
 namespace mb200::blas {
@@ -176,10 +187,244 @@ cudaError_t run(const GemmArgs& g, cudaStream_t stream) {
                                                              stream);
 }
 
+// ---------------------------------------------------------------- split tf32 (fp32)
+
+constexpr int kStages32 = 2;  // 2 x (32 + 64) KB stages
+constexpr int kMaxSplitK = 16;
+constexpr std::size_t kWorkspaceCap = std::size_t{2} << 30;
+
+struct SplitGemmProblem {
+  CUtensorMap ma;  // A planes: dims (k, m, batch, plane), box {32, 128, 1, 2}
+  CUtensorMap mb;  // B planes: dims (k, n, batch, plane), box {32, BN, 1, 2}
+  long long tiles_total;
+  int num_kb;  // k-blocks per split
+  int ksplit;
+  int m, n, tiles_m, tiles_n;
+  float* c;
+  long long ldc, stride_c;
+  float* partial;  // ksplit > 1: [batch][ksplit] m x n column-major raw sums
+  float alpha, beta;
+  const float* alpha_dev;
+  const float* beta_dev;
+
+  __device__ void prefetch() const {
+    tc::prefetch_tensormap(&ma);
+    tc::prefetch_tensormap(&mb);
+  }
+
+  // (batch * ksplit + split, tile row, tile column), GROUP_M tile-rows at a time.
+  __device__ void coords(long long t, int (&c3)[3]) const {
+    const long long per = static_cast<long long>(tiles_m) * tiles_n;
+    const int r = static_cast<int>(t % per);
+    const int in_group = GROUP_M * tiles_n;
+    const int first = (r / in_group) * GROUP_M;
+    const int gsz = min(tiles_m - first, GROUP_M);
+    c3[0] = static_cast<int>(t / per);
+    c3[1] = first + (r % in_group) % gsz;
+    c3[2] = (r % in_group) / gsz;
+  }
+
+  __device__ void load(const int (&c3)[3], int kb, void* sa, void* sb, std::uint64_t* bar) const {
+    const int z = c3[0] / ksplit;
+    const int k = ((c3[0] % ksplit) * num_kb + kb) * tc::kBK32;  // past K reads as zeros
+    tc::tma_load_4d(sa, &ma, k, c3[1] * tc::kBM, z, 0, bar);
+    tc::tma_load_4d(sb, &mb, k, c3[2] * BN, z, 0, bar);
+  }
+
+  __device__ void scalars(float& a, float& b) const {
+    a = alpha_dev ? *alpha_dev : alpha;
+    b = beta_dev ? *beta_dev : beta;
+  }
+
+  __device__ void store(const int (&c3)[3], int row, int col0, const float (&v)[32], float a,
+                        float b) const {
+    const int mm = c3[1] * tc::kBM + row;
+    if (mm >= m) return;
+    const int n0 = c3[2] * BN + col0;
+    if (ksplit > 1) {
+      float* pz = partial + static_cast<long long>(c3[0]) * m * n + mm;
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (n0 + j < n) pz[static_cast<long long>(n0 + j) * m] = v[j];
+      return;
+    }
+    float* cz = c + static_cast<long long>(c3[0]) * stride_c + mm;
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      const int nn = n0 + j;
+      if (nn < n) {
+        float* cp = cz + static_cast<long long>(nn) * ldc;
+        const float prev = (b == 0.0f) ? 0.0f : b * *cp;
+        *cp = fmaf(a, v[j], prev);
+      }
+    }
+  }
+};
+
+// C = alpha * (sum of the ksplit partial sums, in split order) + beta * C.
+__global__ void reduce_splits(const float* __restrict__ partial, int ksplit, int m, int n,
+                              int batch, float* c, long long ldc, long long stride_c,
+                              float alpha, float beta, const float* alpha_dev,
+                              const float* beta_dev) {
+  const float a = alpha_dev ? *alpha_dev : alpha;
+  const float b = beta_dev ? *beta_dev : beta;
+  const long long mn = static_cast<long long>(m) * n;
+  const long long total = mn * batch;
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const long long z = i / mn;
+    const long long e = i % mn;
+    const float* pz = partial + z * ksplit * mn + e;
+    float acc = 0.0f;
+    for (int sp = 0; sp < ksplit; ++sp) acc += pz[sp * mn];
+    float* cp = c + z * stride_c + (e % m) + (e / m) * ldc;
+    const float prev = (b == 0.0f) ? 0.0f : b * *cp;
+    *cp = fmaf(a, acc, prev);
+  }
+}
+
+long long round_up4(long long v) { return (v + 3) / 4 * 4; }
+
+struct SplitPlan {
+  int nb;      // batch entries per chunk
+  int ksplit;  // K splits
+  int kb_per;  // k-blocks per split
+  std::size_t a_floats, b_floats, p_floats;
+  std::size_t bytes() const { return (a_floats + b_floats + p_floats) * sizeof(float); }
+};
+
+SplitPlan plan_split(const GemmArgs& g, int sms, int nb) {
+  SplitPlan pl{};
+  pl.nb = nb;
+  const long long ldk = round_up4(g.k);
+  const int tiles = ((g.m + tc::kBM - 1) / tc::kBM) * ((g.n + BN - 1) / BN) * nb;
+  const int total_kb = (g.k + tc::kBK32 - 1) / tc::kBK32;
+  int ks = 1;
+  if (2 * tiles < sms) {
+    ks = sms / tiles;
+    if (ks > total_kb / 4) ks = total_kb / 4;
+    if (ks > kMaxSplitK) ks = kMaxSplitK;
+    if (ks < 1) ks = 1;
+  }
+  pl.kb_per = (total_kb + ks - 1) / ks;
+  pl.ksplit = (total_kb + pl.kb_per - 1) / pl.kb_per;
+  pl.a_floats = 2ull * nb * g.m * ldk;
+  pl.b_floats = 2ull * nb * g.n * ldk;
+  pl.p_floats = pl.ksplit > 1 ? static_cast<std::size_t>(pl.ksplit) * nb * g.m * g.n : 0;
+  return pl;
+}
+
+// Largest batch chunk whose workspace fits the cap (0 if one entry does not).
+SplitPlan plan_for(const GemmArgs& g, int sms) {
+  int nb = g.batch;
+  SplitPlan pl = plan_split(g, sms, nb);
+  while (pl.bytes() > kWorkspaceCap && nb > 1) {
+    nb = (nb + 1) / 2;
+    pl = plan_split(g, sms, nb);
+  }
+  if (pl.bytes() > kWorkspaceCap) pl.nb = 0;
+  return pl;
+}
+
+bool tf32x3_supported(const GemmArgs& g) {
+  if (g.type != Elem::kF32) return false;
+  if (g.k <= 0 || g.m <= 0 || g.n <= 0 || g.batch <= 0) return false;
+  if (g.stride_a < 0 || g.stride_b < 0) return false;
+  // small problems are faster on the FFMA kernel than split + tensor cores
+  if (static_cast<double>(g.m) * g.n * g.k < double(1 << 24)) return false;
+  return true;
+}
+
+bool make_plane_map(CUtensorMap* map, const float* planes, long long k, long long rows,
+                    int batch, long long ldk, int box_rows) {
+  const cuuint64_t dims[4] = {static_cast<cuuint64_t>(k), static_cast<cuuint64_t>(rows),
+                              static_cast<cuuint64_t>(batch), 2u};
+  const cuuint64_t strides[3] = {static_cast<cuuint64_t>(ldk * 4),
+                                 static_cast<cuuint64_t>(rows * ldk * 4),
+                                 static_cast<cuuint64_t>(batch * rows * ldk * 4)};
+  const cuuint32_t box[4] = {static_cast<cuuint32_t>(tc::kBK32),
+                             static_cast<cuuint32_t>(box_rows), 1u, 2u};
+  return tc::encode_tiled(map, 2, planes, 4, dims, strides, box);
+}
+
+cudaError_t run_chunk(const GemmArgs& g, const SplitPlan& pl, int z0, int nb, float* ws,
+                      int sms, unsigned int* to, cudaStream_t stream) {
+  const long long ldk = round_up4(g.k);
+  float* pa = ws;
+  float* pb = pa + pl.a_floats;
+  float* pp = pb + pl.b_floats;
+  const float* a = static_cast<const float*>(g.a) + z0 * g.stride_a;
+  const float* b = static_cast<const float*>(g.b) + z0 * g.stride_b;
+  // op(A) is m x k: element (i, p) at A[i + p*lda] (N) or A[p + i*lda] (T)
+  cudaError_t e = tc::launch_tf32_split(a, g.m, g.k, nb, g.trans_a ? g.lda : 1,
+                                        g.trans_a ? 1 : g.lda, g.stride_a, pa, ldk, stream);
+  if (e != cudaSuccess) return e;
+  // op(B) is k x n: element (p, j) at B[p + j*ldb] (N) or B[j + p*ldb] (T); rows are j
+  e = tc::launch_tf32_split(b, g.n, g.k, nb, g.trans_b ? 1 : g.ldb, g.trans_b ? g.ldb : 1,
+                            g.stride_b, pb, ldk, stream);
+  if (e != cudaSuccess) return e;
+  SplitGemmProblem p{};
+  if (!make_plane_map(&p.ma, pa, g.k, g.m, nb, ldk, tc::kBM) ||
+      !make_plane_map(&p.mb, pb, g.k, g.n, nb, ldk, BN))
+    return cudaErrorNotSupported;
+  p.m = g.m;
+  p.n = g.n;
+  p.tiles_m = (g.m + tc::kBM - 1) / tc::kBM;
+  p.tiles_n = (g.n + BN - 1) / BN;
+  p.ksplit = pl.ksplit;
+  p.num_kb = pl.kb_per;
+  p.tiles_total = static_cast<long long>(p.tiles_m) * p.tiles_n * nb * pl.ksplit;
+  p.c = static_cast<float*>(g.c) + z0 * g.stride_c;
+  p.ldc = g.ldc;
+  p.stride_c = g.stride_c;
+  p.partial = pp;
+  p.alpha = g.alpha;
+  p.beta = g.beta;
+  p.alpha_dev = g.alpha_dev;
+  p.beta_dev = g.beta_dev;
+  e = tc::launch_tc_gemm<SplitGemmProblem, BN, kStages32, tc::kFmtTf32x3>(p, sms, to, stream);
+  if (e != cudaSuccess || pl.ksplit == 1) return e;
+  const long long total = static_cast<long long>(g.m) * g.n * nb;
+  const long long want = (total + 255) / 256;
+  const long long cap = static_cast<long long>(sms) * 8;
+  reduce_splits<<<static_cast<unsigned>(want < cap ? want : cap), 256, 0, stream>>>(
+      pp, pl.ksplit, g.m, g.n, nb, p.c, g.ldc, g.stride_c, g.alpha, g.beta, g.alpha_dev,
+      g.beta_dev);
+  return cudaGetLastError();
+}
+
 }  // namespace
 
+std::size_t gemm_tf32x3_workspace(const GemmArgs& g) noexcept {
+  if (!tf32x3_supported(g)) return 0;
+  const SplitPlan pl = plan_for(g, sm_count(current_device()));
+  return pl.nb == 0 ? 0 : pl.bytes();
+}
+
+cudaError_t launch_gemm_tf32x3(const GemmArgs& g, void* workspace, std::size_t ws_bytes,
+                               cudaStream_t stream) noexcept {
+  if (!tf32x3_supported(g)) return cudaErrorNotSupported;
+  const int sms = sm_count(current_device());
+  const SplitPlan pl = plan_for(g, sms);
+  if (pl.nb == 0 || workspace == nullptr || ws_bytes < pl.bytes() ||
+      !aligned_to(workspace, 16))
+    return cudaErrorNotSupported;
+  unsigned int* to = timeout_counter();
+  if (to == nullptr) return cudaErrorNotSupported;
+  for (int z0 = 0; z0 < g.batch; z0 += pl.nb) {
+    const int nb = g.batch - z0 < pl.nb ? g.batch - z0 : pl.nb;
+    const SplitPlan cur = nb == pl.nb ? pl : plan_split(g, sms, nb);
+    const cudaError_t e =
+        run_chunk(g, cur, z0, nb, static_cast<float*>(workspace), sms, to, stream);
+    if (e != cudaSuccess) return e;
+  }
+  return cudaSuccess;
+}
+
 const char* gemm_path_name(const GemmArgs& g) noexcept {
-  return tc_supported(g) ? "tcgen05" : "simt";
+  if (tc_supported(g)) return "tcgen05";
+  if (gemm_tf32x3_workspace(g) != 0) return "tcgen05-tf32x3";
+  return "simt";
 }
 
 cudaError_t launch_gemm_tc(const GemmArgs& g, cudaStream_t stream) noexcept {

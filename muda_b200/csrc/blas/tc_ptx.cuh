@@ -90,6 +90,18 @@ __device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, s
       : "memory");
 }
 
+// 5-D tiled TMA load (e.g. the hi/lo planes of an NHWC activation rectangle).
+__device__ __forceinline__ void tma_load_5d(void* dst, const CUtensorMap* map, std::int32_t x,
+                                            std::int32_t y, std::int32_t z, std::int32_t w,
+                                            std::int32_t v, std::uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.5d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3, %4, %5, %6}], [%7];" ::"r"(smem_addr(dst)),
+      "l"(reinterpret_cast<std::uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(w), "r"(v),
+      "r"(smem_addr(bar))
+      : "memory");
+}
+
 // Untiled bulk copies (16-byte aligned addresses, size a multiple of 16).
 __device__ __forceinline__ void bulk_load(void* dst_smem, const void* src, std::uint32_t bytes,
                                           std::uint64_t* bar) {
@@ -162,6 +174,19 @@ __device__ __forceinline__ void mma_f16(std::uint32_t d_tmem, std::uint64_t ades
       : "memory");
 }
 
+// D[tmem] (+)= A[smem] * B[smem]^T with tf32 operands (fp32 words whose low 13
+// mantissa bits are zero), one kind::tf32 MMA: K = 8 elements = 32 bytes per row.
+__device__ __forceinline__ void mma_tf32(std::uint32_t d_tmem, std::uint64_t adesc,
+                                         std::uint64_t bdesc, std::uint32_t idesc,
+                                         std::uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
 // Arrives once on `bar` when all previously issued MMAs of this thread complete.
 __device__ __forceinline__ void mma_commit(std::uint64_t* bar) {
   asm volatile(
@@ -188,6 +213,21 @@ __device__ __forceinline__ void tmem_load_32cols(std::uint32_t taddr, float* v) 
   for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+// 16 consecutive fp32 columns of this thread's tensor-memory lane.
+__device__ __forceinline__ void tmem_load_16cols(std::uint32_t taddr, float* v) {
+  std::uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
 // Shared-memory matrix descriptor for a K-major operand tile stored as rows of
 // 128 bytes with the 128-byte swizzle (8-row atoms of 1024 bytes, stacked along
 // M/N): start address, leading offset 16 B (unused by this layout), stride
@@ -202,8 +242,8 @@ __device__ __forceinline__ std::uint64_t kmajor_sw128_desc(std::uint32_t saddr) 
   return d;
 }
 
-// Instruction descriptor of kind::f16: fp32 accumulate, A/B of the given format
-// (0 = fp16, 1 = bf16), both K-major, tile M x N.
+// Instruction descriptor of kind::f16 / kind::tf32: fp32 accumulate, A/B of the
+// given format (0 = fp16, 1 = bf16, 2 = tf32), both K-major, tile M x N.
 __host__ __device__ constexpr std::uint32_t f16_idesc(int ab_format, int m, int n) {
   return (1u << 4) | (static_cast<std::uint32_t>(ab_format) << 7) |
          (static_cast<std::uint32_t>(ab_format) << 10) |

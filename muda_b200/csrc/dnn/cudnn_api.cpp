@@ -3,6 +3,12 @@
 // Mirrors libraries/dnn/src/cudnn_descriptors.mm and cudnn_ops.mm of the
 // reference: same entry points, validation order and status codes.  Every
 // buffer span is checked against its allocation before a kernel is launched.
+//
+// fp32 convolutions that the split-tf32 tensor-core kernel covers need a device
+// workspace for the hi/lo planes of x and w.  cudnnGetConvolutionForwardWorkspaceSize
+// reports 0 as the reference does (cudnn_ops.mm:112), so the handle owns a
+// workspace (grown on demand, ordered after its previous use by an event); a
+// caller-supplied workSpace that is large enough is used instead.
 #pragma GCC visibility push(default)
 #include "cudnn.h"
 #pragma GCC visibility pop
@@ -14,6 +20,7 @@
 #include <mutex>
 
 #include "common/device.hpp"
+#include "common/lru.hpp"
 #include "common/registry.hpp"
 #include "dnn/dnn.hpp"
 
@@ -26,6 +33,14 @@ using mb200::dnn::View4;
 struct DnnContext {
   std::mutex mu;
   cudaStream_t stream = nullptr;
+  // split-tf32 workspace: held under ws_mu for the whole call that uses it
+  std::mutex ws_mu;
+  std::shared_ptr<mb200::DeviceBuffer> ws;
+  cudaEvent_t ws_done = nullptr;  // recorded after the last call that used ws
+
+  ~DnnContext() {
+    if (ws_done != nullptr) (void)cudaEventDestroy(ws_done);
+  }
 };
 
 struct TensorDesc {
@@ -508,8 +523,42 @@ cudnnStatus_t cudnnConvolutionForward(cudnnHandle_t handle, const void* alpha,
       !mb200::device_span_ok(y, plan.y_bytes))
     return CUDNN_STATUS_BAD_PARAM;
   const cudaStream_t st = stream_of(*h);
-  const cudaError_t e = mb200::dnn::launch_conv(x, w, y, plan.shape, dt, a, b, st);
-  return e == cudaSuccess ? CUDNN_STATUS_SUCCESS : CUDNN_STATUS_EXECUTION_FAILED;
+  const std::size_t need =
+      dt == mb200::dnn::ConvDtype::kF32 ? mb200::dnn::conv_tf32x3_workspace(plan.shape) : 0;
+  if (need == 0) {
+    const cudaError_t e = mb200::dnn::launch_conv(x, w, y, plan.shape, dt, a, b, nullptr, 0, st);
+    return e == cudaSuccess ? CUDNN_STATUS_SUCCESS : CUDNN_STATUS_EXECUTION_FAILED;
+  }
+  if (workSpace != nullptr && workSpaceSizeInBytes >= need && mb200::aligned_to(workSpace, 16) &&
+      mb200::device_span_ok(workSpace, need)) {
+    const cudaError_t e =
+        mb200::dnn::launch_conv(x, w, y, plan.shape, dt, a, b, workSpace, need, st);
+    return e == cudaSuccess ? CUDNN_STATUS_SUCCESS : CUDNN_STATUS_EXECUTION_FAILED;
+  }
+  std::lock_guard<std::mutex> lk(h->ws_mu);
+  const int dev = mb200::current_device();
+  if (!h->ws || h->ws->bytes < need || h->ws->device != dev) {
+    h->ws.reset();
+    h->ws = mb200::DeviceBuffer::make(need);
+  }
+  void* wsp = h->ws ? h->ws->ptr : nullptr;
+  const std::size_t wsb = h->ws ? h->ws->bytes : 0;
+  cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(st, &cap) != cudaSuccess) cap = cudaStreamCaptureStatusNone;
+  const bool ordered = cap == cudaStreamCaptureStatusNone && wsp != nullptr;
+  if (ordered && h->ws_done != nullptr && cudaStreamWaitEvent(st, h->ws_done, 0) != cudaSuccess)
+    return CUDNN_STATUS_EXECUTION_FAILED;
+  const cudaError_t e = mb200::dnn::launch_conv(x, w, y, plan.shape, dt, a, b, wsp, wsb, st);
+  if (e != cudaSuccess) return CUDNN_STATUS_EXECUTION_FAILED;
+  if (ordered) {
+    if (h->ws_done == nullptr &&
+        cudaEventCreateWithFlags(&h->ws_done, cudaEventDisableTiming) != cudaSuccess) {
+      h->ws_done = nullptr;
+      return CUDNN_STATUS_EXECUTION_FAILED;
+    }
+    if (cudaEventRecord(h->ws_done, st) != cudaSuccess) return CUDNN_STATUS_EXECUTION_FAILED;
+  }
+  return CUDNN_STATUS_SUCCESS;
 }
 
 // ---------------------------------------------------------------- softmax --

@@ -3,6 +3,7 @@
 
 #include <cuda_runtime_api.h>
 
+#include <cstddef>
 #include <cstdint>
 
 namespace mb200::dnn {
@@ -53,9 +54,21 @@ bool conv_tc_supported(const ConvShape& s, ConvDtype dt, const void* x, const vo
 cudaError_t launch_conv_tc(const void* x, const void* w, void* y, const ConvShape& s,
                            ConvDtype dt, float alpha, float beta, cudaStream_t stream) noexcept;
 
-// Picks the fastest kernel that supports the geometry and launches it.
+// tcgen05 implicit-GEMM kernel for fp32 tensors in split-tf32 form: NHWC input and
+// output, KRSC or KCRS filter, groups 1, stride 1, C a multiple of 32, K of 4.
+// Needs conv_tf32x3_workspace(s) bytes of device workspace (16-byte aligned) that
+// no other stream touches during the call (0: geometry not covered).
+std::size_t conv_tf32x3_workspace(const ConvShape& s) noexcept;
+cudaError_t launch_conv_tf32x3(const void* x, const void* w, void* y, const ConvShape& s,
+                               float alpha, float beta, void* workspace, std::size_t ws_bytes,
+                               cudaStream_t stream) noexcept;
+
+// Picks the fastest kernel that supports the geometry and launches it; fp32
+// tensors use the tensor cores when `workspace` holds conv_tf32x3_workspace(s)
+// bytes, else the direct kernel.
 cudaError_t launch_conv(const void* x, const void* w, void* y, const ConvShape& s, ConvDtype dt,
-                        float alpha, float beta, cudaStream_t stream) noexcept;
+                        float alpha, float beta, void* workspace, std::size_t ws_bytes,
+                        cudaStream_t stream) noexcept;
 
 // Name of the kernel family launch_conv would use (for tests and benchmarks).
 const char* conv_path_name(const ConvShape& s, ConvDtype dt) noexcept;

@@ -182,6 +182,106 @@ def test_gpu_sgemm_matches_oracle(cuda, built, m, n, k, ta, tb):
     assert np.array_equal(got[mask], C0[mask])
 
 
+def _op_dense(X, ld, stride, z, rows, cols, trans):
+    """op(X) of batch entry z as a dense float64 (rows x cols) array."""
+    base = X[z * stride:]
+    if trans:
+        return base[:ld * rows].reshape(rows, ld)[:, :cols].astype(np.float64)
+    return base[:ld * cols].reshape(cols, ld).T[:rows, :].astype(np.float64)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("m,n,k,batch", [(256, 256, 256, 1), (300, 520, 1000, 3),
+                                         (1024, 1024, 1024, 1), (2048, 64, 4096, 1),
+                                         (129, 1000, 333, 2)])
+@pytest.mark.parametrize("ta,tb", [(False, False), (True, False), (False, True), (True, True)])
+def test_gpu_sgemm_split_tf32_tensor_core(cuda, built, m, n, k, batch, ta, tb):
+    """fp32 GEMM on the tensor cores (hi/lo tf32 planes, split K for small tile
+    counts): every entry within 1e-5 of |alpha| (|op(A)| |op(B)|)_ij + |beta C_ij|
+    of the double-accumulated product, normwise 1e-5, padding untouched, and the
+    same bar for the FFMA kernel under CUBLAS_PEDANTIC_MATH."""
+    torch = cuda
+    rng = np.random.default_rng(m + 3 * n + 7 * k + batch)
+    A, lda, sa, B, ldb, sb, C0, ldc, sc = rand_case(rng, m, n, k, ta, tb, batch)
+    alpha, beta = 1.25, (0.0 if (m + n) % 2 else -0.5)
+    results = {}
+    for mode in (capi.CUBLAS_DEFAULT_MATH, capi.CUBLAS_PEDANTIC_MATH):
+        dA, dB, dC = (torch.from_numpy(x).cuda() for x in (A, B, C0))
+        b = Blas(torch)
+        assert b.L.cublasSetMathMode(b.h, mode) == 0
+        st = b.L.cublasSgemmStridedBatched(
+            b.h, OPS[ta], OPS[tb], m, n, k, C.byref(C.c_float(alpha)), C.c_void_p(dA.data_ptr()),
+            lda, sa, C.c_void_p(dB.data_ptr()), ldb, sb, C.byref(C.c_float(beta)),
+            C.c_void_p(dC.data_ptr()), ldc, sc, batch)
+        torch.cuda.synchronize()
+        b.close()
+        assert st == 0
+        results[mode] = dC.cpu().numpy()
+    for mode, got in results.items():
+        mask = np.ones(len(got), bool)
+        for z in range(batch):
+            a = _op_dense(A, lda, sa, z, m, k, ta)
+            bb = _op_dense(B, ldb, sb, z, k, n, tb)
+            idx = (z * sc + np.arange(n)[None, :] * ldc + np.arange(m)[:, None])  # m x n
+            c0 = C0[idx].astype(np.float64)
+            want = alpha * (a @ bb) + beta * c0
+            scale = abs(alpha) * (np.abs(a) @ np.abs(bb)) + abs(beta) * np.abs(c0)
+            err = np.abs(got[idx].astype(np.float64) - want)
+            assert np.all(err <= 1e-5 * scale + 1e-30), (mode, float((err / scale).max()))
+            assert normwise(got[idx], want) <= 1e-5
+            mask[idx.reshape(-1)] = False
+        assert np.array_equal(got[mask], C0[mask])
+
+
+@pytest.mark.gpu
+def test_gpu_sgemm_split_tf32_stream_switch_and_special_values(cuda, built):
+    """The handle's split workspace stays ordered across cublasSetStream, and
+    inf / -inf / nan propagate as in an fp32 loop, including an infinity meeting a
+    value that tf32 holds exactly (whose lo plane must not be zero)."""
+    torch = cuda
+    m = n = k = 512
+    rng = np.random.default_rng(5)
+    A = rng.uniform(-1, 1, m * k).astype(np.float32)
+    B = rng.uniform(-1, 1, k * n).astype(np.float32)
+    A2 = rng.uniform(-1, 1, m * k).astype(np.float32)
+    A2[3 + 7 * m] = np.inf     # row 3, column 7 of A (column-major)
+    A2[9 + 7 * m] = -np.inf    # row 9, column 7
+    A2[20 + 30 * m] = np.nan   # row 20
+    A2[40 + 41 * m] = 0.5      # exactly representable in tf32 (lo is not zero)
+    B2 = B.copy()
+    B2[41 + 60 * k] = np.inf   # column 60 of B meets the exact 0.5 in row 40
+    dA, dA2, dB = (torch.from_numpy(x).cuda() for x in (A, A2, B))
+    dB2 = torch.from_numpy(B2).cuda()
+    dC, dC2 = torch.zeros(m * n, device="cuda"), torch.zeros(m * n, device="cuda")
+    L = capi.cublas()
+    h = C.c_void_p()
+    assert L.cublasCreate_v2(C.byref(h)) == 0
+    s1, s2 = torch.cuda.Stream(), torch.cuda.Stream()
+    one, zero = C.byref(C.c_float(1.0)), C.byref(C.c_float(0.0))
+    for s, a, bm, c in ((s1, dA, dB, dC), (s2, dA2, dB2, dC2)):
+        assert L.cublasSetStream_v2(h, C.c_void_p(s.cuda_stream)) == 0
+        assert L.cublasSgemm_v2(h, 0, 0, m, n, k, one, C.c_void_p(a.data_ptr()), m,
+                                C.c_void_p(bm.data_ptr()), k, zero, C.c_void_p(c.data_ptr()),
+                                m) == 0
+    torch.cuda.synchronize()
+    assert L.cublasDestroy_v2(h) == 0
+    bb = B.reshape(n, k).T.astype(np.float64)
+    want = A.reshape(k, m).T.astype(np.float64) @ bb
+    assert normwise(dC.cpu().numpy().reshape(n, m).T, want) <= 1e-5
+    got2 = dC2.cpu().numpy().reshape(n, m).T
+    a2 = A2.reshape(k, m).T.astype(np.float64)
+    b2 = B2.reshape(n, k).T.astype(np.float64)
+    with np.errstate(invalid="ignore"):
+        want2 = a2 @ b2
+    assert np.isinf(want2[3]).all() and np.isnan(want2[20]).all() and np.isinf(want2[40, 60])
+    assert np.array_equal(np.isinf(got2), np.isinf(want2))
+    assert np.array_equal(np.isnan(got2), np.isnan(want2))
+    inf = np.isinf(want2)
+    assert np.array_equal(np.sign(got2[inf]), np.sign(want2[inf]))
+    fin = np.isfinite(want2)
+    assert normwise(got2[fin], want2[fin]) <= 1e-5
+
+
 @pytest.mark.gpu
 def test_gpu_sgemm_device_pointer_mode(cuda, built):
     torch = cuda

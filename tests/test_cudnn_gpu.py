@@ -161,6 +161,94 @@ def test_conv_bf16_tensor_core_layout(cuda, built, case):
     assert normwise(g, wv) <= 1e-2
 
 
+TC32_CASES = [
+    # xshape (n, c, h, w), wshape (k, c, r, s), pad, dil, mode, alpha, beta, filter layout
+    ((4, 64, 14, 14), (64, 64, 3, 3), (1, 1), (1, 1), 1, 1.0, 0.0, NHWC),
+    ((3, 128, 9, 13), (96, 128, 3, 3), (1, 1), (1, 1), 1, 1.0, 0.0, NCHW),
+    ((4, 32, 20, 30), (256, 32, 1, 1), (0, 0), (1, 1), 1, 0.5, 0.0, NHWC),
+    ((1, 192, 17, 17), (300, 192, 3, 3), (0, 2), (2, 1), 1, 1.0, 0.75, NCHW),
+    ((2, 64, 8, 70), (128, 64, 5, 3), (2, 1), (1, 1), 0, 1.0, 0.0, NHWC),
+    ((4, 256, 28, 28), (256, 256, 3, 3), (1, 1), (1, 1), 1, 1.0, 0.0, NHWC),
+]
+
+
+@pytest.mark.parametrize("case", TC32_CASES)
+def test_conv_f32_split_tf32_tensor_core(cuda, built, case):
+    """fp32 NHWC input/output, KRSC or KCRS filter, C a multiple of 32: the tcgen05
+    implicit GEMM in split-tf32 form, held to the fp32 bar (normwise 1e-5, per
+    element 2e-5 of conv(|x|, |w|))."""
+    xshape, wshape, pad, dil, mode, alpha, beta, wf = case
+    rng = np.random.default_rng(sum(xshape) * 3 + sum(wshape))
+    x = rng.standard_normal(np.prod(xshape)).astype(np.float32)
+    w = rng.standard_normal(np.prod(wshape)).astype(np.float32)
+    n, c, h, wd = xshape
+    k, _, r, s = wshape
+    oh = 1 + (h + 2 * pad[0] - (1 + (r - 1) * dil[0]))
+    ow = 1 + (wd + 2 * pad[1] - (1 + (s - 1) * dil[1]))
+    y0 = rng.standard_normal(n * k * oh * ow).astype(np.float32)
+    got, _ = run_conv(cuda, x, w, xshape, wshape, x_fmt=NHWC, w_fmt=wf, pad=pad, dil=dil,
+                      mode=mode, alpha=alpha, beta=beta, y0=y0)
+    fmt = {NCHW: "NCHW", NHWC: "NHWC"}
+    kw = dict(x_fmt="NHWC", w_fmt=fmt[wf], pad=pad, dil=dil,
+              mode="conv" if mode == 0 else "cross", accum_f64=True, threads=16)
+    want = oracle.conv2d(x, w, xshape, wshape, alpha=alpha, beta=beta, y=y0.copy(), **kw)
+    mag = oracle.conv2d(np.abs(x), np.abs(w), xshape, wshape, alpha=abs(alpha), beta=abs(beta),
+                        y=np.abs(y0), **kw)
+    check_f32(got, want, scale=mag)
+
+
+def test_conv_f32_user_workspace_and_repeat(cuda, built):
+    """A caller-supplied workSpace large enough for the split planes is used, and two
+    calls in a row on one handle (handle workspace reused) give identical output."""
+    torch = cuda
+    xshape, wshape = (2, 64, 16, 16), (128, 64, 3, 3)
+    rng = np.random.default_rng(3)
+    x = rng.standard_normal(np.prod(xshape)).astype(np.float32)
+    w = rng.standard_normal(np.prod(wshape)).astype(np.float32)
+    outs = []
+    with Dnn(torch) as d:
+        xd = d.tensor(*xshape, fmt=NHWC)
+        wdsc = d.filter(*wshape, fmt=NHWC)
+        cv = d.conv(pad=(1, 1))
+        yd = d.tensor(2, 128, 16, 16, fmt=NHWC)
+        xt, wt = dev(torch, x), dev(torch, w)
+        ws = torch.zeros(8 << 20, dtype=torch.uint8, device="cuda")
+        for space, size in ((None, 0), (None, 0), (ws.data_ptr(), ws.numel())):
+            yt = torch.zeros(2 * 128 * 16 * 16, device="cuda")
+            assert d.L.cudnnConvolutionForward(
+                d.h, fptr(1.0), xd, C.c_void_p(xt.data_ptr()), wdsc, C.c_void_p(wt.data_ptr()), cv,
+                0, C.c_void_p(space) if space else None, size, fptr(0.0), yd,
+                C.c_void_p(yt.data_ptr())) == 0
+            torch.cuda.synchronize()
+            outs.append(yt.cpu().numpy())
+    assert np.array_equal(outs[0], outs[1]) and np.array_equal(outs[0], outs[2])
+    want = oracle.conv2d(x, w, xshape, wshape, x_fmt="NHWC", w_fmt="NHWC", pad=(1, 1),
+                         accum_f64=True)
+    mag = oracle.conv2d(np.abs(x), np.abs(w), xshape, wshape, x_fmt="NHWC", w_fmt="NHWC",
+                        pad=(1, 1), accum_f64=True)
+    check_f32(outs[0], want, scale=mag)
+
+
+def test_conv_f32_config_shape_sampled(cuda, built):
+    """configs[4] conv through the reference's own fp32 API path: NHWC 64x56x56x256 ->
+    256, 3x3, pad 1, KRSC filter; images 0 and 63 checked against the oracle."""
+    torch = cuda
+    from muda_b200 import synth
+    n, c, h, wd, k = 64, 256, 56, 56, 256
+    x = synth.normal(torch, n * h * wd * c, seed=11, std=0.02)
+    w = synth.normal(torch, k * 9 * c, seed=11, std=0.02, offset=(n * h * wd * c + 3) // 4 * 4)
+    xf, wf = x.cpu().numpy(), w.cpu().numpy()
+    got, _ = run_conv(torch, xf, wf, (n, c, h, wd), (k, c, 3, 3), x_fmt=NHWC, w_fmt=NHWC,
+                      pad=(1, 1))
+    per = h * wd * c
+    for img in (0, 63):
+        xi = xf[img * per:(img + 1) * per]
+        kw = dict(x_fmt="NHWC", w_fmt="NHWC", pad=(1, 1), accum_f64=True, threads=16)
+        want = oracle.conv2d(xi, wf, (1, c, h, wd), (k, c, 3, 3), **kw)
+        mag = oracle.conv2d(np.abs(xi), np.abs(wf), (1, c, h, wd), (k, c, 3, 3), **kw)
+        check_f32(got[img * h * wd * k:(img + 1) * h * wd * k], want, scale=mag)
+
+
 def test_conv_bf16_config_shape_sampled(cuda, built):
     """configs[4] conv: NHWC 64x56x56x256 -> 256, 3x3, pad 1 (bf16 extension path); images
     0 and 63 are checked against the oracle."""

@@ -316,11 +316,23 @@ class Suite:
             peak, unit = self.peaks["hbm_gbs"], "GB/s"
         elif bound == "tensor":
             peak, unit = self.peaks.get("bf16_tflops", 1651.6), "TFLOP/s"
+        elif bound == "tensor-tf32x3":
+            # fp32 work done as three tf32 MMAs per product: tf32 runs at half the bf16
+            # rate, so the ceiling for fp32 FLOP/s is bf16 / 2 / 3
+            peak, unit = self.peaks.get("bf16_tflops", 1651.6) / 6.0, "TFLOP/s"
         else:  # fp32 FFMA pipe at the maximum SM clock
-            peak, unit = 148 * 128 * 2 * 1.965e9 / 1e12, "TFLOP/s"
-        return {"bound": bound, "kernel": kernel, "achieved": achieved, "peak": peak,
-                "unit": unit, "frac": achieved / peak, "peak_source": self.peaks["source"]
-                if bound != "ffma" else "148 SMs x 128 FMA x 2 x 1965 MHz"}
+            peak, unit = FFMA_PEAK_TFLOPS, "TFLOP/s"
+        source = {"ffma": "148 SMs x 128 FMA x 2 x 1965 MHz",
+                  "tensor-tf32x3": self.peaks["source"] + " bf16 GEMM / 2 (tf32 rate) / 3 (MMAs "
+                                   "per fp32 product)"}.get(bound, self.peaks["source"])
+        out = {"bound": bound, "kernel": kernel, "achieved": achieved, "peak": peak,
+               "unit": unit, "frac": achieved / peak, "peak_source": source}
+        if bound == "tensor-tf32x3":
+            out["frac_of_ffma_peak"] = achieved / FFMA_PEAK_TFLOPS
+        return out
+
+
+FFMA_PEAK_TFLOPS = 148 * 128 * 2 * 1.965e9 / 1e12
 
 
 def torch_float(torch):
@@ -350,12 +362,20 @@ def suite_sgemm(s: Suite) -> dict:
     args = (h, 0, 0, n, m, k, C.byref(one), C.c_void_p(b.data_ptr()), n,
             C.c_void_p(a.data_ptr()), k, C.byref(zero), C.c_void_p(c.data_ptr()), n)
     ms, launches = s.time(lambda: L.cublasSgemm_v2(*args), flush=True)
+    # the FFMA kernel the same call runs under CUBLAS_PEDANTIC_MATH, for comparison
+    assert L.cublasSetMathMode(h, capi.CUBLAS_PEDANTIC_MATH) == 0
+    ms_ffma, _ = s.time(lambda: L.cublasSgemm_v2(*args), flush=True)
     assert L.cublasDestroy_v2(h) == 0
     flop = 2.0 * m * n * k
     tf = flop / (ms * 1e-3) / 1e12
-    out = {"value": tf, "unit": "TFLOP/s", "ms": ms, "dtype": "f32",
-           "config": f"{m}x{n}x{k} fp32, L2 flushed before each call",
-           "roofline": s.roof("gemm_simt<float,128,64,8,8,4>", tf, "ffma"), "launches": launches}
+    out = {"value": tf, "unit": "TFLOP/s", "ms": ms, "dtype": "f32 (split-tf32 on tcgen05)",
+           "config": f"{m}x{n}x{k} fp32, L2 flushed before each call; hi/lo split of A and B, "
+                     "split-K GEMM, split-order reduction",
+           "roofline": s.roof("tc_gemm_split_kernel<SplitGemmProblem,256,2,2>", tf,
+                              "tensor-tf32x3"),
+           "launches": launches,
+           "pedantic_ffma": {"ms": ms_ffma, "TFLOP/s": flop / (ms_ffma * 1e-3) / 1e12,
+                             "kernel": "gemm_simt<float,128,64,8,8,4>"}}
     if s.cpu:
         import oracle
         A = a.cpu().numpy()
@@ -535,8 +555,8 @@ def suite_gemm_bf16(s: Suite) -> dict:
     return out
 
 
-def suite_conv(s: Suite, dtype: str) -> dict:
-    """configs[4] conv: NHWC x 64x56x56x256, KRSC w 256x3x3x256, pad 1, stride 1,
+def suite_conv(s: Suite, dtype: str, krsc: bool = True) -> dict:
+    """configs[4] conv: NHWC x 64x56x56x256, KRSC (or KCRS) w 256x3x3x256, pad 1, stride 1,
     normal(0, 0.02) seed 11 (x then w), cross-correlation, alpha 1, beta 0."""
     from muda_b200 import capi, synth
     torch = s.torch
@@ -556,7 +576,7 @@ def suite_conv(s: Suite, dtype: str) -> dict:
     assert L.cudnnCreateTensorDescriptor(C.byref(yd)) == 0
     assert L.cudnnSetTensor4dDescriptor(yd, 1, dt_code, n, kk, hh, ww) == 0
     assert L.cudnnCreateFilterDescriptor(C.byref(wd)) == 0
-    assert L.cudnnSetFilter4dDescriptor(wd, dt_code, 1, kk, c, 3, 3) == 0
+    assert L.cudnnSetFilter4dDescriptor(wd, dt_code, 1 if krsc else 0, kk, c, 3, 3) == 0
     assert L.cudnnCreateConvolutionDescriptor(C.byref(cd)) == 0
     assert L.cudnnSetConvolution2dDescriptor(cd, 1, 1, 1, 1, 1, 1, 1, 0) == 0
     one, zero = C.c_float(1.0), C.c_float(0.0)
@@ -573,10 +593,15 @@ def suite_conv(s: Suite, dtype: str) -> dict:
     assert L.cudnnDestroy(h) == 0
     flop = 2.0 * n * kk * hh * ww * c * 9
     tf = flop / (ms * 1e-3) / 1e12
-    bound = "tensor" if dtype == "bf16" else "ffma"
-    return {"value": tf, "unit": "TFLOP/s", "ms": ms, "dtype": dtype,
-            "config": f"NHWC {n}x{hh}x{ww}x{c} -> {kk}, 3x3 pad 1, KRSC filter",
-            "roofline": s.roof(f"conv ({dtype})", tf, bound), "launches": launches}
+    if dtype == "bf16":
+        bound, kern = "tensor", "tc_gemm_kernel<ConvProblem<bf16,1>,256,4,1>"
+    else:
+        bound, kern = "tensor-tf32x3", "tc_gemm_split_kernel<ConvProblem<float,2>,256,2,2>"
+    return {"value": tf, "unit": "TFLOP/s", "ms": ms,
+            "dtype": dtype if dtype == "bf16" else "f32 (split-tf32 on tcgen05)",
+            "config": f"NHWC {n}x{hh}x{ww}x{c} -> {kk}, 3x3 pad 1, "
+                      f"{'KRSC' if krsc else 'KCRS'} filter",
+            "roofline": s.roof(kern, tf, bound), "launches": launches}
 
 
 SUITE = {
@@ -587,6 +612,7 @@ SUITE = {
     "gemm_bf16": suite_gemm_bf16,
     "conv_bf16": lambda s: suite_conv(s, "bf16"),
     "conv_f32": lambda s: suite_conv(s, "f32"),
+    "conv_f32_kcrs": lambda s: suite_conv(s, "f32", krsc=False),
 }
 
 

@@ -12,13 +12,13 @@
 //
 // fp32 GEMM (the reference's cublasSgemm arithmetic, cublas_kernels.metal:969-1006:
 // fp32 products accumulated in fp32, then C = alpha*acc + beta*C) runs on the same
-// loop in split-tf32 form: one pass writes each operand, in any transpose and
+// loop in split-tf32 form: one pass writes both operands, in any transpose and
 // layout, as K-major hi/lo tf32 planes into the handle's workspace, and the
-// tensor cores accumulate lo*hi + hi*lo + hi*hi (within 1.5 * 2^-20 relative
-// per product, the accuracy class of an fp32 FMA loop).  Problems with fewer output tiles
-// than half the SMs split K across CTAs; each split writes raw sums to the
-// workspace and one pass adds them in split order (deterministic) and applies
-// alpha and beta.
+// tensor cores accumulate lo*hi + hi*lo + hi*hi with the chunked fp32 accumulation
+// of tc_gemm_split_kernel (fp32-class accuracy).  Problems with fewer output
+// tiles than half the SMs split K across CTAs; each split writes raw sums to the
+// workspace and one pass over all SMs adds them in split order (deterministic)
+// and applies alpha and beta.
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
@@ -261,25 +261,48 @@ struct SplitGemmProblem {
   }
 };
 
-// C = alpha * (sum of the ksplit partial sums, in split order) + beta * C.
-__global__ void reduce_splits(const float* __restrict__ partial, int ksplit, int m, int n,
-                              int batch, float* c, long long ldc, long long stride_c,
-                              float alpha, float beta, const float* alpha_dev,
-                              const float* beta_dev) {
+// C = alpha * (sum of the ksplit partial sums, in split order) + beta * C; one
+// column of one batch entry per blockIdx.y step, rows across threads (four rows
+// per thread with Vec: m % 4 == 0, ldc % 4 == 0, C 16-byte aligned).
+template <bool Vec>
+__global__ void __launch_bounds__(256)
+    reduce_splits(const float* __restrict__ partial, int ksplit, int m, int n, int batch,
+                  float* c, long long ldc, long long stride_c, float alpha, float beta,
+                  const float* alpha_dev, const float* beta_dev) {
   const float a = alpha_dev ? *alpha_dev : alpha;
   const float b = beta_dev ? *beta_dev : beta;
   const long long mn = static_cast<long long>(m) * n;
-  const long long total = mn * batch;
-  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
-       i += static_cast<long long>(gridDim.x) * blockDim.x) {
-    const long long z = i / mn;
-    const long long e = i % mn;
-    const float* pz = partial + z * ksplit * mn + e;
-    float acc = 0.0f;
-    for (int sp = 0; sp < ksplit; ++sp) acc += pz[sp * mn];
-    float* cp = c + z * stride_c + (e % m) + (e / m) * ldc;
-    const float prev = (b == 0.0f) ? 0.0f : b * *cp;
-    *cp = fmaf(a, acc, prev);
+  const int per = Vec ? m / 4 : m;
+  const long long cols = static_cast<long long>(n) * batch;
+  for (long long cz = blockIdx.y; cz < cols; cz += gridDim.y) {
+    const long long z = cz / n, col = cz % n;
+    const float* pz = partial + z * ksplit * mn + col * m;
+    float* cp = c + z * stride_c + col * ldc;
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < per; i += gridDim.x * blockDim.x) {
+      if constexpr (Vec) {
+        float4 acc = __ldcs(reinterpret_cast<const float4*>(pz) + i);
+        for (int sp = 1; sp < ksplit; ++sp) {
+          const float4 v = __ldcs(reinterpret_cast<const float4*>(pz + sp * mn) + i);
+          acc.x += v.x;
+          acc.y += v.y;
+          acc.z += v.z;
+          acc.w += v.w;
+        }
+        float4* cv = reinterpret_cast<float4*>(cp) + i;
+        float4 prev = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        if (b != 0.0f) {
+          prev = *cv;
+          prev = make_float4(b * prev.x, b * prev.y, b * prev.z, b * prev.w);
+        }
+        *cv = make_float4(fmaf(a, acc.x, prev.x), fmaf(a, acc.y, prev.y), fmaf(a, acc.z, prev.z),
+                          fmaf(a, acc.w, prev.w));
+      } else {
+        float acc = __ldcs(pz + i);
+        for (int sp = 1; sp < ksplit; ++sp) acc += __ldcs(pz + sp * mn + i);
+        const float prev = (b == 0.0f) ? 0.0f : b * cp[i];
+        cp[i] = fmaf(a, acc, prev);
+      }
+    }
   }
 }
 
@@ -290,7 +313,7 @@ struct SplitPlan {
   int ksplit;  // K splits
   int kb_per;  // k-blocks per split
   std::size_t a_floats, b_floats, p_floats;
-  std::size_t bytes() const { return (a_floats + b_floats + p_floats) * sizeof(float); }
+  std::size_t bytes() const { return (a_floats + b_floats + p_floats) * 4; }
 };
 
 SplitPlan plan_split(const GemmArgs& g, int sms, int nb) {
@@ -355,13 +378,13 @@ cudaError_t run_chunk(const GemmArgs& g, const SplitPlan& pl, int z0, int nb, fl
   float* pp = pb + pl.b_floats;
   const float* a = static_cast<const float*>(g.a) + z0 * g.stride_a;
   const float* b = static_cast<const float*>(g.b) + z0 * g.stride_b;
-  // op(A) is m x k: element (i, p) at A[i + p*lda] (N) or A[p + i*lda] (T)
-  cudaError_t e = tc::launch_tf32_split(a, g.m, g.k, nb, g.trans_a ? g.lda : 1,
-                                        g.trans_a ? 1 : g.lda, g.stride_a, pa, ldk, stream);
-  if (e != cudaSuccess) return e;
-  // op(B) is k x n: element (p, j) at B[p + j*ldb] (N) or B[j + p*ldb] (T); rows are j
-  e = tc::launch_tf32_split(b, g.n, g.k, nb, g.trans_b ? 1 : g.ldb, g.trans_b ? g.ldb : 1,
-                            g.stride_b, pb, ldk, stream);
+  // op(A) is m x k: element (i, p) at A[i + p*lda] (N) or A[p + i*lda] (T);
+  // op(B) is k x n: element (p, j) at B[p + j*ldb] (N) or B[j + p*ldb] (T), rows j
+  const tc::SplitJob ja{a, g.m, g.k, nb, g.trans_a ? g.lda : 1, g.trans_a ? 1 : g.lda,
+                        g.stride_a, pa, ldk};
+  const tc::SplitJob jb{b, g.n, g.k, nb, g.trans_b ? 1 : g.ldb, g.trans_b ? g.ldb : 1,
+                        g.stride_b, pb, ldk};
+  cudaError_t e = tc::launch_tf32_split_pair(ja, jb, stream);
   if (e != cudaSuccess) return e;
   SplitGemmProblem p{};
   if (!make_plane_map(&p.ma, pa, g.k, g.m, nb, ldk, tc::kBM) ||
@@ -384,12 +407,20 @@ cudaError_t run_chunk(const GemmArgs& g, const SplitPlan& pl, int z0, int nb, fl
   p.beta_dev = g.beta_dev;
   e = tc::launch_tc_gemm<SplitGemmProblem, BN, kStages32, tc::kFmtTf32x3>(p, sms, to, stream);
   if (e != cudaSuccess || pl.ksplit == 1) return e;
-  const long long total = static_cast<long long>(g.m) * g.n * nb;
-  const long long want = (total + 255) / 256;
-  const long long cap = static_cast<long long>(sms) * 8;
-  reduce_splits<<<static_cast<unsigned>(want < cap ? want : cap), 256, 0, stream>>>(
-      pp, pl.ksplit, g.m, g.n, nb, p.c, g.ldc, g.stride_c, g.alpha, g.beta, g.alpha_dev,
-      g.beta_dev);
+  const bool vec = g.m % 4 == 0 && g.ldc % 4 == 0 && (nb == 1 || g.stride_c % 4 == 0) &&
+                   aligned_to(p.c, 16);
+  const int per = vec ? g.m / 4 : g.m;
+  const long long cols = static_cast<long long>(g.n) * nb;
+  const dim3 grid(static_cast<unsigned>((per + 255) / 256 < 64 ? (per + 255) / 256 : 64),
+                  static_cast<unsigned>(cols < 65535 ? cols : 65535));
+  if (vec)
+    reduce_splits<true><<<grid, 256, 0, stream>>>(pp, pl.ksplit, g.m, g.n, nb, p.c, g.ldc,
+                                                  g.stride_c, g.alpha, g.beta, g.alpha_dev,
+                                                  g.beta_dev);
+  else
+    reduce_splits<false><<<grid, 256, 0, stream>>>(pp, pl.ksplit, g.m, g.n, nb, p.c, g.ldc,
+                                                   g.stride_c, g.alpha, g.beta, g.alpha_dev,
+                                                   g.beta_dev);
   return cudaGetLastError();
 }
 

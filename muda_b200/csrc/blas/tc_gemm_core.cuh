@@ -40,6 +40,7 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include <atomic>
 #include <cstdint>
 
 #include "blas/tc_ptx.cuh"
@@ -486,9 +487,17 @@ cudaError_t launch_tc_gemm(const P& p, int sms, unsigned int* timeouts, cudaStre
     kern = tc_gemm_split_kernel<P, BN, STAGES, kSplitChunkKb>;
   else
     kern = tc_gemm_kernel<P, BN, STAGES, FMT>;
-  const cudaError_t e =
-      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::SMEM);
-  if (e != cudaSuccess) return e;
+  // the shared-memory opt-in is per device and per kernel: set it once
+  static std::atomic<unsigned long long> attr_set{0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return cudaErrorInvalidDevice;
+  const unsigned long long bit = 1ull << (dev & 63);
+  if ((attr_set.load(std::memory_order_acquire) & bit) == 0) {
+    const cudaError_t e =
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::SMEM);
+    if (e != cudaSuccess) return e;
+    attr_set.fetch_or(bit, std::memory_order_release);
+  }
   const long long grid = p.tiles_total < sms ? p.tiles_total : sms;
   if (grid <= 0) return cudaSuccess;
   kern<<<static_cast<unsigned>(grid), split ? kSplitThreads : kThreads, S::SMEM, stream>>>(

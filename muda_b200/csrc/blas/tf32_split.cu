@@ -3,6 +3,8 @@
 
 #include <cuda_runtime.h>
 
+#include "common/device.hpp"
+
 namespace mb200::tc {
 namespace {
 
@@ -24,50 +26,54 @@ __device__ __forceinline__ void split(float x, float& hi, float& lo) {
 constexpr int kTile = 32;
 constexpr int kRowsPerPass = 8;
 
-// One 32 x 32 tile (32 k by 32 rows) per block of 32 x 8 threads, staged in
-// shared memory so both the contiguous read and the k-contiguous write coalesce.
-template <bool KContig>
-__global__ void __launch_bounds__(kTile* kRowsPerPass)
-    split_tiles(const float* __restrict__ src, long long rows, long long cols, int batch,
-                long long rs, long long ks, long long zs, float* __restrict__ dst, long long ldk) {
-  __shared__ float tile[kTile][kTile + 1];  // [row][k]
-  const long long tiles_k = (cols + kTile - 1) / kTile;
-  const long long tiles_r = (rows + kTile - 1) / kTile;
-  const long long plane = static_cast<long long>(batch) * rows * ldk;
+// One 32 x 32 tile (32 k by 32 rows) of job j, staged in shared memory so both
+// the contiguous read (along k or along rows) and the k-contiguous write coalesce.
+__device__ __forceinline__ void split_tile(const SplitJob& j, long long z, long long r0,
+                                           long long k0, float (*tile)[kTile + 1]) {
   const int tx = threadIdx.x, ty = threadIdx.y;
-  for (long long z = blockIdx.z; z < batch; z += gridDim.z) {
-    const float* sz = src + z * zs;
-    float* dz = dst + z * rows * ldk;
-    for (long long tr = blockIdx.y; tr < tiles_r; tr += gridDim.y) {
-      for (long long tk = blockIdx.x; tk < tiles_k; tk += gridDim.x) {
-        const long long r0 = tr * kTile, k0 = tk * kTile;
+  const bool kcontig = j.ks == 1;
+  const float* sz = j.src + z * j.zs;
 #pragma unroll
-        for (int i = 0; i < kTile / kRowsPerPass; ++i) {
-          const int a = ty + i * kRowsPerPass;  // the non-contiguous index of the tile
-          const long long r = KContig ? r0 + a : r0 + tx;
-          const long long k = KContig ? k0 + tx : k0 + a;
-          float v = 0.0f;
-          if (r < rows && k < cols) v = sz[r * rs + k * ks];
-          if (KContig)
-            tile[a][tx] = v;
-          else
-            tile[tx][a] = v;
-        }
-        __syncthreads();
+  for (int i = 0; i < kTile / kRowsPerPass; ++i) {
+    const int a = ty + i * kRowsPerPass;  // the non-contiguous index of the tile
+    const long long r = kcontig ? r0 + a : r0 + tx;
+    const long long k = kcontig ? k0 + tx : k0 + a;
+    float v = 0.0f;
+    if (r < j.rows && k < j.cols) v = sz[r * j.rs + k * j.ks];
+    if (kcontig)
+      tile[a][tx] = v;
+    else
+      tile[tx][a] = v;
+  }
+  __syncthreads();
+  const long long plane = static_cast<long long>(j.batch) * j.rows * j.ldk;
+  float* dz = j.dst + z * j.rows * j.ldk;
 #pragma unroll
-        for (int i = 0; i < kTile / kRowsPerPass; ++i) {
-          const int a = ty + i * kRowsPerPass;
-          const long long r = r0 + a, k = k0 + tx;
-          if (r < rows && k < cols) {
-            float hi, lo;
-            split(tile[a][tx], hi, lo);
-            dz[r * ldk + k] = hi;
-            dz[plane + r * ldk + k] = lo;
-          }
-        }
-        __syncthreads();
-      }
+  for (int i = 0; i < kTile / kRowsPerPass; ++i) {
+    const int a = ty + i * kRowsPerPass;
+    const long long r = r0 + a, k = k0 + tx;
+    if (r < j.rows && k < j.cols) {
+      float hi, lo;
+      split(tile[a][tx], hi, lo);
+      dz[r * j.ldk + k] = hi;
+      dz[plane + r * j.ldk + k] = lo;
     }
+  }
+  __syncthreads();
+}
+
+// Blocks stride over the tiles of job blockIdx.y (0 or 1; one job when y == 1).
+__global__ void __launch_bounds__(kTile* kRowsPerPass)
+    split_jobs(const SplitJob j0, const SplitJob j1) {
+  __shared__ float tile[kTile][kTile + 1];  // [row][k]
+  const SplitJob& j = blockIdx.y == 0 ? j0 : j1;
+  const long long tiles_k = (j.cols + kTile - 1) / kTile;
+  const long long tiles_r = (j.rows + kTile - 1) / kTile;
+  const long long per = tiles_k * tiles_r;
+  const long long total = per * j.batch;
+  for (long long t = blockIdx.x; t < total; t += gridDim.x) {
+    const long long z = t / per, rt = t % per;
+    split_tile(j, z, (rt / tiles_k) * kTile, (rt % tiles_k) * kTile, tile);
   }
 }
 
@@ -91,20 +97,35 @@ __global__ void split_filter(const float* __restrict__ w, int K, int C, int R, i
 
 }  // namespace
 
+namespace {
+
+unsigned split_grid(const SplitJob& a, const SplitJob* b) {
+  auto tiles = [](const SplitJob& j) {
+    return ((j.cols + kTile - 1) / kTile) * ((j.rows + kTile - 1) / kTile) * j.batch;
+  };
+  long long t = tiles(a);
+  if (b != nullptr && tiles(*b) > t) t = tiles(*b);
+  const int sms = sm_count(current_device());
+  const long long cap = static_cast<long long>(sms > 0 ? sms : 148) * 8;
+  return static_cast<unsigned>(t < 1 ? 1 : (t < cap ? t : cap));
+}
+
+}  // namespace
+
 cudaError_t launch_tf32_split(const float* src, long long rows, long long cols, int batch,
                               long long rs, long long ks, long long zs, float* dst,
                               long long ldk, cudaStream_t stream) noexcept {
   if (rows <= 0 || cols <= 0 || batch <= 0) return cudaSuccess;
-  const long long tiles_k = (cols + kTile - 1) / kTile;
-  const long long tiles_r = (rows + kTile - 1) / kTile;
-  const dim3 grid(static_cast<unsigned>(tiles_k < 1024 ? tiles_k : 1024),
-                  static_cast<unsigned>(tiles_r < 65535 ? tiles_r : 65535),
-                  static_cast<unsigned>(batch < 65535 ? batch : 65535));
-  const dim3 block(kTile, kRowsPerPass);
-  if (ks == 1)
-    split_tiles<true><<<grid, block, 0, stream>>>(src, rows, cols, batch, rs, ks, zs, dst, ldk);
-  else
-    split_tiles<false><<<grid, block, 0, stream>>>(src, rows, cols, batch, rs, ks, zs, dst, ldk);
+  const SplitJob j{src, rows, cols, batch, rs, ks, zs, dst, ldk};
+  split_jobs<<<dim3(split_grid(j, nullptr), 1), dim3(kTile, kRowsPerPass), 0, stream>>>(j, j);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_tf32_split_pair(const SplitJob& a, const SplitJob& b,
+                                   cudaStream_t stream) noexcept {
+  if (a.rows <= 0 || a.cols <= 0 || a.batch <= 0 || b.rows <= 0 || b.cols <= 0 || b.batch <= 0)
+    return cudaErrorInvalidValue;
+  split_jobs<<<dim3(split_grid(a, &b), 2), dim3(kTile, kRowsPerPass), 0, stream>>>(a, b);
   return cudaGetLastError();
 }
 

@@ -29,6 +29,20 @@ cudaError_t launch_tf32_split(const float* src, long long rows, long long cols, 
                               long long rs, long long ks, long long zs, float* dst,
                               long long ldk, cudaStream_t stream) noexcept;
 
+// One matrix of a split pass: the arguments of launch_tf32_split.
+struct SplitJob {
+  const float* src;
+  long long rows, cols;
+  int batch;
+  long long rs, ks, zs;
+  float* dst;
+  long long ldk;
+};
+
+// Splits two matrices in one launch (e.g. both GEMM operands).
+cudaError_t launch_tf32_split_pair(const SplitJob& a, const SplitJob& b,
+                                   cudaStream_t stream) noexcept;
+
 // Convolution filter of K output channels, C input channels and R x S taps,
 // stored KRSC (krsc) or KCRS, written as planes dst[p][k][(r*S + s)*C + c].
 cudaError_t launch_tf32_split_filter(const float* w, int K, int C, int R, int S, bool krsc,

@@ -134,7 +134,8 @@ def run_ours(args) -> None:
     gen = C.c_void_p()
     assert L.curandCreateGenerator(C.byref(gen), capi.CURAND_RNG_PSEUDO_PHILOX4_32_10) == 0
     assert L.curandSetPseudoRandomGeneratorSeed(gen, SEED) == 0
-    base_offset = rank * 2 * N_WORDS
+    from muda_b200.partition import rng_rank_offset
+    base_offset = rng_rank_offset(rank, N_WORDS)
     assert L.curandSetGeneratorOffset(gen, base_offset) == 0
     assert L.curandSetStream(gen, sp) == 0
 
@@ -677,6 +678,85 @@ def run_reference(args) -> None:
     print(json.dumps(line), flush=True)
 
 
+def run_spmv_dist(args) -> None:
+    """configs[2] SpMV across the ranks of torchrun (strong scaling: the 4M x 4M matrix
+    is fixed, its rows split into nnz-balanced blocks).  Each step all-gathers x
+    (NCCL, into local HBM) and runs the local cusparseSpMV; reported are the step
+    time (max over ranks) with and without the exchange."""
+    import torch
+    import torch.distributed as dist
+
+    from muda_b200 import synth
+    from muda_b200.dist_spmv import DistSpMV
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    group = None
+    if world > 1:
+        dist.init_process_group("nccl", timeout=__import__("datetime").timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    rows = (1 << 22) // args.scale
+    mtx = synth.powerlaw_csr(torch, rows, rows, seed=7)
+    nnz = mtx["nnz"]
+    d = DistSpMV.from_full(torch, dist if world > 1 else None, group, mtx["row_offsets"],
+                           mtx["col_ind"], mtx["values"], rows)
+    x_local = d.x_slice(mtx["x"])
+    y_local = torch.zeros(max(d.rows, 1), dtype=torch.float32, device="cuda")
+    del mtx
+    torch.cuda.empty_cache()
+    flush = torch.empty(64 << 20, dtype=torch.float32, device="cuda")  # 256 MB > L2
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local])
+        torch.cuda.synchronize()
+
+    full_ms, local_ms, gather_ms = [], [], []
+    for it in range(args.warmup + args.steps):
+        flush.fill_(float(it))
+        barrier()
+        ev[0].record()
+        d.gather_x(x_local)
+        ev[1].record()
+        d.local(1.0, 0.0, y_local)
+        ev[2].record()
+        torch.cuda.synchronize()
+        if it >= args.warmup:
+            gather_ms.append(ev[0].elapsed_time(ev[1]))
+            local_ms.append(ev[1].elapsed_time(ev[2]))
+            full_ms.append(ev[0].elapsed_time(ev[2]))
+    stats = torch.tensor([float(np.mean(full_ms)), float(np.mean(local_ms)),
+                          float(np.mean(gather_ms))], device="cuda")
+    if world > 1:
+        dist.all_reduce(stats, op=dist.ReduceOp.MAX)
+    shares = torch.tensor([d.nnz], dtype=torch.int64, device="cuda")
+    if world > 1:
+        parts = [torch.zeros_like(shares) for _ in range(world)]
+        dist.all_gather(parts, shares)
+        shares = torch.cat(parts)
+    full, loc, gat = (float(v) for v in stats.cpu())
+    alg_bytes = nnz * 8 + (rows + 1) * 4 + rows * 4 + rows * 4
+    if rank == 0:
+        nz = shares.cpu().numpy()
+        print(json.dumps({
+            "routine": "spmv_dist", "metric": "SpMV GB/s (algorithmic bytes of the whole "
+            "matrix / step time, max over ranks)", "value": alg_bytes / (full * 1e-3) / 1e9,
+            "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": full, "scaling": "strong", "higher_is_better": True,
+            "dtype": "f32/i32", "data": "synthetic power-law CSR (configs[2])",
+            "config": {"workload": f"{rows} x {rows}, nnz {nnz}, rows split into "
+                                   f"{world} nnz-balanced blocks", "l2": "256 MB flush "
+                                   "before each step"},
+            "kernel_only": {"ms": loc, "GB/s": alg_bytes / (loc * 1e-3) / 1e9},
+            "allgather_ms": gat, "nnz_per_rank": [int(v) for v in nz],
+            "imbalance": float(nz.max() / max(float(nz.mean()), 1.0))}), flush=True)
+    d.close()
+    if world > 1:
+        dist.destroy_process_group()
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -690,11 +770,15 @@ def main() -> None:
     ap.add_argument("--suite", default="all",
                     help="comma list of other routines to measure at N=1 "
                          f"({','.join(SUITE)}), 'all' or 'none'")
-    ap.add_argument("--routine", default=None, choices=list(SUITE),
-                    help="measure only this routine and print its line (profiling)")
+    ap.add_argument("--routine", default=None, choices=list(SUITE) + ["spmv_dist"],
+                    help="measure only this routine and print its line (profiling); "
+                         "spmv_dist runs under torchrun across the ranks")
     ap.add_argument("--scale", type=int, default=1,
                     help="divide the routine's batch/size by this factor (profiling)")
     args = ap.parse_args()
+    if args.routine == "spmv_dist":
+        run_spmv_dist(args)
+        return
     if args.routine:
         import torch
         torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))

@@ -1,0 +1,195 @@
+"""Row-block distributed CSR SpMV over the ranks of a process group: y = alpha*A*x + beta*y.
+
+The reference's cusparseSpMV (libraries/sparse/src/cusparse_ops.mm:71-211) is a
+single-device call.  Across GPUs the product has exactly one exchange step, the
+vector x, so this module shards the matrix and exchanges only x:
+
+- rows are split into contiguous blocks holding about the same number of stored
+  entries (balanced by nnz, not by row count: power-law rows of up to 4096
+  entries would otherwise load one rank far more than another); rank r keeps its
+  row block (row offsets rebased to its first entry, global column indices) and
+  the matching block of y;
+- x is held in equal contiguous blocks of ceil(cols / world) entries; every call
+  all-gathers the blocks into a full copy of x in this GPU's own memory (one
+  all_gather_into_tensor, NCCL over NVLink), then runs the local product through
+  the library's C ABI (cusparseSpMV) on the current stream, so no kernel ever
+  reads another GPU's memory.
+
+The local product is pluggable (``local_spmv``) only so that the partition and
+exchange logic can be tested on CPU ranks with the gloo backend; the default is
+the CUDA path, which raises if the library is not built.
+"""
+
+from __future__ import annotations
+
+import ctypes as C
+from typing import Callable
+
+import numpy as np
+
+
+def nnz_balanced_bounds(row_offsets, parts: int) -> list[int]:
+    """First row of each of `parts` contiguous row blocks (plus the row count at the
+    end) such that every block holds about nnz / parts stored entries.
+
+    row_offsets: the CSR offsets (rows + 1 entries, base already subtracted), any
+    array-like of integers.  Blocks are cut at the row where the running entry count
+    first reaches r * nnz / parts, so each block is within one row's length of the
+    target; empty blocks are allowed when a single row outweighs a share."""
+    ro = np.asarray(row_offsets, dtype=np.int64)
+    rows = len(ro) - 1
+    if parts < 1:
+        raise ValueError("parts must be positive")
+    nnz = int(ro[-1] - ro[0])
+    bounds = [0]
+    for r in range(1, parts):
+        target = ro[0] + (nnz * r) // parts
+        b = int(np.searchsorted(ro, target, side="left"))
+        bounds.append(min(max(b, bounds[-1]), rows))
+    bounds.append(rows)
+    return bounds
+
+
+def x_block(cols: int, world: int) -> int:
+    """Entries of x each rank holds (the last block is padded)."""
+    return (cols + world - 1) // world
+
+
+class _CudaLocal:
+    """cusparseSpMV on the local row block through the C ABI (handle and
+    descriptors created once per vector buffer pair)."""
+
+    def __init__(self, torch, offsets, col_ind, values, rows, cols, nnz, base):
+        from muda_b200 import capi
+        self.torch = torch
+        self.L = capi.cusparse()  # raises LibraryMissing when the library is not built
+        self.h = C.c_void_p()
+        assert self.L.cusparseCreate(C.byref(self.h)) == 0
+        self.mat = C.c_void_p()
+        st = self.L.cusparseCreateCsr(C.byref(self.mat), rows, cols, nnz,
+                                      C.c_void_p(offsets.data_ptr()),
+                                      C.c_void_p(col_ind.data_ptr()),
+                                      C.c_void_p(values.data_ptr()), 2, 2, base, 0)
+        if st != 0:
+            raise RuntimeError(f"cusparseCreateCsr failed with status {st}")
+        self.rows, self.cols = rows, cols
+        self._vecs: dict[tuple[int, int], tuple[C.c_void_p, C.c_void_p]] = {}
+
+    def __call__(self, x_full, y_local, alpha: float, beta: float) -> None:
+        key = (x_full.data_ptr(), y_local.data_ptr())
+        if key not in self._vecs:
+            vx, vy = C.c_void_p(), C.c_void_p()
+            assert self.L.cusparseCreateDnVec(C.byref(vx), self.cols,
+                                              C.c_void_p(x_full.data_ptr()), 0) == 0
+            assert self.L.cusparseCreateDnVec(C.byref(vy), self.rows,
+                                              C.c_void_p(y_local.data_ptr()), 0) == 0
+            self._vecs[key] = (vx, vy)
+        vx, vy = self._vecs[key]
+        stream = self.torch.cuda.current_stream().cuda_stream
+        assert self.L.cusparseSetStream(self.h, C.c_void_p(stream)) == 0
+        st = self.L.cusparseSpMV(self.h, 0, C.byref(C.c_float(alpha)), self.mat, vx,
+                                 C.byref(C.c_float(beta)), vy, 0, 0, None)
+        if st != 0:
+            raise RuntimeError(f"cusparseSpMV failed with status {st}")
+
+    def close(self) -> None:
+        for vx, vy in self._vecs.values():
+            self.L.cusparseDestroyDnVec(vx)
+            self.L.cusparseDestroyDnVec(vy)
+        self._vecs.clear()
+        if self.mat:
+            self.L.cusparseDestroySpMat(self.mat)
+            self.mat = C.c_void_p()
+        if self.h:
+            self.L.cusparseDestroy(self.h)
+            self.h = C.c_void_p()
+
+
+class DistSpMV:
+    """One rank's share of a row-block distributed CSR matrix.
+
+    Build it with :meth:`from_full` (every rank passes the same full matrix and
+    keeps its block) or directly from the local block.  ``spmv(alpha, x_local,
+    beta, y_local)`` all-gathers x and computes this rank's rows of y.  With
+    ``dist=None`` the object is a single rank (no process group, x is copied)."""
+
+    def __init__(self, torch, dist, group, *, offsets, col_ind, values, row_begin: int,
+                 row_end: int, cols: int, base: int = 0,
+                 local_spmv: Callable | None = None, device=None):
+        self.torch, self.dist, self.group = torch, dist, group
+        self.world = dist.get_world_size(group) if dist is not None else 1
+        self.rank = dist.get_rank(group) if dist is not None else 0
+        self.row_begin, self.row_end = row_begin, row_end
+        self.rows = row_end - row_begin
+        self.cols = cols
+        self.nnz = int(offsets[-1].item() - offsets[0].item()) if self.rows > 0 else 0
+        self.xb = x_block(cols, self.world)
+        dev = device if device is not None else offsets.device
+        self.x_full = torch.zeros(self.xb * self.world, dtype=torch.float32, device=dev)
+        if local_spmv is None:
+            self._local = _CudaLocal(torch, offsets, col_ind, values, self.rows, cols,
+                                     self.nnz, base) if self.rows > 0 else None
+        else:
+            self._local = lambda x, y, a, b: local_spmv(offsets, col_ind, values, x, y, a, b)
+        self._keep = (offsets, col_ind, values)
+
+    @classmethod
+    def from_full(cls, torch, dist, group, row_offsets, col_ind, values, cols: int, *,
+                  base: int = 0, local_spmv: Callable | None = None):
+        """Slices this rank's nnz-balanced row block out of the full CSR matrix (the
+        same on every rank); the block's offsets are rebased so its first entry is
+        entry 0 (plus the index base, which offsets and columns keep)."""
+        world = dist.get_world_size(group) if dist is not None else 1
+        rank = dist.get_rank(group) if dist is not None else 0
+        ro_host = (row_offsets.cpu().numpy().astype(np.int64) - base)
+        bounds = nnz_balanced_bounds(ro_host, world)
+        r0, r1 = bounds[rank], bounds[rank + 1]
+        e0, e1 = int(ro_host[r0]), int(ro_host[r1])
+        # rebased to the block's first entry, still in the caller's index base
+        offs = (row_offsets[r0:r1 + 1].to(torch.int64) - e0).to(torch.int32).contiguous()
+        cols_l = col_ind[e0:e1].contiguous()
+        vals_l = values[e0:e1].contiguous()
+        obj = cls(torch, dist, group, offsets=offs, col_ind=cols_l, values=vals_l, row_begin=r0,
+                  row_end=r1, cols=cols, base=base, local_spmv=local_spmv,
+                  device=row_offsets.device)
+        obj.bounds = bounds
+        return obj
+
+    def x_slice(self, x_global):
+        """This rank's block of a full-length x (padded with zeros at the end)."""
+        lo = self.rank * self.xb
+        hi = min(lo + self.xb, self.cols)
+        out = self.torch.zeros(self.xb, dtype=self.torch.float32, device=self.x_full.device)
+        if hi > lo:
+            out[:hi - lo] = x_global[lo:hi]
+        return out
+
+    def gather_x(self, x_local) -> None:
+        """x_full <- concatenation of every rank's x block (the exchange step)."""
+        if x_local.numel() != self.xb:
+            raise ValueError(f"x block must hold {self.xb} entries, got {x_local.numel()}")
+        if self.world == 1:
+            self.x_full.copy_(x_local)
+            return
+        if self.dist.get_backend(self.group) == "nccl":
+            self.dist.all_gather_into_tensor(self.x_full, x_local, group=self.group)
+        else:
+            parts = list(self.x_full.split(self.xb))
+            self.dist.all_gather(parts, x_local, group=self.group)
+
+    def local(self, alpha: float, beta: float, y_local) -> None:
+        """This rank's rows of y from the gathered x (no communication)."""
+        if self.rows == 0:
+            return
+        if y_local.numel() < self.rows:
+            raise ValueError("y block is shorter than this rank's row block")
+        self._local(self.x_full[:self.cols], y_local, alpha, beta)
+
+    def spmv(self, alpha: float, x_local, beta: float, y_local) -> None:
+        self.gather_x(x_local)
+        self.local(alpha, beta, y_local)
+
+    def close(self) -> None:
+        if isinstance(self._local, _CudaLocal):
+            self._local.close()
+        self._local = None

@@ -1,0 +1,152 @@
+"""N > 1 host logic on CPU ranks (gloo, world size 2, 127.0.0.1).
+
+- Distributed SpMV (muda_b200.dist_spmv): the nnz-balanced row partition, the
+  rebased local blocks and the x exchange, with the oracle's CPU SpMV standing in
+  for the local CUDA product; the ranks' y blocks must reproduce the
+  single-device oracle result bit for bit (same per-row fma order).
+- RNG weak scaling (muda_b200.partition): the ranks' counter ranges are disjoint
+  and contiguous, so their concatenated streams equal one generator's stream.
+"""
+
+import os
+import socket
+
+import numpy as np
+import pytest
+
+import oracle
+from muda_b200.dist_spmv import nnz_balanced_bounds, x_block
+from muda_b200.partition import rng_rank_offset
+
+WORLD = 2
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _run(fn, *args):
+    import torch.multiprocessing as mp
+    port = _free_port()
+    mp.start_processes(fn, args=(WORLD, port, *args), nprocs=WORLD, join=True,
+                       start_method="spawn")
+
+
+def _init(rank, world, port):
+    import datetime
+
+    import torch.distributed as dist
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60))
+    return dist
+
+
+def _csr(seed, rows, cols, heavy_rows=()):
+    rng = np.random.default_rng(seed)
+    k = np.minimum(rng.integers(0, 9, rows), cols)
+    for r in heavy_rows:
+        k[r] = min(cols, 400)
+    ro = np.zeros(rows + 1, np.int64)
+    ro[1:] = np.cumsum(k)
+    ci = np.concatenate([np.sort(rng.choice(cols, kk, replace=False)) for kk in k]
+                        ).astype(np.int32) if ro[-1] else np.zeros(0, np.int32)
+    va = rng.uniform(-1, 1, ro[-1]).astype(np.float32)
+    x = rng.uniform(-1, 1, cols).astype(np.float32)
+    return ro.astype(np.int32), ci, va, x
+
+
+def _cpu_local(offsets, col_ind, values, x, y, alpha, beta):
+    out = oracle.spmv_csr(offsets.numpy(), col_ind.numpy(), values.numpy(), x.numpy(),
+                          alpha=alpha, beta=beta, y=y.numpy()[:len(offsets) - 1].copy(),
+                          threads=1)
+    y[:len(out)] = __import__("torch").from_numpy(out)
+
+
+def _spmv_worker(rank, world, port, rows, cols, heavy, alpha, beta):
+    import torch
+
+    from muda_b200.dist_spmv import DistSpMV
+    dist = _init(rank, world, port)
+    try:
+        ro, ci, va, x = _csr(11, rows, cols, heavy)
+        y0 = np.random.default_rng(3).uniform(-1, 1, rows).astype(np.float32)
+        d = DistSpMV.from_full(torch, dist, None, torch.from_numpy(ro), torch.from_numpy(ci),
+                               torch.from_numpy(va), cols, local_spmv=_cpu_local)
+        assert d.bounds == nnz_balanced_bounds(ro, world)
+        x_local = d.x_slice(torch.from_numpy(x))
+        y_local = torch.from_numpy(y0[d.row_begin:d.row_end].copy())
+        d.spmv(alpha, x_local, beta, y_local)
+        # the gathered x is the full vector on every rank
+        assert np.array_equal(d.x_full[:cols].numpy(), x)
+        # collect every rank's y block on every rank (pad to the longest block)
+        n_max = max(d.bounds[i + 1] - d.bounds[i] for i in range(world))
+        pad = torch.zeros(n_max, dtype=torch.float32)
+        pad[:d.rows] = y_local
+        parts = [torch.zeros(n_max, dtype=torch.float32) for _ in range(world)]
+        dist.all_gather(parts, pad)
+        y = np.concatenate([parts[i][:d.bounds[i + 1] - d.bounds[i]].numpy()
+                            for i in range(world)])
+        want = oracle.spmv_csr(ro, ci, va, x, alpha=alpha, beta=beta, y=y0.copy(), threads=1)
+        assert np.array_equal(y.view(np.uint32), want.view(np.uint32))
+        # nnz balance: every block within one row's length of nnz / world
+        nnz = int(ro[-1])
+        longest = int(np.max(np.diff(ro))) if rows else 0
+        for i in range(world):
+            share = int(ro[d.bounds[i + 1]] - ro[d.bounds[i]])
+            assert abs(share - nnz / world) <= longest + 1
+        d.close()
+    finally:
+        dist.destroy_process_group()
+
+
+def _rng_worker(rank, world, port, n, seed):
+    import torch
+    dist = _init(rank, world, port)
+    try:
+        off = rng_rank_offset(rank, n)
+        assert off % 4 == 0
+        mine, end = oracle.generate_uint(seed, off, 2 * n)
+        assert end == off + 2 * n
+        parts = [torch.zeros(2 * n, dtype=torch.int64) for _ in range(world)]
+        dist.all_gather(parts, torch.from_numpy(mine.astype(np.int64)))
+        got = np.concatenate([p.numpy() for p in parts]).astype(np.uint32)
+        want, _ = oracle.generate_uint(seed, 0, 2 * n * world)
+        assert np.array_equal(got, want)
+        # the uniform and normal blocks of this rank are the reference's calls at
+        # its offset: uniform at off, normal right after
+        u, after = oracle.generate_uniform(seed, off, n)
+        z, _ = oracle.generate_normal(seed, after, n, 0.0, 1.0)
+        assert after == off + n and np.isfinite(z).all() and (u > 0).all() and (u <= 1).all()
+    finally:
+        dist.destroy_process_group()
+
+
+def test_nnz_balanced_bounds_edges():
+    ro = np.array([0, 2, 4, 6, 8], np.int64)
+    assert nnz_balanced_bounds(ro, 2) == [0, 2, 4]
+    assert nnz_balanced_bounds(ro, 1) == [0, 4]
+    # one row outweighs everything: later blocks may be empty, never negative
+    ro = np.array([0, 1000, 1001, 1002], np.int64)
+    b = nnz_balanced_bounds(ro, 4)
+    assert b[0] == 0 and b[-1] == 3 and all(b[i] <= b[i + 1] for i in range(4))
+    # more parts than rows, and an empty matrix
+    assert nnz_balanced_bounds(np.array([0, 3], np.int64), 4)[-1] == 1
+    assert nnz_balanced_bounds(np.zeros(6, np.int64), 3) == [0, 0, 0, 5]
+    assert x_block(10, 4) == 3 and x_block(8, 4) == 2
+    with pytest.raises(ValueError):
+        nnz_balanced_bounds(ro, 0)
+
+
+@pytest.mark.parametrize("rows,cols,heavy,alpha,beta", [(1000, 777, (), 1.0, 0.0),
+                                                        (513, 2049, (0, 7), 0.5, -2.0),
+                                                        (3, 5, (), 1.0, 1.0)])
+def test_dist_spmv_two_gloo_ranks(rows, cols, heavy, alpha, beta):
+    _run(_spmv_worker, rows, cols, heavy, alpha, beta)
+
+
+def test_rng_weak_scaling_partition_two_gloo_ranks():
+    _run(_rng_worker, 4099 * 4, 1234)

@@ -202,3 +202,30 @@ def test_gpu_config_powerlaw(cuda, built):
     check(got, exact, absr, yo)
     lengths = np.diff(m["row_offsets"].cpu().numpy())
     assert lengths.min() >= 2 and lengths.max() <= 4096
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("base", [0, 1])
+def test_dist_spmv_single_rank_cuda_path(cuda, built, base):
+    """muda_b200.dist_spmv on one rank: the local product runs through cusparseSpMV
+    on the GPU (the path each rank takes under torchrun) and matches the oracle."""
+    torch = cuda
+    from muda_b200.dist_spmv import DistSpMV
+    rng = np.random.default_rng(21)
+    rows, cols = 3000, 2500
+    k = rng.integers(0, 40, rows)
+    ro = np.zeros(rows + 1, np.int64)
+    ro[1:] = np.cumsum(k)
+    ci = np.concatenate([np.sort(rng.choice(cols, kk, replace=False)) for kk in k]).astype(np.int32)
+    va = rng.uniform(-1, 1, ro[-1]).astype(np.float32)
+    x = rng.uniform(-1, 1, cols).astype(np.float32)
+    d = DistSpMV.from_full(torch, None, None, torch.from_numpy((ro + base).astype(np.int32)).cuda(),
+                           torch.from_numpy(ci + base).cuda(), torch.from_numpy(va).cuda(), cols,
+                           base=base)
+    y = torch.zeros(rows, dtype=torch.float32, device="cuda")
+    d.spmv(1.5, d.x_slice(torch.from_numpy(x).cuda()), 0.0, y)
+    torch.cuda.synchronize()
+    d.close()
+    want, exact, absr = oracle.spmv_csr(ro.astype(np.int32), ci, va, x, alpha=1.5, with_abs=True)
+    err = np.abs(y.cpu().numpy().astype(np.float64) - exact)  # exact includes alpha
+    assert np.all(err <= 1e-5 * 1.5 * absr + 1e-30)

@@ -24,14 +24,15 @@
 // instruction), and ln, sin and cos are evaluated by this file's own bounded-range
 // methods instead of the general-range library functions:
 //   -2 ln u, u in (0, 1]: u = m 2^e with m in [sqrt(1/2), sqrt(2)), ln m =
-//      2 atanh(s) with s = (m-1)/(m+1), |s| <= 0.1716, by its odd power series
-//      through s^7 (truncation below 9e-8 relative, 4e-8 relative in z);
+//      2 atanh(s) with s = (m-1)/(m+1), |s| <= 0.1716, atanh(s)/s as a quadratic in
+//      s^2 (4.7e-7 relative);
 //   cos, sin of theta in [0, 2pi]: Cody-Waite reduction r = theta - j pi/2 with a
-//      two-term pi/2 (j <= 4), Taylor series of sin through r^9 and of cos through
-//      r^8 on |r| <= pi/4 (truncation below 2e-9 and 2.5e-8), then the quadrant's
-//      swap and signs.
+//      two-term pi/2 (j <= 4), odd degree-7 and even degree-6 polynomials on
+//      |r| <= pi/4 (1e-8 and 3.3e-8 absolute), then the quadrant's swap and signs.
+// The polynomial coefficients are this file's own near-minimax fits (weighted
+// least squares on Chebyshev nodes, reweighted toward the largest error).
 // Against the reference formula evaluated with glibc's float functions the
-// result stays within 5e-7 absolute (scaled by max(1, |z|)).
+// result stays within 1e-6 absolute (scaled by max(1, |z|)).
 // The kernels are bound by the heavy FMA pipe, not by issue or memory: each
 // Philox round's two 32x32->64 multiplies hold it for 4 cycles per warp each,
 // and every packed fp32 instruction for 2.
@@ -151,10 +152,13 @@ constexpr unsigned kPackLog = 2u;    // -2 ln u
 constexpr unsigned kPackTrig = 4u;   // reduction and sin/cos polynomials
 constexpr unsigned kPackOut = 8u;    // radius products and the affine step
 
-// (float(u) + 1.0f) * 2^-32 for two words, each step rounded separately.
+// (float(u) + 1.0f) * 2^-32 for two words.  Evaluated as fma(float(u), 2^-32, 2^-32):
+// scaling by a power of two commutes with rounding (no underflow: the sum is at
+// least 1), so the single rounding of the fma equals the reference's rounded add
+// followed by its exact multiply, bit for bit.
 template <bool P>
 __device__ __forceinline__ Pair to_uniform2(std::uint32_t a, std::uint32_t b) {
-  return mul<P>(add<P>({__uint2float_rn(a), __uint2float_rn(b)}, splat(1.0f)),
+  return fma<P>({__uint2float_rn(a), __uint2float_rn(b)}, splat(2.3283064365386963e-10f),
                 splat(2.3283064365386963e-10f));
 }
 
@@ -177,8 +181,9 @@ __device__ __forceinline__ Pair neg2_log(Pair u) {
   const Pair den = add<P>(m, splat(1.0f));
   const Pair s = mul<P>(num, {rcp_approx(den.x), rcp_approx(den.y)});
   const Pair z = mul<P>(s, s);
-  Pair q = fma<P>(splat(-4.0f / 7.0f), z, splat(-4.0f / 5.0f));
-  q = fma<P>(q, z, splat(-4.0f / 3.0f));
+  // atanh(s)/s = 1 + z (c1 + c2 z) on z <= 0.02944 (near-minimax fit of this file's
+  // own, 4.7e-7 relative error), times -4 so that -2 ln m = s (-4 + z q)
+  const Pair q = fma<P>(splat(-4.0f * 0.20429936f), z, splat(-4.0f * 0.33331743f));
   const Pair lnm = mul<P>(s, fma<P>(z, q, splat(-4.0f)));  // -2 ln m
   return fma<P>(e, splat(-1.38629436111989061883f), lnm);  // -2 ln 2 (exactly twice float ln 2)
 }
@@ -192,14 +197,14 @@ __device__ __forceinline__ void polar2(Pair theta, Pair r, Pair& zc, Pair& zs) {
   const Pair j = add<PT>(magic, splat(-kRound));
   Pair x = fma<PT>(j, splat(-1.57079637050628662109375f), theta);  // float(pi/2)
   x = fma<PT>(j, splat(4.37113900018624283e-8f), x);               // pi/2 - float(pi/2), negated
+  // near-minimax odd / even polynomials on |x| <= pi/4 (fits of this file's own:
+  // sin 1e-8, cos 3.3e-8 absolute error)
   const Pair x2 = mul<PT>(x, x);
-  Pair p = fma<PT>(splat(1.0f / 362880.0f), x2, splat(-1.0f / 5040.0f));
-  p = fma<PT>(p, x2, splat(1.0f / 120.0f));
-  p = fma<PT>(p, x2, splat(-1.0f / 6.0f));
+  Pair p = fma<PT>(splat(-1.958967769e-4f), x2, splat(8.332764730e-3f));
+  p = fma<PT>(p, x2, splat(-1.666666567e-1f));
   const Pair sn = fma<PT>(mul<PT>(x, x2), p, x);
-  Pair c = fma<PT>(splat(1.0f / 40320.0f), x2, splat(-1.0f / 720.0f));
-  c = fma<PT>(c, x2, splat(1.0f / 24.0f));
-  c = fma<PT>(c, x2, splat(-0.5f));
+  Pair c = fma<PT>(splat(-1.359708956e-3f), x2, splat(4.165624082e-2f));
+  c = fma<PT>(c, x2, splat(-4.999989271e-1f));
   const Pair cs = fma<PT>(c, x2, splat(1.0f));
   // quadrant j (low bits of the rounded sum): cos = [c, -s, -c, s][j & 3],
   // sin = [s, c, -s, -c][j & 3]

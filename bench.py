@@ -421,7 +421,7 @@ def suite_spmv(s: Suite) -> dict:
            "config": f"{rows} rows, nnz {nnz} ({nnz / rows:.2f}/row), power law k^-2 on "
                      "[2.2, 4096], L2 flushed before each call",
            "reference_formula_gbs": (nnz * 8 + 2 * rows * 4) / (ms * 1e-3) / 1e9,
-           "roofline": s.roof("spmv_csr_tiles<8>", gbs, "hbm"), "launches": launches,
+           "roofline": s.roof("spmv_csr_tiles<4>", gbs, "hbm"), "launches": launches,
            "algorithmic_bytes_per_launch": alg_bytes}
     if s.cpu:
         import oracle

@@ -478,6 +478,45 @@ inline bool encode_tiled(CUtensorMap* map, int fmt, const void* base, int rank,
          CUDA_SUCCESS;
 }
 
+using EncodeIm2colFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                    const cuuint64_t*, const cuuint64_t*, const int*, const int*,
+                                    cuuint32_t, cuuint32_t, const cuuint32_t*,
+                                    CUtensorMapInterleave, CUtensorMapSwizzle,
+                                    CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+inline EncodeIm2colFn encode_im2col_fn() {
+  static EncodeIm2colFn fn = [] {
+    void* q = nullptr;
+    cudaDriverEntryPointQueryResult r{};
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeIm2col", &q, cudaEnableDefault, &r) !=
+            cudaSuccess ||
+        r != cudaDriverEntryPointSuccess)
+      return static_cast<EncodeIm2colFn>(nullptr);
+    return reinterpret_cast<EncodeIm2colFn>(q);
+  }();
+  return fn;
+}
+
+// im2col map over a (c, w, h, [d,] n) tensor of `rank` dims: the box is
+// `pixels` base pixels x `channels` channels, the spatial bounding box of the base
+// pixels runs from `lower` to dim - 1 + `upper` in each of the rank - 2 spatial
+// dimensions (w first), traversal stride 1, 128-byte swizzle, zero fill.
+inline bool encode_im2col(CUtensorMap* map, int fmt, const void* base, int rank,
+                          const cuuint64_t* dims, const cuuint64_t* strides_bytes,
+                          const int* lower, const int* upper, cuuint32_t channels,
+                          cuuint32_t pixels) {
+  EncodeIm2colFn fn = encode_im2col_fn();
+  if (fn == nullptr) return false;
+  const cuuint32_t estr[5] = {1u, 1u, 1u, 1u, 1u};
+  const CUtensorMapDataType dt = fmt == 2   ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                                 : fmt == 1 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                            : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  return fn(map, dt, static_cast<cuuint32_t>(rank), const_cast<void*>(base), dims,
+            strides_bytes, lower, upper, channels, pixels, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+            CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 template <class P, int BN, int STAGES, int FMT>
 cudaError_t launch_tc_gemm(const P& p, int sms, unsigned int* timeouts, cudaStream_t stream) {
   constexpr bool split = FMT == kFmtTf32x3;

@@ -102,6 +102,36 @@ __device__ __forceinline__ void tma_load_5d(void* dst, const CUtensorMap* map, s
       : "memory");
 }
 
+// im2col TMA loads: the box is `pixels per column` consecutive base pixels of an
+// NHWC (or NHWC-plus-plane) tensor, walked w fastest inside the tensor map's
+// bounding box, then h, then the outer dimensions; each pixel contributes the
+// map's channels-per-pixel channels read at (w + off_w, h + off_h), zero outside
+// the tensor.  (c, w, h, ...) is the first base pixel; c must be 16-byte aligned.
+__device__ __forceinline__ void tma_load_im2col_4d(void* dst, const CUtensorMap* map,
+                                                   std::int32_t c, std::int32_t w, std::int32_t h,
+                                                   std::int32_t n, std::uint16_t off_w,
+                                                   std::uint16_t off_h, std::uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.im2col.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3, %4, %5}], [%6], {%7, %8};" ::"r"(smem_addr(dst)),
+      "l"(reinterpret_cast<std::uint64_t>(map)), "r"(c), "r"(w), "r"(h), "r"(n),
+      "r"(smem_addr(bar)), "h"(off_w), "h"(off_h)
+      : "memory");
+}
+
+__device__ __forceinline__ void tma_load_im2col_5d(void* dst, const CUtensorMap* map,
+                                                   std::int32_t c, std::int32_t w, std::int32_t h,
+                                                   std::int32_t d, std::int32_t n,
+                                                   std::uint16_t off_w, std::uint16_t off_h,
+                                                   std::uint16_t off_d, std::uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.5d.shared::cluster.global.im2col.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3, %4, %5, %6}], [%7], {%8, %9, %10};" ::"r"(smem_addr(dst)),
+      "l"(reinterpret_cast<std::uint64_t>(map)), "r"(c), "r"(w), "r"(h), "r"(d), "r"(n),
+      "r"(smem_addr(bar)), "h"(off_w), "h"(off_h), "h"(off_d)
+      : "memory");
+}
+
 // Untiled bulk copies (16-byte aligned addresses, size a multiple of 16).
 __device__ __forceinline__ void bulk_load(void* dst_smem, const void* src, std::uint32_t bytes,
                                           std::uint64_t* bar) {

@@ -5,25 +5,27 @@
 // (N) and (r, s, c) as the reduction, both operands contiguous in c (K-major).
 // It runs on the persistent tcgen05 main loop of tc_gemm_core.cuh; only the
 // loads and the epilogue are specific:
-//   - the 128 rows of an output tile are a rectangle of HB x WB output pixels of one
-//     image (WB = 64 for 56-pixel rows), and for reduction block (r, s, c0) the
-//     producer loads the matching input rectangle, shifted by the tap, with one 4-D
-//     TMA box {64 channels, WB, HB, 1} of the NHWC input: out-of-image coordinates
-//     (the zero padding) come back as zeros from the TMA unit itself, no index math
-//     or predication in the main loop;
+//   - the 128 rows of an output tile are 128 consecutive output pixels in NHW order
+//     (crossing row and image boundaries), loaded for reduction block (r, s, c0) by
+//     one im2col-mode TMA load: the tensor map's bounding box makes the base pixels
+//     walk the P x Q output positions (corners -pad and pad - (S-1)*dil), the load's
+//     im2col offsets (s*dil, r*dil) pick the tap, and input positions outside the
+//     image (the zero padding) come back as zeros from the TMA unit, with no index
+//     math or predication in the main loop and no padded rows in the tile;
 //   - the weight block is a {64, 256} box of the KRSC filter viewed as a
 //     (R*S*C) x K matrix; CUDNN_CONVOLUTION (flipped filter) just selects the
 //     mirrored tap;
-//   - the epilogue writes each pixel's 32-channel chunk as 64 contiguous bytes of
-//     the NHWC output and skips the rows of the rectangle outside the image.
+//   - the epilogue writes tile row r to output pixel m0 + r, i.e. the contiguous
+//     channels at y + (m0 + r) * K of the packed NHWC output.
 // Arithmetic: products accumulated in fp32, then y = fma(alpha, acc, beta == 0 ?
 // 0 : beta * y) (the reference's direct kernel, cudnn_kernels.metal:20-62).  bf16
 // tensors are this library's extension.  fp32 tensors (the reference's only
 // type: libraries/dnn/src/cudnn_ops.mm:134-137) run in split-tf32 form: one pass
 // writes x and w as hi/lo tf32 planes (x stays NHWC, a KRSC or KCRS filter becomes
-// KRSC) into the handle's workspace, the input box gains a plane dimension (5-D
-// TMA), k-blocks are 32 channels, and each K step issues lo*hi + hi*lo + hi*hi
-// (within 1.5 * 2^-20 relative per product, fp32-class accuracy).
+// KRSC) into the handle's workspace; the x planes form a 5-D tensor (c, w, h, image,
+// plane) loaded with two 5-D im2col loads per k-block (hi, lo), k-blocks are 32
+// channels, and each K step issues lo*hi + hi*lo + hi*hi (within 1.5 * 2^-20
+// relative per product, fp32-class accuracy).
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
@@ -50,19 +52,18 @@ __device__ unsigned int g_conv_tc_timeouts;
 
 template <typename T, int FMT>
 struct ConvProblem {
-  static constexpr int KB = FMT == tc::kFmtTf32x3 ? tc::kBK32 : tc::kBK;  // channels per block
-  // NHWC input: dims (c, w, h, n), box {KB, WB, HB, 1}; split tf32 adds the plane
-  // dimension (c, w, h, n, plane) with a box of both planes
+  static constexpr bool kSplit = FMT == tc::kFmtTf32x3;
+  static constexpr int KB = kSplit ? tc::kBK32 : tc::kBK;  // channels per k-block
+  // im2col map of the NHWC input (c, w, h, n); split tf32: of the planes
+  // (c, w, h, n, plane) with the images as the third spatial dimension
   CUtensorMap mx;
   CUtensorMap mw;  // KRSC filter as (R*S*C) x K (x plane): dims (rsc, k, planes), box {KB, BN, planes}
   long long tiles_total;
+  int pixels;  // output pixels N * P * Q (below 2^31)
   int num_kb;
-  int P, Q, K, C;
-  int HB, WB, tiles_p, tiles_q, tiles_k;
-  int cblocks, R, S;
+  int P, Q, K, C, R, S, cblocks, tiles_k;
   int pad_h, pad_w, dil_h, dil_w, flip;
-  T* y;
-  long long y_ns, y_hs, y_ws;
+  T* y;  // packed NHWC: output pixel m at y + m * K
   float alpha, beta;
 
   __device__ void prefetch() const {
@@ -70,14 +71,12 @@ struct ConvProblem {
     tc::prefetch_tensormap(&mw);
   }
 
-  // (image, pixel rectangle, output-channel block); the channel block varies
-  // fastest so tiles that read the same input rectangle run together.
+  // (128-pixel tile, -, output-channel block); the channel block varies fastest so
+  // the tiles that read the same input pixels run together.
   __device__ void coords(long long t, int (&c3)[3]) const {
-    const long long per_img = static_cast<long long>(tiles_p) * tiles_q * tiles_k;
-    c3[0] = static_cast<int>(t / per_img);
-    const int rem = static_cast<int>(t % per_img);
-    c3[1] = rem / tiles_k;
-    c3[2] = rem % tiles_k;
+    c3[0] = static_cast<int>(t / tiles_k);
+    c3[1] = 0;
+    c3[2] = static_cast<int>(t % tiles_k);
   }
 
   __device__ void load(const int (&c3)[3], int kb, void* sa, void* sb, std::uint64_t* bar) const {
@@ -85,15 +84,25 @@ struct ConvProblem {
     const int cb = kb % cblocks;
     const int r = rs / S;
     const int s = rs % S;
-    const int tp = c3[1] / tiles_q;
-    const int tq = c3[1] % tiles_q;
     const int fr = flip ? R - 1 - r : r;
     const int fs = flip ? S - 1 - s : s;
-    const int xw = tq * WB + s * dil_w - pad_w, xh = tp * HB + r * dil_h - pad_h;
-    if constexpr (FMT == tc::kFmtTf32x3)
-      tc::tma_load_5d(sa, &mx, cb * KB, xw, xh, c3[0], 0, bar);
-    else
-      tc::tma_load_4d(sa, &mx, cb * KB, xw, xh, c3[0], bar);
+    // first base pixel of the tile: output pixel m0 = (n, p, q) -> (q - pad, p - pad, n)
+    const int m0 = c3[0] * tc::kBM;
+    const int pq = P * Q;
+    const int n = m0 / pq;
+    const int rem = m0 - n * pq;
+    const int bh = rem / Q - pad_h;
+    const int bw = rem % Q - pad_w;
+    const auto ow = static_cast<std::uint16_t>(s * dil_w);
+    const auto oh = static_cast<std::uint16_t>(r * dil_h);
+    if constexpr (kSplit) {
+      constexpr int plane = tc::kBM * tc::kRowBytes;
+      std::uint8_t* a = static_cast<std::uint8_t*>(sa);
+      tc::tma_load_im2col_5d(a, &mx, cb * KB, bw, bh, n, 0, ow, oh, 0, bar);          // hi
+      tc::tma_load_im2col_5d(a + plane, &mx, cb * KB, bw, bh, n, 1, ow, oh, 0, bar);  // lo
+    } else {
+      tc::tma_load_im2col_4d(sa, &mx, cb * KB, bw, bh, n, ow, oh, bar);
+    }
     tc::tma_load_3d(sb, &mw, (fr * S + fs) * C + cb * KB, c3[2] * BN, 0, bar);
   }
 
@@ -104,13 +113,10 @@ struct ConvProblem {
 
   __device__ void store(const int (&c3)[3], int row, int col0, const float (&v)[32], float a,
                         float b) const {
-    const int tp = c3[1] / tiles_q;
-    const int tq = c3[1] % tiles_q;
-    const int p = tp * HB + row / WB;
-    const int q = tq * WB + row % WB;
-    if (p >= P || q >= Q) return;
+    const int m = c3[0] * tc::kBM + row;
+    if (m >= pixels) return;
     const int k0 = c3[2] * BN + col0;
-    T* out = y + c3[0] * y_ns + p * y_hs + q * y_ws + k0;
+    T* out = y + static_cast<long long>(m) * K + k0;
     if (k0 + 32 <= K && b == 0.0f) {
       // 32 channels = 32 * sizeof(T) contiguous bytes, as 16-byte stores
       constexpr int E = 16 / static_cast<int>(sizeof(T));
@@ -174,14 +180,19 @@ bool packed_nhwc(const View4& v) {
          v.ns == static_cast<std::int64_t>(v.h) * v.w * v.c;
 }
 
-int pow2_at_least(int v, int lo, int hi) {
-  int p = lo;
-  while (p < v && p < hi) p <<= 1;
-  return p;
+// The im2col tensor map holds the base-pixel bounding box corners and the load
+// offsets in narrow fields: 4-D maps take corners in [-128, 127] and offsets up to
+// 255, 5-D maps [-16, 15] and 31.
+bool im2col_ok(const ConvShape& s, int rank) {
+  const int lo = rank == 4 ? -128 : -16, hi = rank == 4 ? 127 : 15, omax = rank == 4 ? 255 : 31;
+  const int ow = (s.kw - 1) * s.dil_w, oh = (s.kh - 1) * s.dil_h;
+  auto in = [&](int v) { return v >= lo && v <= hi; };
+  return ow >= 0 && oh >= 0 && ow <= omax && oh <= omax && in(-s.pad_w) && in(-s.pad_h) &&
+         in(s.pad_w - ow) && in(s.pad_h - oh);
 }
 
-// Geometry shared by both formats; `x_images` is the number of images the input
-// map covers (a chunk of the batch for split tf32).
+// Geometry shared by both formats for `images` images (a chunk of the batch for
+// split tf32) whose output starts at y.
 template <typename T, int FMT>
 void fill_geometry(ConvProblem<T, FMT>& p, const ConvShape& s, void* y, int images, float alpha,
                    float beta) {
@@ -192,25 +203,29 @@ void fill_geometry(ConvProblem<T, FMT>& p, const ConvShape& s, void* y, int imag
   p.C = s.x.c;
   p.R = s.kh;
   p.S = s.kw;
-  p.WB = pow2_at_least(p.Q, 8, 64);
-  p.HB = tc::kBM / p.WB;
-  p.tiles_p = (p.P + p.HB - 1) / p.HB;
-  p.tiles_q = (p.Q + p.WB - 1) / p.WB;
   p.tiles_k = (p.K + BN - 1) / BN;
   p.cblocks = p.C / P::KB;
   p.num_kb = p.R * p.S * p.cblocks;
-  p.tiles_total = static_cast<long long>(images) * p.tiles_p * p.tiles_q * p.tiles_k;
+  p.pixels = images * p.P * p.Q;
+  p.tiles_total = (p.pixels + tc::kBM - 1) / tc::kBM * p.tiles_k;
   p.pad_h = s.pad_h;
   p.pad_w = s.pad_w;
   p.dil_h = s.dil_h;
   p.dil_w = s.dil_w;
   p.flip = s.convolution ? 1 : 0;
   p.y = static_cast<T*>(y);
-  p.y_ns = s.y.ns;
-  p.y_hs = s.y.hs;
-  p.y_ws = s.y.ws;
   p.alpha = alpha;
   p.beta = beta;
+}
+
+// Bounding box of the base pixels: from -pad to (dim - 1) + pad - (taps - 1) * dil.
+void im2col_corners(const ConvShape& s, int (&lower)[3], int (&upper)[3]) {
+  lower[0] = -s.pad_w;
+  lower[1] = -s.pad_h;
+  lower[2] = 0;
+  upper[0] = s.pad_w - (s.kw - 1) * s.dil_w;
+  upper[1] = s.pad_h - (s.kh - 1) * s.dil_h;
+  upper[2] = 0;
 }
 
 template <typename T, int FMT>
@@ -224,14 +239,14 @@ cudaError_t run16(const void* x, const void* w, void* y, const ConvShape& s, flo
   const cuuint64_t xs[3] = {static_cast<cuuint64_t>(s.x.ws * 2),
                             static_cast<cuuint64_t>(s.x.hs * 2),
                             static_cast<cuuint64_t>(s.x.ns * 2)};
-  const cuuint32_t xb[4] = {static_cast<cuuint32_t>(tc::kBK), static_cast<cuuint32_t>(p.WB),
-                            static_cast<cuuint32_t>(p.HB), 1u};
+  int lower[3], upper[3];
+  im2col_corners(s, lower, upper);
   const long long rsc = static_cast<long long>(p.R) * p.S * C;
   const cuuint64_t wd[3] = {static_cast<cuuint64_t>(rsc), static_cast<cuuint64_t>(K), 1u};
   const cuuint64_t ws[2] = {static_cast<cuuint64_t>(rsc * 2),
                             static_cast<cuuint64_t>(((rsc * K * 2 + 15) / 16) * 16)};
   const cuuint32_t wb[3] = {static_cast<cuuint32_t>(tc::kBK), static_cast<cuuint32_t>(BN), 1u};
-  if (!tc::encode_tiled(&p.mx, FMT, x, 4, xd, xs, xb) ||
+  if (!tc::encode_im2col(&p.mx, FMT, x, 4, xd, xs, lower, upper, tc::kBK, tc::kBM) ||
       !tc::encode_tiled(&p.mw, FMT, w, 3, wd, ws, wb))
     return cudaErrorNotSupported;
   unsigned int* to = timeout_counter();
@@ -260,7 +275,8 @@ Tf32Plan plan_tf32(const ConvShape& s) {
 
 bool tf32_geometry_ok(const ConvShape& s) {
   if (s.groups != 1 || s.stride_h != 1 || s.stride_w != 1) return false;
-  if (!packed_nhwc(s.x) || !packed_nhwc(s.y)) return false;
+  if (!packed_nhwc(s.x) || !packed_nhwc(s.y) || !im2col_ok(s, 5)) return false;
+  if (static_cast<long long>(s.y.n) * s.y.h * s.y.w >= (1ll << 31)) return false;
   if (s.x.c % tc::kBK32 != 0 || s.y.c % 4 != 0) return false;
   const long long total = static_cast<long long>(s.y.n) * s.y.h * s.y.w;
   return total * s.y.c * s.x.c * s.kh * s.kw >= (1ll << 24);  // smaller: direct kernel
@@ -289,14 +305,14 @@ cudaError_t run_tf32x3(const float* x, const float* w, float* y, const ConvShape
     const cuuint64_t xs[4] = {static_cast<cuuint64_t>(C) * 4, static_cast<cuuint64_t>(W) * C * 4,
                               static_cast<cuuint64_t>(H) * W * C * 4,
                               static_cast<cuuint64_t>(pixels) * C * 4};
-    const cuuint32_t xb[5] = {static_cast<cuuint32_t>(tc::kBK32), static_cast<cuuint32_t>(p.WB),
-                              static_cast<cuuint32_t>(p.HB), 1u, 2u};
+    int lower[3], upper[3];
+    im2col_corners(s, lower, upper);
     const long long rsc = static_cast<long long>(s.kh) * s.kw * C;
     const cuuint64_t wd[3] = {static_cast<cuuint64_t>(rsc), static_cast<cuuint64_t>(K), 2u};
     const cuuint64_t wst[2] = {static_cast<cuuint64_t>(rsc * 4),
                                static_cast<cuuint64_t>(rsc * K * 4)};
     const cuuint32_t wb[3] = {static_cast<cuuint32_t>(tc::kBK32), static_cast<cuuint32_t>(BN), 2u};
-    if (!tc::encode_tiled(&p.mx, 2, xp, 5, xd, xs, xb) ||
+    if (!tc::encode_im2col(&p.mx, 2, xp, 5, xd, xs, lower, upper, tc::kBK32, tc::kBM) ||
         !tc::encode_tiled(&p.mw, 2, wp, 3, wd, wst, wb))
       return cudaErrorNotSupported;
     e = tc::launch_tc_gemm<ConvProblem<float, tc::kFmtTf32x3>, BN, STAGES32, tc::kFmtTf32x3>(
@@ -313,7 +329,8 @@ bool conv_tc_supported(const ConvShape& s, ConvDtype dt, const void* x, const vo
   if (dt != ConvDtype::kBF16) return false;
   if (s.groups != 1 || s.stride_h != 1 || s.stride_w != 1) return false;
   if (!s.filter_krsc) return false;
-  if (!packed_nhwc(s.x) || !packed_nhwc(s.y)) return false;
+  if (!packed_nhwc(s.x) || !packed_nhwc(s.y) || !im2col_ok(s, 4)) return false;
+  if (static_cast<long long>(s.y.n) * s.y.h * s.y.w >= (1ll << 31)) return false;
   if (s.x.c % tc::kBK != 0 || s.y.c % 8 != 0) return false;
   if (!aligned_to(x, 16) || !aligned_to(w, 16) || !aligned_to(y, 16)) return false;
   const long long total = static_cast<long long>(s.y.n) * s.y.h * s.y.w;

@@ -605,6 +605,95 @@ def suite_conv(s: Suite, dtype: str, krsc: bool = True) -> dict:
             "roofline": s.roof(kern, tf, bound), "launches": launches}
 
 
+def _blas_handle(s):
+    from muda_b200 import capi
+    L = capi.cublas()
+    h = C.c_void_p()
+    assert L.cublasCreate_v2(C.byref(h)) == 0
+    assert L.cublasSetStream_v2(h, s.sp) == 0
+    return L, h
+
+
+def suite_level1(s: Suite, op: str) -> dict:
+    """cuBLAS level 1: saxpy / sdot on 2^28 fp32 elements (1.07 GB per
+    vector, larger than L2), uniform[-1, 1] from seed 5."""
+    from muda_b200 import synth
+    torch = s.torch
+    n = (1 << 28) // s.scale
+    x = synth.uniform_pm1(torch, n, seed=5)
+    y = synth.uniform_pm1(torch, n, seed=5, offset=(n + 3) // 4 * 4)
+    L, h = _blas_handle(s)
+    px, py = C.c_void_p(x.data_ptr()), C.c_void_p(y.data_ptr())
+    if op == "saxpy":
+        a = C.c_float(0.5)
+        fn = lambda: L.cublasSaxpy_v2(h, n, C.byref(a), px, 1, py, 1)
+        alg, kern = 12 * n, "elementwise<kAxpy, vec>"
+    else:
+        # device pointer mode keeps the timed call asynchronous (host mode waits)
+        assert L.cublasSetPointerMode_v2(h, 1) == 0
+        out = torch.zeros(1, dtype=torch.float32, device="cuda")
+        fn = lambda: L.cublasSdot_v2(h, n, px, 1, py, 1, C.c_void_p(out.data_ptr()))
+        alg, kern = 8 * n, "reduce_kernel<kDot, vec>"
+    ms, launches = s.time(fn)
+    assert L.cublasDestroy_v2(h) == 0
+    gbs = alg / (ms * 1e-3) / 1e9
+    out_d = {"value": gbs, "unit": "GB/s", "ms": ms, "dtype": "f32",
+             "config": f"n = {n}, unit stride, data {alg / 1e9:.2f} GB per call > L2",
+             "roofline": s.roof(kern, gbs, "hbm"), "launches": launches,
+             "algorithmic_bytes_per_launch": alg}
+    if s.cpu:
+        import oracle
+        xs, ys = x[: 1 << 24].cpu().numpy(), y[: 1 << 24].cpu().numpy()
+        if op == "saxpy":
+            dt = cpu_time(lambda: oracle.saxpy(1 << 24, 0.5, xs, 1, ys, 1))
+            per = 12
+        else:
+            dt = cpu_time(lambda: oracle.sreduce("dot", 1 << 24, xs, 1, ys, 1))
+            per = 8
+        out_d["cpu_baseline"] = {"value": per * (1 << 24) / dt / 1e9, "unit": "GB/s", "cores": 1,
+                                 "kind": "port",
+                                 "sample": "2^24 elements, oracle/blas12.cpp sequential loop"}
+    return out_d
+
+
+def suite_gemv(s: Suite, trans: bool) -> dict:
+    """cuBLAS level 2: sgemv on a 16384 x 16384 column-major fp32 matrix
+    (1.07 GB), alpha 1, beta 0, uniform[-1, 1] from seed 6."""
+    from muda_b200 import synth
+    torch = s.torch
+    m = n = 16384 // s.scale
+    A = synth.uniform_pm1(torch, m * n, seed=6)
+    x = synth.uniform_pm1(torch, n, seed=6, offset=(m * n + 3) // 4 * 4)
+    y = torch.zeros(m, dtype=torch.float32, device="cuda")
+    L, h = _blas_handle(s)
+    one, zero = C.c_float(1.0), C.c_float(0.0)
+    args = (h, 1 if trans else 0, m, n, C.byref(one), C.c_void_p(A.data_ptr()), m,
+            C.c_void_p(x.data_ptr()), 1, C.byref(zero), C.c_void_p(y.data_ptr()), 1)
+    ms, launches = s.time(lambda: L.cublasSgemv_v2(*args))
+    assert L.cublasDestroy_v2(h) == 0
+    alg = 4 * m * n + 4 * n + 4 * m
+    gbs = alg / (ms * 1e-3) / 1e9
+    out = {"value": gbs, "unit": "GB/s", "ms": ms, "dtype": "f32",
+           "config": f"{m} x {n}, op {'T' if trans else 'N'}, matrix {4 * m * n / 1e9:.2f} GB > L2",
+           "roofline": s.roof("gemv_t_kernel<vec>" if trans else "gemv_n_kernel", gbs, "hbm"),
+           "launches": launches, "algorithmic_bytes_per_launch": alg}
+    if s.cpu:
+        import oracle
+        rows = 2048
+        Ah = A[: rows * m].cpu().numpy() if not trans else A.cpu().numpy()
+        xh, yh = x.cpu().numpy(), np.zeros(max(m, n), np.float32)
+        if trans:
+            dt = cpu_time(lambda: oracle.sgemv(True, m, rows, 1.0, Ah, m, xh, 1, 0.0, yh, 1,
+                                               threads=os.cpu_count() or 1))
+        else:
+            dt = cpu_time(lambda: oracle.sgemv(False, m, rows, 1.0, Ah, m, xh, 1, 0.0, yh, 1,
+                                               threads=os.cpu_count() or 1))
+        out["cpu_baseline"] = {"value": 4 * m * rows / dt / 1e9, "unit": "GB/s",
+                               "cores": os.cpu_count(), "kind": "port",
+                               "sample": f"{rows} of {n} columns, oracle/blas12.cpp"}
+    return out
+
+
 SUITE = {
     "sgemm": suite_sgemm,
     "spmv": suite_spmv,
@@ -614,6 +703,10 @@ SUITE = {
     "conv_bf16": lambda s: suite_conv(s, "bf16"),
     "conv_f32": lambda s: suite_conv(s, "f32"),
     "conv_f32_kcrs": lambda s: suite_conv(s, "f32", krsc=False),
+    "saxpy": lambda s: suite_level1(s, "saxpy"),
+    "sdot": lambda s: suite_level1(s, "sdot"),
+    "sgemv_n": lambda s: suite_gemv(s, False),
+    "sgemv_t": lambda s: suite_gemv(s, True),
 }
 
 

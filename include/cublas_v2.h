@@ -86,6 +86,32 @@ cublasStatus_t cublasGetMathMode(cublasHandle_t handle, cublasMath_t* mode);
 const char* cublasGetStatusName(cublasStatus_t status);
 const char* cublasGetStatusString(cublasStatus_t status);
 
+/* Level-1 (fp32) — reference cublas_level1.mm:221-656 (kernels cublas_kernels.metal:11-495).
+   Increments follow BLAS: a negative inc walks the vector from its far end; inc = 0
+   repeats element 0.  Reductions write *result on the host (the call then waits for
+   the stream) or, in CUBLAS_POINTER_MODE_DEVICE, to device memory asynchronously. */
+cublasStatus_t cublasSaxpy_v2(cublasHandle_t handle, int n, const float* alpha, const float* x,
+                              int incx, float* y, int incy);      /* cublas_level1.mm:221 */
+cublasStatus_t cublasScopy_v2(cublasHandle_t handle, int n, const float* x, int incx, float* y,
+                              int incy);                          /* cublas_level1.mm:289 */
+cublasStatus_t cublasSscal_v2(cublasHandle_t handle, int n, const float* alpha, float* x,
+                              int incx);                          /* cublas_level1.mm:344 */
+cublasStatus_t cublasSswap_v2(cublasHandle_t handle, int n, float* x, int incx, float* y,
+                              int incy);                          /* cublas_level1.mm:407 */
+cublasStatus_t cublasSdot_v2(cublasHandle_t handle, int n, const float* x, int incx,
+                             const float* y, int incy, float* result); /* cublas_level1.mm:446 */
+cublasStatus_t cublasSnrm2_v2(cublasHandle_t handle, int n, const float* x, int incx,
+                              float* result);                     /* cublas_level1.mm:488 */
+cublasStatus_t cublasSasum_v2(cublasHandle_t handle, int n, const float* x, int incx,
+                              float* result);                     /* cublas_level1.mm:527 */
+cublasStatus_t cublasIsamax_v2(cublasHandle_t handle, int n, const float* x, int incx,
+                               int* result);                      /* cublas_level1.mm:566 */
+
+/* Level-2 (fp32) — reference cublas_level2.mm:38-133 (kernels cublas_kernels.metal:497-592) */
+cublasStatus_t cublasSgemv_v2(cublasHandle_t handle, cublasOperation_t trans, int m, int n,
+                              const float* alpha, const float* A, int lda, const float* x,
+                              int incx, const float* beta, float* y, int incy);
+
 /* Level-3 — reference cublas_level3.mm:474-617 */
 cublasStatus_t cublasSgemm_v2(cublasHandle_t handle, cublasOperation_t transa,
                               cublasOperation_t transb, int m, int n, int k, const float* alpha,
@@ -127,6 +153,15 @@ cublasStatus_t cublasGemmStridedBatchedEx(cublasHandle_t handle, cublasOperation
 #define cublasSetPointerMode cublasSetPointerMode_v2
 #define cublasGetPointerMode cublasGetPointerMode_v2
 #define cublasSgemm cublasSgemm_v2
+#define cublasSaxpy cublasSaxpy_v2
+#define cublasScopy cublasScopy_v2
+#define cublasSscal cublasSscal_v2
+#define cublasSswap cublasSswap_v2
+#define cublasSdot cublasSdot_v2
+#define cublasSnrm2 cublasSnrm2_v2
+#define cublasSasum cublasSasum_v2
+#define cublasIsamax cublasIsamax_v2
+#define cublasSgemv cublasSgemv_v2
 
 #ifdef __cplusplus
 }

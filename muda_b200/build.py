@@ -39,7 +39,7 @@ LIBS: dict[str, list[str]] = {
     "cufft": ["fft/cufft_api.cpp", "fft/stockham_kernels.cu", "fft/dft_kernels.cu",
               "fft/fft_static.cu"],
     "cublas": ["blas/cublas_api.cpp", "blas/gemm_simt_kernels.cu", "blas/gemm_tc_kernels.cu",
-               "blas/tf32_split.cu"],
+               "blas/tf32_split.cu", "blas/level12_kernels.cu"],
 }
 
 COMMON_FLAGS = ["-O3", "-std=c++17", f"-I{INCLUDE}", f"-I{CSRC}"]

@@ -240,6 +240,15 @@ CUBLAS_PROTOS = {
                                    vp, vp, i32, ll, i32], i32),
     "cublasGemmStridedBatchedEx": ([vp, i32, i32, i32, i32, i32, vp, vp, i32, i32, ll, vp, i32,
                                     i32, ll, vp, vp, i32, i32, ll, i32, i32, i32], i32),
+    "cublasSaxpy_v2": ([vp, i32, vp, vp, i32, vp, i32], i32),
+    "cublasScopy_v2": ([vp, i32, vp, i32, vp, i32], i32),
+    "cublasSscal_v2": ([vp, i32, vp, vp, i32], i32),
+    "cublasSswap_v2": ([vp, i32, vp, i32, vp, i32], i32),
+    "cublasSdot_v2": ([vp, i32, vp, i32, vp, i32, vp], i32),
+    "cublasSnrm2_v2": ([vp, i32, vp, i32, vp], i32),
+    "cublasSasum_v2": ([vp, i32, vp, i32, vp], i32),
+    "cublasIsamax_v2": ([vp, i32, vp, i32, vp], i32),
+    "cublasSgemv_v2": ([vp, i32, i32, i32, vp, vp, i32, vp, i32, vp, vp, i32], i32),
 }
 
 

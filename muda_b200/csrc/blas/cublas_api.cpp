@@ -27,6 +27,7 @@
 #include <mutex>
 
 #include "blas/gemm.hpp"
+#include "blas/level12.hpp"
 #include "common/device.hpp"
 #include "common/lru.hpp"
 #include "common/registry.hpp"
@@ -45,12 +46,79 @@ struct BlasContext {
   cublasMath_t math_mode = CUBLAS_DEFAULT_MATH;
   // split-tf32 workspace: held under ws_mu for the whole call that uses it
   std::mutex ws_mu;
-  std::shared_ptr<mb200::DeviceBuffer> ws;
-  cudaEvent_t ws_done = nullptr;  // recorded after the last call that used ws
+  std::shared_ptr<mb200::DeviceBuffer> ws;   // split-tf32 planes, gemv partial sums
+  std::shared_ptr<mb200::DeviceBuffer> red;  // reduction scratch + result slot (zeroed once)
+  cudaEvent_t ws_done = nullptr;  // recorded after the last call that used ws or red
 
   ~BlasContext() {
     if (ws_done != nullptr) (void)cudaEventDestroy(ws_done);
   }
+};
+
+// One call's use of the handle's device buffers: holds ws_mu for the call, orders
+// the stream after the previous such call (an event, skipped while the stream is
+// being captured into a graph) and records this call in done().
+class BufferUse {
+ public:
+  BufferUse(BlasContext& ctx, cudaStream_t stream) : lk_(ctx.ws_mu), ctx_(ctx), stream_(stream) {
+    cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+    if (cudaStreamIsCapturing(stream, &cap) != cudaSuccess) cap = cudaStreamCaptureStatusNone;
+    ordered_ = cap == cudaStreamCaptureStatusNone;
+    if (ordered_ && ctx.ws_done != nullptr)
+      ok_ = cudaStreamWaitEvent(stream, ctx.ws_done, 0) == cudaSuccess;
+  }
+  BufferUse(const BufferUse&) = delete;
+  BufferUse& operator=(const BufferUse&) = delete;
+
+  bool ok() const { return ok_; }
+
+  // The workspace, grown to `need` bytes (null when it cannot be had).
+  void* workspace(std::size_t need) {
+    const int dev = mb200::current_device();
+    if (!ctx_.ws || ctx_.ws->bytes < need || ctx_.ws->device != dev) {
+      ctx_.ws.reset();
+      ctx_.ws = mb200::DeviceBuffer::make(need);
+    }
+    return ctx_.ws ? ctx_.ws->ptr : nullptr;
+  }
+  std::size_t workspace_bytes() const { return ctx_.ws ? ctx_.ws->bytes : 0; }
+
+  // The reduction scratch (zero-filled on the stream when first allocated) and the
+  // 16-byte result slot after it.
+  void* reduction_scratch() {
+    const int dev = mb200::current_device();
+    if (!ctx_.red || ctx_.red->device != dev) {
+      ctx_.red = mb200::DeviceBuffer::make(kSlot + 16);
+      if (!ctx_.red) return nullptr;
+      if (cudaMemsetAsync(ctx_.red->ptr, 0, kSlot + 16, stream_) != cudaSuccess) {
+        ctx_.red.reset();
+        return nullptr;
+      }
+    }
+    return ctx_.red->ptr;
+  }
+  void* result_slot() { return static_cast<char*>(reduction_scratch()) + kSlot; }
+
+  cudaError_t done() {
+    if (!ordered_) return cudaSuccess;
+    if (ctx_.ws_done == nullptr &&
+        cudaEventCreateWithFlags(&ctx_.ws_done, cudaEventDisableTiming) != cudaSuccess) {
+      ctx_.ws_done = nullptr;
+      return cudaErrorUnknown;
+    }
+    return cudaEventRecord(ctx_.ws_done, stream_);
+  }
+
+ private:
+  static std::size_t slot_offset() {
+    return (mb200::blas::reduce_scratch_bytes() + 255) / 256 * 256;
+  }
+  const std::size_t kSlot = slot_offset();
+  std::lock_guard<std::mutex> lk_;
+  BlasContext& ctx_;
+  cudaStream_t stream_;
+  bool ordered_ = true;
+  bool ok_ = true;
 };
 
 // fp32 GEMM on the tensor cores with the handle's workspace; cudaErrorNotSupported
@@ -58,26 +126,13 @@ struct BlasContext {
 cudaError_t run_tf32x3(BlasContext& ctx, const GemmArgs& g, cudaStream_t stream) {
   const std::size_t need = mb200::blas::gemm_tf32x3_workspace(g);
   if (need == 0) return cudaErrorNotSupported;
-  std::lock_guard<std::mutex> lk(ctx.ws_mu);
-  const int dev = mb200::current_device();
-  if (!ctx.ws || ctx.ws->bytes < need || ctx.ws->device != dev) {
-    ctx.ws.reset();
-    ctx.ws = mb200::DeviceBuffer::make(need);
-    if (!ctx.ws) return cudaErrorNotSupported;
-  }
-  cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
-  if (cudaStreamIsCapturing(stream, &cap) != cudaSuccess) cap = cudaStreamCaptureStatusNone;
-  const bool ordered = cap == cudaStreamCaptureStatusNone;
-  if (ordered && ctx.ws_done != nullptr && cudaStreamWaitEvent(stream, ctx.ws_done, 0) != cudaSuccess)
-    return cudaErrorUnknown;
-  const cudaError_t e = mb200::blas::launch_gemm_tf32x3(g, ctx.ws->ptr, ctx.ws->bytes, stream);
-  if (e != cudaSuccess || !ordered) return e;
-  if (ctx.ws_done == nullptr &&
-      cudaEventCreateWithFlags(&ctx.ws_done, cudaEventDisableTiming) != cudaSuccess) {
-    ctx.ws_done = nullptr;
-    return cudaErrorUnknown;
-  }
-  return cudaEventRecord(ctx.ws_done, stream);
+  BufferUse use(ctx, stream);
+  if (!use.ok()) return cudaErrorUnknown;
+  void* ws = use.workspace(need);
+  if (ws == nullptr) return cudaErrorNotSupported;
+  const cudaError_t e = mb200::blas::launch_gemm_tf32x3(g, ws, use.workspace_bytes(), stream);
+  if (e != cudaSuccess) return e;
+  return use.done();
 }
 
 using HandleTable = mb200::Registry<BlasContext, mb200::ObjKind::kBlasHandle>;
@@ -221,6 +276,76 @@ cublasStatus_t run_gemm(BlasContext& ctx, Elem type, cublasOperation_t ta, cubla
     e = mb200::blas::launch_gemm_simt(g, stream);
   }
   return e == cudaSuccess ? CUBLAS_STATUS_SUCCESS : CUBLAS_STATUS_EXECUTION_FAILED;
+}
+
+// Elements a vector of n entries with increment inc spans (reference
+// cublas_level1.mm:48-54): inc = 0 touches one element.
+std::size_t span_elems(int n, int inc) {
+  if (n <= 0) return 0;
+  const std::size_t a = inc == 0 ? 1u : static_cast<std::size_t>(inc > 0 ? inc : -inc);
+  return 1u + static_cast<std::size_t>(n - 1) * a;
+}
+
+bool vec_ok(const float* p, int n, int inc) {
+  return mb200::device_span_ok(p, span_elems(n, inc) * sizeof(float)) &&
+         mb200::aligned_to(p, sizeof(float));
+}
+
+// The handle's stream and pointer mode.
+void snapshot(BlasContext& ctx, cudaStream_t* stream, cublasPointerMode_t* mode) {
+  std::lock_guard<std::mutex> g(ctx.mu);
+  *stream = ctx.stream;
+  *mode = ctx.pointer_mode;
+}
+
+// A scalar argument: its host value, or (device pointer mode) a checked device
+// pointer the kernel reads.
+bool scalar(cublasPointerMode_t mode, const float* p, float* host, const float** dev) {
+  if (mode == CUBLAS_POINTER_MODE_DEVICE) {
+    if (!mb200::device_span_ok(p, sizeof(float))) return false;
+    *dev = p;
+    *host = 0.0f;
+  } else {
+    *host = *p;
+    *dev = nullptr;
+  }
+  return true;
+}
+
+cublasStatus_t status_of(cudaError_t e) {
+  return e == cudaSuccess ? CUBLAS_STATUS_SUCCESS : CUBLAS_STATUS_EXECUTION_FAILED;
+}
+
+// Runs a reduction and delivers its result: in device pointer mode the kernel
+// writes `result` (device memory) directly; in host mode it writes the handle's
+// result slot, copied to `result` after the stream finishes (the reference
+// synchronises the same way, cublas_level1.mm:119-126).
+template <typename T>
+cublasStatus_t run_reduction(BlasContext& ctx, mb200::blas::Reduce op, int n, const float* x,
+                             int incx, const float* y, int incy, T* result) {
+  cudaStream_t stream;
+  cublasPointerMode_t mode;
+  snapshot(ctx, &stream, &mode);
+  if (mode == CUBLAS_POINTER_MODE_DEVICE && !mb200::device_span_ok(result, sizeof(T)))
+    return CUBLAS_STATUS_INVALID_VALUE;
+  const bool empty = n <= 0 || (op != mb200::blas::Reduce::kDot && incx <= 0);
+  if (empty && mode == CUBLAS_POINTER_MODE_HOST) {
+    *result = T{};
+    return CUBLAS_STATUS_SUCCESS;
+  }
+  if (!empty && (!vec_ok(x, n, incx) || (op == mb200::blas::Reduce::kDot && !vec_ok(y, n, incy))))
+    return CUBLAS_STATUS_INVALID_VALUE;
+  BufferUse use(ctx, stream);
+  if (!use.ok()) return CUBLAS_STATUS_EXECUTION_FAILED;
+  void* scratch = use.reduction_scratch();
+  if (scratch == nullptr) return CUBLAS_STATUS_ALLOC_FAILED;
+  void* out = mode == CUBLAS_POINTER_MODE_DEVICE ? static_cast<void*>(result) : use.result_slot();
+  cudaError_t e = mb200::blas::launch_reduce(op, n, x, incx, y, incy, out, scratch, stream);
+  if (e == cudaSuccess && mode == CUBLAS_POINTER_MODE_HOST)
+    e = cudaMemcpyAsync(result, out, sizeof(T), cudaMemcpyDeviceToHost, stream);
+  if (e == cudaSuccess) e = use.done();
+  if (e == cudaSuccess && mode == CUBLAS_POINTER_MODE_HOST) e = cudaStreamSynchronize(stream);
+  return status_of(e);
 }
 
 }  // namespace
@@ -393,6 +518,133 @@ cublasStatus_t cublasGemmEx(cublasHandle_t handle, cublasOperation_t transa,
                             cudaDataType Ctype, int ldc, int computeType, cublasGemmAlgo_t algo) {
   return cublasGemmStridedBatchedEx(handle, transa, transb, m, n, k, alpha, A, Atype, lda, 0, B,
                                     Btype, ldb, 0, beta, C, Ctype, ldc, 0, 1, computeType, algo);
+}
+
+// ---------------------------------------------------------------- level 1
+cublasStatus_t cublasSaxpy_v2(cublasHandle_t handle, int n, const float* alpha, const float* x,
+                              int incx, float* y, int incy) {
+  auto h = handles().get(handle);
+  if (!h) return CUBLAS_STATUS_NOT_INITIALIZED;
+  if (alpha == nullptr) return CUBLAS_STATUS_INVALID_VALUE;
+  if (n <= 0) return CUBLAS_STATUS_SUCCESS;
+  cudaStream_t stream;
+  cublasPointerMode_t mode;
+  snapshot(*h, &stream, &mode);
+  float a;
+  const float* a_dev;
+  if (!scalar(mode, alpha, &a, &a_dev)) return CUBLAS_STATUS_INVALID_VALUE;
+  if (a_dev == nullptr && a == 0.0f) return CUBLAS_STATUS_SUCCESS;
+  if (!vec_ok(x, n, incx) || !vec_ok(y, n, incy)) return CUBLAS_STATUS_INVALID_VALUE;
+  return status_of(mb200::blas::launch_saxpy(n, a, a_dev, x, incx, y, incy, stream));
+}
+
+cublasStatus_t cublasScopy_v2(cublasHandle_t handle, int n, const float* x, int incx, float* y,
+                              int incy) {
+  auto h = handles().get(handle);
+  if (!h) return CUBLAS_STATUS_NOT_INITIALIZED;
+  if (n <= 0) return CUBLAS_STATUS_SUCCESS;
+  if (!vec_ok(x, n, incx) || !vec_ok(y, n, incy)) return CUBLAS_STATUS_INVALID_VALUE;
+  cudaStream_t stream;
+  cublasPointerMode_t mode;
+  snapshot(*h, &stream, &mode);
+  return status_of(mb200::blas::launch_scopy(n, x, incx, y, incy, stream));
+}
+
+cublasStatus_t cublasSscal_v2(cublasHandle_t handle, int n, const float* alpha, float* x,
+                              int incx) {
+  auto h = handles().get(handle);
+  if (!h) return CUBLAS_STATUS_NOT_INITIALIZED;
+  if (alpha == nullptr) return CUBLAS_STATUS_INVALID_VALUE;
+  if (n <= 0 || incx <= 0) return CUBLAS_STATUS_SUCCESS;
+  cudaStream_t stream;
+  cublasPointerMode_t mode;
+  snapshot(*h, &stream, &mode);
+  float a;
+  const float* a_dev;
+  if (!scalar(mode, alpha, &a, &a_dev)) return CUBLAS_STATUS_INVALID_VALUE;
+  if (!vec_ok(x, n, incx)) return CUBLAS_STATUS_INVALID_VALUE;
+  return status_of(mb200::blas::launch_sscal(n, a, a_dev, x, incx, stream));
+}
+
+cublasStatus_t cublasSswap_v2(cublasHandle_t handle, int n, float* x, int incx, float* y,
+                              int incy) {
+  auto h = handles().get(handle);
+  if (!h) return CUBLAS_STATUS_NOT_INITIALIZED;
+  if (n <= 0) return CUBLAS_STATUS_SUCCESS;
+  if (!vec_ok(x, n, incx) || !vec_ok(y, n, incy)) return CUBLAS_STATUS_INVALID_VALUE;
+  cudaStream_t stream;
+  cublasPointerMode_t mode;
+  snapshot(*h, &stream, &mode);
+  return status_of(mb200::blas::launch_sswap(n, x, incx, y, incy, stream));
+}
+
+cublasStatus_t cublasSdot_v2(cublasHandle_t handle, int n, const float* x, int incx,
+                             const float* y, int incy, float* result) {
+  auto h = handles().get(handle);
+  if (!h) return CUBLAS_STATUS_NOT_INITIALIZED;
+  if (result == nullptr) return CUBLAS_STATUS_INVALID_VALUE;
+  return run_reduction(*h, mb200::blas::Reduce::kDot, n, x, incx, y, incy, result);
+}
+
+cublasStatus_t cublasSnrm2_v2(cublasHandle_t handle, int n, const float* x, int incx,
+                              float* result) {
+  auto h = handles().get(handle);
+  if (!h) return CUBLAS_STATUS_NOT_INITIALIZED;
+  if (result == nullptr) return CUBLAS_STATUS_INVALID_VALUE;
+  return run_reduction(*h, mb200::blas::Reduce::kNrm2, n, x, incx, nullptr, 0, result);
+}
+
+cublasStatus_t cublasSasum_v2(cublasHandle_t handle, int n, const float* x, int incx,
+                              float* result) {
+  auto h = handles().get(handle);
+  if (!h) return CUBLAS_STATUS_NOT_INITIALIZED;
+  if (result == nullptr) return CUBLAS_STATUS_INVALID_VALUE;
+  return run_reduction(*h, mb200::blas::Reduce::kAsum, n, x, incx, nullptr, 0, result);
+}
+
+cublasStatus_t cublasIsamax_v2(cublasHandle_t handle, int n, const float* x, int incx,
+                               int* result) {
+  auto h = handles().get(handle);
+  if (!h) return CUBLAS_STATUS_NOT_INITIALIZED;
+  if (result == nullptr) return CUBLAS_STATUS_INVALID_VALUE;
+  return run_reduction(*h, mb200::blas::Reduce::kAmax, n, x, incx, nullptr, 0, result);
+}
+
+// ---------------------------------------------------------------- level 2
+cublasStatus_t cublasSgemv_v2(cublasHandle_t handle, cublasOperation_t trans, int m, int n,
+                              const float* alpha, const float* A, int lda, const float* x,
+                              int incx, const float* beta, float* y, int incy) {
+  auto h = handles().get(handle);
+  if (!h) return CUBLAS_STATUS_NOT_INITIALIZED;
+  // cublas_level2.mm:45-48
+  if (!valid_op(trans) || m < 0 || n < 0 || lda < (m > 1 ? m : 1) || incx == 0 || incy == 0 ||
+      alpha == nullptr || beta == nullptr)
+    return CUBLAS_STATUS_INVALID_VALUE;
+  if (m == 0 || n == 0) return CUBLAS_STATUS_SUCCESS;
+  cudaStream_t stream;
+  cublasPointerMode_t mode;
+  snapshot(*h, &stream, &mode);
+  float a, b;
+  const float *a_dev, *b_dev;
+  if (!scalar(mode, alpha, &a, &a_dev) || !scalar(mode, beta, &b, &b_dev))
+    return CUBLAS_STATUS_INVALID_VALUE;
+  const bool t = trans != CUBLAS_OP_N;
+  const int x_len = t ? m : n, y_len = t ? n : m;
+  const std::size_t a_elems = static_cast<std::size_t>(lda) * (n - 1) + m;
+  if (!mb200::device_span_ok(A, a_elems * sizeof(float)) || !mb200::aligned_to(A, 4) ||
+      !vec_ok(x, x_len, incx) || !vec_ok(y, y_len, incy))
+    return CUBLAS_STATUS_INVALID_VALUE;
+  const std::size_t need = mb200::blas::gemv_workspace_bytes(t, m, n);
+  if (need == 0)
+    return status_of(mb200::blas::launch_sgemv(t, m, n, a, a_dev, A, lda, x, incx, b, b_dev, y,
+                                                incy, nullptr, 0, stream));
+  BufferUse use(*h, stream);
+  if (!use.ok()) return CUBLAS_STATUS_EXECUTION_FAILED;
+  void* ws = use.workspace(need);
+  cudaError_t e = mb200::blas::launch_sgemv(t, m, n, a, a_dev, A, lda, x, incx, b, b_dev, y, incy,
+                                            ws, ws ? use.workspace_bytes() : 0, stream);
+  if (e == cudaSuccess) e = use.done();
+  return status_of(e);
 }
 
 }  // extern "C"

@@ -238,3 +238,61 @@ def bf16_bits(a: np.ndarray) -> np.ndarray:
 
 def bf16_to_f32(b: np.ndarray) -> np.ndarray:
     return (b.astype(np.uint32) << 16).view(np.float32)
+
+
+# ---------------------------------------------------------------- cuBLAS level 1 / 2
+def _f32(a):
+    return np.ascontiguousarray(a, dtype=np.float32)
+
+
+def saxpy(n, alpha, x, incx, y, incy):
+    """y = fma(alpha, x, y) in place on a copy of y (cublas_kernels.metal:11-23)."""
+    x, y = _f32(x), _f32(y).copy()
+    lib().oracle_saxpy(n, alpha, x.ctypes.data, incx, y.ctypes.data, incy)
+    return y
+
+
+def scopy(n, x, incx, y, incy):
+    x, y = _f32(x), _f32(y).copy()
+    lib().oracle_scopy(n, x.ctypes.data, incx, y.ctypes.data, incy)
+    return y
+
+
+def sscal(n, alpha, x, incx):
+    x = _f32(x).copy()
+    lib().oracle_sscal(n, alpha, x.ctypes.data, incx)
+    return x
+
+
+def sswap(n, x, incx, y, incy):
+    x, y = _f32(x).copy(), _f32(y).copy()
+    lib().oracle_sswap(n, x.ctypes.data, incx, y.ctypes.data, incy)
+    return x, y
+
+
+def sreduce(op, n, x, incx, y=None, incy=1):
+    """op 'dot' | 'nrm2' | 'asum' -> (fp32 reference formula, float64 value, float64
+    sum of term magnitudes)."""
+    code = {"dot": 0, "nrm2": 1, "asum": 2}[op]
+    x = _f32(x)
+    yy = _f32(y) if y is not None else np.zeros(1, np.float32)
+    f = np.zeros(1, np.float32)
+    d = np.zeros(2, np.float64)
+    lib().oracle_sreduce(code, n, x.ctypes.data, incx, yy.ctypes.data, incy, f.ctypes.data,
+                         d[:1].ctypes.data, d[1:].ctypes.data)
+    return float(f[0]), float(d[0]), float(d[1])
+
+
+def isamax(n, x, incx):
+    return int(lib().oracle_isamax(n, _f32(x).ctypes.data, incx))
+
+
+def sgemv(trans, m, n, alpha, A, lda, x, incx, beta, y, incy, threads=8):
+    """-> (y after the reference kernel, exact per output, |terms| per output)."""
+    A, x, y = _f32(A), _f32(x), _f32(y).copy()
+    out_len = n if trans else m
+    exact = np.zeros(out_len, np.float64)
+    absv = np.zeros(out_len, np.float64)
+    lib().oracle_sgemv(1 if trans else 0, m, n, alpha, A.ctypes.data, lda, x.ctypes.data, incx,
+                       beta, y.ctypes.data, incy, exact.ctypes.data, absv.ctypes.data, threads)
+    return y, exact, absv

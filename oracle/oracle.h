@@ -74,6 +74,19 @@ void oracle_gemm(int type, int transa, int transb, int m, int n, int k, float al
                  int accum_f64, const int32_t* rows, const int32_t* cols, int64_t n_entries,
                  int threads);
 
+/* ---- cuBLAS level 1 / 2, fp32 (libraries/blas/shaders/cublas_kernels.metal:11-524) ---- */
+void oracle_saxpy(int n, float alpha, const float* x, int incx, float* y, int incy);
+void oracle_scopy(int n, const float* x, int incx, float* y, int incy);
+void oracle_sscal(int n, float alpha, float* x, int incx);
+void oracle_sswap(int n, float* x, int incx, float* y, int incy);
+/* op 0 dot, 1 nrm2, 2 asum */
+void oracle_sreduce(int op, int n, const float* x, int incx, const float* y, int incy,
+                    float* out_f32, double* out_f64, double* out_abs);
+int oracle_isamax(int n, const float* x, int incx);
+void oracle_sgemv(int trans, int m, int n, float alpha, const float* A, int64_t lda,
+                  const float* x, int incx, float beta, float* y, int incy, double* exact,
+                  double* absv, int threads);
+
 /* ---- C2C FFT (libraries/fft/src/cufft_exec.mm:101-211) ---- */
 /* in/out: interleaved complex64 with element strides; use_double != 0 writes the
  * double-precision result to out_f64 (same layout) instead of out. */

@@ -37,6 +37,14 @@ _PROTOS: list[tuple[str, list, object]] = [
     ("oracle_gemm", [C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_float, vp,
                      C.c_int64, C.c_int64, vp, C.c_int64, C.c_int64, C.c_float, vp, C.c_int64,
                      C.c_int64, C.c_int, C.c_int, vp, vp, C.c_int64, C.c_int], None),
+    ("oracle_saxpy", [C.c_int, C.c_float, vp, C.c_int, vp, C.c_int], None),
+    ("oracle_scopy", [C.c_int, vp, C.c_int, vp, C.c_int], None),
+    ("oracle_sscal", [C.c_int, C.c_float, vp, C.c_int], None),
+    ("oracle_sswap", [C.c_int, vp, C.c_int, vp, C.c_int], None),
+    ("oracle_sreduce", [C.c_int, C.c_int, vp, C.c_int, vp, C.c_int, vp, vp, vp], None),
+    ("oracle_isamax", [C.c_int, vp, C.c_int], C.c_int),
+    ("oracle_sgemv", [C.c_int, C.c_int, C.c_int, C.c_float, vp, C.c_int64, vp, C.c_int, C.c_float,
+                      vp, C.c_int, vp, vp, C.c_int], None),
     ("oracle_fft_c2c", [vp, vp, C.c_int, vp, C.c_int64, C.c_int64, C.c_int64, C.c_int64,
                         C.c_int64, C.c_int, C.c_int, vp, C.c_int], None),
     ("oracle_spmv_csr", [C.c_int64, vp, vp, vp, C.c_int, vp, vp, C.c_float, C.c_float, vp,

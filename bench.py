@@ -473,6 +473,52 @@ def suite_fft(s: Suite) -> dict:
     return out
 
 
+def suite_fft_real(s: Suite) -> dict:
+    """R2C then C2R of L = 4096 reals, batch 65536, normal(0,1) seed 5, out of place
+    (reals -> half spectrum -> reals); value = algorithmic bytes (reals and half spectrum,
+    read + write, both directions) per second."""
+    from muda_b200 import capi, synth
+    torch = s.torch
+    n, batch = 4096, 65536 // s.scale
+    h = n // 2 + 1
+    x = synth.normal(torch, n * batch, seed=5)
+    X = torch.empty(batch * h, dtype=torch.complex64, device="cuda")
+    L = capi.cufft()
+    fwd, inv = C.c_void_p(), C.c_void_p()
+    assert L.cufftPlan1d(C.byref(fwd), n, capi.CUFFT_R2C, batch) == 0
+    assert L.cufftPlan1d(C.byref(inv), n, capi.CUFFT_C2R, batch) == 0
+    for p in (fwd, inv):
+        assert L.cufftSetStream(p, s.sp) == 0
+    px, pX = C.c_void_p(x.data_ptr()), C.c_void_p(X.data_ptr())
+
+    y = torch.empty_like(x)
+    py = C.c_void_p(y.data_ptr())
+    # each direction timed on its own (x -> X, X -> y), so no data grows across steps
+    ms_f, lf = s.time(lambda: L.cufftExecR2C(fwd, px, pX))
+    ms_i, li = s.time(lambda: L.cufftExecC2R(inv, pX, py))
+    assert L.cufftDestroy(fwd) == 0 and L.cufftDestroy(inv) == 0
+    per_dir = 4 * n * batch + 8 * h * batch
+    ms = ms_f + ms_i
+    gbs = 2 * per_dir / (ms * 1e-3) / 1e9
+    out = {"value": gbs, "unit": "GB/s", "ms": ms, "dtype": "f32/c64",
+           "config": f"L {n} x batch {batch}, R2C + C2R out of place, reals "
+                     f"{4 * n * batch / 1e9:.2f} GB > L2",
+           "r2c": {"ms": ms_f, "GB/s": per_dir / (ms_f * 1e-3) / 1e9},
+           "c2r": {"ms": ms_i, "GB/s": per_dir / (ms_i * 1e-3) / 1e9},
+           "roofline": s.roof("r2c_bulk_kernel<11> + c2r_bulk_kernel<11>", gbs, "hbm"),
+           "launches": lf + li, "algorithmic_bytes_per_direction": per_dir}
+    if s.cpu:
+        import oracle
+        sample = max(1, batch // 64)
+        xs = x[: n * sample].cpu().numpy()
+        dt = cpu_time(lambda: oracle.fft_r2c(xs, [n], sample, threads=os.cpu_count() or 1))
+        out["cpu_baseline"] = {"value": (4 * n + 8 * h) * sample / dt / 1e9, "unit": "GB/s",
+                               "cores": os.cpu_count(), "kind": "port",
+                               "sample": f"R2C of {sample} of {batch} rows, oracle/fft.cpp "
+                                         "gather + radix-2 Stockham + keep half"}
+    return out
+
+
 def suite_softmax(s: Suite) -> dict:
     """configs[4] softmax: 65536 x 4096 fp32 normal(0, 0.02) seed 11, ACCURATE, INSTANCE."""
     from muda_b200 import capi, synth
@@ -698,6 +744,7 @@ SUITE = {
     "sgemm": suite_sgemm,
     "spmv": suite_spmv,
     "fft": suite_fft,
+    "fft_real": suite_fft_real,
     "softmax": suite_softmax,
     "gemm_bf16": suite_gemm_bf16,
     "conv_bf16": lambda s: suite_conv(s, "bf16"),

@@ -77,6 +77,12 @@ cufftResult cufftDestroy(cufftHandle plan);
 
 /* Execution — reference cufft_exec.mm:101-211 */
 cufftResult cufftExecC2C(cufftHandle plan, cufftComplex* idata, cufftComplex* odata, int direction);
+/* Real-data transforms — reference cufft_exec.mm:213-438: R2C forward over all
+   axes keeping entries 0 .. n/2 of the last axis; C2R the unnormalised inverse
+   from that half spectrum (the imaginary parts of its first and, for even n,
+   middle entries are ignored, as in the reference).  The input is not modified. */
+cufftResult cufftExecR2C(cufftHandle plan, cufftReal* idata, cufftComplex* odata);
+cufftResult cufftExecC2R(cufftHandle plan, cufftComplex* idata, cufftReal* odata);
 
 /* Allocation-free execution.  No counterpart in the reference: an addition of
  * this library for callers that cannot allocate device memory when they need a

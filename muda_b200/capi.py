@@ -191,6 +191,8 @@ CUFFT_PROTOS = {
     "cufftGetSize": ([vp, P(sz)], i32),
     "cufftDestroy": ([vp], i32),
     "cufftExecC2C": ([vp, vp, vp, i32], i32),
+    "cufftExecR2C": ([vp, vp, vp], i32),
+    "cufftExecC2R": ([vp, vp, vp], i32),
     "cufftExecC2CNoAlloc": ([vp, vp, C.c_longlong, C.c_longlong, i32, vp], i32),
 }
 

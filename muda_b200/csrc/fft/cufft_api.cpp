@@ -1,4 +1,4 @@
-// cufft_api.cpp — cuFFT C ABI: plans and C2C execution.
+// cufft_api.cpp — cuFFT C ABI: plans, C2C, R2C and C2R execution.
 //
 // Mirrors libraries/fft/src/cufft_plan.mm and cufft_exec.mm of the reference:
 // same entry points and status codes, the same effective-stride rules
@@ -10,6 +10,12 @@
 // A plan owns device twiddle tables (shared between plans through an LRU keyed
 // by device and length) and, for power-of-two lengths above the single-pass
 // limit, a workspace for the two-pass split; cufftGetSize reports those bytes.
+//
+// Real-data plans (R2C, C2R; cufft_exec.mm:213-438): an even last axis L with
+// unit-stride reals runs as a length-L/2 complex FFT of the reals read as pairs
+// plus one post-pass (R2C) or pre-pass (C2R) of fft/real_kernels.cu; other
+// layouts gather into complex rows, transform and scatter, as the reference does.
+// Leading axes run on the half spectrum.  The plan owns the workspace.
 #pragma GCC visibility push(default)
 #include "cufft.h"
 #pragma GCC visibility pop
@@ -98,6 +104,12 @@ struct Plan {
   std::shared_ptr<DeviceBuffer> workspace;
   std::int64_t split_chunk = 0;  // transforms per workspace fill
   std::size_t work_bytes = 0;
+  // real-data plans: last axis L, half length M, half-spectrum length H = L/2 + 1
+  std::int64_t L = 0, M = 0, H = 0, prefix = 1;
+  bool packed = false;          // even L with unit-stride reals: length-M complex FFT
+  const float2* tw_L = nullptr;  // exp(-2*pi*i*m/L)
+  const float2* tw_M = nullptr;
+  std::shared_ptr<DeviceBuffer> real_ws;
 };
 
 using PlanTable = mb200::Registry<Plan, mb200::ObjKind::kFftPlan>;
@@ -126,23 +138,42 @@ cufftResult configure(Plan& p, int rank, const int* n, const int* inembed, int i
     dims[i] = n[i];
     total *= n[i];
   }
-  // Real-data transforms are outside this library's hot path.
-  if (type != CUFFT_C2C) return CUFFT_NOT_SUPPORTED;
-  for (int i = 0; i < rank; ++i) {
-    if (!axis_supported(dims[i])) return CUFFT_NOT_SUPPORTED;
-    if (rank > 1 && axis_kind(dims[i]) == AxisKind::kSplit) return CUFFT_NOT_SUPPORTED;
+  const bool real = type != CUFFT_C2C;
+  const std::int64_t L = dims[rank - 1];
+  const std::int64_t H = L / 2 + 1;
+  const std::int64_t herm_total = total / L * H;
+  if (real) {
+    // every complex transform a real plan runs must take one pass (no split)
+    auto one_pass = [](std::int64_t n) {
+      const AxisKind k = axis_kind(n);
+      return n == 1 || k == AxisKind::kSinglePass || k == AxisKind::kDirect;
+    };
+    for (int i = 0; i + 1 < rank; ++i)
+      if (!one_pass(dims[i])) return CUFFT_NOT_SUPPORTED;
+    const bool packed_ok = L % 2 == 0 && L >= 4 && one_pass(L / 2);
+    if (!packed_ok && !one_pass(L)) return CUFFT_NOT_SUPPORTED;
+  } else {
+    for (int i = 0; i < rank; ++i) {
+      if (!axis_supported(dims[i])) return CUFFT_NOT_SUPPORTED;
+      if (rank > 1 && axis_kind(dims[i]) == AxisKind::kSplit) return CUFFT_NOT_SUPPORTED;
+    }
   }
   const std::int64_t eis = (inembed != nullptr) ? istride : 1;
   const std::int64_t eos = (onembed != nullptr) ? ostride : 1;
   if (eis <= 0 || eos <= 0) return CUFFT_INVALID_VALUE;
-  const std::int64_t eid = (inembed != nullptr && idist > 0) ? idist : total;
-  const std::int64_t eod = (onembed != nullptr && odist > 0) ? odist : total;
+  // default distances (cufft_plan.mm:74-79): the half spectrum is the dense complex side
+  const std::int64_t def_id = type == CUFFT_C2R ? herm_total : total;
+  const std::int64_t def_od = type == CUFFT_R2C ? herm_total : total;
+  const std::int64_t eid = (inembed != nullptr && idist > 0) ? idist : def_id;
+  const std::int64_t eod = (onembed != nullptr && odist > 0) ? odist : def_od;
   if (mb200::current_device() < 0) return CUFFT_SETUP_FAILED;
 
   std::lock_guard<std::mutex> g(p.mu);
   p.configured = false;
   p.tables.clear();
   p.workspace.reset();
+  p.real_ws.reset();
+  p.packed = false;
   p.rank = rank;
   p.dims = dims;
   p.batch = batch;
@@ -162,12 +193,39 @@ cufftResult configure(Plan& p, int rank, const int* n, const int* inembed, int i
   };
   for (int i = 0; i < rank; ++i) {
     p.axis_tw[i] = nullptr;
+    if (real && i == rank - 1) continue;  // the last axis of a real plan: below
     if (axis_kind(dims[i]) == AxisKind::kSinglePass || axis_kind(dims[i]) == AxisKind::kDirect) {
       p.axis_tw[i] = hold(dims[i]);
       if (p.axis_tw[i] == nullptr) return CUFFT_ALLOC_FAILED;
     }
   }
-  if (rank == 1 && axis_kind(dims[0]) == AxisKind::kSplit) {
+  if (real) {
+    p.L = L;
+    p.H = H;
+    p.M = L / 2;
+    p.prefix = total / L;
+    const AxisKind km = axis_kind(p.M);
+    const bool packed_ok =
+        L % 2 == 0 && L >= 4 && (km == AxisKind::kSinglePass || km == AxisKind::kDirect);
+    p.packed = packed_ok && (type == CUFFT_R2C ? (eis == 1 && eid % 2 == 0)
+                                               : (eos == 1 && eod % 2 == 0));
+    if (L > 1) {
+      p.tw_L = hold(L);
+      if (p.tw_L == nullptr) return CUFFT_ALLOC_FAILED;
+    }
+    if (packed_ok) {
+      p.tw_M = hold(p.M);
+      if (p.tw_M == nullptr) return CUFFT_ALLOC_FAILED;
+    }
+    const std::int64_t rows = batch * p.prefix;
+    const std::int64_t need =
+        p.packed ? rows * (p.M + (type == CUFFT_C2R && rank > 1 ? H : 0))
+                 : rows * (L + (type == CUFFT_C2R ? H : 0));
+    p.real_ws = DeviceBuffer::make(static_cast<std::size_t>(need) * sizeof(float2));
+    if (!p.real_ws) return CUFFT_ALLOC_FAILED;
+    p.work_bytes += p.real_ws->bytes;
+  }
+  if (!real && rank == 1 && axis_kind(dims[0]) == AxisKind::kSplit) {
     int l = 0;
     while ((std::int64_t{1} << l) < dims[0]) ++l;
     p.n1 = std::int64_t{1} << (l / 2);
@@ -250,6 +308,72 @@ cudaError_t run_split(const Plan& p, const float2* in, float2* out, int sign, cu
     if (e != cudaSuccess) return e;
   }
   return cudaSuccess;
+}
+
+// Transforms axes a_hi .. 0 (innermost first) of `batch` row-major arrays of
+// complex elements with dims[0 .. rank) (dims[rank - 1] innermost; axes above
+// a_hi are left alone).  The first axis of length > 1 reads `in` (element stride
+// is, batch distance id) and writes `out` (os, od); the later ones run in place on
+// `out`.  *moved reports whether any axis had length > 1.
+cudaError_t run_axes(int rank, const std::array<std::int64_t, 3>& dims, int a_hi,
+                     const std::array<const float2*, 3>& tw, const float2* in, std::int64_t is,
+                     std::int64_t id, float2* out, std::int64_t os, std::int64_t od,
+                     std::int64_t batch, int sign, cudaStream_t st, bool* moved) {
+  cudaError_t e = cudaSuccess;
+  std::int64_t epb = 1;
+  for (int i = 0; i < rank; ++i) epb *= dims[i];
+  bool first = true;
+  // The first transformed axis reads the input, the others run in place on the
+  // output.  Logical element (o, t, i) of axis a sits at
+  // o*L*S + t*S + i with L = dims[a], S = product of the later dims.
+  for (int a = a_hi; a >= 0 && e == cudaSuccess; --a) {
+    const std::int64_t L = dims[a];
+    std::int64_t S = 1, Pr = 1;
+    for (int i = a + 1; i < rank; ++i) S *= dims[i];
+    for (int i = 0; i < a; ++i) Pr *= dims[i];
+    // A length-1 axis is the identity; the next axis then reads the input.
+    if (L == 1) continue;
+    const float2* src = first ? in : out;
+    const std::int64_t s_str = first ? is : os;
+    const std::int64_t s_dist = first ? id : od;
+    const bool dense = (s_dist == epb * s_str) && (od == epb * os);
+    const std::int64_t nb_loop = (S == 1 || dense) ? 1 : batch;
+    for (std::int64_t bl = 0; bl < nb_loop && e == cudaSuccess; ++bl) {
+      Batch1D b{};
+      b.in = src + bl * s_dist;
+      b.out = out + bl * od;
+      b.in_stride = S * s_str;
+      b.out_stride = S * os;
+      b.post_n = 1;
+      b.inner_count = S;
+      b.in_inner = s_str;
+      b.out_inner = os;
+      if (nb_loop == 1 && S == 1) {
+        // (batch, o) -> contiguous rows of length L
+        b.batch = batch * Pr;
+        b.inner_count = Pr;
+        b.in_outer = s_dist;
+        b.in_inner = L * s_str;
+        b.out_outer = od;
+        b.out_inner = L * os;
+        b.in_stride = s_str;
+        b.out_stride = os;
+      } else if (nb_loop == 1) {
+        // dense batches: (batch, o) fold into one outer index of stride L*S
+        b.batch = batch * Pr * S;
+        b.in_outer = L * S * s_str;
+        b.out_outer = L * S * os;
+      } else {
+        b.batch = Pr * S;
+        b.in_outer = L * S * s_str;
+        b.out_outer = L * S * os;
+      }
+      e = run_axis(L, sign, b, tw[a], st);
+    }
+    first = false;
+  }
+  *moved = !first;
+  return e;
 }
 
 cufftResult make_plan(cufftHandle* plan, int rank, int* n, int* inembed, int istride, int idist,
@@ -374,61 +498,237 @@ cufftResult cufftExecC2C(cufftHandle plan, cufftComplex* idata, cufftComplex* od
     return e == cudaSuccess ? CUFFT_SUCCESS : CUFFT_EXEC_FAILED;
   }
 
-  // Multi-dimensional: innermost axis reads the input, the others run in place
-  // on the output.  Logical element (o, t, i) of axis a sits at
-  // o*L*S + t*S + i with L = dims[a], S = product of the later dims.
-  bool first = true;
-  for (int a = p->rank - 1; a >= 0 && e == cudaSuccess; --a) {
-    const std::int64_t L = p->dims[a];
-    std::int64_t S = 1, Pr = 1;
-    for (int i = a + 1; i < p->rank; ++i) S *= p->dims[i];
-    for (int i = 0; i < a; ++i) Pr *= p->dims[i];
-    // A length-1 axis is the identity; the next axis then reads the input.
-    if (L == 1) continue;
-    const float2* src = first ? idata : odata;
-    const std::int64_t s_str = first ? p->istride : p->ostride;
-    const std::int64_t s_dist = first ? p->idist : p->odist;
-    const bool dense = (s_dist == epb * s_str) && (p->odist == epb * p->ostride);
-    const std::int64_t nb_loop = (S == 1 || dense) ? 1 : p->batch;
-    for (std::int64_t bl = 0; bl < nb_loop && e == cudaSuccess; ++bl) {
-      Batch1D b{};
-      b.in = src + bl * s_dist;
-      b.out = odata + bl * p->odist;
-      b.in_stride = S * s_str;
-      b.out_stride = S * p->ostride;
-      b.post_n = 1;
-      b.inner_count = S;
-      b.in_inner = s_str;
-      b.out_inner = p->ostride;
-      if (nb_loop == 1 && S == 1) {
-        // (batch, o) -> contiguous rows of length L
-        b.batch = p->batch * Pr;
-        b.inner_count = Pr;
-        b.in_outer = s_dist;
-        b.in_inner = L * s_str;
-        b.out_outer = p->odist;
-        b.out_inner = L * p->ostride;
-        b.in_stride = s_str;
-        b.out_stride = p->ostride;
-      } else if (nb_loop == 1) {
-        // dense batches: (batch, o) fold into one outer index of stride L*S
-        b.batch = p->batch * Pr * S;
-        b.in_outer = L * S * s_str;
-        b.out_outer = L * S * p->ostride;
-      } else {
-        b.batch = Pr * S;
-        b.in_outer = L * S * s_str;
-        b.out_outer = L * S * p->ostride;
-      }
-      e = run_axis(L, sign, b, p->axis_tw[a], st);
-    }
-    first = false;
-  }
+  bool moved = false;
+  e = run_axes(p->rank, p->dims, p->rank - 1, p->axis_tw, idata, p->istride, p->idist, odata,
+               p->ostride, p->odist, p->batch, sign, st, &moved);
+  const bool first = !moved;
   if (first && e == cudaSuccess) {
     // every axis has length 1: the transform is the identity
     for (std::int64_t b = 0; b < p->batch && e == cudaSuccess && idata != odata; ++b)
       e = cudaMemcpyAsync(odata + b * p->odist, idata + b * p->idist, sizeof(float2),
                           cudaMemcpyDeviceToDevice, st);
+  }
+  return e == cudaSuccess ? CUFFT_SUCCESS : CUFFT_EXEC_FAILED;
+}
+
+// Length-M complex transforms of rows r = b * prefix + p: the reals of row r seen
+// as M complex pairs at base + b * dist2 + p * M (complex units), dense rows at Z.
+namespace {
+
+Batch1D pair_rows(const Plan& p, const float2* in, std::int64_t in_dist2, float2* out,
+                  std::int64_t out_dist2, bool reals_in) {
+  Batch1D b{};
+  b.in = in;
+  b.out = out;
+  b.in_stride = 1;
+  b.out_stride = 1;
+  b.inner_count = p.prefix;
+  b.batch = p.batch * p.prefix;
+  b.in_outer = reals_in ? in_dist2 : p.prefix * p.M;
+  b.in_inner = p.M;
+  b.out_outer = reals_in ? p.prefix * p.M : out_dist2;
+  b.out_inner = p.M;
+  b.post_n = 1;
+  return b;
+}
+
+// Dense complex rows of length len at base (rows r = b * prefix + p contiguous).
+Batch1D dense_rows(const Plan& p, float2* base, std::int64_t len) {
+  Batch1D b{};
+  b.in = base;
+  b.out = base;
+  b.in_stride = b.out_stride = 1;
+  b.inner_count = 1;
+  b.batch = p.batch * p.prefix;
+  b.in_outer = b.out_outer = len;
+  b.in_inner = b.out_inner = 0;
+  b.post_n = 1;
+  return b;
+}
+
+// The plan's dims with the last axis replaced by `last`.
+std::array<std::int64_t, 3> with_last(const Plan& p, std::int64_t last) {
+  std::array<std::int64_t, 3> d = p.dims;
+  d[p.rank - 1] = last;
+  return d;
+}
+
+// True when the byte ranges [a, a + na) and [b, b + nb) share an address.
+bool overlap(const void* a, std::size_t na, const void* b, std::size_t nb) {
+  const auto x = reinterpret_cast<std::uintptr_t>(a);
+  const auto y = reinterpret_cast<std::uintptr_t>(b);
+  return x < y + nb && y < x + na;
+}
+
+// Grows the plan's real-data workspace to `floats2` complex elements.
+float2* real_workspace(Plan& p, std::int64_t floats2) {
+  const std::size_t need = static_cast<std::size_t>(floats2) * sizeof(float2);
+  if (!p.real_ws || p.real_ws->bytes < need) {
+    p.real_ws.reset();
+    p.real_ws = DeviceBuffer::make(need);
+  }
+  return p.real_ws ? static_cast<float2*>(p.real_ws->ptr) : nullptr;
+}
+
+}  // namespace
+
+cufftResult cufftExecR2C(cufftHandle plan, cufftReal* idata, cufftComplex* odata) {
+  auto p = plans().get(plan);
+  if (!p) return CUFFT_INVALID_PLAN;
+  std::lock_guard<std::mutex> g(p->mu);
+  if (!p->configured) return CUFFT_INVALID_PLAN;
+  if (idata == nullptr || odata == nullptr) return CUFFT_INVALID_VALUE;
+  if (p->type != CUFFT_R2C) return CUFFT_INVALID_TYPE;
+  if (mb200::current_device() != p->device) return CUFFT_INVALID_DEVICE;
+  const std::int64_t epb = elems_per_batch(*p);
+  const std::int64_t hpb = p->prefix * p->H;
+  const std::size_t in_span =
+      static_cast<std::size_t>((p->batch - 1) * p->idist + (epb - 1) * p->istride + 1);
+  const std::size_t out_span =
+      static_cast<std::size_t>((p->batch - 1) * p->odist + (hpb - 1) * p->ostride + 1);
+  if (!mb200::device_span_ok(idata, in_span * sizeof(float)) ||
+      !mb200::device_span_ok(odata, out_span * sizeof(float2)) || !mb200::aligned_to(idata, 4) ||
+      !mb200::aligned_to(odata, 8))
+    return CUFFT_INVALID_VALUE;
+  const cudaStream_t st = p->stream;
+  const std::int64_t rows = p->batch * p->prefix;
+  cudaError_t e = cudaSuccess;
+  const bool dense = p->istride == 1 && p->idist == epb && p->ostride == 1 && p->odist == hpb &&
+                     !overlap(idata, rows * p->L * sizeof(float), odata,
+                              rows * p->H * sizeof(float2));
+  const std::int64_t per =
+      (p->packed && dense && mb200::fft::real_bulk_aligned(true, p->M, idata, odata))
+          ? mb200::fft::real_bulk_rows_per_group(p->M)
+          : 0;
+  if (per > 0 && rows >= per) {
+    // whole groups through the fused kernel, the remaining rows as dense rows below
+    const std::int64_t groups = rows / per, done = groups * per;
+    e = mb200::fft::launch_real_bulk(true, p->M, idata, odata, groups, p->tw_M, p->tw_L, st);
+    if (e == cudaSuccess && done < rows) {
+      float2* Z = real_workspace(*p, (rows - done) * p->M);
+      if (Z == nullptr) return CUFFT_ALLOC_FAILED;
+      Batch1D f = dense_rows(*p, Z, p->M);
+      f.in = reinterpret_cast<const float2*>(idata) + done * p->M;
+      f.batch = rows - done;
+      e = run_axis(p->M, -1, f, p->tw_M, st);
+      const mb200::fft::RealRows rr{rows - done, 1, p->M, p->tw_L};
+      if (e == cudaSuccess)
+        e = mb200::fft::launch_r2c_post(rr, Z, odata + done * p->H, p->H, 1, st);
+    }
+  } else if (p->packed && mb200::aligned_to(idata, 8)) {
+    float2* Z = real_workspace(*p, rows * p->M);
+    if (Z == nullptr) return CUFFT_ALLOC_FAILED;
+    Batch1D f = pair_rows(*p, reinterpret_cast<const float2*>(idata), p->idist / 2, Z, 0, true);
+    e = run_axis(p->M, -1, f, p->tw_M, st);
+    const mb200::fft::RealRows rr{rows, p->prefix, p->M, p->tw_L};
+    if (e == cudaSuccess) e = mb200::fft::launch_r2c_post(rr, Z, odata, p->odist, p->ostride, st);
+  } else {
+    float2* A = real_workspace(*p, rows * p->L);
+    if (A == nullptr) return CUFFT_ALLOC_FAILED;
+    e = mb200::fft::launch_gather_real(rows, p->prefix, p->L, idata, p->idist, p->istride, A, st);
+    if (e == cudaSuccess && p->L > 1) {
+      Batch1D b = dense_rows(*p, A, p->L);
+      e = run_axis(p->L, -1, b, p->tw_L, st);
+    }
+    if (e == cudaSuccess)
+      e = mb200::fft::launch_scatter_half(rows, p->prefix, p->L, A, odata, p->odist, p->ostride,
+                                          st);
+  }
+  // leading axes on the half spectrum, in place on the output
+  if (e == cudaSuccess && p->rank > 1) {
+    bool moved = false;
+    e = run_axes(p->rank, with_last(*p, p->H), p->rank - 2, p->axis_tw, odata, p->ostride,
+                 p->odist, odata, p->ostride, p->odist, p->batch, -1, st, &moved);
+  }
+  return e == cudaSuccess ? CUFFT_SUCCESS : CUFFT_EXEC_FAILED;
+}
+
+cufftResult cufftExecC2R(cufftHandle plan, cufftComplex* idata, cufftReal* odata) {
+  auto p = plans().get(plan);
+  if (!p) return CUFFT_INVALID_PLAN;
+  std::lock_guard<std::mutex> g(p->mu);
+  if (!p->configured) return CUFFT_INVALID_PLAN;
+  if (idata == nullptr || odata == nullptr) return CUFFT_INVALID_VALUE;
+  if (p->type != CUFFT_C2R) return CUFFT_INVALID_TYPE;
+  if (mb200::current_device() != p->device) return CUFFT_INVALID_DEVICE;
+  const std::int64_t epb = elems_per_batch(*p);
+  const std::int64_t hpb = p->prefix * p->H;
+  const std::size_t in_span =
+      static_cast<std::size_t>((p->batch - 1) * p->idist + (hpb - 1) * p->istride + 1);
+  const std::size_t out_span =
+      static_cast<std::size_t>((p->batch - 1) * p->odist + (epb - 1) * p->ostride + 1);
+  if (!mb200::device_span_ok(idata, in_span * sizeof(float2)) ||
+      !mb200::device_span_ok(odata, out_span * sizeof(float)) || !mb200::aligned_to(idata, 8) ||
+      !mb200::aligned_to(odata, 4))
+    return CUFFT_INVALID_VALUE;
+  const cudaStream_t st = p->stream;
+  const std::int64_t rows = p->batch * p->prefix;
+  cudaError_t e = cudaSuccess;
+  if (p->packed && mb200::aligned_to(odata, 8)) {
+    const bool lead = p->rank > 1;
+    float2* base = real_workspace(*p, rows * (p->M + (lead ? p->H : 0)));
+    if (base == nullptr) return CUFFT_ALLOC_FAILED;
+    float2* W = base;                           // leading axes: dense half spectrum
+    float2* Z = base + (lead ? rows * p->H : 0);  // pre-pass output
+    const float2* src = idata;
+    std::int64_t sdist = p->idist, sstr = p->istride;
+    if (lead) {
+      bool moved = false;
+      e = run_axes(p->rank, with_last(*p, p->H), p->rank - 2, p->axis_tw, idata, p->istride,
+                   p->idist, W, 1, hpb, p->batch, +1, st, &moved);
+      if (moved) {
+        src = W;
+        sdist = hpb;
+        sstr = 1;
+      }
+    }
+    const bool dense = sstr == 1 && sdist == hpb && p->ostride == 1 && p->odist == epb &&
+                       mb200::fft::real_bulk_aligned(false, p->M, src, odata) &&
+                       !overlap(src, rows * p->H * sizeof(float2), odata,
+                                rows * p->L * sizeof(float));
+    const std::int64_t per = dense ? mb200::fft::real_bulk_rows_per_group(p->M) : 0;
+    std::int64_t done = 0;
+    if (e == cudaSuccess && per > 0 && rows >= per) {
+      const std::int64_t groups = rows / per;
+      done = groups * per;
+      e = mb200::fft::launch_real_bulk(false, p->M, src, odata, groups, p->tw_M, p->tw_L, st);
+    }
+    if (e == cudaSuccess && done > 0 && done < rows) {
+      // the remaining dense rows
+      const mb200::fft::RealRows rr{rows - done, 1, p->M, p->tw_L};
+      e = mb200::fft::launch_c2r_pre(rr, src + done * p->H, p->H, 1, Z, st);
+      if (e == cudaSuccess) {
+        Batch1D b = dense_rows(*p, Z, p->M);
+        b.out = reinterpret_cast<float2*>(odata) + done * p->M;
+        b.batch = rows - done;
+        e = run_axis(p->M, +1, b, p->tw_M, st);
+      }
+    } else if (e == cudaSuccess && done == 0) {
+      const mb200::fft::RealRows rr{rows, p->prefix, p->M, p->tw_L};
+      e = mb200::fft::launch_c2r_pre(rr, src, sdist, sstr, Z, st);
+      if (e == cudaSuccess) {
+        Batch1D b = pair_rows(*p, Z, 0, reinterpret_cast<float2*>(odata), p->odist / 2, false);
+        e = run_axis(p->M, +1, b, p->tw_M, st);
+      }
+    }
+  } else {
+    float2* A = real_workspace(*p, rows * (p->H + p->L));
+    if (A == nullptr) return CUFFT_ALLOC_FAILED;
+    float2* B = A + rows * p->H;
+    e = mb200::fft::launch_gather_half(rows, p->prefix, p->L, idata, p->idist, p->istride, A, st);
+    if (e == cudaSuccess && p->rank > 1) {
+      bool moved = false;
+      e = run_axes(p->rank, with_last(*p, p->H), p->rank - 2, p->axis_tw, A, 1, hpb, A, 1, hpb,
+                   p->batch, +1, st, &moved);
+    }
+    if (e == cudaSuccess) e = mb200::fft::launch_expand_half(rows, p->L, A, B, st);
+    if (e == cudaSuccess && p->L > 1) {
+      Batch1D b = dense_rows(*p, B, p->L);
+      e = run_axis(p->L, +1, b, p->tw_L, st);
+    }
+    if (e == cudaSuccess)
+      e = mb200::fft::launch_scatter_real(rows, p->prefix, p->L, B, odata, p->odist, p->ostride,
+                                          st);
   }
   return e == cudaSuccess ? CUFFT_SUCCESS : CUFFT_EXEC_FAILED;
 }

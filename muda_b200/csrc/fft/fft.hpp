@@ -47,4 +47,64 @@ cudaError_t launch_direct_dft(std::int64_t n, int sign, const Batch1D& b,
 // Fills tw[0 .. n) with exp(-2*pi*i*m/n) rounded from double precision.
 void host_twiddles(std::int64_t n, float2* tw) noexcept;
 
+// Real-data transforms of even length L = 2M through a length-M complex FFT of
+// the reals read as M complex pairs, z[n] = x[2n] + i x[2n+1].  Rows are indexed
+// r = b * prefix + p (b the batch entry, p the position along the leading axes).
+// Complex element k of row r of a strided operand sits at
+//   base + b * dist + (p * row_len + k) * stride.
+struct RealRows {
+  std::int64_t rows, prefix;
+  std::int64_t M;          // half length
+  const float2* tw;        // exp(-2*pi*i*m/L), m in [0, L)
+};
+
+// Fused real-data transforms of dense rows (reals of row r at r * 2n, half
+// spectrum at r * (n + 1)) for half length n a power of two in [16, 4096]: one
+// kernel per direction, the length-n complex FFT with the R2C post-pass in its
+// epilogue or the C2R pre-pass in its first pass.  `groups` groups of
+// real_bulk_rows_per_group(n) rows each; tw = exp(-2*pi*i*m/n), twl = exp(-2*pi*i*m/(2n)).
+// real_bulk_aligned says whether the pointers meet the kernels' alignment (R2C:
+// 16-byte reals; C2R: 16-byte reals and, for n <= 2048, 16-byte half spectra);
+// input and output must not overlap.
+std::int64_t real_bulk_rows_per_group(std::int64_t n) noexcept;
+bool real_bulk_aligned(bool r2c, std::int64_t n, const void* in, const void* out) noexcept;
+cudaError_t launch_real_bulk(bool r2c, std::int64_t n, const void* in, void* out,
+                             long long groups, const float2* tw, const float2* twl,
+                             cudaStream_t stream) noexcept;
+
+// R2C post-pass: Z (row r at Z + r * M, dense) -> X[0 .. M] of each row,
+// X[k] = (Z[k] + conj(Z[M-k]))/2 - i W^k (Z[k] - conj(Z[M-k]))/2, W = exp(-2*pi*i/L),
+// Z[M] = Z[0]; written to out with row_len M + 1.
+cudaError_t launch_r2c_post(const RealRows& g, const float2* Z, float2* out, std::int64_t odist,
+                            std::int64_t ostride, cudaStream_t stream) noexcept;
+
+// C2R pre-pass: X[0 .. M] of each row (read with row_len M + 1) -> Z' (dense),
+// Z'[k] = E[k] + i O[k], E[k] = X[k] + X[k+M], O[k] = (X[k] - X[k+M]) W^-k with
+// X[k+M] = conj(X[M-k]) for k > 0, the imaginary parts of X[0] and X[M] ignored
+// (the reference expands the half spectrum and keeps the real part of a complex
+// inverse, which drops exactly those); the length-M inverse of Z' is then
+// x[2n] + i x[2n+1] of the unnormalised real inverse.
+cudaError_t launch_c2r_pre(const RealRows& g, const float2* X, std::int64_t idist,
+                           std::int64_t istride, float2* Z, cudaStream_t stream) noexcept;
+
+// Real <-> complex layout moves of the general path: gather reals as (x, 0)
+// into dense complex rows of length L; scatter the first M + 1 (= L/2 + 1)
+// entries of dense complex rows into a strided half-spectrum output; expand a
+// dense half spectrum (row_len L/2 + 1) into full rows by conjugate symmetry;
+// scatter the real parts of dense complex rows into a strided real output.
+cudaError_t launch_gather_real(std::int64_t rows, std::int64_t prefix, std::int64_t L,
+                               const float* in, std::int64_t idist, std::int64_t istride,
+                               float2* out, cudaStream_t stream) noexcept;
+cudaError_t launch_scatter_half(std::int64_t rows, std::int64_t prefix, std::int64_t L,
+                                const float2* in, float2* out, std::int64_t odist,
+                                std::int64_t ostride, cudaStream_t stream) noexcept;
+cudaError_t launch_gather_half(std::int64_t rows, std::int64_t prefix, std::int64_t L,
+                               const float2* in, std::int64_t idist, std::int64_t istride,
+                               float2* out, cudaStream_t stream) noexcept;
+cudaError_t launch_expand_half(std::int64_t rows, std::int64_t L, const float2* in, float2* out,
+                               cudaStream_t stream) noexcept;
+cudaError_t launch_scatter_real(std::int64_t rows, std::int64_t prefix, std::int64_t L,
+                                const float2* in, float* out, std::int64_t odist,
+                                std::int64_t ostride, cudaStream_t stream) noexcept;
+
 }  // namespace mb200::fft

@@ -351,12 +351,35 @@ cudaError_t dispatch(int log2n, const Batch1D& b, cudaStream_t st) {
 
 __device__ unsigned int g_fft_bulk_timeouts;
 
-// Pass of the staged kernel: FIRST reads the staging buffer `st`, LAST writes it;
-// every other read and write goes through the padded work arrays.
-template <int LOG2N, int R, int S, bool FIRST, bool LAST>
+// C2R pre-pass value Z'[k] = E[k] + i O[k] of a half-spectrum row X[0 .. n] held
+// in shared memory: E[k] = X[k] + Xc, O[k] = (X[k] - Xc) conj(W^k), Xc = conj(X[n-k])
+// for k > 0; for k = 0 only the real parts of X[0] and X[n] are used.  W^k is
+// twl[k] = exp(-2*pi*i*k/(2n)).
+__device__ __forceinline__ float2 c2r_point(const float2* raw, int k, int n,
+                                            const float2* __restrict__ twl) {
+  float2 xk = raw[k];
+  float2 xc;
+  if (k == 0) {
+    xk.y = 0.0f;
+    xc = make_float2(raw[n].x, 0.0f);
+  } else {
+    const float2 u = raw[n - k];
+    xc = make_float2(u.x, -u.y);
+  }
+  const float2 e = cadd(xk, xc);
+  const float2 w = __ldg(twl + k);
+  const float2 o = cmul(csub(xk, xc), make_float2(w.x, -w.y));
+  return make_float2(e.x - o.y, e.y + o.x);
+}
+
+// Pass of the staged kernel: FIRST reads the staging buffer `st` (for PRE, the
+// half-spectrum row `raw` through c2r_point), LAST writes `st`; every other read
+// and write goes through the padded work arrays.
+template <int LOG2N, int R, int S, bool FIRST, bool LAST, bool PRE = false>
 __device__ __forceinline__ void spass(float2 (&v)[Plan<LOG2N>::P], int j, int Ns, int log2Ns,
                                       float2* st, float* sre, float* sim,
-                                      const float2* __restrict__ tw) {
+                                      const float2* __restrict__ tw, const float2* raw = nullptr,
+                                      const float2* __restrict__ twl = nullptr) {
   using PL = Plan<LOG2N>;
   constexpr int N = PL::N;
   constexpr int T = PL::T;
@@ -367,7 +390,11 @@ __device__ __forceinline__ void spass(float2 (&v)[Plan<LOG2N>::P], int j, int Ns
 #pragma unroll
     for (int r = 0; r < R; ++r) {
       const int idx = b + r * (N / R);
-      v[q * R + r] = FIRST ? st[idx] : make_float2(sre[pad(idx)], sim[pad(idx)]);
+      if constexpr (FIRST && PRE) {
+        v[q * R + r] = c2r_point(raw, idx, N, twl);
+      } else {
+        v[q * R + r] = FIRST ? st[idx] : make_float2(sre[pad(idx)], sim[pad(idx)]);
+      }
     }
   }
   // The work arrays alias the staging buffer, so every pass finishes its reads
@@ -396,16 +423,18 @@ __device__ __forceinline__ void spass(float2 (&v)[Plan<LOG2N>::P], int j, int Ns
   if constexpr (!LAST) __syncthreads();
 }
 
-template <int LOG2N, int S, int PASS = 0>
+template <int LOG2N, int S, bool PRE = false, int PASS = 0>
 __device__ __forceinline__ void run_spasses(float2 (&v)[Plan<LOG2N>::P], int j, float2* st,
-                                            float* sre, float* sim, const float2* tw) {
+                                            float* sre, float* sim, const float2* tw,
+                                            const float2* raw = nullptr,
+                                            const float2* twl = nullptr) {
   using PL = Plan<LOG2N>;
   if constexpr (PASS < PL::PASSES) {
     constexpr int R = (PASS == 0) ? PL::FIRST_R : 16;
     constexpr int LOG2NS = (PASS == 0) ? 0 : (ilog2(PL::FIRST_R) + 4 * (PASS - 1));
-    spass<LOG2N, R, S, PASS == 0, PASS == PL::PASSES - 1>(v, j, 1 << LOG2NS, LOG2NS, st, sre, sim,
-                                                          tw);
-    run_spasses<LOG2N, S, PASS + 1>(v, j, st, sre, sim, tw);
+    spass<LOG2N, R, S, PASS == 0, PASS == PL::PASSES - 1, PRE>(v, j, 1 << LOG2NS, LOG2NS, st, sre,
+                                                               sim, tw, raw, twl);
+    run_spasses<LOG2N, S, PRE, PASS + 1>(v, j, st, sre, sim, tw, raw, twl);
   }
 }
 
@@ -543,6 +572,259 @@ unsigned int* bulk_timeout_counter() {
   return addr[dev];
 }
 
+// ---------------------------------------------------------------------------
+// Real-data variants of the bulk kernel: R2C / C2R of even length L = 2N through
+// the length-N complex transform of the reals read as N pairs.  Rows are dense on
+// both sides (reals at r * L, half spectra at r * (N + 1)).
+//
+// R2C: the group's reals arrive by bulk copy exactly as a C2C group does; after the
+// last pass the TPC rows Z sit in natural order in the staging buffer and the post-
+// pass X[k] = E - i W^k D, E = (Z[k] + conj Z[N-k])/2, D = (Z[k] - conj Z[N-k])/2,
+// k = 0 .. N (W = exp(-2*pi*i/L), Z[N] = Z[0]) stores the N + 1 entries of each row
+// straight to global memory: one HBM read and one HBM write per element, no
+// intermediate.  Entries k and N - k come from the same two values: with
+// P = W^k D, X[k] = E - i P and, since W^(N-k) = -conj(W^k), X[N-k] = conj(E) -
+// i conj(P); so one thread forms both from two shared-memory reads and one twiddle.
+
+__device__ __forceinline__ void r2c_pair(const float2* z, int k, int n,
+                                         const float2* __restrict__ twl, float2& xk,
+                                         float2& xnk) {
+  const float2 a = z[k];
+  const float2 c = z[k == 0 ? 0 : n - k];
+  const float2 e = make_float2(0.5f * (a.x + c.x), 0.5f * (a.y - c.y));
+  const float2 d = make_float2(0.5f * (a.x - c.x), 0.5f * (a.y + c.y));
+  const float2 q = cmul(__ldg(twl + k), d);
+  xk = make_float2(e.x + q.y, e.y - q.x);
+  xnk = make_float2(e.x - q.y, -e.y - q.x);
+}
+
+template <int LOG2N>
+__global__ void __launch_bounds__(Plan<LOG2N>::THREADS, 3)
+    r2c_bulk_kernel(const float* in, float2* out, long long groups, const float2* __restrict__ tw,
+                    const float2* __restrict__ twl, unsigned int* timeouts) {
+  using PL = Plan<LOG2N>;
+  using BP = BulkPlan<LOG2N>;
+  constexpr int N = PL::N;
+  constexpr int H = N + 1;
+  extern __shared__ __align__(16) std::uint8_t bsmem[];
+  float2* stage0 = reinterpret_cast<float2*>(bsmem);
+  float2* stage1 = reinterpret_cast<float2*>(bsmem + BP::STAGE_BYTES);
+  std::uint64_t* full = reinterpret_cast<std::uint64_t*>(bsmem + 2 * BP::STAGE_BYTES);
+  volatile int* ok_flag = reinterpret_cast<volatile int*>(full + 2);
+  const int tloc = threadIdx.x / PL::T;
+  const int j = threadIdx.x % PL::T;
+  const long long stride = gridDim.x;
+  std::uint32_t phase[2] = {0u, 0u};
+  bool pending[2] = {false, false};
+  const float2* in2 = reinterpret_cast<const float2*>(in);
+
+  if (threadIdx.x == 0) {
+    tc::mbar_init(&full[0], 1);
+    tc::mbar_init(&full[1], 1);
+    tc::mbar_fence_init();
+    for (int s = 0; s < 2; ++s) {
+      const long long g = blockIdx.x + s * stride;
+      if (g < groups) {
+        tc::mbar_arrive_expect_tx(&full[s], BP::GROUP_BYTES);
+        tc::bulk_load(s ? stage1 : stage0, in2 + g * BP::GROUP, BP::GROUP_BYTES, &full[s]);
+        pending[s] = true;
+      }
+    }
+  }
+  __syncthreads();
+
+  int s = 0;
+  for (long long g = blockIdx.x; g < groups; g += stride, s ^= 1) {
+    float2* st = (s ? stage1 : stage0);
+    if (threadIdx.x == 0) {
+      *ok_flag = tc::mbar_wait(&full[s], phase[s]) ? 1 : 0;
+      pending[s] = false;
+    }
+    __syncthreads();
+    if (!*ok_flag) {
+      if (threadIdx.x == 0) atomicAdd(timeouts, 1u);
+      break;
+    }
+    phase[s] ^= 1u;
+    float2 v[PL::P];
+    float* sre = reinterpret_cast<float*>(st) + tloc * PL::REGION * 2;
+    float* sim = sre + PL::REGION;
+    run_spasses<LOG2N, -1>(v, j, st + tloc * N, sre, sim, tw);
+    __syncthreads();  // every row of the group is in natural order in `st`
+    float2* o = out + g * (PL::TPC * static_cast<long long>(H));
+    constexpr int PAIRS = N / 2 + 1;  // k = 0 .. N/2 with partners N .. N/2
+    for (int i = threadIdx.x; i < PL::TPC * PAIRS; i += PL::THREADS) {
+      const int row = i / PAIRS;
+      const int k = i - row * PAIRS;
+      float2 xk, xnk;
+      r2c_pair(st + row * N, k, N, twl, xk, xnk);
+      o[row * H + k] = xk;
+      if (2 * k != N) o[row * H + N - k] = xnk;
+    }
+    __syncthreads();  // staging buffer read completely
+    if (threadIdx.x == 0) {
+      const long long gn = g + 2 * stride;
+      if (gn < groups) {
+        tc::mbar_arrive_expect_tx(&full[s], BP::GROUP_BYTES);
+        tc::bulk_load(st, in2 + gn * BP::GROUP, BP::GROUP_BYTES, &full[s]);
+        pending[s] = true;
+      }
+    }
+  }
+  if (threadIdx.x == 0) {
+    for (int q = 0; q < 2; ++q)
+      if (pending[q] && !tc::mbar_wait(&full[q], phase[q])) atomicAdd(timeouts, 1u);
+  }
+}
+
+// C2R: the group's half-spectrum rows (N + 1 entries each, not 16-byte aligned in
+// general, so 8-byte cp.async copies) are prefetched two groups ahead into the
+// staging ring; the first pass forms its butterfly inputs Z'[k] from them
+// (c2r_point), and the last pass's output — x[2n] + i x[2n+1] of each row — leaves
+// by one bulk store.
+__device__ __forceinline__ void cp_async8(void* dst_smem, const void* src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(tc::smem_addr(dst_smem)),
+               "l"(src)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() {
+  asm volatile("cp.async.commit_group;" ::: "memory");
+}
+__device__ __forceinline__ void cp_async_wait_one() {
+  asm volatile("cp.async.wait_group 1;" ::: "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+  asm volatile("cp.async.wait_all;" ::: "memory");
+}
+
+// With an even number of rows per group (half length <= 2048) a group's half
+// spectra are 16-byte aligned and a multiple of 16 bytes long, so one bulk copy
+// per group completing on an mbarrier replaces the 8-byte copies.
+template <int LOG2N, bool BULK>
+__global__ void __launch_bounds__(Plan<LOG2N>::THREADS, 3)
+    c2r_bulk_kernel(const float2* in, float* out, long long groups, const float2* __restrict__ tw,
+                    const float2* __restrict__ twl, unsigned int* timeouts) {
+  using PL = Plan<LOG2N>;
+  using BP = BulkPlan<LOG2N>;
+  constexpr int N = PL::N;
+  constexpr int H = N + 1;
+  constexpr int ROWS = PL::TPC * H;  // complex values of a group's half spectra
+  static_assert(ROWS * 8 <= BP::STAGE_BYTES, "half-spectrum rows exceed the staging buffer");
+  static_assert(!BULK || (ROWS * 8) % 16 == 0, "bulk copies need 16-byte multiples");
+  extern __shared__ __align__(16) std::uint8_t bsmem[];
+  float2* stage[2] = {reinterpret_cast<float2*>(bsmem),
+                      reinterpret_cast<float2*>(bsmem + BP::STAGE_BYTES)};
+  std::uint64_t* full = reinterpret_cast<std::uint64_t*>(bsmem + 2 * BP::STAGE_BYTES);
+  volatile int* ok_flag = reinterpret_cast<volatile int*>(full + 2);
+  const int tloc = threadIdx.x / PL::T;
+  const int j = threadIdx.x % PL::T;
+  const long long stride = gridDim.x;
+  float2* out2 = reinterpret_cast<float2*>(out);
+  std::uint32_t phase[2] = {0u, 0u};
+  bool pending[2] = {false, false};
+
+  // BULK: thread 0 issues the copy of group g into stage s; otherwise every thread
+  // copies its share and commits one cp.async group (empty or not, which keeps
+  // the wait counts aligned).
+  auto fetch = [&](int s, long long g) {
+    if constexpr (BULK) {
+      if (threadIdx.x == 0 && g < groups) {
+        tc::mbar_arrive_expect_tx(&full[s], ROWS * 8);
+        tc::bulk_load(stage[s], in + g * ROWS, ROWS * 8, &full[s]);
+        pending[s] = true;
+      }
+    } else {
+      if (g < groups) {
+        const float2* src = in + g * ROWS;
+        for (int i = threadIdx.x; i < ROWS; i += PL::THREADS) cp_async8(stage[s] + i, src + i);
+      }
+      cp_async_commit();
+    }
+  };
+  if constexpr (BULK) {
+    if (threadIdx.x == 0) {
+      tc::mbar_init(&full[0], 1);
+      tc::mbar_init(&full[1], 1);
+      tc::mbar_fence_init();
+    }
+  }
+  fetch(0, blockIdx.x);
+  fetch(1, blockIdx.x + stride);
+  __syncthreads();
+
+  int s = 0;
+  for (long long g = blockIdx.x; g < groups; g += stride, s ^= 1) {
+    float2* st = stage[s];
+    if constexpr (BULK) {
+      if (threadIdx.x == 0) {
+        *ok_flag = tc::mbar_wait(&full[s], phase[s]) ? 1 : 0;
+        pending[s] = false;
+      }
+      __syncthreads();
+      if (!*ok_flag) {
+        if (threadIdx.x == 0) atomicAdd(timeouts, 1u);
+        break;
+      }
+      phase[s] ^= 1u;
+    } else {
+      cp_async_wait_one();  // this thread's copies of group g have landed
+      __syncthreads();      // and everyone else's
+    }
+    float2 v[PL::P];
+    float* sre = reinterpret_cast<float*>(st) + tloc * PL::REGION * 2;
+    float* sim = sre + PL::REGION;
+    run_spasses<LOG2N, 1, true>(v, j, st + tloc * N, sre, sim, tw, st + tloc * H, twl);
+    tc::fence_proxy_async_smem();
+    __syncthreads();  // the whole group's output is in the staging buffer
+    if (threadIdx.x == 0) {
+      tc::bulk_store(out2 + g * BP::GROUP, st, BP::GROUP_BYTES);
+      tc::bulk_wait_read_all();  // the staging buffer may be refilled
+    }
+    if constexpr (BULK) {
+      fetch(s, g + 2 * stride);
+    } else {
+      __syncthreads();  // every thread's refill waits for the store's read
+      fetch(s, g + 2 * stride);
+    }
+  }
+  if constexpr (BULK) {
+    if (threadIdx.x == 0) {
+      for (int q = 0; q < 2; ++q)
+        if (pending[q] && !tc::mbar_wait(&full[q], phase[q])) atomicAdd(timeouts, 1u);
+    }
+  } else {
+    cp_async_wait_all();
+  }
+  if (threadIdx.x == 0) tc::bulk_wait_all();
+}
+
+template <int LOG2N>
+cudaError_t launch_real_bulk_len(bool r2c, const void* in, void* out, long long groups,
+                                 const float2* tw, const float2* twl, unsigned int* timeouts,
+                                 cudaStream_t stream) {
+  using BP = BulkPlan<LOG2N>;
+  const int sms = sm_count(current_device());
+  const long long cap = static_cast<long long>(sms > 0 ? sms : 148) * 3;
+  const unsigned grid = static_cast<unsigned>(groups < cap ? groups : cap);
+  if (r2c) {
+    auto kern = r2c_bulk_kernel<LOG2N>;
+    const cudaError_t e =
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, BP::SMEM);
+    if (e != cudaSuccess) return e;
+    kern<<<grid, Plan<LOG2N>::THREADS, BP::SMEM, stream>>>(
+        static_cast<const float*>(in), static_cast<float2*>(out), groups, tw, twl, timeouts);
+  } else {
+    constexpr bool kBulk = Plan<LOG2N>::TPC % 2 == 0;
+    auto kern = c2r_bulk_kernel<LOG2N, kBulk>;
+    const cudaError_t e =
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, BP::SMEM);
+    if (e != cudaSuccess) return e;
+    kern<<<grid, Plan<LOG2N>::THREADS, BP::SMEM, stream>>>(
+        static_cast<const float2*>(in), static_cast<float*>(out), groups, tw, twl, timeouts);
+  }
+  return cudaGetLastError();
+}
+
 }  // namespace
 
 bool single_pass_supported(std::int64_t n) noexcept {
@@ -578,6 +860,39 @@ cudaError_t launch_stockham(std::int64_t n, int sign, const Batch1D& b,
     }
   }
   return sign < 0 ? dispatch<-1>(log2n, b, stream) : dispatch<1>(log2n, b, stream);
+}
+
+std::int64_t real_bulk_rows_per_group(std::int64_t n) noexcept {
+  return (n >= 16 && n <= 4096 && (n & (n - 1)) == 0) ? 4096 / n : 0;
+}
+
+bool real_bulk_aligned(bool r2c, std::int64_t n, const void* in, const void* out) noexcept {
+  const std::int64_t per = real_bulk_rows_per_group(n);
+  if (per == 0) return false;
+  // C2R groups of an even number of half-spectrum rows are bulk-copied
+  const int in_align = (r2c || per % 2 == 0) ? 16 : 8;
+  return aligned_to(in, in_align) && aligned_to(out, r2c ? 8 : 16);
+}
+
+cudaError_t launch_real_bulk(bool r2c, std::int64_t n, const void* in, void* out,
+                             long long groups, const float2* tw, const float2* twl,
+                             cudaStream_t stream) noexcept {
+  if (!real_bulk_aligned(r2c, n, in, out)) return cudaErrorInvalidValue;
+  if (groups <= 0) return cudaSuccess;
+  unsigned int* to = bulk_timeout_counter();
+  if (to == nullptr) return cudaErrorInvalidValue;
+  switch (__builtin_ctzll(static_cast<unsigned long long>(n))) {
+    case 4: return launch_real_bulk_len<4>(r2c, in, out, groups, tw, twl, to, stream);
+    case 5: return launch_real_bulk_len<5>(r2c, in, out, groups, tw, twl, to, stream);
+    case 6: return launch_real_bulk_len<6>(r2c, in, out, groups, tw, twl, to, stream);
+    case 7: return launch_real_bulk_len<7>(r2c, in, out, groups, tw, twl, to, stream);
+    case 8: return launch_real_bulk_len<8>(r2c, in, out, groups, tw, twl, to, stream);
+    case 9: return launch_real_bulk_len<9>(r2c, in, out, groups, tw, twl, to, stream);
+    case 10: return launch_real_bulk_len<10>(r2c, in, out, groups, tw, twl, to, stream);
+    case 11: return launch_real_bulk_len<11>(r2c, in, out, groups, tw, twl, to, stream);
+    case 12: return launch_real_bulk_len<12>(r2c, in, out, groups, tw, twl, to, stream);
+    default: return cudaErrorInvalidValue;
+  }
 }
 
 }  // namespace mb200::fft

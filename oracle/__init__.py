@@ -296,3 +296,60 @@ def sgemv(trans, m, n, alpha, A, lda, x, incx, beta, y, incy, threads=8):
     lib().oracle_sgemv(1 if trans else 0, m, n, alpha, A.ctypes.data, lda, x.ctypes.data, incx,
                        beta, y.ctypes.data, incy, exact.ctypes.data, absv.ctypes.data, threads)
     return y, exact, absv
+
+
+# ---------------------------------------------------------------- cuFFT R2C / C2R
+def fft_r2c(x, dims, batch, *, istride=1, idist=None, ostride=1, odist=None, threads=8):
+    """Reference R2C (libraries/fft/src/cufft_exec.mm:213-303): gather (x, 0) into dense
+    complex rows (cufft_kernels.metal:43-56), forward C2C over all axes, keep entries
+    0 .. L/2 of the last axis (:58-77).  Returns the float64 result in the output layout."""
+    dims = list(dims)
+    L = dims[-1]
+    H = L // 2 + 1
+    epb = int(np.prod(dims))
+    prefix = epb // L
+    idist = epb if idist is None else idist
+    odist = prefix * H if odist is None else odist
+    x = np.asarray(x, np.float32)
+    dense = np.zeros(batch * epb, np.complex64)
+    for b in range(batch):
+        dense[b * epb:(b + 1) * epb] = x[b * idist + np.arange(epb) * istride]
+    X = fft_c2c(dense, dims, batch, -1, exact=True, threads=threads).reshape(batch, prefix, L)
+    out = np.zeros((batch - 1) * odist + (prefix * H - 1) * ostride + 1, np.complex128)
+    for b in range(batch):
+        out[b * odist + np.arange(prefix * H) * ostride] = X[b, :, :H].reshape(-1)
+    return out
+
+
+def fft_c2r(X, dims, batch, *, istride=1, idist=None, ostride=1, odist=None, threads=8):
+    """Reference C2R (cufft_exec.mm:305-436): gather the half spectrum (cufft_kernels.metal:
+    79-92), inverse C2C over the leading axes, expand each last-axis row by conjugate
+    symmetry (:94-117), inverse C2C of the last axis, keep the real part (:119-132).
+    Returns float64 reals in the output layout (no scaling)."""
+    dims = list(dims)
+    L = dims[-1]
+    H = L // 2 + 1
+    epb = int(np.prod(dims))
+    prefix = epb // L
+    idist = prefix * H if idist is None else idist
+    odist = epb if odist is None else odist
+    X = np.asarray(X, np.complex64)
+    A = np.zeros((batch, prefix * H), np.complex128)
+    for b in range(batch):
+        A[b] = X[b * idist + np.arange(prefix * H) * istride]
+    if len(dims) > 1:
+        for b in range(batch):
+            # leading axes: a (rank-1)-dim transform per last-axis entry h (stride H)
+            A[b] = fft_c2c(A[b].astype(np.complex64), dims[:-1], H, +1, istride=H, idist=1,
+                           ostride=H, odist=1, exact=True, threads=threads)
+    A = A.reshape(batch * prefix, H)
+    full = np.zeros((batch * prefix, L), np.complex128)
+    full[:, :H] = A[:, :min(H, L)]
+    if L > H:
+        full[:, H:] = np.conj(A[:, L - np.arange(H, L)])
+    y = fft_c2c(full.reshape(-1).astype(np.complex64), [L], batch * prefix, +1, exact=True,
+                threads=threads).real.reshape(batch, epb)
+    out = np.zeros((batch - 1) * odist + (epb - 1) * ostride + 1, np.float64)
+    for b in range(batch):
+        out[b * odist + np.arange(epb) * ostride] = y[b]
+    return out

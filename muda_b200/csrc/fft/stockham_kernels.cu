@@ -355,8 +355,7 @@ __device__ unsigned int g_fft_bulk_timeouts;
 // in shared memory: E[k] = X[k] + Xc, O[k] = (X[k] - Xc) conj(W^k), Xc = conj(X[n-k])
 // for k > 0; for k = 0 only the real parts of X[0] and X[n] are used.  W^k is
 // twl[k] = exp(-2*pi*i*k/(2n)).
-__device__ __forceinline__ float2 c2r_point(const float2* raw, int k, int n,
-                                            const float2* __restrict__ twl) {
+__device__ __forceinline__ float2 c2r_point(const float2* raw, int k, int n, float2 w) {
   float2 xk = raw[k];
   float2 xc;
   if (k == 0) {
@@ -367,9 +366,25 @@ __device__ __forceinline__ float2 c2r_point(const float2* raw, int k, int n,
     xc = make_float2(u.x, -u.y);
   }
   const float2 e = cadd(xk, xc);
-  const float2 w = __ldg(twl + k);
   const float2 o = cmul(csub(xk, xc), make_float2(w.x, -w.y));
   return make_float2(e.x - o.y, e.y + o.x);
+}
+
+// a * exp(-2*pi*i * m / 32) for m in [0, 16) known at compile time after unrolling.
+__device__ __forceinline__ float2 rot32(float2 a, int m) {
+  constexpr float kC[16] = {1.0f, 0.9807852506637573f, 0.9238795042037964f, 0.8314695954322815f,
+                            0.7071067690849304f, 0.5555702447891235f, 0.3826834261417389f,
+                            0.19509032368659973f, 0.0f, -0.19509032368659973f,
+                            -0.3826834261417389f, -0.5555702447891235f, -0.7071067690849304f,
+                            -0.8314695954322815f, -0.9238795042037964f, -0.9807852506637573f};
+  constexpr float kS[16] = {0.0f, 0.19509032368659973f, 0.3826834261417389f, 0.5555702447891235f,
+                            0.7071067690849304f, 0.8314695954322815f, 0.9238795042037964f,
+                            0.9807852506637573f, 1.0f, 0.9807852506637573f, 0.9238795042037964f,
+                            0.8314695954322815f, 0.7071067690849304f, 0.5555702447891235f,
+                            0.3826834261417389f, 0.19509032368659973f};
+  if (m == 0) return a;
+  if (m == 8) return make_float2(a.y, -a.x);  // times -i
+  return cmul(a, make_float2(kC[m], -kS[m]));
 }
 
 // Pass of the staged kernel: FIRST reads the staging buffer `st` (for PRE, the
@@ -387,11 +402,15 @@ __device__ __forceinline__ void spass(float2 (&v)[Plan<LOG2N>::P], int j, int Ns
 #pragma unroll
   for (int q = 0; q < NB; ++q) {
     const int b = j + q * T;
+    // PRE: the points idx = b + r*N/R of this butterfly need W^idx = W^b * exp(-pi*i*r/R)
+    // (W = exp(-2*pi*i/(2N))): one table read, the rest compile-time rotations
+    float2 wb = make_float2(1.0f, 0.0f);
+    if constexpr (FIRST && PRE) wb = __ldg(twl + b);
 #pragma unroll
     for (int r = 0; r < R; ++r) {
       const int idx = b + r * (N / R);
       if constexpr (FIRST && PRE) {
-        v[q * R + r] = c2r_point(raw, idx, N, twl);
+        v[q * R + r] = c2r_point(raw, idx, N, rot32(wb, r * (16 / R)));
       } else {
         v[q * R + r] = FIRST ? st[idx] : make_float2(sre[pad(idx)], sim[pad(idx)]);
       }

@@ -473,6 +473,47 @@ def suite_fft(s: Suite) -> dict:
     return out
 
 
+def suite_fft_bluestein(s: Suite) -> dict:
+    """C2C of a length that is not a power of two: N = 1000, batch 262144, normal(0,1)
+    re/im seed 4, forward then inverse in place (Bluestein, inner length 2048 on chip);
+    value = bytes moved (read + write, both directions) per second."""
+    from muda_b200 import capi, synth
+    torch = s.torch
+    n, batch = 1000, 262144 // s.scale
+    x = synth.normal(torch, 2 * n * batch, seed=4)
+    L = capi.cufft()
+    p = C.c_void_p()
+    nn = (C.c_int * 1)(n)
+    assert L.cufftPlanMany(C.byref(p), 1, nn, None, 1, n, None, 1, n, capi.CUFFT_C2C, batch) == 0
+    assert L.cufftSetStream(p, s.sp) == 0
+    ptr = C.c_void_p(x.data_ptr())
+
+    def call():
+        assert L.cufftExecC2C(p, ptr, ptr, -1) == 0
+        assert L.cufftExecC2C(p, ptr, ptr, 1) == 0
+    ms, launches = s.time(call, launches_per_call=2)
+    assert L.cufftDestroy(p) == 0
+    per_dir = 2 * 8 * n * batch
+    gbs = 2 * per_dir / (ms * 1e-3) / 1e9
+    out = {"value": gbs, "unit": "GB/s", "ms": ms, "dtype": "c64",
+           "gflops_5nlogn": 2 * 5 * n * np.log2(n) * batch / (ms * 1e-3) / 1e9,
+           "config": f"N {n} x batch {batch}, forward + inverse in place, "
+                     f"data {per_dir / 2e9:.2f} GB > L2",
+           "roofline": s.roof("bluestein_kernel<11>", gbs, "hbm"), "launches": launches,
+           "algorithmic_bytes_per_launch": per_dir}
+    if s.cpu:
+        import oracle
+        sample = max(1, batch // 4096)
+        xs = x[: 2 * n * sample].cpu().numpy().view(np.complex64)
+        dt = cpu_time(lambda: oracle.fft_c2c(xs, [n], sample, -1, threads=os.cpu_count() or 1))
+        out["cpu_baseline"] = {"value": (2 * 8 * n * sample) / dt / 1e9, "unit": "GB/s",
+                               "cores": os.cpu_count(), "kind": "port",
+                               "sample": f"forward transform of {sample} of {batch} sequences, "
+                                         "oracle/fft.cpp direct DFT (the reference's algorithm "
+                                         "for this length)"}
+    return out
+
+
 def suite_fft_real(s: Suite) -> dict:
     """R2C then C2R of L = 4096 reals, batch 65536, normal(0,1) seed 5, out of place
     (reals -> half spectrum -> reals); value = algorithmic bytes (reals and half spectrum,
@@ -745,6 +786,7 @@ SUITE = {
     "spmv": suite_spmv,
     "fft": suite_fft,
     "fft_real": suite_fft_real,
+    "fft_bluestein": suite_fft_bluestein,
     "softmax": suite_softmax,
     "gemm_bf16": suite_gemm_bf16,
     "conv_bf16": lambda s: suite_conv(s, "bf16"),

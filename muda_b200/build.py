@@ -37,6 +37,7 @@ LIBS: dict[str, list[str]] = {
               "dnn/conv_tc_kernels.cu", "dnn/conv_dispatch.cu", "blas/tf32_split.cu"],
     "cusparse": ["sparse/cusparse_api.cpp", "sparse/spmv_kernels.cu"],
     "cufft": ["fft/cufft_api.cpp", "fft/stockham_kernels.cu", "fft/dft_kernels.cu",
+              "fft/bluestein_kernels.cu",
               "fft/fft_static.cu", "fft/real_kernels.cu"],
     "cublas": ["blas/cublas_api.cpp", "blas/gemm_simt_kernels.cu", "blas/gemm_tc_kernels.cu",
                "blas/tf32_split.cu", "blas/level12_kernels.cu"],

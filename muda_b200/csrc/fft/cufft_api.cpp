@@ -46,20 +46,41 @@ constexpr std::size_t kSplitWorkspaceBytes = std::size_t{256} << 20;
 bool is_pow2(std::int64_t n) { return n > 0 && (n & (n - 1)) == 0; }
 
 // How one axis of length n is transformed.
-enum class AxisKind { kTrivial, kSinglePass, kDirect, kSplit };
+enum class AxisKind {
+  kTrivial, kSinglePass, kDirect, kBluestein, kBluesteinGlobal, kSplit, kUnsupported
+};
 
 AxisKind axis_kind(std::int64_t n) {
   if (n == 1) return AxisKind::kTrivial;
   if (mb200::fft::single_pass_supported(n)) return AxisKind::kSinglePass;
-  if (!is_pow2(n) && n <= mb200::fft::kMaxDirect) return AxisKind::kDirect;
+  if (!is_pow2(n) && n < mb200::fft::kMinBluestein) return AxisKind::kDirect;
+  if (!is_pow2(n) && n <= mb200::fft::kMaxBluestein) return AxisKind::kBluestein;
+  if (!is_pow2(n) && n <= mb200::fft::kMaxBluesteinGlobal) return AxisKind::kBluesteinGlobal;
   if (is_pow2(n) && n <= kMaxSplit) return AxisKind::kSplit;
-  return AxisKind::kTrivial;  // unsupported; rejected by plan()
+  return AxisKind::kUnsupported;
 }
 
-bool axis_supported(std::int64_t n) {
-  return n == 1 || mb200::fft::single_pass_supported(n) ||
-         (!is_pow2(n) && n <= mb200::fft::kMaxDirect) || (is_pow2(n) && n <= kMaxSplit);
+bool axis_supported(std::int64_t n) { return axis_kind(n) != AxisKind::kUnsupported; }
+
+// True when run_axis transforms an axis of length n for any Batch1D layout (the
+// power-of-two split is a rank-1 plan of its own).
+bool one_pass(std::int64_t n) {
+  const AxisKind k = axis_kind(n);
+  return k == AxisKind::kTrivial || k == AxisKind::kSinglePass || k == AxisKind::kDirect ||
+         k == AxisKind::kBluestein || k == AxisKind::kBluesteinGlobal;
 }
+
+// Workspace per global-memory Bluestein axis (chunks of transforms).
+constexpr std::size_t kBluesteinWsBytes = std::size_t{256} << 20;
+
+// Tables the transform of one axis reads.
+struct AxisTables {
+  const float2* tw = nullptr;     // exp(-2*pi*i*m/n): single-pass and direct axes
+  const float2* chirp = nullptr;  // Bluestein axes: chirp, FFT of the chirp filter,
+  const float2* bhat = nullptr;   // and the inner length's twiddles
+  const float2* tw_m = nullptr;
+  mb200::fft::BluesteinGlobal glob{};  // longer Bluestein axes: tables and workspace
+};
 
 // Twiddle tables exp(-2*pi*i*m/n), shared per (device, n).
 mb200::LruCache<std::pair<int, std::int64_t>, DeviceBuffer>& twiddle_cache() {
@@ -84,6 +105,27 @@ std::shared_ptr<DeviceBuffer> twiddles(std::int64_t n) {
   return buf;
 }
 
+// Bluestein tables of length n (chirp, then bhat at an even offset), shared per
+// (device, n) in the twiddle cache under the key (device, -n).
+std::shared_ptr<DeviceBuffer> bluestein_tables(std::int64_t n) {
+  const int dev = mb200::current_device();
+  auto key = std::make_pair(dev, -n);
+  if (auto hit = twiddle_cache().find(key)) return hit;
+  const std::int64_t mb = mb200::fft::bluestein_length(n);
+  const std::int64_t off = (n + 1) / 2 * 2;
+  auto buf = DeviceBuffer::make(static_cast<std::size_t>(off + mb) * sizeof(float2));
+  if (!buf) return nullptr;
+  std::vector<float2> host(static_cast<std::size_t>(off + mb));
+  mb200::fft::host_bluestein_tables(n, mb, host.data(), host.data() + off);
+  if (cudaMemcpy(buf->ptr, host.data(), host.size() * sizeof(float2), cudaMemcpyHostToDevice) !=
+      cudaSuccess) {
+    (void)cudaGetLastError();
+    return nullptr;
+  }
+  twiddle_cache().put(key, buf);
+  return buf;
+}
+
 struct Plan {
   std::mutex mu;
   bool configured = false;
@@ -95,7 +137,7 @@ struct Plan {
   cudaStream_t stream = nullptr;
   int device = -1;
   std::vector<std::shared_ptr<DeviceBuffer>> tables;  // keeps twiddles alive
-  std::array<const float2*, 3> axis_tw{};              // per axis
+  std::array<AxisTables, 3> axis_tw{};                 // per axis
   // two-pass split of a long power-of-two axis (rank 1 only)
   std::int64_t n1 = 0, n2 = 0;
   const float2* tw_n1 = nullptr;
@@ -109,6 +151,7 @@ struct Plan {
   bool packed = false;          // even L with unit-stride reals: length-M complex FFT
   const float2* tw_L = nullptr;  // exp(-2*pi*i*m/L)
   const float2* tw_M = nullptr;
+  AxisTables ax_L, ax_M;         // transforms of length L (general path) and M (packed)
   std::shared_ptr<DeviceBuffer> real_ws;
 };
 
@@ -144,10 +187,6 @@ cufftResult configure(Plan& p, int rank, const int* n, const int* inembed, int i
   const std::int64_t herm_total = total / L * H;
   if (real) {
     // every complex transform a real plan runs must take one pass (no split)
-    auto one_pass = [](std::int64_t n) {
-      const AxisKind k = axis_kind(n);
-      return n == 1 || k == AxisKind::kSinglePass || k == AxisKind::kDirect;
-    };
     for (int i = 0; i + 1 < rank; ++i)
       if (!one_pass(dims[i])) return CUFFT_NOT_SUPPORTED;
     const bool packed_ok = L % 2 == 0 && L >= 4 && one_pass(L / 2);
@@ -184,38 +223,83 @@ cufftResult configure(Plan& p, int rank, const int* n, const int* inembed, int i
   p.odist = eod;
   p.device = mb200::current_device();
   p.work_bytes = 0;
-  auto hold = [&](std::int64_t len) -> const float2* {
-    auto t = twiddles(len);
+  auto keep = [&](std::shared_ptr<DeviceBuffer> t) -> const float2* {
     if (!t) return nullptr;
     p.tables.push_back(t);
     p.work_bytes += t->bytes;
     return static_cast<const float2*>(t->ptr);
   };
-  for (int i = 0; i < rank; ++i) {
-    p.axis_tw[i] = nullptr;
-    if (real && i == rank - 1) continue;  // the last axis of a real plan: below
-    if (axis_kind(dims[i]) == AxisKind::kSinglePass || axis_kind(dims[i]) == AxisKind::kDirect) {
-      p.axis_tw[i] = hold(dims[i]);
-      if (p.axis_tw[i] == nullptr) return CUFFT_ALLOC_FAILED;
+  auto hold = [&](std::int64_t len) { return keep(twiddles(len)); };
+  // the tables (and workspace) a transform of length len over `count` rows needs
+  auto axis_tables = [&](std::int64_t len, std::int64_t count, AxisTables& t) -> bool {
+    t = AxisTables{};
+    switch (axis_kind(len)) {
+      case AxisKind::kSinglePass:
+      case AxisKind::kDirect:
+        t.tw = hold(len);
+        return t.tw != nullptr;
+      case AxisKind::kBluestein: {
+        t.tw_m = hold(mb200::fft::bluestein_length(len));
+        t.chirp = keep(bluestein_tables(len));
+        t.bhat = t.chirp ? t.chirp + (len + 1) / 2 * 2 : nullptr;
+        return t.tw_m != nullptr && t.chirp != nullptr;
+      }
+      case AxisKind::kBluesteinGlobal: {
+        const std::int64_t mb = mb200::fft::bluestein_length(len);
+        auto& g = t.glob;
+        g.tw_m = hold(mb);
+        g.chirp = keep(bluestein_tables(len));
+        if (g.tw_m == nullptr || g.chirp == nullptr) return false;
+        g.bhat = g.chirp + (len + 1) / 2 * 2;
+        const std::int64_t row_bytes = mb * static_cast<std::int64_t>(sizeof(float2));
+        g.ws_rows = std::max<std::int64_t>(
+            1, std::min<std::int64_t>(count, static_cast<std::int64_t>(kBluesteinWsBytes) /
+                                                 row_bytes));
+        const auto bytes = static_cast<std::size_t>(g.ws_rows * row_bytes);
+        g.ws = const_cast<float2*>(keep(DeviceBuffer::make(bytes)));
+        if (g.ws == nullptr) return false;
+        if (mb > mb200::fft::kMaxSinglePass) {
+          int l = 0;
+          while ((std::int64_t{1} << l) < mb) ++l;
+          g.n1 = std::int64_t{1} << (l / 2);
+          g.n2 = mb / g.n1;
+          g.tw_n1 = hold(g.n1);
+          g.tw_n2 = hold(g.n2);
+          g.ws2 = const_cast<float2*>(keep(DeviceBuffer::make(bytes)));
+          if (g.tw_n1 == nullptr || g.tw_n2 == nullptr || g.ws2 == nullptr) return false;
+        }
+        return true;
+      }
+      default:
+        return true;
     }
+  };
+  for (int i = 0; i < rank; ++i) {
+    p.axis_tw[i] = AxisTables{};
+    if (real && i == rank - 1) continue;  // the last axis of a real plan: below
+    const std::int64_t count = batch * (real ? herm_total : total) / dims[i];
+    if (!axis_tables(dims[i], count, p.axis_tw[i])) return CUFFT_ALLOC_FAILED;
   }
   if (real) {
     p.L = L;
     p.H = H;
     p.M = L / 2;
     p.prefix = total / L;
-    const AxisKind km = axis_kind(p.M);
-    const bool packed_ok =
-        L % 2 == 0 && L >= 4 && (km == AxisKind::kSinglePass || km == AxisKind::kDirect);
+    const bool packed_ok = L % 2 == 0 && L >= 4 && one_pass(p.M);
     p.packed = packed_ok && (type == CUFFT_R2C ? (eis == 1 && eid % 2 == 0)
                                                : (eos == 1 && eod % 2 == 0));
+    p.tw_L = p.tw_M = nullptr;
+    p.ax_L = p.ax_M = AxisTables{};
     if (L > 1) {
+      // the post-/pre-passes read exp(-2*pi*i*m/L) whatever the kind of L
       p.tw_L = hold(L);
       if (p.tw_L == nullptr) return CUFFT_ALLOC_FAILED;
+      // the general path (odd L, strided or 4-byte aligned reals) transforms length L
+      if (one_pass(L) && !axis_tables(L, batch * p.prefix, p.ax_L)) return CUFFT_ALLOC_FAILED;
     }
     if (packed_ok) {
-      p.tw_M = hold(p.M);
-      if (p.tw_M == nullptr) return CUFFT_ALLOC_FAILED;
+      if (!axis_tables(p.M, batch * p.prefix, p.ax_M)) return CUFFT_ALLOC_FAILED;
+      p.tw_M = p.ax_M.tw;  // the fused kernels' table (power-of-two M)
     }
     const std::int64_t rows = batch * p.prefix;
     const std::int64_t need =
@@ -247,19 +331,23 @@ cufftResult configure(Plan& p, int rank, const int* n, const int* inembed, int i
   return CUFFT_SUCCESS;
 }
 
-cudaError_t run_axis(std::int64_t n, int sign, const Batch1D& b, const float2* tw,
+cudaError_t run_axis(std::int64_t n, int sign, const Batch1D& b, const AxisTables& t,
                      cudaStream_t st) {
   switch (axis_kind(n)) {
     case AxisKind::kSinglePass: {
       Batch1D c = b;
-      c.tw = tw;
+      c.tw = t.tw;
       return mb200::fft::launch_stockham(n, sign, c, st);
     }
     case AxisKind::kDirect: {
       Batch1D c = b;
-      c.tw = tw;
+      c.tw = t.tw;
       return mb200::fft::launch_direct_dft(n, sign, c, st);
     }
+    case AxisKind::kBluestein:
+      return mb200::fft::launch_bluestein(n, sign, b, t.chirp, t.bhat, t.tw_m, st);
+    case AxisKind::kBluesteinGlobal:
+      return mb200::fft::launch_bluestein_global(n, sign, b, t.glob, st);
     default:
       return cudaErrorInvalidValue;
   }
@@ -316,7 +404,7 @@ cudaError_t run_split(const Plan& p, const float2* in, float2* out, int sign, cu
 // is, batch distance id) and writes `out` (os, od); the later ones run in place on
 // `out`.  *moved reports whether any axis had length > 1.
 cudaError_t run_axes(int rank, const std::array<std::int64_t, 3>& dims, int a_hi,
-                     const std::array<const float2*, 3>& tw, const float2* in, std::int64_t is,
+                     const std::array<AxisTables, 3>& tw, const float2* in, std::int64_t is,
                      std::int64_t id, float2* out, std::int64_t os, std::int64_t od,
                      std::int64_t batch, int sign, cudaStream_t st, bool* moved) {
   cudaError_t e = cudaSuccess;
@@ -610,7 +698,7 @@ cufftResult cufftExecR2C(cufftHandle plan, cufftReal* idata, cufftComplex* odata
       Batch1D f = dense_rows(*p, Z, p->M);
       f.in = reinterpret_cast<const float2*>(idata) + done * p->M;
       f.batch = rows - done;
-      e = run_axis(p->M, -1, f, p->tw_M, st);
+      e = run_axis(p->M, -1, f, p->ax_M, st);
       const mb200::fft::RealRows rr{rows - done, 1, p->M, p->tw_L};
       if (e == cudaSuccess)
         e = mb200::fft::launch_r2c_post(rr, Z, odata + done * p->H, p->H, 1, st);
@@ -619,7 +707,7 @@ cufftResult cufftExecR2C(cufftHandle plan, cufftReal* idata, cufftComplex* odata
     float2* Z = real_workspace(*p, rows * p->M);
     if (Z == nullptr) return CUFFT_ALLOC_FAILED;
     Batch1D f = pair_rows(*p, reinterpret_cast<const float2*>(idata), p->idist / 2, Z, 0, true);
-    e = run_axis(p->M, -1, f, p->tw_M, st);
+    e = run_axis(p->M, -1, f, p->ax_M, st);
     const mb200::fft::RealRows rr{rows, p->prefix, p->M, p->tw_L};
     if (e == cudaSuccess) e = mb200::fft::launch_r2c_post(rr, Z, odata, p->odist, p->ostride, st);
   } else {
@@ -628,7 +716,7 @@ cufftResult cufftExecR2C(cufftHandle plan, cufftReal* idata, cufftComplex* odata
     e = mb200::fft::launch_gather_real(rows, p->prefix, p->L, idata, p->idist, p->istride, A, st);
     if (e == cudaSuccess && p->L > 1) {
       Batch1D b = dense_rows(*p, A, p->L);
-      e = run_axis(p->L, -1, b, p->tw_L, st);
+      e = run_axis(p->L, -1, b, p->ax_L, st);
     }
     if (e == cudaSuccess)
       e = mb200::fft::launch_scatter_half(rows, p->prefix, p->L, A, odata, p->odist, p->ostride,
@@ -701,14 +789,14 @@ cufftResult cufftExecC2R(cufftHandle plan, cufftComplex* idata, cufftReal* odata
         Batch1D b = dense_rows(*p, Z, p->M);
         b.out = reinterpret_cast<float2*>(odata) + done * p->M;
         b.batch = rows - done;
-        e = run_axis(p->M, +1, b, p->tw_M, st);
+        e = run_axis(p->M, +1, b, p->ax_M, st);
       }
     } else if (e == cudaSuccess && done == 0) {
       const mb200::fft::RealRows rr{rows, p->prefix, p->M, p->tw_L};
       e = mb200::fft::launch_c2r_pre(rr, src, sdist, sstr, Z, st);
       if (e == cudaSuccess) {
         Batch1D b = pair_rows(*p, Z, 0, reinterpret_cast<float2*>(odata), p->odist / 2, false);
-        e = run_axis(p->M, +1, b, p->tw_M, st);
+        e = run_axis(p->M, +1, b, p->ax_M, st);
       }
     }
   } else {
@@ -724,7 +812,7 @@ cufftResult cufftExecC2R(cufftHandle plan, cufftComplex* idata, cufftReal* odata
     if (e == cudaSuccess) e = mb200::fft::launch_expand_half(rows, p->L, A, B, st);
     if (e == cudaSuccess && p->L > 1) {
       Batch1D b = dense_rows(*p, B, p->L);
-      e = run_axis(p->L, +1, b, p->tw_L, st);
+      e = run_axis(p->L, +1, b, p->ax_L, st);
     }
     if (e == cudaSuccess)
       e = mb200::fft::launch_scatter_real(rows, p->prefix, p->L, B, odata, p->odist, p->ostride,

@@ -9,6 +9,8 @@
 
 #include <cmath>
 #include <cstdint>
+#include <utility>
+#include <vector>
 
 #include "common/device.hpp"
 #include "fft/fft.hpp"
@@ -88,6 +90,66 @@ void host_twiddles(std::int64_t n, float2* tw) noexcept {
     const double a = two_pi * static_cast<double>(m) / static_cast<double>(n);
     tw[m].x = static_cast<float>(std::cos(a));
     tw[m].y = static_cast<float>(-std::sin(a));
+  }
+}
+
+// chirp[m] = exp(-pi*i*q/n) with q = m^2 mod 2n taken in integers, so the angle
+// is exact before the one rounding; bhat = FFT(b) / mb by an in-place iterative
+// radix-2 transform in double precision (host), rounded once.
+void host_bluestein_tables(std::int64_t n, std::int64_t mb, float2* chirp, float2* bhat) noexcept {
+  const double pi = 3.141592653589793238462643383279;
+  std::vector<double> re(static_cast<std::size_t>(mb), 0.0), im(static_cast<std::size_t>(mb), 0.0);
+  for (std::int64_t m = 0; m < n; ++m) {
+    const std::int64_t q = static_cast<std::int64_t>(
+        (static_cast<unsigned long long>(m) * static_cast<unsigned long long>(m)) %
+        static_cast<unsigned long long>(2 * n));
+    const double a = pi * static_cast<double>(q) / static_cast<double>(n);
+    const double c = std::cos(a), sn = std::sin(a);
+    chirp[m].x = static_cast<float>(c);
+    chirp[m].y = static_cast<float>(-sn);
+    // b[m] = conj(chirp[m]) = exp(+pi*i*q/n), mirrored to mb - m
+    re[static_cast<std::size_t>(m)] = c;
+    im[static_cast<std::size_t>(m)] = sn;
+    if (m > 0) {
+      re[static_cast<std::size_t>(mb - m)] = c;
+      im[static_cast<std::size_t>(mb - m)] = sn;
+    }
+  }
+  // bit-reversal permutation, then log2(mb) butterfly stages with exp(-2*pi*i*k/len)
+  for (std::int64_t i = 1, j = 0; i < mb; ++i) {
+    std::int64_t bit = mb >> 1;
+    for (; j & bit; bit >>= 1) j ^= bit;
+    j ^= bit;
+    if (i < j) {
+      std::swap(re[static_cast<std::size_t>(i)], re[static_cast<std::size_t>(j)]);
+      std::swap(im[static_cast<std::size_t>(i)], im[static_cast<std::size_t>(j)]);
+    }
+  }
+  for (std::int64_t len = 2; len <= mb; len <<= 1) {
+    const std::int64_t half = len / 2;
+    std::vector<double> wr(static_cast<std::size_t>(half)), wi(static_cast<std::size_t>(half));
+    for (std::int64_t k = 0; k < half; ++k) {
+      const double a = 2.0 * pi * static_cast<double>(k) / static_cast<double>(len);
+      wr[static_cast<std::size_t>(k)] = std::cos(a);
+      wi[static_cast<std::size_t>(k)] = -std::sin(a);
+    }
+    for (std::int64_t s0 = 0; s0 < mb; s0 += len) {
+      for (std::int64_t k = 0; k < half; ++k) {
+        const std::size_t u = static_cast<std::size_t>(s0 + k);
+        const std::size_t v = static_cast<std::size_t>(s0 + k + half);
+        const double xr = re[v] * wr[static_cast<std::size_t>(k)] - im[v] * wi[static_cast<std::size_t>(k)];
+        const double xi = re[v] * wi[static_cast<std::size_t>(k)] + im[v] * wr[static_cast<std::size_t>(k)];
+        re[v] = re[u] - xr;
+        im[v] = im[u] - xi;
+        re[u] += xr;
+        im[u] += xi;
+      }
+    }
+  }
+  const double inv = 1.0 / static_cast<double>(mb);
+  for (std::int64_t k = 0; k < mb; ++k) {
+    bhat[k].x = static_cast<float>(re[static_cast<std::size_t>(k)] * inv);
+    bhat[k].y = static_cast<float>(im[static_cast<std::size_t>(k)] * inv);
   }
 }
 

@@ -47,6 +47,40 @@ cudaError_t launch_direct_dft(std::int64_t n, int sign, const Batch1D& b,
 // Fills tw[0 .. n) with exp(-2*pi*i*m/n) rounded from double precision.
 void host_twiddles(std::int64_t n, float2* tw) noexcept;
 
+// Bluestein (chirp-z) transforms of a length n that is not a power of two, for n in
+// [kMinBluestein, kMaxBluestein]: one kernel per call, both inner length-Mb FFTs
+// (Mb = bluestein_length(n), the power of two >= 2n - 1) on chip.  Tables of the
+// forward direction: chirp[m] = exp(-pi*i*(m^2 mod 2n)/n), m < n; bhat = FFT(b) / Mb
+// with b[m] = b[Mb - m] = conj(chirp[m]) and zeros between; tw_m = exp(-2*pi*i*m/Mb).
+// In-place calls (same layout) are allowed; post_tw must be null.
+constexpr std::int64_t kMinBluestein = 32;
+constexpr std::int64_t kMaxBluestein = 4096;
+std::int64_t bluestein_length(std::int64_t n) noexcept;
+cudaError_t launch_bluestein(std::int64_t n, int sign, const Batch1D& b, const float2* chirp,
+                             const float2* bhat, const float2* tw_m,
+                             cudaStream_t stream) noexcept;
+// Longer lengths (kMaxBluestein < n <= kMaxBluesteinGlobal) run Bluestein through
+// global memory, chunk by chunk of ws_rows transforms: chirp-multiplied gather into
+// dense rows of Mb, forward FFT, multiply by bhat, inverse FFT, chirp-multiplied
+// scatter.  An inner length above kMaxSinglePass uses the two-pass split
+// Mb = n1 * n2 with the scratch rows ws2.  In-place calls are allowed.
+constexpr std::int64_t kMaxBluesteinGlobal = std::int64_t{1} << 20;
+struct BluesteinGlobal {
+  const float2* chirp;
+  const float2* bhat;
+  const float2* tw_m;  // exp(-2*pi*i*m/Mb)
+  float2* ws;          // ws_rows * Mb
+  float2* ws2;         // ws_rows * Mb when Mb > kMaxSinglePass, else null
+  std::int64_t ws_rows;
+  std::int64_t n1, n2;
+  const float2* tw_n1;
+  const float2* tw_n2;
+};
+cudaError_t launch_bluestein_global(std::int64_t n, int sign, const Batch1D& b,
+                                    const BluesteinGlobal& g, cudaStream_t stream) noexcept;
+// Fills chirp[0 .. n) and bhat[0 .. Mb) in double precision, rounded once.
+void host_bluestein_tables(std::int64_t n, std::int64_t mb, float2* chirp, float2* bhat) noexcept;
+
 // Real-data transforms of even length L = 2M through a length-M complex FFT of
 // the reals read as M complex pairs, z[n] = x[2n] + i x[2n+1].  Rows are indexed
 // r = b * prefix + p (b the batch entry, p the position along the leading axes).

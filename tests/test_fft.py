@@ -180,6 +180,71 @@ def test_gpu_non_pow2_lengths(cuda, built, n):
         assert rel_l2_per_transform(got, want, n, batch) <= TOL
 
 
+# Lengths that are not powers of two: below 32 the direct DFT, 32 .. 4096 the fused
+# Bluestein kernel (inner lengths 64 .. 8192), above that Bluestein through global memory.
+BLUESTEIN = [31, 33, 47, 97, 127, 255, 257, 1000, 1023, 2047, 2049, 3000, 4095, 4097, 6000]
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("n", [4097, 8191, 10007, 100003, (1 << 20) - 1])
+def test_gpu_bluestein_global_lengths(cuda, built, n):
+    """Global-memory Bluestein (inner lengths 16384 .. 2^21, the longer ones through the
+    two-pass split) against numpy's float64 FFT, both directions."""
+    rng = np.random.default_rng(n)
+    batch = max(2, (1 << 21) // n)
+    x = rand_c64(rng, n * batch)
+    xd = x.reshape(batch, n).astype(np.complex128)
+    for sign in (-1, 1):
+        got = gpu_fft(cuda, x, [n], batch, sign)
+        want = (np.fft.fft(xd, axis=1) if sign < 0 else np.fft.ifft(xd, axis=1) * n).reshape(-1)
+        assert rel_l2_per_transform(got, want, n, batch) <= TOL
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("n", BLUESTEIN)
+def test_gpu_bluestein_lengths(cuda, built, n):
+    """Batches that fill several transforms per CTA plus a partial last CTA, both
+    directions, against the double-precision oracle."""
+    rng = np.random.default_rng(n + 1)
+    batch = max(2, min(40, (1 << 15) // n)) + 1
+    x = rand_c64(rng, n * batch)
+    for sign in (-1, 1):
+        got = gpu_fft(cuda, x, [n], batch, sign)
+        want = oracle.fft_c2c(x, [n], batch, sign, exact=True)
+        assert rel_l2_per_transform(got, want, n, batch) <= TOL
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("n", [60, 1000])
+def test_gpu_bluestein_in_place_and_strided(cuda, built, n):
+    rng = np.random.default_rng(n + 2)
+    batch = 6
+    x = rand_c64(rng, n * batch)
+    got = gpu_fft(cuda, x, [n], batch, -1, inplace=True)
+    want = oracle.fft_c2c(x, [n], batch, -1, exact=True)
+    assert rel_l2_per_transform(got, want, n, batch) <= TOL
+    istride, idist, ostride, odist = 2, 2 * n + 3, 3, 3 * n + 1
+    x = rand_c64(rng, (batch - 1) * idist + (n - 1) * istride + 1)
+    out_len = (batch - 1) * odist + (n - 1) * ostride + 1
+    got = gpu_fft(cuda, x, [n], batch, 1, inembed=[n], istride=istride, idist=idist,
+                  onembed=[n], ostride=ostride, odist=odist, out_len=out_len)
+    want = oracle.fft_c2c(x, [n], batch, 1, istride=istride, idist=idist, ostride=ostride,
+                          odist=odist, out_len=out_len, exact=True)
+    assert rel_l2_per_transform(got, want, n, batch, odist, ostride) <= TOL
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("dims", [[100, 60], [33, 5, 40], [48, 1000], [3, 5000]])
+def test_gpu_bluestein_multi_dim(cuda, built, dims):
+    rng = np.random.default_rng(sum(dims))
+    n, batch = int(np.prod(dims)), 2
+    x = rand_c64(rng, n * batch)
+    for sign in (-1, 1):
+        got = gpu_fft(cuda, x, dims, batch, sign)
+        want = oracle.fft_c2c(x, dims, batch, sign, exact=True)
+        assert rel_l2_per_transform(got, want, n, batch) <= TOL
+
+
 @pytest.mark.gpu
 @pytest.mark.parametrize("n", [32768, 1 << 20])
 def test_gpu_large_pow2_split(cuda, built, n):

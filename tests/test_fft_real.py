@@ -84,7 +84,8 @@ def dev_floats(torch, a, offset=0):
 CASES = [  # dims, batch
     ([128], 1), ([4096], 7), ([60], 5), ([1000], 3), ([15], 4), ([2], 3), ([16384], 2),
     ([6, 10], 2), ([16, 32], 3), ([4, 3, 8], 2), ([8, 8, 8], 1), ([7, 9], 2), ([1, 64], 2),
-    ([32], 300), ([64], 200), ([8192], 5), ([512], 40), ([64, 256], 2), ([4, 8, 512], 3)]
+    ([32], 300), ([64], 200), ([8192], 5), ([512], 40), ([64, 256], 2), ([4, 8, 512], 3),
+    ([10000], 2), ([5001], 2)]
 
 
 @pytest.mark.gpu

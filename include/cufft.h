@@ -65,6 +65,12 @@ typedef struct cufftContext* cufftHandle;
 /* Plans — reference cufft_plan.mm:157-318 */
 cufftResult cufftCreate(cufftHandle* handle);
 cufftResult cufftPlan1d(cufftHandle* plan, int nx, cufftType type, int batch);
+/* 2-D / 3-D plans (nx outermost, batch 1) — reference cufft_plan.mm:179-196, 227-261 */
+cufftResult cufftPlan2d(cufftHandle* plan, int nx, int ny, cufftType type);
+cufftResult cufftPlan3d(cufftHandle* plan, int nx, int ny, int nz, cufftType type);
+cufftResult cufftMakePlan2d(cufftHandle plan, int nx, int ny, cufftType type, size_t* workSize);
+cufftResult cufftMakePlan3d(cufftHandle plan, int nx, int ny, int nz, cufftType type,
+                            size_t* workSize);
 cufftResult cufftPlanMany(cufftHandle* plan, int rank, int* n, int* inembed, int istride, int idist,
                           int* onembed, int ostride, int odist, cufftType type, int batch);
 cufftResult cufftMakePlan1d(cufftHandle plan, int nx, cufftType type, int batch, size_t* workSize);

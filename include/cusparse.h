@@ -1,5 +1,5 @@
 /*
- * cusparse.h — C ABI of the B200-native CSR SpMV.
+ * cusparse.h — C ABI of the B200-native CSR SpMV and SpMM.
  *
  * Drop-in for the MUDA cuSPARSE shim's hot path: names, argument lists and
  * numeric enum values follow libraries/sparse/include/cusparse.h of the
@@ -60,12 +60,23 @@ typedef enum {
   CUSPARSE_SPMV_CSR_ALG2 = 3
 } cusparseSpMVAlg_t;
 
+/* reference cusparse.h:64 and :78-82 */
+typedef enum { CUSPARSE_ORDER_COL = 1, CUSPARSE_ORDER_ROW = 2 } cusparseOrder_t;
+
+typedef enum {
+  CUSPARSE_SPMM_ALG_DEFAULT = 0,
+  CUSPARSE_SPMM_CSR_ALG1 = 1,
+  CUSPARSE_SPMM_CSR_ALG2 = 2
+} cusparseSpMMAlg_t;
+
 struct cusparseContext;
 struct cusparseSpMatDescr;
 struct cusparseDnVecDescr;
+struct cusparseDnMatDescr;
 typedef struct cusparseContext* cusparseHandle_t;
 typedef struct cusparseSpMatDescr* cusparseSpMatDescr_t;
 typedef struct cusparseDnVecDescr* cusparseDnVecDescr_t;
+typedef struct cusparseDnMatDescr* cusparseDnMatDescr_t;
 
 /* Context — reference cusparse_descriptors.mm:46-130 */
 cusparseStatus_t cusparseCreate(cusparseHandle_t* handle);
@@ -86,8 +97,16 @@ cusparseStatus_t cusparseDestroySpMat(cusparseSpMatDescr_t spMatDescr);
 cusparseStatus_t cusparseCreateDnVec(cusparseDnVecDescr_t* dnVecDescr, int64_t size, void* values,
                                      cudaDataType valueType);
 cusparseStatus_t cusparseDestroyDnVec(cusparseDnVecDescr_t dnVecDescr);
+/* Dense matrices — reference cusparse_descriptors.mm:196-228: ld >= rows (column
+ * order) or >= cols (row order), at least 1. */
+cusparseStatus_t cusparseCreateDnMat(cusparseDnMatDescr_t* dnMatDescr, int64_t rows, int64_t cols,
+                                     int64_t ld, void* values, cudaDataType valueType,
+                                     cusparseOrder_t order);
+cusparseStatus_t cusparseDestroyDnMat(cusparseDnMatDescr_t dnMatDescr);
 
-/* SpMV — reference cusparse_ops.mm:44-211 */
+/* SpMV — reference cusparse_ops.mm:44-211.  opA TRANSPOSE computes
+ * alpha * A^T * x + beta * y by atomic accumulation (summation order unspecified,
+ * as in the reference's own fp32 path); fp16 values and vectors accumulate in fp32. */
 cusparseStatus_t cusparseSpMV_bufferSize(cusparseHandle_t handle, cusparseOperation_t opA,
                                          const void* alpha, cusparseSpMatDescr_t matA,
                                          cusparseDnVecDescr_t vecX, const void* beta,
@@ -97,6 +116,21 @@ cusparseStatus_t cusparseSpMV(cusparseHandle_t handle, cusparseOperation_t opA, 
                               cusparseSpMatDescr_t matA, cusparseDnVecDescr_t vecX,
                               const void* beta, cusparseDnVecDescr_t vecY, cudaDataType computeType,
                               cusparseSpMVAlg_t alg, void* externalBuffer);
+
+/* SpMM — reference cusparse_ops.mm:213-372: C = alpha * op(A) * op(B) + beta * C,
+ * fp32 only, buffer size 0.  opA NON_TRANSPOSE reproduces the reference's
+ * per-output arithmetic exactly; opA TRANSPOSE accumulates atomically. */
+cusparseStatus_t cusparseSpMM_bufferSize(cusparseHandle_t handle, cusparseOperation_t opA,
+                                         cusparseOperation_t opB, const void* alpha,
+                                         cusparseSpMatDescr_t matA, cusparseDnMatDescr_t matB,
+                                         const void* beta, cusparseDnMatDescr_t matC,
+                                         cudaDataType computeType, cusparseSpMMAlg_t alg,
+                                         size_t* bufferSize);
+cusparseStatus_t cusparseSpMM(cusparseHandle_t handle, cusparseOperation_t opA,
+                              cusparseOperation_t opB, const void* alpha, cusparseSpMatDescr_t matA,
+                              cusparseDnMatDescr_t matB, const void* beta,
+                              cusparseDnMatDescr_t matC, cudaDataType computeType,
+                              cusparseSpMMAlg_t alg, void* externalBuffer);
 
 #ifdef __cplusplus
 }

@@ -139,6 +139,8 @@ CUSPARSE_INDEX_32I = 2
 CUSPARSE_INDEX_64I = 3
 CUSPARSE_INDEX_BASE_ZERO = 0
 CUSPARSE_INDEX_BASE_ONE = 1
+CUSPARSE_ORDER_COL = 1
+CUSPARSE_ORDER_ROW = 2
 CUDA_R_32F = 0
 CUDA_R_16F = 2
 CUDA_R_16BF = 14
@@ -157,6 +159,10 @@ CUSPARSE_PROTOS = {
     "cusparseDestroyDnVec": ([vp], i32),
     "cusparseSpMV_bufferSize": ([vp, i32, vp, vp, vp, vp, vp, i32, i32, P(sz)], i32),
     "cusparseSpMV": ([vp, i32, vp, vp, vp, vp, vp, i32, i32, vp], i32),
+    "cusparseCreateDnMat": ([P(vp), i64, i64, i64, vp, i32, i32], i32),
+    "cusparseDestroyDnMat": ([vp], i32),
+    "cusparseSpMM_bufferSize": ([vp, i32, i32, vp, vp, vp, vp, vp, i32, i32, P(sz)], i32),
+    "cusparseSpMM": ([vp, i32, i32, vp, vp, vp, vp, vp, i32, i32, vp], i32),
 }
 
 
@@ -185,6 +191,10 @@ CUFFT_PROTOS = {
     "cufftPlan1d": ([P(vp), i32, i32, i32], i32),
     "cufftPlanMany": ([P(vp), i32, P(i32), P(i32), i32, i32, P(i32), i32, i32, i32, i32], i32),
     "cufftMakePlan1d": ([vp, i32, i32, i32, P(sz)], i32),
+    "cufftPlan2d": ([P(vp), i32, i32, i32], i32),
+    "cufftPlan3d": ([P(vp), i32, i32, i32, i32], i32),
+    "cufftMakePlan2d": ([vp, i32, i32, i32, P(sz)], i32),
+    "cufftMakePlan3d": ([vp, i32, i32, i32, i32, P(sz)], i32),
     "cufftMakePlanMany": ([vp, i32, P(i32), P(i32), i32, i32, P(i32), i32, i32, i32, i32, P(sz)],
                           i32),
     "cufftSetStream": ([vp, vp], i32),

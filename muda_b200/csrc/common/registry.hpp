@@ -27,6 +27,7 @@ enum class ObjKind : std::uint8_t {
   kSparseHandle = 0x31,
   kSparseCsr = 0x32,
   kSparseDnVec = 0x33,
+  kSparseDnMat = 0x34,
   kRandGenerator = 0x41,
   kDnnHandle = 0x51,
   kDnnTensor = 0x52,

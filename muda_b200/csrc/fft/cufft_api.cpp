@@ -487,6 +487,21 @@ cufftResult cufftMakePlan1d(cufftHandle plan, int nx, cufftType type, int batch,
   return configure(*p, 1, dims, nullptr, 1, 0, nullptr, 1, 0, type, batch, workSize);
 }
 
+cufftResult cufftMakePlan2d(cufftHandle plan, int nx, int ny, cufftType type, size_t* workSize) {
+  auto p = plans().get(plan);
+  if (!p) return CUFFT_INVALID_PLAN;
+  const int dims[2] = {nx, ny};
+  return configure(*p, 2, dims, nullptr, 1, 0, nullptr, 1, 0, type, 1, workSize);
+}
+
+cufftResult cufftMakePlan3d(cufftHandle plan, int nx, int ny, int nz, cufftType type,
+                            size_t* workSize) {
+  auto p = plans().get(plan);
+  if (!p) return CUFFT_INVALID_PLAN;
+  const int dims[3] = {nx, ny, nz};
+  return configure(*p, 3, dims, nullptr, 1, 0, nullptr, 1, 0, type, 1, workSize);
+}
+
 cufftResult cufftMakePlanMany(cufftHandle plan, int rank, int* n, int* inembed, int istride,
                               int idist, int* onembed, int ostride, int odist, cufftType type,
                               int batch, size_t* workSize) {
@@ -499,6 +514,16 @@ cufftResult cufftMakePlanMany(cufftHandle plan, int rank, int* n, int* inembed, 
 cufftResult cufftPlan1d(cufftHandle* plan, int nx, cufftType type, int batch) {
   int dims[1] = {nx};
   return make_plan(plan, 1, dims, nullptr, 1, 0, nullptr, 1, 0, type, batch);
+}
+
+cufftResult cufftPlan2d(cufftHandle* plan, int nx, int ny, cufftType type) {
+  int dims[2] = {nx, ny};
+  return make_plan(plan, 2, dims, nullptr, 1, 0, nullptr, 1, 0, type, 1);
+}
+
+cufftResult cufftPlan3d(cufftHandle* plan, int nx, int ny, int nz, cufftType type) {
+  int dims[3] = {nx, ny, nz};
+  return make_plan(plan, 3, dims, nullptr, 1, 0, nullptr, 1, 0, type, 1);
 }
 
 cufftResult cufftPlanMany(cufftHandle* plan, int rank, int* n, int* inembed, int istride,

@@ -1,0 +1,366 @@
+// spmm_kernels.cu — transposed CSR SpMV and CSR SpMM for sm_100a.
+//
+// Transposed SpMV, y = alpha * A^T * x + beta * y.  The reference's fp32 path
+// (libraries/sparse/src/cusparse_ops.mm:166-191, cusparse_kernels.metal:21-52)
+// scales y by beta and then adds alpha*x[r]*a_rk into y[col] with a CAS loop per
+// stored entry, one thread per row; its fp16 path is the generic kernel (:116-132),
+// one thread per output scanning the whole matrix.  Here both are one pass over the
+// matrix in the forward kernel's warp tiles (S lanes per row, long rows on the
+// whole warp), each entry a fire-and-forget `red.global.add.f32` into y (fp32) or
+// into an fp32 scratch vector that a last pass rounds to half (fp16).
+//
+// SpMM, C = alpha * op(A) * op(B) + beta * C (fp32; cusparse_kernels.metal:201-281).
+// Non-transposed A: one warp per row of A, lanes over output columns (4 per lane
+// with float4 loads when B and C are row-contiguous and 16-byte aligned); the row's
+// entries are read 32 at a time, coalesced, and broadcast by shuffle, so every
+// output is sum = fma(a_k, B(col_k, c), sum) in entry order followed by
+// fma(alpha, sum, beta*C) — the reference's per-output arithmetic, bit for bit.
+// Transposed A: C is scaled by beta, then each row r of A adds alpha*a_rk*B(r, c)
+// into C(col_k, c) with `red.global.add.f32` (B's row is loaded once per row).
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+#include "common/device.hpp"
+#include "sparse/csr_device.cuh"
+#include "sparse/spmv.hpp"
+
+namespace mb200::sparse {
+namespace {
+
+constexpr int kWarps = 8;
+constexpr unsigned kFull = 0xffffffffu;
+
+unsigned grid_for(std::int64_t units, std::int64_t per_cta, int waves) {
+  const std::int64_t want = (units + per_cta - 1) / per_cta;
+  const int sms = sm_count(current_device());
+  const std::int64_t cap = static_cast<std::int64_t>(sms > 0 ? sms : 148) * waves;
+  return static_cast<unsigned>(want < 1 ? 1 : (want < cap ? want : cap));
+}
+
+// ---------------------------------------------------------------- SpMV^T --
+
+// fp32: y = beta == 0 ? 0 : beta * y.  fp16: scratch = 0.
+template <class T>
+__global__ void __launch_bounds__(256)
+    spmv_t_prepare(T* __restrict__ y, float* __restrict__ scratch, std::int64_t n, float beta) {
+  for (std::int64_t i = blockIdx.x * static_cast<std::int64_t>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<std::int64_t>(gridDim.x) * blockDim.x) {
+    if constexpr (sizeof(T) == 4) {
+      y[i] = (beta == 0.0f) ? 0.0f : beta * y[i];
+    } else {
+      scratch[i] = 0.0f;
+    }
+  }
+}
+
+// fp16: y = half(fma(alpha, scratch, beta == 0 ? 0 : beta * y)).
+__global__ void __launch_bounds__(256)
+    spmv_t_finish(__half* __restrict__ y, const float* __restrict__ scratch, std::int64_t n,
+                  float alpha, float beta) {
+  for (std::int64_t i = blockIdx.x * static_cast<std::int64_t>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<std::int64_t>(gridDim.x) * blockDim.x) {
+    const float prev = (beta == 0.0f) ? 0.0f : beta * __half2float(y[i]);
+    y[i] = __float2half_rn(fmaf(alpha, scratch[i], prev));
+  }
+}
+
+// Adds the entries k in [s, e) of row r, lanes gl, gl + S, ...: fp32 adds
+// ax * a_k (ax = alpha * x[r]; rows with ax == 0 and zero products skipped, as the
+// reference does); fp16 adds a_k * x[r] into the fp32 scratch.
+template <class T>
+__device__ __forceinline__ void scatter_row(const CsrView& a, float xr, float alpha, int s, int e,
+                                            int gl, int step, float* __restrict__ target) {
+  const T* vals = static_cast<const T*>(a.values);
+  const float ax = (sizeof(T) == 4) ? alpha * xr : xr;
+  if (sizeof(T) == 4 && ax == 0.0f) return;
+  for (int k = s + gl; k < e; k += step) {
+    const int c = __ldcs(a.col_ind + k) - a.base;
+    if (static_cast<unsigned>(c) >= static_cast<unsigned long long>(a.cols)) continue;
+    const float p = (sizeof(T) == 4) ? ax * widen(__ldcs(vals + k)) : widen(__ldcs(vals + k)) * ax;
+    if (sizeof(T) == 4 && p == 0.0f) continue;
+    atomicAdd(target + c, p);
+  }
+}
+
+template <int S, class T>
+__global__ void __launch_bounds__(kWarps * 32)
+    spmv_t_scatter(const CsrView a, const T* __restrict__ x, float* __restrict__ target,
+                   float alpha) {
+  constexpr int G = 32 / S;
+  constexpr int kLong = 8 * S;
+  const int lane = threadIdx.x & 31;
+  const int grp = lane / S;
+  const int gl = lane % S;
+  const std::int64_t tiles = (a.rows + 31) / 32;
+  const std::int64_t warp0 = static_cast<std::int64_t>(blockIdx.x) * kWarps + (threadIdx.x >> 5);
+  const std::int64_t nwarps = static_cast<std::int64_t>(gridDim.x) * kWarps;
+  for (std::int64_t tile = warp0; tile < tiles; tile += nwarps) {
+    const std::int64_t r0 = tile * 32;
+    int s_i = 0, e_i = 0;
+    float x_i = 0.0f;
+    if (r0 + lane < a.rows) {
+      s_i = clamp_off(a.row_offsets[r0 + lane], a.base, a.nnz);
+      e_i = clamp_off(a.row_offsets[r0 + lane + 1], a.base, a.nnz);
+      if (e_i < s_i) e_i = s_i;
+      x_i = widen(x[r0 + lane]);
+    }
+    unsigned long_rows = __ballot_sync(kFull, e_i - s_i > kLong);
+#pragma unroll 1
+    for (int q = 0; q < S; ++q) {
+      const int rl = q * G + grp;
+      const int s = __shfl_sync(kFull, s_i, rl);
+      const int e = __shfl_sync(kFull, e_i, rl);
+      const float xr = __shfl_sync(kFull, x_i, rl);
+      if (!((long_rows >> rl) & 1u)) scatter_row<T>(a, xr, alpha, s, e, gl, S, target);
+    }
+    while (long_rows != 0u) {
+      const int rl = __ffs(long_rows) - 1;
+      long_rows &= long_rows - 1u;
+      const int s = __shfl_sync(kFull, s_i, rl);
+      const int e = __shfl_sync(kFull, e_i, rl);
+      const float xr = __shfl_sync(kFull, x_i, rl);
+      scatter_row<T>(a, xr, alpha, s, e, lane, 32, target);
+    }
+  }
+}
+
+template <int S, class T>
+cudaError_t scatter_width(const CsrView& a, const T* x, float* target, float alpha,
+                          cudaStream_t st) {
+  spmv_t_scatter<S, T><<<grid_for((a.rows + 31) / 32, kWarps, 32), kWarps * 32, 0, st>>>(
+      a, x, target, alpha);
+  return cudaGetLastError();
+}
+
+template <class T>
+cudaError_t spmv_t_typed(const CsrView& a, const void* xv, void* yv, float alpha, float beta,
+                         float* scratch, cudaStream_t st) {
+  const T* x = static_cast<const T*>(xv);
+  T* y = static_cast<T*>(yv);
+  float* target = (sizeof(T) == 4) ? reinterpret_cast<float*>(y) : scratch;
+  spmv_t_prepare<T><<<grid_for(a.cols, 256, 8), 256, 0, st>>>(y, scratch, a.cols, beta);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  if (a.rows > 0) {
+    switch (spmv_group_width(a.rows, a.nnz)) {
+      case 2: e = scatter_width<2, T>(a, x, target, alpha, st); break;
+      case 4: e = scatter_width<4, T>(a, x, target, alpha, st); break;
+      case 8: e = scatter_width<8, T>(a, x, target, alpha, st); break;
+      case 16: e = scatter_width<16, T>(a, x, target, alpha, st); break;
+      default: e = scatter_width<32, T>(a, x, target, alpha, st); break;
+    }
+    if (e != cudaSuccess) return e;
+  }
+  if constexpr (sizeof(T) == 2) {
+    spmv_t_finish<<<grid_for(a.cols, 256, 8), 256, 0, st>>>(y, scratch, a.cols, alpha, beta);
+    e = cudaGetLastError();
+  }
+  return e;
+}
+
+// ------------------------------------------------------------------ SpMM --
+
+// Element (r, c) of a dense operand; ROW: known at compile time to be
+// row-contiguous (m[r * ld + c]).
+template <bool ROW>
+__device__ __forceinline__ std::int64_t dense_index(const DenseView& d, std::int64_t r,
+                                                    std::int64_t c) {
+  if constexpr (ROW) {
+    return r * d.ld + c;
+  } else {
+    const std::int64_t er = d.trans ? c : r;
+    const std::int64_t ec = d.trans ? r : c;
+    return d.col_major ? er + ec * d.ld : er * d.ld + ec;
+  }
+}
+
+template <int VEC>
+struct Vec {
+  float v[VEC];
+};
+
+template <int VEC, bool ROW>
+__device__ __forceinline__ Vec<VEC> load_b(const DenseView& b, std::int64_t r, std::int64_t c) {
+  Vec<VEC> out;
+  if constexpr (VEC == 4) {
+    const float4 q = __ldg(reinterpret_cast<const float4*>(b.m + dense_index<true>(b, r, c)));
+    out.v[0] = q.x;
+    out.v[1] = q.y;
+    out.v[2] = q.z;
+    out.v[3] = q.w;
+  } else {
+    out.v[0] = __ldg(b.m + dense_index<ROW>(b, r, c));
+  }
+  return out;
+}
+
+// Non-transposed A: warp per row, lane columns c0 + lane*VEC .. +VEC.
+template <int VEC, bool BROW, bool CROW>
+__global__ void __launch_bounds__(kWarps * 32)
+    spmm_rows(const CsrView a, const DenseView b, const DenseView c, std::int64_t ncols,
+              float alpha, float beta) {
+  const int lane = threadIdx.x & 31;
+  const float* vals = static_cast<const float*>(a.values);
+  const std::int64_t warp0 = static_cast<std::int64_t>(blockIdx.x) * kWarps + (threadIdx.x >> 5);
+  const std::int64_t nwarps = static_cast<std::int64_t>(gridDim.x) * kWarps;
+  for (std::int64_t row = warp0; row < a.rows; row += nwarps) {
+    int s = clamp_off(a.row_offsets[row], a.base, a.nnz);
+    const int e0 = clamp_off(a.row_offsets[row + 1], a.base, a.nnz);
+    const int e = e0 < s ? s : e0;
+    for (std::int64_t cb = 0; cb < ncols; cb += 32 * VEC) {
+      const std::int64_t col = cb + static_cast<std::int64_t>(lane) * VEC;
+      const bool live = col < ncols;
+      float acc[VEC];
+#pragma unroll
+      for (int v = 0; v < VEC; ++v) acc[v] = 0.0f;
+      for (int k0 = s; k0 < e; k0 += 32) {
+        int kk = -1;
+        float vv = 0.0f;
+        if (k0 + lane < e) {
+          kk = __ldg(a.col_ind + k0 + lane) - a.base;
+          vv = __ldg(vals + k0 + lane);
+        }
+        const int cnt = (e - k0 < 32) ? e - k0 : 32;
+#pragma unroll 4
+        for (int j = 0; j < cnt; ++j) {
+          const int k = __shfl_sync(kFull, kk, j);
+          const float av = __shfl_sync(kFull, vv, j);
+          if (static_cast<unsigned>(k) < static_cast<unsigned long long>(a.cols) && live) {
+            const Vec<VEC> bv = load_b<VEC, BROW>(b, k, col);
+#pragma unroll
+            for (int v = 0; v < VEC; ++v) acc[v] = fmaf(av, bv.v[v], acc[v]);
+          }
+        }
+      }
+      if (live) {
+#pragma unroll
+        for (int v = 0; v < VEC; ++v) {
+          float* out = c.m + dense_index<CROW>(c, row, col + v);
+          const float prev = (beta == 0.0f) ? 0.0f : beta * *out;
+          *out = fmaf(alpha, acc[v], prev);
+        }
+      }
+    }
+  }
+}
+
+// C = beta == 0 ? 0 : beta * C over out_rows x ncols.
+__global__ void __launch_bounds__(256)
+    spmm_scale(const DenseView c, std::int64_t out_rows, std::int64_t ncols, float beta) {
+  const std::int64_t total = out_rows * ncols;
+  for (std::int64_t i = blockIdx.x * static_cast<std::int64_t>(blockDim.x) + threadIdx.x;
+       i < total; i += static_cast<std::int64_t>(gridDim.x) * blockDim.x) {
+    // walk C in its storage order so that consecutive threads touch consecutive words
+    const std::int64_t r = c.col_major ? i % out_rows : i / ncols;
+    const std::int64_t col = c.col_major ? i / out_rows : i % ncols;
+    float* p = c.m + dense_index<false>(c, r, col);
+    *p = (beta == 0.0f) ? 0.0f : beta * *p;
+  }
+}
+
+// Transposed A: warp per row r of A; every entry (k, a) adds alpha * a * B(r, col)
+// into C(k, col).
+template <bool BROW, bool CROW>
+__global__ void __launch_bounds__(kWarps * 32)
+    spmm_t_scatter(const CsrView a, const DenseView b, const DenseView c, std::int64_t ncols,
+                   float alpha) {
+  const int lane = threadIdx.x & 31;
+  const float* vals = static_cast<const float*>(a.values);
+  const std::int64_t warp0 = static_cast<std::int64_t>(blockIdx.x) * kWarps + (threadIdx.x >> 5);
+  const std::int64_t nwarps = static_cast<std::int64_t>(gridDim.x) * kWarps;
+  for (std::int64_t row = warp0; row < a.rows; row += nwarps) {
+    const int s = clamp_off(a.row_offsets[row], a.base, a.nnz);
+    const int e0 = clamp_off(a.row_offsets[row + 1], a.base, a.nnz);
+    const int e = e0 < s ? s : e0;
+    if (e == s) continue;
+    for (std::int64_t cb = 0; cb < ncols; cb += 32) {
+      const std::int64_t col = cb + lane;
+      const bool live = col < ncols;
+      const float br = live ? alpha * __ldg(b.m + dense_index<BROW>(b, row, col)) : 0.0f;
+      for (int k0 = s; k0 < e; k0 += 32) {
+        int kk = -1;
+        float vv = 0.0f;
+        if (k0 + lane < e) {
+          kk = __ldg(a.col_ind + k0 + lane) - a.base;
+          vv = __ldg(vals + k0 + lane);
+        }
+        const int cnt = (e - k0 < 32) ? e - k0 : 32;
+        for (int j = 0; j < cnt; ++j) {
+          const int k = __shfl_sync(kFull, kk, j);
+          const float av = __shfl_sync(kFull, vv, j);
+          if (static_cast<unsigned>(k) < static_cast<unsigned long long>(a.cols) && live)
+            atomicAdd(c.m + dense_index<CROW>(c, k, col), av * br);
+        }
+      }
+    }
+  }
+}
+
+template <bool BROW, bool CROW>
+cudaError_t spmm_rows_launch(const CsrView& a, const DenseView& b, const DenseView& c,
+                             std::int64_t ncols, float alpha, float beta, bool vec4,
+                             cudaStream_t st) {
+  const unsigned grid = grid_for(a.rows, kWarps, 16);
+  if constexpr (BROW && CROW) {
+    if (vec4) {
+      spmm_rows<4, true, true><<<grid, kWarps * 32, 0, st>>>(a, b, c, ncols, alpha, beta);
+      return cudaGetLastError();
+    }
+  }
+  spmm_rows<1, BROW, CROW><<<grid, kWarps * 32, 0, st>>>(a, b, c, ncols, alpha, beta);
+  return cudaGetLastError();
+}
+
+bool row_contiguous(const DenseView& d) { return d.col_major == d.trans; }
+
+}  // namespace
+
+cudaError_t launch_spmm_csr(const CsrView& a, bool trans_a, const DenseView& b,
+                            const DenseView& c, std::int64_t ncols, float alpha, float beta,
+                            cudaStream_t stream) noexcept {
+  const std::int64_t out_rows = trans_a ? a.cols : a.rows;
+  if (out_rows <= 0 || ncols <= 0) return cudaSuccess;
+  const bool brow = row_contiguous(b);
+  const bool crow = !c.col_major;
+  DenseView bb = b, cc = c;
+  if (brow) {  // normalise: B(r, col) = m[r * ld + col]
+    bb.col_major = false;
+    bb.trans = false;
+  }
+  cc.trans = false;
+  if (!trans_a) {
+    const bool vec4 = brow && crow && ncols % 4 == 0 && b.ld % 4 == 0 && c.ld % 4 == 0 &&
+                      aligned_to(b.m, 16) && aligned_to(c.m, 16);
+    if (brow && crow) return spmm_rows_launch<true, true>(a, bb, cc, ncols, alpha, beta, vec4, stream);
+    if (brow) return spmm_rows_launch<true, false>(a, bb, cc, ncols, alpha, beta, false, stream);
+    if (crow) return spmm_rows_launch<false, true>(a, bb, cc, ncols, alpha, beta, false, stream);
+    return spmm_rows_launch<false, false>(a, bb, cc, ncols, alpha, beta, false, stream);
+  }
+  spmm_scale<<<grid_for(out_rows * ncols, 256, 8), 256, 0, stream>>>(cc, out_rows, ncols, beta);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess || a.rows <= 0) return e;
+  const unsigned grid = grid_for(a.rows, kWarps, 16);
+  if (brow && crow)
+    spmm_t_scatter<true, true><<<grid, kWarps * 32, 0, stream>>>(a, bb, cc, ncols, alpha);
+  else if (brow)
+    spmm_t_scatter<true, false><<<grid, kWarps * 32, 0, stream>>>(a, bb, cc, ncols, alpha);
+  else if (crow)
+    spmm_t_scatter<false, true><<<grid, kWarps * 32, 0, stream>>>(a, bb, cc, ncols, alpha);
+  else
+    spmm_t_scatter<false, false><<<grid, kWarps * 32, 0, stream>>>(a, bb, cc, ncols, alpha);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_spmv_csr_t(const CsrView& a, Value t, const void* x, void* y, float alpha,
+                              float beta, float* scratch, cudaStream_t stream) noexcept {
+  if (a.cols <= 0) return cudaSuccess;
+  if (t == Value::kF16) {
+    if (scratch == nullptr) return cudaErrorInvalidValue;
+    return spmv_t_typed<__half>(a, x, y, alpha, beta, scratch, stream);
+  }
+  return spmv_t_typed<float>(a, x, y, alpha, beta, nullptr, stream);
+}
+
+}  // namespace mb200::sparse

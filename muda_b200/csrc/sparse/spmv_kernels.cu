@@ -15,11 +15,13 @@
 // (the gathered operand, 16.8 MB at the 4M-row configuration) stays resident in
 // the 126 MB L2; x is gathered with L2-only loads (no L1 allocation for sectors
 // that are almost never reused: measured 3-6 % faster than read-only-cache loads).
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
 #include <cstdint>
 
 #include "common/device.hpp"
+#include "sparse/csr_device.cuh"
 #include "sparse/spmv.hpp"
 
 namespace mb200::sparse {
@@ -28,32 +30,29 @@ namespace {
 constexpr int kWarpsPerCta = 8;
 constexpr unsigned kFull = 0xffffffffu;
 
-__device__ __forceinline__ int clamp_off(std::int32_t v, int base, std::int64_t nnz) {
-  const std::int64_t t = static_cast<std::int64_t>(v) - base;
-  return static_cast<int>(t < 0 ? 0 : (t > nnz ? nnz : t));
-}
-
 // sum = fma(values[k], x[col], sum) for one stored entry; an entry whose column
 // is outside [0, cols) contributes nothing.
-__device__ __forceinline__ float accumulate(const CsrView& a, const float* __restrict__ x, int k,
+template <class T>
+__device__ __forceinline__ float accumulate(const CsrView& a, const T* __restrict__ x, int k,
                                             float sum) {
   const int c = __ldcs(a.col_ind + k) - a.base;
-  const float v = __ldcs(a.values + k);
+  const float v = widen(__ldcs(static_cast<const T*>(a.values) + k));
   return (static_cast<unsigned>(c) < static_cast<unsigned long long>(a.cols))
-             ? fmaf(v, __ldcg(x + c), sum)
+             ? fmaf(v, widen(__ldcg(x + c)), sum)
              : sum;
 }
 
-__device__ __forceinline__ void store_y(float* y, std::int64_t row, float sum, float alpha,
+template <class T>
+__device__ __forceinline__ void store_y(T* y, std::int64_t row, float sum, float alpha,
                                         float beta) {
-  const float prev = (beta == 0.0f) ? 0.0f : beta * y[row];
-  y[row] = fmaf(alpha, sum, prev);
+  const float prev = (beta == 0.0f) ? 0.0f : beta * widen(y[row]);
+  y[row] = narrow<T>(fmaf(alpha, sum, prev));
 }
 
-template <int S>
+template <int S, class T>
 __global__ void __launch_bounds__(kWarpsPerCta * 32) spmv_csr_tiles(const CsrView a,
-                                                                   const float* __restrict__ x,
-                                                                   float* __restrict__ y,
+                                                                   const T* __restrict__ x,
+                                                                   T* __restrict__ y,
                                                                    float alpha, float beta) {
   constexpr int G = 32 / S;      // rows per round
   constexpr int kLong = 8 * S;   // longer rows go to the whole warp
@@ -121,16 +120,37 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32) spmv_csr_tiles(const CsrVie
   }
 }
 
-template <int S>
-cudaError_t launch_width(const CsrView& a, const float* x, float* y, float alpha, float beta,
-                         cudaStream_t stream) {
-  const std::int64_t tiles = (a.rows + 31) / 32;
+unsigned tile_grid(std::int64_t rows) {
+  const std::int64_t tiles = (rows + 31) / 32;
   const std::int64_t want = (tiles + kWarpsPerCta - 1) / kWarpsPerCta;
   const int sms = sm_count(current_device());
   const std::int64_t cap = static_cast<std::int64_t>(sms > 0 ? sms : 148) * 32;
-  const unsigned grid = static_cast<unsigned>(want < cap ? want : cap);
-  spmv_csr_tiles<S><<<grid, kWarpsPerCta * 32, 0, stream>>>(a, x, y, alpha, beta);
+  return static_cast<unsigned>(want < 1 ? 1 : (want < cap ? want : cap));
+}
+
+template <int S, class T>
+cudaError_t launch_width(const CsrView& a, const void* x, void* y, float alpha, float beta,
+                         cudaStream_t stream) {
+  spmv_csr_tiles<S, T><<<tile_grid(a.rows), kWarpsPerCta * 32, 0, stream>>>(
+      a, static_cast<const T*>(x), static_cast<T*>(y), alpha, beta);
   return cudaGetLastError();
+}
+
+template <class T>
+cudaError_t launch_typed(const CsrView& a, const void* x, void* y, float alpha, float beta,
+                         cudaStream_t stream) {
+  switch (spmv_group_width(a.rows, a.nnz)) {
+    case 2:
+      return launch_width<2, T>(a, x, y, alpha, beta, stream);
+    case 4:
+      return launch_width<4, T>(a, x, y, alpha, beta, stream);
+    case 8:
+      return launch_width<8, T>(a, x, y, alpha, beta, stream);
+    case 16:
+      return launch_width<16, T>(a, x, y, alpha, beta, stream);
+    default:
+      return launch_width<32, T>(a, x, y, alpha, beta, stream);
+  }
 }
 
 }  // namespace
@@ -147,21 +167,11 @@ int spmv_group_width(std::int64_t rows, std::int64_t nnz) noexcept {
   return 32;
 }
 
-cudaError_t launch_spmv_csr(const CsrView& a, const float* x, float* y, float alpha, float beta,
-                            cudaStream_t stream) noexcept {
+cudaError_t launch_spmv_csr(const CsrView& a, Value t, const void* x, void* y, float alpha,
+                            float beta, cudaStream_t stream) noexcept {
   if (a.rows <= 0) return cudaSuccess;
-  switch (spmv_group_width(a.rows, a.nnz)) {
-    case 2:
-      return launch_width<2>(a, x, y, alpha, beta, stream);
-    case 4:
-      return launch_width<4>(a, x, y, alpha, beta, stream);
-    case 8:
-      return launch_width<8>(a, x, y, alpha, beta, stream);
-    case 16:
-      return launch_width<16>(a, x, y, alpha, beta, stream);
-    default:
-      return launch_width<32>(a, x, y, alpha, beta, stream);
-  }
+  return t == Value::kF16 ? launch_typed<__half>(a, x, y, alpha, beta, stream)
+                          : launch_typed<float>(a, x, y, alpha, beta, stream);
 }
 
 }  // namespace mb200::sparse

@@ -169,6 +169,68 @@ def spmv_csr(row_offsets, col_ind, values, x, *, base=0, alpha=1.0, beta=0.0, y=
     return (y, exact, absr) if with_abs else y
 
 
+def spmv_csr_t(row_offsets, col_ind, values, x, cols, *, base=0, alpha=1.0, beta=0.0, y=None,
+               generic=False, with_abs=False):
+    """Reference transposed CSR SpMV, y = alpha A^T x + beta y (cusparse_ops.mm:166-191
+    and cusparse_kernels.metal:21-52 for generic=False; the generic kernel's op_a = 1
+    branch, cusparse_kernels.metal:79-92, for generic=True).
+
+    Returns y, or with with_abs=True (y, exact result in float64, sum |a x| per
+    output in float64)."""
+    ro = np.ascontiguousarray(row_offsets, dtype=np.int32)
+    ci = np.ascontiguousarray(col_ind, dtype=np.int32)
+    va = np.ascontiguousarray(values, dtype=np.float32)
+    xx = np.ascontiguousarray(x, dtype=np.float32)
+    rows = len(ro) - 1
+    y = np.zeros(cols, np.float32) if y is None else np.ascontiguousarray(y, np.float32).copy()
+    exact = np.zeros(cols, np.float64) if with_abs else None
+    absr = np.zeros(cols, np.float64) if with_abs else None
+    lib().oracle_spmv_csr_t(rows, cols, ro.ctypes.data, ci.ctypes.data, va.ctypes.data, base,
+                            xx.ctypes.data, y.ctypes.data, alpha, beta, int(generic),
+                            exact.ctypes.data if with_abs else None,
+                            absr.ctypes.data if with_abs else None)
+    return (y, exact, absr) if with_abs else y
+
+
+def spmv_csr_f16(row_offsets, col_ind, values, x, *, cols=None, trans=False, base=0, alpha=1.0,
+                 beta=0.0, y=None):
+    """Reference fp16 SpMV (cusparse_kernels.metal:94-133 and the warp kernel :159-184):
+    half values and vectors widened to fp32, fp32 fma accumulation, one rounding of
+    fma(alpha, sum, beta * y) to half.  Returns float16."""
+    va = np.asarray(values, np.float16).astype(np.float32)
+    xx = np.asarray(x, np.float16).astype(np.float32)
+    y32 = None if y is None else np.asarray(y, np.float16).astype(np.float32)
+    if trans:
+        out = spmv_csr_t(row_offsets, col_ind, va, xx, cols, base=base, alpha=alpha, beta=beta,
+                         y=y32, generic=True)
+    else:
+        rows = len(row_offsets) - 1
+        out = spmv_csr(row_offsets, col_ind, va, xx, base=base, alpha=alpha, beta=beta,
+                       y=np.zeros(rows, np.float32) if y32 is None else y32.copy())
+    return out.astype(np.float16)
+
+
+def spmm_csr(row_offsets, col_ind, values, a_cols, B, ldb, order_b, C, ldc, order_c, ncols, *,
+             op_a=0, op_b=0, base=0, alpha=1.0, beta=0.0, with_abs=False, threads: int = 8):
+    """Reference CSR SpMM (cusparse_kernels.metal:201-247), C updated in place (flat
+    float32 array with leading dimension ldc; order 1 = column-major, 2 = row-major).
+    With with_abs=True also returns (exact, mag) as (out_rows, ncols) float64 arrays."""
+    ro = np.ascontiguousarray(row_offsets, dtype=np.int32)
+    ci = np.ascontiguousarray(col_ind, dtype=np.int32)
+    va = np.ascontiguousarray(values, dtype=np.float32)
+    bb = np.ascontiguousarray(B, dtype=np.float32)
+    assert C.dtype == np.float32 and C.flags.c_contiguous
+    a_rows = len(ro) - 1
+    out_rows = a_rows if op_a == 0 else a_cols
+    exact = np.zeros((out_rows, ncols), np.float64) if with_abs else None
+    mag = np.zeros((out_rows, ncols), np.float64) if with_abs else None
+    lib().oracle_spmm_csr(a_rows, a_cols, ro.ctypes.data, ci.ctypes.data, va.ctypes.data, base,
+                          op_a, bb.ctypes.data, ldb, order_b, op_b, C.ctypes.data, ldc, order_c,
+                          ncols, alpha, beta, exact.ctypes.data if with_abs else None,
+                          mag.ctypes.data if with_abs else None, threads)
+    return (C, exact, mag) if with_abs else C
+
+
 def fft_c2c(x: np.ndarray, dims, batch: int, sign: int, *, istride=1, idist=None, ostride=1,
             odist=None, out_len=None, exact=False, threads: int = 8) -> np.ndarray:
     """Reference batched C2C FFT (cufft_exec.mm:101-211) on a flat complex64 array.

@@ -101,6 +101,20 @@ void oracle_spmv_csr(int64_t rows, const int32_t* row_offsets, const int32_t* co
                      const float* values, int base, const float* x, float* y, float alpha,
                      float beta, double* exact_row, double* abs_row, int threads);
 
+/* Transposed CSR SpMV (cusparse_ops.mm:166-191 fast path, generic = 0;
+ * cusparse_kernels.metal:79-92 / 116-132 generic branch, generic = 1). */
+void oracle_spmv_csr_t(int64_t rows, int64_t cols, const int32_t* row_offsets,
+                       const int32_t* col_ind, const float* values, int base, const float* x,
+                       float* y, float alpha, float beta, int generic, double* exact_col,
+                       double* abs_col);
+
+/* CSR SpMM (cusparse_kernels.metal:201-247); order 1 = column-major, 2 = row-major. */
+void oracle_spmm_csr(int64_t a_rows, int64_t a_cols, const int32_t* row_offsets,
+                     const int32_t* col_ind, const float* values, int base, int op_a,
+                     const float* B, int64_t ldb, int order_b, int op_b, float* C, int64_t ldc,
+                     int order_c, int64_t ncols, float alpha, float beta, double* exact,
+                     double* mag, int threads);
+
 /* algo 0 FAST, 1 ACCURATE, 2 LOG; mode_channel 0 INSTANCE, 1 CHANNEL. */
 void oracle_softmax_fwd(const float* x, float* y, const OracleTensor4* xd, const OracleTensor4* yd,
                         int algo, int mode_channel, float alpha, float beta, int threads);

@@ -346,3 +346,57 @@ def test_gpu_config_size(cuda, built):
     err = (x.view(batch, 2 * n) / n - x0.view(batch, 2 * n)).double().norm(dim=1)
     ref = x0.view(batch, 2 * n).double().norm(dim=1)
     assert float((err / ref).max()) <= TOL
+
+
+@pytest.mark.gpu
+def test_gpu_plan2d_plan3d_reference_pins(cuda, built):
+    """tests/cufft_test.cpp:128-193 through cufftPlan2d / cufftPlan3d: a 16 x 32
+    impulse gives a flat spectrum (1e-4), and the 8 x 8 x 8 forward + inverse round
+    trip divided by 512 returns the input (1e-3); cufftMakePlan2d / 3d configure
+    the same plans on a created handle."""
+    torch = cuda
+    L = capi.cufft()
+    p = C.c_void_p()
+    assert L.cufftPlan2d(C.byref(p), 16, 32, capi.CUFFT_C2C) == 0
+    x = torch.zeros(2 * 16 * 32, dtype=torch.float32, device="cuda")
+    x[0] = 1.0
+    ptr = C.c_void_p(x.data_ptr())
+    assert L.cufftExecC2C(p, ptr, ptr, capi.CUFFT_FORWARD) == 0
+    torch.cuda.synchronize()
+    y = x.cpu().numpy().view(np.complex64)
+    assert np.all(np.abs(y.real - 1.0) <= 1e-4) and np.all(np.abs(y.imag) <= 1e-4)
+    assert L.cufftDestroy(p) == 0
+
+    i = np.arange(512)
+    h = (((i % 7) - 3) * np.float32(0.2) + 1j * ((i % 5) - 2) * np.float32(0.1)).astype(np.complex64)
+    for make in (False, True):
+        q = C.c_void_p()
+        if make:
+            ws = C.c_size_t(0)
+            assert L.cufftCreate(C.byref(q)) == 0
+            assert L.cufftMakePlan3d(q, 8, 8, 8, capi.CUFFT_C2C, C.byref(ws)) == 0
+            assert ws.value > 0
+        else:
+            assert L.cufftPlan3d(C.byref(q), 8, 8, 8, capi.CUFFT_C2C) == 0
+        t = torch.from_numpy(h.view(np.float32).copy()).cuda()
+        tp = C.c_void_p(t.data_ptr())
+        assert L.cufftExecC2C(q, tp, tp, capi.CUFFT_FORWARD) == 0
+        assert L.cufftExecC2C(q, tp, tp, capi.CUFFT_INVERSE) == 0
+        torch.cuda.synchronize()
+        out = t.cpu().numpy().view(np.complex64) / 512
+        assert np.all(np.abs(out.real - h.real) < 1e-3) and np.all(np.abs(out.imag - h.imag) < 1e-3)
+        assert L.cufftDestroy(q) == 0
+    # 2-D real plans through the same entry points
+    r = C.c_void_p()
+    ws = C.c_size_t(0)
+    assert L.cufftCreate(C.byref(r)) == 0
+    assert L.cufftMakePlan2d(r, 6, 10, capi.CUFFT_R2C, C.byref(ws)) == 0
+    xr = np.random.default_rng(3).standard_normal(60).astype(np.float32)
+    tx = torch.from_numpy(xr).cuda()
+    X = torch.zeros(6 * 6, dtype=torch.complex64, device="cuda")
+    assert L.cufftExecR2C(r, C.c_void_p(tx.data_ptr()), C.c_void_p(X.data_ptr())) == 0
+    torch.cuda.synchronize()
+    want = np.fft.rfftn(xr.reshape(6, 10).astype(np.float64)).reshape(-1)
+    got = X.cpu().numpy()
+    assert np.linalg.norm(got - want) / np.linalg.norm(want) <= TOL
+    assert L.cufftDestroy(r) == 0

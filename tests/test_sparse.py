@@ -1,4 +1,4 @@
-"""cusparseSpMV (CSR, non-transposed, fp32).
+"""cusparseSpMV (CSR, non-transposed, fp32) and the descriptor / argument checks of SpMM.
 
 CPU: the oracle against the reference's known answer and the C-ABI host logic.
 GPU (marked): the CUDA path through the C ABI against the oracle.  Index handling
@@ -84,16 +84,45 @@ def test_host_logic(built):
         capi.CUSPARSE_STATUS_INVALID_VALUE
     assert L.cusparseSpMV(h, 0, None, m, vx, b, vy, 0, 0, None) == \
         capi.CUSPARSE_STATUS_INVALID_VALUE
-    # transposed product is outside this library's hot path
-    assert L.cusparseSpMV(h, 1, a, m, vx, b, vy, 0, 0, None) == capi.CUSPARSE_STATUS_NOT_SUPPORTED
-    # unaddressable arrays are rejected before launch
+    # unaddressable arrays are rejected before launch, in both directions
+    assert L.cusparseSpMV(h, 1, a, m, vx, b, vy, 0, 0, None) == capi.CUSPARSE_STATUS_INVALID_VALUE
     assert L.cusparseSpMV(h, 0, a, m, vx, b, vy, 0, 0, None) == capi.CUSPARSE_STATUS_INVALID_VALUE
+    # dense matrices (cusparse_descriptors.mm:196-223) and SpMM checks (cusparse_ops.mm:213-273)
+    d = C.c_void_p()
+    assert L.cusparseCreateDnMat(C.byref(d), 4, 2, 3, p, 0, capi.CUSPARSE_ORDER_COL) == \
+        capi.CUSPARSE_STATUS_INVALID_VALUE  # ld < rows
+    assert L.cusparseCreateDnMat(C.byref(d), 4, 2, 1, p, 0, capi.CUSPARSE_ORDER_ROW) == \
+        capi.CUSPARSE_STATUS_INVALID_VALUE  # ld < cols
+    assert L.cusparseCreateDnMat(C.byref(d), 4, 2, 4, p, 0, 3) == capi.CUSPARSE_STATUS_INVALID_VALUE
+    assert L.cusparseCreateDnMat(C.byref(d), 4, 2, 4, None, 0, 1) == \
+        capi.CUSPARSE_STATUS_INVALID_VALUE
+    assert L.cusparseCreateDnMat(C.byref(d), 4, 2, 4, p, 5, 1) == capi.CUSPARSE_STATUS_NOT_SUPPORTED
+    assert L.cusparseCreateDnMat(C.byref(d), 0, 0, 1, None, 0, 1) == 0
+    assert L.cusparseDestroyDnMat(d) == 0
+    assert L.cusparseDestroyDnMat(d) == capi.CUSPARSE_STATUS_INVALID_VALUE
+    mb = _mk(L, "cusparseCreateDnMat", 4, 2, 4, p, 0, capi.CUSPARSE_ORDER_COL)
+    mc = _mk(L, "cusparseCreateDnMat", 4, 2, 2, p, 0, capi.CUSPARSE_ORDER_ROW)
+    mh = _mk(L, "cusparseCreateDnMat", 4, 2, 4, p, 2, capi.CUSPARSE_ORDER_COL)  # fp16
+    assert L.cusparseSpMM_bufferSize(h, 0, 0, a, m, mb, b, mc, 0, 0, C.byref(sz)) == 0
+    assert sz.value == 0
+    assert L.cusparseSpMM_bufferSize(h, 0, 1, a, m, mb, b, mc, 0, 0, C.byref(sz)) == \
+        capi.CUSPARSE_STATUS_INVALID_VALUE  # op(B) is 2 x 4
+    assert L.cusparseSpMM(h, 0, 0, None, m, mb, b, mc, 0, 0, None) == \
+        capi.CUSPARSE_STATUS_INVALID_VALUE
+    assert L.cusparseSpMM(h, 0, 0, a, m, mh, b, mc, 0, 0, None) == \
+        capi.CUSPARSE_STATUS_NOT_SUPPORTED
+    assert L.cusparseSpMM(h, 0, 0, a, m, mb, b, mc, 0, 0, None) == \
+        capi.CUSPARSE_STATUS_INVALID_VALUE  # unaddressable arrays
+    for d in (mb, mc, mh):
+        assert L.cusparseDestroyDnMat(d) == 0
     for d in (vx, vy, vbad):
         assert L.cusparseDestroyDnVec(d) == 0
     assert L.cusparseDestroySpMat(m) == 0
     assert L.cusparseDestroySpMat(m) == capi.CUSPARSE_STATUS_INVALID_VALUE
     assert L.cusparseDestroy(h) == 0
     assert L.cusparseSpMV(h, 0, a, m, vx, b, vy, 0, 0, None) == \
+        capi.CUSPARSE_STATUS_NOT_INITIALIZED
+    assert L.cusparseSpMM(h, 0, 0, a, m, m, b, m, 0, 0, None) == \
         capi.CUSPARSE_STATUS_NOT_INITIALIZED
 
 

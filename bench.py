@@ -433,6 +433,106 @@ def suite_spmv(s: Suite) -> dict:
     return out
 
 
+def _csr_handle(L, s, mtx, rows, cols):
+    h, ma = C.c_void_p(), C.c_void_p()
+    assert L.cusparseCreate(C.byref(h)) == 0
+    assert L.cusparseSetStream(h, s.sp) == 0
+    assert L.cusparseCreateCsr(C.byref(ma), rows, cols, mtx["nnz"],
+                               C.c_void_p(mtx["row_offsets"].data_ptr()),
+                               C.c_void_p(mtx["col_ind"].data_ptr()),
+                               C.c_void_p(mtx["values"].data_ptr()), 2, 2, 0, 0) == 0
+    return h, ma
+
+
+def suite_spmv_t(s: Suite) -> dict:
+    """y = A^T x on the configs[2] matrix (4M x 4M power law, seed 7), beta 0."""
+    from muda_b200 import capi, synth
+    torch = s.torch
+    rows = (1 << 22) // s.scale
+    mtx = synth.powerlaw_csr(torch, rows, rows, seed=7)
+    y = torch.zeros(rows, dtype=torch.float32, device="cuda")
+    L = capi.cusparse()
+    h, ma = _csr_handle(L, s, mtx, rows, rows)
+    vx, vy = C.c_void_p(), C.c_void_p()
+    assert L.cusparseCreateDnVec(C.byref(vx), rows, C.c_void_p(mtx["x"].data_ptr()), 0) == 0
+    assert L.cusparseCreateDnVec(C.byref(vy), rows, C.c_void_p(y.data_ptr()), 0) == 0
+    one, zero = C.c_float(1.0), C.c_float(0.0)
+    ms, launches = s.time(lambda: L.cusparseSpMV(h, 1, C.byref(one), ma, vx, C.byref(zero), vy,
+                                                 0, 0, None), flush=True, launches_per_call=2)
+    for fn, d in (("cusparseDestroyDnVec", vx), ("cusparseDestroyDnVec", vy),
+                  ("cusparseDestroySpMat", ma)):
+        assert getattr(L, fn)(d) == 0
+    assert L.cusparseDestroy(h) == 0
+    nnz = mtx["nnz"]
+    alg_bytes = nnz * 8 + (rows + 1) * 4 + rows * 4 + rows * 4
+    gbs = alg_bytes / (ms * 1e-3) / 1e9
+    out = {"value": gbs, "unit": "GB/s", "ms": ms, "dtype": "f32/i32",
+           "config": f"A^T x, {rows} rows, nnz {nnz}, power law, L2 flushed before each call",
+           "roofline": s.roof("spmv_t_scatter<4,float>", gbs, "hbm"), "launches": launches,
+           "algorithmic_bytes_per_call": alg_bytes}
+    if s.cpu:
+        import oracle
+        sample = max(1, rows // 16)
+        ro = mtx["row_offsets"][: sample + 1].cpu().numpy()
+        ci = mtx["col_ind"][: int(ro[-1])].cpu().numpy()
+        va = mtx["values"][: int(ro[-1])].cpu().numpy()
+        xx = mtx["x"][:sample].cpu().numpy()
+        dt = cpu_time(lambda: oracle.spmv_csr_t(ro, ci, va, xx, rows))
+        sb = int(ro[-1]) * 8 + (sample + 1) * 4 + sample * 4 + rows * 4
+        out["cpu_baseline"] = {"value": sb / dt / 1e9, "unit": "GB/s", "cores": 1, "kind": "port",
+                               "sample": f"first {sample} rows, oracle/spmv.cpp row-order scatter"}
+    return out
+
+
+def suite_spmm(s: Suite) -> dict:
+    """C = A B, A the power-law generator at 1M x 1M (seed 9), B and C row-major with 64
+    columns (the float4 path), beta 0."""
+    from muda_b200 import capi, synth
+    torch = s.torch
+    rows, n = (1 << 20) // s.scale, 64
+    mtx = synth.powerlaw_csr(torch, rows, rows, seed=9)
+    b = synth.uniform_pm1(torch, rows * n, seed=10)
+    c = torch.zeros(rows * n, dtype=torch.float32, device="cuda")
+    L = capi.cusparse()
+    h, ma = _csr_handle(L, s, mtx, rows, rows)
+    mb, mc = C.c_void_p(), C.c_void_p()
+    assert L.cusparseCreateDnMat(C.byref(mb), rows, n, n, C.c_void_p(b.data_ptr()), 0,
+                                 capi.CUSPARSE_ORDER_ROW) == 0
+    assert L.cusparseCreateDnMat(C.byref(mc), rows, n, n, C.c_void_p(c.data_ptr()), 0,
+                                 capi.CUSPARSE_ORDER_ROW) == 0
+    one, zero = C.c_float(1.0), C.c_float(0.0)
+    ms, launches = s.time(lambda: L.cusparseSpMM(h, 0, 0, C.byref(one), ma, mb, C.byref(zero), mc,
+                                                 0, 0, None), flush=True)
+    for fn, d in (("cusparseDestroyDnMat", mb), ("cusparseDestroyDnMat", mc),
+                  ("cusparseDestroySpMat", ma)):
+        assert getattr(L, fn)(d) == 0
+    assert L.cusparseDestroy(h) == 0
+    nnz = mtx["nnz"]
+    alg_bytes = nnz * 8 + (rows + 1) * 4 + 2 * rows * n * 4
+    gbs = alg_bytes / (ms * 1e-3) / 1e9
+    out = {"value": gbs, "unit": "GB/s", "ms": ms, "dtype": "f32/i32",
+           "gflops": 2 * nnz * n / (ms * 1e-3) / 1e9,
+           "config": f"{rows} rows, nnz {nnz}, N {n} row-major, L2 flushed before each call; "
+                     "bytes = A + B + C once (B rows re-gathered per entry come through L2)",
+           "roofline": s.roof("spmm_rows<4,true,true>", gbs, "hbm"), "launches": launches,
+           "algorithmic_bytes_per_call": alg_bytes}
+    if s.cpu:
+        import oracle
+        sample = max(1, rows // 64)
+        ro = mtx["row_offsets"][: sample + 1].cpu().numpy()
+        ci = mtx["col_ind"][: int(ro[-1])].cpu().numpy()
+        va = mtx["values"][: int(ro[-1])].cpu().numpy()
+        bb = b.cpu().numpy()
+        cc = np.zeros(sample * n, np.float32)
+        dt = cpu_time(lambda: oracle.spmm_csr(ro, ci, va, rows, bb, n, 2, cc, n, 2, n,
+                                              threads=os.cpu_count() or 1))
+        sb = int(ro[-1]) * 8 + (sample + 1) * 4 + 2 * sample * n * 4
+        out["cpu_baseline"] = {"value": sb / dt / 1e9, "unit": "GB/s", "cores": os.cpu_count(),
+                               "kind": "port",
+                               "sample": f"first {sample} rows, oracle/spmv.cpp per-output loop"}
+    return out
+
+
 def suite_fft(s: Suite) -> dict:
     """C2C N = 4096, batch 65536, normal(0,1) re/im seed 3, forward then
     inverse in place; value = bytes moved (read + write, both directions) per second."""
@@ -784,6 +884,8 @@ def suite_gemv(s: Suite, trans: bool) -> dict:
 SUITE = {
     "sgemm": suite_sgemm,
     "spmv": suite_spmv,
+    "spmv_t": suite_spmv_t,
+    "spmm": suite_spmm,
     "fft": suite_fft,
     "fft_real": suite_fft_real,
     "fft_bluestein": suite_fft_bluestein,

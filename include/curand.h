@@ -73,6 +73,15 @@ typedef enum curandOrdering {
   CURAND_ORDERING_QUASI_DEFAULT = 201
 } curandOrdering_t;
 
+/* reference curand.h:72-79 */
+typedef enum curandDirectionVectorSet {
+  CURAND_DIRECTION_VECTORS_32_JOEKUO6 = 101,
+  CURAND_SCRAMBLED_DIRECTION_VECTORS_32_JOEKUO6 = 102,
+  CURAND_DIRECTION_VECTORS_64_JOEKUO6 = 103,
+  CURAND_SCRAMBLED_DIRECTION_VECTORS_64_JOEKUO6 = 104
+} curandDirectionVectorSet_t;
+typedef unsigned int curandDirectionVectors32_t[32];
+
 /* Lifecycle — reference curand_api.mm:44-82 */
 curandStatus_t curandCreateGenerator(curandGenerator_t* generator, curandRngType_t rng_type);
 curandStatus_t curandCreateGeneratorHost(curandGenerator_t* generator, curandRngType_t rng_type);
@@ -85,6 +94,10 @@ curandStatus_t curandSetPseudoRandomGeneratorSeed(curandGenerator_t generator,
                                                   unsigned long long seed);
 curandStatus_t curandSetGeneratorOffset(curandGenerator_t generator, unsigned long long offset);
 curandStatus_t curandSetGeneratorOrdering(curandGenerator_t generator, curandOrdering_t order);
+/* reference curand_api.mm:137-149: 1 .. 20000 dimensions, stored (every generator
+ * runs the Philox stream, as in the reference) */
+curandStatus_t curandSetQuasiRandomGeneratorDimensions(curandGenerator_t generator,
+                                                       unsigned int num_dimensions);
 curandStatus_t curandGetVersion(int* version);
 curandStatus_t curandGetProperty(libraryPropertyType type, int* value);
 
@@ -93,6 +106,30 @@ curandStatus_t curandGenerate(curandGenerator_t generator, unsigned int* outputP
 curandStatus_t curandGenerateUniform(curandGenerator_t generator, float* outputPtr, size_t num);
 curandStatus_t curandGenerateNormal(curandGenerator_t generator, float* outputPtr, size_t n,
                                     float mean, float stddev);
+/* exp of the normal stream; offset advances as for curandGenerateNormal
+ * (reference curand_api.mm:363-409) */
+curandStatus_t curandGenerateLogNormal(curandGenerator_t generator, float* outputPtr, size_t n,
+                                       float mean, float stddev);
+/* Double precision: one Philox block per two values, block index offset / 2,
+ * offset += 2 * ceil(n / 2) (reference curand_context.mm:115-223, curand_api.mm:279-297,
+ * 344-361, 411-438).  The uniform is bit-identical to the reference. */
+curandStatus_t curandGenerateUniformDouble(curandGenerator_t generator, double* outputPtr,
+                                           size_t num);
+curandStatus_t curandGenerateNormalDouble(curandGenerator_t generator, double* outputPtr, size_t n,
+                                          double mean, double stddev);
+curandStatus_t curandGenerateLogNormalDouble(curandGenerator_t generator, double* outputPtr,
+                                             size_t n, double mean, double stddev);
+/* Poisson counts, one Philox block index per output, offset += n (reference
+ * curand_api.mm:440-479, curand_kernels.metal:212-264).  Device and host generators
+ * produce the same stream: extra uniforms come from counter word 2 on both (the
+ * reference's host path steps counter word 1 and computes in double instead). */
+curandStatus_t curandGeneratePoisson(curandGenerator_t generator, unsigned int* outputPtr, size_t n,
+                                     double lambda);
+
+/* Direction vectors and scramble constants — reference curand_api.mm:488-507 */
+curandStatus_t curandGetDirectionVectors32(curandDirectionVectors32_t* vectors[],
+                                           curandDirectionVectorSet_t set);
+curandStatus_t curandGetScrambleConstants32(const unsigned int** constants);
 
 #ifdef __cplusplus
 }

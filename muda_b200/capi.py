@@ -67,6 +67,14 @@ CURAND_PROTOS = {
     "curandGenerate": ([vp, vp, sz], i32),
     "curandGenerateUniform": ([vp, vp, sz], i32),
     "curandGenerateNormal": ([vp, vp, sz, f32, f32], i32),
+    "curandGenerateLogNormal": ([vp, vp, sz, f32, f32], i32),
+    "curandGenerateUniformDouble": ([vp, vp, sz], i32),
+    "curandGenerateNormalDouble": ([vp, vp, sz, C.c_double, C.c_double], i32),
+    "curandGenerateLogNormalDouble": ([vp, vp, sz, C.c_double, C.c_double], i32),
+    "curandGeneratePoisson": ([vp, vp, sz, C.c_double], i32),
+    "curandSetQuasiRandomGeneratorDimensions": ([vp, C.c_uint], i32),
+    "curandGetDirectionVectors32": ([P(vp), i32], i32),
+    "curandGetScrambleConstants32": ([P(vp)], i32),
 }
 
 

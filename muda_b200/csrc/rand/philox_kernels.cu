@@ -60,12 +60,17 @@ struct FillArgs {
   KeySchedule key;
   float mean;
   float stddev;
+  double mean_d, stddev_d;    // double-precision streams
+  float lambda, exp_neg_lambda;  // Poisson
 };
 
-__device__ __forceinline__ uint4 philox_block(std::uint64_t ctr, const KeySchedule& key) {
+// Counter (ctr_lo, ctr_hi, c2_in, 0): word 2 is 0 except for the Poisson
+// stream's extra blocks.
+__device__ __forceinline__ uint4 philox_block(std::uint64_t ctr, const KeySchedule& key,
+                                              std::uint32_t c2_in = 0u) {
   std::uint32_t c0 = static_cast<std::uint32_t>(ctr);
   std::uint32_t c1 = static_cast<std::uint32_t>(ctr >> 32);
-  std::uint32_t c2 = 0u;
+  std::uint32_t c2 = c2_in;
   std::uint32_t c3 = 0u;
 #pragma unroll
   for (int r = 0; r < 10; ++r) {
@@ -228,7 +233,13 @@ template <Dist D, bool Scale, unsigned Pack>
 __device__ __forceinline__ uint4 transform(uint4 r, float mean, float stddev) {
   constexpr bool PC = (Pack & kPackConv) != 0u, PL = (Pack & kPackLog) != 0u;
   constexpr bool PT = (Pack & kPackTrig) != 0u, PO = (Pack & kPackOut) != 0u;
-  if constexpr (D == Dist::kUint32) {
+  if constexpr (D == Dist::kLogNormal) {
+    const uint4 z = transform<Dist::kNormal, Scale, Pack>(r, mean, stddev);
+    return make_uint4(__float_as_uint(expf(__uint_as_float(z.x))),
+                      __float_as_uint(expf(__uint_as_float(z.y))),
+                      __float_as_uint(expf(__uint_as_float(z.z))),
+                      __float_as_uint(expf(__uint_as_float(z.w))));
+  } else if constexpr (D == Dist::kUint32) {
     return r;
   } else if constexpr (D == Dist::kUniform) {
     const Pair a = to_uniform2<PC>(r.x, r.y), b = to_uniform2<PC>(r.z, r.w);
@@ -263,7 +274,8 @@ constexpr unsigned kNormalPack = kPackConv | kPackLog | kPackTrig | kPackOut;
 // store per block (output 16-byte aligned); otherwise four 4-byte stores.
 // Scale is false when stddev == 1 (the multiply is then the identity).
 template <Dist D, bool Vec16, bool Scale = true,
-          unsigned Pack = (D == Dist::kNormal ? kNormalPack : kUniformPack)>
+          unsigned Pack = (D == Dist::kNormal || D == Dist::kLogNormal ? kNormalPack
+                                                                       : kUniformPack)>
 __global__ void __launch_bounds__(kThreads) philox_fill_kernel(const FillArgs a) {
   const std::uint64_t full_blocks = a.n >> 2;
   const std::uint64_t stride = static_cast<std::uint64_t>(gridDim.x) * kThreads;
@@ -295,7 +307,7 @@ __global__ void __launch_bounds__(kThreads) philox_fill_kernel(const FillArgs a)
 
 template <Dist D>
 cudaError_t launch_dist(const FillArgs& a, bool vec16, unsigned grid, cudaStream_t stream) {
-  const bool scale = D == Dist::kNormal && a.stddev != 1.0f;
+  const bool scale = (D == Dist::kNormal || D == Dist::kLogNormal) && a.stddev != 1.0f;
   if (vec16) {
     if (scale)
       philox_fill_kernel<D, true, true><<<grid, kThreads, 0, stream>>>(a);
@@ -307,6 +319,124 @@ cudaError_t launch_dist(const FillArgs& a, bool vec16, unsigned grid, cudaStream
     else
       philox_fill_kernel<D, false, false><<<grid, kThreads, 0, stream>>>(a);
   }
+  return cudaGetLastError();
+}
+
+// ------------------------------------------------------ double precision --
+// The 53-bit integers and the uniform (m + 1) * 2^-53 are exact, so that stream is
+// bit-identical to the reference's; the normal uses the device's double log,
+// sqrt and sincos (each within an ulp or two of the host's), every multiply and
+// add of the formula rounded separately.
+template <Dist D>
+__device__ __forceinline__ double2 transform_f64(uint4 r, double mean, double stddev) {
+  constexpr unsigned long long kMask = 0x1FFFFFFFFFFFFFull;
+  constexpr double kTwoPowMinus53 = 1.1102230246251565404236316680908203125e-16;
+  const unsigned long long m0 =
+      ((static_cast<unsigned long long>(r.x) << 21) ^ static_cast<unsigned long long>(r.y)) & kMask;
+  const unsigned long long m1 =
+      ((static_cast<unsigned long long>(r.z) << 21) ^ static_cast<unsigned long long>(r.w)) & kMask;
+  const double u0 = __dmul_rn(__dadd_rn(static_cast<double>(m0), 1.0), kTwoPowMinus53);
+  const double u1 = __dmul_rn(__dadd_rn(static_cast<double>(m1), 1.0), kTwoPowMinus53);
+  if constexpr (D == Dist::kUniformDouble) {
+    return make_double2(u0, u1);
+  } else {
+    const double rad = sqrt(__dmul_rn(-2.0, log(u0)));
+    const double theta = __dmul_rn(6.283185307179586476925286766559, u1);
+    double sn, cs;
+    sincos(theta, &sn, &cs);
+    double z0 = __dadd_rn(__dmul_rn(__dmul_rn(rad, cs), stddev), mean);
+    double z1 = __dadd_rn(__dmul_rn(__dmul_rn(rad, sn), stddev), mean);
+    if constexpr (D == Dist::kLogNormalDouble) {
+      z0 = exp(z0);
+      z1 = exp(z1);
+    }
+    return make_double2(z0, z1);
+  }
+}
+
+template <Dist D, bool Vec16>
+__global__ void __launch_bounds__(kThreads) philox_fill_f64_kernel(const FillArgs a) {
+  const std::uint64_t full_blocks = a.n >> 1;
+  const std::uint64_t stride = static_cast<std::uint64_t>(gridDim.x) * kThreads;
+  std::uint64_t b = static_cast<std::uint64_t>(blockIdx.x) * kThreads + threadIdx.x;
+  double* out = static_cast<double*>(a.out);
+  for (; b < full_blocks; b += stride) {
+    const double2 v = transform_f64<D>(philox_block(a.first_block + b, a.key), a.mean_d, a.stddev_d);
+    if constexpr (Vec16) {
+      reinterpret_cast<double2*>(out)[b] = v;
+    } else {
+      out[2 * b] = v.x;
+      out[2 * b + 1] = v.y;
+    }
+  }
+  if ((a.n & 1u) != 0 && b == full_blocks)
+    out[2 * b] = transform_f64<D>(philox_block(a.first_block + b, a.key), a.mean_d, a.stddev_d).x;
+}
+
+// --------------------------------------------------------------- Poisson --
+__device__ __forceinline__ float uniform_of(std::uint32_t v) {
+  return __fmul_rn(__fadd_rn(static_cast<float>(v), 1.0f), 2.3283064365386963e-10f);
+}
+
+__global__ void __launch_bounds__(kThreads) philox_poisson_kernel(const FillArgs a) {
+  const std::uint64_t stride = static_cast<std::uint64_t>(gridDim.x) * kThreads;
+  unsigned int* out = static_cast<unsigned int*>(a.out);
+  for (std::uint64_t i = static_cast<std::uint64_t>(blockIdx.x) * kThreads + threadIdx.x;
+       i < a.n; i += stride) {
+    const std::uint64_t ctr = a.first_block + i;
+    uint4 r = philox_block(ctr, a.key);
+    unsigned int result;
+    if (a.lambda < 30.0f) {
+      float p = 1.0f;
+      unsigned int k = 0, sub = 0, word = 0;
+      while (p > a.exp_neg_lambda && k < 1000u) {
+        ++k;
+        const std::uint32_t v = word == 0 ? r.x : (word == 1 ? r.y : (word == 2 ? r.z : r.w));
+        p = __fmul_rn(p, uniform_of(v));
+        if (++word == 4) {
+          word = 0;
+          r = philox_block(ctr, a.key, ++sub);
+        }
+      }
+      result = k > 0 ? k - 1 : 0u;
+    } else {
+      const float u0 = uniform_of(r.x), u1 = uniform_of(r.y);
+      const float z = __fmul_rn(sqrtf(__fmul_rn(-2.0f, logf(u0))),
+                                cosf(__fmul_rn(6.28318530717958647692f, u1)));
+      const float val = __fadd_rn(__fadd_rn(a.lambda, __fmul_rn(sqrtf(a.lambda), z)), 0.5f);
+      result = val > 0.0f ? static_cast<unsigned int>(val) : 0u;
+    }
+    out[i] = result;
+  }
+}
+
+KeySchedule key_schedule(std::uint64_t seed) {
+  KeySchedule k{};
+  std::uint32_t k0 = static_cast<std::uint32_t>(seed);
+  std::uint32_t k1 = static_cast<std::uint32_t>(seed >> 32);
+  for (int r = 0; r < 10; ++r) {
+    k.k0[r] = k0;
+    k.k1[r] = k1;
+    k0 += 0x9E3779B9u;
+    k1 += 0xBB67AE85u;
+  }
+  return k;
+}
+
+unsigned grid_for(std::uint64_t threads) {
+  const int sms = sm_count(current_device());
+  const std::uint64_t want = (threads + kThreads - 1) / kThreads;
+  const std::uint64_t cap = static_cast<std::uint64_t>(sms > 0 ? sms : 148) * kCtasPerSm;
+  return static_cast<unsigned>(want < 1 ? 1 : (want < cap ? want : cap));
+}
+
+template <Dist D>
+cudaError_t launch_f64(const FillArgs& a, cudaStream_t stream) {
+  const unsigned grid = grid_for((a.n + 1) / 2);
+  if (aligned_to(a.out, 16))
+    philox_fill_f64_kernel<D, true><<<grid, kThreads, 0, stream>>>(a);
+  else
+    philox_fill_f64_kernel<D, false><<<grid, kThreads, 0, stream>>>(a);
   return cudaGetLastError();
 }
 
@@ -347,8 +477,50 @@ cudaError_t launch_philox_fill(Dist dist, void* out, std::uint64_t n, std::uint6
       return launch_dist<Dist::kUniform>(a, vec16, grid, stream);
     case Dist::kNormal:
       return launch_dist<Dist::kNormal>(a, vec16, grid, stream);
+    case Dist::kLogNormal:
+      return launch_dist<Dist::kLogNormal>(a, vec16, grid, stream);
+    default:
+      return cudaErrorInvalidValue;
   }
-  return cudaErrorInvalidValue;
+}
+
+cudaError_t launch_philox_fill_f64(Dist dist, double* out, std::uint64_t n, std::uint64_t seed,
+                                   std::uint64_t first_block, double mean, double stddev,
+                                   cudaStream_t stream) noexcept {
+  if (n == 0) return cudaSuccess;
+  if (!aligned_to(out, 8)) return cudaErrorInvalidValue;
+  FillArgs a{};
+  a.out = out;
+  a.n = n;
+  a.first_block = first_block;
+  a.mean_d = mean;
+  a.stddev_d = stddev;
+  a.key = key_schedule(seed);
+  switch (dist) {
+    case Dist::kUniformDouble:
+      return launch_f64<Dist::kUniformDouble>(a, stream);
+    case Dist::kNormalDouble:
+      return launch_f64<Dist::kNormalDouble>(a, stream);
+    case Dist::kLogNormalDouble:
+      return launch_f64<Dist::kLogNormalDouble>(a, stream);
+    default:
+      return cudaErrorInvalidValue;
+  }
+}
+
+cudaError_t launch_philox_poisson(unsigned int* out, std::uint64_t n, std::uint64_t seed,
+                                  std::uint64_t first_block, float lambda, float exp_neg_lambda,
+                                  cudaStream_t stream) noexcept {
+  if (n == 0) return cudaSuccess;
+  FillArgs a{};
+  a.out = out;
+  a.n = n;
+  a.first_block = first_block;
+  a.lambda = lambda;
+  a.exp_neg_lambda = exp_neg_lambda;
+  a.key = key_schedule(seed);
+  philox_poisson_kernel<<<grid_for(n), kThreads, 0, stream>>>(a);
+  return cudaGetLastError();
 }
 
 }  // namespace mb200::rand

@@ -196,44 +196,86 @@ __device__ __forceinline__ Vec<VEC> load_b(const DenseView& b, std::int64_t r, s
   return out;
 }
 
-// Non-transposed A: warp per row, lane columns c0 + lane*VEC .. +VEC.
-template <int VEC, bool BROW, bool CROW>
+// acc[v] = fma(a_k, B(col_k, col + v), acc[v]) over the entries k in [s, e), in
+// order.  The G lanes of a group (shuffle mask `mask`) read the entries G at a time
+// (coalesced) and broadcast them; the B rows of kDepth entries are loaded before
+// their fmas, so kDepth gathers are in flight per lane (a power-law row of
+// thousands of entries is one sequential chain: its latency, not bandwidth, is the
+// limit).
+constexpr int kDepth = 4;
+
+template <int VEC, int G, bool BROW>
+__device__ __forceinline__ void accumulate_range(const CsrView& a, const DenseView& b, int s, int e,
+                                                 int gl, unsigned mask, std::int64_t col,
+                                                 bool live, float (&acc)[VEC]) {
+  constexpr int D = kDepth < G ? kDepth : G;
+  const float* vals = static_cast<const float*>(a.values);
+  for (int k0 = s; k0 < e; k0 += G) {
+    int kk = -1;
+    float vv = 0.0f;
+    if (k0 + gl < e) {
+      kk = __ldg(a.col_ind + k0 + gl) - a.base;
+      vv = __ldg(vals + k0 + gl);
+    }
+    const int cnt = (e - k0 < G) ? e - k0 : G;
+    int j = 0;
+    for (; j + D <= cnt; j += D) {
+      int k[D];
+      float av[D];
+      Vec<VEC> bv[D];
+#pragma unroll
+      for (int u = 0; u < D; ++u) {
+        k[u] = __shfl_sync(mask, kk, j + u, G);
+        av[u] = __shfl_sync(mask, vv, j + u, G);
+        if (static_cast<unsigned>(k[u]) < static_cast<unsigned long long>(a.cols) && live)
+          bv[u] = load_b<VEC, BROW>(b, k[u], col);
+      }
+#pragma unroll
+      for (int u = 0; u < D; ++u) {
+        if (static_cast<unsigned>(k[u]) < static_cast<unsigned long long>(a.cols) && live) {
+#pragma unroll
+          for (int v = 0; v < VEC; ++v) acc[v] = fmaf(av[u], bv[u].v[v], acc[v]);
+        }
+      }
+    }
+    for (; j < cnt; ++j) {
+      const int k = __shfl_sync(mask, kk, j, G);
+      const float av = __shfl_sync(mask, vv, j, G);
+      if (static_cast<unsigned>(k) < static_cast<unsigned long long>(a.cols) && live) {
+        const Vec<VEC> bv = load_b<VEC, BROW>(b, k, col);
+#pragma unroll
+        for (int v = 0; v < VEC; ++v) acc[v] = fmaf(av, bv.v[v], acc[v]);
+      }
+    }
+  }
+}
+
+// Non-transposed A: groups of G lanes per row (32 / G rows per warp), lane gl of a
+// group owning columns cb + gl*VEC .. +VEC of each G*VEC-column block; every output
+// is summed in entry order (bit-identical to the reference).
+template <int VEC, int G, bool BROW, bool CROW>
 __global__ void __launch_bounds__(kWarps * 32)
     spmm_rows(const CsrView a, const DenseView b, const DenseView c, std::int64_t ncols,
               float alpha, float beta) {
+  constexpr int RPW = 32 / G;
   const int lane = threadIdx.x & 31;
-  const float* vals = static_cast<const float*>(a.values);
+  const int g = lane / G, gl = lane % G;
+  const unsigned mask = (G == 32) ? kFull : (((1u << G) - 1u) << (g * G));
   const std::int64_t warp0 = static_cast<std::int64_t>(blockIdx.x) * kWarps + (threadIdx.x >> 5);
   const std::int64_t nwarps = static_cast<std::int64_t>(gridDim.x) * kWarps;
-  for (std::int64_t row = warp0; row < a.rows; row += nwarps) {
-    int s = clamp_off(a.row_offsets[row], a.base, a.nnz);
+  for (std::int64_t row0 = warp0 * RPW; row0 < a.rows; row0 += nwarps * RPW) {
+    const std::int64_t row = row0 + g;
+    if (row >= a.rows) continue;  // the whole group leaves together
+    const int s = clamp_off(a.row_offsets[row], a.base, a.nnz);
     const int e0 = clamp_off(a.row_offsets[row + 1], a.base, a.nnz);
     const int e = e0 < s ? s : e0;
-    for (std::int64_t cb = 0; cb < ncols; cb += 32 * VEC) {
-      const std::int64_t col = cb + static_cast<std::int64_t>(lane) * VEC;
+    for (std::int64_t cb = 0; cb < ncols; cb += G * VEC) {
+      const std::int64_t col = cb + static_cast<std::int64_t>(gl) * VEC;
       const bool live = col < ncols;
       float acc[VEC];
 #pragma unroll
       for (int v = 0; v < VEC; ++v) acc[v] = 0.0f;
-      for (int k0 = s; k0 < e; k0 += 32) {
-        int kk = -1;
-        float vv = 0.0f;
-        if (k0 + lane < e) {
-          kk = __ldg(a.col_ind + k0 + lane) - a.base;
-          vv = __ldg(vals + k0 + lane);
-        }
-        const int cnt = (e - k0 < 32) ? e - k0 : 32;
-#pragma unroll 4
-        for (int j = 0; j < cnt; ++j) {
-          const int k = __shfl_sync(kFull, kk, j);
-          const float av = __shfl_sync(kFull, vv, j);
-          if (static_cast<unsigned>(k) < static_cast<unsigned long long>(a.cols) && live) {
-            const Vec<VEC> bv = load_b<VEC, BROW>(b, k, col);
-#pragma unroll
-            for (int v = 0; v < VEC; ++v) acc[v] = fmaf(av, bv.v[v], acc[v]);
-          }
-        }
-      }
+      accumulate_range<VEC, G, BROW>(a, b, s, e, gl, mask, col, live, acc);
       if (live) {
 #pragma unroll
         for (int v = 0; v < VEC; ++v) {
@@ -298,19 +340,30 @@ __global__ void __launch_bounds__(kWarps * 32)
   }
 }
 
+template <int VEC, bool BROW, bool CROW>
+cudaError_t spmm_rows_group(const CsrView& a, const DenseView& b, const DenseView& c,
+                            std::int64_t ncols, float alpha, float beta, cudaStream_t st) {
+  // lanes per row: enough for one pass over the columns, at least 4
+  const std::int64_t lanes = (ncols + VEC - 1) / VEC;
+  const int G = lanes > 16 ? 32 : (lanes > 8 ? 16 : (lanes > 4 ? 8 : 4));
+  const unsigned grid = grid_for((a.rows + 32 / G - 1) / (32 / G), kWarps, 16);
+  switch (G) {
+    case 4: spmm_rows<VEC, 4, BROW, CROW><<<grid, kWarps * 32, 0, st>>>(a, b, c, ncols, alpha, beta); break;
+    case 8: spmm_rows<VEC, 8, BROW, CROW><<<grid, kWarps * 32, 0, st>>>(a, b, c, ncols, alpha, beta); break;
+    case 16: spmm_rows<VEC, 16, BROW, CROW><<<grid, kWarps * 32, 0, st>>>(a, b, c, ncols, alpha, beta); break;
+    default: spmm_rows<VEC, 32, BROW, CROW><<<grid, kWarps * 32, 0, st>>>(a, b, c, ncols, alpha, beta); break;
+  }
+  return cudaGetLastError();
+}
+
 template <bool BROW, bool CROW>
 cudaError_t spmm_rows_launch(const CsrView& a, const DenseView& b, const DenseView& c,
                              std::int64_t ncols, float alpha, float beta, bool vec4,
                              cudaStream_t st) {
-  const unsigned grid = grid_for(a.rows, kWarps, 16);
   if constexpr (BROW && CROW) {
-    if (vec4) {
-      spmm_rows<4, true, true><<<grid, kWarps * 32, 0, st>>>(a, b, c, ncols, alpha, beta);
-      return cudaGetLastError();
-    }
+    if (vec4) return spmm_rows_group<4, true, true>(a, b, c, ncols, alpha, beta, st);
   }
-  spmm_rows<1, BROW, CROW><<<grid, kWarps * 32, 0, st>>>(a, b, c, ncols, alpha, beta);
-  return cudaGetLastError();
+  return spmm_rows_group<1, BROW, CROW>(a, b, c, ncols, alpha, beta, st);
 }
 
 bool row_contiguous(const DenseView& d) { return d.col_major == d.trans; }

@@ -85,6 +85,41 @@ def generate_normal(seed: int, offset: int, n: int, mean: float = 0.0, stddev: f
     return out, int(nxt)
 
 
+def generate_lognormal(seed: int, offset: int, n: int, mean: float = 0.0, stddev: float = 1.0,
+                       threads: int = 1) -> tuple[np.ndarray, int]:
+    """GenerateHostLogNormal (curand_context.mm:225-235)."""
+    out = np.empty(n, dtype=np.float32)
+    nxt = lib().oracle_generate_lognormal(seed, offset, out.ctypes.data, n, mean, stddev, threads)
+    return out, int(nxt)
+
+
+def generate_double(seed: int, offset: int, n: int, kind: str = "uniform", mean: float = 0.0,
+                    stddev: float = 1.0, threads: int = 1) -> tuple[np.ndarray, int]:
+    """Double streams of the reference host generator (curand_context.mm:115-143,
+    187-247); kind "uniform", "normal" or "lognormal"."""
+    k = {"uniform": 0, "normal": 1, "lognormal": 2}[kind]
+    out = np.empty(n, dtype=np.float64)
+    nxt = lib().oracle_generate_double(seed, offset, out.ctypes.data, n, k, mean, stddev, threads)
+    return out, int(nxt)
+
+
+def poisson_threshold(lam: float) -> np.float32:
+    """exp(-lambda) of the fp32 lambda, rounded once from double (the library's
+    threshold for Knuth's method)."""
+    return np.float32(np.exp(-np.float64(np.float32(lam))))
+
+
+def generate_poisson(seed: int, offset: int, n: int, lam: float, *, reference_host=False,
+                     threads: int = 8) -> tuple[np.ndarray, int]:
+    """Poisson counts: the device-kernel definition (curand_kernels.metal:212-264), or
+    with reference_host=True the reference's own host path (curand_context.mm:249-293)."""
+    out = np.empty(n, dtype=np.uint32)
+    nxt = lib().oracle_generate_poisson(seed, offset, out.ctypes.data, n, lam,
+                                        float(poisson_threshold(lam)), int(reference_host),
+                                        threads)
+    return out, int(nxt)
+
+
 def philox_gather(ctrs: np.ndarray, seed: int, threads: int = 8) -> np.ndarray:
     """Philox blocks at the given counters, shape (len(ctrs), 4)."""
     ctrs = np.ascontiguousarray(ctrs, dtype=np.uint64)

@@ -28,6 +28,15 @@ extern "C" {
 
 /* ---- Philox4x32-10 (libraries/rand/src/curand_context.mm:42-185) ---- */
 void oracle_philox_block(uint64_t ctr, uint64_t seed, uint32_t out[4]);
+void oracle_philox_block4(uint64_t ctr, uint32_t c2, uint64_t seed, uint32_t out[4]);
+uint64_t oracle_generate_lognormal(uint64_t seed, uint64_t offset, float* out, size_t n,
+                                   float mean, float stddev, int threads);
+/* kind 0 uniform, 1 normal, 2 log-normal */
+uint64_t oracle_generate_double(uint64_t seed, uint64_t offset, double* out, size_t n, int kind,
+                                double mean, double stddev, int threads);
+/* mode 0: device-kernel definition (this library); mode 1: the reference's host path */
+uint64_t oracle_generate_poisson(uint64_t seed, uint64_t offset, uint32_t* out, size_t n,
+                                 double lambda, float exp_neg_lambda, int mode, int threads);
 /* Writes n words of the stream that starts at generator offset `offset`;
  * returns the generator offset after the call (offset + 4*ceil(n/4)). */
 uint64_t oracle_generate_uint(uint64_t seed, uint64_t offset, uint32_t* out, size_t n,

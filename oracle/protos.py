@@ -49,6 +49,12 @@ _PROTOS: list[tuple[str, list, object]] = [
                         C.c_int64, C.c_int, C.c_int, vp, C.c_int], None),
     ("oracle_spmv_csr", [C.c_int64, vp, vp, vp, C.c_int, vp, vp, C.c_float, C.c_float, vp,
                          vp, C.c_int], None),
+    ("oracle_generate_lognormal", [C.c_uint64, C.c_uint64, vp, C.c_size_t, C.c_float, C.c_float,
+                                   C.c_int], C.c_uint64),
+    ("oracle_generate_double", [C.c_uint64, C.c_uint64, vp, C.c_size_t, C.c_int, C.c_double,
+                                C.c_double, C.c_int], C.c_uint64),
+    ("oracle_generate_poisson", [C.c_uint64, C.c_uint64, vp, C.c_size_t, C.c_double, C.c_float,
+                                 C.c_int, C.c_int], C.c_uint64),
     ("oracle_spmv_csr_t", [C.c_int64, C.c_int64, vp, vp, vp, C.c_int, vp, vp, C.c_float,
                            C.c_float, C.c_int, vp, vp], None),
     ("oracle_spmm_csr", [C.c_int64, C.c_int64, vp, vp, vp, C.c_int, C.c_int, vp, C.c_int64,

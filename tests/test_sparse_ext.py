@@ -233,7 +233,7 @@ def test_gpu_spmv_f16(cuda, built, trans, kind):
 
 # (rows, cols, ncols): odd sizes, one that fills several 32-column chunks, and a
 # float4-eligible one (ncols and ld multiples of 4)
-SPMM_SHAPES = [(300, 200, 7), (257, 300, 130), (500, 400, 64)]
+SPMM_SHAPES = [(300, 200, 7), (257, 300, 130), (500, 400, 64), (600, 3000, 64)]
 
 
 @pytest.mark.gpu
@@ -244,7 +244,7 @@ def test_gpu_spmm(cuda, built, shape, op_a, op_b, order_b, order_c):
     torch = cuda
     rows, cols, n = shape
     rng = np.random.default_rng(rows + op_a * 10 + op_b * 100 + order_b * 1000 + order_c)
-    offsets, ci, va = _matrix("mixed_long" if rows == 257 else "avg16", rng, rows, cols)
+    offsets, ci, va = _matrix("mixed_long" if rows in (257, 600) else "avg16", rng, rows, cols)
     k = rows if op_a else cols
     m = cols if op_a else rows
     b_eff = rng.uniform(-1, 1, (k, n)).astype(np.float32)

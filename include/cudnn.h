@@ -69,10 +69,50 @@ typedef enum {
 
 typedef enum { CUDNN_SOFTMAX_MODE_INSTANCE = 0, CUDNN_SOFTMAX_MODE_CHANNEL = 1 } cudnnSoftmaxMode_t;
 
+/* reference cudnn.h:72-136 */
+typedef enum {
+  CUDNN_CONVOLUTION_BWD_DATA_ALGO_0 = 0,
+  CUDNN_CONVOLUTION_BWD_DATA_ALGO_1 = 1
+} cudnnConvolutionBwdDataAlgo_t;
+
+typedef enum {
+  CUDNN_CONVOLUTION_BWD_FILTER_ALGO_0 = 0,
+  CUDNN_CONVOLUTION_BWD_FILTER_ALGO_1 = 1
+} cudnnConvolutionBwdFilterAlgo_t;
+
+typedef enum {
+  CUDNN_ACTIVATION_SIGMOID = 0,
+  CUDNN_ACTIVATION_RELU = 1,
+  CUDNN_ACTIVATION_TANH = 2,
+  CUDNN_ACTIVATION_CLIPPED_RELU = 3,
+  CUDNN_ACTIVATION_ELU = 4,
+  CUDNN_ACTIVATION_IDENTITY = 5,
+  CUDNN_ACTIVATION_SWISH = 6
+} cudnnActivationMode_t;
+
+typedef enum { CUDNN_NOT_PROPAGATE_NAN = 0, CUDNN_PROPAGATE_NAN = 1 } cudnnNanPropagation_t;
+
+typedef enum {
+  CUDNN_POOLING_MAX = 0,
+  CUDNN_POOLING_AVERAGE_COUNT_INCLUDE_PADDING = 1,
+  CUDNN_POOLING_AVERAGE_COUNT_EXCLUDE_PADDING = 2,
+  CUDNN_POOLING_MAX_DETERMINISTIC = 3
+} cudnnPoolingMode_t;
+
+typedef enum {
+  CUDNN_BATCHNORM_PER_ACTIVATION = 0,
+  CUDNN_BATCHNORM_SPATIAL = 1,
+  CUDNN_BATCHNORM_SPATIAL_PERSISTENT = 2
+} cudnnBatchNormMode_t;
+
 struct cudnnContext;
 struct cudnnTensorStruct;
 struct cudnnFilterStruct;
 struct cudnnConvolutionStruct;
+struct cudnnActivationStruct;
+struct cudnnPoolingStruct;
+typedef struct cudnnActivationStruct* cudnnActivationDescriptor_t;
+typedef struct cudnnPoolingStruct* cudnnPoolingDescriptor_t;
 typedef struct cudnnContext* cudnnHandle_t;
 typedef struct cudnnTensorStruct* cudnnTensorDescriptor_t;
 typedef struct cudnnFilterStruct* cudnnFilterDescriptor_t;
@@ -123,6 +163,31 @@ cudnnStatus_t cudnnGetConvolution2dForwardOutputDim(cudnnConvolutionDescriptor_t
                                                     int* c, int* h, int* w);
 cudnnStatus_t cudnnDestroyConvolutionDescriptor(cudnnConvolutionDescriptor_t convDesc);
 
+/* Activation and pooling descriptors — reference cudnn_descriptors.mm:382-484 */
+cudnnStatus_t cudnnCreateActivationDescriptor(cudnnActivationDescriptor_t* activationDesc);
+cudnnStatus_t cudnnSetActivationDescriptor(cudnnActivationDescriptor_t activationDesc,
+                                           cudnnActivationMode_t mode,
+                                           cudnnNanPropagation_t reluNanOpt, double coef);
+cudnnStatus_t cudnnGetActivationDescriptor(cudnnActivationDescriptor_t activationDesc,
+                                           cudnnActivationMode_t* mode,
+                                           cudnnNanPropagation_t* reluNanOpt, double* coef);
+cudnnStatus_t cudnnDestroyActivationDescriptor(cudnnActivationDescriptor_t activationDesc);
+cudnnStatus_t cudnnCreatePoolingDescriptor(cudnnPoolingDescriptor_t* poolingDesc);
+cudnnStatus_t cudnnSetPooling2dDescriptor(cudnnPoolingDescriptor_t poolingDesc,
+                                          cudnnPoolingMode_t mode,
+                                          cudnnNanPropagation_t maxpoolingNanOpt, int windowHeight,
+                                          int windowWidth, int verticalPadding,
+                                          int horizontalPadding, int verticalStride,
+                                          int horizontalStride);
+cudnnStatus_t cudnnGetPooling2dForwardOutputDim(cudnnPoolingDescriptor_t poolingDesc,
+                                                cudnnTensorDescriptor_t inputTensorDesc, int* n,
+                                                int* c, int* h, int* w);
+cudnnStatus_t cudnnDestroyPoolingDescriptor(cudnnPoolingDescriptor_t poolingDesc);
+/* reference cudnn_descriptors.mm:486-500 */
+cudnnStatus_t cudnnDeriveBNTensorDescriptor(cudnnTensorDescriptor_t derivedBnDesc,
+                                            cudnnTensorDescriptor_t xDesc,
+                                            cudnnBatchNormMode_t mode);
+
 /* Operations — reference cudnn_ops.mm:89-193 (conv) and cudnn_ops.mm:625-720 (softmax) */
 cudnnStatus_t cudnnGetConvolutionForwardWorkspaceSize(
     cudnnHandle_t handle, cudnnTensorDescriptor_t xDesc, cudnnFilterDescriptor_t wDesc,
@@ -139,6 +204,53 @@ cudnnStatus_t cudnnSoftmaxForward(cudnnHandle_t handle, cudnnSoftmaxAlgorithm_t 
                                   cudnnSoftmaxMode_t mode, const void* alpha,
                                   cudnnTensorDescriptor_t xDesc, const void* x, const void* beta,
                                   cudnnTensorDescriptor_t yDesc, void* y);
+
+/* Neighbours of the convolution, fp32 — reference cudnn_ops.mm:195-624, 722-902.
+ * Backward data, AddTensor, ReLU / clipped ReLU / identity and pooling give the
+ * reference's per-output arithmetic exactly; the reductions (backward filter and
+ * bias, batch-norm training statistics) are deterministic but summed in a
+ * different order than the reference's single sequential loop.  The algo and
+ * workspace arguments of the backward calls are ignored: the backward filter's
+ * partial sums live in the handle's workspace. */
+cudnnStatus_t cudnnConvolutionBackwardData(cudnnHandle_t handle, const void* alpha,
+                                           cudnnFilterDescriptor_t wDesc, const void* w,
+                                           cudnnTensorDescriptor_t dyDesc, const void* dy,
+                                           cudnnConvolutionDescriptor_t convDesc,
+                                           cudnnConvolutionBwdDataAlgo_t algo, void* workSpace,
+                                           size_t workSpaceSizeInBytes, const void* beta,
+                                           cudnnTensorDescriptor_t dxDesc, void* dx);
+cudnnStatus_t cudnnConvolutionBackwardFilter(cudnnHandle_t handle, const void* alpha,
+                                             cudnnTensorDescriptor_t xDesc, const void* x,
+                                             cudnnTensorDescriptor_t dyDesc, const void* dy,
+                                             cudnnConvolutionDescriptor_t convDesc,
+                                             cudnnConvolutionBwdFilterAlgo_t algo, void* workSpace,
+                                             size_t workSpaceSizeInBytes, const void* beta,
+                                             cudnnFilterDescriptor_t dwDesc, void* dw);
+cudnnStatus_t cudnnConvolutionBackwardBias(cudnnHandle_t handle, const void* alpha,
+                                           cudnnTensorDescriptor_t dyDesc, const void* dy,
+                                           const void* beta, cudnnTensorDescriptor_t dbDesc,
+                                           void* db);
+cudnnStatus_t cudnnAddTensor(cudnnHandle_t handle, const void* alpha, cudnnTensorDescriptor_t aDesc,
+                             const void* A, const void* beta, cudnnTensorDescriptor_t cDesc,
+                             void* C);
+cudnnStatus_t cudnnActivationForward(cudnnHandle_t handle,
+                                     cudnnActivationDescriptor_t activationDesc, const void* alpha,
+                                     cudnnTensorDescriptor_t xDesc, const void* x, const void* beta,
+                                     cudnnTensorDescriptor_t yDesc, void* y);
+cudnnStatus_t cudnnPoolingForward(cudnnHandle_t handle, cudnnPoolingDescriptor_t poolingDesc,
+                                  const void* alpha, cudnnTensorDescriptor_t xDesc, const void* x,
+                                  const void* beta, cudnnTensorDescriptor_t yDesc, void* y);
+cudnnStatus_t cudnnBatchNormalizationForwardInference(
+    cudnnHandle_t handle, cudnnBatchNormMode_t mode, const void* alpha, const void* beta,
+    cudnnTensorDescriptor_t xDesc, const void* x, cudnnTensorDescriptor_t yDesc, void* y,
+    cudnnTensorDescriptor_t bnScaleBiasMeanVarDesc, const void* bnScale, const void* bnBias,
+    const void* estimatedMean, const void* estimatedVariance, double epsilon);
+cudnnStatus_t cudnnBatchNormalizationForwardTraining(
+    cudnnHandle_t handle, cudnnBatchNormMode_t mode, const void* alpha, const void* beta,
+    cudnnTensorDescriptor_t xDesc, const void* x, cudnnTensorDescriptor_t yDesc, void* y,
+    cudnnTensorDescriptor_t bnScaleBiasMeanVarDesc, const void* bnScale, const void* bnBias,
+    double exponentialAverageFactor, void* resultRunningMean, void* resultRunningVariance,
+    double epsilon, void* resultSaveMean, void* resultSaveInvVariance);
 
 #ifdef __cplusplus
 }

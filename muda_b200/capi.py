@@ -101,6 +101,12 @@ CUDNN_SOFTMAX_ACCURATE = 1
 CUDNN_SOFTMAX_LOG = 2
 CUDNN_SOFTMAX_MODE_INSTANCE = 0
 CUDNN_SOFTMAX_MODE_CHANNEL = 1
+CUDNN_ACTIVATION_SIGMOID, CUDNN_ACTIVATION_RELU, CUDNN_ACTIVATION_TANH = 0, 1, 2
+CUDNN_ACTIVATION_CLIPPED_RELU, CUDNN_ACTIVATION_ELU, CUDNN_ACTIVATION_IDENTITY = 3, 4, 5
+CUDNN_ACTIVATION_SWISH = 6
+CUDNN_POOLING_MAX, CUDNN_POOLING_AVERAGE_COUNT_INCLUDE_PADDING = 0, 1
+CUDNN_POOLING_AVERAGE_COUNT_EXCLUDE_PADDING, CUDNN_POOLING_MAX_DETERMINISTIC = 2, 3
+CUDNN_BATCHNORM_PER_ACTIVATION, CUDNN_BATCHNORM_SPATIAL = 0, 1
 
 _ip = P(i32)
 CUDNN_PROTOS = {
@@ -128,6 +134,25 @@ CUDNN_PROTOS = {
     "cudnnGetConvolutionForwardWorkspaceSize": ([vp, vp, vp, vp, vp, i32, P(sz)], i32),
     "cudnnConvolutionForward": ([vp, vp, vp, vp, vp, vp, vp, i32, vp, sz, vp, vp, vp], i32),
     "cudnnSoftmaxForward": ([vp, i32, i32, vp, vp, vp, vp, vp, vp], i32),
+    "cudnnCreateActivationDescriptor": ([P(vp)], i32),
+    "cudnnSetActivationDescriptor": ([vp, i32, i32, C.c_double], i32),
+    "cudnnGetActivationDescriptor": ([vp, P(i32), P(i32), P(C.c_double)], i32),
+    "cudnnDestroyActivationDescriptor": ([vp], i32),
+    "cudnnCreatePoolingDescriptor": ([P(vp)], i32),
+    "cudnnSetPooling2dDescriptor": ([vp, i32, i32, i32, i32, i32, i32, i32, i32], i32),
+    "cudnnGetPooling2dForwardOutputDim": ([vp, vp, P(i32), P(i32), P(i32), P(i32)], i32),
+    "cudnnDestroyPoolingDescriptor": ([vp], i32),
+    "cudnnDeriveBNTensorDescriptor": ([vp, vp, i32], i32),
+    "cudnnConvolutionBackwardData": ([vp, vp, vp, vp, vp, vp, vp, i32, vp, sz, vp, vp, vp], i32),
+    "cudnnConvolutionBackwardFilter": ([vp, vp, vp, vp, vp, vp, vp, i32, vp, sz, vp, vp, vp], i32),
+    "cudnnConvolutionBackwardBias": ([vp, vp, vp, vp, vp, vp, vp], i32),
+    "cudnnAddTensor": ([vp, vp, vp, vp, vp, vp, vp], i32),
+    "cudnnActivationForward": ([vp, vp, vp, vp, vp, vp, vp, vp], i32),
+    "cudnnPoolingForward": ([vp, vp, vp, vp, vp, vp, vp, vp], i32),
+    "cudnnBatchNormalizationForwardInference": ([vp, i32, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp,
+                                                 vp, C.c_double], i32),
+    "cudnnBatchNormalizationForwardTraining": ([vp, i32, vp, vp, vp, vp, vp, vp, vp, vp, vp,
+                                                C.c_double, vp, vp, C.c_double, vp, vp], i32),
 }
 
 

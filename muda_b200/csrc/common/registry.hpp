@@ -33,6 +33,8 @@ enum class ObjKind : std::uint8_t {
   kDnnTensor = 0x52,
   kDnnFilter = 0x53,
   kDnnConv = 0x54,
+  kDnnActivation = 0x55,
+  kDnnPooling = 0x56,
 };
 
 template <typename T, ObjKind Kind>

@@ -16,8 +16,10 @@
 #include <cuda_runtime_api.h>
 
 #include <cstdint>
+#include <initializer_list>
 #include <memory>
 #include <mutex>
+#include <utility>
 
 #include "common/device.hpp"
 #include "common/lru.hpp"
@@ -68,6 +70,31 @@ struct ConvDesc {
   cudnnConvolutionMode_t mode = CUDNN_CROSS_CORRELATION;
   cudnnDataType_t compute = CUDNN_DATA_FLOAT;
 };
+
+struct ActivationDesc {
+  std::mutex mu;
+  bool configured = false;
+  cudnnActivationMode_t mode = CUDNN_ACTIVATION_RELU;
+  cudnnNanPropagation_t nan_opt = CUDNN_NOT_PROPAGATE_NAN;
+  double coef = 0.0;
+};
+
+struct PoolingDesc {
+  std::mutex mu;
+  bool configured = false;
+  cudnnPoolingMode_t mode = CUDNN_POOLING_MAX;
+  cudnnNanPropagation_t nan_opt = CUDNN_NOT_PROPAGATE_NAN;
+  int win_h = 0, win_w = 0, pad_h = 0, pad_w = 0, stride_h = 1, stride_w = 1;
+};
+
+Registry<ActivationDesc, ObjKind::kDnnActivation>& activations() {
+  static Registry<ActivationDesc, ObjKind::kDnnActivation> r;
+  return r;
+}
+Registry<PoolingDesc, ObjKind::kDnnPooling>& poolings() {
+  static Registry<PoolingDesc, ObjKind::kDnnPooling> r;
+  return r;
+}
 
 Registry<DnnContext, ObjKind::kDnnHandle>& handles() {
   static Registry<DnnContext, ObjKind::kDnnHandle> r;
@@ -605,6 +632,434 @@ cudnnStatus_t cudnnSoftmaxForward(cudnnHandle_t handle, cudnnSoftmaxAlgorithm_t 
                                            al, a, b, st);
   }
   return e == cudaSuccess ? CUDNN_STATUS_SUCCESS : CUDNN_STATUS_EXECUTION_FAILED;
+}
+
+// ------------------------------------------- activation / pooling descriptors --
+// cudnn_descriptors.mm:382-484
+cudnnStatus_t cudnnCreateActivationDescriptor(cudnnActivationDescriptor_t* activationDesc) {
+  if (activationDesc == nullptr) return CUDNN_STATUS_BAD_PARAM;
+  auto h = activations().add<cudnnActivationDescriptor_t>(std::make_shared<ActivationDesc>());
+  if (h == nullptr) return CUDNN_STATUS_ALLOC_FAILED;
+  *activationDesc = h;
+  return CUDNN_STATUS_SUCCESS;
+}
+
+cudnnStatus_t cudnnSetActivationDescriptor(cudnnActivationDescriptor_t activationDesc,
+                                           cudnnActivationMode_t mode,
+                                           cudnnNanPropagation_t reluNanOpt, double coef) {
+  auto d = activations().get(activationDesc);
+  if (!d || mode < CUDNN_ACTIVATION_SIGMOID || mode > CUDNN_ACTIVATION_SWISH)
+    return CUDNN_STATUS_BAD_PARAM;
+  std::lock_guard<std::mutex> g(d->mu);
+  d->configured = true;
+  d->mode = mode;
+  d->nan_opt = reluNanOpt;
+  d->coef = coef;
+  return CUDNN_STATUS_SUCCESS;
+}
+
+cudnnStatus_t cudnnGetActivationDescriptor(cudnnActivationDescriptor_t activationDesc,
+                                           cudnnActivationMode_t* mode,
+                                           cudnnNanPropagation_t* reluNanOpt, double* coef) {
+  auto d = activations().get(activationDesc);
+  if (!d) return CUDNN_STATUS_BAD_PARAM;
+  std::lock_guard<std::mutex> g(d->mu);
+  if (!d->configured) return CUDNN_STATUS_BAD_PARAM;
+  if (mode != nullptr) *mode = d->mode;
+  if (reluNanOpt != nullptr) *reluNanOpt = d->nan_opt;
+  if (coef != nullptr) *coef = d->coef;
+  return CUDNN_STATUS_SUCCESS;
+}
+
+cudnnStatus_t cudnnDestroyActivationDescriptor(cudnnActivationDescriptor_t activationDesc) {
+  return activations().take(activationDesc) ? CUDNN_STATUS_SUCCESS : CUDNN_STATUS_BAD_PARAM;
+}
+
+cudnnStatus_t cudnnCreatePoolingDescriptor(cudnnPoolingDescriptor_t* poolingDesc) {
+  if (poolingDesc == nullptr) return CUDNN_STATUS_BAD_PARAM;
+  auto h = poolings().add<cudnnPoolingDescriptor_t>(std::make_shared<PoolingDesc>());
+  if (h == nullptr) return CUDNN_STATUS_ALLOC_FAILED;
+  *poolingDesc = h;
+  return CUDNN_STATUS_SUCCESS;
+}
+
+cudnnStatus_t cudnnSetPooling2dDescriptor(cudnnPoolingDescriptor_t poolingDesc,
+                                          cudnnPoolingMode_t mode,
+                                          cudnnNanPropagation_t maxpoolingNanOpt, int windowHeight,
+                                          int windowWidth, int verticalPadding,
+                                          int horizontalPadding, int verticalStride,
+                                          int horizontalStride) {
+  auto d = poolings().get(poolingDesc);
+  if (!d || windowHeight <= 0 || windowWidth <= 0 || verticalPadding < 0 ||
+      horizontalPadding < 0 || verticalStride <= 0 || horizontalStride <= 0)
+    return CUDNN_STATUS_BAD_PARAM;
+  if (mode < CUDNN_POOLING_MAX || mode > CUDNN_POOLING_MAX_DETERMINISTIC)
+    return CUDNN_STATUS_BAD_PARAM;
+  std::lock_guard<std::mutex> g(d->mu);
+  d->configured = true;
+  d->mode = mode;
+  d->nan_opt = maxpoolingNanOpt;
+  d->win_h = windowHeight;
+  d->win_w = windowWidth;
+  d->pad_h = verticalPadding;
+  d->pad_w = horizontalPadding;
+  d->stride_h = verticalStride;
+  d->stride_w = horizontalStride;
+  return CUDNN_STATUS_SUCCESS;
+}
+
+cudnnStatus_t cudnnGetPooling2dForwardOutputDim(cudnnPoolingDescriptor_t poolingDesc,
+                                                cudnnTensorDescriptor_t inputTensorDesc, int* n,
+                                                int* c, int* h, int* w) {
+  auto pd = poolings().get(poolingDesc);
+  auto xd = tensors().get(inputTensorDesc);
+  if (!pd || !xd) return CUDNN_STATUS_BAD_PARAM;
+  const TensorSnap xs = snap(*xd);
+  PoolingDesc p;
+  {
+    std::lock_guard<std::mutex> g(pd->mu);
+    p.configured = pd->configured;
+    p.win_h = pd->win_h;
+    p.win_w = pd->win_w;
+    p.pad_h = pd->pad_h;
+    p.pad_w = pd->pad_w;
+    p.stride_h = pd->stride_h;
+    p.stride_w = pd->stride_w;
+  }
+  if (!p.configured || !xs.configured) return CUDNN_STATUS_BAD_PARAM;
+  const int oh = 1 + (xs.v.h + 2 * p.pad_h - p.win_h) / p.stride_h;
+  const int ow = 1 + (xs.v.w + 2 * p.pad_w - p.win_w) / p.stride_w;
+  if (oh <= 0 || ow <= 0) return CUDNN_STATUS_BAD_PARAM;
+  if (n != nullptr) *n = xs.v.n;
+  if (c != nullptr) *c = xs.v.c;
+  if (h != nullptr) *h = oh;
+  if (w != nullptr) *w = ow;
+  return CUDNN_STATUS_SUCCESS;
+}
+
+cudnnStatus_t cudnnDestroyPoolingDescriptor(cudnnPoolingDescriptor_t poolingDesc) {
+  return poolings().take(poolingDesc) ? CUDNN_STATUS_SUCCESS : CUDNN_STATUS_BAD_PARAM;
+}
+
+// cudnn_descriptors.mm:486-500
+cudnnStatus_t cudnnDeriveBNTensorDescriptor(cudnnTensorDescriptor_t derivedBnDesc,
+                                            cudnnTensorDescriptor_t xDesc,
+                                            cudnnBatchNormMode_t mode) {
+  auto xd = tensors().get(xDesc);
+  if (!xd) return CUDNN_STATUS_BAD_PARAM;
+  const TensorSnap xs = snap(*xd);
+  if (!xs.configured) return CUDNN_STATUS_BAD_PARAM;
+  const cudnnDataType_t t = xs.dtype == CUDNN_DATA_HALF ? CUDNN_DATA_FLOAT : xs.dtype;
+  if (mode == CUDNN_BATCHNORM_PER_ACTIVATION)
+    return cudnnSetTensor4dDescriptor(derivedBnDesc, CUDNN_TENSOR_NCHW, t, 1, xs.v.c, xs.v.h,
+                                      xs.v.w);
+  return cudnnSetTensor4dDescriptor(derivedBnDesc, CUDNN_TENSOR_NCHW, t, 1, xs.v.c, 1, 1);
+}
+
+}  // extern "C"
+
+namespace {
+
+bool all_float(std::initializer_list<cudnnDataType_t> ts) {
+  for (auto t : ts)
+    if (t != CUDNN_DATA_FLOAT) return false;
+  return true;
+}
+
+bool spans_ok(std::initializer_list<std::pair<const void*, std::size_t>> spans) {
+  for (const auto& s : spans)
+    if (!mb200::device_span_ok(s.first, s.second * sizeof(float))) return false;
+  return true;
+}
+
+// Runs fn(workspace) with `need` bytes of the handle's workspace, ordered after the
+// previous call that used it (the same protocol as the forward convolution).
+template <class Fn>
+cudnnStatus_t with_workspace(DnnContext& h, std::size_t need, cudaStream_t st, Fn&& fn) {
+  std::lock_guard<std::mutex> lk(h.ws_mu);
+  const int dev = mb200::current_device();
+  if (!h.ws || h.ws->bytes < need || h.ws->device != dev) {
+    h.ws.reset();
+    h.ws = mb200::DeviceBuffer::make(need);
+    if (!h.ws) return CUDNN_STATUS_ALLOC_FAILED;
+  }
+  cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(st, &cap) != cudaSuccess) cap = cudaStreamCaptureStatusNone;
+  const bool ordered = cap == cudaStreamCaptureStatusNone;
+  if (ordered && h.ws_done != nullptr && cudaStreamWaitEvent(st, h.ws_done, 0) != cudaSuccess)
+    return CUDNN_STATUS_EXECUTION_FAILED;
+  if (fn(h.ws->ptr) != cudaSuccess) return CUDNN_STATUS_EXECUTION_FAILED;
+  if (ordered) {
+    if (h.ws_done == nullptr &&
+        cudaEventCreateWithFlags(&h.ws_done, cudaEventDisableTiming) != cudaSuccess) {
+      h.ws_done = nullptr;
+      return CUDNN_STATUS_EXECUTION_FAILED;
+    }
+    if (cudaEventRecord(h.ws_done, st) != cudaSuccess) return CUDNN_STATUS_EXECUTION_FAILED;
+  }
+  return CUDNN_STATUS_SUCCESS;
+}
+
+cudnnStatus_t status_of(cudaError_t e) {
+  return e == cudaSuccess ? CUDNN_STATUS_SUCCESS : CUDNN_STATUS_EXECUTION_FAILED;
+}
+
+}  // namespace
+
+extern "C" {
+
+// cudnn_ops.mm:195-259
+cudnnStatus_t cudnnConvolutionBackwardData(cudnnHandle_t handle, const void* alpha,
+                                           cudnnFilterDescriptor_t wDesc, const void* w,
+                                           cudnnTensorDescriptor_t dyDesc, const void* dy,
+                                           cudnnConvolutionDescriptor_t convDesc,
+                                           cudnnConvolutionBwdDataAlgo_t algo, void* workSpace,
+                                           size_t workSpaceSizeInBytes, const void* beta,
+                                           cudnnTensorDescriptor_t dxDesc, void* dx) {
+  (void)algo;
+  (void)workSpace;
+  (void)workSpaceSizeInBytes;
+  if (alpha == nullptr || beta == nullptr || w == nullptr || dy == nullptr || dx == nullptr)
+    return CUDNN_STATUS_BAD_PARAM;
+  auto h = handles().get(handle);
+  auto dxd = tensors().get(dxDesc);
+  auto fd = filters().get(wDesc);
+  auto cd = convs().get(convDesc);
+  auto dyd = tensors().get(dyDesc);
+  if (!h || !dxd || !fd || !cd || !dyd) return CUDNN_STATUS_BAD_PARAM;
+  ConvPlan plan{};
+  if (!build_conv(*dxd, *fd, *cd, *dyd, &plan)) return CUDNN_STATUS_BAD_PARAM;
+  if (plan.dtype != CUDNN_DATA_FLOAT) return CUDNN_STATUS_NOT_SUPPORTED;
+  if (!mb200::device_span_ok(w, plan.w_bytes) || !mb200::device_span_ok(dy, plan.y_bytes) ||
+      !mb200::device_span_ok(dx, plan.x_bytes))
+    return CUDNN_STATUS_BAD_PARAM;
+  return status_of(mb200::dnn::launch_conv_bwd_data(
+      static_cast<const float*>(w), static_cast<const float*>(dy), static_cast<float*>(dx),
+      plan.shape, *static_cast<const float*>(alpha), *static_cast<const float*>(beta),
+      stream_of(*h)));
+}
+
+// cudnn_ops.mm:261-323
+cudnnStatus_t cudnnConvolutionBackwardFilter(cudnnHandle_t handle, const void* alpha,
+                                             cudnnTensorDescriptor_t xDesc, const void* x,
+                                             cudnnTensorDescriptor_t dyDesc, const void* dy,
+                                             cudnnConvolutionDescriptor_t convDesc,
+                                             cudnnConvolutionBwdFilterAlgo_t algo, void* workSpace,
+                                             size_t workSpaceSizeInBytes, const void* beta,
+                                             cudnnFilterDescriptor_t dwDesc, void* dw) {
+  (void)algo;
+  (void)workSpace;
+  (void)workSpaceSizeInBytes;
+  if (alpha == nullptr || beta == nullptr || x == nullptr || dy == nullptr || dw == nullptr)
+    return CUDNN_STATUS_BAD_PARAM;
+  auto h = handles().get(handle);
+  auto xd = tensors().get(xDesc);
+  auto fd = filters().get(dwDesc);
+  auto cd = convs().get(convDesc);
+  auto dyd = tensors().get(dyDesc);
+  if (!h || !xd || !fd || !cd || !dyd) return CUDNN_STATUS_BAD_PARAM;
+  ConvPlan plan{};
+  if (!build_conv(*xd, *fd, *cd, *dyd, &plan)) return CUDNN_STATUS_BAD_PARAM;
+  if (plan.dtype != CUDNN_DATA_FLOAT) return CUDNN_STATUS_NOT_SUPPORTED;
+  if (!mb200::device_span_ok(x, plan.x_bytes) || !mb200::device_span_ok(dy, plan.y_bytes) ||
+      !mb200::device_span_ok(dw, plan.w_bytes))
+    return CUDNN_STATUS_BAD_PARAM;
+  const float a = *static_cast<const float*>(alpha), b = *static_cast<const float*>(beta);
+  const cudaStream_t st = stream_of(*h);
+  return with_workspace(*h, mb200::dnn::conv_bwd_filter_workspace(plan.shape), st, [&](void* ws) {
+    return mb200::dnn::launch_conv_bwd_filter(static_cast<const float*>(x),
+                                              static_cast<const float*>(dy),
+                                              static_cast<float*>(dw), plan.shape, a, b,
+                                              static_cast<float*>(ws), st);
+  });
+}
+
+// cudnn_ops.mm:325-383
+cudnnStatus_t cudnnConvolutionBackwardBias(cudnnHandle_t handle, const void* alpha,
+                                           cudnnTensorDescriptor_t dyDesc, const void* dy,
+                                           const void* beta, cudnnTensorDescriptor_t dbDesc,
+                                           void* db) {
+  if (alpha == nullptr || beta == nullptr || dy == nullptr || db == nullptr)
+    return CUDNN_STATUS_BAD_PARAM;
+  auto h = handles().get(handle);
+  auto dyd = tensors().get(dyDesc);
+  auto dbd = tensors().get(dbDesc);
+  if (!h || !dyd || !dbd) return CUDNN_STATUS_BAD_PARAM;
+  const TensorSnap ys = snap(*dyd), bs = snap(*dbd);
+  if (!ys.configured || !bs.configured) return CUDNN_STATUS_BAD_PARAM;
+  if (bs.v.n != 1 || bs.v.c != ys.v.c || bs.v.h != 1 || bs.v.w != 1) return CUDNN_STATUS_BAD_PARAM;
+  if (!all_float({ys.dtype, bs.dtype})) return CUDNN_STATUS_NOT_SUPPORTED;
+  if (!spans_ok({{dy, span_elems(ys.v)}, {db, static_cast<std::size_t>(bs.v.c)}}))
+    return CUDNN_STATUS_BAD_PARAM;
+  return status_of(mb200::dnn::launch_conv_bwd_bias(
+      static_cast<const float*>(dy), ys.v, static_cast<float*>(db),
+      *static_cast<const float*>(alpha), *static_cast<const float*>(beta), stream_of(*h)));
+}
+
+// cudnn_ops.mm:385-451
+cudnnStatus_t cudnnAddTensor(cudnnHandle_t handle, const void* alpha, cudnnTensorDescriptor_t aDesc,
+                             const void* A, const void* beta, cudnnTensorDescriptor_t cDesc,
+                             void* C) {
+  if (alpha == nullptr || beta == nullptr || A == nullptr || C == nullptr)
+    return CUDNN_STATUS_BAD_PARAM;
+  auto h = handles().get(handle);
+  auto ad = tensors().get(aDesc);
+  auto cdd = tensors().get(cDesc);
+  if (!h || !ad || !cdd) return CUDNN_STATUS_BAD_PARAM;
+  const TensorSnap as = snap(*ad), cs = snap(*cdd);
+  if (!as.configured || !cs.configured) return CUDNN_STATUS_BAD_PARAM;
+  if ((as.v.n != 1 && as.v.n != cs.v.n) || (as.v.c != 1 && as.v.c != cs.v.c) ||
+      (as.v.h != 1 && as.v.h != cs.v.h) || (as.v.w != 1 && as.v.w != cs.v.w))
+    return CUDNN_STATUS_BAD_PARAM;
+  if (!all_float({as.dtype, cs.dtype})) return CUDNN_STATUS_NOT_SUPPORTED;
+  if (!spans_ok({{A, span_elems(as.v)}, {C, span_elems(cs.v)}})) return CUDNN_STATUS_BAD_PARAM;
+  return status_of(mb200::dnn::launch_add_tensor(
+      static_cast<const float*>(A), as.v, static_cast<float*>(C), cs.v,
+      *static_cast<const float*>(alpha), *static_cast<const float*>(beta), stream_of(*h)));
+}
+
+// cudnn_ops.mm:453-548
+cudnnStatus_t cudnnActivationForward(cudnnHandle_t handle,
+                                     cudnnActivationDescriptor_t activationDesc, const void* alpha,
+                                     cudnnTensorDescriptor_t xDesc, const void* x, const void* beta,
+                                     cudnnTensorDescriptor_t yDesc, void* y) {
+  if (alpha == nullptr || beta == nullptr || x == nullptr || y == nullptr)
+    return CUDNN_STATUS_BAD_PARAM;
+  auto h = handles().get(handle);
+  auto act = activations().get(activationDesc);
+  auto xd = tensors().get(xDesc);
+  auto yd = tensors().get(yDesc);
+  if (!h || !act || !xd || !yd) return CUDNN_STATUS_BAD_PARAM;
+  int mode;
+  float coef;
+  {
+    std::lock_guard<std::mutex> g(act->mu);
+    if (!act->configured) return CUDNN_STATUS_BAD_PARAM;
+    mode = static_cast<int>(act->mode);
+    coef = static_cast<float>(act->coef);
+  }
+  const TensorSnap xs = snap(*xd), ys = snap(*yd);
+  if (!xs.configured || !ys.configured) return CUDNN_STATUS_BAD_PARAM;
+  if (xs.v.n != ys.v.n || xs.v.c != ys.v.c || xs.v.h != ys.v.h || xs.v.w != ys.v.w)
+    return CUDNN_STATUS_BAD_PARAM;
+  if (!all_float({xs.dtype, ys.dtype})) return CUDNN_STATUS_NOT_SUPPORTED;
+  if (!spans_ok({{x, span_elems(xs.v)}, {y, span_elems(ys.v)}})) return CUDNN_STATUS_BAD_PARAM;
+  return status_of(mb200::dnn::launch_activation(
+      static_cast<const float*>(x), xs.v, static_cast<float*>(y), ys.v, mode, coef,
+      *static_cast<const float*>(alpha), *static_cast<const float*>(beta), stream_of(*h)));
+}
+
+// cudnn_ops.mm:550-623
+cudnnStatus_t cudnnPoolingForward(cudnnHandle_t handle, cudnnPoolingDescriptor_t poolingDesc,
+                                  const void* alpha, cudnnTensorDescriptor_t xDesc, const void* x,
+                                  const void* beta, cudnnTensorDescriptor_t yDesc, void* y) {
+  if (alpha == nullptr || beta == nullptr || x == nullptr || y == nullptr)
+    return CUDNN_STATUS_BAD_PARAM;
+  auto h = handles().get(handle);
+  auto pd = poolings().get(poolingDesc);
+  auto xd = tensors().get(xDesc);
+  auto yd = tensors().get(yDesc);
+  if (!h || !pd || !xd || !yd) return CUDNN_STATUS_BAD_PARAM;
+  mb200::dnn::PoolShape p{};
+  {
+    std::lock_guard<std::mutex> g(pd->mu);
+    if (!pd->configured) return CUDNN_STATUS_BAD_PARAM;
+    p.win_h = pd->win_h;
+    p.win_w = pd->win_w;
+    p.pad_h = pd->pad_h;
+    p.pad_w = pd->pad_w;
+    p.stride_h = pd->stride_h;
+    p.stride_w = pd->stride_w;
+    p.mode = static_cast<int>(pd->mode);
+  }
+  const TensorSnap xs = snap(*xd), ys = snap(*yd);
+  if (!xs.configured || !ys.configured) return CUDNN_STATUS_BAD_PARAM;
+  if (xs.v.n != ys.v.n || xs.v.c != ys.v.c) return CUDNN_STATUS_BAD_PARAM;
+  if (!all_float({xs.dtype, ys.dtype})) return CUDNN_STATUS_NOT_SUPPORTED;
+  if (!spans_ok({{x, span_elems(xs.v)}, {y, span_elems(ys.v)}})) return CUDNN_STATUS_BAD_PARAM;
+  p.x = xs.v;
+  p.y = ys.v;
+  return status_of(mb200::dnn::launch_pooling(
+      static_cast<const float*>(x), static_cast<float*>(y), p, *static_cast<const float*>(alpha),
+      *static_cast<const float*>(beta), stream_of(*h)));
+}
+
+// cudnn_ops.mm:722-802
+cudnnStatus_t cudnnBatchNormalizationForwardInference(
+    cudnnHandle_t handle, cudnnBatchNormMode_t mode, const void* alpha, const void* beta,
+    cudnnTensorDescriptor_t xDesc, const void* x, cudnnTensorDescriptor_t yDesc, void* y,
+    cudnnTensorDescriptor_t bnScaleBiasMeanVarDesc, const void* bnScale, const void* bnBias,
+    const void* estimatedMean, const void* estimatedVariance, double epsilon) {
+  if (alpha == nullptr || beta == nullptr || x == nullptr || y == nullptr || bnScale == nullptr ||
+      bnBias == nullptr || estimatedMean == nullptr || estimatedVariance == nullptr ||
+      epsilon <= 0.0)
+    return CUDNN_STATUS_BAD_PARAM;
+  auto h = handles().get(handle);
+  auto xd = tensors().get(xDesc);
+  auto yd = tensors().get(yDesc);
+  auto bd = tensors().get(bnScaleBiasMeanVarDesc);
+  if (!h || !xd || !yd || !bd) return CUDNN_STATUS_BAD_PARAM;
+  const TensorSnap xs = snap(*xd), ys = snap(*yd), bs = snap(*bd);
+  if (!xs.configured || !ys.configured || !bs.configured) return CUDNN_STATUS_BAD_PARAM;
+  if (xs.v.n != ys.v.n || xs.v.c != ys.v.c || xs.v.h != ys.v.h || xs.v.w != ys.v.w)
+    return CUDNN_STATUS_BAD_PARAM;
+  if (!all_float({xs.dtype, ys.dtype})) return CUDNN_STATUS_NOT_SUPPORTED;
+  const bool per_act = mode == CUDNN_BATCHNORM_PER_ACTIVATION;
+  const std::size_t pe = per_act ? static_cast<std::size_t>(xs.v.c) * xs.v.h * xs.v.w
+                                 : static_cast<std::size_t>(xs.v.c);
+  if (!spans_ok({{x, span_elems(xs.v)}, {y, span_elems(ys.v)}, {bnScale, pe}, {bnBias, pe},
+                 {estimatedMean, pe}, {estimatedVariance, pe}}))
+    return CUDNN_STATUS_BAD_PARAM;
+  return status_of(mb200::dnn::launch_bn_inference(
+      static_cast<const float*>(x), xs.v, static_cast<float*>(y), ys.v,
+      static_cast<const float*>(bnScale), static_cast<const float*>(bnBias),
+      static_cast<const float*>(estimatedMean), static_cast<const float*>(estimatedVariance),
+      per_act, static_cast<float>(epsilon), *static_cast<const float*>(alpha),
+      *static_cast<const float*>(beta), stream_of(*h)));
+}
+
+// cudnn_ops.mm:804-902 (the mode argument is ignored there: statistics are always
+// per channel)
+cudnnStatus_t cudnnBatchNormalizationForwardTraining(
+    cudnnHandle_t handle, cudnnBatchNormMode_t mode, const void* alpha, const void* beta,
+    cudnnTensorDescriptor_t xDesc, const void* x, cudnnTensorDescriptor_t yDesc, void* y,
+    cudnnTensorDescriptor_t bnScaleBiasMeanVarDesc, const void* bnScale, const void* bnBias,
+    double exponentialAverageFactor, void* resultRunningMean, void* resultRunningVariance,
+    double epsilon, void* resultSaveMean, void* resultSaveInvVariance) {
+  (void)mode;
+  if (alpha == nullptr || beta == nullptr || x == nullptr || y == nullptr || bnScale == nullptr ||
+      bnBias == nullptr || epsilon <= 0.0)
+    return CUDNN_STATUS_BAD_PARAM;
+  auto h = handles().get(handle);
+  auto xd = tensors().get(xDesc);
+  auto yd = tensors().get(yDesc);
+  auto bd = tensors().get(bnScaleBiasMeanVarDesc);
+  if (!h || !xd || !yd || !bd) return CUDNN_STATUS_BAD_PARAM;
+  const TensorSnap xs = snap(*xd), ys = snap(*yd), bs = snap(*bd);
+  if (!xs.configured || !ys.configured || !bs.configured) return CUDNN_STATUS_BAD_PARAM;
+  if (xs.v.n != ys.v.n || xs.v.c != ys.v.c || xs.v.h != ys.v.h || xs.v.w != ys.v.w)
+    return CUDNN_STATUS_BAD_PARAM;
+  if (!all_float({xs.dtype, ys.dtype})) return CUDNN_STATUS_NOT_SUPPORTED;
+  const auto ce = static_cast<std::size_t>(xs.v.c);
+  if (!spans_ok({{x, span_elems(xs.v)}, {y, span_elems(ys.v)}, {bnScale, ce}, {bnBias, ce}}))
+    return CUDNN_STATUS_BAD_PARAM;
+  const bool has_running = resultRunningMean != nullptr || resultRunningVariance != nullptr;
+  if (has_running && (resultRunningMean == nullptr || resultRunningVariance == nullptr ||
+                      !spans_ok({{resultRunningMean, ce}, {resultRunningVariance, ce}})))
+    return CUDNN_STATUS_BAD_PARAM;
+  const bool has_save = resultSaveMean != nullptr || resultSaveInvVariance != nullptr;
+  if (has_save && (resultSaveMean == nullptr || resultSaveInvVariance == nullptr ||
+                   !spans_ok({{resultSaveMean, ce}, {resultSaveInvVariance, ce}})))
+    return CUDNN_STATUS_BAD_PARAM;
+  return status_of(mb200::dnn::launch_bn_training(
+      static_cast<const float*>(x), xs.v, static_cast<float*>(y), ys.v,
+      static_cast<const float*>(bnScale), static_cast<const float*>(bnBias),
+      static_cast<float*>(has_running ? resultRunningMean : nullptr),
+      static_cast<float*>(has_running ? resultRunningVariance : nullptr),
+      static_cast<float*>(has_save ? resultSaveMean : nullptr),
+      static_cast<float*>(has_save ? resultSaveInvVariance : nullptr),
+      static_cast<float>(exponentialAverageFactor), static_cast<float>(epsilon),
+      *static_cast<const float*>(alpha), *static_cast<const float*>(beta), stream_of(*h)));
 }
 
 }  // extern "C"

@@ -73,4 +73,46 @@ cudaError_t launch_conv(const void* x, const void* w, void* y, const ConvShape& 
 // Name of the kernel family launch_conv would use (for tests and benchmarks).
 const char* conv_path_name(const ConvShape& s, ConvDtype dt) noexcept;
 
+// ---- neighbours of the convolution (fp32; dnn_ops_kernels.cu) ----
+// Backward data: dx = alpha * conv^T(dy, w) + beta * dx, with s.x the dx view and
+// s.y the dy view.
+cudaError_t launch_conv_bwd_data(const float* w, const float* dy, float* dx, const ConvShape& s,
+                                 float alpha, float beta, cudaStream_t stream) noexcept;
+// Backward filter: dw = alpha * sum_(b,p,q) x * dy + beta * dw, through
+// conv_bwd_filter_workspace(s) bytes of device workspace (4-byte aligned).
+std::size_t conv_bwd_filter_workspace(const ConvShape& s) noexcept;
+int conv_bwd_filter_chunks(const ConvShape& s) noexcept;
+cudaError_t launch_conv_bwd_filter(const float* x, const float* dy, float* dw, const ConvShape& s,
+                                   float alpha, float beta, float* workspace,
+                                   cudaStream_t stream) noexcept;
+// Backward bias: db[c] = alpha * sum over (n, h, w) of dy + beta * db[c].
+cudaError_t launch_conv_bwd_bias(const float* dy, const View4& v, float* db, float alpha,
+                                 float beta, cudaStream_t stream) noexcept;
+// c = alpha * a + beta * c, a broadcast along its size-1 dimensions.
+cudaError_t launch_add_tensor(const float* a, const View4& av, float* c, const View4& cv,
+                              float alpha, float beta, cudaStream_t stream) noexcept;
+// y = alpha * act(x) + beta * y; mode = cudnnActivationMode_t.
+cudaError_t launch_activation(const float* x, const View4& xv, float* y, const View4& yv,
+                              int mode, float coef, float alpha, float beta,
+                              cudaStream_t stream) noexcept;
+
+struct PoolShape {
+  View4 x, y;
+  int win_h, win_w, pad_h, pad_w, stride_h, stride_w;
+  int mode;  // cudnnPoolingMode_t
+};
+cudaError_t launch_pooling(const float* x, float* y, const PoolShape& p, float alpha, float beta,
+                           cudaStream_t stream) noexcept;
+
+cudaError_t launch_bn_inference(const float* x, const View4& xv, float* y, const View4& yv,
+                                const float* scale, const float* bias, const float* mean,
+                                const float* var, bool per_activation, float eps, float alpha,
+                                float beta, cudaStream_t stream) noexcept;
+// running_* and save_* may be null (skipped).
+cudaError_t launch_bn_training(const float* x, const View4& xv, float* y, const View4& yv,
+                               const float* scale, const float* bias, float* running_mean,
+                               float* running_var, float* save_mean, float* save_inv_var,
+                               float factor, float eps, float alpha, float beta,
+                               cudaStream_t stream) noexcept;
+
 }  // namespace mb200::dnn

@@ -166,6 +166,115 @@ def conv2d(x: np.ndarray, w: np.ndarray, xshape, wshape, *, x_fmt="NCHW", w_fmt=
     return y
 
 
+def conv_params(xshape, wshape, *, x_fmt="NCHW", w_fmt="NCHW", y_fmt=None, pad=(0, 0),
+                stride=(1, 1), dil=(1, 1), groups=1, mode="cross", alpha=1.0, beta=0.0):
+    """OracleConvParams of a forward convolution and its output shape (n, k, oh, ow)."""
+    from oracle.protos import ConvParams
+    n, c, h, wd = xshape
+    k, cg, r, s = wshape
+    oh = 1 + (h + 2 * pad[0] - (1 + (r - 1) * dil[0])) // stride[0]
+    ow = 1 + (wd + 2 * pad[1] - (1 + (s - 1) * dil[1])) // stride[1]
+    xs = _nchw_strides(xshape, x_fmt)
+    ys = _nchw_strides((n, k, oh, ow), y_fmt or x_fmt)
+    p = ConvParams(n, c, h, wd, *xs, k, oh, ow, groups, *ys, r, s, pad[0], pad[1], stride[0],
+                   stride[1], dil[0], dil[1], 0 if w_fmt == "NCHW" else 1,
+                   0 if mode == "conv" else 1, alpha, beta)
+    return p, (n, k, oh, ow)
+
+
+def conv_bwd_data(w, dy, xshape, wshape, dx=None, *, accum_f64=False, threads=8, **geom):
+    """Reference backward data (cudnn_kernels.metal:194-243): dx (flat, x layout)."""
+    p, _ = conv_params(xshape, wshape, **geom)
+    dx = np.zeros(int(np.prod(xshape)), np.float32) if dx is None else dx
+    lib().oracle_conv_bwd_data(np.ascontiguousarray(w, np.float32).ctypes.data,
+                               np.ascontiguousarray(dy, np.float32).ctypes.data, dx.ctypes.data,
+                               C.byref(p), int(accum_f64), threads)
+    return dx
+
+
+def conv_bwd_filter(x, dy, xshape, wshape, dw=None, *, accum_f64=False, with_mag=False,
+                    threads=8, **geom):
+    """Reference backward filter (cudnn_kernels.metal:245-286): dw (flat, w layout)."""
+    p, _ = conv_params(xshape, wshape, **geom)
+    dw = np.zeros(int(np.prod(wshape)), np.float32) if dw is None else dw
+    mag = np.zeros(dw.shape, np.float64) if with_mag else None
+    lib().oracle_conv_bwd_filter(np.ascontiguousarray(x, np.float32).ctypes.data,
+                                 np.ascontiguousarray(dy, np.float32).ctypes.data, dw.ctypes.data,
+                                 C.byref(p), int(accum_f64),
+                                 mag.ctypes.data if with_mag else None, threads)
+    return (dw, mag) if with_mag else dw
+
+
+def tensor4(shape, strides=None, fmt="NCHW"):
+    from oracle.protos import Tensor4
+    st = strides if strides is not None else _nchw_strides(shape, fmt)
+    return Tensor4(*shape, *st)
+
+
+def conv_bwd_bias(dy, shape, db=None, *, strides=None, alpha=1.0, beta=0.0, accum_f64=False):
+    """Reference backward bias (cudnn_kernels.metal:288-305); returns (db, sum |dy|)."""
+    db = np.zeros(shape[1], np.float32) if db is None else db
+    mag = np.zeros(shape[1], np.float64)
+    lib().oracle_conv_bwd_bias(np.ascontiguousarray(dy, np.float32).ctypes.data,
+                               C.byref(tensor4(shape, strides)), db.ctypes.data, alpha, beta,
+                               int(accum_f64), mag.ctypes.data)
+    return db, mag
+
+
+def add_tensor(a, ashape, c, cshape, *, astrides=None, cstrides=None, alpha=1.0, beta=0.0):
+    """Reference AddTensor (cudnn_kernels.metal:307-331), c updated in place."""
+    lib().oracle_add_tensor(np.ascontiguousarray(a, np.float32).ctypes.data,
+                            C.byref(tensor4(ashape, astrides)), c.ctypes.data,
+                            C.byref(tensor4(cshape, cstrides)), alpha, beta)
+    return c
+
+
+def activation(x, shape, y, mode, *, coef=0.0, xstrides=None, ystrides=None, alpha=1.0,
+               beta=0.0):
+    """Reference activation forward (cudnn_kernels.metal:333-384), y updated in place."""
+    lib().oracle_activation(np.ascontiguousarray(x, np.float32).ctypes.data,
+                            C.byref(tensor4(shape, xstrides)), y.ctypes.data,
+                            C.byref(tensor4(shape, ystrides)), mode, coef, alpha, beta)
+    return y
+
+
+def pooling(x, xshape, y, yshape, win, pad, stride, mode, *, xstrides=None, ystrides=None,
+            alpha=1.0, beta=0.0):
+    """Reference pooling forward (cudnn_kernels.metal:401-445), y updated in place."""
+    lib().oracle_pooling(np.ascontiguousarray(x, np.float32).ctypes.data,
+                         C.byref(tensor4(xshape, xstrides)), y.ctypes.data,
+                         C.byref(tensor4(yshape, ystrides)), win[0], win[1], pad[0], pad[1],
+                         stride[0], stride[1], mode, alpha, beta)
+    return y
+
+
+def bn_inference(x, shape, y, scale, bias, mean, var, *, per_activation=False, eps=1e-5,
+                 alpha=1.0, beta=0.0):
+    """Reference batch-norm inference (cudnn_kernels.metal:570-611), y updated in place."""
+    f = lambda a: np.ascontiguousarray(a, np.float32).ctypes.data
+    lib().oracle_bn_inference(f(x), C.byref(tensor4(shape)), y.ctypes.data,
+                              C.byref(tensor4(shape)), f(scale), f(bias), f(mean), f(var),
+                              int(per_activation), eps, alpha, beta)
+    return y
+
+
+def bn_training(x, shape, y, scale, bias, *, running=None, save=None, factor=0.1, eps=1e-5,
+                alpha=1.0, beta=0.0, accum_f64=False):
+    """Reference batch-norm training (cudnn_kernels.metal:613-714); running = (mean, var)
+    and save = (mean, inv_std) arrays are updated in place when given."""
+    f = lambda a: np.ascontiguousarray(a, np.float32).ctypes.data
+    rm, rv = running if running is not None else (None, None)
+    sm, sv = save if save is not None else (None, None)
+    lib().oracle_bn_training(f(x), C.byref(tensor4(shape)), y.ctypes.data,
+                             C.byref(tensor4(shape)), f(scale), f(bias),
+                             rm.ctypes.data if rm is not None else None,
+                             rv.ctypes.data if rv is not None else None,
+                             sm.ctypes.data if sm is not None else None,
+                             sv.ctypes.data if sv is not None else None, factor, eps, alpha, beta,
+                             int(accum_f64))
+    return y
+
+
 def softmax(x: np.ndarray, shape, *, algo: int = 1, channel: bool = False, alpha=1.0, beta=0.0,
             y: np.ndarray | None = None, x_strides=None, y_strides=None,
             threads: int = 8) -> np.ndarray:

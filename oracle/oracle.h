@@ -72,6 +72,32 @@ float oracle_bf16_round(float v);
  * accum_f64 != 0: accumulate in double (ground truth) instead of the sequential fp32 fma. */
 void oracle_conv2d_fwd(const void* x, const void* w, void* y, const OracleConvParams* p, int bf16,
                        int accum_f64, int threads);
+/* ---- convolution backward, AddTensor, activation, pooling, batch norm
+ * (cudnn_kernels.metal:194-714); accum_f64 != 0: sums in double.  For the backward
+ * calls p describes the forward convolution: x / c_in is the input (dx for backward
+ * data), y / c_out the output (dy). */
+void oracle_conv_bwd_data(const float* w, const float* dy, float* dx, const OracleConvParams* p,
+                          int accum_f64, int threads);
+void oracle_conv_bwd_filter(const float* x, const float* dy, float* dw, const OracleConvParams* p,
+                            int accum_f64, double* mag, int threads);
+void oracle_conv_bwd_bias(const float* dy, const OracleTensor4* v, float* db, float alpha,
+                          float beta, int accum_f64, double* mag);
+void oracle_add_tensor(const float* a, const OracleTensor4* av, float* c, const OracleTensor4* cv,
+                       float alpha, float beta);
+void oracle_activation(const float* x, const OracleTensor4* xv, float* y, const OracleTensor4* yv,
+                       int mode, float coef, float alpha, float beta);
+void oracle_pooling(const float* x, const OracleTensor4* xv, float* y, const OracleTensor4* yv,
+                    int win_h, int win_w, int pad_h, int pad_w, int stride_h, int stride_w,
+                    int mode, float alpha, float beta);
+void oracle_bn_inference(const float* x, const OracleTensor4* xv, float* y,
+                         const OracleTensor4* yv, const float* scale, const float* bias,
+                         const float* mean, const float* var, int per_activation, float eps,
+                         float alpha, float beta);
+void oracle_bn_training(const float* x, const OracleTensor4* xv, float* y, const OracleTensor4* yv,
+                        const float* scale, const float* bias, float* running_mean,
+                        float* running_var, float* save_mean, float* save_inv_var, float factor,
+                        float eps, float alpha, float beta, int accum_f64);
+
 /* ---- GEMM (libraries/blas/shaders/cublas_kernels.metal:969-1045) ---- */
 /* type 0 fp32, 1 fp16, 2 bf16 (A, B, C all of that type); column-major.
  * rows/cols (optional, n_entries long): evaluate only entries (rows[t], cols[t] % n)

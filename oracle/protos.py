@@ -55,6 +55,20 @@ _PROTOS: list[tuple[str, list, object]] = [
                                 C.c_double, C.c_int], C.c_uint64),
     ("oracle_generate_poisson", [C.c_uint64, C.c_uint64, vp, C.c_size_t, C.c_double, C.c_float,
                                  C.c_int, C.c_int], C.c_uint64),
+    ("oracle_conv_bwd_data", [vp, vp, vp, C.POINTER(ConvParams), C.c_int, C.c_int], None),
+    ("oracle_conv_bwd_filter", [vp, vp, vp, C.POINTER(ConvParams), C.c_int, vp, C.c_int], None),
+    ("oracle_conv_bwd_bias", [vp, C.POINTER(Tensor4), vp, C.c_float, C.c_float, C.c_int, vp],
+     None),
+    ("oracle_add_tensor", [vp, C.POINTER(Tensor4), vp, C.POINTER(Tensor4), C.c_float, C.c_float],
+     None),
+    ("oracle_activation", [vp, C.POINTER(Tensor4), vp, C.POINTER(Tensor4), C.c_int, C.c_float,
+                           C.c_float, C.c_float], None),
+    ("oracle_pooling", [vp, C.POINTER(Tensor4), vp, C.POINTER(Tensor4)] + [C.c_int] * 7 +
+     [C.c_float, C.c_float], None),
+    ("oracle_bn_inference", [vp, C.POINTER(Tensor4), vp, C.POINTER(Tensor4), vp, vp, vp, vp,
+                             C.c_int, C.c_float, C.c_float, C.c_float], None),
+    ("oracle_bn_training", [vp, C.POINTER(Tensor4), vp, C.POINTER(Tensor4), vp, vp, vp, vp, vp, vp,
+                            C.c_float, C.c_float, C.c_float, C.c_float, C.c_int], None),
     ("oracle_spmv_csr_t", [C.c_int64, C.c_int64, vp, vp, vp, C.c_int, vp, vp, C.c_float,
                            C.c_float, C.c_int, vp, vp], None),
     ("oracle_spmm_csr", [C.c_int64, C.c_int64, vp, vp, vp, C.c_int, C.c_int, vp, C.c_int64,

@@ -533,6 +533,160 @@ def suite_spmm(s: Suite) -> dict:
     return out
 
 
+class _DnnSetup:
+    """cuDNN handle plus descriptors for the neighbour routines' benchmarks."""
+
+    def __init__(self, s):
+        from muda_b200 import capi
+        self.L = capi.cudnn()
+        self.h = C.c_void_p()
+        assert self.L.cudnnCreate(C.byref(self.h)) == 0
+        assert self.L.cudnnSetStream(self.h, s.sp) == 0
+        self.owned = []
+
+    def tensor(self, n, c, h, w, fmt=0):
+        d = C.c_void_p()
+        assert self.L.cudnnCreateTensorDescriptor(C.byref(d)) == 0
+        assert self.L.cudnnSetTensor4dDescriptor(d, fmt, 0, n, c, h, w) == 0
+        self.owned.append(("cudnnDestroyTensorDescriptor", d))
+        return d
+
+    def close(self):
+        for fn, d in self.owned:
+            assert getattr(self.L, fn)(d) == 0
+        assert self.L.cudnnDestroy(self.h) == 0
+
+
+def suite_conv_bwd(s: Suite) -> dict:
+    """Backward data and backward filter of a 3x3 pad-1 fp32 convolution, NHWC x
+    32x64x56x56, KRSC w 64x64x3x3 (the forward fp32 config's layouts), normal(0, 1)
+    seeds 12-14."""
+    from muda_b200 import synth
+    torch = s.torch
+    n, c, hw, k = 32 // s.scale, 64, 56, 64
+    x = synth.normal(torch, n * c * hw * hw, seed=12)
+    dy = synth.normal(torch, n * k * hw * hw, seed=13)
+    w = synth.normal(torch, k * c * 9, seed=14)
+    dx, dw = torch.empty_like(x), torch.empty_like(w)
+    d = _DnnSetup(s)
+    L = d.L
+    xd, yd = d.tensor(n, c, hw, hw, fmt=1), d.tensor(n, k, hw, hw, fmt=1)
+    wd, cd = C.c_void_p(), C.c_void_p()
+    assert L.cudnnCreateFilterDescriptor(C.byref(wd)) == 0
+    assert L.cudnnSetFilter4dDescriptor(wd, 0, 1, k, c, 3, 3) == 0
+    assert L.cudnnCreateConvolutionDescriptor(C.byref(cd)) == 0
+    assert L.cudnnSetConvolution2dDescriptor(cd, 1, 1, 1, 1, 1, 1, 1, 0) == 0
+    one, zero = C.c_float(1.0), C.c_float(0.0)
+    p = lambda t: C.c_void_p(t.data_ptr())
+    ms_d, ld = s.time(lambda: L.cudnnConvolutionBackwardData(
+        d.h, C.byref(one), wd, p(w), yd, p(dy), cd, 0, None, 0, C.byref(zero), xd, p(dx)))
+    ms_f, lf = s.time(lambda: L.cudnnConvolutionBackwardFilter(
+        d.h, C.byref(one), xd, p(x), yd, p(dy), cd, 0, None, 0, C.byref(zero), wd, p(dw)),
+        launches_per_call=2)
+    assert L.cudnnDestroyFilterDescriptor(wd) == 0
+    assert L.cudnnDestroyConvolutionDescriptor(cd) == 0
+    d.close()
+    flop = 2.0 * n * k * hw * hw * c * 9
+    tf_d, tf_f = flop / (ms_d * 1e-3) / 1e12, flop / (ms_f * 1e-3) / 1e12
+    return {"value": flop * 2 / ((ms_d + ms_f) * 1e-3) / 1e12, "unit": "TFLOP/s",
+            "ms": ms_d + ms_f, "dtype": "f32",
+            "config": f"N {n} C {c} K {k} {hw}x{hw} 3x3 pad 1, NHWC / KRSC",
+            "backward_data": {"ms": ms_d, "TFLOP/s": tf_d,
+                              "kernel": "transpose_filter + tc_gemm_split_kernel<ConvProblem>"},
+            "backward_filter": {"ms": ms_f, "TFLOP/s": tf_f,
+                                "kernel": "im2col + split-tf32 GEMM"},
+            "roofline": s.roof("tc_gemm_split_kernel (backward data)", tf_d, "tensor-tf32x3"),
+            "launches": ld + lf}
+
+
+def suite_dnn_elementwise(s: Suite) -> dict:
+    """ReLU over 2^28 fp32 (packed NCHW), max pooling 3x3 stride 2 pad 1 of
+    32x64x112x112, batch-norm training of 32x64x56x56 (spatial, running averages)."""
+    from muda_b200 import synth
+    torch = s.torch
+    out = {}
+    d = _DnnSetup(s)
+    L = d.L
+    one, zero = C.c_float(1.0), C.c_float(0.0)
+    p = lambda t: C.c_void_p(t.data_ptr())
+    # activation
+    n_act = (1 << 28) // s.scale
+    x = synth.normal(torch, n_act, seed=15)
+    y = torch.empty_like(x)
+    td = d.tensor(n_act // (64 * 64 * 64), 64, 64, 64)
+    act = C.c_void_p()
+    assert L.cudnnCreateActivationDescriptor(C.byref(act)) == 0
+    assert L.cudnnSetActivationDescriptor(act, 1, 0, 0.0) == 0
+    ms, _ = s.time(lambda: L.cudnnActivationForward(d.h, act, C.byref(one), td, p(x),
+                                                    C.byref(zero), td, p(y)))
+    gbs = 8 * n_act / (ms * 1e-3) / 1e9
+    out["relu"] = {"ms": ms, "GB/s": gbs, "roofline": s.roof("activation_vec4", gbs, "hbm")}
+    assert L.cudnnDestroyActivationDescriptor(act) == 0
+    del x, y
+    # pooling
+    n, c = 32 // s.scale, 64
+    xp = synth.normal(torch, n * c * 112 * 112, seed=16)
+    yp = torch.empty(n * c * 56 * 56, device="cuda")
+    pool = C.c_void_p()
+    assert L.cudnnCreatePoolingDescriptor(C.byref(pool)) == 0
+    assert L.cudnnSetPooling2dDescriptor(pool, 0, 0, 3, 3, 1, 1, 2, 2) == 0
+    xd, yd = d.tensor(n, c, 112, 112), d.tensor(n, c, 56, 56)
+    ms, _ = s.time(lambda: L.cudnnPoolingForward(d.h, pool, C.byref(one), xd, p(xp),
+                                                 C.byref(zero), yd, p(yp)))
+    gbs = 4 * (xp.numel() + yp.numel()) / (ms * 1e-3) / 1e9
+    out["maxpool"] = {"ms": ms, "GB/s": gbs, "roofline": s.roof("pooling_fwd", gbs, "hbm")}
+    assert L.cudnnDestroyPoolingDescriptor(pool) == 0
+    del xp, yp
+    # batch-norm training
+    xb = synth.normal(torch, n * c * 56 * 56, seed=17)
+    yb = torch.empty_like(xb)
+    sc, bi = torch.ones(c, device="cuda"), torch.zeros(c, device="cuda")
+    rm, rv = torch.zeros(c, device="cuda"), torch.ones(c, device="cuda")
+    xd = d.tensor(n, c, 56, 56)
+    bn = d.tensor(1, c, 1, 1)
+    ms, _ = s.time(lambda: L.cudnnBatchNormalizationForwardTraining(
+        d.h, 1, C.byref(one), C.byref(zero), xd, p(xb), xd, p(yb), bn, p(sc), p(bi), 0.1, p(rm),
+        p(rv), 1e-5, None, None))
+    gbs = 8 * xb.numel() / (ms * 1e-3) / 1e9
+    out["bn_training"] = {"ms": ms, "GB/s (x + y once)": gbs,
+                          "roofline": s.roof("bn_training", gbs, "hbm"),
+                          "note": "x is read three times (mean, variance, output) from L2/HBM"}
+    d.close()
+    first = out["relu"]
+    return {"value": first["GB/s"], "unit": "GB/s", "ms": first["ms"], "dtype": "f32",
+            "config": "ReLU 2^28 fp32 (value); maxpool 32x64x112x112 3x3/2; BN 32x64x56x56",
+            "roofline": first["roofline"], **out}
+
+
+def suite_rand_dists(s: Suite) -> dict:
+    """Philox log-normal (mean 0, stddev 0.5), Poisson (lambda 4 and 100) and
+    uniform-double streams, 2^28 values each, seed 1234."""
+    from muda_b200 import capi
+    torch = s.torch
+    L = capi.curand()
+    g = C.c_void_p()
+    assert L.curandCreateGenerator(C.byref(g), capi.CURAND_RNG_PSEUDO_PHILOX4_32_10) == 0
+    assert L.curandSetPseudoRandomGeneratorSeed(g, 1234) == 0
+    assert L.curandSetStream(g, s.sp) == 0
+    n = (1 << 28) // s.scale
+    buf = torch.empty(2 * n, dtype=torch.float32, device="cuda")
+    ptr = C.c_void_p(buf.data_ptr())
+    out = {}
+    for name, fn, eb in (
+            ("lognormal", lambda: L.curandGenerateLogNormal(g, ptr, n, C.c_float(0.0),
+                                                            C.c_float(0.5)), 4),
+            ("poisson_4", lambda: L.curandGeneratePoisson(g, ptr, n, 4.0), 4),
+            ("poisson_100", lambda: L.curandGeneratePoisson(g, ptr, n, 100.0), 4),
+            ("uniform_double", lambda: L.curandGenerateUniformDouble(g, ptr, n), 8)):
+        ms, _ = s.time(fn)
+        out[name] = {"ms": ms, "GB/s": eb * n / (ms * 1e-3) / 1e9}
+    assert L.curandDestroyGenerator(g) == 0
+    v = out["lognormal"]["GB/s"]
+    return {"value": v, "unit": "GB/s", "ms": out["lognormal"]["ms"], "dtype": "f32/u32/f64",
+            "config": f"{n} values per call", "roofline": s.roof("philox_fill_kernel<kLogNormal>",
+                                                                  v, "hbm"), **out}
+
+
 def suite_fft(s: Suite) -> dict:
     """C2C N = 4096, batch 65536, normal(0,1) re/im seed 3, forward then
     inverse in place; value = bytes moved (read + write, both directions) per second."""
@@ -889,6 +1043,9 @@ SUITE = {
     "fft": suite_fft,
     "fft_real": suite_fft_real,
     "fft_bluestein": suite_fft_bluestein,
+    "conv_bwd": suite_conv_bwd,
+    "dnn_elementwise": suite_dnn_elementwise,
+    "rand_dists": suite_rand_dists,
     "softmax": suite_softmax,
     "gemm_bf16": suite_gemm_bf16,
     "conv_bf16": lambda s: suite_conv(s, "bf16"),

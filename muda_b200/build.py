@@ -35,7 +35,7 @@ LIBS: dict[str, list[str]] = {
     "curand": ["rand/curand_api.cpp", "rand/philox_kernels.cu"],
     "cudnn": ["dnn/cudnn_api.cpp", "dnn/softmax_kernels.cu", "dnn/conv_direct_kernels.cu",
               "dnn/conv_tc_kernels.cu", "dnn/conv_dispatch.cu", "blas/tf32_split.cu",
-              "dnn/dnn_ops_kernels.cu"],
+              "dnn/dnn_ops_kernels.cu", "dnn/conv_bwd_tc.cu", "blas/gemm_tc_kernels.cu"],
     "cusparse": ["sparse/cusparse_api.cpp", "sparse/spmv_kernels.cu",
                  "sparse/spmm_kernels.cu"],
     "cufft": ["fft/cufft_api.cpp", "fft/stockham_kernels.cu", "fft/dft_kernels.cu",

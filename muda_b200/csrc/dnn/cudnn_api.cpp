@@ -15,6 +15,7 @@
 
 #include <cuda_runtime_api.h>
 
+#include <algorithm>
 #include <cstdint>
 #include <initializer_list>
 #include <memory>
@@ -833,10 +834,22 @@ cudnnStatus_t cudnnConvolutionBackwardData(cudnnHandle_t handle, const void* alp
   if (!mb200::device_span_ok(w, plan.w_bytes) || !mb200::device_span_ok(dy, plan.y_bytes) ||
       !mb200::device_span_ok(dx, plan.x_bytes))
     return CUDNN_STATUS_BAD_PARAM;
-  return status_of(mb200::dnn::launch_conv_bwd_data(
-      static_cast<const float*>(w), static_cast<const float*>(dy), static_cast<float*>(dx),
-      plan.shape, *static_cast<const float*>(alpha), *static_cast<const float*>(beta),
-      stream_of(*h)));
+  const float a = *static_cast<const float*>(alpha), b = *static_cast<const float*>(beta);
+  const cudaStream_t st = stream_of(*h);
+  const auto* wp = static_cast<const float*>(w);
+  const auto* dyp = static_cast<const float*>(dy);
+  auto* dxp = static_cast<float*>(dx);
+  const std::size_t need = mb200::dnn::conv_bwd_data_tc_workspace(plan.shape);
+  if (need > 0) {
+    return with_workspace(*h, need, st, [&](void* ws) {
+      const cudaError_t e =
+          mb200::dnn::launch_conv_bwd_data_tc(wp, dyp, dxp, plan.shape, a, b, ws, need, st);
+      return e == cudaErrorNotSupported
+                 ? mb200::dnn::launch_conv_bwd_data(wp, dyp, dxp, plan.shape, a, b, st)
+                 : e;
+    });
+  }
+  return status_of(mb200::dnn::launch_conv_bwd_data(wp, dyp, dxp, plan.shape, a, b, st));
 }
 
 // cudnn_ops.mm:261-323
@@ -866,10 +879,18 @@ cudnnStatus_t cudnnConvolutionBackwardFilter(cudnnHandle_t handle, const void* a
     return CUDNN_STATUS_BAD_PARAM;
   const float a = *static_cast<const float*>(alpha), b = *static_cast<const float*>(beta);
   const cudaStream_t st = stream_of(*h);
-  return with_workspace(*h, mb200::dnn::conv_bwd_filter_workspace(plan.shape), st, [&](void* ws) {
-    return mb200::dnn::launch_conv_bwd_filter(static_cast<const float*>(x),
-                                              static_cast<const float*>(dy),
-                                              static_cast<float*>(dw), plan.shape, a, b,
+  const std::size_t tc_need = mb200::dnn::conv_bwd_filter_tc_workspace(plan.shape);
+  const std::size_t simt_need = mb200::dnn::conv_bwd_filter_workspace(plan.shape);
+  return with_workspace(*h, std::max(tc_need, simt_need), st, [&](void* ws) {
+    const auto* xp = static_cast<const float*>(x);
+    const auto* dyp = static_cast<const float*>(dy);
+    auto* dwp = static_cast<float*>(dw);
+    if (tc_need > 0) {
+      const cudaError_t e =
+          mb200::dnn::launch_conv_bwd_filter_tc(xp, dyp, dwp, plan.shape, a, b, ws, tc_need, st);
+      if (e != cudaErrorNotSupported) return e;
+    }
+    return mb200::dnn::launch_conv_bwd_filter(xp, dyp, dwp, plan.shape, a, b,
                                               static_cast<float*>(ws), st);
   });
 }

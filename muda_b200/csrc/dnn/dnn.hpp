@@ -85,6 +85,18 @@ int conv_bwd_filter_chunks(const ConvShape& s) noexcept;
 cudaError_t launch_conv_bwd_filter(const float* x, const float* dy, float* dw, const ConvShape& s,
                                    float alpha, float beta, float* workspace,
                                    cudaStream_t stream) noexcept;
+// Tensor-core forms (split tf32, groups 1; conv_bwd_tc.cu): backward data for
+// stride 1 with NHWC dx / dy as a forward convolution of dy with the transposed
+// filter; backward filter as an im2col GEMM.  Workspace 0: geometry not covered.
+std::size_t conv_bwd_data_tc_workspace(const ConvShape& s) noexcept;
+cudaError_t launch_conv_bwd_data_tc(const float* w, const float* dy, float* dx,
+                                    const ConvShape& s, float alpha, float beta, void* workspace,
+                                    std::size_t ws_bytes, cudaStream_t stream) noexcept;
+std::size_t conv_bwd_filter_tc_workspace(const ConvShape& s) noexcept;
+cudaError_t launch_conv_bwd_filter_tc(const float* x, const float* dy, float* dw,
+                                      const ConvShape& s, float alpha, float beta,
+                                      void* workspace, std::size_t ws_bytes,
+                                      cudaStream_t stream) noexcept;
 // Backward bias: db[c] = alpha * sum over (n, h, w) of dy + beta * db[c].
 cudaError_t launch_conv_bwd_bias(const float* dy, const View4& v, float* db, float alpha,
                                  float beta, cudaStream_t stream) noexcept;

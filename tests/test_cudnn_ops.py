@@ -229,7 +229,25 @@ CONV_CASES = [  # xshape, wshape, pad, stride, dil, groups, mode, fmt
     ((3, 8, 10, 6), (8, 8, 1, 1), (0, 0), (2, 3), (1, 1), 1, "cross", "NHWC"),
     ((2, 3, 12, 12), (6, 3, 5, 3), (2, 1), (3, 2), (2, 1), 1, "cross", "NCHW"),
     ((4, 32, 14, 14), (64, 32, 3, 3), (1, 1), (1, 1), (1, 1), 1, "cross", "NHWC"),
+    # tensor-core paths (split tf32): backward data needs stride 1, NHWC, K % 32 == 0
+    ((8, 64, 28, 28), (64, 64, 3, 3), (1, 1), (1, 1), (1, 1), 1, "cross", "NHWC"),
+    ((4, 32, 20, 20), (64, 32, 3, 3), (1, 1), (1, 1), (2, 2), 1, "conv", "NHWC"),
+    ((2, 64, 16, 16), (32, 64, 5, 5), (2, 2), (1, 1), (1, 1), 1, "cross", "NHWC"),
+    ((8, 64, 28, 28), (64, 64, 3, 3), (1, 1), (2, 2), (1, 1), 1, "cross", "NHWC"),
+    ((8, 64, 28, 28), (64, 64, 3, 3), (1, 1), (1, 1), (1, 1), 1, "cross", "NCHW"),
 ]
+
+
+def _tc_paths(case, ys):
+    """(backward data, backward filter) take the split-tf32 tensor-core path: the
+    library's selection rule (conv_bwd_tc.cu, conv_tc_kernels.cu tf32_geometry_ok)."""
+    xs, ws, pad, stride, dil, groups, mode, fmt = case
+    n, c, h, w = xs
+    k, _, r, s = ws
+    data = (groups == 1 and stride == (1, 1) and fmt == "NHWC" and k % 32 == 0 and c % 4 == 0
+            and n * h * w * c * k * r * s >= (1 << 24))
+    filt = groups == 1 and (c * r * s) * k * (ys[0] * ys[2] * ys[3]) >= (1 << 24)
+    return data, filt
 
 
 def _conv_setup(d, case):
@@ -266,8 +284,18 @@ def test_gpu_conv_backward(cuda, built, case):
                                                       yd, _p(_dy), cd, 0, None, 0, fptr(beta), wd,
                                                       _p(tdw)) == 0
             torch.cuda.synchronize()
-            want_dx = oracle.conv_bwd_data(w, dy, xs, ws, dx0.copy(), alpha=alpha, beta=beta, **geom)
-            assert np.array_equal(tdx.cpu().numpy(), want_dx)  # bit-exact
+            tc_data, _ = _tc_paths(case, ys)
+            if not tc_data:
+                want_dx = oracle.conv_bwd_data(w, dy, xs, ws, dx0.copy(), alpha=alpha, beta=beta,
+                                               **geom)
+                assert np.array_equal(tdx.cpu().numpy(), want_dx)  # bit-exact
+            else:
+                exact = oracle.conv_bwd_data(w, dy, xs, ws, dx0.copy(), accum_f64=True,
+                                             alpha=alpha, beta=beta, **geom)
+                mag = oracle.conv_bwd_data(np.abs(w), np.abs(dy), xs, ws, accum_f64=True, **geom)
+                scale = abs(alpha) * mag.astype(np.float64) + abs(beta) * np.abs(dx0)
+                err = np.abs(tdx.cpu().numpy().astype(np.float64) - exact)
+                assert np.all(err <= 1e-5 * scale + 1e-30), np.max(err / (scale + 1e-30))
             exact, mag = oracle.conv_bwd_filter(x, dy, xs, ws, dw0.copy(), accum_f64=True,
                                                 with_mag=True, alpha=alpha, beta=beta, **geom)
             scale = abs(alpha) * mag + abs(beta) * np.abs(dw0)

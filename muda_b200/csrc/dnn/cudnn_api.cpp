@@ -1072,15 +1072,22 @@ cudnnStatus_t cudnnBatchNormalizationForwardTraining(
   if (has_save && (resultSaveMean == nullptr || resultSaveInvVariance == nullptr ||
                    !spans_ok({{resultSaveMean, ce}, {resultSaveInvVariance, ce}})))
     return CUDNN_STATUS_BAD_PARAM;
-  return status_of(mb200::dnn::launch_bn_training(
-      static_cast<const float*>(x), xs.v, static_cast<float*>(y), ys.v,
-      static_cast<const float*>(bnScale), static_cast<const float*>(bnBias),
-      static_cast<float*>(has_running ? resultRunningMean : nullptr),
-      static_cast<float*>(has_running ? resultRunningVariance : nullptr),
-      static_cast<float*>(has_save ? resultSaveMean : nullptr),
-      static_cast<float*>(has_save ? resultSaveInvVariance : nullptr),
-      static_cast<float>(exponentialAverageFactor), static_cast<float>(epsilon),
-      *static_cast<const float*>(alpha), *static_cast<const float*>(beta), stream_of(*h)));
+  const cudaStream_t st = stream_of(*h);
+  auto run = [&](void* ws) {
+    return mb200::dnn::launch_bn_training(
+        static_cast<const float*>(x), xs.v, static_cast<float*>(y), ys.v,
+        static_cast<const float*>(bnScale), static_cast<const float*>(bnBias),
+        static_cast<float*>(has_running ? resultRunningMean : nullptr),
+        static_cast<float*>(has_running ? resultRunningVariance : nullptr),
+        static_cast<float*>(has_save ? resultSaveMean : nullptr),
+        static_cast<float*>(has_save ? resultSaveInvVariance : nullptr),
+        static_cast<float>(exponentialAverageFactor), static_cast<float>(epsilon),
+        *static_cast<const float*>(alpha), *static_cast<const float*>(beta),
+        static_cast<float*>(ws), st);
+  };
+  const std::size_t need = mb200::dnn::bn_training_workspace(xs.v);
+  if (need == 0) return status_of(run(nullptr));
+  return with_workspace(*h, need, st, run);
 }
 
 }  // extern "C"

@@ -120,11 +120,14 @@ cudaError_t launch_bn_inference(const float* x, const View4& xv, float* y, const
                                 const float* scale, const float* bias, const float* mean,
                                 const float* var, bool per_activation, float eps, float alpha,
                                 float beta, cudaStream_t stream) noexcept;
-// running_* and save_* may be null (skipped).
+// running_* and save_* may be null (skipped).  With bn_training_workspace(xv) > 0
+// bytes of workspace each channel is split across several CTAs (three launches);
+// a null workspace runs one CTA per channel.
+std::size_t bn_training_workspace(const View4& xv) noexcept;
 cudaError_t launch_bn_training(const float* x, const View4& xv, float* y, const View4& yv,
                                const float* scale, const float* bias, float* running_mean,
                                float* running_var, float* save_mean, float* save_inv_var,
-                               float factor, float eps, float alpha, float beta,
+                               float factor, float eps, float alpha, float beta, float* workspace,
                                cudaStream_t stream) noexcept;
 
 }  // namespace mb200::dnn

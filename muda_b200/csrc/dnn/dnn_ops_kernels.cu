@@ -383,6 +383,92 @@ __global__ void __launch_bounds__(kRedThreads)
   }
 }
 
+// Split form of the training pass for large N*H*W: each channel's elements are
+// cut into `splits` contiguous ranges, one CTA each (grid splits x C).
+//   stage 0: partial sums of x per (channel, range);
+//   stage 1: every CTA forms the mean from its channel's partial sums (in range
+//            order), then partial sums of (x - mean)^2;
+//   stage 2: every CTA forms mean and variance the same way, range 0 writes the
+//            saved and running statistics, all write y over their range.
+__device__ __forceinline__ void bn_range(std::int64_t m, int splits, int part, std::int64_t& i0,
+                                         std::int64_t& i1) {
+  const std::int64_t per = (m + splits - 1) / splits;
+  i0 = part * per;
+  i1 = i0 + per < m ? i0 + per : m;
+}
+
+template <int STAGE>
+__global__ void __launch_bounds__(kRedThreads)
+    bn_training_split(const float* __restrict__ x, View4 xv, float* __restrict__ y, View4 yv,
+                      const float* __restrict__ scale, const float* __restrict__ bias,
+                      float* __restrict__ running_mean, float* __restrict__ running_var,
+                      float* __restrict__ save_mean, float* __restrict__ save_inv_var,
+                      float* __restrict__ partial, int splits, float factor, float eps,
+                      float alpha, float beta) {
+  __shared__ float scratch[kRedThreads / 32];
+  const int part = blockIdx.x, c = blockIdx.y;
+  const std::int64_t hw = static_cast<std::int64_t>(xv.h) * xv.w;
+  const std::int64_t m = xv.n * hw;
+  const float inv_m = 1.0f / static_cast<float>(m);
+  float* psum = partial + static_cast<std::int64_t>(c) * splits;               // [C][splits]
+  float* psq = partial + static_cast<std::int64_t>(xv.c) * splits + c * splits;  // [C][splits]
+  std::int64_t i0, i1;
+  bn_range(m, splits, part, i0, i1);
+  auto x_at_i = [&](std::int64_t i) {
+    const int b = static_cast<int>(i / hw);
+    const std::int64_t p = i - b * hw;
+    const int h = static_cast<int>(p / xv.w);
+    return at(xv, b, c, h, static_cast<int>(p - h * xv.w));
+  };
+  float mean = 0.0f;
+  if (STAGE >= 1) {
+    float t = 0.0f;
+    for (int q = 0; q < splits; ++q) t += psum[q];
+    mean = t * inv_m;
+  }
+  if (STAGE == 0) {
+    float acc = 0.0f;
+    for (std::int64_t i = i0 + threadIdx.x; i < i1; i += kRedThreads) acc += x[x_at_i(i)];
+    const float total = block_sum<kRedThreads>(acc, scratch);
+    if (threadIdx.x == 0) psum[part] = total;
+  } else if (STAGE == 1) {
+    float sq = 0.0f;
+    for (std::int64_t i = i0 + threadIdx.x; i < i1; i += kRedThreads) {
+      const float d = x[x_at_i(i)] - mean;
+      sq = fmaf(d, d, sq);
+    }
+    const float total = block_sum<kRedThreads>(sq, scratch);
+    if (threadIdx.x == 0) psq[part] = total;
+  } else {
+    float total_sq = 0.0f;
+    for (int q = 0; q < splits; ++q) total_sq += psq[q];
+    const float var = total_sq * inv_m;
+    const float inv_std = rsqrtf(var + eps);
+    if (part == 0 && threadIdx.x == 0) {
+      const float unbiased = (m > 1) ? total_sq / static_cast<float>(m - 1) : var;
+      if (save_mean != nullptr) {
+        save_mean[c] = mean;
+        save_inv_var[c] = inv_std;
+      }
+      if (running_mean != nullptr) {
+        running_mean[c] = (1.0f - factor) * running_mean[c] + factor * mean;
+        running_var[c] = (1.0f - factor) * running_var[c] + factor * unbiased;
+      }
+    }
+    const float sc = scale[c], bi = bias[c];
+    for (std::int64_t i = i0 + threadIdx.x; i < i1; i += kRedThreads) {
+      const int b = static_cast<int>(i / hw);
+      const std::int64_t p = i - b * hw;
+      const int h = static_cast<int>(p / xv.w);
+      const int w = static_cast<int>(p - h * xv.w);
+      const float nv = fmaf((x[at(xv, b, c, h, w)] - mean) * inv_std, sc, bi);
+      const std::int64_t yi = at(yv, b, c, h, w);
+      const float prev = (beta == 0.0f) ? 0.0f : beta * y[yi];
+      y[yi] = fmaf(alpha, nv, prev);
+    }
+  }
+}
+
 }  // namespace
 
 cudaError_t launch_conv_bwd_data(const float* w, const float* dy, float* dx, const ConvShape& s,
@@ -483,15 +569,50 @@ cudaError_t launch_bn_inference(const float* x, const View4& xv, float* y, const
   return cudaGetLastError();
 }
 
+int bn_training_splits(const View4& xv) noexcept {
+  const std::int64_t m = static_cast<std::int64_t>(xv.n) * xv.h * xv.w;
+  if (xv.c <= 0 || m <= 0) return 1;
+  // about four CTAs per SM in total, each range at least 4096 elements
+  const int sms = sm_count(current_device());
+  std::int64_t want = (static_cast<std::int64_t>(sms > 0 ? sms : 148) * 4 + xv.c - 1) / xv.c;
+  const std::int64_t by_len = m / 4096;
+  if (want > by_len) want = by_len;
+  if (want > 1024) want = 1024;
+  return static_cast<int>(want < 1 ? 1 : want);
+}
+
+std::size_t bn_training_workspace(const View4& xv) noexcept {
+  const int splits = bn_training_splits(xv);
+  return splits > 1 ? static_cast<std::size_t>(2) * xv.c * splits * sizeof(float) : 0;
+}
+
 cudaError_t launch_bn_training(const float* x, const View4& xv, float* y, const View4& yv,
                                const float* scale, const float* bias, float* running_mean,
                                float* running_var, float* save_mean, float* save_inv_var,
-                               float factor, float eps, float alpha, float beta,
+                               float factor, float eps, float alpha, float beta, float* workspace,
                                cudaStream_t stream) noexcept {
   if (xv.c <= 0) return cudaSuccess;
-  bn_training<<<xv.c, kRedThreads, 0, stream>>>(x, xv, y, yv, scale, bias, running_mean,
-                                                running_var, save_mean, save_inv_var, factor, eps,
-                                                alpha, beta);
+  const int splits = bn_training_splits(xv);
+  if (splits <= 1 || workspace == nullptr) {
+    bn_training<<<xv.c, kRedThreads, 0, stream>>>(x, xv, y, yv, scale, bias, running_mean,
+                                                  running_var, save_mean, save_inv_var, factor,
+                                                  eps, alpha, beta);
+    return cudaGetLastError();
+  }
+  const dim3 grid(static_cast<unsigned>(splits), static_cast<unsigned>(xv.c));
+  bn_training_split<0><<<grid, kRedThreads, 0, stream>>>(
+      x, xv, y, yv, scale, bias, running_mean, running_var, save_mean, save_inv_var, workspace,
+      splits, factor, eps, alpha, beta);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  bn_training_split<1><<<grid, kRedThreads, 0, stream>>>(
+      x, xv, y, yv, scale, bias, running_mean, running_var, save_mean, save_inv_var, workspace,
+      splits, factor, eps, alpha, beta);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  bn_training_split<2><<<grid, kRedThreads, 0, stream>>>(
+      x, xv, y, yv, scale, bias, running_mean, running_var, save_mean, save_inv_var, workspace,
+      splits, factor, eps, alpha, beta);
   return cudaGetLastError();
 }
 

@@ -251,7 +251,9 @@ constexpr int kSplitEpiWarps = 8;
 template <class P, int BN, int STAGES, int CK>
 __global__ void __launch_bounds__(kSplitThreads, 1)
     tc_gemm_split_kernel(const __grid_constant__ P p, unsigned int* timeouts) {
-  static_assert(BN == 256, "the epilogue splits the tile into two 128-column halves");
+  static_assert(BN == 256 || BN == 128 || BN == 64,
+                "the epilogue splits the tile into two halves of 32-column groups");
+  constexpr int HC = BN / 2;  // columns per epilogue warp
   using S = CoreShape<BN, STAGES, 2>;
   extern __shared__ std::uint8_t smem_raw[];
   std::uint8_t* base = reinterpret_cast<std::uint8_t*>(
@@ -385,7 +387,7 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
     const int half = (warp - 2) >> 2;
     const int row = quarter * 32 + lane;
     const std::uint32_t t_lane = tmem_base + (static_cast<std::uint32_t>(quarter * 32) << 16) +
-                                 static_cast<std::uint32_t>(half * 128);
+                                 static_cast<std::uint32_t>(half * HC);
     const int chunks = (num_kb + CK - 1) / CK;
     float alpha, beta;
     p.scalars(alpha, beta);
@@ -395,9 +397,9 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
     for (long long t = blockIdx.x; ok && t < p.tiles_total && !*aborted; t += gridDim.x) {
       int c[3];
       p.coords(t, c);
-      float run[128];
+      float run[HC];
 #pragma unroll
-      for (int j = 0; j < 128; ++j) run[j] = 0.0f;
+      for (int j = 0; j < HC; ++j) run[j] = 0.0f;
       for (int ch = 0; ch < chunks; ++ch) {
         if (!mbar_wait(&acc_full[acc], acc_phase)) {
           fail();
@@ -407,7 +409,7 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
         tc_fence_after();
         const std::uint32_t ta = t_lane + static_cast<std::uint32_t>(acc * BN);
 #pragma unroll
-        for (int g = 0; g < 8; ++g) {
+        for (int g = 0; g < HC / 16; ++g) {
           float v[16];
           tmem_load_16cols(ta + static_cast<std::uint32_t>(g * 16), v);
 #pragma unroll
@@ -423,8 +425,8 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
       }
       if (!ok) break;
 #pragma unroll
-      for (int g = 0; g < 4; ++g)
-        p.store(c, row, half * 128 + g * 32, *reinterpret_cast<const float(*)[32]>(run + g * 32),
+      for (int g = 0; g < HC / 32; ++g)
+        p.store(c, row, half * HC + g * 32, *reinterpret_cast<const float(*)[32]>(run + g * 32),
                 alpha, beta);
     }
   }

@@ -43,15 +43,20 @@
 namespace mb200::dnn {
 namespace {
 
-constexpr int BN = 256;
+constexpr int BN = 256;     // tile width of the 16-bit path
 constexpr int STAGES = 4;
-constexpr int STAGES32 = 2;  // 2 x (32 + 64) KB stages for the split-tf32 planes
+// Split tf32: the tile width follows the output channels (a 64-channel layer on a
+// 256-wide tile would leave three quarters of every MMA idle); stages fill about
+// 192 KB: A planes 32 KB + B planes BN/4 KB per stage.
+template <int TBN>
+constexpr int kStages32 = TBN == 64 ? 4 : (TBN == 128 ? 3 : 2);
 constexpr std::size_t kWorkspaceCap = std::size_t{4} << 30;
 
 __device__ unsigned int g_conv_tc_timeouts;
 
-template <typename T, int FMT>
+template <typename T, int FMT, int TBN = BN>
 struct ConvProblem {
+  static constexpr int kBN = TBN;  // output channels per tile
   static constexpr bool kSplit = FMT == tc::kFmtTf32x3;
   static constexpr int KB = kSplit ? tc::kBK32 : tc::kBK;  // channels per k-block
   // im2col map of the NHWC input (c, w, h, n); split tf32: of the planes
@@ -103,7 +108,7 @@ struct ConvProblem {
     } else {
       tc::tma_load_im2col_4d(sa, &mx, cb * KB, bw, bh, n, ow, oh, bar);
     }
-    tc::tma_load_3d(sb, &mw, (fr * S + fs) * C + cb * KB, c3[2] * BN, 0, bar);
+    tc::tma_load_3d(sb, &mw, (fr * S + fs) * C + cb * KB, c3[2] * kBN, 0, bar);
   }
 
   __device__ void scalars(float& a, float& b) const {
@@ -115,7 +120,7 @@ struct ConvProblem {
                         float b) const {
     const int m = c3[0] * tc::kBM + row;
     if (m >= pixels) return;
-    const int k0 = c3[2] * BN + col0;
+    const int k0 = c3[2] * kBN + col0;
     T* out = y + static_cast<long long>(m) * K + k0;
     if (k0 + 32 <= K && b == 0.0f) {
       // 32 channels = 32 * sizeof(T) contiguous bytes, as 16-byte stores
@@ -193,17 +198,17 @@ bool im2col_ok(const ConvShape& s, int rank) {
 
 // Geometry shared by both formats for `images` images (a chunk of the batch for
 // split tf32) whose output starts at y.
-template <typename T, int FMT>
-void fill_geometry(ConvProblem<T, FMT>& p, const ConvShape& s, void* y, int images, float alpha,
-                   float beta) {
-  using P = ConvProblem<T, FMT>;
+template <typename T, int FMT, int TBN>
+void fill_geometry(ConvProblem<T, FMT, TBN>& p, const ConvShape& s, void* y, int images,
+                   float alpha, float beta) {
+  using P = ConvProblem<T, FMT, TBN>;
   p.P = s.y.h;
   p.Q = s.y.w;
   p.K = s.y.c;
   p.C = s.x.c;
   p.R = s.kh;
   p.S = s.kw;
-  p.tiles_k = (p.K + BN - 1) / BN;
+  p.tiles_k = (p.K + TBN - 1) / TBN;
   p.cblocks = p.C / P::KB;
   p.num_kb = p.R * p.S * p.cblocks;
   p.pixels = images * p.P * p.Q;
@@ -282,8 +287,10 @@ bool tf32_geometry_ok(const ConvShape& s) {
   return total * s.y.c * s.x.c * s.kh * s.kw >= (1ll << 24);  // smaller: direct kernel
 }
 
-cudaError_t run_tf32x3(const float* x, const float* w, float* y, const ConvShape& s, float alpha,
-                       float beta, float* ws, const Tf32Plan& pl, cudaStream_t stream) {
+template <int TBN>
+cudaError_t run_tf32x3_bn(const float* x, const float* w, float* y, const ConvShape& s,
+                          float alpha, float beta, float* ws, const Tf32Plan& pl,
+                          cudaStream_t stream) {
   const int H = s.x.h, W = s.x.w, C = s.x.c, K = s.y.c;
   float* wp = ws;
   float* xp = ws + pl.w_floats;
@@ -298,7 +305,7 @@ cudaError_t run_tf32x3(const float* x, const float* w, float* y, const ConvShape
     const long long pixels = static_cast<long long>(nb) * H * W;
     e = tc::launch_tf32_split(x + z0 * s.x.ns, pixels, C, 1, C, 1, 0, xp, C, stream);
     if (e != cudaSuccess) return e;
-    ConvProblem<float, tc::kFmtTf32x3> p{};
+    ConvProblem<float, tc::kFmtTf32x3, TBN> p{};
     fill_geometry(p, s, y + z0 * s.y.ns, nb, alpha, beta);
     const cuuint64_t xd[5] = {static_cast<cuuint64_t>(C), static_cast<cuuint64_t>(W),
                               static_cast<cuuint64_t>(H), static_cast<cuuint64_t>(nb), 2u};
@@ -311,15 +318,23 @@ cudaError_t run_tf32x3(const float* x, const float* w, float* y, const ConvShape
     const cuuint64_t wd[3] = {static_cast<cuuint64_t>(rsc), static_cast<cuuint64_t>(K), 2u};
     const cuuint64_t wst[2] = {static_cast<cuuint64_t>(rsc * 4),
                                static_cast<cuuint64_t>(rsc * K * 4)};
-    const cuuint32_t wb[3] = {static_cast<cuuint32_t>(tc::kBK32), static_cast<cuuint32_t>(BN), 2u};
+    const cuuint32_t wb[3] = {static_cast<cuuint32_t>(tc::kBK32), static_cast<cuuint32_t>(TBN),
+                              2u};
     if (!tc::encode_im2col(&p.mx, 2, xp, 5, xd, xs, lower, upper, tc::kBK32, tc::kBM) ||
         !tc::encode_tiled(&p.mw, 2, wp, 3, wd, wst, wb))
       return cudaErrorNotSupported;
-    e = tc::launch_tc_gemm<ConvProblem<float, tc::kFmtTf32x3>, BN, STAGES32, tc::kFmtTf32x3>(
-        p, sms, to, stream);
+    e = tc::launch_tc_gemm<ConvProblem<float, tc::kFmtTf32x3, TBN>, TBN, kStages32<TBN>,
+                           tc::kFmtTf32x3>(p, sms, to, stream);
     if (e != cudaSuccess) return e;
   }
   return cudaSuccess;
+}
+
+cudaError_t run_tf32x3(const float* x, const float* w, float* y, const ConvShape& s, float alpha,
+                       float beta, float* ws, const Tf32Plan& pl, cudaStream_t stream) {
+  if (s.y.c <= 64) return run_tf32x3_bn<64>(x, w, y, s, alpha, beta, ws, pl, stream);
+  if (s.y.c <= 128) return run_tf32x3_bn<128>(x, w, y, s, alpha, beta, ws, pl, stream);
+  return run_tf32x3_bn<256>(x, w, y, s, alpha, beta, ws, pl, stream);
 }
 
 }  // namespace

@@ -169,6 +169,7 @@ TC32_CASES = [
     ((1, 192, 17, 17), (300, 192, 3, 3), (0, 2), (2, 1), 1, 1.0, 0.75, NCHW),
     ((2, 64, 8, 70), (128, 64, 5, 3), (2, 1), (1, 1), 0, 1.0, 0.0, NHWC),
     ((4, 256, 28, 28), (256, 256, 3, 3), (1, 1), (1, 1), 1, 1.0, 0.0, NHWC),
+    ((2, 32, 16, 16), (40, 32, 3, 3), (1, 1), (1, 1), 1, 0.75, 0.5, NHWC),
 ]
 
 

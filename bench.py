@@ -285,6 +285,8 @@ class Suite:
         self.sp = C.c_void_p(int(self.stream.cuda_stream))
         self.peaks = _peaks()
         self._flush = None
+        self.shard = 1          # ranks sharing a batch-sharded workload (its 1/shard per rank)
+        self.barrier = None     # called around the timed region under torchrun
 
     def flush(self):
         if self._flush is None:
@@ -295,6 +297,8 @@ class Suite:
 
     def time(self, fn, flush=False, launches_per_call=1):
         torch = self.torch
+        if self.barrier is not None:
+            self.barrier()
         with torch.cuda.stream(self.stream):
             for _ in range(self.warmup):
                 fn()
@@ -309,6 +313,8 @@ class Suite:
                 e1.record(self.stream)
                 ms.append((e0, e1))
             self.stream.synchronize()
+        if self.barrier is not None:
+            self.barrier()
         t = [a.elapsed_time(b) for a, b in ms]
         return statistics.mean(t), launches_per_call * self.steps
 
@@ -692,7 +698,7 @@ def suite_fft(s: Suite) -> dict:
     inverse in place; value = bytes moved (read + write, both directions) per second."""
     from muda_b200 import capi, synth
     torch = s.torch
-    n, batch = 4096, 65536 // s.scale
+    n, batch = 4096, 65536 // s.scale // s.shard
     x = synth.normal(torch, 2 * n * batch, seed=3)
     L = capi.cufft()
     p = C.c_void_p()
@@ -818,7 +824,7 @@ def suite_softmax(s: Suite) -> dict:
     """configs[4] softmax: 65536 x 4096 fp32 normal(0, 0.02) seed 11, ACCURATE, INSTANCE."""
     from muda_b200 import capi, synth
     torch = s.torch
-    rows, cols = 65536 // s.scale, 4096
+    rows, cols = 65536 // s.scale // s.shard, 4096
     x = synth.normal(torch, rows * cols, seed=11, std=0.02)
     y = torch.empty_like(x)
     L = capi.cudnn()
@@ -855,7 +861,7 @@ def suite_gemm_bf16(s: Suite) -> dict:
     from muda_b200 import capi, synth
     torch = s.torch
     m = n = k = 8192 // s.scale
-    batch = 8
+    batch = max(1, 8 // s.shard)
     a = synth.normal(torch, m * k * batch, seed=11, std=0.02).to(torch.bfloat16)
     b = synth.normal(torch, n * k * batch, seed=11, std=0.02,
                      offset=(m * k * batch + 3) // 4 * 4).to(torch.bfloat16)
@@ -902,7 +908,7 @@ def suite_conv(s: Suite, dtype: str, krsc: bool = True) -> dict:
     normal(0, 0.02) seed 11 (x then w), cross-correlation, alpha 1, beta 0."""
     from muda_b200 import capi, synth
     torch = s.torch
-    n, c, hh, ww, kk = 64 // s.scale, 256, 56, 56, 256
+    n, c, hh, ww, kk = max(1, 64 // s.scale // s.shard), 256, 56, 56, 256
     x = synth.normal(torch, n * hh * ww * c, seed=11, std=0.02)
     w = synth.normal(torch, kk * 9 * c, seed=11, std=0.02, offset=(n * hh * ww * c + 3) // 4 * 4)
     if dtype == "bf16":
@@ -1198,6 +1204,45 @@ def run_spmv_dist(args) -> None:
         dist.destroy_process_group()
 
 
+SHARDED = ("fft", "gemm_bf16", "conv_bf16", "conv_f32", "softmax")
+
+
+def run_sharded(args) -> None:
+    """A batch-sharded suite routine across the ranks of torchrun (strong scaling): each
+    rank runs 1/world of the batch (FFT transforms, GEMM batch entries, conv images,
+    softmax rows) on its own GPU with no collective on the data path; the timed region
+    of every rank is bracketed by a barrier, the step time is the max over ranks and
+    the value is the whole job's work over that time."""
+    import torch
+    import torch.distributed as dist
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dist.init_process_group("nccl", timeout=__import__("datetime").timedelta(seconds=120),
+                            device_id=torch.device("cuda", local))
+
+    def barrier():
+        dist.barrier()
+        torch.cuda.synchronize()
+
+    s = Suite(torch, max(3, args.steps // 4), args.warmup, False, args.scale)
+    s.shard, s.barrier = world, barrier
+    res = SUITE[args.routine](s)
+    ms = torch.tensor([res["ms"]], device="cuda")
+    dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+    ms_max = float(ms.item())
+    total = res["value"] * res["ms"] / ms_max * world
+    if rank == 0:
+        print(json.dumps({"routine": args.routine, "n_gpus": world, "value": total,
+                          "unit": res["unit"], "ms_max_over_ranks": ms_max,
+                          "per_rank_value": res["value"], "scaling": "strong",
+                          "config": res.get("config"), "sharding": f"batch / {world} per rank",
+                          "dtype": res.get("dtype")}), flush=True)
+    dist.barrier()
+    dist.destroy_process_group()
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -1219,6 +1264,9 @@ def main() -> None:
     args = ap.parse_args()
     if args.routine == "spmv_dist":
         run_spmv_dist(args)
+        return
+    if args.routine in SHARDED and int(os.environ.get("WORLD_SIZE", "1")) > 1:
+        run_sharded(args)
         return
     if args.routine:
         import torch

@@ -733,13 +733,14 @@ def suite_fft(s: Suite) -> dict:
     return out
 
 
-def suite_fft_bluestein(s: Suite) -> dict:
-    """C2C of a length that is not a power of two: N = 1000, batch 262144, normal(0,1)
-    re/im seed 4, forward then inverse in place (Bluestein, inner length 2048 on chip);
-    value = bytes moved (read + write, both directions) per second."""
+def suite_fft_nonpow2(s: Suite, n: int, kernel: str, how: str) -> dict:
+    """C2C of a length that is not a power of two, batch 262144 (N = 1000: mixed radix
+    8 x 5 x 5 x 5; N = 1009, a prime: Bluestein with inner length 2048 on chip),
+    normal(0,1) re/im seed 4, forward then inverse in place; value = bytes moved (read
+    + write, both directions) per second."""
     from muda_b200 import capi, synth
     torch = s.torch
-    n, batch = 1000, 262144 // s.scale
+    batch = 262144 // s.scale
     x = synth.normal(torch, 2 * n * batch, seed=4)
     L = capi.cufft()
     p = C.c_void_p()
@@ -757,9 +758,9 @@ def suite_fft_bluestein(s: Suite) -> dict:
     gbs = 2 * per_dir / (ms * 1e-3) / 1e9
     out = {"value": gbs, "unit": "GB/s", "ms": ms, "dtype": "c64",
            "gflops_5nlogn": 2 * 5 * n * np.log2(n) * batch / (ms * 1e-3) / 1e9,
-           "config": f"N {n} x batch {batch}, forward + inverse in place, "
+           "config": f"N {n} x batch {batch}, forward + inverse in place ({how}), "
                      f"data {per_dir / 2e9:.2f} GB > L2",
-           "roofline": s.roof("bluestein_kernel<11>", gbs, "hbm"), "launches": launches,
+           "roofline": s.roof(kernel, gbs, "hbm"), "launches": launches,
            "algorithmic_bytes_per_launch": per_dir}
     if s.cpu:
         import oracle
@@ -1048,7 +1049,9 @@ SUITE = {
     "spmm": suite_spmm,
     "fft": suite_fft,
     "fft_real": suite_fft_real,
-    "fft_bluestein": suite_fft_bluestein,
+    "fft_mixed": lambda s: suite_fft_nonpow2(s, 1000, "mixed_radix_kernel", "mixed radix"),
+    "fft_bluestein": lambda s: suite_fft_nonpow2(s, 1009, "bluestein_kernel<11>",
+                                                 "Bluestein"),
     "conv_bwd": suite_conv_bwd,
     "dnn_elementwise": suite_dnn_elementwise,
     "rand_dists": suite_rand_dists,

@@ -39,7 +39,7 @@ LIBS: dict[str, list[str]] = {
     "cusparse": ["sparse/cusparse_api.cpp", "sparse/spmv_kernels.cu",
                  "sparse/spmm_kernels.cu"],
     "cufft": ["fft/cufft_api.cpp", "fft/stockham_kernels.cu", "fft/dft_kernels.cu",
-              "fft/bluestein_kernels.cu",
+              "fft/bluestein_kernels.cu", "fft/mixed_kernels.cu",
               "fft/fft_static.cu", "fft/real_kernels.cu"],
     "cublas": ["blas/cublas_api.cpp", "blas/gemm_simt_kernels.cu", "blas/gemm_tc_kernels.cu",
                "blas/tf32_split.cu", "blas/level12_kernels.cu"],

@@ -47,13 +47,14 @@ bool is_pow2(std::int64_t n) { return n > 0 && (n & (n - 1)) == 0; }
 
 // How one axis of length n is transformed.
 enum class AxisKind {
-  kTrivial, kSinglePass, kDirect, kBluestein, kBluesteinGlobal, kSplit, kUnsupported
+  kTrivial, kSinglePass, kMixed, kDirect, kBluestein, kBluesteinGlobal, kSplit, kUnsupported
 };
 
 AxisKind axis_kind(std::int64_t n) {
   if (n == 1) return AxisKind::kTrivial;
   if (mb200::fft::single_pass_supported(n)) return AxisKind::kSinglePass;
   if (!is_pow2(n) && n < mb200::fft::kMinBluestein) return AxisKind::kDirect;
+  if (!is_pow2(n) && mb200::fft::mixed_radix_supported(n)) return AxisKind::kMixed;
   if (!is_pow2(n) && n <= mb200::fft::kMaxBluestein) return AxisKind::kBluestein;
   if (!is_pow2(n) && n <= mb200::fft::kMaxBluesteinGlobal) return AxisKind::kBluesteinGlobal;
   if (is_pow2(n) && n <= kMaxSplit) return AxisKind::kSplit;
@@ -66,8 +67,8 @@ bool axis_supported(std::int64_t n) { return axis_kind(n) != AxisKind::kUnsuppor
 // power-of-two split is a rank-1 plan of its own).
 bool one_pass(std::int64_t n) {
   const AxisKind k = axis_kind(n);
-  return k == AxisKind::kTrivial || k == AxisKind::kSinglePass || k == AxisKind::kDirect ||
-         k == AxisKind::kBluestein || k == AxisKind::kBluesteinGlobal;
+  return k == AxisKind::kTrivial || k == AxisKind::kSinglePass || k == AxisKind::kMixed ||
+         k == AxisKind::kDirect || k == AxisKind::kBluestein || k == AxisKind::kBluesteinGlobal;
 }
 
 // Workspace per global-memory Bluestein axis (chunks of transforms).
@@ -235,6 +236,7 @@ cufftResult configure(Plan& p, int rank, const int* n, const int* inembed, int i
     t = AxisTables{};
     switch (axis_kind(len)) {
       case AxisKind::kSinglePass:
+      case AxisKind::kMixed:
       case AxisKind::kDirect:
         t.tw = hold(len);
         return t.tw != nullptr;
@@ -343,6 +345,11 @@ cudaError_t run_axis(std::int64_t n, int sign, const Batch1D& b, const AxisTable
       Batch1D c = b;
       c.tw = t.tw;
       return mb200::fft::launch_direct_dft(n, sign, c, st);
+    }
+    case AxisKind::kMixed: {
+      Batch1D c = b;
+      c.tw = t.tw;
+      return mb200::fft::launch_mixed_radix(n, sign, c, st);
     }
     case AxisKind::kBluestein:
       return mb200::fft::launch_bluestein(n, sign, b, t.chirp, t.bhat, t.tw_m, st);

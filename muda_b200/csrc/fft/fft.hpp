@@ -44,6 +44,14 @@ constexpr std::int64_t kMaxDirect = 25600;
 cudaError_t launch_direct_dft(std::int64_t n, int sign, const Batch1D& b,
                               cudaStream_t stream) noexcept;
 
+// Mixed-radix transforms (radices 16, 8, 4, 2, 3, 5, 7) of lengths that are not powers
+// of two and have no prime factor above 7, n <= kMaxMixed: one kernel, the whole
+// transform in shared memory; b.tw = exp(-2*pi*i*m/n).  In-place calls are allowed.
+constexpr std::int64_t kMaxMixed = 12288;
+bool mixed_radix_supported(std::int64_t n) noexcept;
+cudaError_t launch_mixed_radix(std::int64_t n, int sign, const Batch1D& b,
+                               cudaStream_t stream) noexcept;
+
 // Fills tw[0 .. n) with exp(-2*pi*i*m/n) rounded from double precision.
 void host_twiddles(std::int64_t n, float2* tw) noexcept;
 

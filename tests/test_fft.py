@@ -180,9 +180,30 @@ def test_gpu_non_pow2_lengths(cuda, built, n):
         assert rel_l2_per_transform(got, want, n, batch) <= TOL
 
 
-# Lengths that are not powers of two: below 32 the direct DFT, 32 .. 4096 the fused
-# Bluestein kernel (inner lengths 64 .. 8192), above that Bluestein through global memory.
-BLUESTEIN = [31, 33, 47, 97, 127, 255, 257, 1000, 1023, 2047, 2049, 3000, 4095, 4097, 6000]
+# Lengths that are not powers of two: below 32 the direct DFT; 7-smooth lengths up to
+# 12288 the mixed-radix kernel; other lengths 32 .. 4096 the fused Bluestein kernel
+# (inner lengths 64 .. 8192), above that Bluestein through global memory.
+BLUESTEIN = [31, 33, 47, 97, 127, 255, 257, 1023, 2047, 2049, 4095, 4097]
+# 7-smooth lengths: each radix family alone (3^5, 5^4, 7^4), with a power of two, with
+# several transforms per CTA, and the largest one shared memory holds (12288); 12500
+# is 7-smooth but above that bound, so it runs through global Bluestein.
+MIXED = [36, 48, 96, 243, 343, 625, 1000, 1536, 2401, 3000, 3125, 6000, 6144, 10000,
+         12000, 12288, 12500]
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("n", MIXED)
+def test_gpu_mixed_radix_lengths(cuda, built, n):
+    """Mixed-radix Stockham (radices 16, 8, 4, 2, 3, 5, 7) against numpy's float64 FFT,
+    both directions, with batches that leave a partial last CTA."""
+    rng = np.random.default_rng(n + 3)
+    batch = max(2, min(40, (1 << 16) // n)) + 1
+    x = rand_c64(rng, n * batch)
+    xd = x.reshape(batch, n).astype(np.complex128)
+    for sign in (-1, 1):
+        got = gpu_fft(cuda, x, [n], batch, sign)
+        want = (np.fft.fft(xd, axis=1) if sign < 0 else np.fft.ifft(xd, axis=1) * n).reshape(-1)
+        assert rel_l2_per_transform(got, want, n, batch) <= TOL
 
 
 @pytest.mark.gpu
@@ -215,8 +236,8 @@ def test_gpu_bluestein_lengths(cuda, built, n):
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("n", [60, 1000])
-def test_gpu_bluestein_in_place_and_strided(cuda, built, n):
+@pytest.mark.parametrize("n", [60, 1000, 97, 2049])
+def test_gpu_non_pow2_in_place_and_strided(cuda, built, n):
     rng = np.random.default_rng(n + 2)
     batch = 6
     x = rand_c64(rng, n * batch)

@@ -130,34 +130,50 @@ struct Io {
   bool active;       // false for the padding transforms of the last CTA
 };
 
-// One pass of radix R: n complex values from src to dst.
-template <int R, int S, int MODE>
+// Offset of element e of a transform in the caller's buffer: 32-bit for unit stride.
+template <bool UNIT>
+__device__ __forceinline__ std::int64_t io_offset(int e, std::int64_t stride) {
+  if constexpr (UNIT) {
+    return e;
+  } else {
+    return static_cast<std::int64_t>(e) * stride;
+  }
+}
+
+// One pass of radix R: n complex values from src to dst.  j / ns comes from a float
+// reciprocal: trunc((j + 0.5) * rn(1 / ns)) equals the integer quotient for every
+// j, ns <= 12288 (checked exhaustively), and keeps the integer divide off the FMA pipe
+// the butterflies use.
+template <int R, int S, int MODE, bool UNIT>
 __device__ __forceinline__ void mixed_pass(const float2* src, float2* dst, int n, int ns,
                                            int tid, int threads,
                                            const float2* __restrict__ tw, const Io& io) {
   const int nb = n / R;
   const int step = n / (ns * R);
+  const float inv_ns = __frcp_rn(static_cast<float>(ns));
   for (int j = tid; j < nb; j += threads) {
     float2 v[R];
     if constexpr (MODE == kFromGlobal) {
 #pragma unroll
       for (int r = 0; r < R; ++r)
-        v[r] = io.active ? io.in[(j + r * nb) * io.in_stride] : make_float2(0.0f, 0.0f);
+        v[r] = io.active ? io.in[io_offset<UNIT>(j + r * nb, io.in_stride)]
+                         : make_float2(0.0f, 0.0f);
     } else {
 #pragma unroll
       for (int r = 0; r < R; ++r) v[r] = src[at(j + r * nb)];
     }
-    const int k = j % ns;
+    const int q = __float2int_rz((static_cast<float>(j) + 0.5f) * inv_ns);
+    const int k = j - q * ns;
     if (ns > 1) {
 #pragma unroll
       for (int r = 1; r < R; ++r) v[r] = cmul(v[r], tw_at(tw, r * k * step, S));
     }
     small_dft<R, S>(v);
-    const int o = (j - k) * R + k;  // (j / ns) * ns * R + k
+    const int o = q * ns * R + k;
     if constexpr (MODE == kToGlobal) {
       if (io.active) {
 #pragma unroll
-        for (int r = 0; r < R; ++r) io.out[(o + r * ns) * io.out_stride] = v[r];
+        for (int r = 0; r < R; ++r) io.out[io_offset<UNIT>(o + r * ns, io.out_stride)] = v[r];
       }
     } else {
 #pragma unroll
@@ -168,18 +184,18 @@ __device__ __forceinline__ void mixed_pass(const float2* src, float2* dst, int n
 }
 
 // The `count` passes of radix R, pass numbers p .. p + count - 1 of `total`.
-template <int R, int S>
+template <int R, int S, bool UNIT>
 __device__ __forceinline__ void run_radix(int count, int& p, int total, float2*& src,
                                           float2*& dst, int n, int& ns, int tid,
                                           int threads, const float2* __restrict__ tw,
                                           const Io& io) {
   for (int i = 0; i < count; ++i, ++p, ns *= R) {
     if (p == 0) {
-      mixed_pass<R, S, kFromGlobal>(src, dst, n, ns, tid, threads, tw, io);
+      mixed_pass<R, S, kFromGlobal, UNIT>(src, dst, n, ns, tid, threads, tw, io);
     } else if (p == total - 1) {
-      mixed_pass<R, S, kToGlobal>(src, dst, n, ns, tid, threads, tw, io);
+      mixed_pass<R, S, kToGlobal, UNIT>(src, dst, n, ns, tid, threads, tw, io);
     } else {
-      mixed_pass<R, S, kShared>(src, dst, n, ns, tid, threads, tw, io);
+      mixed_pass<R, S, kShared, UNIT>(src, dst, n, ns, tid, threads, tw, io);
     }
     float2* t = src;
     src = dst;
@@ -187,7 +203,7 @@ __device__ __forceinline__ void run_radix(int count, int& p, int total, float2*&
   }
 }
 
-template <int S>
+template <int S, bool UNIT>
 __global__ void __launch_bounds__(512, 2)
     mixed_radix_kernel(const Batch1D bt, MixedPlan pl) {
   extern __shared__ float2 sbuf[];
@@ -209,17 +225,17 @@ __global__ void __launch_bounds__(512, 2)
     float2* src = sbuf + tl * 2 * padded(n);
     float2* dst = src + padded(n);
     int ns = 1, p = 0;
-    run_radix<16, S>(pl.n16, p, total, src, dst, n, ns, tid, pl.threads, bt.tw, io);
+    run_radix<16, S, UNIT>(pl.n16, p, total, src, dst, n, ns, tid, pl.threads, bt.tw, io);
     if (pl.r2 == 8) {
-      run_radix<8, S>(1, p, total, src, dst, n, ns, tid, pl.threads, bt.tw, io);
+      run_radix<8, S, UNIT>(1, p, total, src, dst, n, ns, tid, pl.threads, bt.tw, io);
     } else if (pl.r2 == 4) {
-      run_radix<4, S>(1, p, total, src, dst, n, ns, tid, pl.threads, bt.tw, io);
+      run_radix<4, S, UNIT>(1, p, total, src, dst, n, ns, tid, pl.threads, bt.tw, io);
     } else if (pl.r2 == 2) {
-      run_radix<2, S>(1, p, total, src, dst, n, ns, tid, pl.threads, bt.tw, io);
+      run_radix<2, S, UNIT>(1, p, total, src, dst, n, ns, tid, pl.threads, bt.tw, io);
     }
-    run_radix<3, S>(pl.n3, p, total, src, dst, n, ns, tid, pl.threads, bt.tw, io);
-    run_radix<5, S>(pl.n5, p, total, src, dst, n, ns, tid, pl.threads, bt.tw, io);
-    run_radix<7, S>(pl.n7, p, total, src, dst, n, ns, tid, pl.threads, bt.tw, io);
+    run_radix<3, S, UNIT>(pl.n3, p, total, src, dst, n, ns, tid, pl.threads, bt.tw, io);
+    run_radix<5, S, UNIT>(pl.n5, p, total, src, dst, n, ns, tid, pl.threads, bt.tw, io);
+    run_radix<7, S, UNIT>(pl.n7, p, total, src, dst, n, ns, tid, pl.threads, bt.tw, io);
     // the last pass ended with a barrier, so the buffers are free for the next transform
   }
 }
@@ -268,7 +284,9 @@ cudaError_t launch_mixed_radix(std::int64_t n, int sign, const Batch1D& b,
   if (b.batch <= 0) return cudaSuccess;
   const int threads = p.threads * p.tpc;
   const std::size_t smem = static_cast<std::size_t>(p.tpc) * 2 * padded(p.n) * sizeof(float2);
-  auto kern = sign < 0 ? mixed_radix_kernel<-1> : mixed_radix_kernel<1>;
+  const bool unit = b.in_stride == 1 && b.out_stride == 1;
+  auto kern = sign < 0 ? (unit ? mixed_radix_kernel<-1, true> : mixed_radix_kernel<-1, false>)
+                       : (unit ? mixed_radix_kernel<1, true> : mixed_radix_kernel<1, false>);
   if (smem > 48 * 1024) {
     const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                static_cast<int>(smem));

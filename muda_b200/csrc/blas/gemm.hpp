@@ -48,6 +48,15 @@ std::size_t gemm_tf32x3_workspace(const GemmArgs& g) noexcept;
 cudaError_t launch_gemm_tf32x3(const GemmArgs& g, void* workspace, std::size_t ws_bytes,
                                cudaStream_t stream) noexcept;
 
+// The same with op(A) already split by the caller: a_planes holds the hi plane and
+// then the lo plane of op(A), each m rows of tf32_plane_ldk(k) floats, element (i, p)
+// of op(A) at a_planes[i * ldk + p] (k contiguous; the padding columns are not read).
+// g.a / g.lda / g.trans_a are ignored; batch 1.  Only B is split, into the workspace.
+std::size_t gemm_tf32x3_aplanes_workspace(const GemmArgs& g) noexcept;
+cudaError_t launch_gemm_tf32x3_aplanes(const GemmArgs& g, const float* a_planes, void* workspace,
+                                       std::size_t ws_bytes, cudaStream_t stream) noexcept;
+inline std::int64_t tf32_plane_ldk(std::int64_t k) { return (k + 3) / 4 * 4; }
+
 // Name of the kernel family that would serve `g` (for tests and benchmarks).
 const char* gemm_path_name(const GemmArgs& g) noexcept;
 

@@ -189,13 +189,18 @@ cudaError_t run(const GemmArgs& g, cudaStream_t stream) {
 
 // ---------------------------------------------------------------- split tf32 (fp32)
 
-constexpr int kStages32 = 2;  // 2 x (32 + 64) KB stages
-constexpr int kMaxSplitK = 16;
+// Tile width by output columns (n <= 64: 64, <= 128: 128, else 256) and the ring
+// depth that fills about 192 KB: stages of 32 KB (A) + TBN * 256 B (B).
+template <int TBN>
+constexpr int kSplitStages = TBN == 64 ? 4 : TBN == 128 ? 3 : 2;
+int split_bn(int n) { return n <= 64 ? 64 : n <= 128 ? 128 : 256; }
+constexpr int kMaxSplitK = 32;
 constexpr std::size_t kWorkspaceCap = std::size_t{2} << 30;
 
+template <int TBN>
 struct SplitGemmProblem {
   CUtensorMap ma;  // A planes: dims (k, m, batch, plane), box {32, 128, 1, 2}
-  CUtensorMap mb;  // B planes: dims (k, n, batch, plane), box {32, BN, 1, 2}
+  CUtensorMap mb;  // B planes: dims (k, n, batch, plane), box {32, TBN, 1, 2}
   long long tiles_total;
   int num_kb;  // k-blocks per split
   int ksplit;
@@ -228,7 +233,7 @@ struct SplitGemmProblem {
     const int z = c3[0] / ksplit;
     const int k = ((c3[0] % ksplit) * num_kb + kb) * tc::kBK32;  // past K reads as zeros
     tc::tma_load_4d(sa, &ma, k, c3[1] * tc::kBM, z, 0, bar);
-    tc::tma_load_4d(sb, &mb, k, c3[2] * BN, z, 0, bar);
+    tc::tma_load_4d(sb, &mb, k, c3[2] * TBN, z, 0, bar);
   }
 
   __device__ void scalars(float& a, float& b) const {
@@ -240,7 +245,7 @@ struct SplitGemmProblem {
                         float b) const {
     const int mm = c3[1] * tc::kBM + row;
     if (mm >= m) return;
-    const int n0 = c3[2] * BN + col0;
+    const int n0 = c3[2] * TBN + col0;
     if (ksplit > 1) {
       float* pz = partial + static_cast<long long>(c3[0]) * m * n + mm;
 #pragma unroll
@@ -320,7 +325,8 @@ SplitPlan plan_split(const GemmArgs& g, int sms, int nb) {
   SplitPlan pl{};
   pl.nb = nb;
   const long long ldk = round_up4(g.k);
-  const int tiles = ((g.m + tc::kBM - 1) / tc::kBM) * ((g.n + BN - 1) / BN) * nb;
+  const int bn = split_bn(g.n);
+  const int tiles = ((g.m + tc::kBM - 1) / tc::kBM) * ((g.n + bn - 1) / bn) * nb;
   const int total_kb = (g.k + tc::kBK32 - 1) / tc::kBK32;
   int ks = 1;
   if (2 * tiles < sms) {
@@ -370,34 +376,23 @@ bool make_plane_map(CUtensorMap* map, const float* planes, long long k, long lon
   return tc::encode_tiled(map, 2, planes, 4, dims, strides, box);
 }
 
-cudaError_t run_chunk(const GemmArgs& g, const SplitPlan& pl, int z0, int nb, float* ws,
-                      int sms, unsigned int* to, cudaStream_t stream) {
+template <int TBN>
+cudaError_t run_split_gemm(const GemmArgs& g, const SplitPlan& pl, int nb, const float* pa,
+                           const float* pb, float* pp, float* c, int sms, unsigned int* to,
+                           cudaStream_t stream) {
   const long long ldk = round_up4(g.k);
-  float* pa = ws;
-  float* pb = pa + pl.a_floats;
-  float* pp = pb + pl.b_floats;
-  const float* a = static_cast<const float*>(g.a) + z0 * g.stride_a;
-  const float* b = static_cast<const float*>(g.b) + z0 * g.stride_b;
-  // op(A) is m x k: element (i, p) at A[i + p*lda] (N) or A[p + i*lda] (T);
-  // op(B) is k x n: element (p, j) at B[p + j*ldb] (N) or B[j + p*ldb] (T), rows j
-  const tc::SplitJob ja{a, g.m, g.k, nb, g.trans_a ? g.lda : 1, g.trans_a ? 1 : g.lda,
-                        g.stride_a, pa, ldk};
-  const tc::SplitJob jb{b, g.n, g.k, nb, g.trans_b ? 1 : g.ldb, g.trans_b ? g.ldb : 1,
-                        g.stride_b, pb, ldk};
-  cudaError_t e = tc::launch_tf32_split_pair(ja, jb, stream);
-  if (e != cudaSuccess) return e;
-  SplitGemmProblem p{};
+  SplitGemmProblem<TBN> p{};
   if (!make_plane_map(&p.ma, pa, g.k, g.m, nb, ldk, tc::kBM) ||
-      !make_plane_map(&p.mb, pb, g.k, g.n, nb, ldk, BN))
+      !make_plane_map(&p.mb, pb, g.k, g.n, nb, ldk, TBN))
     return cudaErrorNotSupported;
   p.m = g.m;
   p.n = g.n;
   p.tiles_m = (g.m + tc::kBM - 1) / tc::kBM;
-  p.tiles_n = (g.n + BN - 1) / BN;
+  p.tiles_n = (g.n + TBN - 1) / TBN;
   p.ksplit = pl.ksplit;
   p.num_kb = pl.kb_per;
   p.tiles_total = static_cast<long long>(p.tiles_m) * p.tiles_n * nb * pl.ksplit;
-  p.c = static_cast<float*>(g.c) + z0 * g.stride_c;
+  p.c = c;
   p.ldc = g.ldc;
   p.stride_c = g.stride_c;
   p.partial = pp;
@@ -405,20 +400,53 @@ cudaError_t run_chunk(const GemmArgs& g, const SplitPlan& pl, int z0, int nb, fl
   p.beta = g.beta;
   p.alpha_dev = g.alpha_dev;
   p.beta_dev = g.beta_dev;
-  e = tc::launch_tc_gemm<SplitGemmProblem, BN, kStages32, tc::kFmtTf32x3>(p, sms, to, stream);
+  return tc::launch_tc_gemm<SplitGemmProblem<TBN>, TBN, kSplitStages<TBN>, tc::kFmtTf32x3>(
+      p, sms, to, stream);
+}
+
+// a_planes: op(A) already split (batch 1), else nullptr and A is split here.
+cudaError_t run_chunk(const GemmArgs& g, const SplitPlan& pl, int z0, int nb, float* ws,
+                      int sms, unsigned int* to, cudaStream_t stream,
+                      const float* a_planes = nullptr) {
+  const long long ldk = round_up4(g.k);
+  float* pa = a_planes != nullptr ? const_cast<float*>(a_planes) : ws;
+  float* pb = a_planes != nullptr ? ws : ws + pl.a_floats;
+  float* pp = pb + pl.b_floats;
+  // op(A) is m x k: element (i, p) at A[i + p*lda] (N) or A[p + i*lda] (T);
+  // op(B) is k x n: element (p, j) at B[p + j*ldb] (N) or B[j + p*ldb] (T), rows j
+  const float* b = static_cast<const float*>(g.b) + z0 * g.stride_b;
+  const tc::SplitJob jb{b, g.n, g.k, nb, g.trans_b ? 1 : g.ldb, g.trans_b ? g.ldb : 1,
+                        g.stride_b, pb, ldk};
+  cudaError_t e;
+  if (a_planes != nullptr) {
+    e = tc::launch_tf32_split(jb.src, jb.rows, jb.cols, jb.batch, jb.rs, jb.ks, jb.zs, jb.dst,
+                              jb.ldk, stream);
+  } else {
+    const float* a = static_cast<const float*>(g.a) + z0 * g.stride_a;
+    const tc::SplitJob ja{a, g.m, g.k, nb, g.trans_a ? g.lda : 1, g.trans_a ? 1 : g.lda,
+                          g.stride_a, pa, ldk};
+    e = tc::launch_tf32_split_pair(ja, jb, stream);
+  }
+  if (e != cudaSuccess) return e;
+  float* c = static_cast<float*>(g.c) + z0 * g.stride_c;
+  switch (split_bn(g.n)) {
+    case 64: e = run_split_gemm<64>(g, pl, nb, pa, pb, pp, c, sms, to, stream); break;
+    case 128: e = run_split_gemm<128>(g, pl, nb, pa, pb, pp, c, sms, to, stream); break;
+    default: e = run_split_gemm<256>(g, pl, nb, pa, pb, pp, c, sms, to, stream); break;
+  }
   if (e != cudaSuccess || pl.ksplit == 1) return e;
   const bool vec = g.m % 4 == 0 && g.ldc % 4 == 0 && (nb == 1 || g.stride_c % 4 == 0) &&
-                   aligned_to(p.c, 16);
+                   aligned_to(c, 16);
   const int per = vec ? g.m / 4 : g.m;
   const long long cols = static_cast<long long>(g.n) * nb;
   const dim3 grid(static_cast<unsigned>((per + 255) / 256 < 64 ? (per + 255) / 256 : 64),
                   static_cast<unsigned>(cols < 65535 ? cols : 65535));
   if (vec)
-    reduce_splits<true><<<grid, 256, 0, stream>>>(pp, pl.ksplit, g.m, g.n, nb, p.c, g.ldc,
+    reduce_splits<true><<<grid, 256, 0, stream>>>(pp, pl.ksplit, g.m, g.n, nb, c, g.ldc,
                                                   g.stride_c, g.alpha, g.beta, g.alpha_dev,
                                                   g.beta_dev);
   else
-    reduce_splits<false><<<grid, 256, 0, stream>>>(pp, pl.ksplit, g.m, g.n, nb, p.c, g.ldc,
+    reduce_splits<false><<<grid, 256, 0, stream>>>(pp, pl.ksplit, g.m, g.n, nb, c, g.ldc,
                                                    g.stride_c, g.alpha, g.beta, g.alpha_dev,
                                                    g.beta_dev);
   return cudaGetLastError();
@@ -450,6 +478,27 @@ cudaError_t launch_gemm_tf32x3(const GemmArgs& g, void* workspace, std::size_t w
     if (e != cudaSuccess) return e;
   }
   return cudaSuccess;
+}
+
+std::size_t gemm_tf32x3_aplanes_workspace(const GemmArgs& g) noexcept {
+  if (!tf32x3_supported(g) || g.batch != 1) return 0;
+  const SplitPlan pl = plan_for(g, sm_count(current_device()));
+  return pl.nb == 0 ? 0 : pl.bytes() - pl.a_floats * 4;
+}
+
+cudaError_t launch_gemm_tf32x3_aplanes(const GemmArgs& g, const float* a_planes, void* workspace,
+                                       std::size_t ws_bytes, cudaStream_t stream) noexcept {
+  if (!tf32x3_supported(g) || g.batch != 1 || a_planes == nullptr ||
+      !aligned_to(a_planes, 16))
+    return cudaErrorNotSupported;
+  const int sms = sm_count(current_device());
+  const SplitPlan pl = plan_for(g, sms);
+  if (pl.nb == 0 || workspace == nullptr || ws_bytes < pl.bytes() - pl.a_floats * 4 ||
+      !aligned_to(workspace, 16))
+    return cudaErrorNotSupported;
+  unsigned int* to = timeout_counter();
+  if (to == nullptr) return cudaErrorNotSupported;
+  return run_chunk(g, pl, 0, 1, static_cast<float*>(workspace), sms, to, stream, a_planes);
 }
 
 const char* gemm_path_name(const GemmArgs& g) noexcept {

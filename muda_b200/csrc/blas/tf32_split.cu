@@ -9,18 +9,7 @@ namespace mb200::tc {
 namespace {
 
 __device__ __forceinline__ void split(float x, float& hi, float& lo) {
-  const unsigned b = __float_as_uint(x);
-  if ((b & 0x7F800000u) == 0x7F800000u) {  // inf / nan: both planes carry x
-    hi = x;
-    lo = x;
-    return;
-  }
-  hi = __uint_as_float(b & 0xFFFFE000u);  // toward zero: lo keeps the sign of x
-  float r = __fsub_rn(x, hi);              // exact
-  if (r == 0.0f) r = __fmul_rn(x, 0x1p-40f);
-  unsigned t;
-  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(t) : "f"(r));
-  lo = __uint_as_float(t);
+  tf32_split_value(x, hi, lo);
 }
 
 constexpr int kTile = 32;

@@ -12,7 +12,12 @@
 // Backward filter: T (K x C*R*S) = dY^T (K x N*P*Q) * Xcol (N*P*Q x C*R*S), Xcol the
 // im2col of x in the filter's (r, s, c) or (c, r, s) order, as one split-tf32 GEMM
 // (gemm_tc_kernels.cu) per chunk of N*P*Q rows accumulating into T; a last pass
-// writes dw = alpha * T^T + beta * dw in the filter layout.
+// writes dw = alpha * T^T + beta * dw in the filter layout.  For packed NHWC x and a
+// KRSC filter the orientation flips: dw (CRS x K) = Xcol^T dY straight into the
+// filter (alpha, beta on the first chunk, then beta 1), with im2col_planes writing
+// Xcol as the GEMM's split-tf32 A planes in one pass (no fp32 im2col matrix, no
+// separate split, no T).  CRS then fills the 128-row side of the tile and K the
+// narrow side, instead of K = 64 leaving half of each 128-row MMA idle.
 // dY is read in place when each pixel's K gradients are contiguous (NHWC), else it
 // is gathered into a dense N*P*Q x K matrix first.
 //
@@ -24,6 +29,7 @@
 #include <cstdint>
 
 #include "blas/gemm.hpp"
+#include "blas/tf32_split.hpp"
 #include "common/device.hpp"
 #include "dnn/dnn.hpp"
 
@@ -148,6 +154,85 @@ __global__ void __launch_bounds__(kThreads)
   }
 }
 
+// im2col of packed NHWC x in (r, s, c) column order written straight as the GEMM's
+// split-tf32 B planes: planes[p][crs][row] (row = pixel within the chunk, ldk floats
+// a column, p = 0 hi, 1 lo), so neither the fp32 im2col matrix nor its transpose is
+// ever stored.  A CTA takes 32 pixels x 32 channels and walks the R*S taps: each
+// pixel is decomposed once (32-bit: the plan keeps N*P*Q below 2^31), each tap reads
+// along the channels (contiguous in x, which stays in L2 across the taps),
+// transposes in shared memory and writes along the pixels.
+constexpr int kPlaneTile = 32;
+
+__global__ void __launch_bounds__(kThreads)
+    im2col_planes(const float* __restrict__ x, ConvShape s, std::int64_t npq0, std::int64_t rows,
+                  std::int64_t ldk, float* __restrict__ planes) {
+  __shared__ float tile[kPlaneTile][kPlaneTile + 1];  // [channel][pixel]
+  constexpr int kRows = kThreads / kPlaneTile;
+  constexpr int kPer = kPlaneTile / kRows;  // pixel rows a thread loads per tap
+  const int C = s.x.c, R = s.kh, S = s.kw;
+  const std::int64_t plane = static_cast<std::int64_t>(C) * R * S * ldk;
+  const int ctiles = (C + kPlaneTile - 1) / kPlaneTile;
+  const std::int64_t total = ((rows + kPlaneTile - 1) / kPlaneTile) * ctiles;
+  const int tx = threadIdx.x % kPlaneTile, ty = threadIdx.x / kPlaneTile;
+  for (std::int64_t t = blockIdx.x; t < total; t += gridDim.x) {
+    const int ct = static_cast<int>(t % ctiles);
+    const std::int64_t row0 = (t / ctiles) * kPlaneTile;
+    const int c = ct * kPlaneTile + tx;
+    // this thread's pixel rows: image base offset and top-left input corner
+    std::int64_t base[kPer];
+    int y0[kPer], x0[kPer];
+#pragma unroll
+    for (int i = 0; i < kPer; ++i) {
+      const std::int64_t row = row0 + ty + i * kRows;
+      if (row < rows && c < C) {
+        const int npq = static_cast<int>(npq0 + row);
+        const int q = npq % s.y.w;
+        const int bp = npq / s.y.w;
+        const int p = bp % s.y.h;
+        const int b = bp / s.y.h;
+        base[i] = static_cast<std::int64_t>(b) * s.x.ns + c;
+        y0[i] = p * s.stride_h - s.pad_h;
+        x0[i] = q * s.stride_w - s.pad_w;
+      } else {
+        base[i] = 0;
+        y0[i] = -(1 << 30);  // never inside the image
+        x0[i] = 0;
+      }
+    }
+    for (int fr = 0; fr < R; ++fr) {
+      const int r = s.convolution ? R - 1 - fr : fr;
+      for (int fs = 0; fs < S; ++fs) {
+        const int sv = s.convolution ? S - 1 - fs : fs;
+#pragma unroll
+        for (int i = 0; i < kPer; ++i) {
+          const int iy = y0[i] + r * s.dil_h;
+          const int ix = x0[i] + sv * s.dil_w;
+          float v = 0.0f;
+          if (iy >= 0 && iy < s.x.h && ix >= 0 && ix < s.x.w)
+            v = __ldg(x + base[i] + (static_cast<std::int64_t>(iy) * s.x.w + ix) * C);
+          tile[tx][ty + i * kRows] = v;
+        }
+        __syncthreads();
+        const std::int64_t col0 = static_cast<std::int64_t>(fr * S + fs) * C;
+#pragma unroll
+        for (int i = 0; i < kPer; ++i) {
+          const int a = ty + i * kRows;
+          const int cc = ct * kPlaneTile + a;
+          const std::int64_t row = row0 + tx;
+          if (cc < C && row < rows) {
+            float hi, lo;
+            tc::tf32_split_value(tile[a][tx], hi, lo);
+            const std::int64_t at = (col0 + cc) * ldk + row;
+            planes[at] = hi;
+            planes[plane + at] = lo;
+          }
+        }
+        __syncthreads();
+      }
+    }
+  }
+}
+
 // dw = alpha * T^T + beta * dw, T the K x CRS column-major GEMM result (T[k + crs*K])
 // and dw the filter layout k*CRS + crs.
 __global__ void __launch_bounds__(kThreads)
@@ -196,6 +281,7 @@ struct FilterPlan {
   std::int64_t npq = 0, chunk = 0;  // rows per GEMM
   std::size_t cols_bytes = 0, dy_bytes = 0, t_bytes = 0, gemm_bytes = 0;
   bool dy_direct = false;
+  bool planes = false;  // im2col written as split planes (packed NHWC x, KRSC filter)
   std::size_t bytes() const { return cols_bytes + dy_bytes + t_bytes + gemm_bytes; }
 };
 
@@ -225,13 +311,37 @@ blas::GemmArgs filter_gemm(const ConvShape& s, std::int64_t rows, const float* c
   return g;
 }
 
+// dw (KRSC: element (crs, k) at dw[k * CRS + crs], a CRS x K column-major matrix)
+// = alpha * Xcol^T dY + beta * dw over one chunk, Xcol given as split planes: CRS on
+// the 128-row side of the tensor-core tile, K on its 64/128/256-column side.
+blas::GemmArgs filter_gemm_planes(const ConvShape& s, std::int64_t rows, const float* dy,
+                                  std::int64_t ldy, float* dw, float alpha, float beta) {
+  const std::int64_t crs = static_cast<std::int64_t>(s.x.c) * s.kh * s.kw;
+  blas::GemmArgs g{};
+  g.type = blas::Elem::kF32;
+  g.trans_b = true;  // dY: element (p, k) at dy[p * ldy + k]
+  g.m = static_cast<int>(crs);
+  g.n = s.y.c;
+  g.k = static_cast<int>(rows);
+  g.b = dy;
+  g.ldb = ldy;
+  g.c = dw;
+  g.ldc = crs;
+  g.batch = 1;
+  g.alpha = alpha;
+  g.beta = beta;
+  return g;
+}
+
 FilterPlan plan_filter(const ConvShape& s) {
   FilterPlan pl{};
   if (s.groups != 1) return pl;
   const std::int64_t crs = static_cast<std::int64_t>(s.x.c) * s.kh * s.kw;
   pl.npq = static_cast<std::int64_t>(s.y.n) * s.y.h * s.y.w;
   if (pl.npq <= 0 || crs <= 0 || pl.npq >= (std::int64_t{1} << 31) || crs >= (1 << 30)) return pl;
-  const std::int64_t cap = static_cast<std::int64_t>(kColsCap / (crs * 4));
+  pl.planes = s.filter_krsc && packed_nhwc(s.x);
+  const std::int64_t cap =
+      static_cast<std::int64_t>(kColsCap / (crs * 4 * (pl.planes ? 2 : 1))) / 4 * 4;
   if (cap <= 0) return {};
   // equal chunks (the last one at most nchunks - 1 rows shorter), each a GEMM the
   // tensor-core path accepts
@@ -239,13 +349,20 @@ FilterPlan plan_filter(const ConvShape& s) {
   pl.chunk = (pl.npq + nchunks - 1) / nchunks;
   const std::int64_t last = pl.npq - (nchunks - 1) * pl.chunk;
   pl.dy_direct = packed_nhwc(s.y);
-  pl.cols_bytes = round256(static_cast<std::size_t>(pl.chunk * crs * 4));
+  pl.cols_bytes =
+      pl.planes
+          ? round256(static_cast<std::size_t>(2 * crs * blas::tf32_plane_ldk(pl.chunk) * 4))
+          : round256(static_cast<std::size_t>(pl.chunk * crs * 4));
   pl.dy_bytes = pl.dy_direct ? 0 : round256(static_cast<std::size_t>(pl.chunk) * s.y.c * 4);
-  pl.t_bytes = round256(static_cast<std::size_t>(crs) * s.y.c * 4);
-  const std::size_t g_full =
-      blas::gemm_tf32x3_workspace(filter_gemm(s, pl.chunk, nullptr, nullptr, s.y.c, nullptr, 0));
-  const std::size_t g_last =
-      blas::gemm_tf32x3_workspace(filter_gemm(s, last, nullptr, nullptr, s.y.c, nullptr, 0));
+  pl.t_bytes = pl.planes ? 0 : round256(static_cast<std::size_t>(crs) * s.y.c * 4);
+  auto ws = [&](std::int64_t rows) {
+    if (pl.planes)
+      return blas::gemm_tf32x3_aplanes_workspace(
+          filter_gemm_planes(s, rows, nullptr, s.y.c, nullptr, 1.0f, 0.0f));
+    return blas::gemm_tf32x3_workspace(filter_gemm(s, rows, nullptr, nullptr, s.y.c, nullptr, 0));
+  };
+  const std::size_t g_full = ws(pl.chunk);
+  const std::size_t g_last = ws(last);
   if (g_full == 0 || g_last == 0) return {};
   pl.gemm_bytes = std::max(g_full, g_last);
   return pl;
@@ -296,10 +413,17 @@ cudaError_t launch_conv_bwd_filter_tc(const float* x, const float* dy, float* dw
   const bool vec = s.filter_krsc && packed_nhwc(s.x) && s.x.c % 4 == 0 && aligned_to(x, 16);
   for (std::int64_t r0 = 0; r0 < pl.npq; r0 += pl.chunk) {
     const std::int64_t rows = std::min(pl.chunk, pl.npq - r0);
-    if (vec)
+    const std::int64_t ldk = blas::tf32_plane_ldk(rows);
+    if (pl.planes) {
+      const std::int64_t tiles =
+          ((rows + kPlaneTile - 1) / kPlaneTile) * ((s.x.c + kPlaneTile - 1) / kPlaneTile);
+      im2col_planes<<<grid_for(tiles * kThreads), kThreads, 0, stream>>>(x, s, r0, rows, ldk,
+                                                                          cols);
+    } else if (vec) {
       im2col_nhwc4<<<grid_for(rows * (s.x.c / 4)), kThreads, 0, stream>>>(x, s, r0, rows, cols);
-    else
+    } else {
       im2col<<<grid_for(rows * crs), kThreads, 0, stream>>>(x, s, r0, rows, cols);
+    }
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
     const float* dmat = dy + r0 * s.y.c;
@@ -309,10 +433,18 @@ cudaError_t launch_conv_bwd_filter_tc(const float* x, const float* dy, float* dw
       if (e != cudaSuccess) return e;
       dmat = dense;
     }
-    const blas::GemmArgs g = filter_gemm(s, rows, cols, dmat, s.y.c, tmat, r0 == 0 ? 0.0f : 1.0f);
-    e = blas::launch_gemm_tf32x3(g, gws, pl.gemm_bytes, stream);
+    if (pl.planes) {
+      const blas::GemmArgs g =
+          filter_gemm_planes(s, rows, dmat, s.y.c, dw, alpha, r0 == 0 ? beta : 1.0f);
+      e = blas::launch_gemm_tf32x3_aplanes(g, cols, gws, pl.gemm_bytes, stream);
+    } else {
+      const blas::GemmArgs g =
+          filter_gemm(s, rows, cols, dmat, s.y.c, tmat, r0 == 0 ? 0.0f : 1.0f);
+      e = blas::launch_gemm_tf32x3(g, gws, pl.gemm_bytes, stream);
+    }
     if (e != cudaSuccess) return e;
   }
+  if (pl.planes) return cudaSuccess;  // the GEMM wrote dw
   finish_filter<<<grid_for(crs * s.y.c), kThreads, 0, stream>>>(tmat, dw, s.y.c, crs, alpha,
                                                                  beta);
   return cudaGetLastError();

@@ -235,6 +235,8 @@ CONV_CASES = [  # xshape, wshape, pad, stride, dil, groups, mode, fmt
     ((2, 64, 16, 16), (32, 64, 5, 5), (2, 2), (1, 1), (1, 1), 1, "cross", "NHWC"),
     ((8, 64, 28, 28), (64, 64, 3, 3), (1, 1), (2, 2), (1, 1), 1, "cross", "NHWC"),
     ((8, 64, 28, 28), (64, 64, 3, 3), (1, 1), (1, 1), (1, 1), 1, "cross", "NCHW"),
+    # channels and pixels that fill neither a 32-channel nor a 32-pixel tile
+    ((6, 40, 13, 11), (64, 40, 3, 3), (1, 1), (1, 1), (1, 1), 1, "cross", "NHWC"),
 ]
 
 

@@ -507,8 +507,9 @@ def suite_spmm(s: Suite) -> dict:
     assert L.cusparseCreateDnMat(C.byref(mc), rows, n, n, C.c_void_p(c.data_ptr()), 0,
                                  capi.CUSPARSE_ORDER_ROW) == 0
     one, zero = C.c_float(1.0), C.c_float(0.0)
+    # two kernels a call: spmm_find_long (the long-row list) and spmm_rows_ring
     ms, launches = s.time(lambda: L.cusparseSpMM(h, 0, 0, C.byref(one), ma, mb, C.byref(zero), mc,
-                                                 0, 0, None), flush=True)
+                                                 0, 0, None), flush=True, launches_per_call=2)
     for fn, d in (("cusparseDestroyDnMat", mb), ("cusparseDestroyDnMat", mc),
                   ("cusparseDestroySpMat", ma)):
         assert getattr(L, fn)(d) == 0
@@ -520,7 +521,7 @@ def suite_spmm(s: Suite) -> dict:
            "gflops": 2 * nnz * n / (ms * 1e-3) / 1e9,
            "config": f"{rows} rows, nnz {nnz}, N {n} row-major, L2 flushed before each call; "
                      "bytes = A + B + C once (B rows re-gathered per entry come through L2)",
-           "roofline": s.roof("spmm_rows<4,true,true>", gbs, "hbm"), "launches": launches,
+           "roofline": s.roof("spmm_rows_ring<16>", gbs, "hbm"), "launches": launches,
            "algorithmic_bytes_per_call": alg_bytes}
     if s.cpu:
         import oracle

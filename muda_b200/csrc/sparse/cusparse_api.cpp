@@ -30,8 +30,9 @@ constexpr int kCusparseVersion = 12000;
 struct SparseContext {
   std::mutex mu;
   cudaStream_t stream = nullptr;
-  // fp32 scratch of the fp16 transposed product: held under ws_mu for the call,
-  // reuse ordered after the previous call's last use by ws_done
+  // device scratch (fp32 sums of the fp16 transposed product, the SpMM row
+  // scheduler): held under ws_mu for the call, reuse ordered after the previous
+  // call's last use by ws_done
   std::mutex ws_mu;
   std::shared_ptr<mb200::DeviceBuffer> ws;
   cudaEvent_t ws_done = nullptr;
@@ -39,6 +40,37 @@ struct SparseContext {
     if (ws_done != nullptr) (void)cudaEventDestroy(ws_done);
   }
 };
+
+// Runs launch(scratch pointer) with at least `need` bytes of the handle's scratch,
+// after the previous user of the scratch in stream order (outside stream capture;
+// a captured call orders by the capture itself).
+template <class Launch>
+cudaError_t with_scratch(SparseContext& ctx, cudaStream_t stream, std::size_t need,
+                         Launch&& launch) {
+  std::lock_guard<std::mutex> g(ctx.ws_mu);
+  cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(stream, &cap) != cudaSuccess) cap = cudaStreamCaptureStatusNone;
+  const bool ordered = cap == cudaStreamCaptureStatusNone;
+  if (ordered && ctx.ws_done != nullptr) {
+    const cudaError_t w = cudaStreamWaitEvent(stream, ctx.ws_done, 0);
+    if (w != cudaSuccess) return w;
+  }
+  if (!ctx.ws || ctx.ws->bytes < need || ctx.ws->device != mb200::current_device()) {
+    ctx.ws.reset();
+    ctx.ws = mb200::DeviceBuffer::make(need);
+    if (!ctx.ws) return cudaErrorMemoryAllocation;
+  }
+  cudaError_t e = launch(ctx.ws->ptr);
+  if (e == cudaSuccess && ordered) {
+    if (ctx.ws_done == nullptr &&
+        cudaEventCreateWithFlags(&ctx.ws_done, cudaEventDisableTiming) != cudaSuccess) {
+      ctx.ws_done = nullptr;
+      return cudaErrorUnknown;
+    }
+    e = cudaEventRecord(ctx.ws_done, stream);
+  }
+  return e;
+}
 
 struct CsrDesc {
   std::int64_t rows = 0, cols = 0, nnz = 0;
@@ -311,29 +343,12 @@ cusparseStatus_t cusparseSpMV(cusparseHandle_t handle, cusparseOperation_t opA, 
                                          stream);
   } else {
     // fp16: fp32 sums in the handle's scratch, reused in stream order across calls
-    SparseContext& ctx = *o.ctx;
-    std::lock_guard<std::mutex> g(ctx.ws_mu);
-    cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
-    if (cudaStreamIsCapturing(stream, &cap) != cudaSuccess) cap = cudaStreamCaptureStatusNone;
-    const bool ordered = cap == cudaStreamCaptureStatusNone;
-    if (ordered && ctx.ws_done != nullptr && cudaStreamWaitEvent(stream, ctx.ws_done, 0) != cudaSuccess)
-      return CUSPARSE_STATUS_EXECUTION_FAILED;
     const std::size_t need = static_cast<std::size_t>(o.a->cols) * sizeof(float);
-    if (!ctx.ws || ctx.ws->bytes < need || ctx.ws->device != mb200::current_device()) {
-      ctx.ws.reset();
-      ctx.ws = mb200::DeviceBuffer::make(need);
-      if (!ctx.ws) return CUSPARSE_STATUS_ALLOC_FAILED;
-    }
-    e = mb200::sparse::launch_spmv_csr_t(a, vt, o.x->values, o.y->values, al, be,
-                                         static_cast<float*>(ctx.ws->ptr), stream);
-    if (e == cudaSuccess && ordered) {
-      if (ctx.ws_done == nullptr &&
-          cudaEventCreateWithFlags(&ctx.ws_done, cudaEventDisableTiming) != cudaSuccess) {
-        ctx.ws_done = nullptr;
-        return CUSPARSE_STATUS_EXECUTION_FAILED;
-      }
-      e = cudaEventRecord(ctx.ws_done, stream);
-    }
+    e = with_scratch(*o.ctx, stream, need, [&](void* ws) {
+      return mb200::sparse::launch_spmv_csr_t(a, vt, o.x->values, o.y->values, al, be,
+                                              static_cast<float*>(ws), stream);
+    });
+    if (e == cudaErrorMemoryAllocation) return CUSPARSE_STATUS_ALLOC_FAILED;
   }
   return e == cudaSuccess ? CUSPARSE_STATUS_SUCCESS : CUSPARSE_STATUS_EXECUTION_FAILED;
 }
@@ -447,9 +462,16 @@ cusparseStatus_t cusparseSpMM(cusparseHandle_t handle, cusparseOperation_t opA,
                                    opB != CUSPARSE_OPERATION_NON_TRANSPOSE};
   const mb200::sparse::DenseView c{static_cast<float*>(o.c->values), o.c->ld,
                                    o.c->order == CUSPARSE_ORDER_COL, false};
-  const cudaError_t e = mb200::sparse::launch_spmm_csr(
-      view_of(*o.a), opA != CUSPARSE_OPERATION_NON_TRANSPOSE, b, c, o.ncols,
-      *static_cast<const float*>(alpha), *static_cast<const float*>(beta), stream_of(*o.ctx));
+  const cudaStream_t stream = stream_of(*o.ctx);
+  const cudaError_t e = with_scratch(*o.ctx, stream, mb200::sparse::kSpmmSchedBytes, [&](void* ws) {
+    const mb200::sparse::SpmmSched sc{static_cast<unsigned*>(ws),
+                                      reinterpret_cast<int*>(static_cast<char*>(ws) + 16),
+                                      mb200::sparse::kSpmmLongCap};
+    return mb200::sparse::launch_spmm_csr(
+        view_of(*o.a), opA != CUSPARSE_OPERATION_NON_TRANSPOSE, b, c, o.ncols,
+        *static_cast<const float*>(alpha), *static_cast<const float*>(beta), &sc, stream);
+  });
+  if (e == cudaErrorMemoryAllocation) return CUSPARSE_STATUS_ALLOC_FAILED;
   return e == cudaSuccess ? CUSPARSE_STATUS_SUCCESS : CUSPARSE_STATUS_EXECUTION_FAILED;
 }
 

@@ -288,6 +288,166 @@ __global__ void __launch_bounds__(kWarps * 32)
   }
 }
 
+// Row-major B and C in 16-byte vectors: the same sums (entry order, bit-identical),
+// scheduled for a power-law row-length distribution.
+// - Gathers: each lane copies its own 16-byte slice of the B row of entry
+//   t + kRing - 1 into a per-lane ring in shared memory with cp.async (L2 only)
+//   while it consumes entry t, so kRing - 1 gathers per lane are in flight without
+//   holding registers.  A lane reads only the slots it wrote (cp.async.wait_group
+//   orders its own copies), so no barrier is needed.  A bit per slot records
+//   entries whose column is out of range; they are skipped, as in spmm_rows.
+// - Lockstep: the 32 / G rows of a warp advance together up to the longest one, so
+//   the warp never splits (a split warp issues each row's instructions separately).
+// - Order: a first pass (spmm_find_long) lists the rows of more than kLongRow
+//   entries; warps take those first, then chunks of kRowsPerGrab rows from a
+//   counter, so the long sequential chains start at once and overlap the short
+//   rows instead of trailing at the end.  If the list overflows, every row is taken
+//   in the second phase instead.
+constexpr int kRing = 16;
+constexpr int kLongRow = 256;
+constexpr int kRowsPerGrab = 16;
+constexpr std::size_t kRingBytes = static_cast<std::size_t>(kRing) * kWarps * 32 * 16;
+
+__device__ __forceinline__ void cp_async16(unsigned dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_commit() {
+  asm volatile("cp.async.commit_group;\n" ::: "memory");
+}
+__device__ __forceinline__ void cp_wait_ring() {
+  asm volatile("cp.async.wait_group %0;\n" ::"n"(kRing - 1) : "memory");
+}
+
+__global__ void __launch_bounds__(256) spmm_find_long(const CsrView a, SpmmSched sc) {
+  for (std::int64_t r = blockIdx.x * static_cast<std::int64_t>(blockDim.x) + threadIdx.x;
+       r < a.rows; r += static_cast<std::int64_t>(gridDim.x) * blockDim.x) {
+    const int s = clamp_off(a.row_offsets[r], a.base, a.nnz);
+    const int e = clamp_off(a.row_offsets[r + 1], a.base, a.nnz);
+    if (e - s > kLongRow) {
+      const unsigned i = atomicAdd(sc.counters + 2, 1u);
+      if (i < sc.long_cap) sc.long_rows[i] = static_cast<int>(r);
+    }
+  }
+}
+
+template <int G>
+struct RingRows {
+  static constexpr int RPW = 32 / G;
+  static constexpr unsigned kSlotBytes = kWarps * 32 * 16;
+  const CsrView& a;
+  const DenseView& b;
+  const DenseView& c;
+  std::int64_t ncols;
+  float alpha, beta;
+  const float4* ring;  // this thread's slot 0
+  unsigned mine;       // its shared-memory address
+  int gl;
+
+  // Rows `row` of the warp's groups (-1: none); skip_long drops rows of more than
+  // kLongRow entries (they were taken in the first phase).
+  __device__ void run(std::int64_t row, bool skip_long) const {
+    int s = 0, len = 0;
+    bool own = row >= 0;
+    if (own) {
+      s = clamp_off(a.row_offsets[row], a.base, a.nnz);
+      const int e = clamp_off(a.row_offsets[row + 1], a.base, a.nnz);
+      len = e > s ? e - s : 0;
+      if (skip_long && len > kLongRow) {
+        own = false;
+        len = 0;
+      }
+    }
+    const int steps = static_cast<int>(__reduce_max_sync(kFull, static_cast<unsigned>(len)));
+    if (__all_sync(kFull, !own)) return;
+    const float* vals = static_cast<const float*>(a.values);
+    const int* cols = a.col_ind + s;
+    for (std::int64_t cb = 0; cb < ncols; cb += G * 4) {
+      const std::int64_t col = cb + static_cast<std::int64_t>(gl) * 4;
+      const bool live = own && col < ncols;
+      const float* bcol = b.m + col;
+      unsigned valid = 0;
+      int kpre = len > 0 ? __ldg(cols) - a.base : -1;
+      auto issue = [&](int q) {
+        const int k = kpre;
+        kpre = q + 1 < len ? __ldg(cols + q + 1) - a.base : -1;
+        const unsigned slot = static_cast<unsigned>(q) & (kRing - 1);
+        if (q < len && live) {
+          if (static_cast<unsigned>(k) < static_cast<unsigned long long>(a.cols)) {
+            cp_async16(mine + slot * kSlotBytes, bcol + static_cast<std::int64_t>(k) * b.ld);
+            valid |= 1u << slot;
+          } else {
+            valid &= ~(1u << slot);
+          }
+        }
+        cp_commit();  // one group per entry (empty past the row's end)
+      };
+      float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+      for (int q = 0; q < kRing - 1; ++q) issue(q);
+      float vpre = len > 0 ? __ldg(vals + s) : 0.0f;
+      for (int j = 0; j < steps; ++j) {
+        issue(j + kRing - 1);
+        const float av = vpre;
+        vpre = j + 1 < len ? __ldg(vals + s + j + 1) : 0.0f;
+        cp_wait_ring();  // entry j's copy has landed
+        const unsigned slot = static_cast<unsigned>(j) & (kRing - 1);
+        if (j < len && live && ((valid >> slot) & 1u)) {
+          const float4 q = ring[slot * (kWarps * 32)];
+          acc.x = fmaf(av, q.x, acc.x);
+          acc.y = fmaf(av, q.y, acc.y);
+          acc.z = fmaf(av, q.z, acc.z);
+          acc.w = fmaf(av, q.w, acc.w);
+        }
+      }
+      if (live) {
+        float* out = c.m + row * c.ld + col;
+        const float v[4] = {acc.x, acc.y, acc.z, acc.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float prev = (beta == 0.0f) ? 0.0f : beta * out[i];
+          out[i] = fmaf(alpha, v[i], prev);
+        }
+      }
+    }
+  }
+};
+
+template <int G>
+__global__ void __launch_bounds__(kWarps * 32)
+    spmm_rows_ring(const CsrView a, const DenseView b, const DenseView c, std::int64_t ncols,
+                   float alpha, float beta, SpmmSched sc) {
+  extern __shared__ float4 ring[];  // [kRing][kWarps * 32]
+  constexpr int RPW = RingRows<G>::RPW;
+  const int lane = threadIdx.x & 31;
+  const int g = lane / G;
+  const RingRows<G> rr{a, b, c, ncols, alpha, beta, ring + threadIdx.x,
+                       static_cast<unsigned>(__cvta_generic_to_shared(ring + threadIdx.x)),
+                       lane % G};
+  const unsigned nlong = sc.counters[2];
+  const bool listed = nlong <= sc.long_cap;
+  if (listed) {
+    for (;;) {
+      unsigned i0 = 0;
+      if (lane == 0) i0 = atomicAdd(sc.counters, static_cast<unsigned>(RPW));
+      i0 = __shfl_sync(kFull, i0, 0);
+      if (i0 >= nlong) break;
+      const unsigned i = i0 + g;
+      rr.run(i < nlong ? sc.long_rows[i] : -1, false);
+    }
+  }
+  for (;;) {
+    unsigned ch = 0;
+    if (lane == 0) ch = atomicAdd(sc.counters + 1, 1u);
+    ch = __shfl_sync(kFull, ch, 0);
+    const std::int64_t r0 = static_cast<std::int64_t>(ch) * kRowsPerGrab;
+    if (r0 >= a.rows) break;
+    for (std::int64_t q = r0; q < r0 + kRowsPerGrab && q < a.rows; q += RPW) {
+      const std::int64_t row = q + g;
+      rr.run(row < a.rows && row < r0 + kRowsPerGrab ? row : -1, listed);
+    }
+  }
+  asm volatile("cp.async.wait_all;\n" ::: "memory");
+}
+
 // C = beta == 0 ? 0 : beta * C over out_rows x ncols.
 __global__ void __launch_bounds__(256)
     spmm_scale(const DenseView c, std::int64_t out_rows, std::int64_t ncols, float beta) {
@@ -356,12 +516,38 @@ cudaError_t spmm_rows_group(const CsrView& a, const DenseView& b, const DenseVie
   return cudaGetLastError();
 }
 
+cudaError_t spmm_ring_launch(const CsrView& a, const DenseView& b, const DenseView& c,
+                             std::int64_t ncols, float alpha, float beta, const SpmmSched& sc,
+                             cudaStream_t st) {
+  const std::int64_t lanes = (ncols + 3) / 4;
+  const int G = lanes > 16 ? 32 : (lanes > 8 ? 16 : (lanes > 4 ? 8 : 4));
+  cudaError_t e = cudaMemsetAsync(sc.counters, 0, 3 * sizeof(unsigned), st);
+  if (e != cudaSuccess) return e;
+  spmm_find_long<<<grid_for(a.rows, 256, 8), 256, 0, st>>>(a, sc);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  const unsigned grid = grid_for((a.rows + 32 / G - 1) / (32 / G), kWarps, 3);
+  auto go = [&](auto kern) {
+    cudaError_t r = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(kRingBytes));
+    if (r != cudaSuccess) return r;
+    kern<<<grid, kWarps * 32, kRingBytes, st>>>(a, b, c, ncols, alpha, beta, sc);
+    return cudaGetLastError();
+  };
+  switch (G) {
+    case 4: return go(spmm_rows_ring<4>);
+    case 8: return go(spmm_rows_ring<8>);
+    case 16: return go(spmm_rows_ring<16>);
+    default: return go(spmm_rows_ring<32>);
+  }
+}
+
 template <bool BROW, bool CROW>
 cudaError_t spmm_rows_launch(const CsrView& a, const DenseView& b, const DenseView& c,
                              std::int64_t ncols, float alpha, float beta, bool vec4,
-                             cudaStream_t st) {
+                             const SpmmSched* sc, cudaStream_t st) {
   if constexpr (BROW && CROW) {
-    if (vec4) return spmm_rows_group<4, true, true>(a, b, c, ncols, alpha, beta, st);
+    if (vec4 && sc != nullptr) return spmm_ring_launch(a, b, c, ncols, alpha, beta, *sc, st);
   }
   return spmm_rows_group<1, BROW, CROW>(a, b, c, ncols, alpha, beta, st);
 }
@@ -372,7 +558,7 @@ bool row_contiguous(const DenseView& d) { return d.col_major == d.trans; }
 
 cudaError_t launch_spmm_csr(const CsrView& a, bool trans_a, const DenseView& b,
                             const DenseView& c, std::int64_t ncols, float alpha, float beta,
-                            cudaStream_t stream) noexcept {
+                            const SpmmSched* sched, cudaStream_t stream) noexcept {
   const std::int64_t out_rows = trans_a ? a.cols : a.rows;
   if (out_rows <= 0 || ncols <= 0) return cudaSuccess;
   const bool brow = row_contiguous(b);
@@ -386,10 +572,13 @@ cudaError_t launch_spmm_csr(const CsrView& a, bool trans_a, const DenseView& b,
   if (!trans_a) {
     const bool vec4 = brow && crow && ncols % 4 == 0 && b.ld % 4 == 0 && c.ld % 4 == 0 &&
                       aligned_to(b.m, 16) && aligned_to(c.m, 16);
-    if (brow && crow) return spmm_rows_launch<true, true>(a, bb, cc, ncols, alpha, beta, vec4, stream);
-    if (brow) return spmm_rows_launch<true, false>(a, bb, cc, ncols, alpha, beta, false, stream);
-    if (crow) return spmm_rows_launch<false, true>(a, bb, cc, ncols, alpha, beta, false, stream);
-    return spmm_rows_launch<false, false>(a, bb, cc, ncols, alpha, beta, false, stream);
+    if (brow && crow)
+      return spmm_rows_launch<true, true>(a, bb, cc, ncols, alpha, beta, vec4, sched, stream);
+    if (brow)
+      return spmm_rows_launch<true, false>(a, bb, cc, ncols, alpha, beta, false, nullptr, stream);
+    if (crow)
+      return spmm_rows_launch<false, true>(a, bb, cc, ncols, alpha, beta, false, nullptr, stream);
+    return spmm_rows_launch<false, false>(a, bb, cc, ncols, alpha, beta, false, nullptr, stream);
   }
   spmm_scale<<<grid_for(out_rows * ncols, 256, 8), 256, 0, stream>>>(cc, out_rows, ncols, beta);
   cudaError_t e = cudaGetLastError();

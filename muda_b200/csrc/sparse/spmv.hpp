@@ -3,6 +3,7 @@
 
 #include <cuda_runtime_api.h>
 
+#include <cstddef>
 #include <cstdint>
 
 namespace mb200::sparse {
@@ -46,15 +47,28 @@ struct DenseView {
   bool trans;
 };
 
+// Device scratch of the row scheduler of the row-major SpMM: counters[3] (zeroed
+// by the launch: first-phase position, row-chunk position, long-row count) and
+// long_rows[long_cap].  No other call may use it while the launch runs.
+struct SpmmSched {
+  unsigned* counters;
+  int* long_rows;
+  unsigned long_cap;
+};
+constexpr unsigned kSpmmLongCap = 65536;
+constexpr std::size_t kSpmmSchedBytes = 16 + std::size_t{kSpmmLongCap} * 4;
+
 // C = alpha * op(A) * op(B) + beta * C, fp32, C with out_rows x ncols entries
 // (out_rows = a.rows, or a.cols when trans_a).  Without trans_a every output is
 // sum_k fma(values[k], B(col_k, c), sum) over the row's entries in order, then
 // fma(alpha, sum, beta == 0 ? 0 : beta * C): the reference's own per-output
 // arithmetic.  With trans_a, C is scaled by beta and the products are added
 // atomically (order unspecified).
+// sched (may be null: a static row order) lets row-major B and C in 16-byte vectors
+// take the scheduled kernel.
 cudaError_t launch_spmm_csr(const CsrView& a, bool trans_a, const DenseView& b,
                             const DenseView& c, std::int64_t ncols, float alpha, float beta,
-                            cudaStream_t stream) noexcept;
+                            const SpmmSched* sched, cudaStream_t stream) noexcept;
 
 // Threads cooperating on one row for a matrix with this shape (for tests/benchmarks).
 int spmv_group_width(std::int64_t rows, std::int64_t nnz) noexcept;

@@ -231,9 +231,11 @@ def test_gpu_spmv_f16(cuda, built, trans, kind):
     a.close()
 
 
-# (rows, cols, ncols): odd sizes, one that fills several 32-column chunks, and a
-# float4-eligible one (ncols and ld multiples of 4)
-SPMM_SHAPES = [(300, 200, 7), (257, 300, 130), (500, 400, 64), (600, 3000, 64)]
+# (rows, cols, ncols): odd sizes, one that fills several 32-column chunks, and
+# float4-eligible ones (ncols and ld multiples of 4) for each group width of the
+# shared-memory ring kernel (4, 8, 16 and 32 lanes per row)
+SPMM_SHAPES = [(300, 200, 7), (257, 300, 130), (500, 400, 64), (600, 3000, 64), (300, 200, 12),
+               (260, 500, 32), (257, 400, 128)]
 
 
 @pytest.mark.gpu

@@ -343,6 +343,69 @@ struct RingRows {
   unsigned mine;       // its shared-memory address
   int gl;
 
+  // G >= 16 lanes: the row's column indices and values come G at a time, one per
+  // lane (coalesced), and are handed out by shuffles; the lookahead of kRing - 1
+  // entries stays within the current and next chunk, the loop is unrolled by G so
+  // every ring slot is a constant, and B offsets are 32-bit bytes (the launch checks
+  // cols * ld * 4 < 2^32).
+  __device__ void chunked(int s, int len, int steps, bool own, std::int64_t row) const {
+    static_assert(G % kRing == 0 && G > kRing - 1, "two chunks cover the lookahead");
+    const float* vals = static_cast<const float*>(a.values) + s;
+    const int* cols = a.col_ind + s;
+    const unsigned ldb = static_cast<unsigned>(b.ld) * 4u;
+    const unsigned ncol = static_cast<unsigned>(a.cols);
+    for (std::int64_t cb = 0; cb < ncols; cb += G * 4) {
+      const std::int64_t col = cb + static_cast<std::int64_t>(gl) * 4;
+      const bool live = own && col < ncols;
+      const char* bcol = reinterpret_cast<const char*>(b.m + col);
+      auto ldcol = [&](int i) { return i < len ? __ldg(cols + i) - a.base : -1; };
+      int col_c = ldcol(gl), col_n = ldcol(G + gl);
+      float val_c = gl < len ? __ldg(vals + gl) : 0.0f;
+      auto issue = [&](int k, unsigned slot, bool on) {
+        if (on && live && static_cast<unsigned>(k) < ncol)
+          cp_async16(mine + slot * kSlotBytes, bcol + static_cast<unsigned>(k) * ldb);
+        cp_commit();  // one group per entry (empty when nothing was copied)
+      };
+#pragma unroll
+      for (int u = 0; u < kRing - 1; ++u)
+        issue(__shfl_sync(kFull, col_c, u, G), static_cast<unsigned>(u), u < len);
+      float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+      for (int j0 = 0; j0 < steps; j0 += G) {
+#pragma unroll
+        for (int u = 0; u < G; ++u) {
+          if (j0 + u >= steps) break;  // warp-uniform
+          constexpr int kAhead = kRing - 1;
+          const int q = u + kAhead;  // entry j0 + q is issued now
+          const int kq = q < G ? __shfl_sync(kFull, col_c, q % G, G)
+                               : __shfl_sync(kFull, col_n, (q - G) % G, G);
+          issue(kq, static_cast<unsigned>(q % kRing), j0 + q < len);
+          const int ku = __shfl_sync(kFull, col_c, u, G);
+          const float au = __shfl_sync(kFull, val_c, u, G);
+          cp_wait_ring();  // entry j0 + u's copy has landed
+          if (j0 + u < len && live && static_cast<unsigned>(ku) < ncol) {
+            const float4 v = ring[(u % kRing) * (kWarps * 32)];
+            acc.x = fmaf(au, v.x, acc.x);
+            acc.y = fmaf(au, v.y, acc.y);
+            acc.z = fmaf(au, v.z, acc.z);
+            acc.w = fmaf(au, v.w, acc.w);
+          }
+        }
+        col_c = col_n;
+        col_n = ldcol(j0 + 2 * G + gl);
+        val_c = j0 + G + gl < len ? __ldg(vals + j0 + G + gl) : 0.0f;
+      }
+      if (live) {
+        float* out = c.m + row * c.ld + col;
+        const float v[4] = {acc.x, acc.y, acc.z, acc.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float prev = (beta == 0.0f) ? 0.0f : beta * out[i];
+          out[i] = fmaf(alpha, v[i], prev);
+        }
+      }
+    }
+  }
+
   // Rows `row` of the warp's groups (-1: none); skip_long drops rows of more than
   // kLongRow entries (they were taken in the first phase).
   __device__ void run(std::int64_t row, bool skip_long) const {
@@ -359,6 +422,10 @@ struct RingRows {
     }
     const int steps = static_cast<int>(__reduce_max_sync(kFull, static_cast<unsigned>(len)));
     if (__all_sync(kFull, !own)) return;
+    if constexpr (G >= 16) {
+      chunked(s, len, steps, own, row);
+      return;
+    }
     const float* vals = static_cast<const float*>(a.values);
     const int* cols = a.col_ind + s;
     for (std::int64_t cb = 0; cb < ncols; cb += G * 4) {
@@ -521,6 +588,9 @@ cudaError_t spmm_ring_launch(const CsrView& a, const DenseView& b, const DenseVi
                              cudaStream_t st) {
   const std::int64_t lanes = (ncols + 3) / 4;
   const int G = lanes > 16 ? 32 : (lanes > 8 ? 16 : (lanes > 4 ? 8 : 4));
+  // 32-bit byte offsets into B on the chunked (G >= 16) path
+  if (G >= 16 && static_cast<double>(a.cols) * static_cast<double>(b.ld) * 4.0 >= 4294967296.0)
+    return spmm_rows_group<4, true, true>(a, b, c, ncols, alpha, beta, st);
   cudaError_t e = cudaMemsetAsync(sc.counters, 0, 3 * sizeof(unsigned), st);
   if (e != cudaSuccess) return e;
   spmm_find_long<<<grid_for(a.rows, 256, 8), 256, 0, st>>>(a, sc);

@@ -1131,9 +1131,11 @@ def run_reference(args) -> None:
 
 def run_spmv_dist(args) -> None:
     """configs[2] SpMV across the ranks of torchrun (strong scaling: the 4M x 4M matrix
-    is fixed, its rows split into nnz-balanced blocks).  Each step all-gathers x
-    (NCCL, into local HBM) and runs the local cusparseSpMV; reported are the step
-    time (max over ranks) with and without the exchange."""
+    is fixed, its rows split into nnz-balanced blocks).  Each step gathers x into
+    local HBM and runs the local cusparseSpMV.  Two exchanges are timed on the same
+    blocks: the NVLink peer-memory pull of libmuda_peer (the value) and NCCL's
+    all_gather_into_tensor (reported beside it); both must give the same y, bit for
+    bit.  Reported are the step time (max over ranks) with and without the exchange."""
     import torch
     import torch.distributed as dist
 
@@ -1150,10 +1152,12 @@ def run_spmv_dist(args) -> None:
     rows = (1 << 22) // args.scale
     mtx = synth.powerlaw_csr(torch, rows, rows, seed=7)
     nnz = mtx["nnz"]
-    d = DistSpMV.from_full(torch, dist if world > 1 else None, group, mtx["row_offsets"],
-                           mtx["col_ind"], mtx["values"], rows)
+    dd = dist if world > 1 else None
+    arms = {ex: DistSpMV.from_full(torch, dd, group, mtx["row_offsets"], mtx["col_ind"],
+                                   mtx["values"], rows, exchange=ex) for ex in ("peer", "nccl")}
+    d = arms["peer"]
     x_local = d.x_slice(mtx["x"])
-    y_local = torch.zeros(max(d.rows, 1), dtype=torch.float32, device="cuda")
+    ys = {ex: torch.zeros(max(d.rows, 1), dtype=torch.float32, device="cuda") for ex in arms}
     del mtx
     torch.cuda.empty_cache()
     flush = torch.empty(64 << 20, dtype=torch.float32, device="cuda")  # 256 MB > L2
@@ -1164,31 +1168,39 @@ def run_spmv_dist(args) -> None:
             dist.barrier(device_ids=[local])
         torch.cuda.synchronize()
 
-    full_ms, local_ms, gather_ms = [], [], []
+    times = {ex: ([], [], []) for ex in arms}
     for it in range(args.warmup + args.steps):
-        flush.fill_(float(it))
-        barrier()
-        ev[0].record()
-        d.gather_x(x_local)
-        ev[1].record()
-        d.local(1.0, 0.0, y_local)
-        ev[2].record()
-        torch.cuda.synchronize()
-        if it >= args.warmup:
-            gather_ms.append(ev[0].elapsed_time(ev[1]))
-            local_ms.append(ev[1].elapsed_time(ev[2]))
-            full_ms.append(ev[0].elapsed_time(ev[2]))
-    stats = torch.tensor([float(np.mean(full_ms)), float(np.mean(local_ms)),
-                          float(np.mean(gather_ms))], device="cuda")
+        for ex, arm in arms.items():
+            flush.fill_(float(it))
+            barrier()
+            ev[0].record()
+            arm.gather_x(x_local)
+            ev[1].record()
+            arm.local(1.0, 0.0, ys[ex])
+            ev[2].record()
+            torch.cuda.synchronize()
+            if it >= args.warmup:
+                full_ms, local_ms, gather_ms = times[ex]
+                gather_ms.append(ev[0].elapsed_time(ev[1]))
+                local_ms.append(ev[1].elapsed_time(ev[2]))
+                full_ms.append(ev[0].elapsed_time(ev[2]))
+    barrier()
+    status = d._peer.take_status()
+    same = bool(torch.equal(ys["peer"], ys["nccl"])) and status == 0
+    check = torch.tensor([0 if same else 1], dtype=torch.int32, device="cuda")
+    stats = torch.tensor([float(np.mean(v)) for ex in ("peer", "nccl") for v in times[ex]],
+                         device="cuda")
     if world > 1:
         dist.all_reduce(stats, op=dist.ReduceOp.MAX)
+        dist.all_reduce(check, op=dist.ReduceOp.MAX)
     shares = torch.tensor([d.nnz], dtype=torch.int64, device="cuda")
     if world > 1:
         parts = [torch.zeros_like(shares) for _ in range(world)]
         dist.all_gather(parts, shares)
         shares = torch.cat(parts)
-    full, loc, gat = (float(v) for v in stats.cpu())
+    full, loc, gat, n_full, n_loc, n_gat = (float(v) for v in stats.cpu())
     alg_bytes = nnz * 8 + (rows + 1) * 4 + rows * 4 + rows * 4
+    ok = int(check.item()) == 0
     if rank == 0:
         nz = shares.cpu().numpy()
         print(json.dumps({
@@ -1199,13 +1211,20 @@ def run_spmv_dist(args) -> None:
             "dtype": "f32/i32", "data": "synthetic power-law CSR (configs[2])",
             "config": {"workload": f"{rows} x {rows}, nnz {nnz}, rows split into "
                                    f"{world} nnz-balanced blocks", "l2": "256 MB flush "
-                                   "before each step"},
+                                   "before each step",
+                       "exchange": "peer-memory pull over NVLink (libmuda_peer)"},
             "kernel_only": {"ms": loc, "GB/s": alg_bytes / (loc * 1e-3) / 1e9},
-            "allgather_ms": gat, "nnz_per_rank": [int(v) for v in nz],
+            "exchange_ms": gat,
+            "nccl_all_gather": {"ms_per_step": n_full, "exchange_ms": n_gat,
+                                "GB/s": alg_bytes / (n_full * 1e-3) / 1e9},
+            "y_identical_to_nccl": ok, "nnz_per_rank": [int(v) for v in nz],
             "imbalance": float(nz.max() / max(float(nz.mean()), 1.0))}), flush=True)
-    d.close()
+    for arm in arms.values():
+        arm.close()
     if world > 1:
         dist.destroy_process_group()
+    if not ok:
+        raise SystemExit("peer exchange result differs from the NCCL exchange")
 
 
 SHARDED = ("fft", "gemm_bf16", "conv_bf16", "conv_f32", "softmax")

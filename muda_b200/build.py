@@ -41,6 +41,7 @@ LIBS: dict[str, list[str]] = {
     "cufft": ["fft/cufft_api.cpp", "fft/stockham_kernels.cu", "fft/dft_kernels.cu",
               "fft/bluestein_kernels.cu", "fft/mixed_kernels.cu",
               "fft/fft_static.cu", "fft/real_kernels.cu"],
+    "peer": ["peer/peer_exchange.cu"],
     "cublas": ["blas/cublas_api.cpp", "blas/gemm_simt_kernels.cu", "blas/gemm_tc_kernels.cu",
                "blas/tf32_split.cu", "blas/level12_kernels.cu"],
 }

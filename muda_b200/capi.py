@@ -302,12 +302,39 @@ def cublas() -> C.CDLL:
     return _declare(_load("cublas"), CUBLAS_PROTOS)
 
 
+# ---------------------------------------------------------- peer exchange --
+MB200_PEER_SUCCESS = 0
+MB200_PEER_INVALID_VALUE = 1
+MB200_PEER_CUDA_ERROR = 2
+MB200_PEER_HANDLE_BYTES = 64
+MB200_PEER_MAX_RANKS = 32
+MB200_PEER_STATUS_WORD = 48
+MB200_PEER_HEADER_BYTES = 256
+
+PEER_PROTOS = {
+    "mb200PeerAlloc": ([C.c_size_t, P(C.c_void_p), C.c_void_p], C.c_int),
+    "mb200PeerOpen": ([C.c_void_p, P(C.c_void_p)], C.c_int),
+    "mb200PeerClose": ([C.c_void_p], C.c_int),
+    "mb200PeerFree": ([C.c_void_p], C.c_int),
+    "mb200PeerBuffer": ([C.c_void_p, C.c_size_t, C.c_uint], C.c_void_p),
+    "mb200PeerAllgather": ([P(C.c_void_p), C.c_int, C.c_int, C.c_size_t, C.c_size_t, C.c_uint,
+                            C.c_void_p, C.c_void_p], C.c_int),
+    "mb200PeerTakeStatus": ([C.c_void_p, P(C.c_uint)], C.c_int),
+}
+
+
+@lru_cache(maxsize=None)
+def peer() -> C.CDLL:
+    return _declare(_load("peer"), PEER_PROTOS)
+
+
 ALL_PROTOS: dict[str, dict[str, tuple[list, object]]] = {
     "curand": CURAND_PROTOS,
     "cudnn": CUDNN_PROTOS,
     "cusparse": CUSPARSE_PROTOS,
     "cufft": CUFFT_PROTOS,
     "cublas": CUBLAS_PROTOS,
+    "peer": PEER_PROTOS,
 }
 
 LOADERS = {
@@ -316,4 +343,5 @@ LOADERS = {
     "cusparse": cusparse,
     "cufft": cufft,
     "cublas": cublas,
+    "peer": peer,
 }

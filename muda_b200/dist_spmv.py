@@ -10,10 +10,13 @@ vector x, so this module shards the matrix and exchanges only x:
   row block (row offsets rebased to its first entry, global column indices) and
   the matching block of y;
 - x is held in equal contiguous blocks of ceil(cols / world) entries; every call
-  all-gathers the blocks into a full copy of x in this GPU's own memory (one
-  all_gather_into_tensor, NCCL over NVLink), then runs the local product through
-  the library's C ABI (cusparseSpMV) on the current stream, so no kernel ever
-  reads another GPU's memory.
+  gathers the blocks into a full copy of x in this GPU's own memory, then runs the
+  local product through the library's C ABI (cusparseSpMV) on the current stream.
+  The gather is either one NCCL all_gather_into_tensor (``exchange="nccl"``) or
+  the peer-memory pull of libmuda_peer (``exchange="peer"``, mb200_peer.h): every
+  rank announces its block with a flag store into the other ranks' memory and pulls
+  theirs over NVLink with 16-byte loads, one kernel and no collective per call.
+  Only that pull kernel reads another GPU's memory; the product reads local x.
 
 The local product is pluggable (``local_spmv``) only so that the partition and
 exchange logic can be tested on CPU ranks with the gloo backend; the default is
@@ -55,6 +58,81 @@ def x_block(cols: int, world: int) -> int:
     return (cols + world - 1) // world
 
 
+def _peer_check(status: int, what: str) -> None:
+    if status != 0:
+        raise RuntimeError(f"{what} failed with status {status}")
+
+
+class PeerExchange:
+    """The x exchange over NVLink peer memory (libmuda_peer, mb200_peer.h).
+
+    Each rank allocates an exchange buffer (flags + two x buffers of world * block
+    floats), shares its CUDA IPC handle through the process group and maps every
+    peer's buffer.  ``gather(x_local)`` runs one epoch on the current stream and
+    returns the device address of the full x it produced (valid until the epoch
+    after next reuses the buffer)."""
+
+    def __init__(self, torch, dist, group, block: int):
+        from muda_b200 import capi
+        self.torch, self.dist, self.group = torch, dist, group
+        self.L = capi.peer()
+        self.world = dist.get_world_size(group) if dist is not None else 1
+        self.rank = dist.get_rank(group) if dist is not None else 0
+        self.block, self.count = block, block * self.world
+        self.base = C.c_void_p()
+        handle = (C.c_ubyte * capi.MB200_PEER_HANDLE_BYTES)()
+        _peer_check(self.L.mb200PeerAlloc(self.count, C.byref(self.base), handle), "mb200PeerAlloc")
+        self.bases = (C.c_void_p * self.world)()
+        self._opened: list[C.c_void_p] = []
+        self.bases[self.rank] = self.base
+        if self.world > 1:
+            mine = torch.tensor(list(bytes(handle)), dtype=torch.uint8, device="cuda")
+            parts = [torch.empty_like(mine) for _ in range(self.world)]
+            dist.all_gather(parts, mine, group=group)
+            for p in range(self.world):
+                if p == self.rank:
+                    continue
+                h = (C.c_ubyte * capi.MB200_PEER_HANDLE_BYTES).from_buffer_copy(
+                    parts[p].cpu().numpy().tobytes())
+                pb = C.c_void_p()
+                _peer_check(self.L.mb200PeerOpen(h, C.byref(pb)), "mb200PeerOpen")
+                self.bases[p] = pb
+                self._opened.append(pb)
+            dist.barrier(group=group)  # every buffer is zeroed and mapped before use
+        self.epoch = 0
+
+    def gather(self, x_local) -> int:
+        if x_local.numel() != self.block:
+            raise ValueError(f"x block must hold {self.block} entries, got {x_local.numel()}")
+        self.epoch = (self.epoch + 1) & 0xFFFFFFFF or 1
+        stream = self.torch.cuda.current_stream().cuda_stream
+        _peer_check(self.L.mb200PeerAllgather(self.bases, self.world, self.rank, self.count,
+                                              self.block, self.epoch,
+                                              C.c_void_p(x_local.data_ptr()), C.c_void_p(stream)),
+                    "mb200PeerAllgather")
+        return int(self.L.mb200PeerBuffer(self.base, self.count, self.epoch))
+
+    def take_status(self) -> int:
+        """Bit p set: a wait for rank p ran out since the last call (synchronises)."""
+        st = C.c_uint(0)
+        _peer_check(self.L.mb200PeerTakeStatus(self.base, C.byref(st)), "mb200PeerTakeStatus")
+        return st.value
+
+    def close(self) -> None:
+        if not self.base:
+            return
+        self.torch.cuda.synchronize()
+        if self.world > 1:
+            self.dist.barrier(group=self.group)  # nobody still reads a peer buffer
+        for pb in self._opened:
+            self.L.mb200PeerClose(pb)
+        self._opened.clear()
+        if self.world > 1:
+            self.dist.barrier(group=self.group)  # every mapping of this buffer is closed
+        self.L.mb200PeerFree(self.base)
+        self.base = C.c_void_p()
+
+
 class _CudaLocal:
     """cusparseSpMV on the local row block through the C ABI (handle and
     descriptors created once per vector buffer pair)."""
@@ -76,11 +154,14 @@ class _CudaLocal:
         self._vecs: dict[tuple[int, int], tuple[C.c_void_p, C.c_void_p]] = {}
 
     def __call__(self, x_full, y_local, alpha: float, beta: float) -> None:
-        key = (x_full.data_ptr(), y_local.data_ptr())
+        self.at(x_full.data_ptr(), y_local, alpha, beta)
+
+    def at(self, x_ptr: int, y_local, alpha: float, beta: float) -> None:
+        """The product with x at device address x_ptr (cols floats)."""
+        key = (x_ptr, y_local.data_ptr())
         if key not in self._vecs:
             vx, vy = C.c_void_p(), C.c_void_p()
-            assert self.L.cusparseCreateDnVec(C.byref(vx), self.cols,
-                                              C.c_void_p(x_full.data_ptr()), 0) == 0
+            assert self.L.cusparseCreateDnVec(C.byref(vx), self.cols, C.c_void_p(x_ptr), 0) == 0
             assert self.L.cusparseCreateDnVec(C.byref(vy), self.rows,
                                               C.c_void_p(y_local.data_ptr()), 0) == 0
             self._vecs[key] = (vx, vy)
@@ -110,12 +191,14 @@ class DistSpMV:
 
     Build it with :meth:`from_full` (every rank passes the same full matrix and
     keeps its block) or directly from the local block.  ``spmv(alpha, x_local,
-    beta, y_local)`` all-gathers x and computes this rank's rows of y.  With
-    ``dist=None`` the object is a single rank (no process group, x is copied)."""
+    beta, y_local)`` gathers x and computes this rank's rows of y.  With
+    ``dist=None`` the object is a single rank (no process group, x is copied).
+    ``exchange`` selects the gather: "nccl" (all_gather_into_tensor, or the gloo
+    all_gather on CPU ranks) or "peer" (NVLink peer-memory pull, CUDA path only)."""
 
     def __init__(self, torch, dist, group, *, offsets, col_ind, values, row_begin: int,
                  row_end: int, cols: int, base: int = 0,
-                 local_spmv: Callable | None = None, device=None):
+                 local_spmv: Callable | None = None, device=None, exchange: str = "nccl"):
         self.torch, self.dist, self.group = torch, dist, group
         self.world = dist.get_world_size(group) if dist is not None else 1
         self.rank = dist.get_rank(group) if dist is not None else 0
@@ -125,7 +208,15 @@ class DistSpMV:
         self.nnz = int(offsets[-1].item() - offsets[0].item()) if self.rows > 0 else 0
         self.xb = x_block(cols, self.world)
         dev = device if device is not None else offsets.device
-        self.x_full = torch.zeros(self.xb * self.world, dtype=torch.float32, device=dev)
+        if exchange not in ("nccl", "peer"):
+            raise ValueError(f"unknown exchange {exchange!r}")
+        if exchange == "peer" and local_spmv is not None:
+            raise ValueError("the peer exchange runs on the CUDA path only")
+        self.exchange = exchange
+        self._peer = PeerExchange(torch, dist, group, self.xb) if exchange == "peer" else None
+        self._x_ptr = 0
+        self.x_full = torch.zeros(self.xb * self.world if self._peer is None else 1,
+                                  dtype=torch.float32, device=dev)
         if local_spmv is None:
             self._local = _CudaLocal(torch, offsets, col_ind, values, self.rows, cols,
                                      self.nnz, base) if self.rows > 0 else None
@@ -135,7 +226,7 @@ class DistSpMV:
 
     @classmethod
     def from_full(cls, torch, dist, group, row_offsets, col_ind, values, cols: int, *,
-                  base: int = 0, local_spmv: Callable | None = None):
+                  base: int = 0, local_spmv: Callable | None = None, exchange: str = "nccl"):
         """Slices this rank's nnz-balanced row block out of the full CSR matrix (the
         same on every rank); the block's offsets are rebased so its first entry is
         entry 0 (plus the index base, which offsets and columns keep)."""
@@ -151,7 +242,7 @@ class DistSpMV:
         vals_l = values[e0:e1].contiguous()
         obj = cls(torch, dist, group, offsets=offs, col_ind=cols_l, values=vals_l, row_begin=r0,
                   row_end=r1, cols=cols, base=base, local_spmv=local_spmv,
-                  device=row_offsets.device)
+                  device=row_offsets.device, exchange=exchange)
         obj.bounds = bounds
         return obj
 
@@ -168,6 +259,9 @@ class DistSpMV:
         """x_full <- concatenation of every rank's x block (the exchange step)."""
         if x_local.numel() != self.xb:
             raise ValueError(f"x block must hold {self.xb} entries, got {x_local.numel()}")
+        if self._peer is not None:
+            self._x_ptr = self._peer.gather(x_local)
+            return
         if self.world == 1:
             self.x_full.copy_(x_local)
             return
@@ -183,6 +277,11 @@ class DistSpMV:
             return
         if y_local.numel() < self.rows:
             raise ValueError("y block is shorter than this rank's row block")
+        if self._peer is not None:
+            if not self._x_ptr:
+                raise RuntimeError("gather_x must run before local with the peer exchange")
+            self._local.at(self._x_ptr, y_local, alpha, beta)
+            return
         self._local(self.x_full[:self.cols], y_local, alpha, beta)
 
     def spmv(self, alpha: float, x_local, beta: float, y_local) -> None:
@@ -193,3 +292,6 @@ class DistSpMV:
         if isinstance(self._local, _CudaLocal):
             self._local.close()
         self._local = None
+        if self._peer is not None:
+            self._peer.close()
+            self._peer = None

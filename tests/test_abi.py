@@ -19,6 +19,7 @@ HEADER_LIB = {
     "cusparse.h": "cusparse",
     "cufft.h": "cufft",
     "cublas_v2.h": "cublas",
+    "mb200_peer.h": "peer",
 }
 
 

@@ -2,9 +2,11 @@
 //
 // Each rank's exchange buffer (header + two x buffers) is mapped into every other
 // rank's address space with CUDA IPC.  One kernel per epoch and rank:
-//   1. announce: st.release.sys of the epoch into word `rank` of every peer's header
-//      (the rank's own block was copied into its buffer earlier on the stream);
-//   2. pull: CTAs take (peer, 16 KB chunk) items; thread 0 waits for the peer's
+//   1. own block: every CTA copies its share of x_local into the rank's epoch buffer
+//      and counts itself done in header word kArriveWord; the CTA that completes the
+//      count (no CTA waits for another) resets it and announces: st.release.sys of
+//      the epoch into word `rank` of every peer's header;
+//   2. pull: CTAs take (peer, 32 KB chunk) items; thread 0 waits for the peer's
 //      announcement with ld.acquire.sys (bounded by %globaltimer, about one second),
 //      then the CTA copies the chunk from the peer's buffer with 16-byte loads over
 //      NVLink into the same offsets of this rank's buffer.
@@ -26,17 +28,19 @@ namespace {
 
 constexpr std::size_t kHeaderBytes = 256;
 constexpr int kThreads = 256;
-constexpr int kVecPerThread = 4;
+constexpr int kVecPerThread = 8;
+constexpr int kArriveWord = MB200_PEER_STATUS_WORD + 1;  // CTAs done with the own block
 constexpr std::size_t kChunkFloats = static_cast<std::size_t>(kThreads) * kVecPerThread * 4;
 constexpr unsigned long long kWaitNs = 1000000000ull;  // about one second per peer
 
 static_assert(MB200_PEER_STATUS_WORD >= MB200_PEER_MAX_RANKS &&
-                  (MB200_PEER_STATUS_WORD + 1) * 4 <= kHeaderBytes,
+                  (kArriveWord + 1) * 4 <= static_cast<int>(kHeaderBytes),
               "header layout");
 static_assert(sizeof(cudaIpcMemHandle_t) == MB200_PEER_HANDLE_BYTES, "IPC handle size");
 
 struct PullArgs {
   void* bases[MB200_PEER_MAX_RANKS];
+  const float* x_local;
   int world, rank;
   unsigned epoch;
   unsigned long long count, block;
@@ -84,18 +88,61 @@ __device__ bool wait_announced(unsigned* own_header, int p, unsigned epoch) {
   }
 }
 
+// dst[i] = src[i] for i in [lo, hi) by this CTA (16-byte copies when VEC).
+template <bool VEC>
+__device__ __forceinline__ void copy_range(const float* src, float* dst, unsigned long long lo,
+                                           unsigned long long hi) {
+  if constexpr (VEC) {
+    const float4* s4 = reinterpret_cast<const float4*>(src + lo);
+    float4* d4 = reinterpret_cast<float4*>(dst + lo);
+    const long long n4 = static_cast<long long>((hi - lo) / 4);
+    for (long long i0 = 0; i0 < n4; i0 += static_cast<long long>(kThreads) * kVecPerThread) {
+      float4 v[kVecPerThread];
+#pragma unroll
+      for (int u = 0; u < kVecPerThread; ++u) {
+        const long long i = i0 + threadIdx.x + static_cast<long long>(u) * kThreads;
+        if (i < n4) v[u] = s4[i];
+      }
+#pragma unroll
+      for (int u = 0; u < kVecPerThread; ++u) {
+        const long long i = i0 + threadIdx.x + static_cast<long long>(u) * kThreads;
+        if (i < n4) d4[i] = v[u];
+      }
+    }
+  } else {
+    for (unsigned long long i = lo + threadIdx.x; i < hi; i += kThreads) dst[i] = src[i];
+  }
+}
+
 template <bool VEC>
 __global__ void __launch_bounds__(kThreads) peer_pull(const PullArgs a) {
   __shared__ int ready;
   unsigned* own = header(a.bases[a.rank]);
-  if (blockIdx.x == 0 && static_cast<int>(threadIdx.x) < a.world &&
-      static_cast<int>(threadIdx.x) != a.rank) {
-    __threadfence_system();
-    store_release(header(a.bases[threadIdx.x]) + a.rank, a.epoch);
+  float* dst_buf = buffer(a.bases[a.rank], a.count, a.epoch);
+  // 1. this CTA's share of the own block (a multiple of 4 floats when VEC)
+  {
+    const unsigned long long per =
+        ((a.block + gridDim.x - 1) / gridDim.x + 3) / 4 * 4;
+    const unsigned long long lo = blockIdx.x * per < a.block ? blockIdx.x * per : a.block;
+    const unsigned long long hi = lo + per < a.block ? lo + per : a.block;
+    const unsigned long long off = static_cast<unsigned long long>(a.rank) * a.block;
+    copy_range<VEC>(a.x_local, dst_buf + off, lo, hi);
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) ready = atomicAdd(own + kArriveWord, 1u) == gridDim.x - 1 ? 1 : 0;
+    __syncthreads();
+    if (ready) {  // the last CTA: the whole own block is in place
+      if (threadIdx.x == 0) own[kArriveWord] = 0;
+      if (static_cast<int>(threadIdx.x) < a.world && static_cast<int>(threadIdx.x) != a.rank) {
+        __threadfence_system();
+        store_release(header(a.bases[threadIdx.x]) + a.rank, a.epoch);
+      }
+    }
+    __syncthreads();
   }
+  // 2. the peers' blocks
   const unsigned long long chunks = (a.block + kChunkFloats - 1) / kChunkFloats;
   const unsigned long long items = static_cast<unsigned long long>(a.world - 1) * chunks;
-  float* dst_buf = buffer(a.bases[a.rank], a.count, a.epoch);
   for (unsigned long long it = blockIdx.x; it < items; it += gridDim.x) {
     const int q = static_cast<int>(it / chunks);
     const int peer = q < a.rank ? q : q + 1;
@@ -107,26 +154,8 @@ __global__ void __launch_bounds__(kThreads) peer_pull(const PullArgs a) {
                                     c * kChunkFloats;
       const unsigned long long end = static_cast<unsigned long long>(peer) * a.block + a.block;
       const unsigned long long hi = lo + kChunkFloats < end ? lo + kChunkFloats : end;
-      const float* src = buffer(a.bases[peer], a.count, a.epoch);
-      if constexpr (VEC) {
-        // lo and hi are multiples of 4 (block % 4 == 0): 16-byte copies
-        const float4* s4 = reinterpret_cast<const float4*>(src + lo);
-        float4* d4 = reinterpret_cast<float4*>(dst_buf + lo);
-        const int n4 = static_cast<int>((hi - lo) / 4);
-        float4 v[kVecPerThread];
-#pragma unroll
-        for (int u = 0; u < kVecPerThread; ++u) {
-          const int i = static_cast<int>(threadIdx.x) + u * kThreads;
-          if (i < n4) v[u] = s4[i];
-        }
-#pragma unroll
-        for (int u = 0; u < kVecPerThread; ++u) {
-          const int i = static_cast<int>(threadIdx.x) + u * kThreads;
-          if (i < n4) d4[i] = v[u];
-        }
-      } else {
-        for (unsigned long long i = lo + threadIdx.x; i < hi; i += kThreads) dst_buf[i] = src[i];
-      }
+      // lo and hi are multiples of 4 when VEC (block % 4 == 0)
+      copy_range<VEC>(buffer(a.bases[peer], a.count, a.epoch), dst_buf, lo, hi);
     }
     __syncthreads();
   }
@@ -197,22 +226,16 @@ mb200PeerStatus_t mb200PeerAllgather(void* const* bases, int world, int rank, si
     if (bases[p] == nullptr) return MB200_PEER_INVALID_VALUE;
     a.bases[p] = bases[p];
   }
+  a.x_local = x_local;
   a.world = world;
   a.rank = rank;
   a.epoch = epoch;
   a.count = count;
   a.block = block;
-  float* own = mb200PeerBuffer(bases[rank], count, epoch) + static_cast<std::size_t>(rank) * block;
-  cudaError_t e = cudaMemcpyAsync(own, x_local, block * sizeof(float), cudaMemcpyDeviceToDevice,
-                                  stream);
-  if (e != cudaSuccess) return MB200_PEER_CUDA_ERROR;
-  if (world == 1) return MB200_PEER_SUCCESS;
-  const unsigned long long chunks = (block + kChunkFloats - 1) / kChunkFloats;
-  const unsigned long long items = static_cast<unsigned long long>(world - 1) * chunks;
   const int sms = mb200::sm_count(mb200::current_device());
-  const unsigned long long cap = static_cast<unsigned long long>(sms > 0 ? sms : 148) * 4;
-  const unsigned grid = static_cast<unsigned>(items < cap ? items : cap);
-  const bool vec = block % 4 == 0 && count % 4 == 0;
+  const unsigned grid = static_cast<unsigned>((sms > 0 ? sms : 148) * 2);
+  const bool vec = block % 4 == 0 && count % 4 == 0 &&
+                   reinterpret_cast<std::uintptr_t>(x_local) % 16 == 0;
   if (vec)
     peer_pull<true><<<grid, kThreads, 0, stream>>>(a);
   else

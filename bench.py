@@ -378,7 +378,7 @@ def suite_sgemm(s: Suite) -> dict:
     out = {"value": tf, "unit": "TFLOP/s", "ms": ms, "dtype": "f32 (split-tf32 on tcgen05)",
            "config": f"{m}x{n}x{k} fp32, L2 flushed before each call; hi/lo split of A and B, "
                      "split-K GEMM, split-order reduction",
-           "roofline": s.roof("tc_gemm_split_kernel<SplitGemmProblem,256,2,2>", tf,
+           "roofline": s.roof("tc_gemm_split_kernel<SplitGemmProblem<256>,256,2,2>", tf,
                               "tensor-tf32x3"),
            "launches": launches,
            "pedantic_ffma": {"ms": ms_ffma, "TFLOP/s": flop / (ms_ffma * 1e-3) / 1e12,

@@ -265,10 +265,12 @@ __device__ __forceinline__ uint4 transform(uint4 r, float mean, float stddev) {
   }
 }
 
-// Packing chosen by measurement on B200: all-packed normal 1.466 ms per 2^30
-// words, all-scalar 1.602 ms; packed uniform conversion 0.745 ms, scalar 0.805 ms.
+// Packing chosen by measurement on B200 (2^30 words, 8 CTAs per SM): the normal's
+// 16 mixes ran 1.368 (conversion, log and output packed, trig scalar) to 1.605 ms
+// (output and conversion packed only); all-packed 1.400, all-scalar 1.521.  The
+// uniform conversion: packed 0.745 ms, scalar 0.805 ms.
 constexpr unsigned kUniformPack = kPackConv;
-constexpr unsigned kNormalPack = kPackConv | kPackLog | kPackTrig | kPackOut;
+constexpr unsigned kNormalPack = kPackConv | kPackLog | kPackOut;
 
 // One thread per Philox block, grid-stride.  Vec16 selects a single 16-byte
 // store per block (output 16-byte aligned); otherwise four 4-byte stores.

@@ -3,6 +3,8 @@
 
 #include <cuda_runtime.h>
 
+#include <cstdint>
+
 #include "common/device.hpp"
 
 namespace mb200::tc {
@@ -51,11 +53,47 @@ __device__ __forceinline__ void split_tile(const SplitJob& j, long long z, long 
   __syncthreads();
 }
 
+// A job whose k is contiguous and whose rows, planes and pointers keep 16-byte
+// alignment needs no transpose: each thread splits four consecutive k of a row
+// (one 16-byte load, two 16-byte stores).
+__host__ __device__ inline bool streaming(const SplitJob& j) {
+  return j.ks == 1 && j.cols % 4 == 0 && j.rs % 4 == 0 && j.zs % 4 == 0 && j.ldk % 4 == 0 &&
+         reinterpret_cast<std::uintptr_t>(j.src) % 16 == 0 &&
+         reinterpret_cast<std::uintptr_t>(j.dst) % 16 == 0;
+}
+
+__device__ void split_stream(const SplitJob& j) {
+  const long long k4 = j.cols / 4;
+  const long long per_z = j.rows * k4;
+  const long long total = per_z * j.batch;
+  const long long plane = static_cast<long long>(j.batch) * j.rows * j.ldk;
+  const long long stride = static_cast<long long>(gridDim.x) * blockDim.x * blockDim.y;
+  for (long long t = static_cast<long long>(blockIdx.x) * blockDim.x * blockDim.y +
+                     threadIdx.y * blockDim.x + threadIdx.x;
+       t < total; t += stride) {
+    const long long z = t / per_z, rem = t - z * per_z;
+    const long long r = rem / k4, k = (rem - r * k4) * 4;
+    const float4 v = __ldg(reinterpret_cast<const float4*>(j.src + z * j.zs + r * j.rs + k));
+    float4 hi, lo;
+    split(v.x, hi.x, lo.x);
+    split(v.y, hi.y, lo.y);
+    split(v.z, hi.z, lo.z);
+    split(v.w, hi.w, lo.w);
+    float* d = j.dst + (z * j.rows + r) * j.ldk + k;
+    *reinterpret_cast<float4*>(d) = hi;
+    *reinterpret_cast<float4*>(d + plane) = lo;
+  }
+}
+
 // Blocks stride over the tiles of job blockIdx.y (0 or 1; one job when y == 1).
 __global__ void __launch_bounds__(kTile* kRowsPerPass)
     split_jobs(const SplitJob j0, const SplitJob j1) {
   __shared__ float tile[kTile][kTile + 1];  // [row][k]
   const SplitJob& j = blockIdx.y == 0 ? j0 : j1;
+  if (streaming(j)) {
+    split_stream(j);
+    return;
+  }
   const long long tiles_k = (j.cols + kTile - 1) / kTile;
   const long long tiles_r = (j.rows + kTile - 1) / kTile;
   const long long per = tiles_k * tiles_r;
@@ -90,6 +128,8 @@ namespace {
 
 unsigned split_grid(const SplitJob& a, const SplitJob* b) {
   auto tiles = [](const SplitJob& j) {
+    if (streaming(j))  // CTAs of kTile * kRowsPerPass threads, one 4-float group each
+      return (j.rows * (j.cols / 4) * j.batch + kTile * kRowsPerPass - 1) / (kTile * kRowsPerPass);
     return ((j.cols + kTile - 1) / kTile) * ((j.rows + kTile - 1) / kTile) * j.batch;
   };
   long long t = tiles(a);

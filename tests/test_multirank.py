@@ -150,3 +150,24 @@ def test_dist_spmv_two_gloo_ranks(rows, cols, heavy, alpha, beta):
 
 def test_rng_weak_scaling_partition_two_gloo_ranks():
     _run(_rng_worker, 4099 * 4, 1234)
+
+
+def test_dist_spmv_exchange_arguments():
+    """The exchange is "nccl" or "peer"; the peer exchange is the CUDA path only, so
+    a pluggable CPU product with it is refused before anything is allocated."""
+    import torch
+
+    from muda_b200.dist_spmv import DistSpMV
+    offsets = torch.tensor([0, 1, 2], dtype=torch.int32)
+    cols = torch.tensor([0, 1], dtype=torch.int32)
+    vals = torch.tensor([1.0, 2.0])
+    common = dict(offsets=offsets, col_ind=cols, values=vals, row_begin=0, row_end=2, cols=2,
+                  local_spmv=lambda *a: None)
+    with pytest.raises(ValueError, match="unknown exchange"):
+        DistSpMV(torch, None, None, exchange="nvshmem", **common)
+    with pytest.raises(ValueError, match="CUDA path only"):
+        DistSpMV(torch, None, None, exchange="peer", **common)
+    d = DistSpMV(torch, None, None, exchange="nccl", **common)
+    x = torch.tensor([3.0, 4.0])
+    d.gather_x(x)
+    assert torch.equal(d.x_full[:2], x)

@@ -276,3 +276,29 @@ def test_gpu_spmm(cuda, built, shape, op_a, op_b, order_b, order_c):
             err = np.abs(g - exact)
             assert np.all(err <= 1e-5 * scale + 1e-30), np.max(err / (scale + 1e-30))
     a.close()
+
+
+@pytest.mark.gpu
+def test_gpu_spmm_long_row_list_overflow(cuda, built):
+    """More rows above the scheduler's 256-entry threshold than its list holds
+    (65536): every row is then taken in the chunked phase, and the results stay
+    bit-identical to the oracle (checked on a sample of rows)."""
+    torch = cuda
+    rng = np.random.default_rng(4242)
+    rows, cols, n, k = 66000, 2048, 64, 257
+    ci = np.sort(rng.integers(0, cols, (rows, k)), axis=1).astype(np.int32)
+    offsets = np.arange(rows + 1, dtype=np.int64) * k
+    va = rng.uniform(-1, 1, (rows, k)).astype(np.float32)
+    b = rng.uniform(-1, 1, (cols, n)).astype(np.float32)
+    a = Csr(torch, offsets, ci.reshape(-1), va.reshape(-1), rows, cols)
+    tb = torch.from_numpy(b.reshape(-1)).cuda()
+    tc = torch.zeros(rows * n, dtype=torch.float32, device="cuda")
+    assert a.spmm(0, 0, tb, (cols, n), n, 2, tc, (rows, n), n, 2, 1.0, 0.0) == 0
+    got = tc.cpu().numpy().reshape(rows, n)
+    sample = np.unique(np.r_[0:64, rows - 64:rows, rng.integers(0, rows, 128)])
+    sub_off = np.arange(len(sample) + 1, dtype=np.int64) * k
+    want = np.zeros(len(sample) * n, np.float32)
+    oracle.spmm_csr(sub_off, ci[sample].reshape(-1), va[sample].reshape(-1), cols, b.reshape(-1),
+                    n, 2, want, n, 2, n)
+    np.testing.assert_array_equal(got[sample], want.reshape(len(sample), n))
+    a.close()

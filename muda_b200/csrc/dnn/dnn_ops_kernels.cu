@@ -301,6 +301,74 @@ __global__ void __launch_bounds__(kThreads)
   }
 }
 
+// Packed NCHW input and output: blockIdx.y is the (n, c) plane, so the index math is
+// 32-bit within a plane and the plane offset is formed once.  For a window known at
+// compile time (WH, WW > 0) every in-range tap is loaded before the first is used,
+// so the loads overlap instead of waiting on each other through the running result;
+// the taps are then combined in the same order as pooling_fwd, out-of-range taps
+// skipped (bit-identical results).
+template <int WH, int WW>
+__global__ void __launch_bounds__(kThreads)
+    pooling_planes(const float* __restrict__ x, float* __restrict__ y, PoolShape p, float alpha,
+                   float beta) {
+  const int OW = p.y.w, OH = p.y.h, W = p.x.w, H = p.x.h;
+  const int per_plane = OH * OW;
+  const std::int64_t plane = blockIdx.y;
+  const float* xp = x + plane * (static_cast<std::int64_t>(H) * W);
+  float* yp = y + plane * static_cast<std::int64_t>(per_plane);
+  const bool is_max = p.mode == 0 || p.mode == 3;
+  const int wh = WH > 0 ? WH : p.win_h, ww = WW > 0 ? WW : p.win_w;
+  for (int t = blockIdx.x * blockDim.x + threadIdx.x; t < per_plane; t += gridDim.x * blockDim.x) {
+    const int oy = t / OW, ox = t - oy * OW;
+    const int y0 = oy * p.stride_h - p.pad_h, x0 = ox * p.stride_w - p.pad_w;
+    float acc = is_max ? -INFINITY : 0.0f;
+    int count = 0;
+    if constexpr (WH > 0 && WW > 0) {
+      float v[WH][WW];
+      bool in[WH][WW];
+#pragma unroll
+      for (int r = 0; r < WH; ++r) {
+#pragma unroll
+        for (int q = 0; q < WW; ++q) {
+          const int iy = y0 + r, ix = x0 + q;
+          in[r][q] = iy >= 0 && iy < H && ix >= 0 && ix < W;
+          v[r][q] = in[r][q] ? __ldg(xp + iy * W + ix) : 0.0f;
+        }
+      }
+#pragma unroll
+      for (int r = 0; r < WH; ++r) {
+#pragma unroll
+        for (int q = 0; q < WW; ++q) {
+          if (in[r][q]) {
+            acc = is_max ? fmaxf(acc, v[r][q]) : acc + v[r][q];
+            ++count;
+          }
+        }
+      }
+    } else {
+      for (int r = 0; r < wh; ++r) {
+        const int iy = y0 + r;
+        if (iy < 0 || iy >= H) continue;
+        const float* row = xp + iy * W;
+        for (int q = 0; q < ww; ++q) {
+          const int ix = x0 + q;
+          if (ix < 0 || ix >= W) continue;
+          const float v = __ldg(row + ix);
+          acc = is_max ? fmaxf(acc, v) : acc + v;
+          ++count;
+        }
+      }
+    }
+    float out = acc;
+    if (!is_max) {
+      const int denom = (p.mode == 1) ? wh * ww : (count > 1 ? count : 1);
+      out = acc / static_cast<float>(denom);
+    }
+    const float prev = (beta == 0.0f) ? 0.0f : beta * yp[t];
+    yp[t] = fmaf(alpha, out, prev);
+  }
+}
+
 // --------------------------------------------------------- batch norm --
 // Inference (cudnn_kernels.metal:570-611): y = alpha * (((x - mean) * inv_std) *
 // scale + bias) + beta * y with inv_std = rsqrt(var + eps); parameters per
@@ -554,6 +622,25 @@ cudaError_t launch_pooling(const float* x, float* y, const PoolShape& p, float a
                            cudaStream_t stream) noexcept {
   const std::int64_t total = static_cast<std::int64_t>(p.y.n) * p.y.c * p.y.h * p.y.w;
   if (total <= 0) return cudaSuccess;
+  auto packed = [](const View4& v) {
+    return v.ws == 1 && v.hs == v.w && v.cs == static_cast<std::int64_t>(v.h) * v.w &&
+           v.ns == static_cast<std::int64_t>(v.c) * v.h * v.w;
+  };
+  const std::int64_t planes = static_cast<std::int64_t>(p.y.n) * p.y.c;
+  const std::int64_t per_plane = static_cast<std::int64_t>(p.y.h) * p.y.w;
+  const std::int64_t in_plane = static_cast<std::int64_t>(p.x.h) * p.x.w;
+  if (packed(p.x) && packed(p.y) && planes <= 65535 && per_plane < (1 << 30) &&
+      in_plane < (1 << 30)) {
+    const std::int64_t cta = (per_plane + kThreads - 1) / kThreads;
+    const dim3 grid(static_cast<unsigned>(cta < 64 ? cta : 64), static_cast<unsigned>(planes));
+    if (p.win_h == 3 && p.win_w == 3)
+      pooling_planes<3, 3><<<grid, kThreads, 0, stream>>>(x, y, p, alpha, beta);
+    else if (p.win_h == 2 && p.win_w == 2)
+      pooling_planes<2, 2><<<grid, kThreads, 0, stream>>>(x, y, p, alpha, beta);
+    else
+      pooling_planes<0, 0><<<grid, kThreads, 0, stream>>>(x, y, p, alpha, beta);
+    return cudaGetLastError();
+  }
   pooling_fwd<<<grid_for(total), kThreads, 0, stream>>>(x, y, p, alpha, beta);
   return cudaGetLastError();
 }

@@ -384,7 +384,8 @@ def test_gpu_activation(cuda, built, mode, layout):
 @pytest.mark.parametrize("mode", range(4))
 @pytest.mark.parametrize("win,pad,stride", [((2, 2), (0, 0), (2, 2)), ((3, 3), (1, 1), (2, 2)),
                                             ((3, 2), (1, 0), (1, 2))])
-def test_gpu_pooling(cuda, built, mode, win, pad, stride):
+@pytest.mark.parametrize("yfmt", ["NHWC", "NCHW"])  # NCHW in and out: the per-plane kernel
+def test_gpu_pooling(cuda, built, mode, win, pad, stride, yfmt):
     torch = cuda
     xs = (2, 5, 11, 10)
     rng = np.random.default_rng(mode + win[0])
@@ -397,14 +398,14 @@ def test_gpu_pooling(cuda, built, mode, win, pad, stride):
         dims = [C.c_int() for _ in range(4)]
         assert d.L.cudnnGetPooling2dForwardOutputDim(pool, xd, *[C.byref(v) for v in dims]) == 0
         ys = tuple(v.value for v in dims)
-        yd = _tdesc(d, ys, "NHWC")
+        yd = _tdesc(d, ys, yfmt)
         y0 = rng.standard_normal(int(np.prod(ys))).astype(np.float32)
         ty = _dev(torch, y0)
         assert d.L.cudnnPoolingForward(d.h, pool, fptr(1.0), xd, _p(_dev(torch, x)), fptr(0.5), yd,
                                        _p(ty)) == 0
         torch.cuda.synchronize()
         want = oracle.pooling(x, xs, y0.copy(), ys, win, pad, stride, mode,
-                              ystrides=_strides(ys, "NHWC"), beta=0.5)
+                              ystrides=_strides(ys, yfmt), beta=0.5)
         assert np.array_equal(ty.cpu().numpy(), want)
         assert d.L.cudnnDestroyPoolingDescriptor(pool) == 0
 

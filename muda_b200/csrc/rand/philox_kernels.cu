@@ -380,35 +380,50 @@ __device__ __forceinline__ float uniform_of(std::uint32_t v) {
   return __fmul_rn(__fadd_rn(static_cast<float>(v), 1.0f), 2.3283064365386963e-10f);
 }
 
+// Output i draws Knuth's product from its own stream: block ctr = first_block + i,
+// then (ctr, c2 = 1, 2, ...) while more words are needed; k counts the factors until
+// the product falls to exp(-lambda) or below.  Each step of a thread's loop computes
+// one Philox block of its current output and takes up to four factors from it; a
+// thread whose output ends writes it and starts its next output at the next step.
+// So a warp runs about as many steps as its lanes' own outputs need, instead of the
+// longest of 32 outputs each time (the Philox arithmetic never diverges), and no
+// block is computed that is not used.
 __global__ void __launch_bounds__(kThreads) philox_poisson_kernel(const FillArgs a) {
   const std::uint64_t stride = static_cast<std::uint64_t>(gridDim.x) * kThreads;
   unsigned int* out = static_cast<unsigned int*>(a.out);
-  for (std::uint64_t i = static_cast<std::uint64_t>(blockIdx.x) * kThreads + threadIdx.x;
-       i < a.n; i += stride) {
-    const std::uint64_t ctr = a.first_block + i;
-    uint4 r = philox_block(ctr, a.key);
-    unsigned int result;
-    if (a.lambda < 30.0f) {
-      float p = 1.0f;
-      unsigned int k = 0, sub = 0, word = 0;
-      while (p > a.exp_neg_lambda && k < 1000u) {
-        ++k;
-        const std::uint32_t v = word == 0 ? r.x : (word == 1 ? r.y : (word == 2 ? r.z : r.w));
-        p = __fmul_rn(p, uniform_of(v));
-        if (++word == 4) {
-          word = 0;
-          r = philox_block(ctr, a.key, ++sub);
-        }
-      }
-      result = k > 0 ? k - 1 : 0u;
-    } else {
+  std::uint64_t i = static_cast<std::uint64_t>(blockIdx.x) * kThreads + threadIdx.x;
+  if (a.lambda >= 30.0f) {
+    for (; i < a.n; i += stride) {
+      const uint4 r = philox_block(a.first_block + i, a.key);
       const float u0 = uniform_of(r.x), u1 = uniform_of(r.y);
       const float z = __fmul_rn(sqrtf(__fmul_rn(-2.0f, logf(u0))),
                                 cosf(__fmul_rn(6.28318530717958647692f, u1)));
       const float val = __fadd_rn(__fadd_rn(a.lambda, __fmul_rn(sqrtf(a.lambda), z)), 0.5f);
-      result = val > 0.0f ? static_cast<unsigned int>(val) : 0u;
+      out[i] = val > 0.0f ? static_cast<unsigned int>(val) : 0u;
     }
-    out[i] = result;
+    return;
+  }
+  float p = 1.0f;
+  unsigned int k = 0, sub = 0;
+  while (i < a.n) {
+    const uint4 r = philox_block(a.first_block + i, a.key, sub);
+    const std::uint32_t w[4] = {r.x, r.y, r.z, r.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      if (p > a.exp_neg_lambda && k < 1000u) {
+        ++k;
+        p = __fmul_rn(p, uniform_of(w[j]));
+      }
+    }
+    if (p > a.exp_neg_lambda && k < 1000u) {
+      ++sub;  // the same output needs the next block of its stream
+    } else {
+      out[i] = k > 0 ? k - 1 : 0u;
+      i += stride;
+      p = 1.0f;
+      k = 0;
+      sub = 0;
+    }
   }
 }
 

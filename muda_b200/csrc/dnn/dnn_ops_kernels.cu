@@ -465,6 +465,33 @@ __device__ __forceinline__ void bn_range(std::int64_t m, int splits, int part, s
   i1 = i0 + per < m ? i0 + per : m;
 }
 
+// Image b and pixel p (within the H x W plane) of element i of a channel's N*H*W
+// range, stepped by kRedThreads without dividing (a 64-bit division per element
+// would cost more than the memory traffic).
+struct PlaneWalk {
+  int b;
+  std::int64_t p, hw;
+  __device__ PlaneWalk(std::int64_t i, std::int64_t hw_) : hw(hw_) {
+    b = static_cast<int>(i / hw_);
+    p = i - static_cast<std::int64_t>(b) * hw_;
+  }
+  __device__ void next() {
+    p += kRedThreads;
+    while (p >= hw) {
+      p -= hw;
+      ++b;
+    }
+  }
+};
+
+// Offset of (b, c, pixel p) in a view; one multiply-add when a plane's rows are
+// contiguous (hs == w * ws).
+__device__ __forceinline__ std::int64_t plane_at(const View4& v, int b, int c, std::int64_t p) {
+  if (v.hs == static_cast<std::int64_t>(v.w) * v.ws) return b * v.ns + c * v.cs + p * v.ws;
+  const int h = static_cast<int>(p / v.w);
+  return at(v, b, c, h, static_cast<int>(p - static_cast<std::int64_t>(h) * v.w));
+}
+
 template <int STAGE>
 __global__ void __launch_bounds__(kRedThreads)
     bn_training_split(const float* __restrict__ x, View4 xv, float* __restrict__ y, View4 yv,
@@ -482,12 +509,7 @@ __global__ void __launch_bounds__(kRedThreads)
   float* psq = partial + static_cast<std::int64_t>(xv.c) * splits + c * splits;  // [C][splits]
   std::int64_t i0, i1;
   bn_range(m, splits, part, i0, i1);
-  auto x_at_i = [&](std::int64_t i) {
-    const int b = static_cast<int>(i / hw);
-    const std::int64_t p = i - b * hw;
-    const int h = static_cast<int>(p / xv.w);
-    return at(xv, b, c, h, static_cast<int>(p - h * xv.w));
-  };
+  PlaneWalk pw(i0 + threadIdx.x, hw);
   float mean = 0.0f;
   if (STAGE >= 1) {
     float t = 0.0f;
@@ -496,13 +518,14 @@ __global__ void __launch_bounds__(kRedThreads)
   }
   if (STAGE == 0) {
     float acc = 0.0f;
-    for (std::int64_t i = i0 + threadIdx.x; i < i1; i += kRedThreads) acc += x[x_at_i(i)];
+    for (std::int64_t i = i0 + threadIdx.x; i < i1; i += kRedThreads, pw.next())
+      acc += x[plane_at(xv, pw.b, c, pw.p)];
     const float total = block_sum<kRedThreads>(acc, scratch);
     if (threadIdx.x == 0) psum[part] = total;
   } else if (STAGE == 1) {
     float sq = 0.0f;
-    for (std::int64_t i = i0 + threadIdx.x; i < i1; i += kRedThreads) {
-      const float d = x[x_at_i(i)] - mean;
+    for (std::int64_t i = i0 + threadIdx.x; i < i1; i += kRedThreads, pw.next()) {
+      const float d = x[plane_at(xv, pw.b, c, pw.p)] - mean;
       sq = fmaf(d, d, sq);
     }
     const float total = block_sum<kRedThreads>(sq, scratch);
@@ -524,13 +547,9 @@ __global__ void __launch_bounds__(kRedThreads)
       }
     }
     const float sc = scale[c], bi = bias[c];
-    for (std::int64_t i = i0 + threadIdx.x; i < i1; i += kRedThreads) {
-      const int b = static_cast<int>(i / hw);
-      const std::int64_t p = i - b * hw;
-      const int h = static_cast<int>(p / xv.w);
-      const int w = static_cast<int>(p - h * xv.w);
-      const float nv = fmaf((x[at(xv, b, c, h, w)] - mean) * inv_std, sc, bi);
-      const std::int64_t yi = at(yv, b, c, h, w);
+    for (std::int64_t i = i0 + threadIdx.x; i < i1; i += kRedThreads, pw.next()) {
+      const float nv = fmaf((x[plane_at(xv, pw.b, c, pw.p)] - mean) * inv_std, sc, bi);
+      const std::int64_t yi = plane_at(yv, pw.b, c, pw.p);
       const float prev = (beta == 0.0f) ? 0.0f : beta * y[yi];
       y[yi] = fmaf(alpha, nv, prev);
     }

@@ -32,9 +32,20 @@ __device__ __forceinline__ std::int64_t at(const View4& v, int b, int c, int h, 
   return b * v.ns + c * v.cs + h * v.hs + w * v.ws;
 }
 
-// (n, c, h, w) of linear index t in w-fastest order.
+// (n, c, h, w) of linear index t in w-fastest order; 32-bit divisions when t fits
+// (a 64-bit division costs several times as many instructions).
 __device__ __forceinline__ void unflatten(std::int64_t t, int c, int h, int w, int& b, int& ic,
                                           int& ih, int& iw) {
+  if (t >= 0 && t <= 0x7fffffff) {
+    unsigned u = static_cast<unsigned>(t);
+    iw = static_cast<int>(u % static_cast<unsigned>(w));
+    u /= static_cast<unsigned>(w);
+    ih = static_cast<int>(u % static_cast<unsigned>(h));
+    u /= static_cast<unsigned>(h);
+    ic = static_cast<int>(u % static_cast<unsigned>(c));
+    b = static_cast<int>(u / static_cast<unsigned>(c));
+    return;
+  }
   iw = static_cast<int>(t % w);
   t /= w;
   ih = static_cast<int>(t % h);

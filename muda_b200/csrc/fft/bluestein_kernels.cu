@@ -118,23 +118,33 @@ __device__ __forceinline__ void inner_fft(float2 (&v)[Plan<LOG2M>::P], int j, co
   }
 }
 
-// Two inner FFTs keep more state live than one: the register budget is sized for
-// two resident CTAs of 256 threads (one of 512) per SM.
+// CTA shape of the fused kernel: one transform per CTA once a transform has 64
+// threads or more (a CTA's barriers then wait only for its own transform, as the
+// mixed-radix kernel measured), else the Stockham plan's packing.  Two inner FFTs
+// keep more state live than one: the register budget is 128 a thread, 512 threads
+// of resident CTAs per SM.
 template <int LOG2M>
-constexpr int kBlueCtas = Plan<LOG2M>::THREADS >= 512 ? 1 : 2;
+struct BlueShape {
+  static constexpr int TPC = Plan<LOG2M>::T >= 64 ? 1 : Plan<LOG2M>::TPC;
+  static constexpr int THREADS = Plan<LOG2M>::T * TPC;
+  static constexpr int CTAS = THREADS >= 512 ? 1 : 512 / THREADS;
+};
+template <int LOG2M>
+constexpr int kBlueCtas = BlueShape<LOG2M>::CTAS;
 
 template <int LOG2M, int DIR>
-__global__ void __launch_bounds__(Plan<LOG2M>::THREADS, kBlueCtas<LOG2M>)
+__global__ void __launch_bounds__(BlueShape<LOG2M>::THREADS, kBlueCtas<LOG2M>)
     bluestein_kernel(const Batch1D bt, int n, const float2* __restrict__ chirp,
                      const float2* __restrict__ bhat, const float2* __restrict__ tw_m) {
   using PL = Plan<LOG2M>;
+  using BS = BlueShape<LOG2M>;
   extern __shared__ float smem[];
   const int tloc = threadIdx.x / PL::T;
   const int j = threadIdx.x % PL::T;
   float* sre = smem + tloc * PL::REGION * 2;
   float* sim = sre + PL::REGION;
-  for (std::int64_t t0 = static_cast<std::int64_t>(blockIdx.x) * PL::TPC; t0 < bt.batch;
-       t0 += static_cast<std::int64_t>(gridDim.x) * PL::TPC) {
+  for (std::int64_t t0 = static_cast<std::int64_t>(blockIdx.x) * BS::TPC; t0 < bt.batch;
+       t0 += static_cast<std::int64_t>(gridDim.x) * BS::TPC) {
     const std::int64_t tr = t0 + tloc;
     Io io;
     io.active = tr < bt.batch;
@@ -157,18 +167,19 @@ template <int LOG2M, int DIR>
 cudaError_t launch_m(int n, const Batch1D& b, const float2* chirp, const float2* bhat,
                      const float2* tw_m, cudaStream_t stream) {
   using PL = Plan<LOG2M>;
+  using BS = BlueShape<LOG2M>;
   auto kern = bluestein_kernel<LOG2M, DIR>;
-  constexpr int kSmem = PL::TPC * PL::REGION * 2 * 4;
+  constexpr int kSmem = BS::TPC * PL::REGION * 2 * 4;
   if (kSmem > 48 * 1024) {
     const cudaError_t e =
         cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
     if (e != cudaSuccess) return e;
   }
-  const std::int64_t ctas = (b.batch + PL::TPC - 1) / PL::TPC;
+  const std::int64_t ctas = (b.batch + BS::TPC - 1) / BS::TPC;
   const int sms = sm_count(current_device());
   const std::int64_t cap = static_cast<std::int64_t>(sms > 0 ? sms : 148) * kBlueCtas<LOG2M> * 8;
   const unsigned grid = static_cast<unsigned>(ctas < cap ? ctas : cap);
-  kern<<<grid, PL::THREADS, kSmem, stream>>>(b, n, chirp, bhat, tw_m);
+  kern<<<grid, BS::THREADS, kSmem, stream>>>(b, n, chirp, bhat, tw_m);
   return cudaGetLastError();
 }
 

@@ -75,7 +75,25 @@ __device__ __forceinline__ void scatter_row(const CsrView& a, float xr, float al
   const T* vals = static_cast<const T*>(a.values);
   const float ax = (sizeof(T) == 4) ? alpha * xr : xr;
   if (sizeof(T) == 4 && ax == 0.0f) return;
-  for (int k = s + gl; k < e; k += step) {
+  int k = s + gl;
+  // four entries at a time: all eight loads are in flight before the first reduction
+  for (; k + 3 * step < e; k += 4 * step) {
+    int c[4];
+    T v[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      c[u] = __ldcs(a.col_ind + k + u * step) - a.base;
+      v[u] = __ldcs(vals + k + u * step);
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      if (static_cast<unsigned>(c[u]) >= static_cast<unsigned long long>(a.cols)) continue;
+      const float p = (sizeof(T) == 4) ? ax * widen(v[u]) : widen(v[u]) * ax;
+      if (sizeof(T) == 4 && p == 0.0f) continue;
+      atomicAdd(target + c[u], p);
+    }
+  }
+  for (; k < e; k += step) {
     const int c = __ldcs(a.col_ind + k) - a.base;
     if (static_cast<unsigned>(c) >= static_cast<unsigned long long>(a.cols)) continue;
     const float p = (sizeof(T) == 4) ? ax * widen(__ldcs(vals + k)) : widen(__ldcs(vals + k)) * ax;

@@ -1043,6 +1043,42 @@ def suite_gemv(s: Suite, trans: bool) -> dict:
     return out
 
 
+
+def suite_geam(s: Suite) -> dict:
+    """cuBLAS Sgeam C = A^T + B on 16384 x 16384 column-major fp32 matrices (1.07 GB
+    each, larger than L2), alpha 1, beta 1, uniform[-1, 1] from seed 8; the
+    transposed operand makes this the staged (shared-memory) form of the kernel."""
+    from muda_b200 import synth
+    torch = s.torch
+    m = n = 16384 // s.scale
+    A = synth.uniform_pm1(torch, m * n, seed=8)
+    B = synth.uniform_pm1(torch, m * n, seed=8, offset=(m * n + 3) // 4 * 4)
+    Cm = torch.empty(m * n, dtype=torch.float32, device="cuda")
+    L, h = _blas_handle(s)
+    one = C.c_float(1.0)
+    args = (h, 1, 0, m, n, C.byref(one), C.c_void_p(A.data_ptr()), n, C.byref(one),
+            C.c_void_p(B.data_ptr()), m, C.c_void_p(Cm.data_ptr()), m)
+    ms, launches = s.time(lambda: L.cublasSgeam(*args))
+    assert L.cublasDestroy_v2(h) == 0
+    alg = 12 * m * n
+    gbs = alg / (ms * 1e-3) / 1e9
+    out = {"value": gbs, "unit": "GB/s", "ms": ms, "dtype": "f32",
+           "config": f"{m} x {n}, op(A) T, op(B) N, {alg / 1e9:.2f} GB per call > L2",
+           "roofline": s.roof("geam_kernel<float,1,0>", gbs, "hbm"), "launches": launches,
+           "algorithmic_bytes_per_launch": alg}
+    if s.cpu:
+        import oracle
+        cols = 256
+        Ah = A.cpu().numpy()
+        Bh = B[: m * cols].cpu().numpy()
+        Ch = np.zeros(m * cols, np.float32)
+        dt = cpu_time(lambda: oracle.geam(np.float32, True, False, m, cols, 1.0, Ah, n, 1.0,
+                                          Bh, m, Ch, m))
+        out["cpu_baseline"] = {"value": 12 * m * cols / dt / 1e9, "unit": "GB/s", "cores": 1,
+                               "kind": "port",
+                               "sample": f"{cols} of {n} columns, oracle/blas12.cpp loop"}
+    return out
+
 SUITE = {
     "sgemm": suite_sgemm,
     "spmv": suite_spmv,
@@ -1065,6 +1101,7 @@ SUITE = {
     "sdot": lambda s: suite_level1(s, "sdot"),
     "sgemv_n": lambda s: suite_gemv(s, False),
     "sgemv_t": lambda s: suite_gemv(s, True),
+    "sgeam": suite_geam,
 }
 
 

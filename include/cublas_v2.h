@@ -113,6 +113,17 @@ cublasStatus_t cublasSgemv_v2(cublasHandle_t handle, cublasOperation_t trans, in
                               int incx, const float* beta, float* y, int incy);
 
 /* Level-3 — reference cublas_level3.mm:474-617 */
+/* C = alpha * op(A) + beta * op(B), column-major m x n; an operand whose scalar is 0
+ * is not read.  Reference: libraries/blas/include/cublas_v2.h:194-201 (implemented
+ * at libraries/blas/src/cublas_level3.mm:619-712 and :821-927). */
+cublasStatus_t cublasSgeam(cublasHandle_t handle, cublasOperation_t transa,
+                           cublasOperation_t transb, int m, int n, const float* alpha,
+                           const float* A, int lda, const float* beta, const float* B, int ldb,
+                           float* C, int ldc);
+cublasStatus_t cublasDgeam(cublasHandle_t handle, cublasOperation_t transa,
+                           cublasOperation_t transb, int m, int n, const double* alpha,
+                           const double* A, int lda, const double* beta, const double* B,
+                           int ldb, double* C, int ldc);
 cublasStatus_t cublasSgemm_v2(cublasHandle_t handle, cublasOperation_t transa,
                               cublasOperation_t transb, int m, int n, int k, const float* alpha,
                               const float* A, int lda, const float* B, int ldb, const float* beta,

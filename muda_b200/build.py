@@ -43,7 +43,8 @@ LIBS: dict[str, list[str]] = {
               "fft/fft_static.cu", "fft/real_kernels.cu"],
     "peer": ["peer/peer_exchange.cu"],
     "cublas": ["blas/cublas_api.cpp", "blas/gemm_simt_kernels.cu", "blas/gemm_tc_kernels.cu",
-               "blas/tf32_split.cu", "blas/level12_kernels.cu"],
+               "blas/tf32_split.cu", "blas/level12_kernels.cu",
+               "blas/geam_kernels.cu"],
 }
 
 COMMON_FLAGS = ["-O3", "-std=c++17", f"-I{INCLUDE}", f"-I{CSRC}"]

@@ -294,6 +294,8 @@ CUBLAS_PROTOS = {
     "cublasSasum_v2": ([vp, i32, vp, i32, vp], i32),
     "cublasIsamax_v2": ([vp, i32, vp, i32, vp], i32),
     "cublasSgemv_v2": ([vp, i32, i32, i32, vp, vp, i32, vp, i32, vp, vp, i32], i32),
+    "cublasSgeam": ([vp, i32, i32, i32, i32, vp, vp, i32, vp, vp, i32, vp, i32], i32),
+    "cublasDgeam": ([vp, i32, i32, i32, i32, vp, vp, i32, vp, vp, i32, vp, i32], i32),
 }
 
 

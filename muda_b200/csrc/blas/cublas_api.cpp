@@ -26,6 +26,7 @@
 #include <memory>
 #include <mutex>
 
+#include "blas/geam.hpp"
 #include "blas/gemm.hpp"
 #include "blas/level12.hpp"
 #include "common/device.hpp"
@@ -311,6 +312,16 @@ bool scalar(cublasPointerMode_t mode, const float* p, float* host, const float**
   }
   return true;
 }
+
+// One geam call (cublas_level3.mm:619-712 for fp32, :821-927 for fp64): the
+// reference's argument checks and status codes, then the kernel.  In host pointer
+// mode an operand whose scalar is zero is not checked (nor read); in device
+// pointer mode the scalars are unknown here, so both operands must be valid.
+template <typename T>
+cublasStatus_t run_geam(cublasHandle_t handle, cublasOperation_t transa,
+                        cublasOperation_t transb, int m, int n, const T* alpha, const T* A,
+                        int lda, const T* beta, const T* B, int ldb, T* C, int ldc,
+                        bool c_null_is_invalid);
 
 cublasStatus_t status_of(cudaError_t e) {
   return e == cudaSuccess ? CUBLAS_STATUS_SUCCESS : CUBLAS_STATUS_EXECUTION_FAILED;
@@ -647,4 +658,74 @@ cublasStatus_t cublasSgemv_v2(cublasHandle_t handle, cublasOperation_t trans, in
   return status_of(e);
 }
 
+cublasStatus_t cublasSgeam(cublasHandle_t handle, cublasOperation_t transa,
+                           cublasOperation_t transb, int m, int n, const float* alpha,
+                           const float* A, int lda, const float* beta, const float* B, int ldb,
+                           float* C, int ldc) {
+  return run_geam(handle, transa, transb, m, n, alpha, A, lda, beta, B, ldb, C, ldc, false);
+}
+
+cublasStatus_t cublasDgeam(cublasHandle_t handle, cublasOperation_t transa,
+                           cublasOperation_t transb, int m, int n, const double* alpha,
+                           const double* A, int lda, const double* beta, const double* B,
+                           int ldb, double* C, int ldc) {
+  // The reference's fp64 path also rejects a null C up front (cublas_level3.mm:829-831).
+  return run_geam(handle, transa, transb, m, n, alpha, A, lda, beta, B, ldb, C, ldc, true);
+}
+
 }  // extern "C"
+
+namespace {
+
+template <typename T>
+bool scalar_of(cublasPointerMode_t mode, const T* p, T* host, const T** dev) {
+  if (mode == CUBLAS_POINTER_MODE_DEVICE) {
+    if (!mb200::device_span_ok(p, sizeof(T))) return false;
+    *dev = p;
+    *host = T(0);
+  } else {
+    *host = *p;
+    *dev = nullptr;
+  }
+  return true;
+}
+
+template <typename T>
+bool matrix_ok(const T* p, int rows, int cols, int ld) {
+  const std::size_t elems = static_cast<std::size_t>(ld) * (cols - 1) + rows;
+  return mb200::device_span_ok(p, elems * sizeof(T)) && mb200::aligned_to(p, sizeof(T));
+}
+
+template <typename T>
+cublasStatus_t run_geam(cublasHandle_t handle, cublasOperation_t transa,
+                        cublasOperation_t transb, int m, int n, const T* alpha, const T* A,
+                        int lda, const T* beta, const T* B, int ldb, T* C, int ldc,
+                        bool c_null_is_invalid) {
+  auto h = handles().get(handle);
+  if (!h) return CUBLAS_STATUS_NOT_INITIALIZED;
+  if (!valid_op(transa) || !valid_op(transb) || m < 0 || n < 0 || alpha == nullptr ||
+      beta == nullptr || (c_null_is_invalid && C == nullptr))
+    return CUBLAS_STATUS_INVALID_VALUE;
+  const bool ta = transa != CUBLAS_OP_N, tb = transb != CUBLAS_OP_N;
+  const int m1 = m > 1 ? m : 1, n1 = n > 1 ? n : 1;
+  if (lda < (ta ? n1 : m1) || ldb < (tb ? n1 : m1) || ldc < m1)
+    return CUBLAS_STATUS_INVALID_VALUE;
+  if (m == 0 || n == 0) return CUBLAS_STATUS_SUCCESS;
+  cudaStream_t stream;
+  cublasPointerMode_t mode;
+  snapshot(*h, &stream, &mode);
+  T a, b;
+  const T *a_dev, *b_dev;
+  if (!scalar_of(mode, alpha, &a, &a_dev) || !scalar_of(mode, beta, &b, &b_dev))
+    return CUBLAS_STATUS_INVALID_VALUE;
+  const bool device_mode = mode == CUBLAS_POINTER_MODE_DEVICE;
+  if (!matrix_ok(C, m, n, ldc)) return CUBLAS_STATUS_INVALID_VALUE;
+  if ((device_mode || a != T(0)) && !matrix_ok(A, ta ? n : m, ta ? m : n, lda))
+    return CUBLAS_STATUS_INVALID_VALUE;
+  if ((device_mode || b != T(0)) && !matrix_ok(B, tb ? n : m, tb ? m : n, ldb))
+    return CUBLAS_STATUS_INVALID_VALUE;
+  return status_of(mb200::blas::launch_geam<T>(ta, tb, m, n, a, a_dev, A, lda, b, b_dev, B, ldb,
+                                               C, ldc, stream));
+}
+
+}  // namespace

@@ -1,0 +1,160 @@
+// geam_kernels.cu — cuBLAS geam, C = alpha * op(A) + beta * op(B) (HBM-bound).
+//
+// Per-element arithmetic follows the reference.  Sgeam (libraries/blas/shaders/
+// cublas_kernels.metal:1047-1076): each term is rounded on its own, a zero
+// scalar's term is +0 and its operand is not read, then C = term_a + term_b.
+// Dgeam (libraries/blas/src/cublas_level3.mm:906-927, a host loop there):
+// val = 0; val += alpha * a when alpha != 0; val += beta * b when beta != 0.
+// Both are evaluated here with explicit round-to-nearest multiplies and adds, so
+// nothing is contracted into an fma and the results are bit-identical to the CPU
+// restatement built with -ffp-contract=off.
+//
+// B200 layout: the m x n output is cut into 32 x 32 tiles, walked grid-stride by
+// a whole number of waves (8 CTAs of 256 threads per SM).  A warp always writes
+// 32 consecutive rows of one column of C (one 128-byte line for fp32).  An
+// untransposed operand is read the same way.  A transposed operand is read along
+// its own columns (rows of op(X)) into a 32 x 33 shared tile and read back across
+// it, so both its global reads and the writes of C stay coalesced.
+#include "blas/geam.hpp"
+
+#include <cuda_runtime.h>
+
+#include "common/device.hpp"
+
+namespace mb200::blas {
+namespace {
+
+constexpr int kTile = 32;
+constexpr int kRowsPerPass = 8;  // blockDim.y
+constexpr int kCtasPerSm = 8;
+
+template <typename T>
+struct GeamArgs {
+  const T* A;
+  const T* B;
+  T* C;
+  const T* alpha_dev;
+  const T* beta_dev;
+  long long lda, ldb, ldc;
+  int m, n;
+  int tiles_m;
+  long long tiles;
+  T alpha, beta;
+};
+
+__device__ __forceinline__ float mul_rn(float a, float b) { return __fmul_rn(a, b); }
+__device__ __forceinline__ double mul_rn(double a, double b) { return __dmul_rn(a, b); }
+__device__ __forceinline__ float add_rn(float a, float b) { return __fadd_rn(a, b); }
+__device__ __forceinline__ double add_rn(double a, double b) { return __dadd_rn(a, b); }
+
+// Sgeam: term_a + term_b, each term +0 when its scalar is zero.
+__device__ __forceinline__ float combine(bool use_a, float ta, bool use_b, float tb) {
+  return add_rn(use_a ? ta : 0.0f, use_b ? tb : 0.0f);
+}
+// Dgeam: 0 + term_a (when used) + term_b (when used), in that order.
+__device__ __forceinline__ double combine(bool use_a, double ta, bool use_b, double tb) {
+  double v = 0.0;
+  if (use_a) v = add_rn(v, ta);
+  if (use_b) v = add_rn(v, tb);
+  return v;
+}
+
+// Stages rows [r0, r0+32) x cols [c0, c0+32) of op(X) = X^T into s[row][col];
+// X[c + r * ldx] is op(X)[r][c], so lanes walk c (contiguous in X).
+template <typename T>
+__device__ __forceinline__ void stage_transposed(T (*s)[kTile + 1], const T* X, long long ldx,
+                                                 int m, int n, int r0, int c0) {
+  const int c = c0 + threadIdx.x;
+#pragma unroll
+  for (int k = 0; k < kTile / kRowsPerPass; ++k) {
+    const int rr = threadIdx.y + k * kRowsPerPass;
+    const int r = r0 + rr;
+    if (r < m && c < n) s[rr][threadIdx.x] = X[c + static_cast<long long>(r) * ldx];
+  }
+}
+
+template <typename T, bool TA, bool TB>
+__global__ void __launch_bounds__(kTile* kRowsPerPass) geam_kernel(GeamArgs<T> g) {
+  __shared__ T sa[TA ? kTile : 1][kTile + 1];
+  __shared__ T sb[TB ? kTile : 1][kTile + 1];
+  const T alpha = g.alpha_dev ? *g.alpha_dev : g.alpha;
+  const T beta = g.beta_dev ? *g.beta_dev : g.beta;
+  const bool use_a = alpha != T(0);
+  const bool use_b = beta != T(0);
+  for (long long t = blockIdx.x; t < g.tiles; t += gridDim.x) {
+    const int r0 = static_cast<int>(t % g.tiles_m) * kTile;
+    const int c0 = static_cast<int>(t / g.tiles_m) * kTile;
+    if constexpr (TA || TB) {
+      if (TA && use_a) stage_transposed(sa, g.A, g.lda, g.m, g.n, r0, c0);
+      if (TB && use_b) stage_transposed(sb, g.B, g.ldb, g.m, g.n, r0, c0);
+      __syncthreads();
+    }
+    const int r = r0 + threadIdx.x;
+#pragma unroll
+    for (int k = 0; k < kTile / kRowsPerPass; ++k) {
+      const int cc = threadIdx.y + k * kRowsPerPass;
+      const int c = c0 + cc;
+      if (r < g.m && c < g.n) {
+        T ta = T(0), tb = T(0);
+        if (use_a) {
+          const T a = TA ? sa[threadIdx.x][cc] : g.A[r + static_cast<long long>(c) * g.lda];
+          ta = mul_rn(alpha, a);
+        }
+        if (use_b) {
+          const T b = TB ? sb[threadIdx.x][cc] : g.B[r + static_cast<long long>(c) * g.ldb];
+          tb = mul_rn(beta, b);
+        }
+        g.C[r + static_cast<long long>(c) * g.ldc] = combine(use_a, ta, use_b, tb);
+      }
+    }
+    if constexpr (TA || TB) __syncthreads();  // the next tile overwrites the staging tiles
+  }
+}
+
+template <typename T, bool TA, bool TB>
+cudaError_t launch(const GeamArgs<T>& g, unsigned grid, cudaStream_t stream) {
+  geam_kernel<T, TA, TB><<<grid, dim3(kTile, kRowsPerPass), 0, stream>>>(g);
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+template <typename T>
+cudaError_t launch_geam(bool trans_a, bool trans_b, int m, int n, T alpha, const T* alpha_dev,
+                        const T* A, int lda, T beta, const T* beta_dev, const T* B, int ldb,
+                        T* C, int ldc, cudaStream_t stream) noexcept {
+  if (m <= 0 || n <= 0) return cudaSuccess;
+  GeamArgs<T> g{};
+  g.A = A;
+  g.B = B;
+  g.C = C;
+  g.alpha_dev = alpha_dev;
+  g.beta_dev = beta_dev;
+  g.lda = lda;
+  g.ldb = ldb;
+  g.ldc = ldc;
+  g.m = m;
+  g.n = n;
+  g.tiles_m = (m + kTile - 1) / kTile;
+  g.tiles = static_cast<long long>(g.tiles_m) * ((n + kTile - 1) / kTile);
+  g.alpha = alpha;
+  g.beta = beta;
+  const long long wave = static_cast<long long>(sm_count(current_device())) * kCtasPerSm;
+  const unsigned grid = static_cast<unsigned>(g.tiles < wave ? g.tiles : wave);
+  if (trans_a) {
+    return trans_b ? launch<T, true, true>(g, grid, stream)
+                   : launch<T, true, false>(g, grid, stream);
+  }
+  return trans_b ? launch<T, false, true>(g, grid, stream)
+                 : launch<T, false, false>(g, grid, stream);
+}
+
+template cudaError_t launch_geam<float>(bool, bool, int, int, float, const float*, const float*,
+                                        int, float, const float*, const float*, int, float*,
+                                        int, cudaStream_t) noexcept;
+template cudaError_t launch_geam<double>(bool, bool, int, int, double, const double*,
+                                         const double*, int, double, const double*,
+                                         const double*, int, double*, int,
+                                         cudaStream_t) noexcept;
+
+}  // namespace mb200::blas

@@ -493,6 +493,20 @@ def isamax(n, x, incx):
     return int(lib().oracle_isamax(n, _f32(x).ctypes.data, incx))
 
 
+def geam(dtype, transa, transb, m, n, alpha, A, lda, beta, B, ldb, C, ldc):
+    """Reference Sgeam / Dgeam (dtype np.float32 / np.float64) on column-major arrays;
+    returns a copy of C with the m x n block written.  A or B may be None when its
+    scalar is 0 (the reference does not read it)."""
+    dt = np.dtype(dtype)
+    C = np.ascontiguousarray(C, dt).copy()
+    A = np.zeros(1, dt) if A is None else np.ascontiguousarray(A, dt)
+    B = np.zeros(1, dt) if B is None else np.ascontiguousarray(B, dt)
+    fn = lib().oracle_sgeam if dt == np.float32 else lib().oracle_dgeam
+    fn(1 if transa else 0, 1 if transb else 0, m, n, alpha, A.ctypes.data, lda, beta,
+       B.ctypes.data, ldb, C.ctypes.data, ldc)
+    return C
+
+
 def sgemv(trans, m, n, alpha, A, lda, x, incx, beta, y, incy, threads=8):
     """-> (y after the reference kernel, exact per output, |terms| per output)."""
     A, x, y = _f32(A), _f32(x), _f32(y).copy()

@@ -118,6 +118,11 @@ void oracle_sswap(int n, float* x, int incx, float* y, int incy);
 void oracle_sreduce(int op, int n, const float* x, int incx, const float* y, int incy,
                     float* out_f32, double* out_f64, double* out_abs);
 int oracle_isamax(int n, const float* x, int incx);
+void oracle_sgeam(int transa, int transb, int m, int n, float alpha, const float* A,
+                  int64_t lda, float beta, const float* B, int64_t ldb, float* C, int64_t ldc);
+void oracle_dgeam(int transa, int transb, int m, int n, double alpha, const double* A,
+                  int64_t lda, double beta, const double* B, int64_t ldb, double* C,
+                  int64_t ldc);
 void oracle_sgemv(int trans, int m, int n, float alpha, const float* A, int64_t lda,
                   const float* x, int incx, float beta, float* y, int incy, double* exact,
                   double* absv, int threads);

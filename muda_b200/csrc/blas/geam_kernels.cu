@@ -9,12 +9,14 @@
 // nothing is contracted into an fma and the results are bit-identical to the CPU
 // restatement built with -ffp-contract=off.
 //
-// B200 layout: the m x n output is cut into 32 x 32 tiles, walked grid-stride by
-// a whole number of waves (8 CTAs of 256 threads per SM).  A warp always writes
+// B200 layout: the m x n output is cut into 32 x 64 tiles, walked grid-stride by
+// one wave of CTAs (256 threads each, as many per SM as fit).  A warp always writes
 // 32 consecutive rows of one column of C (one 128-byte line for fp32).  An
-// untransposed operand is read the same way.  A transposed operand is read along
-// its own columns (rows of op(X)) into a 32 x 33 shared tile and read back across
-// it, so both its global reads and the writes of C stay coalesced.
+// untransposed operand is read the same way, into registers.  A transposed
+// operand is read along its own columns (rows of op(X)) into a 32 x 65 shared
+// tile and read back across it, so both its global reads and the writes of C stay
+// coalesced.  All of a tile's loads (16 per thread) are issued before its one
+// barrier, so the tile waits on memory once.
 #include "blas/geam.hpp"
 
 #include <cuda_runtime.h>
@@ -24,9 +26,10 @@
 namespace mb200::blas {
 namespace {
 
-constexpr int kTile = 32;
-constexpr int kRowsPerPass = 8;  // blockDim.y
-constexpr int kCtasPerSm = 8;
+constexpr int kTile = 32;         // rows of C per tile (one per lane)
+constexpr int kCols = 64;         // columns of C per tile
+constexpr int kRowsPerPass = 8;   // blockDim.y
+constexpr int kColSteps = kCols / kRowsPerPass;
 
 template <typename T>
 struct GeamArgs {
@@ -59,51 +62,64 @@ __device__ __forceinline__ double combine(bool use_a, double ta, bool use_b, dou
   return v;
 }
 
-// Stages rows [r0, r0+32) x cols [c0, c0+32) of op(X) = X^T into s[row][col];
-// X[c + r * ldx] is op(X)[r][c], so lanes walk c (contiguous in X).
-template <typename T>
-__device__ __forceinline__ void stage_transposed(T (*s)[kTile + 1], const T* X, long long ldx,
-                                                 int m, int n, int r0, int c0) {
-  const int c = c0 + threadIdx.x;
+// One operand's values for the thread's kColSteps outputs of a tile (row r0 + lane,
+// columns c0 + ty + 8k).  Transposed: rows [r0, r0+32) x cols [c0, c0+64) of
+// op(X) = X^T go through s[row][col] first; X[c + r * ldx] is op(X)[r][c], so the
+// loads walk c (contiguous in X).  Untransposed: read straight into registers.
+// Every global load of the tile is issued before the caller's barrier.
+template <typename T, bool TRANS>
+__device__ __forceinline__ void load_operand(T (*s)[kCols + 1], T (&v)[kColSteps], const T* X,
+                                             long long ldx, int m, int n, int r0, int c0) {
+  if constexpr (TRANS) {
 #pragma unroll
-  for (int k = 0; k < kTile / kRowsPerPass; ++k) {
-    const int rr = threadIdx.y + k * kRowsPerPass;
-    const int r = r0 + rr;
-    if (r < m && c < n) s[rr][threadIdx.x] = X[c + static_cast<long long>(r) * ldx];
+    for (int k = 0; k < kTile / kRowsPerPass; ++k) {
+      const int rr = threadIdx.y + k * kRowsPerPass;
+      const int r = r0 + rr;
+#pragma unroll
+      for (int j = 0; j < kCols / kTile; ++j) {
+        const int c = c0 + threadIdx.x + j * kTile;
+        if (r < m && c < n)
+          s[rr][threadIdx.x + j * kTile] = X[c + static_cast<long long>(r) * ldx];
+      }
+    }
+  } else {
+    const int r = r0 + threadIdx.x;
+#pragma unroll
+    for (int k = 0; k < kColSteps; ++k) {
+      const int c = c0 + threadIdx.y + k * kRowsPerPass;
+      v[k] = (r < m && c < n) ? X[r + static_cast<long long>(c) * ldx] : T(0);
+    }
   }
+}
+
+template <typename T, bool TRANS>
+__device__ __forceinline__ T operand_at(T (*s)[kCols + 1], const T (&v)[kColSteps], int k) {
+  if constexpr (TRANS) return s[threadIdx.x][threadIdx.y + k * kRowsPerPass];
+  else return v[k];
 }
 
 template <typename T, bool TA, bool TB>
 __global__ void __launch_bounds__(kTile* kRowsPerPass) geam_kernel(GeamArgs<T> g) {
-  __shared__ T sa[TA ? kTile : 1][kTile + 1];
-  __shared__ T sb[TB ? kTile : 1][kTile + 1];
+  __shared__ T sa[TA ? kTile : 1][kCols + 1];
+  __shared__ T sb[TB ? kTile : 1][kCols + 1];
   const T alpha = g.alpha_dev ? *g.alpha_dev : g.alpha;
   const T beta = g.beta_dev ? *g.beta_dev : g.beta;
   const bool use_a = alpha != T(0);
   const bool use_b = beta != T(0);
   for (long long t = blockIdx.x; t < g.tiles; t += gridDim.x) {
     const int r0 = static_cast<int>(t % g.tiles_m) * kTile;
-    const int c0 = static_cast<int>(t / g.tiles_m) * kTile;
-    if constexpr (TA || TB) {
-      if (TA && use_a) stage_transposed(sa, g.A, g.lda, g.m, g.n, r0, c0);
-      if (TB && use_b) stage_transposed(sb, g.B, g.ldb, g.m, g.n, r0, c0);
-      __syncthreads();
-    }
+    const int c0 = static_cast<int>(t / g.tiles_m) * kCols;
+    T va[kColSteps], vb[kColSteps];
+    if (use_a) load_operand<T, TA>(sa, va, g.A, g.lda, g.m, g.n, r0, c0);
+    if (use_b) load_operand<T, TB>(sb, vb, g.B, g.ldb, g.m, g.n, r0, c0);
+    if constexpr (TA || TB) __syncthreads();
     const int r = r0 + threadIdx.x;
 #pragma unroll
-    for (int k = 0; k < kTile / kRowsPerPass; ++k) {
-      const int cc = threadIdx.y + k * kRowsPerPass;
-      const int c = c0 + cc;
+    for (int k = 0; k < kColSteps; ++k) {
+      const int c = c0 + threadIdx.y + k * kRowsPerPass;
       if (r < g.m && c < g.n) {
-        T ta = T(0), tb = T(0);
-        if (use_a) {
-          const T a = TA ? sa[threadIdx.x][cc] : g.A[r + static_cast<long long>(c) * g.lda];
-          ta = mul_rn(alpha, a);
-        }
-        if (use_b) {
-          const T b = TB ? sb[threadIdx.x][cc] : g.B[r + static_cast<long long>(c) * g.ldb];
-          tb = mul_rn(beta, b);
-        }
+        const T ta = use_a ? mul_rn(alpha, operand_at<T, TA>(sa, va, k)) : T(0);
+        const T tb = use_b ? mul_rn(beta, operand_at<T, TB>(sb, vb, k)) : T(0);
         g.C[r + static_cast<long long>(c) * g.ldc] = combine(use_a, ta, use_b, tb);
       }
     }
@@ -111,8 +127,20 @@ __global__ void __launch_bounds__(kTile* kRowsPerPass) geam_kernel(GeamArgs<T> g
   }
 }
 
+// One wave: as many CTAs as the SMs hold at this instance's occupancy (its register
+// and shared-memory use differ by type and transposition), so that no CTA of the
+// grid-stride loop waits for a second wave.
 template <typename T, bool TA, bool TB>
-cudaError_t launch(const GeamArgs<T>& g, unsigned grid, cudaStream_t stream) {
+cudaError_t launch(const GeamArgs<T>& g, cudaStream_t stream) {
+  static const int per_sm = [] {
+    int b = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b, geam_kernel<T, TA, TB>,
+                                                      kTile * kRowsPerPass, 0) != cudaSuccess)
+      b = 0;
+    return b > 0 ? b : 1;
+  }();
+  const long long wave = static_cast<long long>(sm_count(current_device())) * per_sm;
+  const unsigned grid = static_cast<unsigned>(g.tiles < wave ? g.tiles : wave);
   geam_kernel<T, TA, TB><<<grid, dim3(kTile, kRowsPerPass), 0, stream>>>(g);
   return cudaGetLastError();
 }
@@ -136,17 +164,12 @@ cudaError_t launch_geam(bool trans_a, bool trans_b, int m, int n, T alpha, const
   g.m = m;
   g.n = n;
   g.tiles_m = (m + kTile - 1) / kTile;
-  g.tiles = static_cast<long long>(g.tiles_m) * ((n + kTile - 1) / kTile);
+  g.tiles = static_cast<long long>(g.tiles_m) * ((n + kCols - 1) / kCols);
   g.alpha = alpha;
   g.beta = beta;
-  const long long wave = static_cast<long long>(sm_count(current_device())) * kCtasPerSm;
-  const unsigned grid = static_cast<unsigned>(g.tiles < wave ? g.tiles : wave);
-  if (trans_a) {
-    return trans_b ? launch<T, true, true>(g, grid, stream)
-                   : launch<T, true, false>(g, grid, stream);
-  }
-  return trans_b ? launch<T, false, true>(g, grid, stream)
-                 : launch<T, false, false>(g, grid, stream);
+  if (trans_a)
+    return trans_b ? launch<T, true, true>(g, stream) : launch<T, true, false>(g, stream);
+  return trans_b ? launch<T, false, true>(g, stream) : launch<T, false, false>(g, stream);
 }
 
 template cudaError_t launch_geam<float>(bool, bool, int, int, float, const float*, const float*,

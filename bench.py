@@ -1059,10 +1059,14 @@ def suite_geam(s: Suite) -> dict:
     args = (h, 1, 0, m, n, C.byref(one), C.c_void_p(A.data_ptr()), n, C.byref(one),
             C.c_void_p(B.data_ptr()), m, C.c_void_p(Cm.data_ptr()), m)
     ms, launches = s.time(lambda: L.cublasSgeam(*args))
+    # the untransposed form (both operands read straight into registers), same bytes
+    args_nn = args[:1] + (0,) + args[2:7] + (m,) + args[8:]
+    ms_nn, _ = s.time(lambda: L.cublasSgeam(*args_nn))
     assert L.cublasDestroy_v2(h) == 0
     alg = 12 * m * n
     gbs = alg / (ms * 1e-3) / 1e9
     out = {"value": gbs, "unit": "GB/s", "ms": ms, "dtype": "f32",
+           "op_n_n": {"value": alg / (ms_nn * 1e-3) / 1e9, "unit": "GB/s", "ms": ms_nn},
            "config": f"{m} x {n}, op(A) T, op(B) N, {alg / 1e9:.2f} GB per call > L2",
            "roofline": s.roof("geam_kernel<float,1,0>", gbs, "hbm"), "launches": launches,
            "algorithmic_bytes_per_launch": alg}

@@ -9,14 +9,14 @@
 // nothing is contracted into an fma and the results are bit-identical to the CPU
 // restatement built with -ffp-contract=off.
 //
-// B200 layout: the m x n output is cut into 32 x 64 tiles, walked grid-stride by
-// one wave of CTAs (256 threads each, as many per SM as fit).  A warp always writes
-// 32 consecutive rows of one column of C (one 128-byte line for fp32).  An
-// untransposed operand is read the same way, into registers.  A transposed
-// operand is read along its own columns (rows of op(X)) into a 32 x 65 shared
-// tile and read back across it, so both its global reads and the writes of C stay
-// coalesced.  All of a tile's loads (16 per thread) are issued before its one
-// barrier, so the tile waits on memory once.
+// B200 layout: the m x n output is cut into 64 x 64 tiles (32 x 64 for fp64), walked grid-stride by
+// one wave of CTAs (256 threads each, as many per SM as fit).  A warp writes 64
+// consecutive rows of one column of C (two 128-byte lines for fp32, adjacent in
+// DRAM).  An untransposed operand is read the same way, into registers.  A
+// transposed operand is read along its own columns (rows of op(X)), 64 elements
+// at a time, into a 64 x 65 (fp64: 32 x 65) shared tile and read back across it, so both its
+// global reads and the writes of C stay coalesced.  All of a tile's loads (up to 32
+// per thread) are issued before its one barrier, so the tile waits on memory once.
 #include "blas/geam.hpp"
 
 #include <cuda_runtime.h>
@@ -26,10 +26,15 @@
 namespace mb200::blas {
 namespace {
 
-constexpr int kTile = 32;         // rows of C per tile (one per lane)
+constexpr int kLanes = 32;
 constexpr int kCols = 64;         // columns of C per tile
 constexpr int kRowsPerPass = 8;   // blockDim.y
 constexpr int kColSteps = kCols / kRowsPerPass;
+// Rows of C per tile: 256 bytes of a column (64 fp32, 32 fp64), one or two per lane.
+template <typename T>
+constexpr int kTile = 256 / static_cast<int>(sizeof(T));
+template <typename T>
+constexpr int kRowReps = kTile<T> / kLanes;
 
 template <typename T>
 struct GeamArgs {
@@ -62,65 +67,74 @@ __device__ __forceinline__ double combine(bool use_a, double ta, bool use_b, dou
   return v;
 }
 
-// One operand's values for the thread's kColSteps outputs of a tile (row r0 + lane,
-// columns c0 + ty + 8k).  Transposed: rows [r0, r0+32) x cols [c0, c0+64) of
-// op(X) = X^T go through s[row][col] first; X[c + r * ldx] is op(X)[r][c], so the
-// loads walk c (contiguous in X).  Untransposed: read straight into registers.
-// Every global load of the tile is issued before the caller's barrier.
+// One operand's values for the thread's kRowReps x kColSteps outputs of a tile
+// (rows r0 + lane + 32i, columns c0 + ty + 8k).  Transposed: rows [r0, r0+kTile) x
+// cols [c0, c0+64) of op(X) = X^T go through s[row][col] first; X[c + r * ldx] is
+// op(X)[r][c], so the loads walk c (contiguous in X).  Untransposed: read straight
+// into registers.  Every global load of the tile is issued before the caller's
+// barrier.
 template <typename T, bool TRANS>
-__device__ __forceinline__ void load_operand(T (*s)[kCols + 1], T (&v)[kColSteps], const T* X,
-                                             long long ldx, int m, int n, int r0, int c0) {
+__device__ __forceinline__ void load_operand(T (*s)[kCols + 1], T (&v)[kRowReps<T>][kColSteps],
+                                             const T* X, long long ldx, int m, int n, int r0,
+                                             int c0) {
   if constexpr (TRANS) {
 #pragma unroll
-    for (int k = 0; k < kTile / kRowsPerPass; ++k) {
+    for (int k = 0; k < kTile<T> / kRowsPerPass; ++k) {
       const int rr = threadIdx.y + k * kRowsPerPass;
       const int r = r0 + rr;
 #pragma unroll
-      for (int j = 0; j < kCols / kTile; ++j) {
-        const int c = c0 + threadIdx.x + j * kTile;
+      for (int j = 0; j < kCols / kLanes; ++j) {
+        const int c = c0 + threadIdx.x + j * kLanes;
         if (r < m && c < n)
-          s[rr][threadIdx.x + j * kTile] = X[c + static_cast<long long>(r) * ldx];
+          s[rr][threadIdx.x + j * kLanes] = X[c + static_cast<long long>(r) * ldx];
       }
     }
   } else {
-    const int r = r0 + threadIdx.x;
 #pragma unroll
     for (int k = 0; k < kColSteps; ++k) {
       const int c = c0 + threadIdx.y + k * kRowsPerPass;
-      v[k] = (r < m && c < n) ? X[r + static_cast<long long>(c) * ldx] : T(0);
+#pragma unroll
+      for (int i = 0; i < kRowReps<T>; ++i) {
+        const int r = r0 + threadIdx.x + i * kLanes;
+        v[i][k] = (r < m && c < n) ? X[r + static_cast<long long>(c) * ldx] : T(0);
+      }
     }
   }
 }
 
 template <typename T, bool TRANS>
-__device__ __forceinline__ T operand_at(T (*s)[kCols + 1], const T (&v)[kColSteps], int k) {
-  if constexpr (TRANS) return s[threadIdx.x][threadIdx.y + k * kRowsPerPass];
-  else return v[k];
+__device__ __forceinline__ T operand_at(T (*s)[kCols + 1], const T (&v)[kRowReps<T>][kColSteps],
+                                        int i, int k) {
+  if constexpr (TRANS) return s[threadIdx.x + i * kLanes][threadIdx.y + k * kRowsPerPass];
+  else return v[i][k];
 }
 
 template <typename T, bool TA, bool TB>
-__global__ void __launch_bounds__(kTile* kRowsPerPass) geam_kernel(GeamArgs<T> g) {
-  __shared__ T sa[TA ? kTile : 1][kCols + 1];
-  __shared__ T sb[TB ? kTile : 1][kCols + 1];
+__global__ void __launch_bounds__(kLanes* kRowsPerPass, 4) geam_kernel(GeamArgs<T> g) {
+  __shared__ T sa[TA ? kTile<T> : 1][kCols + 1];
+  __shared__ T sb[TB ? kTile<T> : 1][kCols + 1];
   const T alpha = g.alpha_dev ? *g.alpha_dev : g.alpha;
   const T beta = g.beta_dev ? *g.beta_dev : g.beta;
   const bool use_a = alpha != T(0);
   const bool use_b = beta != T(0);
   for (long long t = blockIdx.x; t < g.tiles; t += gridDim.x) {
-    const int r0 = static_cast<int>(t % g.tiles_m) * kTile;
+    const int r0 = static_cast<int>(t % g.tiles_m) * kTile<T>;
     const int c0 = static_cast<int>(t / g.tiles_m) * kCols;
-    T va[kColSteps], vb[kColSteps];
+    T va[kRowReps<T>][kColSteps], vb[kRowReps<T>][kColSteps];
     if (use_a) load_operand<T, TA>(sa, va, g.A, g.lda, g.m, g.n, r0, c0);
     if (use_b) load_operand<T, TB>(sb, vb, g.B, g.ldb, g.m, g.n, r0, c0);
     if constexpr (TA || TB) __syncthreads();
-    const int r = r0 + threadIdx.x;
 #pragma unroll
     for (int k = 0; k < kColSteps; ++k) {
       const int c = c0 + threadIdx.y + k * kRowsPerPass;
-      if (r < g.m && c < g.n) {
-        const T ta = use_a ? mul_rn(alpha, operand_at<T, TA>(sa, va, k)) : T(0);
-        const T tb = use_b ? mul_rn(beta, operand_at<T, TB>(sb, vb, k)) : T(0);
-        g.C[r + static_cast<long long>(c) * g.ldc] = combine(use_a, ta, use_b, tb);
+#pragma unroll
+      for (int i = 0; i < kRowReps<T>; ++i) {
+        const int r = r0 + threadIdx.x + i * kLanes;
+        if (r < g.m && c < g.n) {
+          const T ta = use_a ? mul_rn(alpha, operand_at<T, TA>(sa, va, i, k)) : T(0);
+          const T tb = use_b ? mul_rn(beta, operand_at<T, TB>(sb, vb, i, k)) : T(0);
+          g.C[r + static_cast<long long>(c) * g.ldc] = combine(use_a, ta, use_b, tb);
+        }
       }
     }
     if constexpr (TA || TB) __syncthreads();  // the next tile overwrites the staging tiles
@@ -135,13 +149,13 @@ cudaError_t launch(const GeamArgs<T>& g, cudaStream_t stream) {
   static const int per_sm = [] {
     int b = 0;
     if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b, geam_kernel<T, TA, TB>,
-                                                      kTile * kRowsPerPass, 0) != cudaSuccess)
+                                                      kLanes * kRowsPerPass, 0) != cudaSuccess)
       b = 0;
     return b > 0 ? b : 1;
   }();
   const long long wave = static_cast<long long>(sm_count(current_device())) * per_sm;
   const unsigned grid = static_cast<unsigned>(g.tiles < wave ? g.tiles : wave);
-  geam_kernel<T, TA, TB><<<grid, dim3(kTile, kRowsPerPass), 0, stream>>>(g);
+  geam_kernel<T, TA, TB><<<grid, dim3(kLanes, kRowsPerPass), 0, stream>>>(g);
   return cudaGetLastError();
 }
 
@@ -163,7 +177,7 @@ cudaError_t launch_geam(bool trans_a, bool trans_b, int m, int n, T alpha, const
   g.ldc = ldc;
   g.m = m;
   g.n = n;
-  g.tiles_m = (m + kTile - 1) / kTile;
+  g.tiles_m = (m + kTile<T> - 1) / kTile<T>;
   g.tiles = static_cast<long long>(g.tiles_m) * ((n + kCols - 1) / kCols);
   g.alpha = alpha;
   g.beta = beta;

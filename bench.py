@@ -14,9 +14,15 @@ offset r * 2 * 2^30 words), so per-GPU work is fixed and there is no collective
 on the data path ("scaling": "weak").  Timing is on the device with CUDA events,
 barrier + synchronize on both sides, max over ranks.
 
-``--impl reference`` times the reference's CPU path for the same workload: the
-reference cannot be built off macOS, so it runs the oracle's restatement of its
-host generator (oracle/philox.cpp) on all host cores, each step a bounded sample.
+``--impl reference`` times the reference's CPU path for the same workload: its own
+host generator (libraries/rand/src/curand_context.mm, compiled unmodified into
+oracle/_ref by oracle/ref/build.py) on all host cores, one generator per thread
+on consecutive Philox-block slices of each call (the oracle restatement
+oracle/philox.cpp where that library is absent).  N > 1 adds the strong-scaling
+split of the same two calls and the multi-GPU paths of the other routines
+(batch-sharded FFT / GEMM / conv / softmax and the row-block SpMV with its x
+exchange); the final line carries a compact summary of every routine, the full
+per-routine records go to stderr, one JSON line each.
 """
 
 from __future__ import annotations
@@ -43,7 +49,7 @@ BYTES_PER_STEP = 2 * BYTES_PER_CALL
 METRIC = ("RNG HBM GB/s: Philox4x32-10 curandGenerateUniform + curandGenerateNormal, "
           "2^30 fp32 each, seed 1234")
 UNIT = "GB/s"
-CPU_SAMPLE_WORDS = 1 << 30  # per call: the full config size (about 1.5 s on 16 host cores)
+CPU_SAMPLE_WORDS = 1 << 30  # per call: the full config size (about 1.3 s on 16 host cores)
 
 
 def _peaks() -> dict:
@@ -223,14 +229,47 @@ def run_ours(args) -> None:
     if rank == 0 and world == 1 and not args.no_cpu:
         cpu = cpu_baseline()
 
+    # ---- strong scaling of the same workload (N > 1): the config's two 2^30-word calls
+    # split over the ranks, rank r drawing words [r n/N, (r+1) n/N) of each call
+    strong = None
+    if world > 1:
+        part = N_WORDS // world
+        ps = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+
+        def sstep():
+            assert L.curandSetGeneratorOffset(gen, rank * part) == 0
+            assert L.curandGenerateUniform(gen, pu, part) == 0
+            assert L.curandSetGeneratorOffset(gen, N_WORDS + rank * part) == 0
+            assert L.curandGenerateNormal(gen, pn, part, C.c_float(0.0), C.c_float(1.0)) == 0
+        for _ in range(args.warmup):
+            sstep()
+        barrier()
+        ps[0].record(stream)
+        for _ in range(args.steps):
+            sstep()
+        ps[1].record(stream)
+        barrier()
+        st_ms = torch.tensor([ps[0].elapsed_time(ps[1]) / args.steps], device="cuda")
+        dist.all_reduce(st_ms, op=dist.ReduceOp.MAX)
+        strong = {"value": BYTES_PER_STEP / (float(st_ms.item()) * 1e-3) / 1e9, "unit": UNIT,
+                  "ms_per_step": float(st_ms.item()), "scaling": "strong",
+                  "partition": f"the config's 2 x 2^30 words split {world} ways by counter range"}
+
     assert L.curandDestroyGenerator(gen) == 0
     del uni, nor
     torch.cuda.empty_cache()
     suite = None
-    if world == 1 and args.suite != "none":
-        names = list(SUITE) if args.suite == "all" else args.suite.split(",")
-        suite = run_suite(names, args, torch)
-    if rank == 0:
+    if args.suite != "none":
+        if world == 1:
+            names = list(SUITE) if args.suite == "all" else args.suite.split(",")
+            suite = run_suite(names, args, torch)
+        else:
+            names = list(SHARDED) + ["spmv_dist"] if args.suite == "all" else \
+                args.suite.split(",")
+            suite = run_suite_sharded(names, args, torch, dist, world, rank, local)
+    if rank == 0 and suite:
+        for name, res in suite.items():  # full per-routine records, one JSON line each
+            print(json.dumps({"routine": name, **res}), file=sys.stderr, flush=True)
         peaks = _peaks()
         mu, mn = statistics.mean(uni_ms), statistics.mean(nor_ms)
         dom_name, dom_ms = ("philox_fill<normal>", mn) if mn >= mu else ("philox_fill<uniform>", mu)
@@ -258,7 +297,9 @@ def run_ours(args) -> None:
             "clocks": clk.summary(),
             "e2e": e2e,
             "cpu_baseline": cpu,
-            "suite": suite,
+            "strong": strong,
+            "suite_summary": summarize(suite),
+            "suite_summary_fields": ["value", "unit", "roofline frac (of measured)", "ms per call"],
         }
         print(json.dumps(line), flush=True)
     if world > 1:
@@ -964,7 +1005,7 @@ def _blas_handle(s):
 
 
 def suite_level1(s: Suite, op: str) -> dict:
-    """cuBLAS level 1 (SURVEY 8f): saxpy / sdot on 2^28 fp32 elements (1.07 GB per
+    """cuBLAS level 1: saxpy / sdot on 2^28 fp32 elements (1.07 GB per
     vector, larger than L2), uniform[-1, 1] from seed 5."""
     from muda_b200 import synth
     torch = s.torch
@@ -1006,7 +1047,7 @@ def suite_level1(s: Suite, op: str) -> dict:
 
 
 def suite_gemv(s: Suite, trans: bool) -> dict:
-    """cuBLAS level 2 (SURVEY 8f): sgemv on a 16384 x 16384 column-major fp32 matrix
+    """cuBLAS level 2: sgemv on a 16384 x 16384 column-major fp32 matrix
     (1.07 GB), alpha 1, beta 0, uniform[-1, 1] from seed 6."""
     from muda_b200 import synth
     torch = s.torch
@@ -1072,15 +1113,17 @@ def suite_geam(s: Suite) -> dict:
            "algorithmic_bytes_per_launch": alg}
     if s.cpu:
         import oracle
-        cols = 256
         Ah = A.cpu().numpy()
-        Bh = B[: m * cols].cpu().numpy()
-        Ch = np.zeros(m * cols, np.float32)
-        dt = cpu_time(lambda: oracle.geam(np.float32, True, False, m, cols, 1.0, Ah, n, 1.0,
-                                          Bh, m, Ch, m))
-        out["cpu_baseline"] = {"value": 12 * m * cols / dt / 1e9, "unit": "GB/s", "cores": 1,
+        Bh = B.cpu().numpy()
+        Ch = np.zeros(m * n, np.float32)
+        Ch.fill(1.0)
+        cores = os.cpu_count() or 1
+        dt = cpu_time(lambda: oracle.geam(np.float32, True, False, m, n, 1.0, Ah, n, 1.0,
+                                          Bh, m, Ch, m, threads=cores))
+        out["cpu_baseline"] = {"value": alg / dt / 1e9, "unit": "GB/s", "cores": cores,
                                "kind": "port",
-                               "sample": f"{cols} of {n} columns, oracle/blas12.cpp loop"}
+                               "sample": "full problem, oracle/blas12.cpp column loop split over "
+                                         "host threads"}
     return out
 
 SUITE = {
@@ -1121,18 +1164,51 @@ def run_suite(names, args, torch) -> dict:
     return out
 
 
-def cpu_baseline() -> dict:
-    """The reference's host generator path (oracle restatement), all host cores."""
-    import oracle
+def _cpu_generator():
+    """The reference's host generator for the CPU legs: its own curand_context.mm
+    compiled by oracle/ref/build.py ("reference"), else the oracle's restatement of it
+    ("port").  Returns (kind, description, uniform(out, offset), normal(out, offset))."""
     threads = os.cpu_count() or 1
+    import oracle.ref as ref
+    if ref.available():
+        def uni(out, offset):
+            ref.generate_parallel(ref.UNIFORM, SEED, offset, len(out), threads=threads, out=out)
+
+        def nor(out, offset):
+            ref.generate_parallel(ref.NORMAL, SEED, offset, len(out), 0.0, 1.0, threads=threads,
+                                  out=out)
+        return ("reference", "the reference's GenerateHostUniform / GenerateHostNormal "
+                "(libraries/rand/src/curand_context.mm, compiled unmodified by "
+                "oracle/ref/build.py), one generator per host thread on consecutive "
+                "Philox-block slices of the call", uni, nor)
+    import oracle
+
+    def uni_p(out, offset):
+        out[:] = oracle.generate_uniform(SEED, offset, len(out), threads=threads)[0]
+
+    def nor_p(out, offset):
+        out[:] = oracle.generate_normal(SEED, offset, len(out), 0.0, 1.0, threads=threads)[0]
+    return ("port", "oracle/philox.cpp, the restatement of "
+            "libraries/rand/src/curand_context.mm:42-185", uni_p, nor_p)
+
+
+def cpu_baseline() -> dict:
+    """The reference's host generator path on all host cores, the config's two calls."""
+    threads = os.cpu_count() or 1
+    kind, what, uni, nor = _cpu_generator()
+    hu = np.empty(CPU_SAMPLE_WORDS, np.float32)
+    hn = np.empty(CPU_SAMPLE_WORDS, np.float32)
+    uni(hu[: 1 << 20], 0)  # touch the code paths once
+    hu.fill(0.0)
+    hn.fill(0.0)
     t0 = time.perf_counter()
-    oracle.generate_uniform(SEED, 0, CPU_SAMPLE_WORDS, threads=threads)
-    oracle.generate_normal(SEED, 4 * CPU_SAMPLE_WORDS, CPU_SAMPLE_WORDS, 0.0, 1.0, threads=threads)
+    uni(hu, 0)
+    nor(hn, CPU_SAMPLE_WORDS)
     dt = time.perf_counter() - t0
     return {"value": 2 * 4 * CPU_SAMPLE_WORDS / dt / 1e9, "unit": UNIT, "cores": threads,
-            "kind": "port", "seconds": dt,
+            "kind": kind, "seconds": dt,
             "sample": f"uniform + normal, 2^{CPU_SAMPLE_WORDS.bit_length() - 1} words each "
-                      f"(1/{N_WORDS // CPU_SAMPLE_WORDS} of the config), oracle/philox.cpp"}
+                      f"(1/{N_WORDS // CPU_SAMPLE_WORDS} of the config), {what}"}
 
 
 def run_reference(args) -> None:
@@ -1141,15 +1217,19 @@ def run_reference(args) -> None:
     world = int(os.environ.get("WORLD_SIZE", "1"))
     if rank != 0:
         return
-    import oracle
     threads = os.cpu_count() or 1
+    kind, what, uni, nor = _cpu_generator()
+    hu = np.empty(CPU_SAMPLE_WORDS, np.float32)
+    hn = np.empty(CPU_SAMPLE_WORDS, np.float32)
+    hu.fill(0.0)  # fault the pages in before the timed region
+    hn.fill(0.0)
     for _ in range(args.warmup):
-        oracle.generate_uniform(SEED, 0, CPU_SAMPLE_WORDS // 8, threads=threads)
+        uni(hu[: CPU_SAMPLE_WORDS // 8], 0)
+        nor(hn[: CPU_SAMPLE_WORDS // 8], CPU_SAMPLE_WORDS)
     t0 = time.perf_counter()
     for _ in range(args.steps):
-        oracle.generate_uniform(SEED, 0, CPU_SAMPLE_WORDS, threads=threads)
-        oracle.generate_normal(SEED, 4 * CPU_SAMPLE_WORDS, CPU_SAMPLE_WORDS, 0.0, 1.0,
-                               threads=threads)
+        uni(hu, 0)
+        nor(hn, CPU_SAMPLE_WORDS)
     dt = (time.perf_counter() - t0) / args.steps
     value = 2 * 4 * CPU_SAMPLE_WORDS / dt / 1e9
     sample = (f"per step uniform + normal of 2^{CPU_SAMPLE_WORDS.bit_length() - 1} words each "
@@ -1159,18 +1239,37 @@ def run_reference(args) -> None:
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1e3,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "u32->f32",
         "data": "synthetic (counter-based RNG output)",
-        "config": {"workload": "configs[1]: Philox4x32-10 uniform 2^30 + normal(0,1) 2^30, seed 1234",
+        "config": {"workload": "configs[1]: Philox4x32-10 uniform 2^30 + normal(0,1) 2^30, "
+                               "seed 1234, offset 0, same generator and stream",
                    "sample": sample},
-        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
-                         "sample": sample + "; oracle/philox.cpp restates "
-                                   "libraries/rand/src/curand_context.mm:42-185 (the reference "
-                                   "builds only on macOS/Metal)"},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": kind,
+                         "sample": sample + "; " + what},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
 
 
 def run_spmv_dist(args) -> None:
+    """`--routine spmv_dist` under torchrun: spmv_dist_measure's line on rank 0."""
+    import torch
+    import torch.distributed as dist
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=__import__("datetime").timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    res = spmv_dist_measure(args, torch, dist if world > 1 else None, world, rank, local)
+    if rank == 0:
+        print(json.dumps({"routine": "spmv_dist", **res}), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+    if not res["y_identical_peer_vs_nccl"]:
+        raise SystemExit("peer exchange result differs from the NCCL exchange")
+
+
+def spmv_dist_measure(args, torch, dist, world: int, rank: int, local: int) -> dict:
     """configs[2] SpMV across the ranks of torchrun (strong scaling: the 4M x 4M matrix
     is fixed, its rows split into nnz-balanced blocks).  Each step gathers x into
     local HBM and runs the local cusparseSpMV.  Two exchanges are timed on the same
@@ -1178,25 +1277,14 @@ def run_spmv_dist(args) -> None:
     all_gather_into_tensor; both must give the same y, bit for bit.  The value is the
     faster of the two (named in config.exchange; the peer pull wins at 2 ranks, NCCL at
     8), the other is reported beside it.  Reported are the step time (max over ranks)
-    with and without the exchange."""
-    import torch
-    import torch.distributed as dist
-
+    with and without the exchange.  `dist` is None on one rank."""
     from muda_b200 import synth
     from muda_b200.dist_spmv import DistSpMV
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    torch.cuda.set_device(local)
     group = None
-    if world > 1:
-        dist.init_process_group("nccl", timeout=__import__("datetime").timedelta(seconds=120),
-                                device_id=torch.device("cuda", local))
     rows = (1 << 22) // args.scale
     mtx = synth.powerlaw_csr(torch, rows, rows, seed=7)
     nnz = mtx["nnz"]
-    dd = dist if world > 1 else None
-    arms = {ex: DistSpMV.from_full(torch, dd, group, mtx["row_offsets"], mtx["col_ind"],
+    arms = {ex: DistSpMV.from_full(torch, dist, group, mtx["row_offsets"], mtx["col_ind"],
                                    mtx["values"], rows, exchange=ex) for ex in ("peer", "nccl")}
     d = arms["peer"]
     x_local = d.x_slice(mtx["x"])
@@ -1247,42 +1335,99 @@ def run_spmv_dist(args) -> None:
     peer_wins = p_full <= n_full
     full, loc, gat = (p_full, p_loc, p_gat) if peer_wins else (n_full, n_loc, n_gat)
     other = ("nccl_all_gather", n_full, n_gat) if peer_wins else ("peer_pull", p_full, p_gat)
-    if rank == 0:
-        nz = shares.cpu().numpy()
-        print(json.dumps({
-            "routine": "spmv_dist", "metric": "SpMV GB/s (algorithmic bytes of the whole "
-            "matrix / step time, max over ranks)", "value": alg_bytes / (full * 1e-3) / 1e9,
-            "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": full, "scaling": "strong", "higher_is_better": True,
-            "dtype": "f32/i32", "data": "synthetic power-law CSR (configs[2])",
-            "config": {"workload": f"{rows} x {rows}, nnz {nnz}, rows split into "
-                                   f"{world} nnz-balanced blocks", "l2": "256 MB flush "
-                                   "before each step",
-                       "exchange": "peer-memory pull over NVLink (libmuda_peer)" if peer_wins
-                                   else "NCCL all_gather_into_tensor"},
-            "kernel_only": {"ms": loc, "GB/s": alg_bytes / (loc * 1e-3) / 1e9},
-            "exchange_ms": gat,
-            other[0]: {"ms_per_step": other[1], "exchange_ms": other[2],
-                       "GB/s": alg_bytes / (other[1] * 1e-3) / 1e9},
-            "y_identical_peer_vs_nccl": ok, "nnz_per_rank": [int(v) for v in nz],
-            "imbalance": float(nz.max() / max(float(nz.mean()), 1.0))}), flush=True)
+    nz = shares.cpu().numpy()
+    res = {
+        "metric": "SpMV GB/s (algorithmic bytes of the whole matrix / step time, max over "
+                  "ranks)", "value": alg_bytes / (full * 1e-3) / 1e9,
+        "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms": full, "ms_per_step": full, "scaling": "strong", "higher_is_better": True,
+        "dtype": "f32/i32", "data": "synthetic power-law CSR (configs[2])",
+        "config": {"workload": f"{rows} x {rows}, nnz {nnz}, rows split into "
+                               f"{world} nnz-balanced blocks", "l2": "256 MB flush "
+                               "before each step",
+                   "exchange": "peer-memory pull over NVLink (libmuda_peer)" if peer_wins
+                               else "NCCL all_gather_into_tensor"},
+        "kernel_only": {"ms": loc, "GB/s": alg_bytes / (loc * 1e-3) / 1e9},
+        "exchange_ms": gat, "exchange_share": gat / full if full > 0 else None,
+        other[0]: {"ms_per_step": other[1], "exchange_ms": other[2],
+                   "GB/s": alg_bytes / (other[1] * 1e-3) / 1e9},
+        "y_identical_peer_vs_nccl": ok, "nnz_per_rank": [int(v) for v in nz],
+        "imbalance": float(nz.max() / max(float(nz.mean()), 1.0)),
+        "roofline": {"bound": "hbm", "kernel": "spmv_csr_tiles (per rank) + x exchange",
+                     "frac": alg_bytes / (full * 1e-3) / 1e9 / world / _peaks()["hbm_gbs"],
+                     "peak": _peaks()["hbm_gbs"], "unit": "GB/s",
+                     "note": "whole-job GB/s / N / per-GPU measured HBM"}}
     for arm in arms.values():
         arm.close()
-    if world > 1:
-        dist.destroy_process_group()
-    if not ok:
-        raise SystemExit("peer exchange result differs from the NCCL exchange")
+    return res
+
+
+def summarize(suite: dict | None) -> dict | None:
+    """{routine: [value, unit, roofline frac, ms per call]} for the final line."""
+    if not suite:
+        return None
+    out = {}
+    for name, r in suite.items():
+        if "error" in r:
+            out[name] = ["error", r["error"][:120]]
+            continue
+        frac = (r.get("roofline") or {}).get("frac")
+        out[name] = [float(f"{r['value']:.5g}"), r["unit"],
+                     None if frac is None else round(float(frac), 3),
+                     None if r.get("ms") is None else float(f"{r['ms']:.4g}")]
+    return out
+
+
+def run_suite_sharded(names, args, torch, dist, world: int, rank: int, local: int) -> dict:
+    """The multi-GPU paths at N > 1, every rank in the same order: each batch-sharded
+    routine (1/N of the batch per rank, no collective on the data path) and the
+    row-block SpMV with its x exchange."""
+    out = {}
+    for name in names:
+        try:
+            if name == "spmv_dist":
+                out[name] = spmv_dist_measure(args, torch, dist, world, rank, local)
+            else:
+                out[name] = sharded_measure(name, args, torch, dist, world)
+        except Exception as e:  # recorded; the other routines still run
+            out[name] = {"error": f"{type(e).__name__}: {e}"}
+        torch.cuda.empty_cache()
+    return out
 
 
 SHARDED = ("fft", "gemm_bf16", "conv_bf16", "conv_f32", "softmax")
 
 
+def sharded_measure(name: str, args, torch, dist, world: int) -> dict:
+    """A batch-sharded suite routine across the ranks (strong scaling): each rank runs
+    1/world of the batch (FFT transforms, GEMM batch entries, conv images, softmax rows)
+    on its own GPU with no collective on the data path; every rank's timed region is
+    bracketed by a barrier, the step time is the max over ranks and the value is the
+    whole job's work over that time."""
+    def barrier():
+        dist.barrier()
+        torch.cuda.synchronize()
+
+    s = Suite(torch, max(3, args.steps // 4), args.warmup, False, args.scale)
+    s.shard, s.barrier = world, barrier
+    res = SUITE[name](s)
+    ms = torch.tensor([res["ms"]], device="cuda")
+    dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+    ms_max = float(ms.item())
+    total = res["value"] * res["ms"] / ms_max * world
+    roof = res.get("roofline") or {}
+    peak = roof.get("peak")
+    return {"value": total, "unit": res["unit"], "ms": ms_max, "n_gpus": world,
+            "per_rank_value": res["value"], "scaling": "strong", "config": res.get("config"),
+            "sharding": f"batch / {world} per rank", "dtype": res.get("dtype"),
+            "roofline": {"kernel": roof.get("kernel"), "bound": roof.get("bound"),
+                         "per_gpu_achieved": total / world, "peak": peak,
+                         "unit": roof.get("unit"),
+                         "frac": total / world / peak if peak else None}}
+
+
 def run_sharded(args) -> None:
-    """A batch-sharded suite routine across the ranks of torchrun (strong scaling): each
-    rank runs 1/world of the batch (FFT transforms, GEMM batch entries, conv images,
-    softmax rows) on its own GPU with no collective on the data path; the timed region
-    of every rank is bracketed by a barrier, the step time is the max over ranks and
-    the value is the whole job's work over that time."""
+    """`--routine NAME` under torchrun for a batch-sharded routine: its line on rank 0."""
     import torch
     import torch.distributed as dist
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -1291,24 +1436,9 @@ def run_sharded(args) -> None:
     torch.cuda.set_device(local)
     dist.init_process_group("nccl", timeout=__import__("datetime").timedelta(seconds=120),
                             device_id=torch.device("cuda", local))
-
-    def barrier():
-        dist.barrier()
-        torch.cuda.synchronize()
-
-    s = Suite(torch, max(3, args.steps // 4), args.warmup, False, args.scale)
-    s.shard, s.barrier = world, barrier
-    res = SUITE[args.routine](s)
-    ms = torch.tensor([res["ms"]], device="cuda")
-    dist.all_reduce(ms, op=dist.ReduceOp.MAX)
-    ms_max = float(ms.item())
-    total = res["value"] * res["ms"] / ms_max * world
+    res = sharded_measure(args.routine, args, torch, dist, world)
     if rank == 0:
-        print(json.dumps({"routine": args.routine, "n_gpus": world, "value": total,
-                          "unit": res["unit"], "ms_max_over_ranks": ms_max,
-                          "per_rank_value": res["value"], "scaling": "strong",
-                          "config": res.get("config"), "sharding": f"batch / {world} per rank",
-                          "dtype": res.get("dtype")}), flush=True)
+        print(json.dumps({"routine": args.routine, **res}), flush=True)
     dist.barrier()
     dist.destroy_process_group()
 

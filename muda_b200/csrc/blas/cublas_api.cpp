@@ -317,6 +317,28 @@ bool scalar(cublasPointerMode_t mode, const float* p, float* host, const float**
 // reference's argument checks and status codes, then the kernel.  In host pointer
 // mode an operand whose scalar is zero is not checked (nor read); in device
 // pointer mode the scalars are unknown here, so both operands must be valid.
+// True when the element spans of two column-major matrices share any byte.
+template <typename T>
+bool spans_overlap(const T* p, int rows, int cols, int ld, const T* c, int m, int n, int ldc) {
+  const auto a0 = reinterpret_cast<std::uintptr_t>(p);
+  const auto a1 = a0 + (static_cast<std::uintptr_t>(ld) * (cols - 1) + rows) * sizeof(T);
+  const auto c0 = reinterpret_cast<std::uintptr_t>(c);
+  const auto c1 = c0 + (static_cast<std::uintptr_t>(ldc) * (n - 1) + m) * sizeof(T);
+  return a0 < c1 && c0 < a1;
+}
+
+// In-place geam: C may be the operand itself when that operand is not transposed and
+// has C's leading dimension, since each element is then read and written by the same
+// thread.  Any other overlap between C and an operand that is read would let one tile
+// overwrite values that another tile has still to read (the tiles run in parallel,
+// where the reference's host loop runs in order), so it is refused.
+template <typename T>
+bool bad_alias(bool trans, const T* X, int rows, int cols, int ld, const T* C, int m, int n,
+               int ldc) {
+  if (!spans_overlap(X, rows, cols, ld, C, m, n, ldc)) return false;
+  return trans || X != C || ld != ldc;
+}
+
 template <typename T>
 cublasStatus_t run_geam(cublasHandle_t handle, cublasOperation_t transa,
                         cublasOperation_t transb, int m, int n, const T* alpha, const T* A,
@@ -723,6 +745,10 @@ cublasStatus_t run_geam(cublasHandle_t handle, cublasOperation_t transa,
   if ((device_mode || a != T(0)) && !matrix_ok(A, ta ? n : m, ta ? m : n, lda))
     return CUBLAS_STATUS_INVALID_VALUE;
   if ((device_mode || b != T(0)) && !matrix_ok(B, tb ? n : m, tb ? m : n, ldb))
+    return CUBLAS_STATUS_INVALID_VALUE;
+  if ((device_mode || a != T(0)) && bad_alias(ta, A, ta ? n : m, ta ? m : n, lda, C, m, n, ldc))
+    return CUBLAS_STATUS_INVALID_VALUE;
+  if ((device_mode || b != T(0)) && bad_alias(tb, B, tb ? n : m, tb ? m : n, ldb, C, m, n, ldc))
     return CUBLAS_STATUS_INVALID_VALUE;
   return status_of(mb200::blas::launch_geam<T>(ta, tb, m, n, a, a_dev, A, lda, b, b_dev, B, ldb,
                                                C, ldc, stream));

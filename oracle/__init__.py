@@ -493,7 +493,7 @@ def isamax(n, x, incx):
     return int(lib().oracle_isamax(n, _f32(x).ctypes.data, incx))
 
 
-def geam(dtype, transa, transb, m, n, alpha, A, lda, beta, B, ldb, C, ldc):
+def geam(dtype, transa, transb, m, n, alpha, A, lda, beta, B, ldb, C, ldc, threads=1):
     """Reference Sgeam / Dgeam (dtype np.float32 / np.float64) on column-major arrays;
     returns a copy of C with the m x n block written.  A or B may be None when its
     scalar is 0 (the reference does not read it)."""
@@ -503,7 +503,7 @@ def geam(dtype, transa, transb, m, n, alpha, A, lda, beta, B, ldb, C, ldc):
     B = np.zeros(1, dt) if B is None else np.ascontiguousarray(B, dt)
     fn = lib().oracle_sgeam if dt == np.float32 else lib().oracle_dgeam
     fn(1 if transa else 0, 1 if transb else 0, m, n, alpha, A.ctypes.data, lda, beta,
-       B.ctypes.data, ldb, C.ctypes.data, ldc)
+       B.ctypes.data, ldb, C.ctypes.data, ldc, threads)
     return C
 
 

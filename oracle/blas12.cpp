@@ -144,28 +144,30 @@ void oracle_sgemv(int trans, int m, int n, float alpha, const float* A, int64_t 
  * term = scalar != 0 ? scalar * x : +0 for each operand (the operand is not read
  * when its scalar is 0), C = term_a + term_b.  Column-major, op T reads X[c + r*ldx]. */
 void oracle_sgeam(int transa, int transb, int m, int n, float alpha, const float* A,
-                  int64_t lda, float beta, const float* B, int64_t ldb, float* C, int64_t ldc) {
-  for (int64_t c = 0; c < n; ++c) {
+                  int64_t lda, float beta, const float* B, int64_t ldb, float* C, int64_t ldc,
+                  int threads) {
+  // columns are independent; `threads` splits them for the multi-core CPU baseline
+  oracle_detail::parallel_for(0, n, threads, [&](std::int64_t c) {
     for (int64_t r = 0; r < m; ++r) {
       float ta = 0.0f, tb = 0.0f;
       if (alpha != 0.0f) ta = alpha * (transa ? A[c + r * lda] : A[r + c * lda]);
       if (beta != 0.0f) tb = beta * (transb ? B[c + r * ldb] : B[r + c * ldb]);
       C[r + c * ldc] = ta + tb;
     }
-  }
+  });
 }
 
 /* Dgeam, restated from the host loop at libraries/blas/src/cublas_level3.mm:906-927:
  * val = 0; val += alpha * a when alpha != 0; val += beta * b when beta != 0. */
 void oracle_dgeam(int transa, int transb, int m, int n, double alpha, const double* A,
                   int64_t lda, double beta, const double* B, int64_t ldb, double* C,
-                  int64_t ldc) {
-  for (int64_t c = 0; c < n; ++c) {
+                  int64_t ldc, int threads) {
+  oracle_detail::parallel_for(0, n, threads, [&](std::int64_t c) {
     for (int64_t r = 0; r < m; ++r) {
       double val = 0.0;
       if (alpha != 0.0) val += alpha * (transa ? A[c + r * lda] : A[r + c * lda]);
       if (beta != 0.0) val += beta * (transb ? B[c + r * ldb] : B[r + c * ldb]);
       C[r + c * ldc] = val;
     }
-  }
+  });
 }

@@ -7,11 +7,15 @@
  * the checker or the timed CPU baseline.
  *
  * Each function names the reference file:line it restates.  The reference
- * (AshitomW/MUDA) is Objective-C++ plus Metal and builds only on macOS
- * (CMakeLists.txt:14-15), so it cannot be compiled or run here; these oracles are
- * pinned instead against every known-answer test the reference's own test suite
- * holds for the path (tests/curand_test.cpp, cublas_test.cpp, cufft_test.cpp,
- * cusparse_test.cpp, cudnn_test.cpp), restated in tests/test_oracle_pins.py.
+ * (AshitomW/MUDA) is Objective-C++ plus Metal and its build runs only on macOS
+ * (CMakeLists.txt:14-15).  Its host Philox generator is plain C++, though:
+ * oracle/ref/build.py compiles that file (libraries/rand/src/curand_context.mm)
+ * unmodified into oracle/_ref/, and tests/test_oracle_ref.py holds the Philox
+ * restatement below to it bit for bit.  The other oracles restate Metal kernel
+ * arithmetic and are pinned against every known-answer test the reference's own
+ * test suite holds for the path (tests/curand_test.cpp, cublas_test.cpp,
+ * cufft_test.cpp, cusparse_test.cpp, cudnn_test.cpp), restated in
+ * tests/test_oracle_pins.py.
  *
  * Built with -ffp-contract=off so that every float operation rounds separately,
  * as written in the restated source.
@@ -119,10 +123,11 @@ void oracle_sreduce(int op, int n, const float* x, int incx, const float* y, int
                     float* out_f32, double* out_f64, double* out_abs);
 int oracle_isamax(int n, const float* x, int incx);
 void oracle_sgeam(int transa, int transb, int m, int n, float alpha, const float* A,
-                  int64_t lda, float beta, const float* B, int64_t ldb, float* C, int64_t ldc);
+                  int64_t lda, float beta, const float* B, int64_t ldb, float* C, int64_t ldc,
+                  int threads);
 void oracle_dgeam(int transa, int transb, int m, int n, double alpha, const double* A,
                   int64_t lda, double beta, const double* B, int64_t ldb, double* C,
-                  int64_t ldc);
+                  int64_t ldc, int threads);
 void oracle_sgemv(int trans, int m, int n, float alpha, const float* A, int64_t lda,
                   const float* x, int incx, float beta, float* y, int incy, double* exact,
                   double* absv, int threads);

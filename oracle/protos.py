@@ -44,9 +44,9 @@ _PROTOS: list[tuple[str, list, object]] = [
     ("oracle_sreduce", [C.c_int, C.c_int, vp, C.c_int, vp, C.c_int, vp, vp, vp], None),
     ("oracle_isamax", [C.c_int, vp, C.c_int], C.c_int),
     ("oracle_sgeam", [C.c_int, C.c_int, C.c_int, C.c_int, C.c_float, vp, C.c_int64, C.c_float,
-                      vp, C.c_int64, vp, C.c_int64], None),
+                      vp, C.c_int64, vp, C.c_int64, C.c_int], None),
     ("oracle_dgeam", [C.c_int, C.c_int, C.c_int, C.c_int, C.c_double, vp, C.c_int64,
-                      C.c_double, vp, C.c_int64, vp, C.c_int64], None),
+                      C.c_double, vp, C.c_int64, vp, C.c_int64, C.c_int], None),
     ("oracle_sgemv", [C.c_int, C.c_int, C.c_int, C.c_float, vp, C.c_int64, vp, C.c_int, C.c_float,
                       vp, C.c_int, vp, vp, C.c_int], None),
     ("oracle_fft_c2c", [vp, vp, C.c_int, vp, C.c_int64, C.c_int64, C.c_int64, C.c_int64,

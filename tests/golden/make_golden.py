@@ -2,12 +2,13 @@
 
 Run from the repository root:  python tests/golden/make_golden.py
 
-Philox goldens are produced twice, independently: by the C++ oracle
-(oracle/philox.cpp, a restatement of libraries/rand/src/curand_context.mm:42-185)
-and by the vectorised numpy restatement below; the script refuses to write a
-file unless both agree bit for bit.  The reference itself cannot run here (it
-builds only on macOS with Metal), so these files pin the oracle against drift
-and give the GPU tests fixed expected values.
+Philox goldens come from the reference's own host generator: its unmodified
+libraries/rand/src/curand_context.mm compiled as C++ by oracle/ref/build.py
+(GenerateHostUint / GenerateHostUniform / GenerateHostNormal, lines 75-185).
+Two independent restatements must agree with it bit for bit before a file is
+written: the C++ oracle (oracle/philox.cpp) and the vectorised numpy
+restatement below.  The committed file then pins the oracle, and gives the GPU
+tests fixed expected values, on machines where the reference tree is absent.
 """
 
 from __future__ import annotations
@@ -22,6 +23,8 @@ ROOT = Path(__file__).resolve().parents[2]
 sys.path.insert(0, str(ROOT))
 
 import oracle  # noqa: E402
+import oracle.ref as ref  # noqa: E402
+from oracle.ref.build import build as build_ref  # noqa: E402
 
 OUT = Path(__file__).resolve().parent
 
@@ -63,6 +66,8 @@ def uniform_numpy(words: np.ndarray) -> np.ndarray:
 
 
 def main() -> None:
+    if build_ref() is None:
+        raise SystemExit("the reference tree is needed: oracle/ref/build.py found none")
     cases = []
     # (seed, offset, n): config seed, reference test seeds, tails, odd offsets,
     # a counter that crosses 2^32 and a 64-bit seed.
@@ -71,21 +76,33 @@ def main() -> None:
         (42, 0, 67), (777, 1024, 33), (9999, 6, 19), (12345, 0, 16),
         (0xDEADBEEFCAFEF00D, (1 << 34) - 8, 40), (0, 0, 8),
     ]:
-        words, nxt = oracle.generate_uint(seed, offset, n)
-        ref = stream_numpy(seed, offset, n)
-        if not np.array_equal(words, ref):
-            raise SystemExit(f"oracle and numpy restatement disagree at seed={seed} offset={offset}")
-        uni, _ = oracle.generate_uniform(seed, offset, n)
-        if not np.array_equal(uni.view(np.uint32), uniform_numpy(ref).view(np.uint32)):
+        words, nxt = ref.generate(ref.UINT, seed, offset, n)
+        uni, nxt_u = ref.generate(ref.UNIFORM, seed, offset, n)
+        nor, nxt_n = ref.generate(ref.NORMAL, seed, offset, n, 0.0, 1.0)
+        o_words, o_nxt = oracle.generate_uint(seed, offset, n)
+        o_uni, _ = oracle.generate_uniform(seed, offset, n)
+        o_nor, _ = oracle.generate_normal(seed, offset, n, 0.0, 1.0)
+        np_words = stream_numpy(seed, offset, n)
+        if not (np.array_equal(words, o_words) and np.array_equal(words, np_words)
+                and nxt == o_nxt == nxt_u == nxt_n):
+            raise SystemExit(f"uint disagreement at seed={seed} offset={offset}")
+        if not (np.array_equal(uni.view(np.uint32), o_uni.view(np.uint32)) and
+                np.array_equal(uni.view(np.uint32), uniform_numpy(np_words).view(np.uint32))):
             raise SystemExit(f"uniform disagreement at seed={seed} offset={offset}")
-        nor, _ = oracle.generate_normal(seed, offset, n, 0.0, 1.0)
+        if not np.array_equal(nor.view(np.uint32), o_nor.view(np.uint32)):
+            raise SystemExit(f"normal disagreement at seed={seed} offset={offset}")
         cases.append({
             "seed": seed, "offset": offset, "n": n, "next_offset": nxt,
             "uint": [int(v) for v in words],
             "uniform_bits": [int(v) for v in uni.view(np.uint32)],
             "normal": [float(v) for v in nor],
+            "normal_bits": [int(v) for v in nor.view(np.uint32)],
         })
-    (OUT / "philox.json").write_text(json.dumps({"cases": cases}, indent=0) + "\n")
+    doc = {"source": "reference libraries/rand/src/curand_context.mm:42-185 compiled by "
+                     "oracle/ref/build.py (g++ -ffp-contract=off, glibc libm); the oracle and "
+                     "the numpy restatement agree bit for bit",
+           "cases": cases}
+    (OUT / "philox.json").write_text(json.dumps(doc, indent=0) + "\n")
     print(f"wrote {OUT / 'philox.json'} ({len(cases)} cases)")
 
 

@@ -120,25 +120,72 @@ def test_reference_gpu_moments(cuda, built):
     assert abs(z.mean()) < 0.03 and abs(z.var() - 1.0) < 0.05
 
 
-def test_full_size_stream_sampled(cuda, built):
-    """2^30 uniforms (the config size): 2^20 randomly sampled Philox blocks plus the
-    first and last blocks are bit-exact with the oracle."""
+def test_config_streams_against_reference(cuda, built):
+    """configs[1] at full size: seed 1234, curandGenerateUniform of 2^30 words from
+    offset 0, then curandGenerateNormal of 2^30 words on the same generator and
+    stream (offset 2^30, first counter 2^28).  2^16 randomly sampled Philox blocks
+    of each call plus the first and last blocks are compared with the reference's
+    own host generator (oracle/_ref, its curand_context.mm compiled here): uniform
+    bit for bit, normal within NORMAL_TOL * max(1, |z|).  The oracle restatement
+    is checked on the same blocks, so the test also runs where oracle/_ref is
+    missing."""
+    import oracle.ref as ref
     torch = cuda
     L = capi.curand()
     n = 1 << 30
-    buf = torch.empty(n, dtype=torch.float32, device="cuda")
+    u = torch.empty(n, dtype=torch.float32, device="cuda")
+    z = torch.empty(n, dtype=torch.float32, device="cuda")
     with curand_generator(1234, torch) as g:
-        assert L.curandGenerateUniform(g, C.c_void_p(buf.data_ptr()), n) == 0
+        assert L.curandGenerateUniform(g, C.c_void_p(u.data_ptr()), n) == 0
+        assert L.curandGenerateNormal(g, C.c_void_p(z.data_ptr()), n, C.c_float(0.0),
+                                      C.c_float(1.0)) == 0
+    torch.cuda.synchronize()
     blocks = n // 4
     rng = np.random.default_rng(0)
-    idx = np.unique(np.concatenate([rng.integers(0, blocks, 1 << 20), [0, blocks - 1]]))
-    got = buf.view(-1, 4)[torch.from_numpy(idx).cuda()].cpu().numpy().view(np.uint32)
-    words = oracle.philox_gather(idx.astype(np.uint64), 1234)
-    want = ((words.astype(np.float32) + np.float32(1.0)) *
-            np.float32(2.3283064365386963e-10)).astype(np.float32)
-    assert np.array_equal(got, want.view(np.uint32))
-    del buf
+    idx = np.unique(np.concatenate([rng.integers(0, blocks, 1 << 16), [0, 1, blocks - 1]]))
+    sel = torch.from_numpy(idx).cuda()
+    got_u = u.view(-1, 4)[sel].cpu().numpy()
+    got_z = z.view(-1, 4)[sel].cpu().numpy().astype(np.float64)
+    del u, z
     torch.cuda.empty_cache()
+    words = oracle.philox_gather(idx.astype(np.uint64), 1234)
+    want_u = ((words.astype(np.float32) + np.float32(1.0)) *
+              np.float32(2.3283064365386963e-10)).astype(np.float32)
+    assert np.array_equal(got_u.view(np.uint32), want_u.view(np.uint32))
+    offs = 4 * idx.astype(np.uint64)
+    if ref.available():
+        ref_u = ref.generate_at(ref.UNIFORM, 1234, offs, 4)
+        assert np.array_equal(got_u.view(np.uint32), ref_u.view(np.uint32))
+        want_z = ref.generate_at(ref.NORMAL, 1234, offs + np.uint64(n), 4).astype(np.float64)
+    else:
+        want_z = np.stack([oracle.generate_normal(1234, n + int(o), 4)[0] for o in offs])
+        want_z = want_z.astype(np.float64)
+    err = np.abs(got_z - want_z)
+    assert np.all(err <= NORMAL_TOL * np.maximum(1.0, np.abs(want_z))), f"max err {err.max()}"
+    exact = np.mean(got_z.astype(np.float32).view(np.uint32) == want_z.astype(np.float32).view(np.uint32))
+    print(f"config normal vs {'reference' if ref.available() else 'oracle'}: "
+          f"max |err| {err.max():.3e}, {exact:.2%} bit-identical")
+
+
+@pytest.mark.parametrize("seed,offset,n", [(1234, 0, 4099), (9, 6, 1001), (1234, 1 << 30, 65537)])
+def test_streams_against_reference(cuda, built, seed, offset, n):
+    """uint32, uniform and normal against the reference's compiled host generator."""
+    import oracle.ref as ref
+    if not ref.available():
+        pytest.skip("oracle/_ref/libcurand_ref.so missing: build() ran without the reference tree")
+    torch = cuda
+    L = capi.curand()
+    with curand_generator(seed, torch, offset=offset) as g:
+        got = _gen(torch, L.curandGenerate, g, n, torch.int32).view(np.uint32)
+    assert np.array_equal(got, ref.generate(ref.UINT, seed, offset, n)[0])
+    with curand_generator(seed, torch, offset=offset) as g:
+        got = _gen(torch, L.curandGenerateUniform, g, n, torch.float32)
+    assert np.array_equal(got.view(np.uint32), ref.generate(ref.UNIFORM, seed, offset, n)[0].view(np.uint32))
+    with curand_generator(seed, torch, offset=offset) as g:
+        got = _gen(torch, L.curandGenerateNormal, g, n, torch.float32, 0, C.c_float(0.0),
+                   C.c_float(1.0)).astype(np.float64)
+    want = ref.generate(ref.NORMAL, seed, offset, n)[0].astype(np.float64)
+    assert np.all(np.abs(got - want) <= NORMAL_TOL * np.maximum(1.0, np.abs(want)))
 
 
 def test_unaddressable_output_is_rejected(cuda, built):

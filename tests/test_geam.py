@@ -89,7 +89,9 @@ def test_geam_argument_checks(built):
     # Sgeam with an empty output and null C succeeds; Dgeam rejects a null C first
     assert L.cublasSgeam(h, 0, 0, 0, 4, one_f, p, 1, one_f, p, 1, None, 1) == ok
     assert L.cublasDgeam(h, 0, 0, 0, 4, one_d, p, 1, one_d, p, 1, None, 1) == inv
-    # zero scalars: A and B are not checked, C still is
+    # an unaddressable C is refused even when both scalars are 0 (the null A and B
+    # are then not examined; tests/test_geam.py::test_geam_zero_scalars_skip_operands
+    # shows on the GPU that they are skipped)
     assert L.cublasSgeam(h, 0, 0, 4, 4, zero_f, None, 4, zero_f, None, 4, p, 4) == inv
     assert L.cublasDestroy_v2(h) == 0
 
@@ -191,4 +193,88 @@ def test_sgeam_in_place_and_large_transpose(cuda, built):
     torch.cuda.synchronize()
     want = (A.t() * 0.5) + (B * 1.25)
     assert torch.equal(Cm, want)
+    assert L.cublasDestroy_v2(h) == 0
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("dtype", [F32, F64])
+def test_geam_zero_scalars_skip_operands(cuda, built, dtype):
+    """Host pointer mode, alpha = beta = 0, A = B = NULL and a valid C: the operands are
+    neither checked nor read (cublas_level3.mm:633-640) and C becomes +0."""
+    torch = cuda
+    L = capi.cublas()
+    h = C.c_void_p()
+    assert L.cublasCreate_v2(C.byref(h)) == 0
+    assert L.cublasSetStream_v2(h, C.c_void_p(stream_ptr(torch))) == 0
+    tdt = torch.float32 if dtype == F32 else torch.float64
+    ctype = C.c_float if dtype == F32 else C.c_double
+    fn = L.cublasSgeam if dtype == F32 else L.cublasDgeam
+    c = torch.full((37 * 19,), -5.0, dtype=tdt, device="cuda")
+    zero = C.byref(ctype(0.0))
+    assert fn(h, 0, 1, 37, 19, zero, None, 37, zero, None, 19, C.c_void_p(c.data_ptr()), 37) == 0
+    torch.cuda.synchronize()
+    got = c.cpu().numpy()
+    assert np.all(got == 0.0) and not np.any(np.signbit(got))
+    # only alpha 0: A NULL is fine, B is read
+    b = torch.full((37 * 19,), 2.0, dtype=tdt, device="cuda")
+    assert fn(h, 0, 0, 37, 19, zero, None, 37, C.byref(ctype(0.5)), C.c_void_p(b.data_ptr()),
+              37, C.c_void_p(c.data_ptr()), 37) == 0
+    torch.cuda.synchronize()
+    assert np.all(c.cpu().numpy() == 1.0)
+    assert L.cublasDestroy_v2(h) == 0
+
+
+@pytest.mark.gpu
+def test_geam_device_mode_requires_both_operands(cuda, built):
+    """Documented difference: in device pointer mode the scalars are read on the GPU
+    inside the kernel, so both operands must be addressable even when a scalar is 0.
+    The reference synchronises the stream, reads the scalar on the host and skips the
+    operand; here a NULL operand is CUBLAS_STATUS_INVALID_VALUE."""
+    torch = cuda
+    L = capi.cublas()
+    h = C.c_void_p()
+    assert L.cublasCreate_v2(C.byref(h)) == 0
+    assert L.cublasSetStream_v2(h, C.c_void_p(stream_ptr(torch))) == 0
+    assert L.cublasSetPointerMode_v2(h, capi.CUBLAS_POINTER_MODE_DEVICE) == 0
+    sc = torch.tensor([0.0, 1.0], dtype=torch.float32, device="cuda")
+    b = torch.ones(64, device="cuda")
+    c = torch.zeros(64, device="cuda")
+    st = L.cublasSgeam(h, 0, 0, 8, 8, C.c_void_p(sc.data_ptr()), None, 8,
+                       C.c_void_p(sc.data_ptr() + 4), C.c_void_p(b.data_ptr()), 8,
+                       C.c_void_p(c.data_ptr()), 8)
+    assert st == capi.CUBLAS_STATUS_INVALID_VALUE
+    assert L.cublasDestroy_v2(h) == 0
+
+
+@pytest.mark.gpu
+def test_geam_refuses_racing_overlap(cuda, built):
+    """In-place use is supported when C is the operand itself, not transposed, with the
+    same leading dimension.  C overlapping a transposed operand, or the same memory at
+    a different leading dimension, would race between tiles and is refused."""
+    torch = cuda
+    L = capi.cublas()
+    h = C.c_void_p()
+    assert L.cublasCreate_v2(C.byref(h)) == 0
+    assert L.cublasSetStream_v2(h, C.c_void_p(stream_ptr(torch))) == 0
+    one = C.byref(C.c_float(1.0))
+    zero = C.byref(C.c_float(0.0))
+    buf = torch.rand(256 * 256 + 512, device="cuda")
+    b = torch.rand(256 * 256, device="cuda")
+    p = C.c_void_p(buf.data_ptr())
+    pb = C.c_void_p(b.data_ptr())
+    inv = capi.CUBLAS_STATUS_INVALID_VALUE
+    assert L.cublasSgeam(h, 1, 0, 256, 256, one, p, 256, one, pb, 256, p, 256) == inv  # C == A^T
+    assert L.cublasSgeam(h, 0, 0, 256, 256, one, p, 257, one, pb, 256, p, 256) == inv  # other ld
+    shifted = C.c_void_p(buf.data_ptr() + 4 * 100)
+    assert L.cublasSgeam(h, 0, 0, 256, 256, one, p, 256, one, pb, 256, shifted, 256) == inv
+    # alpha 0 in host mode: A is not read, so its overlap does not matter
+    assert L.cublasSgeam(h, 1, 0, 256, 256, zero, p, 256, one, pb, 256, p, 256) == 0
+    # C == B, op N, same ld: supported in place
+    want = buf[:256 * 256].clone() * 0 + b  # alpha 0 above wrote C = B
+    torch.cuda.synchronize()
+    assert torch.equal(buf[:256 * 256], want)
+    assert L.cublasSgeam(h, 0, 0, 256, 256, zero, None, 256, C.byref(C.c_float(2.0)), p, 256,
+                         p, 256) == 0
+    torch.cuda.synchronize()
+    assert torch.equal(buf[:256 * 256], want * 2.0)
     assert L.cublasDestroy_v2(h) == 0

@@ -56,8 +56,13 @@ def _peaks() -> dict:
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
         d = json.loads(p.read_text())
-        return {"hbm_gbs": float(d["hbm_gbs"]), "source": "measured"}
-    return {"hbm_gbs": 6650.0, "source": "fallback"}
+        out = {"hbm_gbs": float(d["hbm_gbs"]), "source": "measured"}
+        for key in ("bf16_tflops", "bf16_tflops_sustained"):
+            if key in d:
+                out[key] = float(d[key])
+        return out
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0,
+            "source": "fallback"}
 
 
 def _traffic_record() -> dict | None:
@@ -900,7 +905,10 @@ def suite_softmax(s: Suite) -> dict:
 
 def suite_gemm_bf16(s: Suite) -> dict:
     """configs[4] GEMM: bf16 M = N = K = 8192, batch 8, fp32 accumulate, normal(0, 0.02)
-    seed 11; cublasGemmStridedBatchedEx(T, N) (both operands K-major), alpha 1, beta 0."""
+    seed 11, alpha 1, beta 0, through cublasGemmStridedBatchedEx.  The value is the
+    N,N call (both operands as stored by a column-major caller, the call a row-major
+    caller makes with its operands swapped: A is MN-major, B K-major); T,N (both
+    K-major), N,T and T,T are timed beside it on the same buffers."""
     from muda_b200 import capi, synth
     torch = s.torch
     m = n = k = 8192 // s.scale
@@ -914,17 +922,26 @@ def suite_gemm_bf16(s: Suite) -> dict:
     assert L.cublasCreate_v2(C.byref(h)) == 0
     assert L.cublasSetStream_v2(h, s.sp) == 0
     one, zero = C.c_float(1.0), C.c_float(0.0)
-    args = (h, 1, 0, m, n, k, C.byref(one), C.c_void_p(a.data_ptr()), 14, k, m * k,
-            C.c_void_p(b.data_ptr()), 14, k, n * k, C.byref(zero), C.c_void_p(c.data_ptr()), 14,
-            m, m * n, batch, 68, -1)
-    ms, launches = s.time(lambda: L.cublasGemmStridedBatchedEx(*args))
-    assert L.cublasDestroy_v2(h) == 0
+
+    def args(ta, tb):
+        return (h, ta, tb, m, n, k, C.byref(one), C.c_void_p(a.data_ptr()), 14, k if ta else m,
+                m * k, C.c_void_p(b.data_ptr()), 14, n if tb else k, n * k, C.byref(zero),
+                C.c_void_p(c.data_ptr()), 14, m, m * n, batch, 68, -1)
     flop = 2.0 * m * n * k * batch
+    layouts = {}
+    for name, ta, tb in (("NN", 0, 0), ("TN", 1, 0), ("NT", 0, 1), ("TT", 1, 1)):
+        a_ = args(ta, tb)
+        ms_l, launches_l = s.time(lambda: L.cublasGemmStridedBatchedEx(*a_))
+        layouts[name] = {"ms": ms_l, "TFLOP/s": flop / (ms_l * 1e-3) / 1e12,
+                         "launches": launches_l}
+    assert L.cublasDestroy_v2(h) == 0
+    ms, launches = layouts["NN"]["ms"], layouts["NN"]["launches"]
     tf = flop / (ms * 1e-3) / 1e12
     out = {"value": tf, "unit": "TFLOP/s", "ms": ms, "dtype": "bf16 (fp32 accumulate)",
-           "config": f"{m}x{n}x{k} x batch {batch}, TN, operands "
+           "config": f"{m}x{n}x{k} x batch {batch}, N,N (A MN-major, B K-major), operands "
                      f"{3 * m * k * batch * 2 / 1e9:.1f} GB",
-           "roofline": s.roof("gemm_tc_kernel<bf16>", tf, "tensor"), "launches": launches,
+           "roofline": s.roof("tc_gemm_kernel<GemmProblem<bf16,MN,K>>", tf, "tensor"),
+           "launches": launches, "layouts": layouts,
            "frac_of_sustained": tf / s.peaks.get("bf16_tflops_sustained", 1391.1)}
     if s.cpu:
         import oracle
@@ -935,9 +952,9 @@ def suite_gemm_bf16(s: Suite) -> dict:
         rows = rng.integers(0, m, ne).astype(np.int32)
         cols = (rng.integers(0, batch, ne) * n + rng.integers(0, n, ne)).astype(np.int32)
         Cs = np.zeros(m * n * batch, np.uint16)
-        dt = cpu_time(lambda: oracle.gemm("bf16", True, False, m, n, k, 1.0, A, k, B, k, 0.0, Cs,
-                                          m, stride_a=m * k, stride_b=n * k, stride_c=m * n,
-                                          batch=batch, entries=(rows, cols),
+        dt = cpu_time(lambda: oracle.gemm("bf16", False, False, m, n, k, 1.0, A, m, B, k, 0.0,
+                                          Cs, m, stride_a=m * k, stride_b=n * k,
+                                          stride_c=m * n, batch=batch, entries=(rows, cols),
                                           threads=os.cpu_count() or 1))
         out["cpu_baseline"] = {"value": 2.0 * k * ne / dt / 1e12, "unit": "TFLOP/s",
                                "cores": os.cpu_count(), "kind": "port",

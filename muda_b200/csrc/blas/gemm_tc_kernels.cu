@@ -6,9 +6,13 @@
 //
 // The main loop is the persistent warp-specialized kernel of tc_gemm_core.cuh
 // with 128 x 256 output tiles and a 4-stage TMA ring.  Tiles are visited in
-// groups of 16 tile-rows so the CTAs in flight share A and B panels in L2.  A and
-// B must be K-major (cublas transa = T, transb = N) with 16-byte aligned leading
-// dimensions; other layouts use the FFMA kernel.
+// groups of 16 tile-rows so the CTAs in flight share A and B panels in L2.  Every
+// transpose combination runs on it: a K-major operand (A with transa = T, B with
+// transb = N) arrives as one 128-byte-wide box per k-block, an MN-major operand
+// (A with transa = N, B with transb = T: M or N is the contiguous dimension) as
+// 64 x 64 boxes that the MMA reads through MN-major descriptors.  Leading
+// dimensions and batch strides must be multiples of 8 elements (16 bytes) and the
+// operands 16-byte aligned; other layouts and small problems use the FFMA kernel.
 //
 // fp32 GEMM (the reference's cublasSgemm arithmetic, cublas_kernels.metal:969-1006:
 // fp32 products accumulated in fp32, then C = alpha*acc + beta*C) runs on the same
@@ -42,10 +46,11 @@ constexpr int GROUP_M = 16;
 
 __device__ unsigned int g_gemm_tc_timeouts;
 
-template <typename T>
+template <typename T, bool AMN, bool BMN>
 struct GemmProblem {
-  CUtensorMap ma;  // K-major A: dims (k, m, batch)
-  CUtensorMap mb;  // K-major B: dims (k, n, batch)
+  static constexpr bool kAMn = AMN, kBMn = BMN;
+  CUtensorMap ma;  // A: dims (k, m, batch) K-major, (m, k, batch) MN-major
+  CUtensorMap mb;  // B: dims (k, n, batch) K-major, (n, k, batch) MN-major
   long long tiles_total;
   int num_kb;
   int m, n, tiles_m, tiles_n;
@@ -73,9 +78,26 @@ struct GemmProblem {
     c3[2] = (r % in_group) / gsz;
   }
 
+  // K-major: one box of (64 K) x (rows of the tile).  MN-major: boxes of 64 rows of
+  // the tile (128 bytes) x 64 K, one after another every 8 KB.
   __device__ void load(const int (&c3)[3], int kb, void* sa, void* sb, std::uint64_t* bar) const {
-    tc::tma_load_3d(sa, &ma, kb * tc::kBK, c3[1] * tc::kBM, a_batched ? c3[0] : 0, bar);
-    tc::tma_load_3d(sb, &mb, kb * tc::kBK, c3[2] * BN, b_batched ? c3[0] : 0, bar);
+    const int za = a_batched ? c3[0] : 0, zb = b_batched ? c3[0] : 0;
+    if constexpr (AMN) {
+#pragma unroll
+      for (int j = 0; j < tc::kBM / 64; ++j)
+        tc::tma_load_3d(static_cast<std::uint8_t*>(sa) + j * tc::kMnBoxBytes, &ma,
+                        c3[1] * tc::kBM + 64 * j, kb * tc::kBK, za, bar);
+    } else {
+      tc::tma_load_3d(sa, &ma, kb * tc::kBK, c3[1] * tc::kBM, za, bar);
+    }
+    if constexpr (BMN) {
+#pragma unroll
+      for (int j = 0; j < BN / 64; ++j)
+        tc::tma_load_3d(static_cast<std::uint8_t*>(sb) + j * tc::kMnBoxBytes, &mb,
+                        c3[2] * BN + 64 * j, kb * tc::kBK, zb, bar);
+    } else {
+      tc::tma_load_3d(sb, &mb, kb * tc::kBK, c3[2] * BN, zb, bar);
+    }
   }
 
   __device__ void scalars(float& a, float& b) const {
@@ -117,22 +139,24 @@ struct GemmProblem {
   }
 };
 
-// K-major operand: element (k, row) of batch z at base + k + row*ld + z*stride.
-bool make_map(CUtensorMap* map, const void* base, int fmt, int k, int rows, long long ld,
-              long long stride, int batch, int box_rows) {
+// Operand of `rows` rows (M or N) by k, element (k, row) of batch z at
+// base + k + row*ld + z*stride when K-major, base + row + k*ld + z*stride when
+// MN-major.  K-major boxes are 64 K x box_rows rows; MN-major boxes 64 rows x 64 K.
+bool make_map(CUtensorMap* map, const void* base, int fmt, bool mn_major, int k, int rows,
+              long long ld, long long stride, int batch, int box_rows) {
+  const long long inner = mn_major ? rows : k, outer = mn_major ? k : rows;
   long long zs = stride;
-  if (batch == 1 || zs == 0) zs = ((ld * rows * 2 + 15) / 16) * 8;  // z is always 0 then
-  const cuuint64_t dims[3] = {static_cast<cuuint64_t>(k), static_cast<cuuint64_t>(rows),
+  if (batch == 1 || zs == 0) zs = ((ld * outer * 2 + 15) / 16) * 8;  // z is always 0 then
+  const cuuint64_t dims[3] = {static_cast<cuuint64_t>(inner), static_cast<cuuint64_t>(outer),
                               static_cast<cuuint64_t>(batch)};
   const cuuint64_t strides[2] = {static_cast<cuuint64_t>(ld * 2), static_cast<cuuint64_t>(zs * 2)};
-  const cuuint32_t box[3] = {static_cast<cuuint32_t>(tc::kBK), static_cast<cuuint32_t>(box_rows),
-                             1u};
+  const cuuint32_t box[3] = {static_cast<cuuint32_t>(mn_major ? 64 : tc::kBK),
+                             static_cast<cuuint32_t>(mn_major ? tc::kBK : box_rows), 1u};
   return tc::encode_tiled(map, fmt, base, 3, dims, strides, box);
 }
 
 bool tc_supported(const GemmArgs& g) {
   if (g.type == Elem::kF32) return false;
-  if (!g.trans_a || g.trans_b) return false;  // both operands K-major
   if (g.k <= 0 || g.m <= 0 || g.n <= 0) return false;
   if ((g.lda * 2) % 16 != 0 || (g.ldb * 2) % 16 != 0) return false;
   if (g.batch > 1 && ((g.stride_a * 2) % 16 != 0 || (g.stride_b * 2) % 16 != 0)) return false;
@@ -160,11 +184,11 @@ unsigned int* timeout_counter() {
   return addr[dev];
 }
 
-template <typename T, int FMT>
+template <typename T, int FMT, bool AMN, bool BMN>
 cudaError_t run(const GemmArgs& g, cudaStream_t stream) {
-  GemmProblem<T> p{};
-  if (!make_map(&p.ma, g.a, FMT, g.k, g.m, g.lda, g.stride_a, g.batch, tc::kBM) ||
-      !make_map(&p.mb, g.b, FMT, g.k, g.n, g.ldb, g.stride_b, g.batch, BN))
+  GemmProblem<T, AMN, BMN> p{};
+  if (!make_map(&p.ma, g.a, FMT, AMN, g.k, g.m, g.lda, g.stride_a, g.batch, tc::kBM) ||
+      !make_map(&p.mb, g.b, FMT, BMN, g.k, g.n, g.ldb, g.stride_b, g.batch, BN))
     return cudaErrorNotSupported;
   p.m = g.m;
   p.n = g.n;
@@ -183,8 +207,18 @@ cudaError_t run(const GemmArgs& g, cudaStream_t stream) {
   p.beta_dev = g.beta_dev;
   unsigned int* to = timeout_counter();
   if (to == nullptr) return cudaErrorNotSupported;
-  return tc::launch_tc_gemm<GemmProblem<T>, BN, STAGES, FMT>(p, sm_count(current_device()), to,
-                                                             stream);
+  return tc::launch_tc_gemm<GemmProblem<T, AMN, BMN>, BN, STAGES, FMT>(
+      p, sm_count(current_device()), to, stream);
+}
+
+// A is MN-major when not transposed (column-major m x k), B when transposed.
+template <typename T, int FMT>
+cudaError_t run_layout(const GemmArgs& g, cudaStream_t stream) {
+  const bool amn = !g.trans_a, bmn = g.trans_b;
+  if (amn && bmn) return run<T, FMT, true, true>(g, stream);
+  if (amn) return run<T, FMT, true, false>(g, stream);
+  if (bmn) return run<T, FMT, false, true>(g, stream);
+  return run<T, FMT, false, false>(g, stream);
 }
 
 // ---------------------------------------------------------------- split tf32 (fp32)
@@ -514,7 +548,8 @@ const char* gemm_path_name(const GemmArgs& g) noexcept {
 
 cudaError_t launch_gemm_tc(const GemmArgs& g, cudaStream_t stream) noexcept {
   if (!tc_supported(g)) return cudaErrorNotSupported;
-  return g.type == Elem::kBF16 ? run<__nv_bfloat16, 1>(g, stream) : run<__half, 0>(g, stream);
+  return g.type == Elem::kBF16 ? run_layout<__nv_bfloat16, 1>(g, stream)
+                               : run_layout<__half, 0>(g, stream);
 }
 
 }  // namespace mb200::blas

@@ -32,6 +32,12 @@
 //   void store(const int (&c)[3], int row, int col0, const float (&v)[32], float alpha,
 //              float beta) const;                           // row in [0,128), 32 columns
 //
+// Operands are K-major by default.  A problem may declare `static constexpr bool
+// kAMn, kBMn`: an MN-major operand arrives as 64 x 64 boxes (64 M or N elements of
+// 128 bytes per K row, 8 KB per box, boxes along M/N every 8 KB), which the MMA
+// reads through MN-major descriptors (tc_ptx.cuh), each 16-element K step 16 rows
+// (2048 bytes) further on.  Only the 16-bit kernel (FMT 0 / 1) accepts them.
+//
 // Every mbarrier wait is bounded (tc_ptx.cuh).  A wait that runs out marks the CTA
 // aborted, counts the event in the problem's timeout counter, drains the copies and
 // MMAs the CTA issued (bounded), frees its tensor memory and returns.
@@ -42,6 +48,7 @@
 
 #include <atomic>
 #include <cstdint>
+#include <type_traits>
 
 #include "blas/tc_ptx.cuh"
 
@@ -55,6 +62,28 @@ constexpr int kStepBytes = 32;  // K bytes consumed by one MMA (16 x 16-bit, 8 x
 constexpr int kAcc = 2;
 constexpr int kThreads = 192;
 constexpr int kFmtTf32x3 = 2;
+
+// Operand majorness of a problem type (see above): K-major unless it says otherwise.
+template <class P, class = void>
+struct OperandMajor {
+  static constexpr bool a_mn = false, b_mn = false;
+};
+template <class P>
+struct OperandMajor<P, std::void_t<decltype(P::kAMn), decltype(P::kBMn)>> {
+  static constexpr bool a_mn = P::kAMn, b_mn = P::kBMn;
+};
+
+constexpr std::uint32_t kMnBoxBytes = 64 * kRowBytes;   // one 64 x 64 box of 16-bit elements
+constexpr std::uint32_t kMnStepBytes = 16 * kRowBytes;  // 16 K rows per MMA K step
+
+// Descriptor of K step k (16 elements) of an operand tile at shared address `base`.
+template <bool MN>
+__device__ __forceinline__ std::uint64_t operand_desc(std::uint32_t base, int k) {
+  if constexpr (MN)
+    return mnmajor_sw128_desc(base + static_cast<std::uint32_t>(k) * kMnStepBytes, kMnBoxBytes);
+  else
+    return kmajor_sw128_desc(base + static_cast<std::uint32_t>(k * kStepBytes));
+}
 
 template <int BN, int STAGES, int PLANES = 1>
 struct CoreShape {
@@ -146,7 +175,8 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(const __grid_const
   } else if (warp == 1) {
     if (lane == 0) {
       // ---------------- MMA issuer
-      constexpr std::uint32_t idesc = f16_idesc(FMT, kBM, BN);
+      constexpr bool AMN = OperandMajor<P>::a_mn, BMN = OperandMajor<P>::b_mn;
+      constexpr std::uint32_t idesc = f16_idesc(FMT, kBM, BN, AMN, BMN);
       int stage = 0;
       std::uint32_t phase = 0;
       int acc = 0;
@@ -169,11 +199,9 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(const __grid_const
           const std::uint32_t a0 = smem_addr(sa + stage * S::A_STAGE);
           const std::uint32_t b0 = smem_addr(sb + stage * S::B_STAGE);
 #pragma unroll
-          for (int k = 0; k < kRowBytes / kStepBytes; ++k) {
-            const std::uint32_t ak = a0 + k * kStepBytes, bk = b0 + k * kStepBytes;
-            mma_f16(d_tmem, kmajor_sw128_desc(ak), kmajor_sw128_desc(bk), idesc,
+          for (int k = 0; k < kRowBytes / kStepBytes; ++k)
+            mma_f16(d_tmem, operand_desc<AMN>(a0, k), operand_desc<BMN>(b0, k), idesc,
                     (kb | k) != 0 ? 1u : 0u);
-          }
           mma_commit(&empty[stage]);
           if (++stage == STAGES) {
             stage = 0;
@@ -253,6 +281,8 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
     tc_gemm_split_kernel(const __grid_constant__ P p, unsigned int* timeouts) {
   static_assert(BN == 256 || BN == 128 || BN == 64,
                 "the epilogue splits the tile into two halves of 32-column groups");
+  static_assert(!OperandMajor<P>::a_mn && !OperandMajor<P>::b_mn,
+                "split tf32 reads K-major planes only");
   constexpr int HC = BN / 2;  // columns per epilogue warp
   using S = CoreShape<BN, STAGES, 2>;
   extern __shared__ std::uint8_t smem_raw[];

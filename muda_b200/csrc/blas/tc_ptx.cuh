@@ -272,11 +272,32 @@ __device__ __forceinline__ std::uint64_t kmajor_sw128_desc(std::uint32_t saddr) 
   return d;
 }
 
+// Shared-memory matrix descriptor for an MN-major operand tile stored as the
+// 128-byte-swizzle MN-major atoms a 64 x 64 TMA box of 16-bit elements produces:
+// each K index is one 128-byte row of 64 consecutive M (or N) elements, 8 rows
+// form a 1024-byte atom, atoms follow each other along K every 1024 bytes (stride
+// byte offset) and 64-element column blocks along M/N every `mn_block_bytes`
+// (leading byte offset), version 1, layout SWIZZLE_128B.
+__device__ __forceinline__ std::uint64_t mnmajor_sw128_desc(std::uint32_t saddr,
+                                                            std::uint32_t mn_block_bytes) {
+  std::uint64_t d = 0;
+  d |= static_cast<std::uint64_t>((saddr >> 4) & 0x3FFFu);
+  d |= static_cast<std::uint64_t>((mn_block_bytes >> 4) & 0x3FFFu) << 16;  // leading offset
+  d |= static_cast<std::uint64_t>(1024u >> 4) << 32;                        // stride offset
+  d |= static_cast<std::uint64_t>(1u) << 46;
+  d |= static_cast<std::uint64_t>(2u) << 61;
+  return d;
+}
+
 // Instruction descriptor of kind::f16 / kind::tf32: fp32 accumulate, A/B of the
-// given format (0 = fp16, 1 = bf16, 2 = tf32), both K-major, tile M x N.
-__host__ __device__ constexpr std::uint32_t f16_idesc(int ab_format, int m, int n) {
+// given format (0 = fp16, 1 = bf16, 2 = tf32), tile M x N; a_mn / b_mn mark an
+// MN-major operand (bits 15 / 16; otherwise K-major).
+__host__ __device__ constexpr std::uint32_t f16_idesc(int ab_format, int m, int n,
+                                                      bool a_mn = false, bool b_mn = false) {
   return (1u << 4) | (static_cast<std::uint32_t>(ab_format) << 7) |
          (static_cast<std::uint32_t>(ab_format) << 10) |
+         (static_cast<std::uint32_t>(a_mn ? 1u : 0u) << 15) |
+         (static_cast<std::uint32_t>(b_mn ? 1u : 0u) << 16) |
          (static_cast<std::uint32_t>(n >> 3) << 17) | (static_cast<std::uint32_t>(m >> 4) << 24);
 }
 

@@ -379,6 +379,65 @@ def test_gpu_gemm_ex_tensor_core_layout(cuda, built, typ, m, n, k, batch, beta):
 
 
 @pytest.mark.gpu
+@pytest.mark.parametrize("typ", ["bf16", "f16"])
+@pytest.mark.parametrize("ta,tb", [(False, False), (True, False), (False, True), (True, True)])
+@pytest.mark.parametrize("m,n,k,batch,beta,pad", [(2048, 2048, 2048, 1, 0.0, 0),
+                                                  (1000, 777, 520, 2, 0.5, 8),
+                                                  (129, 2304, 72, 3, -1.0, 16),
+                                                  (4096, 136, 1000, 1, 0.0, 24)])
+def test_gpu_gemm_ex_tensor_core_all_layouts(cuda, built, typ, ta, tb, m, n, k, batch, beta, pad):
+    """Every transpose combination on the tcgen05 kernel: K-major operands (A with T,
+    B with N) and MN-major ones (A with N, B with T), partial tiles in M, N and K,
+    padded leading dimensions, batches, beta != 0.  Against the oracle's 16-bit GEMM
+    (cublas_kernels.metal:1008-1045): normwise 1e-2 per batch entry on 16384 sampled
+    entries (all entries when fewer), padding untouched."""
+    torch = cuda
+    rng = np.random.default_rng(m * 3 + n * 5 + k * 7 + 11 * ta + 13 * tb)
+    lda = (k if ta else m) + pad
+    ldb = (n if tb else k) + pad
+    ldc = m + 3
+    sa = lda * (m if ta else k) + 64
+    sb = ldb * (k if tb else n) + 128
+    sc = ldc * n + 5
+    conv = oracle.half_bits if typ == "f16" else oracle.bf16_bits
+    A16 = conv(rng.uniform(-1, 1, sa * batch).astype(np.float32))
+    B16 = conv(rng.uniform(-1, 1, sb * batch).astype(np.float32))
+    C16 = conv(rng.uniform(-1, 1, sc * batch).astype(np.float32))
+    dA, dB, dC = (torch.from_numpy(x.view(np.int16).copy()).cuda() for x in (A16, B16, C16))
+    dtype = capi.CUDA_R_16F if typ == "f16" else capi.CUDA_R_16BF
+    b = Blas(torch)
+    st = b.L.cublasGemmStridedBatchedEx(
+        b.h, OPS[ta], OPS[tb], m, n, k, C.byref(C.c_float(1.0)), C.c_void_p(dA.data_ptr()), dtype,
+        lda, sa, C.c_void_p(dB.data_ptr()), dtype, ldb, sb, C.byref(C.c_float(beta)),
+        C.c_void_p(dC.data_ptr()), dtype, ldc, sc, batch, capi.CUBLAS_COMPUTE_32F, -1)
+    torch.cuda.synchronize()
+    b.close()
+    assert st == 0
+    got = dC.cpu().numpy().view(np.uint16)
+    dec = (lambda v: v.view(np.float16).astype(np.float64)) if typ == "f16" else \
+        (lambda v: oracle.bf16_to_f32(v).astype(np.float64))
+    total = m * n * batch
+    ne = min(total, 16384)
+    pick = rng.choice(total, ne, replace=False) if ne < total else np.arange(total)
+    z, rem = pick // (m * n), pick % (m * n)
+    rows, cols = (rem % m).astype(np.int32), (rem // m)
+    want = C16.copy()
+    oracle.gemm(typ, ta, tb, m, n, k, 1.0, A16, lda, B16, ldb, beta, want, ldc, stride_a=sa,
+                stride_b=sb, stride_c=sc, batch=batch, entries=(rows, (z * n + cols).astype(np.int32)),
+                threads=16)
+    flat = z * sc + cols * ldc + rows
+    for zz in range(batch):
+        sel = flat[z == zz]
+        assert normwise(dec(got[sel]), dec(want[sel])) <= 1e-2, (zz, typ, ta, tb)
+    err = np.abs(dec(got[flat]) - dec(want[flat]))
+    assert np.all(err <= 2e-2 * np.abs(dec(want[flat])) + 0.05), float(err.max())
+    mask = np.ones(len(got), bool)
+    for zz in range(batch):
+        mask[(zz * sc + np.arange(n)[:, None] * ldc + np.arange(m)[None, :]).reshape(-1)] = False
+    assert np.array_equal(got[mask], C16[mask])
+
+
+@pytest.mark.gpu
 def test_gpu_hgemm_reference_pin(cuda, built):
     """tests/cublas_test.cpp:383-410: 16^3, A = 0.5, B = 0.25 -> 2.0 (fp16 scalars)."""
     torch = cuda

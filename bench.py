@@ -275,6 +275,7 @@ def run_ours(args) -> None:
     if rank == 0 and suite:
         for name, res in suite.items():  # full per-routine records, one JSON line each
             print(json.dumps({"routine": name, **res}), file=sys.stderr, flush=True)
+    if rank == 0:
         peaks = _peaks()
         mu, mn = statistics.mean(uni_ms), statistics.mean(nor_ms)
         dom_name, dom_ms = ("philox_fill<normal>", mn) if mn >= mu else ("philox_fill<uniform>", mu)

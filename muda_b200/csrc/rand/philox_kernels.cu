@@ -18,24 +18,24 @@
 // warp covering 512 contiguous bytes.  The grid is a whole number of waves over
 // the 148 SMs and strides over the output.
 //
-// The normal transform is instruction-issue bound, not memory bound, so it is
-// written for sm_100's packed fp32 pipe: the two Box-Muller pairs of a block are
-// the two lanes of add/mul/fma.rn.f32x2 (each lane rounded exactly as the scalar
-// instruction), and ln, sin and cos are evaluated by this file's own bounded-range
-// methods instead of the general-range library functions:
+// The normal transform is bound by instruction issue and by the heavy FMA pipe, which
+// Philox's twenty 32x32->64 multiplies per block already hold for 80 of the 91
+// cycles a warp-block may take at the HBM write rate.  So its fp32 work is written
+// to leave that pipe: the two Box-Muller pairs of a block are the two lanes of
+// sm_100's packed add/mul/fma.rn.f32x2 (each lane rounded exactly as the scalar
+// instruction), and -2 ln u, sin and cos come from the hardware's approximate
+// lg2 / sin / cos (XU pipe) wherever those are accurate enough, with this file's own
+// bounded-range series elsewhere (see kHw below):
 //   -2 ln u, u in (0, 1]: u = m 2^e with m in [sqrt(1/2), sqrt(2)), ln m =
 //      2 atanh(s) with s = (m-1)/(m+1), |s| <= 0.1716, atanh(s)/s as a quadratic in
-//      s^2 (4.7e-7 relative);
+//      s^2 (4.7e-7 relative); near u = 1 a series in d = u - 1;
 //   cos, sin of theta in [0, 2pi]: Cody-Waite reduction r = theta - j pi/2 with a
 //      two-term pi/2 (j <= 4), odd degree-7 and even degree-6 polynomials on
 //      |r| <= pi/4 (1e-8 and 3.3e-8 absolute), then the quadrant's swap and signs.
 // The polynomial coefficients are this file's own near-minimax fits (weighted
 // least squares on Chebyshev nodes, reweighted toward the largest error).
 // Against the reference formula evaluated with glibc's float functions the
-// result stays within 1e-6 absolute (scaled by max(1, |z|)).
-// The kernels are bound by the heavy FMA pipe, not by issue or memory: each
-// Philox round's two 32x32->64 multiplies hold it for 4 cycles per warp each,
-// and every packed fp32 instruction for 2.
+// result stays within 2e-6 * max(1, |z|).
 #include "rand/philox.hpp"
 
 #include <cuda_runtime.h>
@@ -150,12 +150,32 @@ __device__ __forceinline__ float sqrt_approx(float x) {
   asm("sqrt.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
   return r;
 }
+__device__ __forceinline__ float lg2_approx(float x) {
+  float r;
+  asm("lg2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
+  return r;
+}
+__device__ __forceinline__ float sin_approx(float x) {
+  float r;
+  asm("sin.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
+  return r;
+}
+__device__ __forceinline__ float cos_approx(float x) {
+  float r;
+  asm("cos.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
+  return r;
+}
 
 // Which stages of the transforms use the packed form (bit set) or scalar pairs.
 constexpr unsigned kPackConv = 1u;   // word -> uniform float
 constexpr unsigned kPackLog = 2u;    // -2 ln u
 constexpr unsigned kPackTrig = 4u;   // reduction and sin/cos polynomials
 constexpr unsigned kPackOut = 8u;    // radius products and the affine step
+// With kHw the normal transform takes -2 ln u and sin / cos from the hardware's
+// approximate lg2 / sin / cos (the XU pipe, off the FMA pipes that Philox's
+// multiplies fill), keeping this file's series for the inputs where those are not
+// accurate enough (see neg2_log_hw and polar2_hw).
+constexpr unsigned kHw = 16u;
 
 // (float(u) + 1.0f) * 2^-32 for two words.  Evaluated as fma(float(u), 2^-32, 2^-32):
 // scaling by a power of two commutes with rounding (no underflow: the sum is at
@@ -193,27 +213,39 @@ __device__ __forceinline__ Pair neg2_log(Pair u) {
   return fma<P>(e, splat(-1.38629436111989061883f), lnm);  // -2 ln 2 (exactly twice float ln 2)
 }
 
-// r*cos(theta) and r*sin(theta), theta in [0, 2pi], both lanes; the quadrant's
-// signs are folded into the radius.
-template <bool PT, bool PO>
-__device__ __forceinline__ void polar2(Pair theta, Pair r, Pair& zc, Pair& zs) {
+// theta in [0, 2pi] -> x = theta - j pi/2 with |x| <= pi/4 (Cody-Waite, two-term pi/2,
+// j <= 4) and the bits of the rounded sum, whose low two bits are j mod 4.
+template <bool PT>
+__device__ __forceinline__ Pair reduce_quadrant(Pair theta, std::uint32_t (&q)[2]) {
   constexpr float kRound = 12582912.0f;  // 1.5 * 2^23: adding it rounds to an integer
   const Pair magic = fma<PT>(theta, splat(0.636619772367581343076f), splat(kRound));  // 2/pi
   const Pair j = add<PT>(magic, splat(-kRound));
   Pair x = fma<PT>(j, splat(-1.57079637050628662109375f), theta);  // float(pi/2)
   x = fma<PT>(j, splat(4.37113900018624283e-8f), x);               // pi/2 - float(pi/2), negated
-  // near-minimax odd / even polynomials on |x| <= pi/4 (fits of this file's own:
-  // sin 1e-8, cos 3.3e-8 absolute error)
+  q[0] = __float_as_uint(magic.x);
+  q[1] = __float_as_uint(magic.y);
+  return x;
+}
+
+// sin and cos of |x| <= pi/4 by near-minimax odd / even polynomials (fits of this
+// file's own: sin 1e-8, cos 3.3e-8 absolute error).
+template <bool PT>
+__device__ __forceinline__ void sincos_poly(Pair x, Pair& sn, Pair& cs) {
   const Pair x2 = mul<PT>(x, x);
   Pair p = fma<PT>(splat(-1.958967769e-4f), x2, splat(8.332764730e-3f));
   p = fma<PT>(p, x2, splat(-1.666666567e-1f));
-  const Pair sn = fma<PT>(mul<PT>(x, x2), p, x);
+  sn = fma<PT>(mul<PT>(x, x2), p, x);
   Pair c = fma<PT>(splat(-1.359708956e-3f), x2, splat(4.165624082e-2f));
   c = fma<PT>(c, x2, splat(-4.999989271e-1f));
-  const Pair cs = fma<PT>(c, x2, splat(1.0f));
-  // quadrant j (low bits of the rounded sum): cos = [c, -s, -c, s][j & 3],
-  // sin = [s, c, -s, -c][j & 3]
-  const std::uint32_t q[2] = {__float_as_uint(magic.x), __float_as_uint(magic.y)};
+  cs = fma<PT>(c, x2, splat(1.0f));
+}
+
+// r*cos(theta) and r*sin(theta) from sin / cos of the reduced angle: quadrant j
+// (low bits of q) gives cos = [c, -s, -c, s][j & 3], sin = [s, c, -s, -c][j & 3]; the
+// signs are folded into the radius.
+template <bool PO>
+__device__ __forceinline__ void rotate_quadrant(const std::uint32_t (&q)[2], Pair sn, Pair cs,
+                                                Pair r, Pair& zc, Pair& zs) {
   const float csl[2] = {cs.x, cs.y}, snl[2] = {sn.x, sn.y}, rl[2] = {r.x, r.y};
   float cv[2], sv[2], rc[2], rs[2];
 #pragma unroll
@@ -227,6 +259,78 @@ __device__ __forceinline__ void polar2(Pair theta, Pair r, Pair& zc, Pair& zs) {
   }
   zc = mul<PO>({rc[0], rc[1]}, {cv[0], cv[1]});
   zs = mul<PO>({rs[0], rs[1]}, {sv[0], sv[1]});
+}
+
+// r*cos(theta) and r*sin(theta), theta in [0, 2pi], both lanes.
+template <bool PT, bool PO>
+__device__ __forceinline__ void polar2(Pair theta, Pair r, Pair& zc, Pair& zs) {
+  std::uint32_t q[2];
+  const Pair x = reduce_quadrant<PT>(theta, q);
+  Pair sn, cs;
+  sincos_poly<PT>(x, sn, cs);
+  rotate_quadrant<PO>(q, sn, cs, r, zc, zs);
+}
+
+// ---- hardware-approximation variant of the normal transform (kHw) --------------
+// The error bound of the transform is 2e-6 * max(1, |z|) against the reference
+// formula.  Measured over every fp32 input each step can see (all u in [2^-32, 1],
+// all reduced angles |x| <= pi/2):
+//   sin.approx / cos.approx of x: at most 3.65e-7 absolute;
+//   lg2.approx(u) * -2 ln 2: accurate relative to w = -2 ln u except near u = 1,
+//     where lg2 of a mantissa near 2 cancels; for u > kNearOne the series
+//     w = d (-2 + d (1 + d (-2/3 + d / 2))) in d = u - 1 (exact) is used instead
+//     (2.7e-9 absolute); with that split the radius r = sqrt(w) is within
+//     3.5e-7 * max(1, r) of sqrt(-2 ln u).
+// z = r cos(theta) then errs by at most 3.5e-7 max(1, r)|cos| + r * 3.65e-7 (+ the
+// product's rounding), which stays below 2e-6 max(1, |z|) for r <= kRadHw = 3.75;
+// lanes with a larger radius (u < exp(-7.03), one pair in 1100) take this file's
+// polynomials for sin / cos.  Both fallbacks are taken per warp only when one of
+// its lanes needs them.
+constexpr float kNearOne = 0.995f;
+constexpr float kRadHw = 3.75f;
+
+template <bool P>
+__device__ __forceinline__ Pair neg2_log_hw(Pair u) {
+  Pair w = mul<P>({lg2_approx(u.x), lg2_approx(u.y)}, splat(-1.38629436111989061883f));
+  const bool nx = u.x > kNearOne, ny = u.y > kNearOne;
+  if (__any_sync(__activemask(), nx || ny)) {
+    const Pair d = add<P>(u, splat(-1.0f));
+    const Pair q = fma<P>(d, splat(0.5f), splat(-0.6666666865f));
+    const Pair sr = mul<P>(d, fma<P>(d, fma<P>(d, q, splat(1.0f)), splat(-2.0f)));
+    if (nx) w.x = sr.x;
+    if (ny) w.y = sr.y;
+  }
+  return w;
+}
+
+// r*cos(theta) and r*sin(theta) with the hardware sin / cos: theta is reduced by
+// pi (x = theta - k pi, |x| <= pi/2, two-term pi), so cos and sin of theta are those
+// of x with one common sign (-1)^k, folded into the radius.
+template <bool PT, bool PO>
+__device__ __forceinline__ void polar2_hw(Pair theta, Pair r, Pair& zc, Pair& zs) {
+  constexpr float kRound = 12582912.0f;  // 1.5 * 2^23: adding it rounds to an integer
+  const Pair magic = fma<PT>(theta, splat(0.318309886183790671538f), splat(kRound));  // 1/pi
+  const Pair k = add<PT>(magic, splat(-kRound));
+  Pair x = fma<PT>(k, splat(-3.1415927410125732421875f), theta);  // float(pi)
+  x = fma<PT>(k, splat(8.74227800037248566e-8f), x);              // pi - float(pi), negated
+  const Pair rk = {__uint_as_float(__float_as_uint(r.x) ^ (__float_as_uint(magic.x) << 31)),
+                   __uint_as_float(__float_as_uint(r.y) ^ (__float_as_uint(magic.y) << 31))};
+  zc = mul<PO>(rk, {cos_approx(x.x), cos_approx(x.y)});
+  zs = mul<PO>(rk, {sin_approx(x.x), sin_approx(x.y)});
+  const bool fx = r.x > kRadHw, fy = r.y > kRadHw;
+  if (__any_sync(__activemask(), fx || fy)) {
+    // large radius: this file's polynomials on the pi/2 reduction
+    Pair pc, ps;
+    polar2<PT, PO>(theta, r, pc, ps);
+    if (fx) {
+      zc.x = pc.x;
+      zs.x = ps.x;
+    }
+    if (fy) {
+      zc.y = pc.y;
+      zs.y = ps.y;
+    }
+  }
 }
 
 template <Dist D, bool Scale, unsigned Pack>
@@ -247,12 +351,16 @@ __device__ __forceinline__ uint4 transform(uint4 r, float mean, float stddev) {
                       __float_as_uint(b.y));
   } else {
     // lane x is the pair (u0, u1), lane y the pair (u2, u3)
+    constexpr bool HW = (Pack & kHw) != 0u;
     const Pair ue = to_uniform2<PC>(r.x, r.z), uo = to_uniform2<PC>(r.y, r.w);
-    const Pair w = neg2_log<PL>(ue);
+    const Pair w = HW ? neg2_log_hw<PL>(ue) : neg2_log<PL>(ue);
     const Pair rad = {sqrt_approx(w.x), sqrt_approx(w.y)};
     const Pair theta = mul<PT>(splat(6.28318530717958647692f), uo);
     Pair zc, zs;
-    polar2<PT, PO>(theta, rad, zc, zs);
+    if constexpr (HW)
+      polar2_hw<PT, PO>(theta, rad, zc, zs);
+    else
+      polar2<PT, PO>(theta, rad, zc, zs);
     if constexpr (Scale) {
       zc = mul<PO>(zc, splat(stddev));
       zs = mul<PO>(zs, splat(stddev));
@@ -272,32 +380,52 @@ __device__ __forceinline__ uint4 transform(uint4 r, float mean, float stddev) {
 // The log-normal (2^28 words, stddev != 1): all four stages packed 0.408 ms, the
 // normal's mix 0.418 ms, all scalar 0.442 ms.
 constexpr unsigned kUniformPack = kPackConv;
-constexpr unsigned kNormalPack = kPackConv | kPackLog | kPackOut;
+constexpr unsigned kNormalPack = kHw | kPackConv | kPackLog | kPackTrig | kPackOut;
 constexpr unsigned kLogNormalPack = kPackConv | kPackLog | kPackTrig | kPackOut;
+
+// Writes one Philox block's four words at block index b.
+template <bool Vec16>
+__device__ __forceinline__ void store_block(std::uint32_t* out, std::uint64_t b, uint4 v) {
+  if constexpr (Vec16) {
+    reinterpret_cast<uint4*>(out)[b] = v;
+  } else {
+    std::uint32_t* p = out + 4 * b;
+    p[0] = v.x;
+    p[1] = v.y;
+    p[2] = v.z;
+    p[3] = v.w;
+  }
+}
 
 // One thread per Philox block, grid-stride.  Vec16 selects a single 16-byte
 // store per block (output 16-byte aligned); otherwise four 4-byte stores.
-// Scale is false when stddev == 1 (the multiply is then the identity).
+// Scale is false when stddev == 1 (the multiply is then the identity).  The
+// uint32 and uniform streams take two blocks (b and b + stride) per loop step,
+// which measured 3.4 % faster for the uniform (less loop overhead on the pipe the
+// Philox multiplies fill); for the normal it measured slower and is not used.
 template <Dist D, bool Vec16, bool Scale = true,
           unsigned Pack = (D == Dist::kNormal      ? kNormalPack
                            : D == Dist::kLogNormal ? kLogNormalPack
                                                    : kUniformPack)>
 __global__ void __launch_bounds__(kThreads) philox_fill_kernel(const FillArgs a) {
+  constexpr bool kPairs = D == Dist::kUniform || D == Dist::kUint32;
   const std::uint64_t full_blocks = a.n >> 2;
   const std::uint64_t stride = static_cast<std::uint64_t>(gridDim.x) * kThreads;
   std::uint64_t b = static_cast<std::uint64_t>(blockIdx.x) * kThreads + threadIdx.x;
   std::uint32_t* out = static_cast<std::uint32_t*>(a.out);
+  if constexpr (kPairs) {
+    for (; b + stride < full_blocks; b += 2 * stride) {
+      const uint4 v0 = transform<D, Scale, Pack>(philox_block(a.first_block + b, a.key), a.mean,
+                                                 a.stddev);
+      const uint4 v1 = transform<D, Scale, Pack>(philox_block(a.first_block + b + stride, a.key),
+                                                 a.mean, a.stddev);
+      store_block<Vec16>(out, b, v0);
+      store_block<Vec16>(out, b + stride, v1);
+    }
+  }
   for (; b < full_blocks; b += stride) {
     const uint4 v = transform<D, Scale, Pack>(philox_block(a.first_block + b, a.key), a.mean, a.stddev);
-    if constexpr (Vec16) {
-      reinterpret_cast<uint4*>(out)[b] = v;
-    } else {
-      std::uint32_t* p = out + 4 * b;
-      p[0] = v.x;
-      p[1] = v.y;
-      p[2] = v.z;
-      p[3] = v.w;
-    }
+    store_block<Vec16>(out, b, v);
   }
   // The partial last block (n % 4 words) belongs to the thread whose next
   // grid-stride index is exactly full_blocks.

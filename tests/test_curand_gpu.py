@@ -167,6 +167,36 @@ def test_config_streams_against_reference(cuda, built):
           f"max |err| {err.max():.3e}, {exact:.2%} bit-identical")
 
 
+def test_config_normal_every_output(cuda, built):
+    """The whole normal call of configs[1] (2^30 words from offset 2^30, seed 1234):
+    every output against the oracle restatement of the reference formula (glibc
+    float functions), within NORMAL_TOL * max(1, |z|), in chunks of 2^26 words."""
+    import os
+    torch = cuda
+    L = capi.curand()
+    n = 1 << 30
+    z = torch.empty(n, dtype=torch.float32, device="cuda")
+    with curand_generator(1234, torch, offset=n) as g:
+        assert L.curandGenerateNormal(g, C.c_void_p(z.data_ptr()), n, C.c_float(0.0),
+                                      C.c_float(1.0)) == 0
+    torch.cuda.synchronize()
+    chunk = 1 << 26
+    worst = 0.0
+    exact = 0
+    for c0 in range(0, n, chunk):
+        got = z[c0:c0 + chunk].cpu().numpy()
+        want, _ = oracle.generate_normal(1234, n + c0, chunk, 0.0, 1.0,
+                                         threads=os.cpu_count() or 1)
+        err = np.abs(got.astype(np.float64) - want.astype(np.float64))
+        ratio = err / (NORMAL_TOL * np.maximum(1.0, np.abs(want.astype(np.float64))))
+        worst = max(worst, float(ratio.max()))
+        exact += int(np.count_nonzero(got.view(np.uint32) == want.view(np.uint32)))
+        assert worst <= 1.0, f"chunk at {c0}: max err / bound {worst}"
+    del z
+    torch.cuda.empty_cache()
+    print(f"2^30 normals: max err / bound {worst:.3f}, {exact / n:.2%} bit-identical")
+
+
 @pytest.mark.parametrize("seed,offset,n", [(1234, 0, 4099), (9, 6, 1001), (1234, 1 << 30, 65537)])
 def test_streams_against_reference(cuda, built, seed, offset, n):
     """uint32, uniform and normal against the reference's compiled host generator."""

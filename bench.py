@@ -374,9 +374,12 @@ class Suite:
             # fp32 work done as three tf32 MMAs per product: tf32 runs at half the bf16
             # rate, so the ceiling for fp32 FLOP/s is bf16 / 2 / 3
             peak, unit = self.peaks.get("bf16_tflops", 1651.6) / 6.0, "TFLOP/s"
+        elif bound == "fp64":  # DFMA pipe at the maximum SM clock
+            peak, unit = DFMA_PEAK_TFLOPS, "TFLOP/s"
         else:  # fp32 FFMA pipe at the maximum SM clock
             peak, unit = FFMA_PEAK_TFLOPS, "TFLOP/s"
         source = {"ffma": "148 SMs x 128 FMA x 2 x 1965 MHz",
+                  "fp64": "148 SMs x 64 DFMA x 2 x 1965 MHz (nominal)",
                   "tensor-tf32x3": self.peaks["source"] + " bf16 GEMM / 2 (tf32 rate) / 3 (MMAs "
                                    "per fp32 product)"}.get(bound, self.peaks["source"])
         out = {"bound": bound, "kernel": kernel, "achieved": achieved, "peak": peak,
@@ -387,6 +390,7 @@ class Suite:
 
 
 FFMA_PEAK_TFLOPS = 148 * 128 * 2 * 1.965e9 / 1e12
+DFMA_PEAK_TFLOPS = 148 * 64 * 2 * 1.965e9 / 1e12
 
 
 def torch_float(torch):
@@ -1144,6 +1148,46 @@ def suite_geam(s: Suite) -> dict:
                                          "host threads"}
     return out
 
+def suite_dgemm(s: Suite) -> dict:
+    """cublasDgemm fp64 M = N = K = 4096 (column-major, N,N), alpha 1, beta 0,
+    uniform[-1, 1] from seed 21, through the register-blocked DFMA kernel."""
+    from muda_b200 import synth
+    torch = s.torch
+    m = n = k = 4096 // s.scale
+    a = synth.uniform_pm1(torch, m * k, seed=21).double()
+    b = synth.uniform_pm1(torch, k * n, seed=21, offset=(m * k + 3) // 4 * 4).double()
+    c = torch.empty(m * n, dtype=torch.float64, device="cuda")
+    L, h = _blas_handle(s)
+    one, zero = C.c_double(1.0), C.c_double(0.0)
+    args = (h, 0, 0, m, n, k, C.byref(one), C.c_void_p(a.data_ptr()), m,
+            C.c_void_p(b.data_ptr()), k, C.byref(zero), C.c_void_p(c.data_ptr()), m)
+    ms, launches = s.time(lambda: L.cublasDgemm_v2(*args), flush=True)
+    assert L.cublasDestroy_v2(h) == 0
+    flop = 2.0 * m * n * k
+    tf = flop / (ms * 1e-3) / 1e12
+    out = {"value": tf, "unit": "TFLOP/s", "ms": ms, "dtype": "f64",
+           "config": f"{m}x{n}x{k} fp64 N,N, L2 flushed before each call",
+           "roofline": s.roof("dgemm_kernel<128,128,false,false>", tf, "fp64"),
+           "launches": launches}
+    if s.cpu:
+        import oracle
+        A = a.cpu().numpy()
+        B = b.cpu().numpy()
+        rng = np.random.default_rng(0)
+        ne = 8192
+        pick = rng.choice(m * n, ne, replace=False)
+        rows, cols = (pick % m).astype(np.int32), (pick // m).astype(np.int32)
+        dt = cpu_time(lambda: oracle.dgemm(False, False, m, n, k, 1.0, A, m, B, k, 0.0,
+                                           np.zeros(m * n), m, entries=(rows, cols),
+                                           threads=os.cpu_count() or 1))
+        out["cpu_baseline"] = {"value": 2.0 * k * ne / dt / 1e12, "unit": "TFLOP/s",
+                               "cores": os.cpu_count(), "kind": "port",
+                               "sample": f"{ne} sampled output entries (of {m * n}), "
+                                         "oracle/blas64.cpp extended-precision dot products, "
+                                         "rate extrapolated"}
+    return out
+
+
 SUITE = {
     "sgemm": suite_sgemm,
     "spmv": suite_spmv,
@@ -1167,6 +1211,7 @@ SUITE = {
     "sgemv_n": lambda s: suite_gemv(s, False),
     "sgemv_t": lambda s: suite_gemv(s, True),
     "sgeam": suite_geam,
+    "dgemm": suite_dgemm,
 }
 
 

@@ -112,6 +112,32 @@ cublasStatus_t cublasSgemv_v2(cublasHandle_t handle, cublasOperation_t trans, in
                               const float* alpha, const float* A, int lda, const float* x,
                               int incx, const float* beta, float* y, int incy);
 
+/* Level-1 / level-2 (fp64) — reference cublas_level1.mm:658-979, cublas_level2.mm:135-200,
+   which call the host CBLAS; here GPU kernels (blas/dblas_kernels.cu) with the
+   reference-BLAS element rules above.  Reductions deliver *result as for fp32. */
+cublasStatus_t cublasDaxpy_v2(cublasHandle_t handle, int n, const double* alpha,
+                              const double* x, int incx, double* y,
+                              int incy);                          /* cublas_level1.mm:658 */
+cublasStatus_t cublasDcopy_v2(cublasHandle_t handle, int n, const double* x, int incx, double* y,
+                              int incy);                          /* cublas_level1.mm:705 */
+cublasStatus_t cublasDscal_v2(cublasHandle_t handle, int n, const double* alpha, double* x,
+                              int incx);                          /* cublas_level1.mm:744 */
+cublasStatus_t cublasDswap_v2(cublasHandle_t handle, int n, double* x, int incx, double* y,
+                              int incy);                          /* cublas_level1.mm:784 */
+cublasStatus_t cublasDdot_v2(cublasHandle_t handle, int n, const double* x, int incx,
+                             const double* y, int incy,
+                             double* result);                     /* cublas_level1.mm:823 */
+cublasStatus_t cublasDnrm2_v2(cublasHandle_t handle, int n, const double* x, int incx,
+                              double* result);                    /* cublas_level1.mm:865 */
+cublasStatus_t cublasDasum_v2(cublasHandle_t handle, int n, const double* x, int incx,
+                              double* result);                    /* cublas_level1.mm:903 */
+cublasStatus_t cublasIdamax_v2(cublasHandle_t handle, int n, const double* x, int incx,
+                               int* result);                      /* cublas_level1.mm:941 */
+cublasStatus_t cublasDgemv_v2(cublasHandle_t handle, cublasOperation_t trans, int m, int n,
+                              const double* alpha, const double* A, int lda, const double* x,
+                              int incx, const double* beta, double* y,
+                              int incy);                          /* cublas_level2.mm:135 */
+
 /* Level-3 — reference cublas_level3.mm:474-617 */
 /* C = alpha * op(A) + beta * op(B), column-major m x n; an operand whose scalar is 0
  * is not read.  Reference: libraries/blas/include/cublas_v2.h:194-201 (implemented
@@ -147,6 +173,20 @@ cublasStatus_t cublasSgemmStridedBatched(cublasHandle_t handle, cublasOperation_
                                          long long int strideB, const float* beta, float* C,
                                          int ldc, long long int strideC, int batchCount);
 
+/* fp64 GEMM — reference cublas_level3.mm:714-819 (host CBLAS dgemm per batch entry);
+   here the register-blocked DFMA kernel of blas/dblas_kernels.cu. */
+cublasStatus_t cublasDgemm_v2(cublasHandle_t handle, cublasOperation_t transa,
+                              cublasOperation_t transb, int m, int n, int k, const double* alpha,
+                              const double* A, int lda, const double* B, int ldb,
+                              const double* beta, double* C, int ldc); /* cublas_level3.mm:714 */
+cublasStatus_t cublasDgemmStridedBatched(cublasHandle_t handle, cublasOperation_t transa,
+                                         cublasOperation_t transb, int m, int n, int k,
+                                         const double* alpha, const double* A, int lda,
+                                         long long int strideA, const double* B, int ldb,
+                                         long long int strideB, const double* beta, double* C,
+                                         int ldc, long long int strideC,
+                                         int batchCount);         /* cublas_level3.mm:722 */
+
 cublasStatus_t cublasGemmStridedBatchedEx(cublasHandle_t handle, cublasOperation_t transa,
                                           cublasOperation_t transb, int m, int n, int k,
                                           const void* alpha, const void* A, cudaDataType Atype,
@@ -173,6 +213,16 @@ cublasStatus_t cublasGemmStridedBatchedEx(cublasHandle_t handle, cublasOperation
 #define cublasSasum cublasSasum_v2
 #define cublasIsamax cublasIsamax_v2
 #define cublasSgemv cublasSgemv_v2
+#define cublasDaxpy cublasDaxpy_v2
+#define cublasDcopy cublasDcopy_v2
+#define cublasDscal cublasDscal_v2
+#define cublasDswap cublasDswap_v2
+#define cublasDdot cublasDdot_v2
+#define cublasDnrm2 cublasDnrm2_v2
+#define cublasDasum cublasDasum_v2
+#define cublasIdamax cublasIdamax_v2
+#define cublasDgemv cublasDgemv_v2
+#define cublasDgemm cublasDgemm_v2
 
 #ifdef __cplusplus
 }

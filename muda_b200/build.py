@@ -44,7 +44,7 @@ LIBS: dict[str, list[str]] = {
     "peer": ["peer/peer_exchange.cu"],
     "cublas": ["blas/cublas_api.cpp", "blas/gemm_simt_kernels.cu", "blas/gemm_tc_kernels.cu",
                "blas/tf32_split.cu", "blas/level12_kernels.cu",
-               "blas/geam_kernels.cu"],
+               "blas/geam_kernels.cu", "blas/dblas_kernels.cu"],
 }
 
 COMMON_FLAGS = ["-O3", "-std=c++17", f"-I{INCLUDE}", f"-I{CSRC}"]

@@ -296,6 +296,18 @@ CUBLAS_PROTOS = {
     "cublasSgemv_v2": ([vp, i32, i32, i32, vp, vp, i32, vp, i32, vp, vp, i32], i32),
     "cublasSgeam": ([vp, i32, i32, i32, i32, vp, vp, i32, vp, vp, i32, vp, i32], i32),
     "cublasDgeam": ([vp, i32, i32, i32, i32, vp, vp, i32, vp, vp, i32, vp, i32], i32),
+    "cublasDaxpy_v2": ([vp, i32, vp, vp, i32, vp, i32], i32),
+    "cublasDcopy_v2": ([vp, i32, vp, i32, vp, i32], i32),
+    "cublasDscal_v2": ([vp, i32, vp, vp, i32], i32),
+    "cublasDswap_v2": ([vp, i32, vp, i32, vp, i32], i32),
+    "cublasDdot_v2": ([vp, i32, vp, i32, vp, i32, vp], i32),
+    "cublasDnrm2_v2": ([vp, i32, vp, i32, vp], i32),
+    "cublasDasum_v2": ([vp, i32, vp, i32, vp], i32),
+    "cublasIdamax_v2": ([vp, i32, vp, i32, vp], i32),
+    "cublasDgemv_v2": ([vp, i32, i32, i32, vp, vp, i32, vp, i32, vp, vp, i32], i32),
+    "cublasDgemm_v2": ([vp, i32, i32, i32, i32, i32, vp, vp, i32, vp, i32, vp, vp, i32], i32),
+    "cublasDgemmStridedBatched": ([vp, i32, i32, i32, i32, i32, vp, vp, i32, ll, vp, i32, ll,
+                                   vp, vp, i32, ll, i32], i32),
 }
 
 

@@ -27,6 +27,7 @@
 #include <mutex>
 
 #include "blas/geam.hpp"
+#include "blas/dblas.hpp"
 #include "blas/gemm.hpp"
 #include "blas/level12.hpp"
 #include "common/device.hpp"
@@ -111,8 +112,11 @@ class BufferUse {
   }
 
  private:
+  // one scratch serves the fp32 and the fp64 reductions (same counter word first)
   static std::size_t slot_offset() {
-    return (mb200::blas::reduce_scratch_bytes() + 255) / 256 * 256;
+    const std::size_t a = mb200::blas::reduce_scratch_bytes();
+    const std::size_t b = mb200::blas::dreduce_scratch_bytes();
+    return ((a > b ? a : b) + 255) / 256 * 256;
   }
   const std::size_t kSlot = slot_offset();
   std::lock_guard<std::mutex> lk_;
@@ -287,9 +291,10 @@ std::size_t span_elems(int n, int inc) {
   return 1u + static_cast<std::size_t>(n - 1) * a;
 }
 
-bool vec_ok(const float* p, int n, int inc) {
-  return mb200::device_span_ok(p, span_elems(n, inc) * sizeof(float)) &&
-         mb200::aligned_to(p, sizeof(float));
+template <typename T>
+bool vec_ok(const T* p, int n, int inc) {
+  return mb200::device_span_ok(p, span_elems(n, inc) * sizeof(T)) &&
+         mb200::aligned_to(p, sizeof(T));
 }
 
 // The handle's stream and pointer mode.
@@ -301,11 +306,12 @@ void snapshot(BlasContext& ctx, cudaStream_t* stream, cublasPointerMode_t* mode)
 
 // A scalar argument: its host value, or (device pointer mode) a checked device
 // pointer the kernel reads.
-bool scalar(cublasPointerMode_t mode, const float* p, float* host, const float** dev) {
+template <typename T>
+bool scalar(cublasPointerMode_t mode, const T* p, T* host, const T** dev) {
   if (mode == CUBLAS_POINTER_MODE_DEVICE) {
-    if (!mb200::device_span_ok(p, sizeof(float))) return false;
+    if (!mb200::device_span_ok(p, sizeof(T))) return false;
     *dev = p;
-    *host = 0.0f;
+    *host = T(0);
   } else {
     *host = *p;
     *dev = nullptr;
@@ -353,9 +359,14 @@ cublasStatus_t status_of(cudaError_t e) {
 // writes `result` (device memory) directly; in host mode it writes the handle's
 // result slot, copied to `result` after the stream finishes (the reference
 // synchronises the same way, cublas_level1.mm:119-126).
-template <typename T>
-cublasStatus_t run_reduction(BlasContext& ctx, mb200::blas::Reduce op, int n, const float* x,
-                             int incx, const float* y, int incy, T* result) {
+template <typename E>
+struct NoDeduce {
+  using type = E;
+};
+
+template <typename T, typename E = float>
+cublasStatus_t run_reduction(BlasContext& ctx, mb200::blas::Reduce op, int n, const E* x,
+                             int incx, const typename NoDeduce<E>::type* y, int incy, T* result) {
   cudaStream_t stream;
   cublasPointerMode_t mode;
   snapshot(ctx, &stream, &mode);
@@ -373,7 +384,11 @@ cublasStatus_t run_reduction(BlasContext& ctx, mb200::blas::Reduce op, int n, co
   void* scratch = use.reduction_scratch();
   if (scratch == nullptr) return CUBLAS_STATUS_ALLOC_FAILED;
   void* out = mode == CUBLAS_POINTER_MODE_DEVICE ? static_cast<void*>(result) : use.result_slot();
-  cudaError_t e = mb200::blas::launch_reduce(op, n, x, incx, y, incy, out, scratch, stream);
+  cudaError_t e;
+  if constexpr (sizeof(E) == 8)
+    e = mb200::blas::launch_dreduce(op, n, x, incx, y, incy, out, scratch, stream);
+  else
+    e = mb200::blas::launch_reduce(op, n, x, incx, y, incy, out, scratch, stream);
   if (e == cudaSuccess && mode == CUBLAS_POINTER_MODE_HOST)
     e = cudaMemcpyAsync(result, out, sizeof(T), cudaMemcpyDeviceToHost, stream);
   if (e == cudaSuccess) e = use.done();
@@ -678,6 +693,193 @@ cublasStatus_t cublasSgemv_v2(cublasHandle_t handle, cublasOperation_t trans, in
                                             ws, ws ? use.workspace_bytes() : 0, stream);
   if (e == cudaSuccess) e = use.done();
   return status_of(e);
+}
+
+// ---------------------------------------------------------------- fp64
+// Argument checks and status codes of the reference's host-BLAS wrappers
+// (cublas_level1.mm:658-979, cublas_level2.mm:135-200, cublas_level3.mm:714-819),
+// in their order; the arithmetic is blas/dblas_kernels.cu.
+cublasStatus_t cublasDaxpy_v2(cublasHandle_t handle, int n, const double* alpha, const double* x,
+                              int incx, double* y, int incy) {
+  auto h = handles().get(handle);
+  if (!h) return CUBLAS_STATUS_NOT_INITIALIZED;
+  if (n <= 0) return CUBLAS_STATUS_SUCCESS;
+  if (alpha == nullptr) return CUBLAS_STATUS_INVALID_VALUE;
+  cudaStream_t stream;
+  cublasPointerMode_t mode;
+  snapshot(*h, &stream, &mode);
+  double a;
+  const double* a_dev;
+  if (!scalar(mode, alpha, &a, &a_dev)) return CUBLAS_STATUS_INVALID_VALUE;
+  if (a_dev == nullptr && a == 0.0) return CUBLAS_STATUS_SUCCESS;
+  if (!vec_ok(x, n, incx) || !vec_ok(y, n, incy)) return CUBLAS_STATUS_INVALID_VALUE;
+  return status_of(mb200::blas::launch_daxpy(n, a, a_dev, x, incx, y, incy, stream));
+}
+
+cublasStatus_t cublasDcopy_v2(cublasHandle_t handle, int n, const double* x, int incx, double* y,
+                              int incy) {
+  auto h = handles().get(handle);
+  if (!h) return CUBLAS_STATUS_NOT_INITIALIZED;
+  if (n <= 0) return CUBLAS_STATUS_SUCCESS;
+  if (!vec_ok(x, n, incx) || !vec_ok(y, n, incy)) return CUBLAS_STATUS_INVALID_VALUE;
+  cudaStream_t stream;
+  cublasPointerMode_t mode;
+  snapshot(*h, &stream, &mode);
+  return status_of(mb200::blas::launch_dcopy(n, x, incx, y, incy, stream));
+}
+
+cublasStatus_t cublasDscal_v2(cublasHandle_t handle, int n, const double* alpha, double* x,
+                              int incx) {
+  auto h = handles().get(handle);
+  if (!h) return CUBLAS_STATUS_NOT_INITIALIZED;
+  if (n <= 0 || incx <= 0) return CUBLAS_STATUS_SUCCESS;
+  if (alpha == nullptr) return CUBLAS_STATUS_INVALID_VALUE;
+  cudaStream_t stream;
+  cublasPointerMode_t mode;
+  snapshot(*h, &stream, &mode);
+  double a;
+  const double* a_dev;
+  if (!scalar(mode, alpha, &a, &a_dev)) return CUBLAS_STATUS_INVALID_VALUE;
+  if (!vec_ok(x, n, incx)) return CUBLAS_STATUS_INVALID_VALUE;
+  return status_of(mb200::blas::launch_dscal(n, a, a_dev, x, incx, stream));
+}
+
+cublasStatus_t cublasDswap_v2(cublasHandle_t handle, int n, double* x, int incx, double* y,
+                              int incy) {
+  auto h = handles().get(handle);
+  if (!h) return CUBLAS_STATUS_NOT_INITIALIZED;
+  if (n <= 0) return CUBLAS_STATUS_SUCCESS;
+  if (!vec_ok(x, n, incx) || !vec_ok(y, n, incy)) return CUBLAS_STATUS_INVALID_VALUE;
+  cudaStream_t stream;
+  cublasPointerMode_t mode;
+  snapshot(*h, &stream, &mode);
+  return status_of(mb200::blas::launch_dswap(n, x, incx, y, incy, stream));
+}
+
+cublasStatus_t cublasDdot_v2(cublasHandle_t handle, int n, const double* x, int incx,
+                             const double* y, int incy, double* result) {
+  auto h = handles().get(handle);
+  if (!h) return CUBLAS_STATUS_NOT_INITIALIZED;
+  if (result == nullptr) return CUBLAS_STATUS_INVALID_VALUE;
+  return run_reduction(*h, mb200::blas::Reduce::kDot, n, x, incx, y, incy, result);
+}
+
+cublasStatus_t cublasDnrm2_v2(cublasHandle_t handle, int n, const double* x, int incx,
+                              double* result) {
+  auto h = handles().get(handle);
+  if (!h) return CUBLAS_STATUS_NOT_INITIALIZED;
+  if (result == nullptr) return CUBLAS_STATUS_INVALID_VALUE;
+  return run_reduction<double, double>(*h, mb200::blas::Reduce::kNrm2, n, x, incx, nullptr, 0,
+                                       result);
+}
+
+cublasStatus_t cublasDasum_v2(cublasHandle_t handle, int n, const double* x, int incx,
+                              double* result) {
+  auto h = handles().get(handle);
+  if (!h) return CUBLAS_STATUS_NOT_INITIALIZED;
+  if (result == nullptr) return CUBLAS_STATUS_INVALID_VALUE;
+  return run_reduction<double, double>(*h, mb200::blas::Reduce::kAsum, n, x, incx, nullptr, 0,
+                                       result);
+}
+
+cublasStatus_t cublasIdamax_v2(cublasHandle_t handle, int n, const double* x, int incx,
+                               int* result) {
+  auto h = handles().get(handle);
+  if (!h) return CUBLAS_STATUS_NOT_INITIALIZED;
+  if (result == nullptr) return CUBLAS_STATUS_INVALID_VALUE;
+  return run_reduction<int, double>(*h, mb200::blas::Reduce::kAmax, n, x, incx, nullptr, 0,
+                                    result);
+}
+
+cublasStatus_t cublasDgemv_v2(cublasHandle_t handle, cublasOperation_t trans, int m, int n,
+                              const double* alpha, const double* A, int lda, const double* x,
+                              int incx, const double* beta, double* y, int incy) {
+  auto h = handles().get(handle);
+  if (!h) return CUBLAS_STATUS_NOT_INITIALIZED;
+  // cublas_level2.mm:142-145
+  if (!valid_op(trans) || m < 0 || n < 0 || lda < (m > 1 ? m : 1) || incx == 0 || incy == 0 ||
+      alpha == nullptr || beta == nullptr)
+    return CUBLAS_STATUS_INVALID_VALUE;
+  if (m == 0 || n == 0) return CUBLAS_STATUS_SUCCESS;
+  cudaStream_t stream;
+  cublasPointerMode_t mode;
+  snapshot(*h, &stream, &mode);
+  double a, b;
+  const double *a_dev, *b_dev;
+  if (!scalar(mode, alpha, &a, &a_dev) || !scalar(mode, beta, &b, &b_dev))
+    return CUBLAS_STATUS_INVALID_VALUE;
+  const bool t = trans != CUBLAS_OP_N;
+  const int x_len = t ? m : n, y_len = t ? n : m;
+  const std::size_t a_elems = static_cast<std::size_t>(lda) * (n - 1) + m;
+  if (!mb200::device_span_ok(A, a_elems * sizeof(double)) || !mb200::aligned_to(A, 8) ||
+      !vec_ok(x, x_len, incx) || !vec_ok(y, y_len, incy))
+    return CUBLAS_STATUS_INVALID_VALUE;
+  const std::size_t need = mb200::blas::dgemv_workspace_bytes(t, m, n);
+  if (need == 0)
+    return status_of(mb200::blas::launch_dgemv(t, m, n, a, a_dev, A, lda, x, incx, b, b_dev, y,
+                                                incy, nullptr, 0, stream));
+  BufferUse use(*h, stream);
+  if (!use.ok()) return CUBLAS_STATUS_EXECUTION_FAILED;
+  void* ws = use.workspace(need);
+  cudaError_t e = mb200::blas::launch_dgemv(t, m, n, a, a_dev, A, lda, x, incx, b, b_dev, y, incy,
+                                            ws, ws ? use.workspace_bytes() : 0, stream);
+  if (e == cudaSuccess) e = use.done();
+  return status_of(e);
+}
+
+cublasStatus_t cublasDgemmStridedBatched(cublasHandle_t handle, cublasOperation_t transa,
+                                         cublasOperation_t transb, int m, int n, int k,
+                                         const double* alpha, const double* A, int lda,
+                                         long long int strideA, const double* B, int ldb,
+                                         long long int strideB, const double* beta, double* C,
+                                         int ldc, long long int strideC, int batchCount) {
+  auto h = handles().get(handle);
+  if (!h) return CUBLAS_STATUS_NOT_INITIALIZED;
+  const cublasStatus_t st =
+      check_args(transa, transb, m, n, k, lda, ldb, ldc, batchCount, alpha, beta);
+  if (st != CUBLAS_STATUS_SUCCESS) return st;
+  if (m == 0 || n == 0 || batchCount == 0) return CUBLAS_STATUS_SUCCESS;
+  cudaStream_t stream;
+  cublasPointerMode_t mode;
+  snapshot(*h, &stream, &mode);
+  mb200::blas::DgemmArgs g{};
+  if (!scalar(mode, alpha, &g.alpha, &g.alpha_dev) || !scalar(mode, beta, &g.beta, &g.beta_dev))
+    return CUBLAS_STATUS_INVALID_VALUE;
+  g.trans_a = transa != CUBLAS_OP_N;
+  g.trans_b = transb != CUBLAS_OP_N;
+  g.m = m;
+  g.n = n;
+  g.k = k;
+  g.a = A;
+  g.lda = lda;
+  g.stride_a = strideA;
+  g.b = B;
+  g.ldb = ldb;
+  g.stride_b = strideB;
+  g.c = C;
+  g.ldc = ldc;
+  g.stride_c = strideC;
+  g.batch = batchCount;
+  // the buffers of A, B and C are resolved as in cublas_level3.mm:753-778
+  const int a_rows = g.trans_a ? k : m, a_cols = g.trans_a ? m : k;
+  const int b_rows = g.trans_b ? n : k, b_cols = g.trans_b ? k : n;
+  if (k > 0 &&
+      (!mb200::device_span_ok(A, batch_span(a_rows, a_cols, lda, strideA, batchCount) * 8) ||
+       !mb200::device_span_ok(B, batch_span(b_rows, b_cols, ldb, strideB, batchCount) * 8)))
+    return CUBLAS_STATUS_INVALID_VALUE;
+  if (!mb200::device_span_ok(C, batch_span(m, n, ldc, strideC, batchCount) * 8))
+    return CUBLAS_STATUS_INVALID_VALUE;
+  if (!mb200::aligned_to(A, 8) || !mb200::aligned_to(B, 8) || !mb200::aligned_to(C, 8))
+    return CUBLAS_STATUS_INVALID_VALUE;
+  return status_of(mb200::blas::launch_dgemm(g, stream));
+}
+
+cublasStatus_t cublasDgemm_v2(cublasHandle_t handle, cublasOperation_t transa,
+                              cublasOperation_t transb, int m, int n, int k, const double* alpha,
+                              const double* A, int lda, const double* B, int ldb,
+                              const double* beta, double* C, int ldc) {
+  return cublasDgemmStridedBatched(handle, transa, transb, m, n, k, alpha, A, lda, 0, B, ldb, 0,
+                                   beta, C, ldc, 0, 1);
 }
 
 cublasStatus_t cublasSgeam(cublasHandle_t handle, cublasOperation_t transa,

@@ -507,6 +507,79 @@ def geam(dtype, transa, transb, m, n, alpha, A, lda, beta, B, ldb, C, ldc, threa
     return C
 
 
+# ---------------------------------------------------------------- fp64 BLAS
+def _d(a):
+    return np.ascontiguousarray(a, dtype=np.float64)
+
+
+def daxpy(n, alpha, x, incx, y, incy):
+    """Reference-BLAS daxpy (oracle/blas64.cpp); returns the updated copy of y."""
+    x, y = _d(x), _d(y).copy()
+    lib().oracle_daxpy(n, alpha, x.ctypes.data, incx, y.ctypes.data, incy)
+    return y
+
+
+def dcopy(n, x, incx, y, incy):
+    x, y = _d(x), _d(y).copy()
+    lib().oracle_dcopy(n, x.ctypes.data, incx, y.ctypes.data, incy)
+    return y
+
+
+def dscal(n, alpha, x, incx):
+    x = _d(x).copy()
+    lib().oracle_dscal(n, alpha, x.ctypes.data, incx)
+    return x
+
+
+def dswap(n, x, incx, y, incy):
+    x, y = _d(x).copy(), _d(y).copy()
+    lib().oracle_dswap(n, x.ctypes.data, incx, y.ctypes.data, incy)
+    return x, y
+
+
+def dreduce(op, n, x, incx, y=None, incy=1):
+    """op "dot" / "nrm2" / "asum": (value in element order, extended value, magnitude sum)."""
+    x = _d(x)
+    y = _d(y) if y is not None else np.zeros(1)
+    out = np.zeros(3)
+    lib().oracle_dreduce({"dot": 0, "nrm2": 1, "asum": 2}[op], n, x.ctypes.data, incx,
+                         y.ctypes.data, incy, out.ctypes.data)
+    return float(out[0]), float(out[1]), float(out[2])
+
+
+def idamax(n, x, incx):
+    return int(lib().oracle_idamax(n, _d(x).ctypes.data, incx))
+
+
+def dgemv(trans, m, n, alpha, A, lda, x, incx, beta, y, incy, threads=8):
+    """Returns (y, bound) with bound_i = |alpha| (|op(A)||x|)_i + |beta y_i|."""
+    A, x, y = _d(A), _d(x), _d(y).copy()
+    bound = np.zeros(n if trans else m)
+    lib().oracle_dgemv(int(trans), m, n, alpha, A.ctypes.data, lda, x.ctypes.data, incx, beta,
+                       y.ctypes.data, incy, bound.ctypes.data, threads)
+    return y, bound
+
+
+def dgemm(transa, transb, m, n, k, alpha, A, lda, B, ldb, beta, C, ldc, *, stride_a=0,
+          stride_b=0, stride_c=0, batch=1, entries=None, threads=8):
+    """Returns (C, bound); bound per evaluated entry (all m*n*batch entries, batch-major
+    then column-major, or the given (rows, batch*n + cols) entries)."""
+    A, B, C = _d(A), _d(B), _d(C).copy()
+    rows = cols = None
+    ne = 0
+    if entries is not None:
+        rows = np.ascontiguousarray(entries[0], dtype=np.int32)
+        cols = np.ascontiguousarray(entries[1], dtype=np.int32)
+        ne = len(rows)
+    bound = np.zeros(ne if ne else m * n * batch)
+    lib().oracle_dgemm(int(transa), int(transb), m, n, k, alpha, A.ctypes.data, lda, stride_a,
+                       B.ctypes.data, ldb, stride_b, beta, C.ctypes.data, ldc, stride_c, batch,
+                       rows.ctypes.data if rows is not None else None,
+                       cols.ctypes.data if cols is not None else None, ne, bound.ctypes.data,
+                       threads)
+    return C, bound
+
+
 def sgemv(trans, m, n, alpha, A, lda, x, incx, beta, y, incy, threads=8):
     """-> (y after the reference kernel, exact per output, |terms| per output)."""
     A, x, y = _f32(A), _f32(x), _f32(y).copy()

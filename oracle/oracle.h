@@ -128,6 +128,23 @@ void oracle_sgeam(int transa, int transb, int m, int n, float alpha, const float
 void oracle_dgeam(int transa, int transb, int m, int n, double alpha, const double* A,
                   int64_t lda, double beta, const double* B, int64_t ldb, double* C,
                   int64_t ldc, int threads);
+/* ---- fp64 BLAS: the reference-BLAS definitions behind the reference's host CBLAS
+   calls (libraries/blas/src/cublas_level1.mm:658-979, cublas_level2.mm:135-200,
+   cublas_level3.mm:714-819); oracle/blas64.cpp ---- */
+void oracle_daxpy(int n, double alpha, const double* x, int incx, double* y, int incy);
+void oracle_dcopy(int n, const double* x, int incx, double* y, int incy);
+void oracle_dscal(int n, double alpha, double* x, int incx);
+void oracle_dswap(int n, double* x, int incx, double* y, int incy);
+/* op 0 dot, 1 nrm2, 2 asum: out = {double value, extended value, sum of magnitudes} */
+void oracle_dreduce(int op, int n, const double* x, int incx, const double* y, int incy,
+                    double* out);
+int oracle_idamax(int n, const double* x, int incx);
+void oracle_dgemv(int trans, int m, int n, double alpha, const double* A, int lda, const double* x,
+                  int incx, double beta, double* y, int incy, double* bound, int threads);
+void oracle_dgemm(int transa, int transb, int m, int n, int k, double alpha, const double* A,
+                  int64_t lda, int64_t sa, const double* B, int64_t ldb, int64_t sb, double beta,
+                  double* C, int64_t ldc, int64_t sc, int batch, const int* rows, const int* cols,
+                  int ne, double* bound, int threads);
 void oracle_sgemv(int trans, int m, int n, float alpha, const float* A, int64_t lda,
                   const float* x, int incx, float beta, float* y, int incy, double* exact,
                   double* absv, int threads);

@@ -38,6 +38,17 @@ _PROTOS: list[tuple[str, list, object]] = [
                      C.c_int64, C.c_int64, vp, C.c_int64, C.c_int64, C.c_float, vp, C.c_int64,
                      C.c_int64, C.c_int, C.c_int, vp, vp, C.c_int64, C.c_int], None),
     ("oracle_saxpy", [C.c_int, C.c_float, vp, C.c_int, vp, C.c_int], None),
+    ("oracle_daxpy", [C.c_int, C.c_double, vp, C.c_int, vp, C.c_int], None),
+    ("oracle_dcopy", [C.c_int, vp, C.c_int, vp, C.c_int], None),
+    ("oracle_dscal", [C.c_int, C.c_double, vp, C.c_int], None),
+    ("oracle_dswap", [C.c_int, vp, C.c_int, vp, C.c_int], None),
+    ("oracle_dreduce", [C.c_int, C.c_int, vp, C.c_int, vp, C.c_int, vp], None),
+    ("oracle_idamax", [C.c_int, vp, C.c_int], C.c_int),
+    ("oracle_dgemv", [C.c_int, C.c_int, C.c_int, C.c_double, vp, C.c_int, vp, C.c_int,
+                      C.c_double, vp, C.c_int, vp, C.c_int], None),
+    ("oracle_dgemm", [C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_double, vp, C.c_int64,
+                      C.c_int64, vp, C.c_int64, C.c_int64, C.c_double, vp, C.c_int64, C.c_int64,
+                      C.c_int, vp, vp, C.c_int, vp, C.c_int], None),
     ("oracle_scopy", [C.c_int, vp, C.c_int, vp, C.c_int], None),
     ("oracle_sscal", [C.c_int, C.c_float, vp, C.c_int], None),
     ("oracle_sswap", [C.c_int, vp, C.c_int, vp, C.c_int], None),

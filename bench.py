@@ -472,6 +472,7 @@ def suite_spmv(s: Suite) -> dict:
         assert getattr(L, fn)(d) == 0
     assert L.cusparseDestroy(h) == 0
     nnz = mtx["nnz"]
+    ceiling = gather_ceiling(s, mtx["x"], mtx["col_ind"], nnz)
     alg_bytes = nnz * 8 + (rows + 1) * 4 + rows * 4 + rows * 4
     gbs = alg_bytes / (ms * 1e-3) / 1e9
     out = {"value": gbs, "unit": "GB/s", "ms": ms, "dtype": "f32/i32",
@@ -479,7 +480,9 @@ def suite_spmv(s: Suite) -> dict:
                      "[2.2, 4096], L2 flushed before each call",
            "reference_formula_gbs": (nnz * 8 + 2 * rows * 4) / (ms * 1e-3) / 1e9,
            "roofline": s.roof("spmv_csr_tiles<4>", gbs, "hbm"), "launches": launches,
-           "algorithmic_bytes_per_launch": alg_bytes}
+           "algorithmic_bytes_per_launch": alg_bytes,
+           "gather_ceiling": {**ceiling, "spmv_gathers_per_s": nnz / (ms * 1e-3),
+                              "spmv_frac_of_ceiling": ceiling["ms"] / ms}}
     if s.cpu:
         import oracle
         ro, ci, va, xx = (mtx[k].cpu().numpy() for k in ("row_offsets", "col_ind", "values", "x"))
@@ -488,6 +491,31 @@ def suite_spmv(s: Suite) -> dict:
                                "cores": os.cpu_count(), "kind": "port",
                                "sample": "full problem, oracle/spmv.cpp thread-per-row loop"}
     return out
+
+
+def gather_ceiling(s: Suite, x, col_ind, nnz: int) -> dict:
+    """The matrix's own column stream read and its x gathered, nothing else
+    (mb200ProbeGather): the least work of any CSR SpMV of this matrix.  Best of one
+    and four indices per lane, 4 and 8 CTAs of 256 per SM."""
+    from muda_b200 import capi
+    P = capi.probe()
+    sms = s.torch.cuda.get_device_properties(s.torch.cuda.current_device()).multi_processor_count
+    best = None
+    for per_lane in (1, 4):
+        for ctas in (4, 8):
+            grid = sms * ctas
+            out = s.torch.empty(grid * 256, dtype=s.torch.float32, device="cuda")
+            ms, _ = s.time(lambda: P.mb200ProbeGather(
+                C.c_void_p(x.data_ptr()), C.c_void_p(col_ind.data_ptr()), nnz, per_lane,
+                C.c_void_p(out.data_ptr()), grid, s.sp), flush=True)
+            n_done = nnz if per_lane == 1 else nnz // 4 * 4
+            rate = n_done / (ms * 1e-3)
+            if best is None or rate > best["gathers_per_s"]:
+                best = {"gathers_per_s": rate, "ms": nnz / rate * 1e3, "per_lane": per_lane,
+                        "grid": grid}
+    best["what"] = ("mb200ProbeGather: column indices streamed (evict-first) and x gathered "
+                    "(L2-only), no values, rows or y")
+    return best
 
 
 def _csr_handle(L, s, mtx, rows, cols):

@@ -1,0 +1,25 @@
+/* mb200_probe.h — benchmark probes of this repository (not part of the drop-in API).
+ *
+ * No counterpart in the reference: these entry points exist only to measure a
+ * hardware ceiling against which a library kernel is judged. */
+#ifndef MUDA_B200_PROBE_H_
+#define MUDA_B200_PROBE_H_
+
+#include <cuda_runtime_api.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Streams n int32 indices (per_lane 1, or 4 read as one 16-byte load; idx then
+ * 16-byte aligned) and gathers x[idx[i]] with L2-only loads, writing one partial sum
+ * per thread to out (grid * 256 floats).  Returns 0 on success, 1 on a bad argument,
+ * 2 on a launch error.  The indices must lie inside x. */
+int mb200ProbeGather(const float* x, const int* idx, long long n, int per_lane, float* out,
+                     unsigned grid, cudaStream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MUDA_B200_PROBE_H_ */

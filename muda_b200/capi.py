@@ -342,6 +342,18 @@ def peer() -> C.CDLL:
     return _declare(_load("peer"), PEER_PROTOS)
 
 
+PROBE_PROTOS = {
+    "mb200ProbeGather": ([C.c_void_p, C.c_void_p, C.c_longlong, C.c_int, C.c_void_p, C.c_uint,
+                          C.c_void_p], C.c_int),
+}
+
+
+@lru_cache(maxsize=None)
+def probe() -> C.CDLL:
+    """Benchmark probes (not part of the drop-in API)."""
+    return _declare(_load("probe"), PROBE_PROTOS)
+
+
 ALL_PROTOS: dict[str, dict[str, tuple[list, object]]] = {
     "curand": CURAND_PROTOS,
     "cudnn": CUDNN_PROTOS,
@@ -349,6 +361,7 @@ ALL_PROTOS: dict[str, dict[str, tuple[list, object]]] = {
     "cufft": CUFFT_PROTOS,
     "cublas": CUBLAS_PROTOS,
     "peer": PEER_PROTOS,
+    "probe": PROBE_PROTOS,
 }
 
 LOADERS = {
@@ -358,4 +371,5 @@ LOADERS = {
     "cufft": cufft,
     "cublas": cublas,
     "peer": peer,
+    "probe": probe,
 }

@@ -1,0 +1,60 @@
+// gather_probe.cu — the gather ceiling of a CSR SpMV, measured (benchmark tool).
+//
+// Not part of the drop-in API.  mb200ProbeGather streams an index array the way an
+// SpMV streams its column indices (coalesced, evict-first) and gathers x[idx] the
+// way it gathers the dense vector (L2-only loads), summing the gathered values so
+// that nothing is optimised away, and nothing else: no values, no row structure,
+// no output vector.  Run on a matrix's own column indices it gives the rate at
+// which this GPU can serve that matrix's random x gathers, the ceiling against
+// which an SpMV kernel's gather rate is judged.
+//
+// Layout: grid-stride over the indices; kPerLane consecutive indices per lane per
+// step (one 16-byte load of four indices when kPerLane is 4), all gathers of a step
+// issued before any is used.
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+#pragma GCC visibility push(default)
+#include "mb200_probe.h"
+#pragma GCC visibility pop
+
+namespace {
+
+constexpr int kThreads = 256;
+
+template <int kPerLane>
+__global__ void __launch_bounds__(kThreads)
+    gather_kernel(const float* __restrict__ x, const int* __restrict__ idx, long long n,
+                  float* __restrict__ out) {
+  const long long stride = static_cast<long long>(gridDim.x) * kThreads;
+  long long t = static_cast<long long>(blockIdx.x) * kThreads + threadIdx.x;
+  float s = 0.0f;
+  if constexpr (kPerLane == 4) {
+    const int4* idx4 = reinterpret_cast<const int4*>(idx);
+    const long long n4 = n / 4;
+    for (; t < n4; t += stride) {
+      const int4 c = __ldcs(idx4 + t);
+      const float a = __ldcg(x + c.x), b = __ldcg(x + c.y), d = __ldcg(x + c.z),
+                  e = __ldcg(x + c.w);
+      s += (a + b) + (d + e);
+    }
+  } else {
+    for (; t < n; t += stride) s += __ldcg(x + __ldcs(idx + t));
+  }
+  out[static_cast<long long>(blockIdx.x) * kThreads + threadIdx.x] = s;
+}
+
+}  // namespace
+
+extern "C" int mb200ProbeGather(const float* x, const int* idx, long long n, int per_lane,
+                                float* out, unsigned grid, cudaStream_t stream) {
+  if (x == nullptr || idx == nullptr || out == nullptr || n < 0 || grid == 0) return 1;
+  if (per_lane == 4) {
+    if ((reinterpret_cast<std::uintptr_t>(idx) & 15u) != 0) return 1;
+    gather_kernel<4><<<grid, kThreads, 0, stream>>>(x, idx, n, out);
+  } else {
+    gather_kernel<1><<<grid, kThreads, 0, stream>>>(x, idx, n, out);
+  }
+  return cudaGetLastError() == cudaSuccess ? 0 : 2;
+}

@@ -20,6 +20,7 @@ HEADER_LIB = {
     "cufft.h": "cufft",
     "cublas_v2.h": "cublas",
     "mb200_peer.h": "peer",
+    "mb200_probe.h": "probe",
 }
 
 

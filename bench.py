@@ -941,7 +941,8 @@ def suite_gemm_bf16(s: Suite) -> dict:
     seed 11, alpha 1, beta 0, through cublasGemmStridedBatchedEx.  The value is the
     N,N call (both operands as stored by a column-major caller, the call a row-major
     caller makes with its operands swapped: A is MN-major, B K-major); T,N (both
-    K-major), N,T and T,T are timed beside it on the same buffers."""
+    K-major) is timed beside it on the same buffers (N,T and T,T run the same kernel
+    with MN-major B; tests cover them)."""
     from muda_b200 import capi, synth
     torch = s.torch
     m = n = k = 8192 // s.scale
@@ -962,7 +963,7 @@ def suite_gemm_bf16(s: Suite) -> dict:
                 C.c_void_p(c.data_ptr()), 14, m, m * n, batch, 68, -1)
     flop = 2.0 * m * n * k * batch
     layouts = {}
-    for name, ta, tb in (("NN", 0, 0), ("TN", 1, 0), ("NT", 0, 1), ("TT", 1, 1)):
+    for name, ta, tb in (("NN", 0, 0), ("TN", 1, 0)):
         a_ = args(ta, tb)
         ms_l, launches_l = s.time(lambda: L.cublasGemmStridedBatchedEx(*a_))
         layouts[name] = {"ms": ms_l, "TFLOP/s": flop / (ms_l * 1e-3) / 1e12,
@@ -1024,7 +1025,7 @@ def suite_conv(s: Suite, dtype: str, krsc: bool = True) -> dict:
     args = (h, C.byref(one), xd, C.c_void_p(x.data_ptr()), wd, C.c_void_p(w.data_ptr()), cd, 0,
             None, 0, C.byref(zero), yd, C.c_void_p(y.data_ptr()))
     steps, warm = s.steps, s.warmup
-    s.steps, s.warmup = max(1, min(steps, 3)), 1
+    s.steps, s.warmup = max(3, min(steps, 5)), 2
     ms, launches = s.time(lambda: L.cudnnConvolutionForward(*args))
     s.steps, s.warmup = steps, warm
     for fn, d in (("cudnnDestroyTensorDescriptor", xd), ("cudnnDestroyTensorDescriptor", yd),
@@ -1243,9 +1244,13 @@ SUITE = {
 }
 
 
+SUITE_GAP_S = 0.5  # idle time between routines, so that no routine inherits another's power state
+
+
 def run_suite(names, args, torch) -> dict:
     out = {}
     for name in names:
+        time.sleep(SUITE_GAP_S)
         s = Suite(torch, max(3, args.steps // 4), args.warmup, not args.no_cpu, args.scale)
         try:
             out[name] = SUITE[name](s)
@@ -1475,6 +1480,7 @@ def run_suite_sharded(names, args, torch, dist, world: int, rank: int, local: in
     row-block SpMV with its x exchange."""
     out = {}
     for name in names:
+        time.sleep(SUITE_GAP_S)
         try:
             if name == "spmv_dist":
                 out[name] = spmv_dist_measure(args, torch, dist, world, rank, local)

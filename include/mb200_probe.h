@@ -18,6 +18,12 @@ extern "C" {
 int mb200ProbeGather(const float* x, const int* idx, long long n, int per_lane, float* out,
                      unsigned grid, cudaStream_t stream);
 
+/* Error budget of the cuRAND normal transform, every fp32 input of each step: writes
+ * six floats to device memory `out` (radius error / max(1, r); hardware cos, sin error;
+ * polynomial cos, sin error; the radius threshold of the hardware path).  Returns 0 on
+ * success, 1 on a bad argument, 2 on a launch error. */
+int mb200ProbeNormalError(float* out, cudaStream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

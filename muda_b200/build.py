@@ -42,7 +42,7 @@ LIBS: dict[str, list[str]] = {
               "fft/bluestein_kernels.cu", "fft/mixed_kernels.cu",
               "fft/fft_static.cu", "fft/real_kernels.cu"],
     "peer": ["peer/peer_exchange.cu"],
-    "probe": ["probe/gather_probe.cu"],
+    "probe": ["probe/gather_probe.cu", "probe/normal_probe.cu"],
     "cublas": ["blas/cublas_api.cpp", "blas/gemm_simt_kernels.cu", "blas/gemm_tc_kernels.cu",
                "blas/tf32_split.cu", "blas/level12_kernels.cu",
                "blas/geam_kernels.cu", "blas/dblas_kernels.cu"],

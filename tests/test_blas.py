@@ -234,6 +234,42 @@ def test_gpu_sgemm_split_tf32_tensor_core(cuda, built, m, n, k, batch, ta, tb):
 
 
 @pytest.mark.gpu
+def test_gpu_sgemm_error_flat_in_k(cuda, built):
+    """The split-tf32 path restarts its tensor-memory accumulator every two k-blocks and
+    adds the chunks with round-to-nearest fp32 adds, so its error does not grow with K
+    (the tensor core's own fp32 accumulation truncates).  Normwise error against a
+    float64 product for K = 256 ... 16384, normal and positive data, beside the FFMA
+    kernel (CUBLAS_PEDANTIC_MATH): both stay at the fp32 FMA loop's level."""
+    torch = cuda
+    m = n = 256
+    rows = []
+    for k, positive in ((256, False), (4096, False), (16384, False), (16384, True)):
+        g = torch.Generator(device="cuda").manual_seed(k + positive)
+        A = torch.randn(k, m, device="cuda", generator=g)   # column-major m x k, lda m
+        B = torch.randn(n, k, device="cuda", generator=g)   # column-major k x n, ldb k
+        if positive:
+            A, B = A.abs(), B.abs()
+        want = (A.double().t() @ B.double().t())             # m x n
+        errs = []
+        for mode in (capi.CUBLAS_DEFAULT_MATH, capi.CUBLAS_PEDANTIC_MATH):
+            Cm = torch.empty(n, m, device="cuda")
+            b = Blas(torch)
+            assert b.L.cublasSetMathMode(b.h, mode) == 0
+            assert b.L.cublasSgemm_v2(b.h, 0, 0, m, n, k, C.byref(C.c_float(1.0)),
+                                      C.c_void_p(A.data_ptr()), m, C.c_void_p(B.data_ptr()), k,
+                                      C.byref(C.c_float(0.0)), C.c_void_p(Cm.data_ptr()), m) == 0
+            torch.cuda.synchronize()
+            b.close()
+            got = Cm.double().t()
+            errs.append(float((got - want).norm() / want.norm()))
+        rows.append((k, positive, *errs))
+        assert errs[0] <= 2e-6 and errs[1] <= 5e-6, (k, positive, errs)
+    for k, pos, e_tc, e_ffma in rows:
+        print(f"K {k:6d} {'positive' if pos else 'normal  '}: split-tf32 {e_tc:.2e}  "
+              f"FFMA {e_ffma:.2e}")
+
+
+@pytest.mark.gpu
 def test_gpu_sgemm_split_tf32_stream_switch_and_special_values(cuda, built):
     """The handle's split workspace stays ordered across cublasSetStream, and
     inf / -inf / nan propagate as in an fp32 loop, including an infinity meeting a

@@ -167,6 +167,33 @@ def test_config_streams_against_reference(cuda, built):
           f"max |err| {err.max():.3e}, {exact:.2%} bit-identical")
 
 
+def test_normal_transform_error_budget(cuda, built):
+    """The error bound of the normal transform from its parts, each measured over every
+    fp32 input of its step (mb200ProbeNormalError runs the shipped device code):
+    |dz| <= |dr| |cos| + r |dcos| (+ the product's rounding and the reference formula's
+    own rounding, 2^-24 |z| each) stays below NORMAL_TOL * max(1, |z|) for r up to the
+    hardware path's threshold; above it the polynomial path's error is negligible."""
+    torch = cuda
+    P = capi.probe()
+    out = torch.zeros(8, dtype=torch.float32, device="cuda")
+    assert P.mb200ProbeNormalError(C.c_void_p(out.data_ptr()),
+                                   C.c_void_p(torch.cuda.current_stream().cuda_stream)) == 0
+    torch.cuda.synchronize()
+    dr, dc_hw, ds_hw, dc_poly, ds_poly, r_max = (float(v) for v in out[:6].cpu())
+    print(f"radius {dr:.3e} * max(1, r); hw cos {dc_hw:.3e} sin {ds_hw:.3e}; "
+          f"poly cos {dc_poly:.3e} sin {ds_poly:.3e}; hw up to r = {r_max}")
+    d_trig = max(dc_hw, ds_hw)
+    rounding = 2.0 * 2.0 ** -24
+    # |z| < 1 (then |cos| <= 1 / r): |dz| <= dr * max(1, r) |cos| + r d_trig <= dr + r d_trig
+    worst_small = dr + r_max * d_trig + rounding
+    # |z| >= 1: |dz| / |z| <= dr + d_trig / |cos| <= dr + r d_trig (|cos| >= 1 / r)
+    worst_rel = dr + r_max * d_trig + rounding
+    assert worst_small <= NORMAL_TOL and worst_rel <= NORMAL_TOL, (worst_small, worst_rel)
+    assert max(dc_poly, ds_poly) <= 1e-7
+    # the fallback radius range: r up to sqrt(-2 ln 2^-32) = 6.66
+    assert dr + 6.67 * max(dc_poly, ds_poly) + rounding <= NORMAL_TOL
+
+
 def test_config_normal_every_output(cuda, built):
     """The whole normal call of configs[1] (2^30 words from offset 2^30, seed 1234):
     every output against the oracle restatement of the reference formula (glibc

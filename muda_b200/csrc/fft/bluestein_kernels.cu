@@ -349,6 +349,65 @@ cudaError_t launch_bluestein_global(std::int64_t n, int sign, const Batch1D& b,
   return sign < 0 ? global_dir<-1>(n, b, g, stream) : global_dir<1>(n, b, g, stream);
 }
 
+namespace {
+
+__global__ void __launch_bounds__(kMoveThreads) twiddle_table(float2* tw, std::int64_t n) {
+  for (std::int64_t m = blockIdx.x * static_cast<std::int64_t>(blockDim.x) + threadIdx.x; m < n;
+       m += static_cast<std::int64_t>(gridDim.x) * blockDim.x) {
+    double s, c;
+    sincospi(2.0 * static_cast<double>(m) / static_cast<double>(n), &s, &c);
+    tw[m] = make_float2(static_cast<float>(c), static_cast<float>(-s));
+  }
+}
+
+// chirp[m] = exp(-pi*i*q/n), q = m^2 mod 2n exactly; b[m] = b[mb - m] = conj(chirp[m])
+// (b zero-filled beforehand).
+__global__ void __launch_bounds__(kMoveThreads)
+    chirp_table(std::int64_t n, std::int64_t mb, float2* chirp, float2* b) {
+  for (std::int64_t m = blockIdx.x * static_cast<std::int64_t>(blockDim.x) + threadIdx.x; m < n;
+       m += static_cast<std::int64_t>(gridDim.x) * blockDim.x) {
+    const unsigned long long q =
+        (static_cast<unsigned long long>(m) * static_cast<unsigned long long>(m)) %
+        static_cast<unsigned long long>(2 * n);
+    double s, c;
+    sincospi(static_cast<double>(q) / static_cast<double>(n), &s, &c);
+    const float cf = static_cast<float>(c), sf = static_cast<float>(s);
+    chirp[m] = make_float2(cf, -sf);
+    b[m] = make_float2(cf, sf);
+    if (m > 0) b[mb - m] = make_float2(cf, sf);
+  }
+}
+
+__global__ void __launch_bounds__(kMoveThreads) scale_table(float2* v, std::int64_t n, float f) {
+  for (std::int64_t i = blockIdx.x * static_cast<std::int64_t>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<std::int64_t>(gridDim.x) * blockDim.x)
+    v[i] = make_float2(v[i].x * f, v[i].y * f);
+}
+
+}  // namespace
+
+cudaError_t build_twiddles(float2* tw, std::int64_t n, cudaStream_t stream) noexcept {
+  if (tw == nullptr || n <= 0) return cudaErrorInvalidValue;
+  twiddle_table<<<move_grid(n), kMoveThreads, 0, stream>>>(tw, n);
+  return cudaGetLastError();
+}
+
+cudaError_t build_bluestein_tables(std::int64_t n, float2* chirp, float2* bhat,
+                                   const BluesteinGlobal& g, cudaStream_t stream) noexcept {
+  const std::int64_t mb = bluestein_length(n);
+  if (chirp == nullptr || bhat == nullptr || g.tw_m == nullptr ||
+      (mb > kMaxSinglePass && g.ws2 == nullptr))
+    return cudaErrorInvalidValue;
+  cudaError_t e = cudaMemsetAsync(bhat, 0, static_cast<std::size_t>(mb) * sizeof(float2), stream);
+  if (e != cudaSuccess) return e;
+  chirp_table<<<move_grid(n), kMoveThreads, 0, stream>>>(n, mb, chirp, bhat);
+  if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  if ((e = dense_pow2_fft(mb, -1, bhat, 1, g, stream)) != cudaSuccess) return e;
+  scale_table<<<move_grid(mb), kMoveThreads, 0, stream>>>(bhat, mb,
+                                                          1.0f / static_cast<float>(mb));
+  return cudaGetLastError();
+}
+
 std::int64_t bluestein_length(std::int64_t n) noexcept {
   std::int64_t m = 1;
   while (m < 2 * n - 1) m <<= 1;

@@ -95,6 +95,16 @@ std::shared_ptr<DeviceBuffer> twiddles(std::int64_t n) {
   if (auto hit = twiddle_cache().find(key)) return hit;
   auto buf = DeviceBuffer::make(static_cast<std::size_t>(n) * sizeof(float2));
   if (!buf) return nullptr;
+  if (n > mb200::fft::kMaxHostTwiddles) {
+    // long tables on the device (the host loop would take seconds); ready before return
+    if (mb200::fft::build_twiddles(static_cast<float2*>(buf->ptr), n, nullptr) != cudaSuccess ||
+        cudaStreamSynchronize(nullptr) != cudaSuccess) {
+      (void)cudaGetLastError();
+      return nullptr;
+    }
+    twiddle_cache().put(key, buf);
+    return buf;
+  }
   std::vector<float2> host(static_cast<std::size_t>(n));
   mb200::fft::host_twiddles(n, host.data());
   if (cudaMemcpy(buf->ptr, host.data(), host.size() * sizeof(float2), cudaMemcpyHostToDevice) !=
@@ -107,8 +117,10 @@ std::shared_ptr<DeviceBuffer> twiddles(std::int64_t n) {
 }
 
 // Bluestein tables of length n (chirp, then bhat at an even offset), shared per
-// (device, n) in the twiddle cache under the key (device, -n).
-std::shared_ptr<DeviceBuffer> bluestein_tables(std::int64_t n) {
+// (device, n) in the twiddle cache under the key (device, -n).  Lengths above
+// kMaxHostBluestein are built on the device with the FFT resources of `g`.
+std::shared_ptr<DeviceBuffer> bluestein_tables(std::int64_t n,
+                                               const mb200::fft::BluesteinGlobal* g = nullptr) {
   const int dev = mb200::current_device();
   auto key = std::make_pair(dev, -n);
   if (auto hit = twiddle_cache().find(key)) return hit;
@@ -116,6 +128,17 @@ std::shared_ptr<DeviceBuffer> bluestein_tables(std::int64_t n) {
   const std::int64_t off = (n + 1) / 2 * 2;
   auto buf = DeviceBuffer::make(static_cast<std::size_t>(off + mb) * sizeof(float2));
   if (!buf) return nullptr;
+  if (n > mb200::fft::kMaxHostBluestein) {
+    float2* base = static_cast<float2*>(buf->ptr);
+    if (g == nullptr ||
+        mb200::fft::build_bluestein_tables(n, base, base + off, *g, nullptr) != cudaSuccess ||
+        cudaStreamSynchronize(nullptr) != cudaSuccess) {
+      (void)cudaGetLastError();
+      return nullptr;
+    }
+    twiddle_cache().put(key, buf);
+    return buf;
+  }
   std::vector<float2> host(static_cast<std::size_t>(off + mb));
   mb200::fft::host_bluestein_tables(n, mb, host.data(), host.data() + off);
   if (cudaMemcpy(buf->ptr, host.data(), host.size() * sizeof(float2), cudaMemcpyHostToDevice) !=
@@ -250,9 +273,7 @@ cufftResult configure(Plan& p, int rank, const int* n, const int* inembed, int i
         const std::int64_t mb = mb200::fft::bluestein_length(len);
         auto& g = t.glob;
         g.tw_m = hold(mb);
-        g.chirp = keep(bluestein_tables(len));
-        if (g.tw_m == nullptr || g.chirp == nullptr) return false;
-        g.bhat = g.chirp + (len + 1) / 2 * 2;
+        if (g.tw_m == nullptr) return false;
         const std::int64_t row_bytes = mb * static_cast<std::int64_t>(sizeof(float2));
         g.ws_rows = std::max<std::int64_t>(
             1, std::min<std::int64_t>(count, static_cast<std::int64_t>(kBluesteinWsBytes) /
@@ -270,6 +291,10 @@ cufftResult configure(Plan& p, int rank, const int* n, const int* inembed, int i
           g.ws2 = const_cast<float2*>(keep(DeviceBuffer::make(bytes)));
           if (g.tw_n1 == nullptr || g.tw_n2 == nullptr || g.ws2 == nullptr) return false;
         }
+        // the tables last: long ones are built with the FFT resources set up above
+        g.chirp = keep(bluestein_tables(len, &g));
+        if (g.chirp == nullptr) return false;
+        g.bhat = g.chirp + (len + 1) / 2 * 2;
         return true;
       }
       default:

@@ -72,7 +72,13 @@ cudaError_t launch_bluestein(std::int64_t n, int sign, const Batch1D& b, const f
 // dense rows of Mb, forward FFT, multiply by bhat, inverse FFT, chirp-multiplied
 // scatter.  An inner length above kMaxSinglePass uses the two-pass split
 // Mb = n1 * n2 with the scratch rows ws2.  In-place calls are allowed.
-constexpr std::int64_t kMaxBluesteinGlobal = std::int64_t{1} << 20;
+// Up to 2^27, so that Mb <= 2^28 = kMaxSinglePass^2 (the two-pass split's limit).
+constexpr std::int64_t kMaxBluesteinGlobal = std::int64_t{1} << 27;
+// Tables of lengths up to these are built on the host in double precision; longer ones on
+// the device (build_twiddles, build_bluestein_tables), where the host work would take
+// seconds.
+constexpr std::int64_t kMaxHostTwiddles = std::int64_t{1} << 22;
+constexpr std::int64_t kMaxHostBluestein = std::int64_t{1} << 20;
 struct BluesteinGlobal {
   const float2* chirp;
   const float2* bhat;
@@ -88,6 +94,14 @@ cudaError_t launch_bluestein_global(std::int64_t n, int sign, const Batch1D& b,
                                     const BluesteinGlobal& g, cudaStream_t stream) noexcept;
 // Fills chirp[0 .. n) and bhat[0 .. Mb) in double precision, rounded once.
 void host_bluestein_tables(std::int64_t n, std::int64_t mb, float2* chirp, float2* bhat) noexcept;
+// Device versions for long lengths: tw[m] = exp(-2*pi*i*m/n) from double sincospi, rounded
+// once; chirp as above from double sincospi of the exact (m^2 mod 2n)/n; bhat = the fp32
+// FFT of the rounded b, scaled by 1/Mb (exact), computed in place in bhat with g's
+// twiddles and scratch (g.tw_m, and for Mb > kMaxSinglePass g.n1, g.n2, g.tw_n1, g.tw_n2,
+// g.ws2).  Stream-ordered.
+cudaError_t build_twiddles(float2* tw, std::int64_t n, cudaStream_t stream) noexcept;
+cudaError_t build_bluestein_tables(std::int64_t n, float2* chirp, float2* bhat,
+                                   const BluesteinGlobal& g, cudaStream_t stream) noexcept;
 
 // Real-data transforms of even length L = 2M through a length-M complex FFT of
 // the reals read as M complex pairs, z[n] = x[2n] + i x[2n+1].  Rows are indexed

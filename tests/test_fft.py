@@ -222,6 +222,41 @@ def test_gpu_bluestein_global_lengths(cuda, built, n):
 
 
 @pytest.mark.gpu
+@pytest.mark.parametrize("n,batch", [((1 << 20) + 7, 2), (3 * (1 << 21) + 1, 1),
+                                     ((1 << 25) + 1, 1)])
+def test_gpu_bluestein_long_lengths(cuda, built, n, batch):
+    """Lengths above 2^20 (the reference transforms any length): Bluestein through global
+    memory with chirp, inner twiddles and bhat built on the device, inner lengths 2^22 ..
+    2^27 through the two-pass split; against numpy's float64 FFT, both directions."""
+    rng = np.random.default_rng(n)
+    x = rand_c64(rng, n * batch)
+    xd = x.reshape(batch, n).astype(np.complex128)
+    for sign in (-1, 1):
+        got = gpu_fft(cuda, x, [n], batch, sign)
+        want = (np.fft.fft(xd, axis=1) if sign < 0 else np.fft.ifft(xd, axis=1) * n).reshape(-1)
+        assert rel_l2_per_transform(got, want, n, batch) <= TOL, (n, sign)
+
+
+@pytest.mark.gpu
+def test_gpu_bluestein_longest_length(cuda, built):
+    """The longest non-power-of-two length served, 2^27 - 1 (inner length 2^28): the
+    forward transform at three frequencies against float64 sums, and the round trip."""
+    n = (1 << 27) - 1
+    rng = np.random.default_rng(5)
+    x = rand_c64(rng, n)
+    got = gpu_fft(cuda, x, [n], 1, -1)
+    xd = x.astype(np.complex128)
+    idx = np.arange(n, dtype=np.float64)
+    for k in (1, n // 2, n - 1):
+        w = np.exp(-2j * np.pi * ((idx * k) % n) / n)
+        want = np.dot(xd, w)
+        scale = np.sqrt(n) * np.sqrt(np.mean(np.abs(xd) ** 2))
+        assert abs(got[k] - want) <= 1e-5 * scale, (k, abs(got[k] - want) / scale)
+    back = gpu_fft(cuda, got, [n], 1, 1) / n
+    assert rel_l2_per_transform(back, x, n, 1) <= TOL
+
+
+@pytest.mark.gpu
 @pytest.mark.parametrize("n", BLUESTEIN)
 def test_gpu_bluestein_lengths(cuda, built, n):
     """Batches that fill several transforms per CTA plus a partial last CTA, both

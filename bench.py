@@ -433,7 +433,10 @@ def suite_sgemm(s: Suite) -> dict:
                               "tensor-tf32x3"),
            "launches": launches,
            "pedantic_ffma": {"ms": ms_ffma, "TFLOP/s": flop / (ms_ffma * 1e-3) / 1e12,
-                             "kernel": "gemm_simt<float,128,64,8,8,4>"}}
+                             "frac_of_ffma_peak": flop / (ms_ffma * 1e-3) / 1e12 /
+                             FFMA_PEAK_TFLOPS,
+                             "kernel": "gemm_ffma_vec<false,false,stream-K> + "
+                                       "ffma_stream_reduce"}}
     if s.cpu:
         import oracle
         A = a.cpu().numpy()
@@ -791,11 +794,35 @@ def suite_fft(s: Suite) -> dict:
         assert L.cufftExecC2C(p, ptr, ptr, -1) == 0
         assert L.cufftExecC2C(p, ptr, ptr, 1) == 0
     ms, launches = s.time(call, launches_per_call=2)
-    assert L.cufftDestroy(p) == 0
     per_dir = 2 * 8 * n * batch
+    # end to end through the C ABI with host buffers: pinned input copied in, forward
+    # then inverse, result copied back, all inside the timed region
+    e2e = None
+    if s.shard == 1:
+        h_in = torch.empty(2 * n * batch, dtype=torch.float32, pin_memory=True)
+        h_in.copy_(x)
+        h_out = torch.empty_like(h_in)
+        y = torch.empty_like(x)
+        py = C.c_void_p(y.data_ptr())
+
+        def e2e_call():
+            y.copy_(h_in, non_blocking=True)
+            assert L.cufftExecC2C(p, py, py, -1) == 0
+            assert L.cufftExecC2C(p, py, py, 1) == 0
+            h_out.copy_(y, non_blocking=True)
+        steps, warm = s.steps, s.warmup
+        s.steps, s.warmup = 3, 1
+        e_ms, _ = s.time(e2e_call)
+        s.steps, s.warmup = steps, warm
+        e2e = {"value": 2 * per_dir / (e_ms * 1e-3) / 1e9, "unit": "GB/s", "ms": e_ms,
+               "h2d_bytes_per_step": 8 * n * batch, "d2h_bytes_per_step": 8 * n * batch,
+               "path": "pinned host -> device copy, cufftExecC2C forward + inverse in place, "
+                       "device -> pinned host copy"}
+        del h_in, h_out, y
+    assert L.cufftDestroy(p) == 0
     gbs = 2 * per_dir / (ms * 1e-3) / 1e9
     flops = 2 * 5 * n * 12 * batch
-    out = {"value": gbs, "unit": "GB/s", "ms": ms, "dtype": "c64",
+    out = {"value": gbs, "unit": "GB/s", "ms": ms, "dtype": "c64", "e2e": e2e,
            "gflops_5nlogn": flops / (ms * 1e-3) / 1e9,
            "config": f"N {n} x batch {batch}, forward + inverse in place, "
                      f"data {per_dir / 2e9:.2f} GB > L2",
@@ -1196,7 +1223,7 @@ def suite_dgemm(s: Suite) -> dict:
     tf = flop / (ms * 1e-3) / 1e12
     out = {"value": tf, "unit": "TFLOP/s", "ms": ms, "dtype": "f64",
            "config": f"{m}x{n}x{k} fp64 N,N, L2 flushed before each call",
-           "roofline": s.roof("dgemm_kernel<128,128,false,false>", tf, "fp64"),
+           "roofline": s.roof("dgemm_kernel<128,64,false,false>", tf, "fp64"),
            "launches": launches}
     if s.cpu:
         import oracle
@@ -1361,8 +1388,9 @@ def run_spmv_dist(args) -> None:
         print(json.dumps({"routine": "spmv_dist", **res}), flush=True)
     if world > 1:
         dist.destroy_process_group()
-    if not res["y_identical_peer_vs_nccl"]:
-        raise SystemExit("peer exchange result differs from the NCCL exchange")
+    if not res["y_check"]:
+        raise SystemExit("distributed SpMV arms disagree (peer vs NCCL bit for bit, "
+                         "overlapped vs sequential within the summation bound)")
 
 
 def spmv_dist_measure(args, torch, dist, world: int, rank: int, local: int) -> dict:
@@ -1370,21 +1398,36 @@ def spmv_dist_measure(args, torch, dist, world: int, rank: int, local: int) -> d
     is fixed, its rows split into nnz-balanced blocks).  Each step gathers x into
     local HBM and runs the local cusparseSpMV.  Two exchanges are timed on the same
     blocks: the NVLink peer-memory pull of libmuda_peer and NCCL's
-    all_gather_into_tensor; both must give the same y, bit for bit.  The value is the
-    faster of the two (named in config.exchange; the peer pull wins at 2 ranks, NCCL at
-    8), the other is reported beside it.  Reported are the step time (max over ranks)
-    with and without the exchange.  `dist` is None on one rank."""
+    all_gather_into_tensor; both must give the same y, bit for bit.  Each is timed twice:
+    exchange then product, and overlapped (DistSpMV overlap=True: the product over this
+    rank's own x block runs on a side stream during the exchange, the rest after it;
+    the overlapped y must match the sequential one within the float32 summation bound).
+    The value is the fastest of the four (named in config.exchange), the others are
+    reported beside it.  Reported are the step time (max over ranks) with and without
+    the exchange.  `dist` is None on one rank."""
     from muda_b200 import synth
     from muda_b200.dist_spmv import DistSpMV
     group = None
     rows = (1 << 22) // args.scale
     mtx = synth.powerlaw_csr(torch, rows, rows, seed=7)
     nnz = mtx["nnz"]
-    arms = {ex: DistSpMV.from_full(torch, dist, group, mtx["row_offsets"], mtx["col_ind"],
-                                   mtx["values"], rows, exchange=ex) for ex in ("peer", "nccl")}
+    names = ("peer", "nccl", "peer+overlap", "nccl+overlap")
+    arms = {nm: DistSpMV.from_full(torch, dist, group, mtx["row_offsets"], mtx["col_ind"],
+                                   mtx["values"], rows, exchange=nm.split("+")[0],
+                                   overlap=nm.endswith("overlap")) for nm in names}
     d = arms["peer"]
     x_local = d.x_slice(mtx["x"])
     ys = {ex: torch.zeros(max(d.rows, 1), dtype=torch.float32, device="cuda") for ex in arms}
+    # |A| |x| per local row, for the bound on the overlapped (two-part) row sums
+    o64 = mtx["row_offsets"][d.row_begin:d.row_end + 1].to(torch.int64)
+    e0, e1 = int(o64[0].item()), int(o64[-1].item())
+    ax = (mtx["values"][e0:e1].abs() * mtx["x"][mtx["col_ind"][e0:e1].to(torch.int64)].abs())
+    row_id = torch.repeat_interleave(torch.arange(d.rows, device="cuda"), o64[1:] - o64[:-1])
+    mag = torch.zeros(max(d.rows, 1), dtype=torch.float64, device="cuda")
+    mag.index_add_(0, row_id, ax.double())
+    row_len = torch.zeros(max(d.rows, 1), dtype=torch.float64, device="cuda")
+    row_len[:d.rows] = (o64[1:] - o64[:-1]).double()
+    del o64, ax, row_id
     del mtx
     torch.cuda.empty_cache()
     flush = torch.empty(64 << 20, dtype=torch.float32, device="cuda")  # 256 MB > L2
@@ -1401,21 +1444,29 @@ def spmv_dist_measure(args, torch, dist, world: int, rank: int, local: int) -> d
             flush.fill_(float(it))
             barrier()
             ev[0].record()
-            arm.gather_x(x_local)
-            ev[1].record()
-            arm.local(1.0, 0.0, ys[ex])
+            if arm.overlap:
+                arm.spmv(1.0, x_local, 0.0, ys[ex])
+                ev[1].record()
+            else:
+                arm.gather_x(x_local)
+                ev[1].record()
+                arm.local(1.0, 0.0, ys[ex])
             ev[2].record()
             torch.cuda.synchronize()
             if it >= args.warmup:
                 full_ms, local_ms, gather_ms = times[ex]
-                gather_ms.append(ev[0].elapsed_time(ev[1]))
-                local_ms.append(ev[1].elapsed_time(ev[2]))
+                gather_ms.append(ev[0].elapsed_time(ev[1]) if not arm.overlap else 0.0)
+                local_ms.append(ev[1].elapsed_time(ev[2]) if not arm.overlap else 0.0)
                 full_ms.append(ev[0].elapsed_time(ev[2]))
     barrier()
-    status = d._peer.take_status()
-    same = bool(torch.equal(ys["peer"], ys["nccl"])) and status == 0
+    status = d._peer.take_status() | arms["peer+overlap"]._peer.take_status()
+    bound = (row_len + 3) * 2.0 ** -24 * mag + 1e-30
+    within = bool((ys["peer+overlap"].double() - ys["peer"].double()).abs()
+                  .le(2 * bound).all().item())
+    same = (bool(torch.equal(ys["peer"], ys["nccl"])) and status == 0 and
+            bool(torch.equal(ys["peer+overlap"], ys["nccl+overlap"])) and within)
     check = torch.tensor([0 if same else 1], dtype=torch.int32, device="cuda")
-    stats = torch.tensor([float(np.mean(v)) for ex in ("peer", "nccl") for v in times[ex]],
+    stats = torch.tensor([float(np.mean(v)) for ex in names for v in times[ex]],
                          device="cuda")
     if world > 1:
         dist.all_reduce(stats, op=dist.ReduceOp.MAX)
@@ -1425,12 +1476,19 @@ def spmv_dist_measure(args, torch, dist, world: int, rank: int, local: int) -> d
         parts = [torch.zeros_like(shares) for _ in range(world)]
         dist.all_gather(parts, shares)
         shares = torch.cat(parts)
-    p_full, p_loc, p_gat, n_full, n_loc, n_gat = (float(v) for v in stats.cpu())
+    st = [float(v) for v in stats.cpu()]
+    per = {nm: st[3 * i:3 * i + 3] for i, nm in enumerate(names)}  # full, local, gather
     alg_bytes = nnz * 8 + (rows + 1) * 4 + rows * 4 + rows * 4
     ok = int(check.item()) == 0
-    peer_wins = p_full <= n_full
-    full, loc, gat = (p_full, p_loc, p_gat) if peer_wins else (n_full, n_loc, n_gat)
-    other = ("nccl_all_gather", n_full, n_gat) if peer_wins else ("peer_pull", p_full, p_gat)
+    best = min(names, key=lambda nm: per[nm][0])
+    full = per[best][0]
+    # the exchange's own time and the kernel-only time come from the sequential arm
+    # of the same exchange
+    _, loc, gat = per[best.split("+")[0]]
+    exchange_name = {"peer": "peer-memory pull over NVLink (libmuda_peer)",
+                     "nccl": "NCCL all_gather_into_tensor"}[best.split("+")[0]]
+    if best.endswith("overlap"):
+        exchange_name += ", overlapped with the own-block product"
     nz = shares.cpu().numpy()
     res = {
         "metric": "SpMV GB/s (algorithmic bytes of the whole matrix / step time, max over "
@@ -1441,13 +1499,15 @@ def spmv_dist_measure(args, torch, dist, world: int, rank: int, local: int) -> d
         "config": {"workload": f"{rows} x {rows}, nnz {nnz}, rows split into "
                                f"{world} nnz-balanced blocks", "l2": "256 MB flush "
                                "before each step",
-                   "exchange": "peer-memory pull over NVLink (libmuda_peer)" if peer_wins
-                               else "NCCL all_gather_into_tensor"},
+                   "exchange": exchange_name},
         "kernel_only": {"ms": loc, "GB/s": alg_bytes / (loc * 1e-3) / 1e9},
-        "exchange_ms": gat, "exchange_share": gat / full if full > 0 else None,
-        other[0]: {"ms_per_step": other[1], "exchange_ms": other[2],
-                   "GB/s": alg_bytes / (other[1] * 1e-3) / 1e9},
-        "y_identical_peer_vs_nccl": ok, "nnz_per_rank": [int(v) for v in nz],
+        "exchange_ms": gat,
+        # the part of the step the exchange adds over the product alone
+        "exchange_share": max(full - loc, 0.0) / full if full > 0 else None,
+        "arms": {nm: {"ms_per_step": per[nm][0], "GB/s": alg_bytes / (per[nm][0] * 1e-3) / 1e9,
+                      **({"exchange_ms": per[nm][2]} if not nm.endswith("overlap") else {})}
+                 for nm in names},
+        "y_check": ok, "nnz_per_rank": [int(v) for v in nz],
         "imbalance": float(nz.max() / max(float(nz.mean()), 1.0)),
         "roofline": {"bound": "hbm", "kernel": "spmv_csr_tiles (per rank) + x exchange",
                      "frac": alg_bytes / (full * 1e-3) / 1e9 / world / _peaks()["hbm_gbs"],
@@ -1471,6 +1531,11 @@ def summarize(suite: dict | None) -> dict | None:
         out[name] = [float(f"{r['value']:.5g}"), r["unit"],
                      None if frac is None else round(float(frac), 3),
                      None if r.get("ms") is None else float(f"{r['ms']:.4g}")]
+        if r.get("exchange_share") is not None:  # the x exchange's share of the SpMV step
+            out[name].append({"exchange_share": round(float(r["exchange_share"]), 3)})
+        if (r.get("gather_ceiling") or {}).get("spmv_frac_of_ceiling") is not None:
+            out[name].append({"frac_of_gather_ceiling":
+                              round(float(r["gather_ceiling"]["spmv_frac_of_ceiling"]), 3)})
     return out
 
 

@@ -278,7 +278,17 @@ cublasStatus_t run_gemm(BlasContext& ctx, Elem type, cublasOperation_t ta, cubla
     e = run_tf32x3(ctx, g, stream);
   if (e == cudaErrorNotSupported) {
     (void)cudaGetLastError();
-    e = mb200::blas::launch_gemm_simt(g, stream);
+    const std::size_t need = mb200::blas::gemm_simt_workspace(g);
+    if (need == 0) {
+      e = mb200::blas::launch_gemm_simt(g, stream);
+    } else {
+      // K split across CTAs, partial sums in the handle's workspace
+      BufferUse use(ctx, stream);
+      if (!use.ok()) return CUBLAS_STATUS_EXECUTION_FAILED;
+      void* ws = use.workspace(need);
+      e = mb200::blas::launch_gemm_simt_split(g, ws, ws ? use.workspace_bytes() : 0, stream);
+      if (e == cudaSuccess) e = use.done();
+    }
   }
   return e == cudaSuccess ? CUBLAS_STATUS_SUCCESS : CUBLAS_STATUS_EXECUTION_FAILED;
 }

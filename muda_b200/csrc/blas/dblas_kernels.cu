@@ -440,7 +440,8 @@ int dgemv_chunks(bool trans, int m, int n) {
 // 2*tm + 32*q + e and columns 2*tn + 32*q' + f (q < TM/2, e, f < 2), so the double2
 // reads of a k-row by the 16 threads of a half-warp are one contiguous 256 bytes.
 template <int BM, int BN, bool TA, bool TB>
-__global__ void __launch_bounds__(kThreads, 1) dgemm_kernel(const DgemmArgs g) {
+__global__ void __launch_bounds__(kThreads, BM * BN >= 128 * 128 ? 1 : 2)
+    dgemm_kernel(const DgemmArgs g) {
   constexpr int BK = 8;
   constexpr int TM = BM / 16, TN = BN / 16;
   constexpr int A_PER = BM * BK / kThreads;
@@ -672,9 +673,11 @@ cudaError_t launch_dgemv(bool trans, int m, int n, double alpha, const double* a
 cudaError_t launch_dgemm(const DgemmArgs& g, cudaStream_t stream) noexcept {
   if (g.m <= 0 || g.n <= 0 || g.batch <= 0) return cudaSuccess;
   const int sms = sm_count(current_device());
-  const long long big_tiles = static_cast<long long>((g.m + 127) / 128) * ((g.n + 127) / 128) *
+  // 128 x 64 tiles, two CTAs per SM, when they fill the GPU twice (at 4096^3 they run
+  // 5% faster than 128 x 128 tiles at one CTA per SM, and 24% faster than 64 x 64)
+  const long long big_tiles = static_cast<long long>((g.m + 127) / 128) * ((g.n + 63) / 64) *
                               g.batch;
-  if (big_tiles >= 2ll * (sms > 0 ? sms : 148)) return launch_dgemm_tiles<128, 128>(g, stream);
+  if (big_tiles >= 2ll * (sms > 0 ? sms : 148)) return launch_dgemm_tiles<128, 64>(g, stream);
   return launch_dgemm_tiles<64, 64>(g, stream);
 }
 

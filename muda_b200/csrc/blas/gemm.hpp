@@ -32,6 +32,13 @@ struct GemmArgs {
 // Register-blocked FFMA kernel: any type, transposes, leading dimensions and
 // strides (fp32 accumulate).  The fp32 path of cublasSgemm.
 cudaError_t launch_gemm_simt(const GemmArgs& g, cudaStream_t stream) noexcept;
+// The same kernel with K split across CTAs for batch-1 problems whose tiles cannot fill
+// the GPU: raw per-split sums in `workspace` (gemm_simt_workspace(g) bytes, 0 when no
+// split is used), added in split order by one more pass (deterministic).  Without
+// enough workspace it runs launch_gemm_simt.
+std::size_t gemm_simt_workspace(const GemmArgs& g) noexcept;
+cudaError_t launch_gemm_simt_split(const GemmArgs& g, void* workspace, std::size_t ws_bytes,
+                                   cudaStream_t stream) noexcept;
 
 // tcgen05 tensor-core kernel for 16-bit A/B (bf16 or fp16) with fp32 accumulation
 // in tensor memory.  Returns cudaErrorNotSupported when the shape or layout is not

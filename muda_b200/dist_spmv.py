@@ -186,6 +186,32 @@ class _CudaLocal:
             self.h = C.c_void_p()
 
 
+def split_by_columns(torch, offsets, col_ind, values, base: int, lo: int, hi: int):
+    """Splits a CSR block into the entries whose (0-based) column lies in [lo, hi) and
+    the rest, both CSR with the same rows, entries kept in row order.  The first part's
+    columns are rebased to lo (still in the index base), so that it indexes x[lo:hi]."""
+    offs = offsets.to(torch.int64)
+    rows = offs.numel() - 1
+    nnz = int(offs[-1].item() - offs[0].item())
+    cols0 = col_ind[:nnz].to(torch.int64) - base
+    own = (cols0 >= lo) & (cols0 < hi)
+    row_id = torch.repeat_interleave(torch.arange(rows, device=offs.device),
+                                     (offs[1:] - offs[:-1]))
+    parts = []
+    for mask, shift in ((own, lo), (~own, 0)):
+        counts = torch.bincount(row_id[mask], minlength=rows)
+        o = torch.zeros(rows + 1, dtype=torch.int64, device=offs.device)
+        o[1:] = torch.cumsum(counts, 0)
+        c = (cols0[mask] - shift + base).to(torch.int32).contiguous()
+        v = values[:nnz][mask].contiguous()
+        # keep the arrays non-empty so that their device pointers are valid
+        if c.numel() == 0:
+            c = torch.full((1,), base, dtype=torch.int32, device=offs.device)
+            v = torch.zeros(1, dtype=values.dtype, device=offs.device)
+        parts.append(((o + base).to(torch.int32).contiguous(), c, v))
+    return parts[0], parts[1]
+
+
 class DistSpMV:
     """One rank's share of a row-block distributed CSR matrix.
 
@@ -194,11 +220,20 @@ class DistSpMV:
     beta, y_local)`` gathers x and computes this rank's rows of y.  With
     ``dist=None`` the object is a single rank (no process group, x is copied).
     ``exchange`` selects the gather: "nccl" (all_gather_into_tensor, or the gloo
-    all_gather on CPU ranks) or "peer" (NVLink peer-memory pull, CUDA path only)."""
+    all_gather on CPU ranks) or "peer" (NVLink peer-memory pull, CUDA path only).
+
+    With ``overlap=True`` (CUDA path) the block is split once into the entries whose
+    column lies in this rank's own x block and the rest, each kept in row order.
+    ``spmv`` then computes y = alpha * A_own * x_local + beta * y on a side stream
+    while x is exchanged, and y = alpha * A_rest * x + y after it: the exchange is
+    hidden behind the own-block product (half of the entries at 2 ranks, 1/N at N).
+    Each row's sum is then formed in two parts, so y differs from the one-pass
+    product in the last bits."""
 
     def __init__(self, torch, dist, group, *, offsets, col_ind, values, row_begin: int,
                  row_end: int, cols: int, base: int = 0,
-                 local_spmv: Callable | None = None, device=None, exchange: str = "nccl"):
+                 local_spmv: Callable | None = None, device=None, exchange: str = "nccl",
+                 overlap: bool = False, own_cols: tuple[int, int] | None = None):
         self.torch, self.dist, self.group = torch, dist, group
         self.world = dist.get_world_size(group) if dist is not None else 1
         self.rank = dist.get_rank(group) if dist is not None else 0
@@ -217,16 +252,35 @@ class DistSpMV:
         self._x_ptr = 0
         self.x_full = torch.zeros(self.xb * self.world if self._peer is None else 1,
                                   dtype=torch.float32, device=dev)
+        self.overlap = overlap
+        self._own = self._rest = None
         if local_spmv is None:
             self._local = _CudaLocal(torch, offsets, col_ind, values, self.rows, cols,
                                      self.nnz, base) if self.rows > 0 else None
         else:
             self._local = lambda x, y, a, b: local_spmv(offsets, col_ind, values, x, y, a, b)
         self._keep = (offsets, col_ind, values)
+        if overlap and self.rows > 0:
+            lo, hi = own_cols if own_cols is not None else (self.rank * self.xb,
+                                                            min(cols, (self.rank + 1) * self.xb))
+            self._own_lo, self._own_n = lo, max(hi - lo, 0)
+            own, rest = split_by_columns(torch, offsets, col_ind, values, base, lo, hi)
+            if local_spmv is None:
+                self._own = _CudaLocal(torch, *own, self.rows, max(self._own_n, 1),
+                                       int(own[0][-1].item()) - base, base)
+                self._rest = _CudaLocal(torch, *rest, self.rows, cols,
+                                        int(rest[0][-1].item()) - base, base)
+                self._side = torch.cuda.Stream()
+            else:
+                self._own = lambda x, y, a, b: local_spmv(*own, x, y, a, b)
+                self._rest = lambda x, y, a, b: local_spmv(*rest, x, y, a, b)
+                self._side = None
+            self._keep = self._keep + own + rest
 
     @classmethod
     def from_full(cls, torch, dist, group, row_offsets, col_ind, values, cols: int, *,
-                  base: int = 0, local_spmv: Callable | None = None, exchange: str = "nccl"):
+                  base: int = 0, local_spmv: Callable | None = None, exchange: str = "nccl",
+                  overlap: bool = False):
         """Slices this rank's nnz-balanced row block out of the full CSR matrix (the
         same on every rank); the block's offsets are rebased so its first entry is
         entry 0 (plus the index base, which offsets and columns keep)."""
@@ -242,7 +296,7 @@ class DistSpMV:
         vals_l = values[e0:e1].contiguous()
         obj = cls(torch, dist, group, offsets=offs, col_ind=cols_l, values=vals_l, row_begin=r0,
                   row_end=r1, cols=cols, base=base, local_spmv=local_spmv,
-                  device=row_offsets.device, exchange=exchange)
+                  device=row_offsets.device, exchange=exchange, overlap=overlap)
         obj.bounds = bounds
         return obj
 
@@ -285,6 +339,25 @@ class DistSpMV:
         self._local(self.x_full[:self.cols], y_local, alpha, beta)
 
     def spmv(self, alpha: float, x_local, beta: float, y_local) -> None:
+        if self.overlap and self.rows > 0 and self._side is None:  # pluggable product
+            self._own(x_local, y_local, alpha, beta)
+            self.gather_x(x_local)
+            self._rest(self.x_full[:self.cols], y_local, alpha, 1.0)
+            return
+        if self.overlap and self.rows > 0:
+            torch = self.torch
+            main = torch.cuda.current_stream()
+            self._side.wait_stream(main)  # x_local and y are ready
+            with torch.cuda.stream(self._side):
+                # own-block columns index x_local (rebased), while x is exchanged
+                self._own.at(x_local.data_ptr(), y_local, alpha, beta)
+            self.gather_x(x_local)
+            main.wait_stream(self._side)
+            if self._peer is not None:
+                self._rest.at(self._x_ptr, y_local, alpha, 1.0)
+            else:
+                self._rest(self.x_full[:self.cols], y_local, alpha, 1.0)
+            return
         self.gather_x(x_local)
         self.local(alpha, beta, y_local)
 
@@ -292,6 +365,10 @@ class DistSpMV:
         if isinstance(self._local, _CudaLocal):
             self._local.close()
         self._local = None
+        for part in (self._own, self._rest):
+            if isinstance(part, _CudaLocal):
+                part.close()
+        self._own = self._rest = None
         if self._peer is not None:
             self._peer.close()
             self._peer = None

@@ -234,6 +234,81 @@ def test_gpu_sgemm_split_tf32_tensor_core(cuda, built, m, n, k, batch, ta, tb):
 
 
 @pytest.mark.gpu
+@pytest.mark.parametrize("m,n,k,batch,pad_c", [(2048, 1280, 520, 1, 4), (1024, 1024, 1024, 1, 4),
+                                               (1028, 516, 2052, 1, 4), (1536, 1024, 256, 2, 4),
+                                               (2048, 1280, 96, 1, 3), (512, 512, 4096, 1, 3)])
+@pytest.mark.parametrize("ta,tb", [(False, False), (True, False), (False, True), (True, True)])
+def test_gpu_sgemm_ffma_aligned_operands(cuda, built, m, n, k, batch, pad_c, ta, tb):
+    """The FFMA kernel for 16-byte aligned fp32 operands (CUBLAS_PEDANTIC_MATH; leading
+    dimensions and strides multiples of 4, m, n, k multiples of 4): whole-grid and
+    split-K launches, partial tiles in m, n and k, batches, beta != 0, and C with a
+    leading dimension that rules out 16-byte stores.  Every entry within 1e-5 of
+    |alpha| (|op(A)| |op(B)|)_ij + |beta C_ij| of the float64 product, padding untouched."""
+    torch = cuda
+    rng = np.random.default_rng(m + 5 * n + 11 * k + batch)
+    lda = (k if ta else m) + 4
+    ldb = (n if tb else k) + 8
+    ldc = m + pad_c
+    sa = lda * (m if ta else k) + 4
+    sb = ldb * (k if tb else n) + 12
+    sc = ldc * n + 5
+    A = rng.uniform(-1, 1, sa * batch).astype(np.float32)
+    B = rng.uniform(-1, 1, sb * batch).astype(np.float32)
+    C0 = rng.uniform(-1, 1, sc * batch).astype(np.float32)
+    alpha, beta = 0.75, (-0.5 if k % 8 else 0.0)
+    dA, dB, dC = (torch.from_numpy(x).cuda() for x in (A, B, C0))
+    b = Blas(torch)
+    assert b.L.cublasSetMathMode(b.h, capi.CUBLAS_PEDANTIC_MATH) == 0
+    st = b.L.cublasSgemmStridedBatched(
+        b.h, OPS[ta], OPS[tb], m, n, k, C.byref(C.c_float(alpha)), C.c_void_p(dA.data_ptr()),
+        lda, sa, C.c_void_p(dB.data_ptr()), ldb, sb, C.byref(C.c_float(beta)),
+        C.c_void_p(dC.data_ptr()), ldc, sc, batch)
+    torch.cuda.synchronize()
+    b.close()
+    assert st == 0
+    got = dC.cpu().numpy()
+    mask = np.ones(len(got), bool)
+    for z in range(batch):
+        a = _op_dense(A, lda, sa, z, m, k, ta)
+        bb = _op_dense(B, ldb, sb, z, k, n, tb)
+        idx = (z * sc + np.arange(n)[None, :] * ldc + np.arange(m)[:, None])
+        c0 = C0[idx].astype(np.float64)
+        want = alpha * (a @ bb) + beta * c0
+        scale = abs(alpha) * (np.abs(a) @ np.abs(bb)) + abs(beta) * np.abs(c0)
+        err = np.abs(got[idx].astype(np.float64) - want)
+        assert np.all(err <= 1e-5 * scale + 1e-30), float((err / scale).max())
+        mask[idx.reshape(-1)] = False
+    assert np.array_equal(got[mask], C0[mask])
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("m,n,k", [(1024, 1024, 1024), (516, 1028, 3076), (128, 128, 4096)])
+def test_gpu_sgemm_ffma_stream_k_is_deterministic(cuda, built, m, n, k):
+    """Problems with fewer 128 x 128 tiles than SMs run as equal k runs per CTA whose
+    pieces are added back in k order: repeated calls give the same bits."""
+    torch = cuda
+    g = torch.Generator(device="cuda").manual_seed(m + n + k)
+    a = torch.rand(m * k, device="cuda", generator=g) - 0.5
+    bm = torch.rand(k * n, device="cuda", generator=g) - 0.5
+    outs = []
+    b = Blas(torch)
+    assert b.L.cublasSetMathMode(b.h, capi.CUBLAS_PEDANTIC_MATH) == 0
+    for _ in range(3):
+        c = torch.full((m * n,), float("nan"), device="cuda")
+        assert b.L.cublasSgemm_v2(b.h, 0, 0, m, n, k, C.byref(C.c_float(1.0)),
+                                  C.c_void_p(a.data_ptr()), m, C.c_void_p(bm.data_ptr()), k,
+                                  C.byref(C.c_float(0.0)), C.c_void_p(c.data_ptr()), m) == 0
+        outs.append(c)
+    torch.cuda.synchronize()
+    b.close()
+    want = (a.double().view(k, m).T @ bm.double().view(n, k).T)  # m x n
+    got = outs[0].view(n, m).T.double()
+    assert float((got - want).norm() / want.norm()) <= 1e-6
+    for o in outs[1:]:
+        assert torch.equal(o, outs[0])
+
+
+@pytest.mark.gpu
 def test_gpu_sgemm_error_flat_in_k(cuda, built):
     """The split-tf32 path restarts its tensor-memory accumulator every two k-blocks and
     adds the chunks with round-to-nearest fp32 adds, so its error does not grow with K

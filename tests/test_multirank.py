@@ -66,7 +66,7 @@ def _cpu_local(offsets, col_ind, values, x, y, alpha, beta):
     y[:len(out)] = __import__("torch").from_numpy(out)
 
 
-def _spmv_worker(rank, world, port, rows, cols, heavy, alpha, beta):
+def _spmv_worker(rank, world, port, rows, cols, heavy, alpha, beta, overlap=False):
     import torch
 
     from muda_b200.dist_spmv import DistSpMV
@@ -75,7 +75,8 @@ def _spmv_worker(rank, world, port, rows, cols, heavy, alpha, beta):
         ro, ci, va, x = _csr(11, rows, cols, heavy)
         y0 = np.random.default_rng(3).uniform(-1, 1, rows).astype(np.float32)
         d = DistSpMV.from_full(torch, dist, None, torch.from_numpy(ro), torch.from_numpy(ci),
-                               torch.from_numpy(va), cols, local_spmv=_cpu_local)
+                               torch.from_numpy(va), cols, local_spmv=_cpu_local,
+                               overlap=overlap)
         assert d.bounds == nnz_balanced_bounds(ro, world)
         x_local = d.x_slice(torch.from_numpy(x))
         y_local = torch.from_numpy(y0[d.row_begin:d.row_end].copy())
@@ -91,7 +92,12 @@ def _spmv_worker(rank, world, port, rows, cols, heavy, alpha, beta):
         y = np.concatenate([parts[i][:d.bounds[i + 1] - d.bounds[i]].numpy()
                             for i in range(world)])
         want = oracle.spmv_csr(ro, ci, va, x, alpha=alpha, beta=beta, y=y0.copy(), threads=1)
-        assert np.array_equal(y.view(np.uint32), want.view(np.uint32))
+        if not overlap:
+            assert np.array_equal(y.view(np.uint32), want.view(np.uint32))
+        else:
+            # each row summed in two parts (own x block, then the rest): within the
+            # float32 summation bound of the one-pass product
+            _assert_within_sum_bound(ro, ci, va, x, y0, alpha, beta, y)
         # nnz balance: every block within one row's length of nnz / world
         nnz = int(ro[-1])
         longest = int(np.max(np.diff(ro))) if rows else 0
@@ -101,6 +107,20 @@ def _spmv_worker(rank, world, port, rows, cols, heavy, alpha, beta):
         d.close()
     finally:
         dist.destroy_process_group()
+
+
+def _assert_within_sum_bound(ro, ci, va, x, y0, alpha, beta, y):
+    """|y - exact| <= (row length + 3) * 2^-24 * (|alpha| sum |a x| + |beta y0|) per row."""
+    rows = len(ro) - 1
+    exact = beta * y0.astype(np.float64)
+    mag = np.abs(beta * y0.astype(np.float64))
+    for r in range(rows):
+        s = slice(ro[r], ro[r + 1])
+        p = va[s].astype(np.float64) * x[ci[s]].astype(np.float64)
+        exact[r] += alpha * p.sum()
+        mag[r] += abs(alpha) * np.abs(p).sum()
+    bound = (np.diff(ro) + 3) * 2.0 ** -24 * mag + 1e-30
+    assert np.all(np.abs(y.astype(np.float64) - exact) <= bound)
 
 
 def _rng_worker(rank, world, port, n, seed):
@@ -146,6 +166,37 @@ def test_nnz_balanced_bounds_edges():
                                                         (3, 5, (), 1.0, 1.0)])
 def test_dist_spmv_two_gloo_ranks(rows, cols, heavy, alpha, beta):
     _run(_spmv_worker, rows, cols, heavy, alpha, beta)
+
+
+@pytest.mark.parametrize("rows,cols,heavy", [(1000, 777, ()), (513, 2049, (0, 7)), (3, 5, ())])
+def test_dist_spmv_overlap_two_gloo_ranks(rows, cols, heavy):
+    """The overlapped step (own x block first, the rest after the exchange)."""
+    _run(_spmv_worker, rows, cols, heavy, 0.5, -2.0, True)
+
+
+def test_split_by_columns_keeps_every_entry_in_row_order():
+    import torch
+
+    from muda_b200.dist_spmv import split_by_columns
+    ro, ci, va, _ = _csr(5, 300, 500, (4,))
+    for base in (0, 1):
+        for lo, hi in ((0, 500), (100, 250), (499, 500), (300, 300)):
+            own, rest = split_by_columns(torch, torch.from_numpy(ro + base),
+                                         torch.from_numpy(ci + base), torch.from_numpy(va),
+                                         base, lo, hi)
+            o_ro, o_ci, o_va = (t.numpy() for t in own)
+            r_ro, r_ci, r_va = (t.numpy() for t in rest)
+            assert o_ro[0] == base and r_ro[0] == base
+            for r in range(300):
+                s = slice(ro[r], ro[r + 1])
+                c, v = ci[s], va[s]
+                m = (c >= lo) & (c < hi)
+                so = slice(o_ro[r] - base, o_ro[r + 1] - base)
+                sr = slice(r_ro[r] - base, r_ro[r + 1] - base)
+                assert np.array_equal(o_ci[so] - base + lo, c[m])
+                assert np.array_equal(o_va[so], v[m])
+                assert np.array_equal(r_ci[sr] - base, c[~m])
+                assert np.array_equal(r_va[sr], v[~m])
 
 
 def test_rng_weak_scaling_partition_two_gloo_ranks():

@@ -258,3 +258,43 @@ def test_dist_spmv_single_rank_cuda_path(cuda, built, base):
     want, exact, absr = oracle.spmv_csr(ro.astype(np.int32), ci, va, x, alpha=1.5, with_abs=True)
     err = np.abs(y.cpu().numpy().astype(np.float64) - exact)  # exact includes alpha
     assert np.all(err <= 1e-5 * 1.5 * absr + 1e-30)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("mean,long_frac", [(1, 0.001), (10, 0.005), (30, 0.005)])
+@pytest.mark.parametrize("base", [0, 1])
+def test_gpu_spmv_array_alignment(cuda, built, mean, long_frac, base):
+    """fp32 SpMV whose column and value arrays start on a 16-byte boundary and 4 bytes
+    past one (element offset 0 and 1 into a fresh allocation) on the same matrix: both
+    must meet the oracle's bound.  Rows from empty to 3000 entries (whole-warp rows),
+    nnz not a multiple of 4, mean lengths that select 2, 4 and 8 lanes per row."""
+    torch = cuda
+    rng = np.random.default_rng(100 * mean + base)
+    rows, cols = 4099, 5000
+    lengths = rng.integers(0, 2 * mean + 1, rows)
+    long_rows = rng.random(rows) < long_frac
+    lengths[long_rows] = rng.integers(100, 3000, int(long_rows.sum()))
+    lengths[-1] = 0
+    if lengths.sum() % 4 == 0:
+        lengths[0] += 1
+    offsets, col, vals = random_csr(rng, rows, cols, lengths)
+    x = rng.uniform(-1, 1, cols).astype(np.float32)
+    y0 = rng.uniform(-1, 1, rows).astype(np.float32)
+    L = capi.cusparse()
+    nnz = len(vals)
+    ro = torch.from_numpy((offsets + base).astype(np.int32)).cuda()
+    xx = torch.from_numpy(x).cuda()
+    outs = []
+    for shift in (0, 1):  # element offset into a fresh (256-byte aligned) allocation
+        ci = torch.empty(nnz + 4, dtype=torch.int32, device="cuda")[shift:shift + nnz]
+        va = torch.empty(nnz + 4, dtype=torch.float32, device="cuda")[shift:shift + nnz]
+        ci.copy_(torch.from_numpy((col + base).astype(np.int32)))
+        va.copy_(torch.from_numpy(vals))
+        assert (ci.data_ptr() % 16 == 0) == (shift == 0)
+        yy = torch.from_numpy(y0.copy()).cuda()
+        outs.append(_spmv_dev(torch, L, ro, ci, va, xx, yy, rows, cols, nnz, base, -0.5, 1.25))
+    yo, exact, absr = oracle.spmv_csr(offsets + base, col + base, vals, x, base=base, alpha=-0.5,
+                                      beta=1.25, y=y0.copy(), with_abs=True)
+    scale = 0.5 * absr + 1.25 * np.abs(y0)
+    for got in outs:
+        check(got, exact, scale, yo)

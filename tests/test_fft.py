@@ -222,8 +222,7 @@ def test_gpu_bluestein_global_lengths(cuda, built, n):
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("n,batch", [((1 << 20) + 7, 2), (3 * (1 << 21) + 1, 1),
-                                     ((1 << 25) + 1, 1)])
+@pytest.mark.parametrize("n,batch", [((1 << 20) + 7, 2), (3 * (1 << 21) + 1, 1)])
 def test_gpu_bluestein_long_lengths(cuda, built, n, batch):
     """Lengths above 2^20 (the reference transforms any length): Bluestein through global
     memory with chirp, inner twiddles and bhat built on the device, inner lengths 2^22 ..
@@ -238,10 +237,11 @@ def test_gpu_bluestein_long_lengths(cuda, built, n, batch):
 
 
 @pytest.mark.gpu
-def test_gpu_bluestein_longest_length(cuda, built):
-    """The longest non-power-of-two length served, 2^27 - 1 (inner length 2^28): the
-    forward transform at three frequencies against float64 sums, and the round trip."""
-    n = (1 << 27) - 1
+@pytest.mark.parametrize("n", [(1 << 25) + 1, (1 << 27) - 1])
+def test_gpu_bluestein_longest_length(cuda, built, n):
+    """Long non-power-of-two lengths up to the longest served, 2^27 - 1 (inner length
+    2^28): the forward transform at three frequencies against float64 sums, and the
+    round trip (numpy's own FFT of these lengths takes minutes on the host)."""
     rng = np.random.default_rng(5)
     x = rand_c64(rng, n)
     got = gpu_fft(cuda, x, [n], 1, -1)

@@ -47,11 +47,11 @@ __global__ void angle_probe(unsigned lo, unsigned hi, unsigned* res) {
        b += gridDim.x * blockDim.x) {
     const float th = __uint_as_float(b);
     const double c = cos(static_cast<double>(th)), s = sin(static_cast<double>(th));
-    Pair zc, zs;
-    // radius 1: the products r*cos, r*sin are the bare sin / cos
-    polar2_hw<true, true>(Pair{th, th}, Pair{1.0f, 1.0f}, zc, zs);
-    record(res + 1, zc.x - c);
-    record(res + 2, zs.x - s);
+    Pair p0, p1, zc, zs;
+    // radius 1: the products r*cos, r*sin are the bare cos / sin
+    polar_pairs_hw<true>(Pair{th, th}, Pair{1.0f, 1.0f}, p0, p1);
+    record(res + 1, p0.x - c);
+    record(res + 2, p0.y - s);
     polar2<true, true>(Pair{th, th}, Pair{1.0f, 1.0f}, zc, zs);
     record(res + 3, zc.x - c);
     record(res + 4, zs.x - s);

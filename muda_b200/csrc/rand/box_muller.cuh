@@ -200,16 +200,28 @@ __device__ __forceinline__ void polar2(Pair theta, Pair r, Pair& zc, Pair& zs) {
 // z = r cos(theta) then errs by at most 3.5e-7 max(1, r)|cos| + r * 3.65e-7 (+ the
 // product's rounding), which stays below 2e-6 max(1, |z|) for r <= kRadHw = 3.75;
 // lanes with a larger radius (u < exp(-7.03), one pair in 1100) take this file's
-// polynomials for sin / cos.  Both fallbacks are taken per warp only when one of
-// its lanes needs them.
+// polynomials for sin / cos.  Both fallbacks are branches that a warp enters only when
+// one of its lanes needs them.
 constexpr float kNearOne = 0.995f;
 constexpr float kRadHw = 3.75f;
 
+// Bit 0 of x moved to bit 31 (a funnel shift: an integer-pipe instruction, which keeps
+// the sign fold off the FMA pipes that Philox's multiplies fill).
+__device__ __forceinline__ std::uint32_t low_bit_to_sign(std::uint32_t x) {
+  std::uint32_t r;
+  asm("shf.l.wrap.b32 %0, %1, %1, 31;" : "=r"(r) : "r"(x));
+  return r & 0x80000000u;
+}
+
+// -2 ln u for u in (0, 1] in both lanes: the hardware lg2 times -2 ln 2, replaced by the
+// series in d = u - 1 for u > kNearOne.  u is positive, so its bits order as its values
+// and the test is an integer compare.
 template <bool P>
 __device__ __forceinline__ Pair neg2_log_hw(Pair u) {
   Pair w = mul<P>({lg2_approx(u.x), lg2_approx(u.y)}, splat(-1.38629436111989061883f));
-  const bool nx = u.x > kNearOne, ny = u.y > kNearOne;
-  if (__any_sync(__activemask(), nx || ny)) {
+  const bool nx = __float_as_uint(u.x) > __float_as_uint(kNearOne);
+  const bool ny = __float_as_uint(u.y) > __float_as_uint(kNearOne);
+  if (nx || ny) {
     const Pair d = add<P>(u, splat(-1.0f));
     const Pair q = fma<P>(d, splat(0.5f), splat(-0.6666666865f));
     const Pair sr = mul<P>(d, fma<P>(d, fma<P>(d, q, splat(1.0f)), splat(-2.0f)));
@@ -219,34 +231,57 @@ __device__ __forceinline__ Pair neg2_log_hw(Pair u) {
   return w;
 }
 
-// r*cos(theta) and r*sin(theta) with the hardware sin / cos: theta is reduced by
-// pi (x = theta - k pi, |x| <= pi/2, two-term pi), so cos and sin of theta are those
-// of x with one common sign (-1)^k, folded into the radius.
-template <bool PT, bool PO>
-__device__ __forceinline__ void polar2_hw(Pair theta, Pair r, Pair& zc, Pair& zs) {
+// The two Box-Muller pairs of a block as output pairs: p0 = (r.x cos theta.x,
+// r.x sin theta.x), p1 = (r.y cos theta.y, r.y sin theta.y), theta in [0, 2pi], so that
+// each product is one packed multiply and the four outputs leave in store order.  theta
+// is reduced by pi (x = theta - k pi, |x| <= pi/2, two-term pi): cos and sin of theta are
+// those of x with one common sign (-1)^k, folded into the radius.  Radii above kRadHw
+// take this file's polynomials on the pi/2 reduction instead.
+template <bool P>
+__device__ __forceinline__ void polar_pairs_hw(Pair theta, Pair r, Pair& p0, Pair& p1) {
   constexpr float kRound = 12582912.0f;  // 1.5 * 2^23: adding it rounds to an integer
-  const Pair magic = fma<PT>(theta, splat(0.318309886183790671538f), splat(kRound));  // 1/pi
-  const Pair k = add<PT>(magic, splat(-kRound));
-  Pair x = fma<PT>(k, splat(-3.1415927410125732421875f), theta);  // float(pi)
-  x = fma<PT>(k, splat(8.74227800037248566e-8f), x);              // pi - float(pi), negated
-  const Pair rk = {__uint_as_float(__float_as_uint(r.x) ^ (__float_as_uint(magic.x) << 31)),
-                   __uint_as_float(__float_as_uint(r.y) ^ (__float_as_uint(magic.y) << 31))};
-  zc = mul<PO>(rk, {cos_approx(x.x), cos_approx(x.y)});
-  zs = mul<PO>(rk, {sin_approx(x.x), sin_approx(x.y)});
-  const bool fx = r.x > kRadHw, fy = r.y > kRadHw;
-  if (__any_sync(__activemask(), fx || fy)) {
-    // large radius: this file's polynomials on the pi/2 reduction
+  const Pair magic = fma<P>(theta, splat(0.318309886183790671538f), splat(kRound));  // 1/pi
+  const Pair k = add<P>(magic, splat(-kRound));
+  Pair x = fma<P>(k, splat(-3.1415927410125732421875f), theta);  // float(pi)
+  x = fma<P>(k, splat(8.74227800037248566e-8f), x);              // pi - float(pi), negated
+  const float rx = __uint_as_float(__float_as_uint(r.x) ^ low_bit_to_sign(__float_as_uint(magic.x)));
+  const float ry = __uint_as_float(__float_as_uint(r.y) ^ low_bit_to_sign(__float_as_uint(magic.y)));
+  p0 = mul<P>(splat(rx), {cos_approx(x.x), sin_approx(x.x)});
+  p1 = mul<P>(splat(ry), {cos_approx(x.y), sin_approx(x.y)});
+  // r >= 0, so the threshold test is an integer compare of the bits
+  const bool fx = __float_as_uint(r.x) > __float_as_uint(kRadHw);
+  const bool fy = __float_as_uint(r.y) > __float_as_uint(kRadHw);
+  if (fx || fy) {
     Pair pc, ps;
-    polar2<PT, PO>(theta, r, pc, ps);
-    if (fx) {
-      zc.x = pc.x;
-      zs.x = ps.x;
-    }
-    if (fy) {
-      zc.y = pc.y;
-      zs.y = ps.y;
-    }
+    polar2<P, P>(theta, r, pc, ps);
+    if (fx) p0 = {pc.x, ps.x};
+    if (fy) p1 = {pc.y, ps.y};
   }
+}
+
+// The normal transform of one Philox block (u0..u3 = the four words as uniforms):
+// (r0 cos t0, r0 sin t0, r1 cos t1, r1 sin t1) with r_i = sqrt(-2 ln u_2i), t_i = 2pi u_2i+1,
+// then * stddev (Aff 2) and + mean (Aff >= 1), each rounded as in the reference.  Aff 0
+// serves mean 0 and stddev 1: the product by 1 is exact and adding 0 only turns a zero
+// output's sign from - to +, so both are left out.
+template <int Aff>
+__device__ __forceinline__ uint4 normal_block_hw(uint4 r, float mean, float stddev) {
+  const Pair ue = to_uniform2<true>(r.x, r.z), uo = to_uniform2<true>(r.y, r.w);
+  const Pair w = neg2_log_hw<true>(ue);
+  const Pair rad = {sqrt_approx(w.x), sqrt_approx(w.y)};
+  const Pair theta = mul<true>(splat(6.28318530717958647692f), uo);
+  Pair p0, p1;
+  polar_pairs_hw<true>(theta, rad, p0, p1);
+  if constexpr (Aff == 2) {
+    p0 = mul<true>(p0, splat(stddev));
+    p1 = mul<true>(p1, splat(stddev));
+  }
+  if constexpr (Aff >= 1) {
+    p0 = add<true>(p0, splat(mean));
+    p1 = add<true>(p1, splat(mean));
+  }
+  return make_uint4(__float_as_uint(p0.x), __float_as_uint(p0.y), __float_as_uint(p1.x),
+                    __float_as_uint(p1.y));
 }
 
 }  // namespace

@@ -46,6 +46,6 @@ cudaError_t launch_philox_poisson(unsigned int* out, std::uint64_t n, std::uint6
                                   cudaStream_t stream) noexcept;
 
 // Number of device kernels one launch_philox_fill call issues (0 for n == 0).
-int philox_fill_launch_count(std::uint64_t n) noexcept;
+int philox_fill_launch_count(std::uint64_t n, std::uint64_t first_block) noexcept;
 
 }  // namespace mb200::rand

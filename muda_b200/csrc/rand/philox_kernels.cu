@@ -16,16 +16,21 @@
 // computed once on the host and read from the kernel parameter bank; each
 // thread then owns whole Philox blocks and writes them as one 16-byte store, a
 // warp covering 512 contiguous bytes.  The grid is a whole number of waves over
-// the 148 SMs and strides over the output.
+// the 148 SMs and strides over the output.  A call is cut on the host into segments
+// within which the counter's high word is constant (at most 2^31 blocks each, almost
+// always one launch): inside a segment the block counter is a 32-bit index, the high
+// word a kernel constant that the first round folds, and no carry is propagated.
 //
-// The normal transform is bound by instruction issue and by the heavy FMA pipe, which
-// Philox's twenty 32x32->64 multiplies per block already hold for 80 of the 91
-// cycles a warp-block may take at the HBM write rate.  So its fp32 work is written
-// to leave that pipe: the two Box-Muller pairs of a block are the two lanes of
-// sm_100's packed add/mul/fma.rn.f32x2 (each lane rounded exactly as the scalar
-// instruction), and -2 ln u, sin and cos come from the hardware's approximate
-// lg2 / sin / cos (XU pipe) wherever those are accurate enough, with this file's own
-// bounded-range series elsewhere (see kHw below):
+// The normal transform is bound by the FMA pipes, which Philox's twenty 32x32->64
+// multiplies per block already hold for 80 of the 91 cycles a warp-block may take at
+// the HBM write rate (per-opcode counts: every instruction the transform adds to those
+// pipes costs about two cycles of elapsed time).  So its fp32 work is written to leave
+// them: the two Box-Muller pairs of a block are the two lanes of sm_100's packed
+// add/mul/fma.rn.f32x2 (each lane rounded exactly as the scalar instruction), the
+// outputs are formed as (r cos, r sin) pairs that leave in store order, sign folds and
+// threshold tests are integer instructions, and -2 ln u, sin and cos come from the
+// hardware's approximate lg2 / sin / cos (XU pipe) wherever those are accurate enough,
+// with this file's own bounded-range series elsewhere (box_muller.cuh):
 //   -2 ln u, u in (0, 1]: u = m 2^e with m in [sqrt(1/2), sqrt(2)), ln m =
 //      2 atanh(s) with s = (m-1)/(m+1), |s| <= 0.1716, atanh(s)/s as a quadratic in
 //      s^2 (4.7e-7 relative); near u = 1 a series in d = u - 1;
@@ -63,6 +68,9 @@ struct FillArgs {
   float stddev;
   double mean_d, stddev_d;    // double-precision streams
   float lambda, exp_neg_lambda;  // Poisson
+  // fp32 segment (philox_fill_kernel): blocks i < nblk use the counter (clo + i, chi, 0, 0)
+  // and go to out[4i .. 4i+3]; then `tail` (0..3) words of block nblk
+  std::uint32_t nblk, clo, chi, tail;
 };
 
 // Counter (ctr_lo, ctr_hi, c2_in, 0): word 2 is 0 except for the Poisson
@@ -87,46 +95,53 @@ __device__ __forceinline__ uint4 philox_block(std::uint64_t ctr, const KeySchedu
   return make_uint4(c0, c1, c2, c3);
 }
 
+// The same rounds for the counter (lo, hi, 0, 0) with hi constant over a segment.
+__device__ __forceinline__ uint4 philox_block32(std::uint32_t lo, std::uint32_t hi,
+                                                const KeySchedule& key) {
+  std::uint32_t c0 = lo, c1 = hi, c2 = 0u, c3 = 0u;
+#pragma unroll
+  for (int r = 0; r < 10; ++r) {
+    const std::uint32_t hi0 = __umulhi(0xD2511F53u, c0);
+    const std::uint32_t lo0 = 0xD2511F53u * c0;
+    const std::uint32_t hi1 = __umulhi(0xCD9E8D57u, c2);
+    const std::uint32_t lo1 = 0xCD9E8D57u * c2;
+    c0 = hi1 ^ c1 ^ key.k0[r];
+    c1 = lo1;
+    c2 = hi0 ^ c3 ^ key.k1[r];
+    c3 = lo0;
+  }
+  return make_uint4(c0, c1, c2, c3);
+}
+
 
 // Which stages of the transforms use the packed form (bit set) or scalar pairs.
 constexpr unsigned kPackConv = 1u;   // word -> uniform float
 constexpr unsigned kPackLog = 2u;    // -2 ln u
 constexpr unsigned kPackTrig = 4u;   // reduction and sin/cos polynomials
 constexpr unsigned kPackOut = 8u;    // radius products and the affine step
-// With kHw the normal transform takes -2 ln u and sin / cos from the hardware's
-// approximate lg2 / sin / cos (the XU pipe, off the FMA pipes that Philox's
-// multiplies fill), keeping this file's series for the inputs where those are not
-// accurate enough (see neg2_log_hw and polar2_hw).
-constexpr unsigned kHw = 16u;
 
+// uint32, uniform and log-normal words of one block.  The log-normal keeps this file's
+// bounded-range series for ln / sin / cos (its exp amplifies the normal's error); the
+// normal itself runs normal_block_hw (box_muller.cuh).
 template <Dist D, bool Scale, unsigned Pack>
 __device__ __forceinline__ uint4 transform(uint4 r, float mean, float stddev) {
   constexpr bool PC = (Pack & kPackConv) != 0u, PL = (Pack & kPackLog) != 0u;
   constexpr bool PT = (Pack & kPackTrig) != 0u, PO = (Pack & kPackOut) != 0u;
-  if constexpr (D == Dist::kLogNormal) {
-    const uint4 z = transform<Dist::kNormal, Scale, Pack>(r, mean, stddev);
-    return make_uint4(__float_as_uint(expf(__uint_as_float(z.x))),
-                      __float_as_uint(expf(__uint_as_float(z.y))),
-                      __float_as_uint(expf(__uint_as_float(z.z))),
-                      __float_as_uint(expf(__uint_as_float(z.w))));
-  } else if constexpr (D == Dist::kUint32) {
+  if constexpr (D == Dist::kUint32) {
     return r;
   } else if constexpr (D == Dist::kUniform) {
     const Pair a = to_uniform2<PC>(r.x, r.y), b = to_uniform2<PC>(r.z, r.w);
     return make_uint4(__float_as_uint(a.x), __float_as_uint(a.y), __float_as_uint(b.x),
                       __float_as_uint(b.y));
   } else {
+    static_assert(D == Dist::kLogNormal, "normal blocks go through normal_block_hw");
     // lane x is the pair (u0, u1), lane y the pair (u2, u3)
-    constexpr bool HW = (Pack & kHw) != 0u;
     const Pair ue = to_uniform2<PC>(r.x, r.z), uo = to_uniform2<PC>(r.y, r.w);
-    const Pair w = HW ? neg2_log_hw<PL>(ue) : neg2_log<PL>(ue);
+    const Pair w = neg2_log<PL>(ue);
     const Pair rad = {sqrt_approx(w.x), sqrt_approx(w.y)};
     const Pair theta = mul<PT>(splat(6.28318530717958647692f), uo);
     Pair zc, zs;
-    if constexpr (HW)
-      polar2_hw<PT, PO>(theta, rad, zc, zs);
-    else
-      polar2<PT, PO>(theta, rad, zc, zs);
+    polar2<PT, PO>(theta, rad, zc, zs);
     if constexpr (Scale) {
       zc = mul<PO>(zc, splat(stddev));
       zs = mul<PO>(zs, splat(stddev));
@@ -134,28 +149,36 @@ __device__ __forceinline__ uint4 transform(uint4 r, float mean, float stddev) {
     // (z * stddev) + mean, rounded separately; with stddev == 1 the product is z
     zc = add<PO>(zc, splat(mean));
     zs = add<PO>(zs, splat(mean));
-    return make_uint4(__float_as_uint(zc.x), __float_as_uint(zs.x), __float_as_uint(zc.y),
-                      __float_as_uint(zs.y));
+    return make_uint4(__float_as_uint(expf(zc.x)), __float_as_uint(expf(zs.x)),
+                      __float_as_uint(expf(zc.y)), __float_as_uint(expf(zs.y)));
   }
 }
 
-// Packing chosen by measurement on B200 (2^30 words, 8 CTAs per SM): the normal's
-// 16 mixes ran 1.368 (conversion, log and output packed, trig scalar) to 1.605 ms
-// (output and conversion packed only); all-packed 1.400, all-scalar 1.521.  The
-// uniform conversion: packed 0.745 ms, scalar 0.805 ms.
-// The log-normal (2^28 words, stddev != 1): all four stages packed 0.408 ms, the
-// normal's mix 0.418 ms, all scalar 0.442 ms.
+// Packing chosen by measurement on B200 (2^30 words, 8 CTAs per SM): the uniform
+// conversion packed 0.745 ms, scalar 0.805 ms.  The log-normal (2^28 words, stddev != 1):
+// all four stages packed 0.408 ms, all scalar 0.442 ms.
 constexpr unsigned kUniformPack = kPackConv;
-constexpr unsigned kNormalPack = kHw | kPackConv | kPackLog | kPackTrig | kPackOut;
 constexpr unsigned kLogNormalPack = kPackConv | kPackLog | kPackTrig | kPackOut;
 
-// Writes one Philox block's four words at block index b.
+// Aff: the affine step of the normal and log-normal words (0: none, mean 0 and stddev 1;
+// 1: + mean; 2: * stddev + mean).
+template <Dist D, int Aff>
+__device__ __forceinline__ uint4 block_words(std::uint32_t lo, std::uint32_t hi,
+                                             const FillArgs& a) {
+  const uint4 r = philox_block32(lo, hi, a.key);
+  if constexpr (D == Dist::kNormal)
+    return normal_block_hw<Aff>(r, a.mean, a.stddev);
+  else if constexpr (D == Dist::kLogNormal)
+    return transform<D, Aff == 2, kLogNormalPack>(r, a.mean, a.stddev);
+  else
+    return transform<D, false, kUniformPack>(r, a.mean, a.stddev);
+}
+
 template <bool Vec16>
-__device__ __forceinline__ void store_block(std::uint32_t* out, std::uint64_t b, uint4 v) {
+__device__ __forceinline__ void store_block(std::uint32_t* p, uint4 v) {
   if constexpr (Vec16) {
-    reinterpret_cast<uint4*>(out)[b] = v;
+    *reinterpret_cast<uint4*>(p) = v;
   } else {
-    std::uint32_t* p = out + 4 * b;
     p[0] = v.x;
     p[1] = v.y;
     p[2] = v.z;
@@ -163,63 +186,66 @@ __device__ __forceinline__ void store_block(std::uint32_t* out, std::uint64_t b,
   }
 }
 
-// One thread per Philox block, grid-stride.  Vec16 selects a single 16-byte
-// store per block (output 16-byte aligned); otherwise four 4-byte stores.
-// Scale is false when stddev == 1 (the multiply is then the identity).  The
-// uint32 and uniform streams take two blocks (b and b + stride) per loop step,
-// which measured 3.4 % faster for the uniform (less loop overhead on the pipe the
-// Philox multiplies fill); for the normal it measured slower and is not used.
-template <Dist D, bool Vec16, bool Scale = true,
-          unsigned Pack = (D == Dist::kNormal      ? kNormalPack
-                           : D == Dist::kLogNormal ? kLogNormalPack
-                                                   : kUniformPack)>
+// One segment (FillArgs::nblk blocks of constant counter high word), one thread per
+// Philox block, grid-stride with a 32-bit block index, the output pointer and the
+// counter stepped by the stride.  Vec16 selects a single 16-byte store per block
+// (output 16-byte aligned); otherwise four 4-byte stores.  The uint32 and uniform
+// streams take two blocks (b and b + stride) per loop step.  Measured on 2^30 words
+// against the previous 64-bit-counter loop: uniform 0.776 -> 0.664 ms, normal (with
+// normal_block_hw's pair layout and integer tests) 1.218 -> 1.057 ms.
+template <Dist D, bool Vec16, int Aff>
 __global__ void __launch_bounds__(kThreads) philox_fill_kernel(const FillArgs a) {
   constexpr bool kPairs = D == Dist::kUniform || D == Dist::kUint32;
-  const std::uint64_t full_blocks = a.n >> 2;
-  const std::uint64_t stride = static_cast<std::uint64_t>(gridDim.x) * kThreads;
-  std::uint64_t b = static_cast<std::uint64_t>(blockIdx.x) * kThreads + threadIdx.x;
-  std::uint32_t* out = static_cast<std::uint32_t*>(a.out);
+  const std::uint32_t stride = gridDim.x * kThreads;
+  std::uint32_t b = blockIdx.x * kThreads + threadIdx.x;
+  std::uint32_t* p = static_cast<std::uint32_t*>(a.out) + 4ull * b;
+  std::uint32_t c = a.clo + b;
   if constexpr (kPairs) {
-    for (; b + stride < full_blocks; b += 2 * stride) {
-      const uint4 v0 = transform<D, Scale, Pack>(philox_block(a.first_block + b, a.key), a.mean,
-                                                 a.stddev);
-      const uint4 v1 = transform<D, Scale, Pack>(philox_block(a.first_block + b + stride, a.key),
-                                                 a.mean, a.stddev);
-      store_block<Vec16>(out, b, v0);
-      store_block<Vec16>(out, b + stride, v1);
+    for (; b + stride < a.nblk; b += 2 * stride) {
+      const uint4 v0 = block_words<D, Aff>(c, a.chi, a);
+      const uint4 v1 = block_words<D, Aff>(c + stride, a.chi, a);
+      store_block<Vec16>(p, v0);
+      store_block<Vec16>(p + 4ull * stride, v1);
+      p += 8ull * stride;
+      c += 2 * stride;
     }
   }
-  for (; b < full_blocks; b += stride) {
-    const uint4 v = transform<D, Scale, Pack>(philox_block(a.first_block + b, a.key), a.mean, a.stddev);
-    store_block<Vec16>(out, b, v);
+  for (; b < a.nblk; b += stride) {
+    store_block<Vec16>(p, block_words<D, Aff>(c, a.chi, a));
+    p += 4ull * stride;
+    c += stride;
   }
-  // The partial last block (n % 4 words) belongs to the thread whose next
-  // grid-stride index is exactly full_blocks.
-  const unsigned rem = static_cast<unsigned>(a.n & 3u);
-  if (rem != 0 && b == full_blocks) {
-    const uint4 v = transform<D, Scale, Pack>(philox_block(a.first_block + b, a.key), a.mean, a.stddev);
-    std::uint32_t* p = out + 4 * b;
+  // The partial last block (tail words) belongs to the thread whose next grid-stride
+  // index is exactly nblk; the host keeps its counter inside the segment's high word.
+  if (a.tail != 0 && b == a.nblk) {
+    const uint4 v = block_words<D, Aff>(c, a.chi, a);
     p[0] = v.x;
-    if (rem > 1) p[1] = v.y;
-    if (rem > 2) p[2] = v.z;
+    if (a.tail > 1) p[1] = v.y;
+    if (a.tail > 2) p[2] = v.z;
   }
+}
+
+template <Dist D, int Aff>
+cudaError_t launch_segment(const FillArgs& a, bool vec16, unsigned grid, cudaStream_t stream) {
+  if (vec16)
+    philox_fill_kernel<D, true, Aff><<<grid, kThreads, 0, stream>>>(a);
+  else
+    philox_fill_kernel<D, false, Aff><<<grid, kThreads, 0, stream>>>(a);
+  return cudaGetLastError();
 }
 
 template <Dist D>
 cudaError_t launch_dist(const FillArgs& a, bool vec16, unsigned grid, cudaStream_t stream) {
-  const bool scale = (D == Dist::kNormal || D == Dist::kLogNormal) && a.stddev != 1.0f;
-  if (vec16) {
-    if (scale)
-      philox_fill_kernel<D, true, true><<<grid, kThreads, 0, stream>>>(a);
-    else
-      philox_fill_kernel<D, true, false><<<grid, kThreads, 0, stream>>>(a);
+  if constexpr (D == Dist::kNormal) {
+    if (a.stddev != 1.0f) return launch_segment<D, 2>(a, vec16, grid, stream);
+    if (a.mean != 0.0f) return launch_segment<D, 1>(a, vec16, grid, stream);
+    return launch_segment<D, 0>(a, vec16, grid, stream);
+  } else if constexpr (D == Dist::kLogNormal) {
+    if (a.stddev != 1.0f) return launch_segment<D, 2>(a, vec16, grid, stream);
+    return launch_segment<D, 1>(a, vec16, grid, stream);
   } else {
-    if (scale)
-      philox_fill_kernel<D, false, true><<<grid, kThreads, 0, stream>>>(a);
-    else
-      philox_fill_kernel<D, false, false><<<grid, kThreads, 0, stream>>>(a);
+    return launch_segment<D, 0>(a, vec16, grid, stream);
   }
-  return cudaGetLastError();
 }
 
 // ------------------------------------------------------ double precision --
@@ -355,48 +381,87 @@ cudaError_t launch_f64(const FillArgs& a, cudaStream_t stream) {
   return cudaGetLastError();
 }
 
+
+// The fp32 fill's segments: runs of at most 2^31 blocks whose counters share their high
+// word, the partial last block (n % 4 words) inside the last run, or alone when the last
+// run ends exactly where the high word changes.  Calls fn(first block, blocks, tail,
+// word offset) for each.
+template <class Fn>
+cudaError_t for_each_segment(std::uint64_t n, std::uint64_t first_block, Fn&& fn) {
+  constexpr std::uint64_t kMaxSeg = 1ull << 31;
+  std::uint64_t blk = first_block, left = n >> 2, word = 0;
+  const auto tail = static_cast<std::uint32_t>(n & 3u);
+  for (;;) {
+    const std::uint64_t room = (1ull << 32) - (blk & 0xFFFFFFFFull);
+    const std::uint64_t seg = left < room ? (left < kMaxSeg ? left : kMaxSeg)
+                                          : (room < kMaxSeg ? room : kMaxSeg);
+    const bool last = seg == left;
+    const bool tail_here = last && tail != 0 && seg < room;
+    if (seg > 0 || tail_here) {
+      const cudaError_t e = fn(blk, seg, tail_here ? tail : 0u, word);
+      if (e != cudaSuccess) return e;
+    }
+    blk += seg;
+    left -= seg;
+    word += 4 * seg;
+    if (last) {
+      if (tail != 0 && !tail_here) return fn(blk, 0, tail, word);
+      return cudaSuccess;
+    }
+  }
+}
+
 }  // namespace
 
-int philox_fill_launch_count(std::uint64_t n) noexcept { return n == 0 ? 0 : 1; }
+int philox_fill_launch_count(std::uint64_t n, std::uint64_t first_block) noexcept {
+  int count = 0;
+  if (n == 0) return 0;
+  for_each_segment(n, first_block, [&](std::uint64_t, std::uint64_t, std::uint32_t,
+                                       std::uint64_t) {
+    ++count;
+    return cudaSuccess;
+  });
+  return count;
+}
 
 cudaError_t launch_philox_fill(Dist dist, void* out, std::uint64_t n, std::uint64_t seed,
                                std::uint64_t first_block, float mean, float stddev,
                                cudaStream_t stream) noexcept {
   if (n == 0) return cudaSuccess;
   FillArgs a{};
-  a.out = out;
   a.n = n;
   a.first_block = first_block;
   a.mean = mean;
   a.stddev = stddev;
-  std::uint32_t k0 = static_cast<std::uint32_t>(seed);
-  std::uint32_t k1 = static_cast<std::uint32_t>(seed >> 32);
-  for (int r = 0; r < 10; ++r) {
-    a.key.k0[r] = k0;
-    a.key.k1[r] = k1;
-    k0 += 0x9E3779B9u;
-    k1 += 0xBB67AE85u;
-  }
+  a.key = key_schedule(seed);
   const int dev = current_device();
   const int sms = sm_count(dev);
   if (sms <= 0) return cudaErrorInvalidDevice;
-  const std::uint64_t blocks = (n + 3) / 4;
-  const std::uint64_t want = (blocks + kThreads - 1) / kThreads;
   const std::uint64_t cap = static_cast<std::uint64_t>(sms) * kCtasPerSm;
-  const unsigned grid = static_cast<unsigned>(want < cap ? want : cap);
   const bool vec16 = aligned_to(out, 16);
-  switch (dist) {
-    case Dist::kUint32:
-      return launch_dist<Dist::kUint32>(a, vec16, grid, stream);
-    case Dist::kUniform:
-      return launch_dist<Dist::kUniform>(a, vec16, grid, stream);
-    case Dist::kNormal:
-      return launch_dist<Dist::kNormal>(a, vec16, grid, stream);
-    case Dist::kLogNormal:
-      return launch_dist<Dist::kLogNormal>(a, vec16, grid, stream);
-    default:
-      return cudaErrorInvalidValue;
-  }
+  return for_each_segment(n, first_block, [&](std::uint64_t blk, std::uint64_t seg,
+                                              std::uint32_t tail, std::uint64_t word) {
+    FillArgs s = a;
+    s.out = static_cast<std::uint32_t*>(out) + word;
+    s.nblk = static_cast<std::uint32_t>(seg);
+    s.clo = static_cast<std::uint32_t>(blk);
+    s.chi = static_cast<std::uint32_t>(blk >> 32);
+    s.tail = tail;
+    const std::uint64_t want = (seg + (tail != 0 ? 1 : 0) + kThreads - 1) / kThreads;
+    const unsigned grid = static_cast<unsigned>(want < 1 ? 1 : (want < cap ? want : cap));
+    switch (dist) {
+      case Dist::kUint32:
+        return launch_dist<Dist::kUint32>(s, vec16, grid, stream);
+      case Dist::kUniform:
+        return launch_dist<Dist::kUniform>(s, vec16, grid, stream);
+      case Dist::kNormal:
+        return launch_dist<Dist::kNormal>(s, vec16, grid, stream);
+      case Dist::kLogNormal:
+        return launch_dist<Dist::kLogNormal>(s, vec16, grid, stream);
+      default:
+        return cudaErrorInvalidValue;
+    }
+  });
 }
 
 cudaError_t launch_philox_fill_f64(Dist dist, double* out, std::uint64_t n, std::uint64_t seed,

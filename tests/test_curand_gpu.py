@@ -30,8 +30,13 @@ def _gen(torch, fn, g, n, dtype, offset_elems=0, *extra):
     return buf[offset_elems:offset_elems + n].cpu().numpy()
 
 
+# The last three cases put the counter's high word change (block 2^32) inside the call,
+# right after its last full block (the partial block then runs as its own segment), and
+# in a call of fewer than four words just below it.
 CASES = [(1234, 0, 1 << 16), (1234, 4096, 1000), (42, 0, 4097), (777, 1024, 1023),
-         (9999, 6, 19), (0xDEADBEEFCAFEF00D, (1 << 34) - 64, 100003), (5, 0, 1), (5, 0, 3)]
+         (9999, 6, 19), (0xDEADBEEFCAFEF00D, (1 << 34) - 64, 100003), (5, 0, 1), (5, 0, 3),
+         (0xDEADBEEFCAFEF00D, (1 << 34) - 64, 67), (7, (1 << 34) - 4, 2),
+         (11, (1 << 35) - 4 * 300000, 1 << 21)]
 
 
 @pytest.mark.parametrize("seed,offset,n", CASES)
@@ -53,7 +58,7 @@ def test_uint_and_uniform_bit_exact(cuda, built, seed, offset, n, misalign):
 def test_normal_within_tolerance(cuda, built, seed, offset, n):
     torch = cuda
     L = capi.curand()
-    for mean, std in ((0.0, 1.0), (10.0, 3.0)):
+    for mean, std in ((0.0, 1.0), (3.0, 1.0), (10.0, 3.0)):
         with curand_generator(seed, torch, offset=offset) as g:
             got = _gen(torch, L.curandGenerateNormal, g, n, torch.float32, 0,
                        C.c_float(mean), C.c_float(std))

@@ -482,7 +482,7 @@ def suite_spmv(s: Suite) -> dict:
            "config": f"{rows} rows, nnz {nnz} ({nnz / rows:.2f}/row), power law k^-2 on "
                      "[2.2, 4096], L2 flushed before each call",
            "reference_formula_gbs": (nnz * 8 + 2 * rows * 4) / (ms * 1e-3) / 1e9,
-           "roofline": s.roof("spmv_csr_tiles<4>", gbs, "hbm"), "launches": launches,
+           "roofline": s.roof("spmv_csr_ranges", gbs, "hbm"), "launches": launches,
            "algorithmic_bytes_per_launch": alg_bytes,
            "gather_ceiling": {**ceiling, "spmv_gathers_per_s": nnz / (ms * 1e-3),
                               "spmv_frac_of_ceiling": ceiling["ms"] / ms}}
@@ -1509,7 +1509,7 @@ def spmv_dist_measure(args, torch, dist, world: int, rank: int, local: int) -> d
                  for nm in names},
         "y_check": ok, "nnz_per_rank": [int(v) for v in nz],
         "imbalance": float(nz.max() / max(float(nz.mean()), 1.0)),
-        "roofline": {"bound": "hbm", "kernel": "spmv_csr_tiles (per rank) + x exchange",
+        "roofline": {"bound": "hbm", "kernel": "spmv_csr_ranges (per rank) + x exchange",
                      "frac": alg_bytes / (full * 1e-3) / 1e9 / world / _peaks()["hbm_gbs"],
                      "peak": _peaks()["hbm_gbs"], "unit": "GB/s",
                      "note": "whole-job GB/s / N / per-GPU measured HBM"}}

@@ -337,7 +337,18 @@ cusparseStatus_t cusparseSpMV(cusparseHandle_t handle, cusparseOperation_t opA, 
   const cudaStream_t stream = stream_of(*o.ctx);
   cudaError_t e = cudaSuccess;
   if (!trans) {
-    e = mb200::sparse::launch_spmv_csr(a, vt, o.x->values, o.y->values, al, be, stream);
+    // the entry-range kernel's per-range partial sums live in the handle's scratch
+    const std::size_t need = mb200::sparse::spmv_csr_scratch_bytes(a);
+    if (need == 0) {
+      e = mb200::sparse::launch_spmv_csr(a, vt, o.x->values, o.y->values, al, be, nullptr,
+                                         stream);
+    } else {
+      e = with_scratch(*o.ctx, stream, need, [&](void* ws) {
+        return mb200::sparse::launch_spmv_csr(a, vt, o.x->values, o.y->values, al, be, ws,
+                                              stream);
+      });
+      if (e == cudaErrorMemoryAllocation) return CUSPARSE_STATUS_ALLOC_FAILED;
+    }
   } else if (vt == mb200::sparse::Value::kF32) {
     e = mb200::sparse::launch_spmv_csr_t(a, vt, o.x->values, o.y->values, al, be, nullptr,
                                          stream);

@@ -25,9 +25,12 @@ struct CsrView {
 // y = alpha * A * x + beta * y (beta == 0: y is not read), A in CSR.
 // Malformed input cannot make the kernel read outside the arrays: row offsets
 // are clamped to [0, nnz] and entries whose column is outside [0, cols) are
-// skipped.
+// skipped.  `scratch` must hold spmv_csr_scratch_bytes(a) bytes of device memory
+// (16-byte aligned; may be null when that is 0) that no other launch uses until this
+// one's kernels have run.
+std::size_t spmv_csr_scratch_bytes(const CsrView& a) noexcept;
 cudaError_t launch_spmv_csr(const CsrView& a, Value t, const void* x, void* y, float alpha,
-                            float beta, cudaStream_t stream) noexcept;
+                            float beta, void* scratch, cudaStream_t stream) noexcept;
 
 // y = alpha * A^T * x + beta * y (y has a.cols entries).  fp32: y is first scaled by
 // beta (beta == 0: set to 0), then every stored entry adds alpha*x[r]*value to

@@ -15,6 +15,17 @@
 // (the gathered operand, 16.8 MB at the 4M-row configuration) stays resident in
 // the 126 MB L2; x is gathered with L2-only loads (no L1 allocation for sectors
 // that are almost never reused: measured 3-6 % faster than read-only-cache loads).
+//
+// Matrices with at least four entries per row on average take the entry-range kernel
+// (spmv_csr_ranges) instead: every warp owns an equal range of stored entries (2048), whatever
+// the rows, so power-law rows neither idle lanes nor leave a warp with a 4096-entry row
+// while others finish.  A warp walks its range 128 entries at a time (four per lane, one
+// 16-byte load per stream), marks the rows that start inside each chunk in a shared head
+// bitmap, sums each lane's four products segment by segment, and joins the lanes'
+// segments with a segmented scan (shuffles): rows that end inside the range are written
+// there, the row still open at the range's end is finished by a second small kernel from
+// the ranges' partial sums (handle-owned scratch), in range order.  The summation order is
+// fixed by the matrix alone, so results are deterministic.
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
@@ -120,6 +131,264 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32) spmv_csr_tiles(const CsrVie
   }
 }
 
+// ------------------------------------------------------------ entry ranges --
+constexpr int kRangeLane = 4;                  // entries per lane per chunk
+constexpr int kRangeChunk = 32 * kRangeLane;   // entries per warp step
+constexpr long long kRangeEntries = 2048;      // entries per warp (16 chunks)
+
+// Looks up y[row] and writes alpha * sum + beta * y[row] (beta == 0: y is not read).
+template <class T>
+__device__ __forceinline__ void store_row(T* y, long long row, float sum, float alpha,
+                                          float beta) {
+  const float prev = (beta == 0.0f) ? 0.0f : beta * widen(y[row]);
+  y[row] = narrow<T>(fmaf(alpha, sum, prev));
+}
+
+// First row r in [0, rows] whose (clamped) start is >= e, by a 32-way search of the
+// whole warp: each round samples 32 evenly spaced rows and keeps the span between the
+// last sample below e and the first at or above it.
+__device__ __forceinline__ long long first_row_at(const CsrView& a, long long e) {
+  const int lane = threadIdx.x & 31;
+  long long lo = 0, hi = a.rows;  // the answer lies in [lo, hi]; start(rows) = nnz >= e
+  while (hi > lo) {
+    const long long step = (hi - lo + 31) / 32;
+    const long long r = lo + step * lane;
+    const bool ge = r >= hi || clamp_off(a.row_offsets[r], a.base, a.nnz) >= e;
+    const unsigned m = __ballot_sync(kFull, ge);
+    const int first = m != 0u ? __ffs(m) - 1 : 32;
+    if (first == 0) break;  // start(lo) >= e
+    const long long nhi = lo + step * first;
+    lo = lo + step * (first - 1) + 1;
+    hi = nhi < hi ? nhi : hi;
+    if (step == 1) lo = hi;
+  }
+  return lo;
+}
+
+// Per-range record for the second pass.
+struct RangeTail {
+  float lead;    // sum of the range's entries before its first row start (or all of them)
+  float tail;    // partial sum of the row still open at the range's end
+  int tail_row;  // that row, -1 when no row starts inside the range
+  int has_head;  // 1 when a row starts inside the range
+};
+
+// Vec: column indices and values read as one 16-byte (fp16 values: 8-byte) vector per
+// lane (both arrays aligned to that).  Warp w owns entries [w * kRangeEntries, ...) and the
+// rows that start there (a row that starts at nnz, empty, belongs to the last range).
+template <class T, bool Vec>
+__global__ void __launch_bounds__(kWarpsPerCta * 32, 5) spmv_csr_ranges(const CsrView a,
+                                                                    const T* __restrict__ x,
+                                                                    T* __restrict__ y,
+                                                                    float alpha, float beta,
+                                                                    RangeTail* tails) {
+  __shared__ unsigned heads[kWarpsPerCta][kRangeChunk / 32];
+  __shared__ int rowid[kWarpsPerCta][kRangeChunk];
+  const int lane = threadIdx.x & 31, wi = threadIdx.x >> 5;
+  const long long w = static_cast<long long>(blockIdx.x) * kWarpsPerCta + wi;
+  const long long E0 = w * kRangeEntries;
+  if (E0 >= a.nnz) return;
+  const long long E1 = E0 + kRangeEntries < a.nnz ? E0 + kRangeEntries : a.nnz;
+  const T* vals = static_cast<const T*>(a.values);
+
+  // this lane's next four entries (vector path), loaded one chunk ahead
+  int ci[kRangeLane];
+  float va[kRangeLane];
+  auto load_vec = [&](long long e) {
+    if (e + kRangeLane <= E1) {
+      const int4 c = __ldcs(reinterpret_cast<const int4*>(a.col_ind + e));
+      ci[0] = c.x; ci[1] = c.y; ci[2] = c.z; ci[3] = c.w;
+      if constexpr (sizeof(T) == 4) {
+        const float4 v = __ldcs(reinterpret_cast<const float4*>(vals + e));
+        va[0] = v.x; va[1] = v.y; va[2] = v.z; va[3] = v.w;
+      } else {
+        const uint2 v = __ldcs(reinterpret_cast<const uint2*>(vals + e));
+        const __half2 h0 = *reinterpret_cast<const __half2*>(&v.x);
+        const __half2 h1 = *reinterpret_cast<const __half2*>(&v.y);
+        va[0] = __low2float(h0); va[1] = __high2float(h0);
+        va[2] = __low2float(h1); va[3] = __high2float(h1);
+      }
+    }
+  };
+  if constexpr (Vec) load_vec(E0 + lane * kRangeLane);
+
+  // rows window: lane l holds the start b and the next start bn of row wbase + l
+  long long rnext = first_row_at(a, E0);
+  long long wbase = rnext, wb = 0, wbn = 0;
+  auto load_window = [&]() {
+    const long long r = wbase + lane;
+    wb = wbn = a.nnz + 1;  // past every chunk: never "in"
+    if (r < a.rows) {
+      wb = clamp_off(a.row_offsets[r], a.base, a.nnz);
+      wbn = clamp_off(a.row_offsets[r + 1], a.base, a.nnz);
+      if (wbn < wb) wbn = wb;
+    }
+  };
+  load_window();
+
+  float carry = 0.0f;  // partial sum of the row open at the current chunk's start
+  int carry_row = -1;  // -1: that row started before E0 (rows < 2^31 on this path)
+  float lead = 0.0f;
+  bool any_head = false;
+  for (long long c0 = E0; c0 < E1; c0 += kRangeChunk) {
+    const long long e = c0 + lane * kRangeLane;
+    float p[kRangeLane];
+    if (Vec && e + kRangeLane <= E1) {
+#pragma unroll
+      for (int j = 0; j < kRangeLane; ++j) {
+        const int c = ci[j] - a.base;
+        p[j] = (static_cast<unsigned>(c) < static_cast<unsigned long long>(a.cols))
+                   ? va[j] * widen(__ldcg(x + c))
+                   : 0.0f;
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < kRangeLane; ++j) {
+        p[j] = 0.0f;
+        if (e + j < E1) {
+          const int c = __ldcs(a.col_ind + e + j) - a.base;
+          const float v = widen(__ldcs(vals + e + j));
+          if (static_cast<unsigned>(c) < static_cast<unsigned long long>(a.cols))
+            p[j] = v * widen(__ldcg(x + c));
+        }
+      }
+    }
+    if constexpr (Vec) load_vec(e + kRangeChunk);  // in flight during the reduction
+
+    // rows that start inside [c0, cend): head bits and row ids; empty rows written now
+    const long long cend = c0 + kRangeChunk < E1 ? c0 + kRangeChunk : E1;
+    if (lane < kRangeChunk / 32) heads[wi][lane] = 0u;
+    __syncwarp();
+    for (;;) {
+      const long long r = wbase + lane;
+      // (starts below c0 appear only in malformed, decreasing offsets: skipped)
+      const bool in = r >= rnext && r < a.rows && wb >= c0 && wb < cend;
+      if (in) {
+        if (wbn == wb) {
+          store_row(y, r, 0.0f, alpha, beta);
+        } else {
+          const int pos = static_cast<int>(wb - c0);
+          atomicOr(&heads[wi][pos >> 5], 1u << (pos & 31));
+          rowid[wi][pos] = static_cast<int>(r);
+        }
+      }
+      rnext += __popc(__ballot_sync(kFull, in));
+      if (rnext < wbase + 32 || rnext >= a.rows) break;
+      wbase = rnext;
+      load_window();
+    }
+    __syncwarp();
+    const unsigned hb = (heads[wi][(lane * kRangeLane) >> 5] >> ((lane * kRangeLane) & 31)) &
+                        ((1u << kRangeLane) - 1u);
+
+    // lane-local segments: lp before the first head, whole rows written, tp after
+    float lp = 0.0f, tp = 0.0f;
+    int trow = -1;
+#pragma unroll
+    for (int j = 0; j < kRangeLane; ++j) {
+      if ((hb >> j) & 1u) {
+        if (trow >= 0)
+          store_row(y, trow, tp, alpha, beta);
+        else
+          lp = tp;
+        trow = rowid[wi][lane * kRangeLane + j];
+        tp = 0.0f;
+      }
+      tp += p[j];
+    }
+    const bool has = hb != 0u;
+    // segmented inclusive scan over the lanes of (partial of the open row, its id):
+    // a lane without a head extends the segment of the lane to its left
+    float v = tp;
+    int vr = trow;
+    if (lane == 0 && !has) {
+      v = carry + tp;
+      vr = carry_row;
+    }
+    bool f = has || lane == 0;
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) {
+      const float vu = __shfl_up_sync(kFull, v, d);
+      const int ru = __shfl_up_sync(kFull, vr, d);
+      const bool fu = __shfl_up_sync(kFull, f, d);
+      if (lane >= d && !f) {
+        v = vu + v;
+        vr = ru;
+        f = fu;
+      }
+    }
+    float cin = __shfl_up_sync(kFull, v, 1);
+    int cinr = __shfl_up_sync(kFull, vr, 1);
+    if (lane == 0) {
+      cin = carry;
+      cinr = carry_row;
+    }
+    // the open row ends at this lane's first head
+    const float s = cin + lp;
+    if (has && cinr >= 0) store_row(y, cinr, s, alpha, beta);
+    const unsigned lm = __ballot_sync(kFull, has && cinr < 0);  // only at the first head
+    if (lm != 0u) lead = __shfl_sync(kFull, s, __ffs(lm) - 1);
+    carry = __shfl_sync(kFull, v, 31);
+    carry_row = __shfl_sync(kFull, vr, 31);
+    any_head = any_head || __ballot_sync(kFull, has) != 0u;
+  }
+  // the last range also writes the empty rows that start at nnz
+  if (E1 == a.nnz)
+    for (long long r = rnext + lane; r < a.rows; r += 32) store_row(y, r, 0.0f, alpha, beta);
+  if (lane == 0) {
+    RangeTail t;
+    t.lead = any_head ? lead : carry;
+    t.tail = carry;
+    t.tail_row = any_head ? carry_row : -1;
+    t.has_head = any_head ? 1 : 0;
+    tails[w] = t;
+  }
+}
+
+// The row open at a range's end: the owner's tail plus the lead sums of the following
+// ranges, in range order, up to the first range in which a row starts.
+template <class T>
+__global__ void spmv_ranges_finish(const RangeTail* __restrict__ tails, long long nranges,
+                                   T* __restrict__ y, float alpha, float beta) {
+  const long long w = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (w >= nranges) return;
+  const RangeTail t = tails[w];
+  if (t.tail_row < 0) return;
+  float s = t.tail;
+  for (long long u = w + 1; u < nranges; ++u) {
+    const RangeTail n = tails[u];
+    s += n.lead;
+    if (n.has_head) break;
+  }
+  store_row(y, t.tail_row, s, alpha, beta);
+}
+
+long long range_count(const CsrView& a) {
+  return (a.nnz + kRangeEntries - 1) / kRangeEntries;
+}
+
+// The entry-range kernel serves matrices with at least four entries per row on average
+// (fewer: the rows, not the entries, dominate, and the row tiles balance them).
+bool use_ranges(const CsrView& a) { return a.nnz > 0 && a.nnz >= 4 * a.rows && a.rows < (1ll << 31); }
+
+template <class T>
+cudaError_t launch_ranges(const CsrView& a, const void* x, void* y, float alpha, float beta,
+                          void* scratch, cudaStream_t stream) {
+  const long long nr = range_count(a);
+  const unsigned grid = static_cast<unsigned>((nr + kWarpsPerCta - 1) / kWarpsPerCta);
+  auto* tails = static_cast<RangeTail*>(scratch);
+  const bool vec = aligned_to(a.col_ind, 16) && aligned_to(a.values, 4 * sizeof(T));
+  if (vec)
+    spmv_csr_ranges<T, true><<<grid, kWarpsPerCta * 32, 0, stream>>>(
+        a, static_cast<const T*>(x), static_cast<T*>(y), alpha, beta, tails);
+  else
+    spmv_csr_ranges<T, false><<<grid, kWarpsPerCta * 32, 0, stream>>>(
+        a, static_cast<const T*>(x), static_cast<T*>(y), alpha, beta, tails);
+  spmv_ranges_finish<T><<<static_cast<unsigned>((nr + 255) / 256), 256, 0, stream>>>(
+      tails, nr, static_cast<T*>(y), alpha, beta);
+  return cudaGetLastError();
+}
+
 unsigned tile_grid(std::int64_t rows) {
   const std::int64_t tiles = (rows + 31) / 32;
   const std::int64_t want = (tiles + kWarpsPerCta - 1) / kWarpsPerCta;
@@ -167,9 +436,18 @@ int spmv_group_width(std::int64_t rows, std::int64_t nnz) noexcept {
   return 32;
 }
 
+std::size_t spmv_csr_scratch_bytes(const CsrView& a) noexcept {
+  return use_ranges(a) ? static_cast<std::size_t>(range_count(a)) * sizeof(RangeTail) : 0;
+}
+
 cudaError_t launch_spmv_csr(const CsrView& a, Value t, const void* x, void* y, float alpha,
-                            float beta, cudaStream_t stream) noexcept {
+                            float beta, void* scratch, cudaStream_t stream) noexcept {
   if (a.rows <= 0) return cudaSuccess;
+  if (use_ranges(a)) {
+    if (scratch == nullptr) return cudaErrorInvalidValue;
+    return t == Value::kF16 ? launch_ranges<__half>(a, x, y, alpha, beta, scratch, stream)
+                            : launch_ranges<float>(a, x, y, alpha, beta, scratch, stream);
+  }
   return t == Value::kF16 ? launch_typed<__half>(a, x, y, alpha, beta, stream)
                           : launch_typed<float>(a, x, y, alpha, beta, stream);
 }

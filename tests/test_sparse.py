@@ -298,3 +298,59 @@ def test_gpu_spmv_array_alignment(cuda, built, mean, long_frac, base):
     scale = 0.5 * absr + 1.25 * np.abs(y0)
     for got in outs:
         check(got, exact, scale, yo)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("base", [0, 1])
+def test_gpu_entry_ranges_rows_across_ranges(cuda, built, base):
+    """The entry-range kernel (2048 stored entries per warp): rows of 12000, 8192 and 4096
+    entries that span several ranges (ranges in which no row starts pass their whole sum
+    on), empty rows at the start, between long rows and after the last entry, a row that
+    starts exactly on a range boundary; two calls must agree bit for bit (the summation
+    order depends on the matrix only)."""
+    torch = cuda
+    rng = np.random.default_rng(7 + base)
+    cols = 20000
+    lengths = [0, 0, 5, 12000, 0, 3, 9000, 4096, 1, 0, 2] + list(rng.integers(0, 60, 300)) + \
+        [8192, 0, 0]
+    lengths = np.asarray(lengths, np.int64)
+    # make one row start exactly on a range boundary (a multiple of 4096 entries)
+    offs = np.concatenate([[0], np.cumsum(lengths)])
+    k = int(np.searchsorted(offs, 3 * 4096))
+    lengths[k - 1] = 3 * 4096 - offs[k - 1]
+    offsets, col, vals = random_csr(rng, len(lengths), cols, lengths)
+    assert (offsets == 3 * 4096).any()
+    x = rng.uniform(-1, 1, cols).astype(np.float32)
+    y0 = rng.uniform(-1, 1, len(lengths)).astype(np.float32)
+    for alpha, beta in ((1.0, 0.0), (0.75, -2.0)):
+        got = gpu_spmv(cuda, offsets + base, col + base, vals, x, base=base, alpha=alpha,
+                       beta=beta, y0=y0)
+        again = gpu_spmv(cuda, offsets + base, col + base, vals, x, base=base, alpha=alpha,
+                         beta=beta, y0=y0)
+        assert np.array_equal(got.view(np.uint32), again.view(np.uint32))
+        yo, exact, absr = oracle.spmv_csr(offsets + base, col + base, vals, x, base=base,
+                                          alpha=alpha, beta=beta, y=y0.copy(), with_abs=True)
+        scale = abs(alpha) * absr + (abs(beta) * np.abs(y0) if beta else 0)
+        check(got, exact, scale, yo)
+
+
+@pytest.mark.gpu
+def test_gpu_spmv_decreasing_offsets_stay_in_bounds(cuda, built):
+    """Malformed CSR (row offsets that decrease, or point past nnz) must not make either
+    SpMV kernel read or write outside its arrays: the call returns success (the values
+    of the malformed rows are unspecified), and a well-formed call right after it on the
+    same device gives the oracle's result."""
+    torch = cuda
+    rng = np.random.default_rng(3)
+    cols = 500
+    for lengths in ([8] * 200, [1] * 200):  # entry-range kernel, row-tile kernel
+        offsets, col, vals = random_csr(rng, len(lengths), cols, lengths)
+        bad = offsets.copy()
+        bad[50] = bad[40]             # decreasing
+        bad[120] = offsets[-1] + 999  # past nnz (clamped)
+        x = rng.uniform(-1, 1, cols).astype(np.float32)
+        got = gpu_spmv(cuda, bad, col, vals, x)
+        assert np.all(np.isfinite(got))
+        got = gpu_spmv(cuda, offsets, col, vals, x)
+        yo, exact, absr = oracle.spmv_csr(offsets, col, vals, x, with_abs=True)
+        check(got, exact, absr, yo)

@@ -382,15 +382,99 @@ __global__ void __launch_bounds__(Plan<LOG2N>::THREADS, 3)
   }
 }
 
+// Three staging buffers, two CTAs per SM: group i computes in buffer i % 3 while group
+// i + 1's load has landed or is landing in the next buffer, and the load of group i + 2 goes
+// into the buffer whose store (group i - 1) was issued one group earlier, so no thread waits
+// for a store to drain before the next group can start.
+template <int LOG2N, int S>
+__global__ void __launch_bounds__(Plan<LOG2N>::THREADS, 2)
+    stockham_bulk3_kernel(const float2* in, float2* out, long long groups,
+                          const float2* __restrict__ tw, unsigned int* timeouts) {
+  using PL = Plan<LOG2N>;
+  using BP = BulkPlan<LOG2N>;
+  extern __shared__ __align__(16) std::uint8_t bsmem[];
+  std::uint64_t* full = reinterpret_cast<std::uint64_t*>(bsmem + 3 * BP::STAGE_BYTES);
+  volatile int* ok_flag = reinterpret_cast<volatile int*>(full + 3);
+  auto stage = [&](int b) { return reinterpret_cast<float2*>(bsmem + b * BP::STAGE_BYTES); };
+  const int tloc = threadIdx.x / PL::T;
+  const int j = threadIdx.x % PL::T;
+  const long long stride = gridDim.x;
+  std::uint32_t phase[3] = {0u, 0u, 0u};
+  bool pending[3] = {false, false, false};
+
+  if (threadIdx.x == 0) {
+    for (int b = 0; b < 3; ++b) tc::mbar_init(&full[b], 1);
+    tc::mbar_fence_init();
+    for (int b = 0; b < 2; ++b) {
+      const long long g = blockIdx.x + b * stride;
+      if (g < groups) {
+        tc::mbar_arrive_expect_tx(&full[b], BP::GROUP_BYTES);
+        tc::bulk_load(stage(b), in + g * BP::GROUP, BP::GROUP_BYTES, &full[b]);
+        pending[b] = true;
+      }
+    }
+  }
+  __syncthreads();
+
+  int b = 0;
+  for (long long g = blockIdx.x; g < groups; g += stride, b = (b == 2 ? 0 : b + 1)) {
+    float2* st = stage(b);
+    if (threadIdx.x == 0) {
+      *ok_flag = tc::mbar_wait(&full[b], phase[b]) ? 1 : 0;
+      pending[b] = false;
+    }
+    __syncthreads();
+    if (!*ok_flag) {
+      if (threadIdx.x == 0) atomicAdd(timeouts, 1u);
+      break;
+    }
+    phase[b] ^= 1u;
+    float2 v[PL::P];
+    float* sre = reinterpret_cast<float*>(st) + tloc * PL::REGION * 2;
+    float* sim = sre + PL::REGION;
+    run_spasses<LOG2N, S>(v, j, st + tloc * PL::N, sre, sim, tw);
+    tc::fence_proxy_async_smem();
+    __syncthreads();  // the whole group is in the staging buffer
+    if (threadIdx.x == 0) {
+      tc::bulk_store(out + g * BP::GROUP, st, BP::GROUP_BYTES);
+      tc::bulk_wait_read_but_one();  // the previous group's store has read its buffer
+      const long long gn = g + 2 * stride;
+      const int bn = b == 0 ? 2 : b - 1;  // (b + 2) % 3: the previous group's buffer
+      if (gn < groups) {
+        tc::mbar_arrive_expect_tx(&full[bn], BP::GROUP_BYTES);
+        tc::bulk_load(stage(bn), in + gn * BP::GROUP, BP::GROUP_BYTES, &full[bn]);
+        pending[bn] = true;
+      }
+    }
+  }
+  if (threadIdx.x == 0) {
+    // drain: copies still in flight (only after a timeout) and all stores
+    for (int q = 0; q < 3; ++q)
+      if (pending[q] && !tc::mbar_wait(&full[q], phase[q])) atomicAdd(timeouts, 1u);
+    tc::bulk_wait_all();
+  }
+}
+
 template <int LOG2N, int S>
 cudaError_t launch_bulk_len(const float2* in, float2* out, long long groups, const float2* tw,
                             unsigned int* timeouts, cudaStream_t stream) {
   using BP = BulkPlan<LOG2N>;
+  const int sms = sm_count(current_device());
+  if constexpr (LOG2N >= 11) {
+    constexpr int smem3 = 3 * BP::STAGE_BYTES + 64;
+    auto kern = stockham_bulk3_kernel<LOG2N, S>;
+    const cudaError_t e =
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem3);
+    if (e != cudaSuccess) return e;
+    const long long cap = static_cast<long long>(sms > 0 ? sms : 148) * 2;
+    const unsigned grid = static_cast<unsigned>(groups < cap ? groups : cap);
+    kern<<<grid, Plan<LOG2N>::THREADS, smem3, stream>>>(in, out, groups, tw, timeouts);
+    return cudaGetLastError();
+  }
   auto kern = stockham_bulk_kernel<LOG2N, S>;
   const cudaError_t e =
       cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, BP::SMEM);
   if (e != cudaSuccess) return e;
-  const int sms = sm_count(current_device());
   const long long cap = static_cast<long long>(sms > 0 ? sms : 148) * 3;
   const unsigned grid = static_cast<unsigned>(groups < cap ? groups : cap);
   kern<<<grid, Plan<LOG2N>::THREADS, BP::SMEM, stream>>>(in, out, groups, tw, timeouts);

@@ -830,7 +830,7 @@ def suite_fft(s: Suite) -> dict:
            "gflops_5nlogn": flops / (ms * 1e-3) / 1e9,
            "config": f"N {n} x batch {batch}, forward + inverse in place, "
                      f"data {per_dir / 2e9:.2f} GB > L2",
-           "roofline": s.roof("stockham_kernel<12>", gbs, "hbm"), "launches": launches,
+           "roofline": s.roof("stockham_bulk3_kernel<12>", gbs, "hbm"), "launches": launches,
            "algorithmic_bytes_per_launch": per_dir}
     if s.cpu:
         import oracle

@@ -336,15 +336,12 @@ class Suite:
         self.barrier = None     # called around the timed region under torchrun
 
     def flush(self):
-        """Evicts L2 by READING a buffer twice its size: the lines it leaves are clean, so
-        the timed call's own traffic does not also pay for writing the flush back to
-        DRAM (a write-based flush leaves ~126 MB of dirty lines, whose write-back lands
-        inside the next timed region)."""
+        """Evicts L2 by writing a buffer twice its size (outside the timed region)."""
+        if self._flush is None:
+            self._flush = self.torch.empty(L2_FLUSH_BYTES // 4, dtype=torch_float(self.torch),
+                                           device="cuda")
         with self.torch.cuda.stream(self.stream):
-            if self._flush is None:
-                self._flush = self.torch.ones(L2_FLUSH_BYTES // 4, dtype=torch_float(self.torch),
-                                              device="cuda")
-            self._flush_sink = self._flush.sum()
+            self._flush.fill_(1.0)
 
     def time(self, fn, flush=False, launches_per_call=1):
         torch = self.torch

@@ -16,6 +16,7 @@
 #include <cuda_runtime.h>
 
 #include <cstdint>
+#include <type_traits>
 
 #include "common/device.hpp"
 #include "fft/fft.hpp"
@@ -203,7 +204,10 @@ __device__ __forceinline__ void run_radix(int count, int& p, int total, float2*&
   }
 }
 
-template <int S, bool UNIT>
+// R16: the plan has radix-16 passes.  Lengths without them (no factor 16, e.g. 1000 =
+// 8 * 5^3) take an instantiation without the radix-16 code, whose registers would
+// otherwise spill in every pass.
+template <int S, bool UNIT, bool R16>
 __global__ void __launch_bounds__(512, 2)
     mixed_radix_kernel(const Batch1D bt, MixedPlan pl) {
   extern __shared__ float2 sbuf[];
@@ -225,7 +229,8 @@ __global__ void __launch_bounds__(512, 2)
     float2* src = sbuf + tl * 2 * padded(n);
     float2* dst = src + padded(n);
     int ns = 1, p = 0;
-    run_radix<16, S, UNIT>(pl.n16, p, total, src, dst, n, ns, tid, pl.threads, bt.tw, io);
+    if constexpr (R16)
+      run_radix<16, S, UNIT>(pl.n16, p, total, src, dst, n, ns, tid, pl.threads, bt.tw, io);
     if (pl.r2 == 8) {
       run_radix<8, S, UNIT>(1, p, total, src, dst, n, ns, tid, pl.threads, bt.tw, io);
     } else if (pl.r2 == 4) {
@@ -285,8 +290,12 @@ cudaError_t launch_mixed_radix(std::int64_t n, int sign, const Batch1D& b,
   const int threads = p.threads * p.tpc;
   const std::size_t smem = static_cast<std::size_t>(p.tpc) * 2 * padded(p.n) * sizeof(float2);
   const bool unit = b.in_stride == 1 && b.out_stride == 1;
-  auto kern = sign < 0 ? (unit ? mixed_radix_kernel<-1, true> : mixed_radix_kernel<-1, false>)
-                       : (unit ? mixed_radix_kernel<1, true> : mixed_radix_kernel<1, false>);
+  auto pick = [&](auto r16) {
+    constexpr bool R = decltype(r16)::value;
+    return sign < 0 ? (unit ? mixed_radix_kernel<-1, true, R> : mixed_radix_kernel<-1, false, R>)
+                    : (unit ? mixed_radix_kernel<1, true, R> : mixed_radix_kernel<1, false, R>);
+  };
+  auto kern = p.n16 > 0 ? pick(std::true_type{}) : pick(std::false_type{});
   if (smem > 48 * 1024) {
     const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                static_cast<int>(smem));

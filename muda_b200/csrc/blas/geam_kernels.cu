@@ -110,7 +110,10 @@ __device__ __forceinline__ T operand_at(T (*s)[kCols + 1], const T (&v)[kRowReps
 }
 
 template <typename T, bool TA, bool TB>
-__global__ void __launch_bounds__(kLanes* kRowsPerPass, 4) geam_kernel(GeamArgs<T> g) {
+// Without a transposed operand the 2 x 8 values of A and of B a thread holds in flight
+// need more than 64 registers (4 CTAs per SM spilled them, 3 still did): 2 CTAs per SM there.
+__global__ void __launch_bounds__(kLanes* kRowsPerPass, (TA || TB) ? 4 : 2)
+    geam_kernel(GeamArgs<T> g) {
   __shared__ T sa[TA ? kTile<T> : 1][kCols + 1];
   __shared__ T sb[TB ? kTile<T> : 1][kCols + 1];
   const T alpha = g.alpha_dev ? *g.alpha_dev : g.alpha;

@@ -206,9 +206,10 @@ __device__ __forceinline__ void run_radix(int count, int& p, int total, float2*&
 
 // R16: the plan has radix-16 passes.  Lengths without them (no factor 16, e.g. 1000 =
 // 8 * 5^3) take an instantiation without the radix-16 code, whose registers would
-// otherwise spill in every pass.
+// otherwise spill in every pass; capped at 56 registers, it keeps 9 CTAs of 128 threads
+// on an SM instead of 8.
 template <int S, bool UNIT, bool R16>
-__global__ void __launch_bounds__(512, 2)
+__global__ void __launch_bounds__(512) __maxnreg__(R16 ? 64 : 56)
     mixed_radix_kernel(const Batch1D bt, MixedPlan pl) {
   extern __shared__ float2 sbuf[];
   const int tl = threadIdx.x / pl.threads;  // transform within the CTA

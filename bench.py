@@ -991,7 +991,7 @@ def suite_gemm_bf16(s: Suite) -> dict:
                 C.c_void_p(c.data_ptr()), 14, m, m * n, batch, 68, -1)
     flop = 2.0 * m * n * k * batch
     layouts = {}
-    for name, ta, tb in (("NN", 0, 0), ("TN", 1, 0)):
+    for name, ta, tb in (("NN", 0, 0), ("TN", 1, 0), ("TT", 1, 1), ("NT", 0, 1)):
         a_ = args(ta, tb)
         ms_l, launches_l = s.time(lambda: L.cublasGemmStridedBatchedEx(*a_))
         layouts[name] = {"ms": ms_l, "TFLOP/s": flop / (ms_l * 1e-3) / 1e12,

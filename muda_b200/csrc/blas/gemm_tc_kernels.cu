@@ -46,7 +46,11 @@ constexpr int GROUP_M = 16;
 
 __device__ unsigned int g_gemm_tc_timeouts;
 
-template <typename T, bool AMN, bool BMN>
+// TOUT: the problem computes C^T = op(B)^T op(A)^T (its M is C's n, its N is C's m), so
+// tile row r is column r of C and a thread's 32 accumulator columns are 32 consecutive
+// rows of that column: one 64-byte run of C, written as 16-byte stores.  It turns op
+// T,T (B MN-major, the slower operand form) into the A-MN-major / B-K-major form.
+template <typename T, bool AMN, bool BMN, bool TOUT = false>
 struct GemmProblem {
   static constexpr bool kAMn = AMN, kBMn = BMN;
   CUtensorMap ma;  // A: dims (k, m, batch) K-major, (m, k, batch) MN-major
@@ -60,6 +64,7 @@ struct GemmProblem {
   float alpha, beta;
   const float* alpha_dev;
   const float* beta_dev;
+  int vec_out;  // TOUT: C, ldc and stride_c keep 16-byte alignment of every 8-element run
 
   __device__ void prefetch() const {
     tc::prefetch_tensormap(&ma);
@@ -108,6 +113,30 @@ struct GemmProblem {
   // Row `row` of the tile is output row m; columns col0..col0+31 are output columns.
   __device__ void store(const int (&c3)[3], int row, int col0, const float (&v)[32], float a,
                         float b) const {
+    if constexpr (TOUT) {
+      const int nn = c3[1] * tc::kBM + row;  // column of C
+      if (nn >= m) return;
+      const int m0 = c3[2] * BN + col0;      // first of 32 consecutive rows of C
+      T* cp = c + static_cast<long long>(c3[0]) * stride_c + static_cast<long long>(nn) * ldc + m0;
+      if (vec_out && b == 0.0f && m0 + 32 <= n) {
+#pragma unroll
+        for (int g = 0; g < 4; ++g) {
+          T h[8];
+#pragma unroll
+          for (int j = 0; j < 8; ++j) h[j] = from_float(a * v[g * 8 + j]);
+          *reinterpret_cast<uint4*>(cp + g * 8) = *reinterpret_cast<const uint4*>(h);
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          if (m0 + j < n) {
+            const float prev = (b == 0.0f) ? 0.0f : b * to_float(cp[j]);
+            cp[j] = from_float(fmaf(a, v[j], prev));
+          }
+        }
+      }
+      return;
+    }
     const int mm = c3[1] * tc::kBM + row;
     if (mm >= m) return;
     T* cz = c + static_cast<long long>(c3[0]) * stride_c + mm;
@@ -184,9 +213,9 @@ unsigned int* timeout_counter() {
   return addr[dev];
 }
 
-template <typename T, int FMT, bool AMN, bool BMN>
+template <typename T, int FMT, bool AMN, bool BMN, bool TOUT = false>
 cudaError_t run(const GemmArgs& g, cudaStream_t stream) {
-  GemmProblem<T, AMN, BMN> p{};
+  GemmProblem<T, AMN, BMN, TOUT> p{};
   if (!make_map(&p.ma, g.a, FMT, AMN, g.k, g.m, g.lda, g.stride_a, g.batch, tc::kBM) ||
       !make_map(&p.mb, g.b, FMT, BMN, g.k, g.n, g.ldb, g.stride_b, g.batch, BN))
     return cudaErrorNotSupported;
@@ -205,9 +234,11 @@ cudaError_t run(const GemmArgs& g, cudaStream_t stream) {
   p.beta = g.beta;
   p.alpha_dev = g.alpha_dev;
   p.beta_dev = g.beta_dev;
+  p.vec_out = (aligned_to(g.c, 16) && g.ldc % 8 == 0 && (g.batch == 1 || g.stride_c % 8 == 0))
+                  ? 1 : 0;
   unsigned int* to = timeout_counter();
   if (to == nullptr) return cudaErrorNotSupported;
-  return tc::launch_tc_gemm<GemmProblem<T, AMN, BMN>, BN, STAGES, FMT>(
+  return tc::launch_tc_gemm<GemmProblem<T, AMN, BMN, TOUT>, BN, STAGES, FMT>(
       p, sm_count(current_device()), to, stream);
 }
 
@@ -217,7 +248,20 @@ cudaError_t run_layout(const GemmArgs& g, cudaStream_t stream) {
   const bool amn = !g.trans_a, bmn = g.trans_b;
   if (amn && bmn) return run<T, FMT, true, true>(g, stream);
   if (amn) return run<T, FMT, true, false>(g, stream);
-  if (bmn) return run<T, FMT, false, true>(g, stream);
+  if (bmn) {
+    // T,T as C^T = op(B)^T op(A)^T: op(B)^T (n x k) is MN-major in B, op(A)^T (k x m)
+    // K-major in A, the operand forms of N,N; C is written back transposed
+    GemmArgs s = g;
+    s.m = g.n;
+    s.n = g.m;
+    s.a = g.b;
+    s.lda = g.ldb;
+    s.stride_a = g.stride_b;
+    s.b = g.a;
+    s.ldb = g.lda;
+    s.stride_b = g.stride_a;
+    return run<T, FMT, true, false, true>(s, stream);
+  }
   return run<T, FMT, false, false>(g, stream);
 }
 

@@ -495,21 +495,23 @@ def test_gpu_gemm_ex_tensor_core_layout(cuda, built, typ, m, n, k, batch, beta):
 @pytest.mark.parametrize("m,n,k,batch,beta,pad", [(2048, 2048, 2048, 1, 0.0, 0),
                                                   (1000, 777, 520, 2, 0.5, 8),
                                                   (129, 2304, 72, 3, -1.0, 16),
-                                                  (4096, 136, 1000, 1, 0.0, 24)])
+                                                  (4096, 136, 1000, 1, 0.0, 24),
+                                                  (1000, 1536, 256, 2, 0.0, 0)])
 def test_gpu_gemm_ex_tensor_core_all_layouts(cuda, built, typ, ta, tb, m, n, k, batch, beta, pad):
     """Every transpose combination on the tcgen05 kernel: K-major operands (A with T,
     B with N) and MN-major ones (A with N, B with T), partial tiles in M, N and K,
     padded leading dimensions, batches, beta != 0.  Against the oracle's 16-bit GEMM
     (cublas_kernels.metal:1008-1045): normwise 1e-2 per batch entry on 16384 sampled
-    entries (all entries when fewer), padding untouched."""
+    entries (all entries when fewer), padding untouched.  Unpadded cases keep C's columns
+    16-byte aligned (the transposed-output store of T,T writes 16-byte runs there)."""
     torch = cuda
     rng = np.random.default_rng(m * 3 + n * 5 + k * 7 + 11 * ta + 13 * tb)
     lda = (k if ta else m) + pad
     ldb = (n if tb else k) + pad
-    ldc = m + 3
+    ldc = m + 3 if pad else m
     sa = lda * (m if ta else k) + 64
     sb = ldb * (k if tb else n) + 128
-    sc = ldc * n + 5
+    sc = ldc * n + (5 if pad else 64)
     conv = oracle.half_bits if typ == "f16" else oracle.bf16_bits
     A16 = conv(rng.uniform(-1, 1, sa * batch).astype(np.float32))
     B16 = conv(rng.uniform(-1, 1, sb * batch).astype(np.float32))

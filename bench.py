@@ -421,13 +421,33 @@ def suite_sgemm(s: Suite) -> dict:
     args = (h, 0, 0, n, m, k, C.byref(one), C.c_void_p(b.data_ptr()), n,
             C.c_void_p(a.data_ptr()), k, C.byref(zero), C.c_void_p(c.data_ptr()), n)
     ms, launches = s.time(lambda: L.cublasSgemm_v2(*args), flush=True)
+    flop = 2.0 * m * n * k
+    # end to end through the C ABI with host buffers: A and B copied in from pinned host
+    # memory, the call, C copied back, all inside the timed region
+    ha, hb = (t.cpu().pin_memory() for t in (a, b))
+    hc = torch.empty(m * n, dtype=torch.float32, pin_memory=True)
+    da, db, dc = torch.empty_like(a), torch.empty_like(b), torch.empty_like(c)
+    e_args = (h, 0, 0, n, m, k, C.byref(one), C.c_void_p(db.data_ptr()), n,
+              C.c_void_p(da.data_ptr()), k, C.byref(zero), C.c_void_p(dc.data_ptr()), n)
+
+    def e2e_call():
+        da.copy_(ha, non_blocking=True)
+        db.copy_(hb, non_blocking=True)
+        assert L.cublasSgemm_v2(*e_args) == 0
+        hc.copy_(dc, non_blocking=True)
+    e_ms, _ = s.time(e2e_call, flush=True)
+    e2e = {"value": flop / (e_ms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms": e_ms,
+           "h2d_bytes_per_step": 4 * (m * k + k * n), "d2h_bytes_per_step": 4 * m * n,
+           "path": "pinned host -> device copies of A and B, cublasSgemm_v2, device -> "
+                   "pinned host copy of C"}
+    del ha, hb, hc, da, db, dc
     # the FFMA kernel the same call runs under CUBLAS_PEDANTIC_MATH, for comparison
     assert L.cublasSetMathMode(h, capi.CUBLAS_PEDANTIC_MATH) == 0
     ms_ffma, _ = s.time(lambda: L.cublasSgemm_v2(*args), flush=True)
     assert L.cublasDestroy_v2(h) == 0
-    flop = 2.0 * m * n * k
     tf = flop / (ms * 1e-3) / 1e12
-    out = {"value": tf, "unit": "TFLOP/s", "ms": ms, "dtype": "f32 (split-tf32 on tcgen05)",
+    out = {"value": tf, "unit": "TFLOP/s", "ms": ms, "e2e": e2e,
+           "dtype": "f32 (split-tf32 on tcgen05)",
            "config": f"{m}x{n}x{k} fp32, L2 flushed before each call; hi/lo split of A and B, "
                      "split-K GEMM, split-order reduction",
            "roofline": s.roof("tc_gemm_split_kernel<SplitGemmProblem<256>,256,2,2>", tf,
@@ -471,15 +491,52 @@ def suite_spmv(s: Suite) -> dict:
     one, zero = C.c_float(1.0), C.c_float(0.0)
     ms, launches = s.time(lambda: L.cusparseSpMV(h, 0, C.byref(one), ma, vx, C.byref(zero), vy,
                                                  0, 0, None), flush=True)
+    nnz = mtx["nnz"]
+    alg_bytes = nnz * 8 + (rows + 1) * 4 + rows * 4 + rows * 4
+    # end to end through the C ABI with host buffers: the CSR arrays and x copied in from
+    # pinned host memory into the buffers a second descriptor names, the call, y copied
+    # back, all inside the timed region
+    e2e = None
+    if s.shard == 1:
+        keys = ("row_offsets", "col_ind", "values", "x")
+        host = {kk: mtx[kk].cpu().pin_memory() for kk in keys}
+        dev = {kk: torch.empty_like(mtx[kk]) for kk in keys}
+        hy = torch.empty(rows, dtype=torch.float32, pin_memory=True)
+        dy = torch.empty_like(y)
+        mb, ex, ey = C.c_void_p(), C.c_void_p(), C.c_void_p()
+        assert L.cusparseCreateCsr(C.byref(mb), rows, rows, nnz,
+                                   C.c_void_p(dev["row_offsets"].data_ptr()),
+                                   C.c_void_p(dev["col_ind"].data_ptr()),
+                                   C.c_void_p(dev["values"].data_ptr()), 2, 2, 0, 0) == 0
+        assert L.cusparseCreateDnVec(C.byref(ex), rows, C.c_void_p(dev["x"].data_ptr()), 0) == 0
+        assert L.cusparseCreateDnVec(C.byref(ey), rows, C.c_void_p(dy.data_ptr()), 0) == 0
+
+        def e2e_call():
+            for kk in keys:
+                dev[kk].copy_(host[kk], non_blocking=True)
+            assert L.cusparseSpMV(h, 0, C.byref(one), mb, ex, C.byref(zero), ey, 0, 0,
+                                  None) == 0
+            hy.copy_(dy, non_blocking=True)
+        steps, warm = s.steps, s.warmup
+        s.steps, s.warmup = 3, 1
+        e_ms, _ = s.time(e2e_call)
+        s.steps, s.warmup = steps, warm
+        e2e = {"value": alg_bytes / (e_ms * 1e-3) / 1e9, "unit": "GB/s", "ms": e_ms,
+               "h2d_bytes_per_step": sum(host[kk].numel() * 4 for kk in keys),
+               "d2h_bytes_per_step": rows * 4,
+               "path": "pinned host -> device copies of row offsets, column indices, values "
+                       "and x, cusparseSpMV, device -> pinned host copy of y"}
+        for fn, d in (("cusparseDestroyDnVec", ex), ("cusparseDestroyDnVec", ey),
+                      ("cusparseDestroySpMat", mb)):
+            assert getattr(L, fn)(d) == 0
+        del host, dev, hy, dy
     for fn, d in (("cusparseDestroyDnVec", vx), ("cusparseDestroyDnVec", vy),
                   ("cusparseDestroySpMat", ma)):
         assert getattr(L, fn)(d) == 0
     assert L.cusparseDestroy(h) == 0
-    nnz = mtx["nnz"]
     ceiling = gather_ceiling(s, mtx["x"], mtx["col_ind"], nnz)
-    alg_bytes = nnz * 8 + (rows + 1) * 4 + rows * 4 + rows * 4
     gbs = alg_bytes / (ms * 1e-3) / 1e9
-    out = {"value": gbs, "unit": "GB/s", "ms": ms, "dtype": "f32/i32",
+    out = {"value": gbs, "unit": "GB/s", "ms": ms, "dtype": "f32/i32", "e2e": e2e,
            "config": f"{rows} rows, nnz {nnz} ({nnz / rows:.2f}/row), power law k^-2 on "
                      "[2.2, 4096], L2 flushed before each call",
            "reference_formula_gbs": (nnz * 8 + 2 * rows * 4) / (ms * 1e-3) / 1e9,
@@ -996,10 +1053,35 @@ def suite_gemm_bf16(s: Suite) -> dict:
         ms_l, launches_l = s.time(lambda: L.cublasGemmStridedBatchedEx(*a_))
         layouts[name] = {"ms": ms_l, "TFLOP/s": flop / (ms_l * 1e-3) / 1e12,
                          "launches": launches_l}
+    # end to end through the C ABI with host buffers (N,N): A and B copied in from pinned
+    # host memory, the call, C copied back, all inside the timed region
+    e2e = None
+    if s.shard == 1:
+        ha, hb = (t.cpu().pin_memory() for t in (a, b))
+        hc = torch.empty(m * n * batch, dtype=torch.bfloat16, pin_memory=True)
+        da, db = torch.empty_like(a), torch.empty_like(b)
+        e_args = list(args(0, 0))
+        e_args[7], e_args[11] = C.c_void_p(da.data_ptr()), C.c_void_p(db.data_ptr())
+
+        def e2e_call():
+            da.copy_(ha, non_blocking=True)
+            db.copy_(hb, non_blocking=True)
+            assert L.cublasGemmStridedBatchedEx(*e_args) == 0
+            hc.copy_(c, non_blocking=True)
+        steps, warm = s.steps, s.warmup
+        s.steps, s.warmup = 3, 1
+        e_ms, _ = s.time(e2e_call)
+        s.steps, s.warmup = steps, warm
+        e2e = {"value": flop / (e_ms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms": e_ms,
+               "h2d_bytes_per_step": 2 * (m * k + k * n) * batch,
+               "d2h_bytes_per_step": 2 * m * n * batch,
+               "path": "pinned host -> device copies of A and B, cublasGemmStridedBatchedEx "
+                       "(N,N), device -> pinned host copy of C"}
+        del ha, hb, hc, da, db
     assert L.cublasDestroy_v2(h) == 0
     ms, launches = layouts["NN"]["ms"], layouts["NN"]["launches"]
     tf = flop / (ms * 1e-3) / 1e12
-    out = {"value": tf, "unit": "TFLOP/s", "ms": ms, "dtype": "bf16 (fp32 accumulate)",
+    out = {"value": tf, "unit": "TFLOP/s", "ms": ms, "dtype": "bf16 (fp32 accumulate)", "e2e": e2e,
            "config": f"{m}x{n}x{k} x batch {batch}, N,N (A MN-major, B K-major), operands "
                      f"{3 * m * k * batch * 2 / 1e9:.1f} GB",
            "roofline": s.roof("tc_gemm_kernel<GemmProblem<bf16,MN,K>>", tf, "tensor"),
@@ -1534,6 +1616,8 @@ def summarize(suite: dict | None) -> dict | None:
                      None if r.get("ms") is None else float(f"{r['ms']:.4g}")]
         if r.get("exchange_share") is not None:  # the x exchange's share of the SpMV step
             out[name].append({"exchange_share": round(float(r["exchange_share"]), 3)})
+        if r.get("e2e"):  # the same metric through host buffers
+            out[name].append({"e2e": float(f"{r['e2e']['value']:.4g}")})
         if (r.get("gather_ceiling") or {}).get("spmv_frac_of_ceiling") is not None:
             out[name].append({"frac_of_gather_ceiling":
                               round(float(r["gather_ceiling"]["spmv_frac_of_ceiling"]), 3)})

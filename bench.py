@@ -1289,7 +1289,7 @@ def suite_geam(s: Suite) -> dict:
 
 def suite_dgemm(s: Suite) -> dict:
     """cublasDgemm fp64 M = N = K = 4096 (column-major, N,N), alpha 1, beta 0,
-    uniform[-1, 1] from seed 21, through the register-blocked DFMA kernel."""
+    uniform[-1, 1] from seed 21, through the fp64 tensor-core MMA kernel."""
     from muda_b200 import synth
     torch = s.torch
     m = n = k = 4096 // s.scale
@@ -1306,7 +1306,7 @@ def suite_dgemm(s: Suite) -> dict:
     tf = flop / (ms * 1e-3) / 1e12
     out = {"value": tf, "unit": "TFLOP/s", "ms": ms, "dtype": "f64",
            "config": f"{m}x{n}x{k} fp64 N,N, L2 flushed before each call",
-           "roofline": s.roof("dgemm_kernel<128,64,false,false>", tf, "fp64"),
+           "roofline": s.roof("dgemm_kernel<128,false,false> (fp64 MMA)", tf, "fp64"),
            "launches": launches}
     if s.cpu:
         import oracle

@@ -19,11 +19,10 @@
 // reductions are one launch whose last CTA adds the per-CTA partials in CTA order
 // (deterministic).  dgemv gives every thread one row (op N, columns streamed in
 // order) or every warp one column (op T), splitting the inner dimension into chunks
-// when the outer one cannot fill the GPU.  dgemm is register-blocked DFMA: a CTA of
-// 256 threads owns a 128 x 128 tile (64 x 64 for problems with fewer tiles than
-// twice the SM count), 8 x 8 (4 x 4) accumulators per thread on a stride-2
-// interleave so that each warp's shared-memory reads of a k-row are contiguous,
-// k in steps of 8 staged through two shared buffers.
+// when the outer one cannot fill the GPU.  dgemm runs on the fp64 tensor-core MMA
+// (mma.m8n8k4 .f64): a CTA owns a 128 x 64 tile (64 x 64 for problems with fewer
+// tiles than twice the SM count), each warp 32 x 32, k in stages staged through a
+// cp.async ring in shared memory.
 #include "blas/dblas.hpp"
 
 #include <cuda_runtime.h>
@@ -436,140 +435,179 @@ int dgemv_chunks(bool trans, int m, int n) {
 
 // ------------------------------------------------------------------ gemm
 
-// Tile BM x BN, k step 8, 256 threads as 16 x 16; thread (tm, tn) owns rows
-// 2*tm + 32*q + e and columns 2*tn + 32*q' + f (q < TM/2, e, f < 2), so the double2
-// reads of a k-row by the 16 threads of a half-warp are one contiguous 256 bytes.
+// fp64 tensor-core MMA, D(8x8) = A(8x4) B(4x8) + D.  Fragments (PTX ISA, mma.m8n8k4 with
+// .f64 operands): lane l holds A(l/4, l%4), B(l%4, l/4) and D(l/4, 2(l%4)) and
+// D(l/4, 2(l%4) + 1).
+__device__ __forceinline__ void dmma(double (&d)[2], double a, double b) {
+  asm("mma.sync.aligned.m8n8k4.row.col.f64.f64.f64.f64 {%0,%1}, {%2}, {%3}, {%0,%1};"
+      : "+d"(d[0]), "+d"(d[1])
+      : "d"(a), "d"(b));
+}
+
+// 8-byte asynchronous copy global -> shared; `ok` false writes zero and reads nothing.
+__device__ __forceinline__ void cp_async8(double* dst, const double* src, bool ok) {
+  const unsigned s = static_cast<unsigned>(__cvta_generic_to_shared(dst));
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 8, %2;" ::"r"(s), "l"(src),
+               "r"(ok ? 8 : 0)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() {
+  asm volatile("cp.async.commit_group;" ::: "memory");
+}
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+constexpr int kDBK = 32;     // k per stage: eight MMA k-steps
+constexpr int kDStages = 2;  // the copy of stage kt + 1 flies while stage kt computes
+
+// One operand's stage in shared memory: element (i, kk), i along M (or N) and kk along
+// K, sits at kk * (ROWS + 4) + i when the operand is contiguous along M / N in global
+// memory and at i * (kDBK + 4) + kk when it is contiguous along K, so the copies write
+// contiguous runs.  Both strides are 4 (mod 16) doubles: the 16 (i, kk) pairs a
+// half-warp reads for one fragment (4 consecutive i by 4 consecutive kk) land in 16
+// different bank pairs.
+template <int ROWS, bool MN_CONTIG>
+struct DTile {
+  static constexpr int kElems = MN_CONTIG ? kDBK * (ROWS + 4) : ROWS * (kDBK + 4);
+  __device__ static int at(int i, int kk) {
+    return MN_CONTIG ? kk * (ROWS + 4) + i : i * (kDBK + 4) + kk;
+  }
+};
+
+// Stage sizes: the larger of the two layouts of each operand, so one size serves every
+// transpose.
+template <int BM, int BN>
+struct DStage {
+  static constexpr int kA = DTile<BM, true>::kElems > DTile<BM, false>::kElems
+                                ? DTile<BM, true>::kElems
+                                : DTile<BM, false>::kElems;
+  static constexpr int kB = DTile<BN, true>::kElems > DTile<BN, false>::kElems
+                                ? DTile<BN, true>::kElems
+                                : DTile<BN, false>::kElems;
+  static constexpr int kSmemBytes = kDStages * (kA + kB) * 8;
+};
+
+// Copies rows r0 .. r0 + ROWS - 1 (i) by k0 .. k0 + kDBK - 1 (kk) of an operand into
+// `dst`: element (i, kk) of op(X) is X[r + k * ld] when X is contiguous along M / N and
+// X[k + r * ld] otherwise; rows >= R and k >= K read as zero.
+template <int ROWS, int THREADS, bool MN_CONTIG>
+__device__ __forceinline__ void dgemm_stage_copy(double* dst, const double* X, long long ld,
+                                                 int r0, int R, int k0, int K, int tid) {
+  using TL = DTile<ROWS, MN_CONTIG>;
+#pragma unroll
+  for (int p = 0; p < ROWS * kDBK / THREADS; ++p) {
+    const int e = tid + THREADS * p;
+    const int i = MN_CONTIG ? e % ROWS : e / kDBK;
+    const int kk = MN_CONTIG ? e / ROWS : e % kDBK;
+    const bool ok = r0 + i < R && k0 + kk < K;
+    const double* src =
+        !ok ? X
+            : (MN_CONTIG ? X + (r0 + i) + static_cast<long long>(k0 + kk) * ld
+                         : X + (k0 + kk) + static_cast<long long>(r0 + i) * ld);
+    cp_async8(dst + TL::at(i, kk), src, ok);
+  }
+}
+
+// CTA tile BM x 64 (BM = 128: 8 warps as 4 x 2; BM = 64: 4 warps as 2 x 2), warp tile
+// 32 x 32 = 4 x 4 MMA tiles (32 accumulators per lane), k in stages through a cp.async
+// ring.  Per k-step a warp reads 8 fragments (one double per lane each) for 16 MMAs of
+// 256 FMAs: shared-memory traffic is a small fraction of the fp64 pipe's time, where a
+// register-blocked DFMA kernel is bound by its operand reads.
 template <int BM, int BN, bool TA, bool TB>
-__global__ void __launch_bounds__(kThreads, BM * BN >= 128 * 128 ? 1 : 2)
+__global__ void __launch_bounds__(BM * BN / 32, BM * BN >= 128 * 128 ? 1 : (BM == 128 ? 2 : 3))
     dgemm_kernel(const DgemmArgs g) {
-  constexpr int BK = 8;
-  constexpr int TM = BM / 16, TN = BN / 16;
-  constexpr int A_PER = BM * BK / kThreads;
-  constexpr int B_PER = BN * BK / kThreads;
-  __shared__ __align__(16) double As[2][BK][BM + 2];
-  __shared__ __align__(16) double Bs[2][BK][BN + 2];
+  constexpr int THREADS = BM * BN / 32;
+  using TileA = DTile<BM, !TA>;
+  using TileB = DTile<BN, TB>;
+  constexpr int kStageA = DStage<BM, BN>::kA, kStageB = DStage<BM, BN>::kB;
+  extern __shared__ __align__(16) double dsm[];
+  double* As = dsm;
+  double* Bs = dsm + kDStages * kStageA;
 
   const double alpha = scalar_of(g.alpha, g.alpha_dev);
   const double beta = scalar_of(g.beta, g.beta_dev);
-  const int tid = threadIdx.x;
-  const int tm = tid % 16, tn = tid / 16;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int wm = warp % (BM / 32), wn = warp / (BM / 32);
   const int m0 = blockIdx.x * BM, n0 = blockIdx.y * BN;
+  const int kt_count = (g.k + kDBK - 1) / kDBK;
 
   for (int z = blockIdx.z; z < g.batch; z += gridDim.z) {
     const double* A = g.a + z * g.stride_a;
     const double* B = g.b + z * g.stride_b;
     double* Cm = g.c + z * g.stride_c;
-    double acc[TM][TN];
+    double acc[4][4][2];
 #pragma unroll
-    for (int i = 0; i < TM; ++i)
+    for (int i = 0; i < 4; ++i)
 #pragma unroll
-      for (int j = 0; j < TN; ++j) acc[i][j] = 0.0;
+      for (int j = 0; j < 4; ++j) acc[i][j][0] = acc[i][j][1] = 0.0;
 
     if (alpha != 0.0 && g.k > 0) {
-      double ra[A_PER], rb[B_PER];
-      // element p of this thread's share of the A tile: (row mi, k index kk)
-      auto a_pos = [&](int p, int& mi, int& kk) {
-        const int t = tid + kThreads * p;
-        if constexpr (TA) {
-          kk = t % BK;
-          mi = t / BK;
-        } else {
-          mi = t % BM;
-          kk = t / BM;
-        }
+      auto load = [&](int slot, int kt) {
+        dgemm_stage_copy<BM, THREADS, !TA>(As + slot * kStageA, A, g.lda, m0, g.m, kt * kDBK,
+                                           g.k, tid);
+        dgemm_stage_copy<BN, THREADS, TB>(Bs + slot * kStageB, B, g.ldb, n0, g.n, kt * kDBK,
+                                            g.k, tid);
       };
-      auto b_pos = [&](int p, int& kk, int& nj) {
-        const int t = tid + kThreads * p;
-        if constexpr (TB) {
-          nj = t % BN;
-          kk = t / BN;
-        } else {
-          kk = t % BK;
-          nj = t / BK;
-        }
-      };
-      auto fetch = [&](int k0) {
 #pragma unroll
-        for (int p = 0; p < A_PER; ++p) {
-          int mi, kk;
-          a_pos(p, mi, kk);
-          const int gm = m0 + mi, gk = k0 + kk;
-          ra[p] = (gm < g.m && gk < g.k)
-                      ? __ldg(TA ? A + gk + static_cast<long long>(gm) * g.lda
-                                 : A + gm + static_cast<long long>(gk) * g.lda)
-                      : 0.0;
-        }
-#pragma unroll
-        for (int p = 0; p < B_PER; ++p) {
-          int kk, nj;
-          b_pos(p, kk, nj);
-          const int gk = k0 + kk, gn = n0 + nj;
-          rb[p] = (gk < g.k && gn < g.n)
-                      ? __ldg(TB ? B + gn + static_cast<long long>(gk) * g.ldb
-                                 : B + gk + static_cast<long long>(gn) * g.ldb)
-                      : 0.0;
-        }
-      };
-      auto stash = [&](int buf) {
-#pragma unroll
-        for (int p = 0; p < A_PER; ++p) {
-          int mi, kk;
-          a_pos(p, mi, kk);
-          As[buf][kk][mi] = ra[p];
-        }
-#pragma unroll
-        for (int p = 0; p < B_PER; ++p) {
-          int kk, nj;
-          b_pos(p, kk, nj);
-          Bs[buf][kk][nj] = rb[p];
-        }
-      };
-      fetch(0);
-      stash(0);
-      __syncthreads();
-      int buf = 0;
-      for (int k0 = 0; k0 < g.k; k0 += BK) {
-        const bool more = k0 + BK < g.k;
-        if (more) fetch(k0 + BK);
-#pragma unroll
-        for (int kk = 0; kk < BK; ++kk) {
-          double a[TM], b[TN];
-#pragma unroll
-          for (int q = 0; q < TM / 2; ++q) {
-            const double2 v = *reinterpret_cast<const double2*>(&As[buf][kk][2 * tm + 32 * q]);
-            a[2 * q] = v.x;
-            a[2 * q + 1] = v.y;
-          }
-#pragma unroll
-          for (int q = 0; q < TN / 2; ++q) {
-            const double2 v = *reinterpret_cast<const double2*>(&Bs[buf][kk][2 * tn + 32 * q]);
-            b[2 * q] = v.x;
-            b[2 * q + 1] = v.y;
-          }
-#pragma unroll
-          for (int i = 0; i < TM; ++i)
-#pragma unroll
-            for (int j = 0; j < TN; ++j) acc[i][j] = fma(a[i], b[j], acc[i][j]);
-        }
-        if (more) stash(buf ^ 1);
-        __syncthreads();
-        buf ^= 1;
+      for (int s = 0; s < kDStages - 1; ++s) {
+        if (s < kt_count) load(s, s);
+        cp_async_commit();
       }
+      for (int kt = 0; kt < kt_count; ++kt) {
+        cp_async_wait<kDStages - 2>();  // stage kt has landed (this thread's copies)
+        __syncthreads();                // everyone's, and stage kt - 1 is no longer read
+        const int nk = kt + kDStages - 1;
+        if (nk < kt_count) load(nk % kDStages, nk);
+        cp_async_commit();
+        const double* as = As + (kt % kDStages) * kStageA;
+        const double* bs = Bs + (kt % kDStages) * kStageB;
+#pragma unroll
+        for (int ks = 0; ks < kDBK / 4; ++ks) {
+          const int kk = ks * 4 + (lane & 3);
+          double a[4], b[4];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) a[i] = as[TileA::at(wm * 32 + i * 8 + (lane >> 2), kk)];
+#pragma unroll
+          for (int j = 0; j < 4; ++j) b[j] = bs[TileB::at(wn * 32 + j * 8 + (lane >> 2), kk)];
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+#pragma unroll
+            for (int j = 0; j < 4; ++j) dmma(acc[i][j], a[i], b[j]);
+        }
+      }
+      cp_async_wait<0>();
+      __syncthreads();  // the next batch entry refills the ring
     }
 #pragma unroll
-    for (int i = 0; i < TM; ++i) {
-      const int gm = m0 + 2 * tm + 32 * (i / 2) + (i & 1);
+    for (int i = 0; i < 4; ++i) {
+      const int gm = m0 + wm * 32 + i * 8 + (lane >> 2);
       if (gm >= g.m) continue;
 #pragma unroll
-      for (int j = 0; j < TN; ++j) {
-        const int gn = n0 + 2 * tn + 32 * (j / 2) + (j & 1);
-        if (gn >= g.n) continue;
-        double* cp = Cm + gm + static_cast<long long>(gn) * g.ldc;
-        const double prev = beta == 0.0 ? 0.0 : beta * *cp;
-        *cp = fma(alpha, acc[i][j], prev);
+      for (int j = 0; j < 4; ++j) {
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const int gn = n0 + wn * 32 + j * 8 + 2 * (lane & 3) + e;
+          if (gn >= g.n) continue;
+          double* cp = Cm + gm + static_cast<long long>(gn) * g.ldc;
+          const double prev = beta == 0.0 ? 0.0 : beta * *cp;
+          *cp = fma(alpha, acc[i][j][e], prev);
+        }
       }
     }
   }
+}
+
+template <int BM, int BN, bool TA, bool TB>
+cudaError_t launch_dgemm_kernel(const DgemmArgs& g, dim3 grid, cudaStream_t stream) {
+  constexpr int smem = DStage<BM, BN>::kSmemBytes;
+  auto kern = dgemm_kernel<BM, BN, TA, TB>;
+  const cudaError_t e =
+      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) return e;
+  kern<<<grid, BM * BN / 32, smem, stream>>>(g);
+  return cudaGetLastError();
 }
 
 template <int BM, int BN>
@@ -577,17 +615,11 @@ cudaError_t launch_dgemm_tiles(const DgemmArgs& g, cudaStream_t stream) {
   const dim3 grid((g.m + BM - 1) / BM, (g.n + BN - 1) / BN,
                   static_cast<unsigned>(g.batch < 65535 ? g.batch : 65535));
   if (g.trans_a) {
-    if (g.trans_b)
-      dgemm_kernel<BM, BN, true, true><<<grid, kThreads, 0, stream>>>(g);
-    else
-      dgemm_kernel<BM, BN, true, false><<<grid, kThreads, 0, stream>>>(g);
-  } else {
-    if (g.trans_b)
-      dgemm_kernel<BM, BN, false, true><<<grid, kThreads, 0, stream>>>(g);
-    else
-      dgemm_kernel<BM, BN, false, false><<<grid, kThreads, 0, stream>>>(g);
+    return g.trans_b ? launch_dgemm_kernel<BM, BN, true, true>(g, grid, stream)
+                     : launch_dgemm_kernel<BM, BN, true, false>(g, grid, stream);
   }
-  return cudaGetLastError();
+  return g.trans_b ? launch_dgemm_kernel<BM, BN, false, true>(g, grid, stream)
+                   : launch_dgemm_kernel<BM, BN, false, false>(g, grid, stream);
 }
 
 }  // namespace
@@ -673,8 +705,7 @@ cudaError_t launch_dgemv(bool trans, int m, int n, double alpha, const double* a
 cudaError_t launch_dgemm(const DgemmArgs& g, cudaStream_t stream) noexcept {
   if (g.m <= 0 || g.n <= 0 || g.batch <= 0) return cudaSuccess;
   const int sms = sm_count(current_device());
-  // 128 x 64 tiles, two CTAs per SM, when they fill the GPU twice (at 4096^3 they run
-  // 5% faster than 128 x 128 tiles at one CTA per SM, and 24% faster than 64 x 64)
+  // 128 x 64 tiles (two CTAs per SM) when they fill the GPU twice, else 64 x 64
   const long long big_tiles = static_cast<long long>((g.m + 127) / 128) * ((g.n + 63) / 64) *
                               g.batch;
   if (big_tiles >= 2ll * (sms > 0 ? sms : 148)) return launch_dgemm_tiles<128, 64>(g, stream);

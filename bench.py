@@ -579,6 +579,31 @@ def gather_ceiling(s: Suite, x, col_ind, nnz: int) -> dict:
     return best
 
 
+def scatter_ceiling(s: Suite, y, col_ind, nnz: int) -> dict:
+    """The matrix's own column stream read and 1.0 added to y[col] by reductions that
+    return nothing (mb200ProbeScatter): the scatter of A^T x without its loads of values
+    and x.  Best of one and four indices per lane, 4 and 8 CTAs of 256 per SM.  Leaves
+    garbage in y."""
+    from muda_b200 import capi
+    P = capi.probe()
+    sms = s.torch.cuda.get_device_properties(s.torch.cuda.current_device()).multi_processor_count
+    best = None
+    for per_lane in (1, 4):
+        for ctas in (4, 8):
+            grid = sms * ctas
+            ms, _ = s.time(lambda: P.mb200ProbeScatter(
+                C.c_void_p(y.data_ptr()), C.c_void_p(col_ind.data_ptr()), nnz, per_lane, grid,
+                s.sp), flush=True)
+            n_done = nnz if per_lane == 1 else nnz // 4 * 4
+            rate = n_done / (ms * 1e-3)
+            if best is None or rate > best["reductions_per_s"]:
+                best = {"reductions_per_s": rate, "ms": nnz / rate * 1e3, "per_lane": per_lane,
+                        "grid": grid}
+    best["what"] = ("mb200ProbeScatter: column indices streamed (evict-first), 1.0 added to "
+                    "y[col] by red.global.add.f32, no values or x")
+    return best
+
+
 def _csr_handle(L, s, mtx, rows, cols):
     h, ma = C.c_void_p(), C.c_void_p()
     assert L.cusparseCreate(C.byref(h)) == 0
@@ -612,10 +637,13 @@ def suite_spmv_t(s: Suite) -> dict:
     nnz = mtx["nnz"]
     alg_bytes = nnz * 8 + (rows + 1) * 4 + rows * 4 + rows * 4
     gbs = alg_bytes / (ms * 1e-3) / 1e9
+    ceiling = scatter_ceiling(s, y, mtx["col_ind"], nnz)
     out = {"value": gbs, "unit": "GB/s", "ms": ms, "dtype": "f32/i32",
            "config": f"A^T x, {rows} rows, nnz {nnz}, power law, L2 flushed before each call",
            "roofline": s.roof("spmv_t_scatter<4,float>", gbs, "hbm"), "launches": launches,
-           "algorithmic_bytes_per_call": alg_bytes}
+           "algorithmic_bytes_per_call": alg_bytes,
+           "scatter_ceiling": {**ceiling, "spmv_t_reductions_per_s": nnz / (ms * 1e-3),
+                               "spmv_t_frac_of_ceiling": ceiling["ms"] / ms}}
     if s.cpu:
         import oracle
         sample = max(1, rows // 16)
@@ -1621,6 +1649,9 @@ def summarize(suite: dict | None) -> dict | None:
         if (r.get("gather_ceiling") or {}).get("spmv_frac_of_ceiling") is not None:
             out[name].append({"frac_of_gather_ceiling":
                               round(float(r["gather_ceiling"]["spmv_frac_of_ceiling"]), 3)})
+        if (r.get("scatter_ceiling") or {}).get("spmv_t_frac_of_ceiling") is not None:
+            out[name].append({"frac_of_scatter_ceiling":
+                              round(float(r["scatter_ceiling"]["spmv_t_frac_of_ceiling"]), 3)})
     return out
 
 

@@ -18,6 +18,13 @@ extern "C" {
 int mb200ProbeGather(const float* x, const int* idx, long long n, int per_lane, float* out,
                      unsigned grid, cudaStream_t stream);
 
+/* Streams n int32 indices (per_lane as for mb200ProbeGather) and adds 1.0f to
+ * y[idx[i]] for each by a reduction that returns nothing (red.global.add.f32), so that
+ * y[j] gains the count of j in idx (exact below 2^24 per element).  Returns 0 on
+ * success, 1 on a bad argument, 2 on a launch error.  The indices must lie inside y. */
+int mb200ProbeScatter(float* y, const int* idx, long long n, int per_lane, unsigned grid,
+                      cudaStream_t stream);
+
 /* Error budget of the cuRAND normal transform, every fp32 input of each step: writes
  * six floats to device memory `out` (radius error / max(1, r); hardware cos, sin error;
  * polynomial cos, sin error; the radius threshold of the hardware path).  Returns 0 on

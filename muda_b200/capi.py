@@ -345,6 +345,8 @@ def peer() -> C.CDLL:
 PROBE_PROTOS = {
     "mb200ProbeGather": ([C.c_void_p, C.c_void_p, C.c_longlong, C.c_int, C.c_void_p, C.c_uint,
                           C.c_void_p], C.c_int),
+    "mb200ProbeScatter": ([C.c_void_p, C.c_void_p, C.c_longlong, C.c_int, C.c_uint,
+                           C.c_void_p], C.c_int),
     "mb200ProbeNormalError": ([C.c_void_p, C.c_void_p], C.c_int),
 }
 

@@ -6,7 +6,9 @@
 // that nothing is optimised away, and nothing else: no values, no row structure,
 // no output vector.  Run on a matrix's own column indices it gives the rate at
 // which this GPU can serve that matrix's random x gathers, the ceiling against
-// which an SpMV kernel's gather rate is judged.
+// which an SpMV kernel's gather rate is judged.  mb200ProbeScatter does the same for
+// the transposed product: it streams the indices and adds to y[idx] by reductions that
+// return nothing, the scatter of A^T x without its loads of values and x.
 //
 // Layout: grid-stride over the indices; kPerLane consecutive indices per lane per
 // step (one 16-byte load of four indices when kPerLane is 4), all gathers of a step
@@ -45,7 +47,41 @@ __global__ void __launch_bounds__(kThreads)
   out[static_cast<long long>(blockIdx.x) * kThreads + threadIdx.x] = s;
 }
 
+// The scatter of a transposed SpMV without its products: y[idx[i]] += 1 by a
+// reduction that returns nothing (red.global.add.f32, resolved in L2).
+template <int kPerLane>
+__global__ void __launch_bounds__(kThreads)
+    scatter_kernel(float* y, const int* __restrict__ idx, long long n) {
+  const long long stride = static_cast<long long>(gridDim.x) * kThreads;
+  long long t = static_cast<long long>(blockIdx.x) * kThreads + threadIdx.x;
+  if constexpr (kPerLane == 4) {
+    const int4* idx4 = reinterpret_cast<const int4*>(idx);
+    const long long n4 = n / 4;
+    for (; t < n4; t += stride) {
+      const int4 c = __ldcs(idx4 + t);
+      atomicAdd(y + c.x, 1.0f);
+      atomicAdd(y + c.y, 1.0f);
+      atomicAdd(y + c.z, 1.0f);
+      atomicAdd(y + c.w, 1.0f);
+    }
+  } else {
+    for (; t < n; t += stride) atomicAdd(y + __ldcs(idx + t), 1.0f);
+  }
+}
+
 }  // namespace
+
+extern "C" int mb200ProbeScatter(float* y, const int* idx, long long n, int per_lane,
+                                 unsigned grid, cudaStream_t stream) {
+  if (y == nullptr || idx == nullptr || n < 0 || grid == 0) return 1;
+  if (per_lane == 4) {
+    if ((reinterpret_cast<std::uintptr_t>(idx) & 15u) != 0) return 1;
+    scatter_kernel<4><<<grid, kThreads, 0, stream>>>(y, idx, n);
+  } else {
+    scatter_kernel<1><<<grid, kThreads, 0, stream>>>(y, idx, n);
+  }
+  return cudaGetLastError() == cudaSuccess ? 0 : 2;
+}
 
 extern "C" int mb200ProbeGather(const float* x, const int* idx, long long n, int per_lane,
                                 float* out, unsigned grid, cudaStream_t stream) {

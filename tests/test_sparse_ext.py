@@ -194,6 +194,29 @@ def test_gpu_spmv_transpose_f32(cuda, built, kind, base):
     a.close()
 
 
+@pytest.mark.gpu
+@pytest.mark.parametrize("per_lane", [1, 4])
+def test_gpu_scatter_probe_counts(cuda, built, per_lane):
+    """The scatter-ceiling probe (mb200ProbeScatter) adds 1 per index: y ends as the
+    index histogram, exactly (counts far below 2^24), including a ragged tail that the
+    four-per-lane form leaves out (n not a multiple of 4)."""
+    torch = cuda
+    rng = np.random.default_rng(per_lane)
+    n, size = 1_000_003, 70_000
+    idx = rng.integers(0, size, n).astype(np.int32)
+    idx[:5000] = 17  # one hot entry
+    d_idx = torch.from_numpy(idx).cuda()
+    y = torch.zeros(size, dtype=torch.float32, device="cuda")
+    P = capi.probe()
+    assert P.mb200ProbeScatter(C.c_void_p(y.data_ptr()), C.c_void_p(d_idx.data_ptr()), n,
+                               per_lane, 296, stream_ptr(torch)) == 0
+    torch.cuda.synchronize()
+    done = n if per_lane == 1 else n // 4 * 4
+    assert np.array_equal(y.cpu().numpy(), np.bincount(idx[:done], minlength=size).astype(np.float32))
+    assert P.mb200ProbeScatter(None, C.c_void_p(d_idx.data_ptr()), n, per_lane, 296,
+                               stream_ptr(torch)) == 1
+
+
 def _half_check(got, exact, scale):
     got = got.astype(np.float64)
     bound = 2.0 ** -11 * np.abs(exact) + 2e-5 * scale + 2.0 ** -24

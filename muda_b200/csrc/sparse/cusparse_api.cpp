@@ -476,7 +476,8 @@ cusparseStatus_t cusparseSpMM(cusparseHandle_t handle, cusparseOperation_t opA,
   const cudaStream_t stream = stream_of(*o.ctx);
   const cudaError_t e = with_scratch(*o.ctx, stream, mb200::sparse::kSpmmSchedBytes, [&](void* ws) {
     const mb200::sparse::SpmmSched sc{static_cast<unsigned*>(ws),
-                                      reinterpret_cast<int*>(static_cast<char*>(ws) + 16),
+                                      reinterpret_cast<int*>(static_cast<char*>(ws) +
+                                                           mb200::sparse::kSpmmSchedHeader),
                                       mb200::sparse::kSpmmLongCap};
     return mb200::sparse::launch_spmm_csr(
         view_of(*o.a), opA != CUSPARSE_OPERATION_NON_TRANSPOSE, b, c, o.ncols,

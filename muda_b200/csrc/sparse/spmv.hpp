@@ -50,16 +50,21 @@ struct DenseView {
   bool trans;
 };
 
-// Device scratch of the row scheduler of the row-major SpMM: counters[3] (zeroed
-// by the launch: first-phase position, row-chunk position, long-row count) and
-// long_rows[long_cap].  No other call may use it while the launch runs.
+// Device scratch of the row scheduler of the row-major SpMM: counters[2 +
+// kSpmmLongBuckets] (zeroed by the launch: first-phase position, row-chunk position,
+// then the long-row count of each length bucket) and long_rows[long_cap], one region
+// of long_cap / kSpmmLongBuckets rows per bucket.  No other call may use it while the
+// launch runs.
+constexpr int kSpmmLongBuckets = 8;
 struct SpmmSched {
   unsigned* counters;
   int* long_rows;
   unsigned long_cap;
 };
 constexpr unsigned kSpmmLongCap = 65536;
-constexpr std::size_t kSpmmSchedBytes = 16 + std::size_t{kSpmmLongCap} * 4;
+constexpr std::size_t kSpmmSchedHeader = 64;  // counters, padded
+static_assert((2 + kSpmmLongBuckets) * 4 <= kSpmmSchedHeader, "counters fit the header");
+constexpr std::size_t kSpmmSchedBytes = kSpmmSchedHeader + std::size_t{kSpmmLongCap} * 4;
 
 // C = alpha * op(A) * op(B) + beta * C, fp32, C with out_rows x ncols entries
 // (out_rows = a.rows, or a.cols when trans_a).  Without trans_a every output is

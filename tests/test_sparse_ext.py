@@ -303,9 +303,10 @@ def test_gpu_spmm(cuda, built, shape, op_a, op_b, order_b, order_c):
 
 @pytest.mark.gpu
 def test_gpu_spmm_long_row_list_overflow(cuda, built):
-    """More rows above the scheduler's 256-entry threshold than its list holds
-    (65536): every row is then taken in the chunked phase, and the results stay
-    bit-identical to the oracle (checked on a sample of rows)."""
+    """More rows above the scheduler's 256-entry threshold in one length bucket than
+    its region of the list holds (8192 of 65536): every row is then taken in the
+    chunked phase, and the results stay bit-identical to the oracle (checked on a
+    sample of rows)."""
     torch = cuda
     rng = np.random.default_rng(4242)
     rows, cols, n, k = 66000, 2048, 64, 257
@@ -324,4 +325,29 @@ def test_gpu_spmm_long_row_list_overflow(cuda, built):
     oracle.spmm_csr(sub_off, ci[sample].reshape(-1), va[sample].reshape(-1), cols, b.reshape(-1),
                     n, 2, want, n, 2, n)
     np.testing.assert_array_equal(got[sample], want.reshape(len(sample), n))
+    a.close()
+
+
+@pytest.mark.gpu
+def test_gpu_spmm_long_rows_every_bucket(cuda, built):
+    """Long rows in every length bucket of the scheduler (257 .. 6000 entries, the last
+    bucket open-ended), between short and empty rows: the first phase takes them
+    longest bucket first, the second sorts each 32-row chunk by length, and every
+    output stays bit-identical to the oracle's entry-order sums."""
+    torch = cuda
+    rng = np.random.default_rng(5151)
+    rows, cols, n = 3001, 8192, 64
+    lengths = np.where(rng.random(rows) < 0.12, rng.integers(257, 6001, rows),
+                       rng.integers(0, 24, rows))
+    lengths[:8] = [257, 383, 384, 511, 512, 767, 2896, 6000]
+    offsets, ci, va = random_csr(rng, rows, cols, lengths)
+    b = rng.uniform(-1, 1, (cols, n)).astype(np.float32)
+    a = Csr(torch, offsets, ci, va, rows, cols)
+    tb = torch.from_numpy(b.reshape(-1)).cuda()
+    tc = torch.full((rows * n,), 7.0, dtype=torch.float32, device="cuda")
+    assert a.spmm(0, 0, tb, (cols, n), n, 2, tc, (rows, n), n, 2, 1.0, 0.0) == 0
+    got = tc.cpu().numpy()
+    want = np.zeros(rows * n, np.float32)
+    oracle.spmm_csr(offsets, ci, va, cols, b.reshape(-1), n, 2, want, n, 2, n)
+    np.testing.assert_array_equal(got, want)
     a.close()

@@ -685,8 +685,24 @@ def suite_spmm(s: Suite) -> dict:
     nnz = mtx["nnz"]
     alg_bytes = nnz * 8 + (rows + 1) * 4 + 2 * rows * n * 4
     gbs = alg_bytes / (ms * 1e-3) / 1e9
+    # the row gathers alone (mb200ProbeRowGather on the matrix's own column indices)
+    P = capi.probe()
+    sms = torch.cuda.get_device_properties(torch.cuda.current_device()).multi_processor_count
+    best = None
+    for ctas in (4, 8):
+        grid = sms * ctas
+        scratch = torch.empty(grid * 256, dtype=torch.float32, device="cuda")
+        g_ms, _ = s.time(lambda: P.mb200ProbeRowGather(
+            C.c_void_p(b.data_ptr()), C.c_void_p(mtx["col_ind"].data_ptr()), nnz,
+            C.c_void_p(scratch.data_ptr()), grid, s.sp), flush=True)
+        if best is None or g_ms < best["ms"]:
+            best = {"ms": g_ms, "grid": grid, "row_bytes_per_s": nnz * n * 4 / (g_ms * 1e-3)}
+    best["what"] = ("mb200ProbeRowGather: column indices streamed, row col of B (256 bytes) "
+                    "gathered per entry with L2-only 16-byte loads, no values, no products, "
+                    "no C")
     out = {"value": gbs, "unit": "GB/s", "ms": ms, "dtype": "f32/i32",
            "gflops": 2 * nnz * n / (ms * 1e-3) / 1e9,
+           "row_gather_ceiling": {**best, "spmm_frac_of_ceiling": best["ms"] / ms},
            "config": f"{rows} rows, nnz {nnz}, N {n} row-major, L2 flushed before each call; "
                      "bytes = A + B + C once (B rows re-gathered per entry come through L2)",
            "roofline": s.roof("spmm_rows_ring<16>", gbs, "hbm"), "launches": launches,
@@ -1649,6 +1665,9 @@ def summarize(suite: dict | None) -> dict | None:
         if (r.get("gather_ceiling") or {}).get("spmv_frac_of_ceiling") is not None:
             out[name].append({"frac_of_gather_ceiling":
                               round(float(r["gather_ceiling"]["spmv_frac_of_ceiling"]), 3)})
+        if (r.get("row_gather_ceiling") or {}).get("spmm_frac_of_ceiling") is not None:
+            out[name].append({"frac_of_row_gather_ceiling":
+                              round(float(r["row_gather_ceiling"]["spmm_frac_of_ceiling"]), 3)})
         if (r.get("scatter_ceiling") or {}).get("spmv_t_frac_of_ceiling") is not None:
             out[name].append({"frac_of_scatter_ceiling":
                               round(float(r["scatter_ceiling"]["spmv_t_frac_of_ceiling"]), 3)})

@@ -25,6 +25,13 @@ int mb200ProbeGather(const float* x, const int* idx, long long n, int per_lane, 
 int mb200ProbeScatter(float* y, const int* idx, long long n, int per_lane, unsigned grid,
                       cudaStream_t stream);
 
+/* For each of n int32 indices, gathers row idx[i] of a row-major float matrix of 64
+ * columns (b 16-byte aligned; 16 lanes load one 16-byte slice each, L2-only) and writes
+ * one partial sum per thread to out (grid * 256 floats).  Returns 0 on success, 1 on a
+ * bad argument, 2 on a launch error.  The indices must lie inside b's rows. */
+int mb200ProbeRowGather(const float* b, const int* idx, long long n, float* out, unsigned grid,
+                        cudaStream_t stream);
+
 /* Error budget of the cuRAND normal transform, every fp32 input of each step: writes
  * six floats to device memory `out` (radius error / max(1, r); hardware cos, sin error;
  * polynomial cos, sin error; the radius threshold of the hardware path).  Returns 0 on

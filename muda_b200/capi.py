@@ -347,6 +347,8 @@ PROBE_PROTOS = {
                           C.c_void_p], C.c_int),
     "mb200ProbeScatter": ([C.c_void_p, C.c_void_p, C.c_longlong, C.c_int, C.c_uint,
                            C.c_void_p], C.c_int),
+    "mb200ProbeRowGather": ([C.c_void_p, C.c_void_p, C.c_longlong, C.c_void_p, C.c_uint,
+                             C.c_void_p], C.c_int),
     "mb200ProbeNormalError": ([C.c_void_p, C.c_void_p], C.c_int),
 }
 

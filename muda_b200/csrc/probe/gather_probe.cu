@@ -8,7 +8,9 @@
 // which this GPU can serve that matrix's random x gathers, the ceiling against
 // which an SpMV kernel's gather rate is judged.  mb200ProbeScatter does the same for
 // the transposed product: it streams the indices and adds to y[idx] by reductions that
-// return nothing, the scatter of A^T x without its loads of values and x.
+// return nothing, the scatter of A^T x without its loads of values and x; and
+// mb200ProbeRowGather gathers whole 256-byte rows of a 64-column B per index, the
+// gathers of an SpMM without its products.
 //
 // Layout: grid-stride over the indices; kPerLane consecutive indices per lane per
 // step (one 16-byte load of four indices when kPerLane is 4), all gathers of a step
@@ -69,7 +71,51 @@ __global__ void __launch_bounds__(kThreads)
   }
 }
 
+// The row gathers of an SpMM with a row-major B of 64 columns without its products:
+// for each index, the 16 lanes of a group load the 16 float4 slices of row idx[i]
+// (L2-only loads), four entries per group in flight, and sum them.
+__global__ void __launch_bounds__(kThreads)
+    row_gather_kernel(const float4* __restrict__ b, const int* __restrict__ idx, long long n,
+                      float* __restrict__ out) {
+  constexpr int G = 16, U = 4;
+  const long long groups = static_cast<long long>(gridDim.x) * (kThreads / G);
+  const long long grp = static_cast<long long>(blockIdx.x) * (kThreads / G) + threadIdx.x / G;
+  const int lane = threadIdx.x % G;
+  float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+  for (long long e = grp; e < n; e += U * groups) {
+    int c[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const long long t = e + u * groups;
+      c[u] = t < n ? __ldcs(idx + t) : -1;
+    }
+    float4 v[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u)
+      v[u] = c[u] >= 0 ? __ldcg(b + static_cast<long long>(c[u]) * G + lane)
+                       : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      acc.x += v[u].x;
+      acc.y += v[u].y;
+      acc.z += v[u].z;
+      acc.w += v[u].w;
+    }
+  }
+  out[static_cast<long long>(blockIdx.x) * kThreads + threadIdx.x] =
+      (acc.x + acc.y) + (acc.z + acc.w);
+}
+
 }  // namespace
+
+extern "C" int mb200ProbeRowGather(const float* b, const int* idx, long long n, float* out,
+                                   unsigned grid, cudaStream_t stream) {
+  if (b == nullptr || idx == nullptr || out == nullptr || n < 0 || grid == 0) return 1;
+  if ((reinterpret_cast<std::uintptr_t>(b) & 15u) != 0) return 1;
+  row_gather_kernel<<<grid, kThreads, 0, stream>>>(reinterpret_cast<const float4*>(b), idx, n,
+                                                   out);
+  return cudaGetLastError() == cudaSuccess ? 0 : 2;
+}
 
 extern "C" int mb200ProbeScatter(float* y, const int* idx, long long n, int per_lane,
                                  unsigned grid, cudaStream_t stream) {

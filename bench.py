@@ -332,6 +332,7 @@ class Suite:
         self.sp = C.c_void_p(int(self.stream.cuda_stream))
         self.peaks = _peaks()
         self._flush = None
+        self.e2e = True         # time the host-buffer legs (bench.py --no-e2e turns them off)
         self.shard = 1          # ranks sharing a batch-sharded workload (its 1/shard per rank)
         self.barrier = None     # called around the timed region under torchrun
 
@@ -424,23 +425,25 @@ def suite_sgemm(s: Suite) -> dict:
     flop = 2.0 * m * n * k
     # end to end through the C ABI with host buffers: A and B copied in from pinned host
     # memory, the call, C copied back, all inside the timed region
-    ha, hb = (t.cpu().pin_memory() for t in (a, b))
-    hc = torch.empty(m * n, dtype=torch.float32, pin_memory=True)
-    da, db, dc = torch.empty_like(a), torch.empty_like(b), torch.empty_like(c)
-    e_args = (h, 0, 0, n, m, k, C.byref(one), C.c_void_p(db.data_ptr()), n,
-              C.c_void_p(da.data_ptr()), k, C.byref(zero), C.c_void_p(dc.data_ptr()), n)
+    e2e = None
+    if s.e2e:
+        ha, hb = (t.cpu().pin_memory() for t in (a, b))
+        hc = torch.empty(m * n, dtype=torch.float32, pin_memory=True)
+        da, db, dc = torch.empty_like(a), torch.empty_like(b), torch.empty_like(c)
+        e_args = (h, 0, 0, n, m, k, C.byref(one), C.c_void_p(db.data_ptr()), n,
+                  C.c_void_p(da.data_ptr()), k, C.byref(zero), C.c_void_p(dc.data_ptr()), n)
 
-    def e2e_call():
-        da.copy_(ha, non_blocking=True)
-        db.copy_(hb, non_blocking=True)
-        assert L.cublasSgemm_v2(*e_args) == 0
-        hc.copy_(dc, non_blocking=True)
-    e_ms, _ = s.time(e2e_call, flush=True)
-    e2e = {"value": flop / (e_ms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms": e_ms,
-           "h2d_bytes_per_step": 4 * (m * k + k * n), "d2h_bytes_per_step": 4 * m * n,
-           "path": "pinned host -> device copies of A and B, cublasSgemm_v2, device -> "
-                   "pinned host copy of C"}
-    del ha, hb, hc, da, db, dc
+        def e2e_call():
+            da.copy_(ha, non_blocking=True)
+            db.copy_(hb, non_blocking=True)
+            assert L.cublasSgemm_v2(*e_args) == 0
+            hc.copy_(dc, non_blocking=True)
+        e_ms, _ = s.time(e2e_call, flush=True)
+        e2e = {"value": flop / (e_ms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms": e_ms,
+               "h2d_bytes_per_step": 4 * (m * k + k * n), "d2h_bytes_per_step": 4 * m * n,
+               "path": "pinned host -> device copies of A and B, cublasSgemm_v2, device -> "
+                       "pinned host copy of C"}
+        del ha, hb, hc, da, db, dc
     # the FFMA kernel the same call runs under CUBLAS_PEDANTIC_MATH, for comparison
     assert L.cublasSetMathMode(h, capi.CUBLAS_PEDANTIC_MATH) == 0
     ms_ffma, _ = s.time(lambda: L.cublasSgemm_v2(*args), flush=True)
@@ -497,7 +500,7 @@ def suite_spmv(s: Suite) -> dict:
     # pinned host memory into the buffers a second descriptor names, the call, y copied
     # back, all inside the timed region
     e2e = None
-    if s.shard == 1:
+    if s.shard == 1 and s.e2e:
         keys = ("row_offsets", "col_ind", "values", "x")
         host = {kk: mtx[kk].cpu().pin_memory() for kk in keys}
         dev = {kk: torch.empty_like(mtx[kk]) for kk in keys}
@@ -900,7 +903,7 @@ def suite_fft(s: Suite) -> dict:
     # end to end through the C ABI with host buffers: pinned input copied in, forward
     # then inverse, result copied back, all inside the timed region
     e2e = None
-    if s.shard == 1:
+    if s.shard == 1 and s.e2e:
         h_in = torch.empty(2 * n * batch, dtype=torch.float32, pin_memory=True)
         h_in.copy_(x)
         h_out = torch.empty_like(h_in)
@@ -1100,7 +1103,7 @@ def suite_gemm_bf16(s: Suite) -> dict:
     # end to end through the C ABI with host buffers (N,N): A and B copied in from pinned
     # host memory, the call, C copied back, all inside the timed region
     e2e = None
-    if s.shard == 1:
+    if s.shard == 1 and s.e2e:
         ha, hb = (t.cpu().pin_memory() for t in (a, b))
         hc = torch.empty(m * n * batch, dtype=torch.bfloat16, pin_memory=True)
         da, db = torch.empty_like(a), torch.empty_like(b)
@@ -1406,6 +1409,7 @@ def run_suite(names, args, torch) -> dict:
     for name in names:
         time.sleep(SUITE_GAP_S)
         s = Suite(torch, max(3, args.steps // 4), args.warmup, not args.no_cpu, args.scale)
+        s.e2e = not args.no_e2e
         try:
             out[name] = SUITE[name](s)
         except Exception as e:  # one failing routine must not hide the others

@@ -1317,7 +1317,7 @@ def suite_geam(s: Suite) -> dict:
     out = {"value": gbs, "unit": "GB/s", "ms": ms, "dtype": "f32",
            "op_n_n": {"value": alg / (ms_nn * 1e-3) / 1e9, "unit": "GB/s", "ms": ms_nn},
            "config": f"{m} x {n}, op(A) T, op(B) N, {alg / 1e9:.2f} GB per call > L2",
-           "roofline": s.roof("geam_kernel<float,1,0>", gbs, "hbm"), "launches": launches,
+           "roofline": s.roof("geam_kernel_db<float,1>", gbs, "hbm"), "launches": launches,
            "algorithmic_bytes_per_launch": alg}
     if s.cpu:
         import oracle

@@ -144,21 +144,124 @@ __global__ void __launch_bounds__(kLanes* kRowsPerPass, (TA || TB) ? 4 : 2)
   }
 }
 
+// Exactly one transposed operand: its staging tile is double-buffered and filled by
+// cp.async one tile ahead (element copies, skipped outside the matrix), so the copy of
+// tile t + 1 is in flight while tile t is combined and stored; the untransposed
+// operand is read into registers as in geam_kernel.
+template <typename T>
+__device__ __forceinline__ void cp_async_elem(T* dst, const T* src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], %2;" ::"r"(static_cast<unsigned>(
+                   __cvta_generic_to_shared(dst))),
+               "l"(src), "n"(static_cast<int>(sizeof(T)))
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() {
+  asm volatile("cp.async.commit_group;" ::: "memory");
+}
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+// Rows [r0, r0 + kTile) x cols [c0, c0 + 64) of op(X) = X^T into s (X[c + r * ldx] is
+// op(X)[r][c]; the copies walk c, contiguous in X), as one cp.async group.
+template <typename T>
+__device__ __forceinline__ void copy_transposed(T (*s)[kCols + 1], const T* X, long long ldx,
+                                                int m, int n, int r0, int c0) {
+#pragma unroll
+  for (int k = 0; k < kTile<T> / kRowsPerPass; ++k) {
+    const int rr = threadIdx.y + k * kRowsPerPass;
+    const int r = r0 + rr;
+#pragma unroll
+    for (int j = 0; j < kCols / kLanes; ++j) {
+      const int c = c0 + threadIdx.x + j * kLanes;
+      if (r < m && c < n)
+        cp_async_elem(&s[rr][threadIdx.x + j * kLanes], X + c + static_cast<long long>(r) * ldx);
+    }
+  }
+  cp_async_commit();
+}
+
+template <typename T, bool TA>
+__global__ void __launch_bounds__(kLanes* kRowsPerPass, 4) geam_kernel_db(GeamArgs<T> g) {
+  __shared__ T st[2][kTile<T>][kCols + 1];
+  const T alpha = g.alpha_dev ? *g.alpha_dev : g.alpha;
+  const T beta = g.beta_dev ? *g.beta_dev : g.beta;
+  const bool use_a = alpha != T(0);
+  const bool use_b = beta != T(0);
+  const bool use_t = TA ? use_a : use_b;  // the transposed operand is read
+  const bool use_n = TA ? use_b : use_a;
+  const T* xt = TA ? g.A : g.B;
+  const T* xn = TA ? g.B : g.A;
+  const long long ldt = TA ? g.lda : g.ldb;
+  const long long ldn = TA ? g.ldb : g.lda;
+  auto corner = [&](long long t, int& r0, int& c0) {
+    r0 = static_cast<int>(t % g.tiles_m) * kTile<T>;
+    c0 = static_cast<int>(t / g.tiles_m) * kCols;
+  };
+  int r0, c0;
+  corner(blockIdx.x, r0, c0);
+  if (use_t && blockIdx.x < g.tiles) {
+    copy_transposed(st[0], xt, ldt, g.m, g.n, r0, c0);
+  } else {
+    cp_async_commit();
+  }
+  int buf = 0;
+  for (long long t = blockIdx.x; t < g.tiles; t += gridDim.x, buf ^= 1) {
+    corner(t, r0, c0);
+    const long long tn = t + gridDim.x;
+    if (use_t && tn < g.tiles) {
+      int rn, cn;
+      corner(tn, rn, cn);
+      copy_transposed(st[buf ^ 1], xt, ldt, g.m, g.n, rn, cn);
+    } else {
+      cp_async_commit();  // an empty group keeps the wait counts aligned
+    }
+    T vn[kRowReps<T>][kColSteps];
+    if (use_n) load_operand<T, false>(nullptr, vn, xn, ldn, g.m, g.n, r0, c0);
+    cp_async_wait<1>();  // this thread's copies of tile t have landed
+    __syncthreads();     // and everyone's
+#pragma unroll
+    for (int k = 0; k < kColSteps; ++k) {
+      const int c = c0 + threadIdx.y + k * kRowsPerPass;
+#pragma unroll
+      for (int i = 0; i < kRowReps<T>; ++i) {
+        const int r = r0 + threadIdx.x + i * kLanes;
+        if (r < g.m && c < g.n) {
+          const T xtv = st[buf][threadIdx.x + i * kLanes][threadIdx.y + k * kRowsPerPass];
+          const T xa = TA ? xtv : vn[i][k];
+          const T xb = TA ? vn[i][k] : xtv;
+          const T ta = use_a ? mul_rn(alpha, xa) : T(0);
+          const T tb = use_b ? mul_rn(beta, xb) : T(0);
+          g.C[r + static_cast<long long>(c) * g.ldc] = combine(use_a, ta, use_b, tb);
+        }
+      }
+    }
+    __syncthreads();  // st[buf] is refilled by the next iteration's copy
+  }
+  cp_async_wait<0>();
+}
+
 // One wave: as many CTAs as the SMs hold at this instance's occupancy (its register
 // and shared-memory use differ by type and transposition), so that no CTA of the
 // grid-stride loop waits for a second wave.
 template <typename T, bool TA, bool TB>
 cudaError_t launch(const GeamArgs<T>& g, cudaStream_t stream) {
-  static const int per_sm = [] {
+  constexpr bool kDb = TA != TB;
+  auto kern = [] {
+    if constexpr (kDb) return geam_kernel_db<T, TA>;
+    else return geam_kernel<T, TA, TB>;
+  }();
+  static const int per_sm = [&] {
     int b = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b, geam_kernel<T, TA, TB>,
-                                                      kLanes * kRowsPerPass, 0) != cudaSuccess)
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b, kern, kLanes * kRowsPerPass, 0) !=
+        cudaSuccess)
       b = 0;
     return b > 0 ? b : 1;
   }();
   const long long wave = static_cast<long long>(sm_count(current_device())) * per_sm;
   const unsigned grid = static_cast<unsigned>(g.tiles < wave ? g.tiles : wave);
-  geam_kernel<T, TA, TB><<<grid, dim3(kLanes, kRowsPerPass), 0, stream>>>(g);
+  kern<<<grid, dim3(kLanes, kRowsPerPass), 0, stream>>>(g);
   return cudaGetLastError();
 }
 

@@ -242,6 +242,80 @@ __global__ void __launch_bounds__(kLanes* kRowsPerPass, 4) geam_kernel_db(GeamAr
   cp_async_wait<0>();
 }
 
+// Neither operand transposed, every column 16-byte aligned (pointers aligned, m and the
+// leading dimensions multiples of 16 / sizeof(T)): a CTA takes whole columns and its
+// threads stream them in 16-byte vectors, four vectors of each operand in flight per
+// thread, the arithmetic per element as in geam_kernel.
+template <typename T>
+struct Vec16;
+template <>
+struct Vec16<float> {
+  using V = float4;
+  static constexpr int kN = 4;
+};
+template <>
+struct Vec16<double> {
+  using V = double2;
+  static constexpr int kN = 2;
+};
+
+template <typename T>
+__device__ __forceinline__ T lane_of(const typename Vec16<T>::V& v, int e) {
+  if constexpr (Vec16<T>::kN == 4) {
+    return e == 0 ? v.x : e == 1 ? v.y : e == 2 ? v.z : v.w;
+  } else {
+    return e == 0 ? v.x : v.y;
+  }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(256) geam_nn_vec(GeamArgs<T> g) {
+  using VT = typename Vec16<T>::V;
+  constexpr int kN = Vec16<T>::kN;
+  constexpr int kU = 4;
+  const T alpha = g.alpha_dev ? *g.alpha_dev : g.alpha;
+  const T beta = g.beta_dev ? *g.beta_dev : g.beta;
+  const bool use_a = alpha != T(0);
+  const bool use_b = beta != T(0);
+  const int mv = g.m / kN;  // vectors per column
+  for (long long c = blockIdx.x; c < g.n; c += gridDim.x) {
+    const VT* a = reinterpret_cast<const VT*>(g.A + c * g.lda);
+    const VT* b = reinterpret_cast<const VT*>(g.B + c * g.ldb);
+    VT* out = reinterpret_cast<VT*>(g.C + c * g.ldc);
+    for (int v0 = threadIdx.x; v0 < mv; v0 += kU * blockDim.x) {
+      VT va[kU], vb[kU];
+#pragma unroll
+      for (int u = 0; u < kU; ++u) {
+        const int v = v0 + u * blockDim.x;
+        if (v < mv) {
+          if (use_a) va[u] = __ldcs(a + v);
+          if (use_b) vb[u] = __ldcs(b + v);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < kU; ++u) {
+        const int v = v0 + u * blockDim.x;
+        if (v < mv) {
+          T r[kN];
+#pragma unroll
+          for (int e = 0; e < kN; ++e) {
+            const T ta = use_a ? mul_rn(alpha, lane_of<T>(va[u], e)) : T(0);
+            const T tb = use_b ? mul_rn(beta, lane_of<T>(vb[u], e)) : T(0);
+            r[e] = combine(use_a, ta, use_b, tb);
+          }
+          VT o;
+          if constexpr (kN == 4) {
+            o = make_float4(r[0], r[1], r[2], r[3]);
+          } else {
+            o = make_double2(r[0], r[1]);
+          }
+          __stcs(out + v, o);
+        }
+      }
+    }
+  }
+}
+
 // One wave: as many CTAs as the SMs hold at this instance's occupancy (its register
 // and shared-memory use differ by type and transposition), so that no CTA of the
 // grid-stride loop waits for a second wave.
@@ -287,6 +361,15 @@ cudaError_t launch_geam(bool trans_a, bool trans_b, int m, int n, T alpha, const
   g.tiles = static_cast<long long>(g.tiles_m) * ((n + kCols - 1) / kCols);
   g.alpha = alpha;
   g.beta = beta;
+  constexpr int kVec = 16 / static_cast<int>(sizeof(T));
+  if (!trans_a && !trans_b && m % kVec == 0 && lda % kVec == 0 && ldb % kVec == 0 &&
+      ldc % kVec == 0 && aligned_to(A, 16) && aligned_to(B, 16) && aligned_to(C, 16)) {
+    // a null operand is never read (its scalar is zero), so its alignment does not matter
+    const long long wave = static_cast<long long>(sm_count(current_device())) * 8;
+    const unsigned grid = static_cast<unsigned>(n < wave ? n : wave);
+    geam_nn_vec<T><<<grid, 256, 0, stream>>>(g);
+    return cudaGetLastError();
+  }
   if (trans_a)
     return trans_b ? launch<T, true, true>(g, stream) : launch<T, true, false>(g, stream);
   return trans_b ? launch<T, false, true>(g, stream) : launch<T, false, false>(g, stream);

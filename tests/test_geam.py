@@ -107,6 +107,11 @@ CASES = [
     (4099, 131, False, False, 3, 0, 0, 0.0, 1.5),     # alpha 0: A not read
     (129, 4099, True, True, 0, 0, 0, -0.7, 0.0),       # beta 0: B not read
     (64, 64, False, False, 0, 0, 0, 0.0, 0.0),         # both 0: C = +0
+    # op N,N with 16-byte aligned columns: the vectorised column-streaming kernel
+    (1028, 300, False, False, 0, 4, 8, 1.5, -0.25),
+    (2048, 33, False, False, 0, 0, 0, 0.0, 2.0),       # alpha 0 on that kernel
+    (512, 77, False, False, 4, 0, 0, 1.25, 0.0),       # beta 0 on that kernel
+    (1024, 40, False, False, 2, 0, 0, 1.0, 1.0),       # lda not a multiple of 4: tiled kernel
 ]
 
 

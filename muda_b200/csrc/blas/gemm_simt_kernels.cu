@@ -317,6 +317,15 @@ __device__ __forceinline__ int cta_of(long long s, const StreamK& sk) {
 // Row tm*4 + r + 64*h of a tile is held in acc[4h + r][.], column tn*8 + j in acc[.][j].
 // (One kernel body for both forms: the tile loop compiles measurably faster inline
 // than behind a helper function.)
+__device__ __forceinline__ unsigned long long pack2(float lo, float hi) {
+  unsigned long long r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ void unpack2(unsigned long long v, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+
 template <bool TA, bool TB, bool STREAM>
 __global__ void __launch_bounds__(kThreads, 2)
     gemm_ffma_vec(const GemmArgs g, float* __restrict__ ws, const StreamK sk) {
@@ -433,10 +442,18 @@ __global__ void __launch_bounds__(kThreads, 2)
         const float4 b1 = *reinterpret_cast<const float4*>(Bs + p * LDS + tn * 8 + 4);
         const float av[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
         const float bv[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+        // two columns per fma.rn.f32x2 (each lane the scalar fma, rounded alike): half
+        // the issue slots of the scalar form for the same FMA-pipe work
 #pragma unroll
-        for (int i = 0; i < 8; ++i)
+        for (int i = 0; i < 8; ++i) {
+          const unsigned long long a2 = pack2(av[i], av[i]);
 #pragma unroll
-          for (int j = 0; j < 8; ++j) acc[i][j] = fmaf(av[i], bv[j], acc[i][j]);
+          for (int j = 0; j < 8; j += 2) {
+            unsigned long long c2 = pack2(acc[i][j], acc[i][j + 1]);
+            asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(c2) : "l"(a2), "l"(pack2(bv[j], bv[j + 1])));
+            unpack2(c2, acc[i][j], acc[i][j + 1]);
+          }
+        }
       }
       if (more) {
         stash(buf ^ 1);
